@@ -1,0 +1,356 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 PQ build path.
+
+Workload (one "step"): ``pq.train`` over 1,521,797 x 64 f32 unit residuals,
+M = 16 subspaces x 4 dims, 256 centroids each, k-means++ seeding plus 20
+Lloyd iterations (tol = -inf), then ``pq.encode`` of all rows. Inputs are
+seeded synthetic vectors (``synth.make_corpus``: normalize(anchor +
+0.35 N(0, I)), anchors Zipf(1.1) over 19,221 token ids); the PQ input is each
+vector's unit residual from its token anchor. The 389 MB input is larger
+than L2 (126 MB), so no explicit L2 flush is needed between steps.
+
+Metric: ``pq.train s/Lloyd-iter`` = device time of one full pq.train call
+(seeding included) / 20; lower is better. ``e2e`` is the same metric through
+the host-pointer C ABI (``mvr_pq_train``) with the rows copied from pinned
+host memory every step. Encode throughput is reported beside it.
+
+``--impl reference`` times the CPU restatement of the reference
+(oracle/, multithreaded like the reference's work-stealing ``pq.train``) on
+this host's cores, on a bounded row sample of the same workload.
+
+Multi-GPU (``--gpus N`` under torchrun): each rank runs the full workload
+as an independent replica ("replicas only" in this round); the reported time
+is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_ROWS = 1_521_797
+DIM = 64
+PQ_M = 16
+K = 256
+ITERS = 20
+SEED = 42 + 0xA1B2C3D4  # storage.build passes params.seed +% 0xa1b2c3d4 to pq.train
+METRIC = "pq.train s/Lloyd-iter"
+UNIT = "s/iter"
+WORKLOAD = "configs[1]: synthetic 1,521,797 x 64 f32, PQ M=16x4, 256 centroids, k-means++ + 20 Lloyd iters, + pq.encode"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def make_input(n: int = N_ROWS) -> np.ndarray:
+    from ir_multivector_retrieval_b200 import synth
+
+    c = synth.make_corpus(n, DIM, seed=42)
+    return synth.anchor_residuals(c)
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU arm
+
+
+def cpu_lloyd_seconds_per_iter(x: np.ndarray, threads: int, target_s: float = 15.0) -> dict:
+    """One Lloyd iteration of every subspace (oracle, all host threads) on a
+    row sample sized for ~target_s of CPU time, scaled linearly to N_ROWS
+    (Lloyd cost is linear in the rows)."""
+    from oracle import oracle
+
+    oracle.build()
+    n_probe = min(len(x), 20_000)
+    cb0 = np.ascontiguousarray(
+        x[np.linspace(0, len(x) - 1, K).astype(np.int64)].reshape(K, PQ_M, DIM // PQ_M).transpose(1, 0, 2)
+    ).reshape(-1)
+    t0 = time.perf_counter()
+    oracle.pq_lloyd_iters(x[:n_probe], DIM, PQ_M, 1, threads, cb0)
+    probe = time.perf_counter() - t0
+    n_sample = int(min(len(x), max(n_probe, n_probe * target_s / max(probe, 1e-6))))
+    t0 = time.perf_counter()
+    oracle.pq_lloyd_iters(x[:n_sample], DIM, PQ_M, 1, threads, cb0)
+    dt = time.perf_counter() - t0
+    return {"s_per_iter": dt * N_ROWS / n_sample, "rows": n_sample, "wall_s": dt}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = host_threads()
+    x = make_input()
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_lloyd_seconds_per_iter(x, threads, target_s=args.cpu_target_s)
+        if i >= args.warmup:
+            vals.append(info["s_per_iter"])
+    v = statistics.median(vals)
+    sample = (f"1 Lloyd iteration of all 16 subspaces over the first {info['rows']} rows "
+              f"(of {N_ROWS}), scaled linearly to all rows; C restatement of pq.train's Lloyd loop")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": "cpu", "l2": "inputs > L2"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+
+
+def run_b200(args) -> None:
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    from ir_multivector_retrieval_b200 import Context
+    from ir_multivector_retrieval_b200._lib import PqTrainStats
+
+    x = make_input()
+    n = x.shape[0]
+    x_pin = torch.from_numpy(x).pin_memory()
+    dx = x_pin.to(f"cuda:{local}", non_blocking=False)
+    dcb = torch.empty(PQ_M * K * (DIM // PQ_M), dtype=torch.float32, device=f"cuda:{local}")
+    dcodes = torch.empty((n, PQ_M), dtype=torch.uint8, device=f"cuda:{local}")
+    stream = torch.cuda.current_stream()
+    ctx = Context(local)
+    ctx.set_stream(stream.cuda_stream)
+    lib = ctx.lib
+
+    def train_dev(st):
+        ctx.check(lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), x.size, DIM, SEED, 1, PQ_M,
+                                          ITERS, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()), C.byref(st)))
+
+    def encode_dev():
+        ctx.check(lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), DIM, PQ_M,
+                                           C.c_void_p(dx.data_ptr()), n, C.c_void_p(dcodes.data_ptr())))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        train_dev(PqTrainStats())
+        encode_dev()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    stats = []
+    enc_ev = []
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        st = PqTrainStats()
+        train_dev(st)
+        stats.append(st)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        encode_dev()
+        e1.record(stream)
+        enc_ev.append((e0, e1))
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = t_start.elapsed_time(t_end) / args.steps
+    train_ms = statistics.mean(s.total_ms for s in stats)
+    seed_ms = statistics.mean(s.seed_ms for s in stats)
+    lloyd_ms = statistics.mean(s.lloyd_ms for s in stats)
+    enc_ms = statistics.mean(a.elapsed_time(b) for a, b in enc_ev)
+    assign_ms = sum(s.assign_ms for s in stats) / sum(s.assign_launches for s in stats)
+    launches = int(statistics.mean(s.launches for s in stats)) + 1
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    train_ms = max_over_ranks(train_ms)
+    step_ms = max_over_ranks(step_ms)
+    enc_ms = max_over_ranks(enc_ms)
+    value = train_ms / 1e3 / ITERS
+
+    # ---- e2e: host-pointer C ABI, rows copied from pinned memory each step
+    cb_host = np.empty(PQ_M * K * (DIM // PQ_M), dtype=np.float32)
+    codes_host = torch.empty((n, PQ_M), dtype=torch.uint8).pin_memory()
+    e2e_train, e2e_enc = [], []
+    for i in range(max(1, args.e2e_steps) + 1):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ctx.check(lib.mvr_pq_train(ctx.handle, C.c_void_p(x_pin.data_ptr()), x.size, DIM, SEED, 1, PQ_M, ITERS,
+                                   C.c_float(-math.inf), C.c_void_p(cb_host.ctypes.data), None))
+        t1 = time.perf_counter()
+        ctx.check(lib.mvr_pq_encode(ctx.handle, C.c_void_p(cb_host.ctypes.data), DIM, PQ_M,
+                                    C.c_void_p(x_pin.data_ptr()), n, C.c_void_p(codes_host.data_ptr())))
+        t2 = time.perf_counter()
+        if i > 0:  # first call grows the staging buffers
+            e2e_train.append(t1 - t0)
+            e2e_enc.append(t2 - t1)
+    e2e_value = max_over_ranks(statistics.median(e2e_train)) / ITERS
+    e2e_enc_s = max_over_ranks(statistics.median(e2e_enc))
+    assert np.array_equal(cb_host, dcb.cpu().numpy()), "host and device entry points disagree"
+
+    # ---- roofline of the dominant kernel (Lloyd assignment)
+    flops_per_launch = n * K * 3 * DIM  # 3 flops per coordinate per (row, centroid)
+    achieved = flops_per_launch / (assign_ms / 1e3) / 1e12
+    sm_mhz = clk.get("sm_mhz") or 1965.0
+    peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # FP32 lanes x clock (one op per lane per cycle)
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("pq_assign_kernel_lloyd_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows": n, "dim": DIM, "pq_m": PQ_M, "centroids": K,
+                       "lloyd_iters": ITERS, "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+                       "l2": "inputs (389 MB) > L2, no flush"},
+            "pq_train_ms": train_ms, "seed_ms": seed_ms, "lloyd_ms": lloyd_ms,
+            "lloyd_only_s_per_iter": lloyd_ms / 1e3 / ITERS,
+            "pq_encode_ms": enc_ms, "pq_encode_mvec_s": n / (enc_ms / 1e3) / 1e6,
+            "seed_fallbacks": int(stats[-1].seed_fallbacks), "reseeds": int(stats[-1].reseeds),
+            "gpu_launches": launches,
+            "clocks": clk,
+            "roofline": {"kernel": "pq_assign_kernel<4,Lloyd>", "bound": "fp32", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": ("nominal FP32 issue rate, 148 SM x 128 lanes x median SM clock of "
+                                         "this run; MEASURED_PEAKS.json has no FP32 entry"),
+                         "algorithmic_flops_per_launch": flops_per_launch,
+                         "avg_launch_ms": assign_ms},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes),
+                    "d2h_bytes_per_step": int(cb_host.nbytes),
+                    "encode_mvec_s": n / e2e_enc_s / 1e6},
+        }
+        if world == 1 and not args.no_cpu:
+            cpu = cpu_lloyd_seconds_per_iter(x, host_threads(), target_s=args.cpu_target_s)
+            line["cpu_baseline"] = {
+                "value": cpu["s_per_iter"], "unit": UNIT, "cores": host_threads(), "kind": "port",
+                "sample": (f"1 Lloyd iteration of all 16 subspaces over {cpu['rows']} rows, scaled to "
+                           f"{N_ROWS}; Lloyd only (seeding excluded, GPU value includes it)")}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-target-s", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

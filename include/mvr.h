@@ -1,0 +1,250 @@
+/*
+ * mvr.h — C ABI of the B200 build path for the TAC multivector index:
+ * PQ codebook training, PQ encoding, the shared k-means primitive and
+ * TAC per-token clustering.
+ *
+ * Every entry point replaces one function of the reference Zig build path
+ * (BleedingDev/ir-multivector-retrieval). The citation beside each
+ * declaration names the reference function it stands in for, as
+ * `path:line` inside that project. A Zig host binds these symbols with
+ * `@cImport(@cInclude("mvr.h"))` and keeps its own signatures.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. Host-pointer entry points copy inputs
+ *     to the GPU and results back; `*_device` entry points take device
+ *     pointers and run on the context's stream.
+ *   - Caller-allocated outputs. The library owns only its device scratch,
+ *     which lives in the opaque `mvr_ctx`.
+ *   - Every entry point returns an `int` status. `MVR_OK` is 0; the other
+ *     codes map one-to-one onto the reference's Zig error names (listed
+ *     beside each code). `mvr_last_error(ctx)` gives the message of the last
+ *     failing call on that context.
+ *   - Validation order follows the reference, so the same bad input yields
+ *     the same error name.
+ *   - Calls on one context are serialised by the caller (the reference's
+ *     callers are single-threaded at these call sites).
+ *   - `n_threads` arguments are accepted for signature parity. They change
+ *     nothing on the GPU except the WCSS summation order that
+ *     `tac.clusterFlat` reports, which the reference defines per thread count.
+ *   - Lloyd stopping rule: the reference's `rel_delta < tol` test. Pass
+ *     `tol = -INFINITY` to run exactly `max_iters` iterations.
+ */
+#ifndef MVR_H
+#define MVR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  MVR_OK = 0,
+  MVR_E_KMEANS_BUDGET_TOO_SMALL = 1, /* kmeans.KMeansError.KmeansBudgetTooSmall */
+  MVR_E_EMPTY_VECTOR_SET = 2,        /* kmeans.KMeansError.EmptyVectorSet */
+  MVR_E_DIM_MISMATCH = 3,            /* kmeans/pq DimMismatch */
+  MVR_E_DIM_NOT_DIVISIBLE_BY_M = 4,  /* pq.PqError.DimNotDivisibleByM */
+  MVR_E_EMPTY_CORPUS = 5,            /* pq.PqError.EmptyCorpus */
+  MVR_E_OUT_BUFFER_WRONG_SIZE = 6,   /* pq.PqError.OutBufferWrongSize */
+  MVR_E_NQ_MISMATCH = 7,             /* pq.PqError.NQMismatch */
+  MVR_E_EMPTY_DISTRIBUTION = 8,      /* rng.RngError.EmptyDistribution */
+  MVR_E_NON_FINITE = 9,              /* rng.RngError.NonFinite */
+  MVR_E_ALL_ZERO = 10,               /* rng.RngError.AllZero */
+  MVR_E_BUDGET_TOO_SMALL = 11,       /* tac.ClusteringError.BudgetTooSmall */
+  MVR_E_BUDGET_TOO_LARGE = 12,       /* tac.ClusteringError.BudgetTooLarge */
+  MVR_E_INVALID_THRESHOLDS = 13,     /* tac.ClusteringError.InvalidThresholds */
+  MVR_E_EMPTY_TOKEN_DUMP = 14,       /* tac.ClusteringError.EmptyTokenDump */
+  MVR_E_LENGTH_MISMATCH = 15,        /* vec.VecError.LengthMismatch */
+  MVR_E_EMPTY_INPUT = 16,            /* vec.VecError.EmptyInput */
+  MVR_E_OUT_OF_MEMORY = 17,          /* Allocator.Error.OutOfMemory (host or device) */
+  /* B200-side failures with no reference counterpart */
+  MVR_E_CUDA = 100,             /* a CUDA runtime call failed */
+  MVR_E_NCCL = 101,             /* an NCCL call failed */
+  MVR_E_TIMEOUT = 102,          /* a bounded device wait ran out */
+  MVR_E_INVALID_ARGUMENT = 103, /* null pointer, unsupported shape */
+  MVR_E_NO_DEVICE = 104         /* no CUDA device with sm_100 */
+};
+
+/* Number of centroids per PQ subspace (reference constants.PQ_CENTROIDS). */
+#define MVR_PQ_CENTROIDS 256u
+
+typedef struct mvr_ctx mvr_ctx;
+
+/* ---- context ----------------------------------------------------------- */
+
+/* Create a context bound to CUDA device `device_ordinal`. The context owns a
+ * stream and grows device scratch on demand. No reference counterpart: the
+ * Zig build keeps all state in `gpa`-allocated slices. */
+int mvr_ctx_create(int device_ordinal, mvr_ctx** out);
+
+/* Free the context and all its device scratch. */
+int mvr_ctx_destroy(mvr_ctx* ctx);
+
+/* Message of the last failing call on `ctx` ("" if none). */
+const char* mvr_last_error(const mvr_ctx* ctx);
+
+/* Zig error name of a status code, e.g. "DimNotDivisibleByM". */
+const char* mvr_status_name(int status);
+
+/* Use an existing CUDA stream (a `cudaStream_t`) for the `*_device` entry
+ * points. NULL restores the context's own stream. */
+int mvr_ctx_set_stream(mvr_ctx* ctx, void* cuda_stream);
+
+/* Release device scratch held by the context (it is regrown on demand). */
+int mvr_ctx_trim(mvr_ctx* ctx);
+
+/* ---- kmeans.fit -------------------------------------------------------- */
+
+/* Replaces `kmeans.fit(vectors, dim, KMeansParams{k, max_iters, tol, seed,
+ * n_threads}, gpa)` (src/tac/kmeans.zig:67-72; params :28-41; result
+ * :43-54). `vectors` holds `vectors_len` floats, row-major, n =
+ * vectors_len / dim rows. Outputs: centroids k*dim floats, assignments n
+ * u32, wcss and iters_run scalars (any output pointer may be NULL except
+ * `centroids_out`). k-means++ seeding, Lloyd iterations with the reference's
+ * serial in-order centroid sums, empty-cluster reseed and relative-WCSS
+ * stopping, bit-exact with the reference arithmetic. */
+int mvr_kmeans_fit(mvr_ctx* ctx, const float* vectors, uint64_t vectors_len,
+                   uint32_t dim, uint32_t k, uint32_t max_iters, float tol,
+                   uint64_t seed, uint32_t n_threads, float* centroids_out,
+                   uint32_t* assignments_out, float* wcss_out,
+                   uint32_t* iters_run_out);
+
+/* ---- pq.train / PQ.encode ---------------------------------------------- */
+
+/* Per-call timing and iteration report of `mvr_pq_train*` (no reference
+ * counterpart; the reference prints `[stage]` lines instead,
+ * src/index/storage.zig:382). Times are device times in milliseconds. */
+typedef struct mvr_pq_train_stats {
+  double seed_ms;        /* k-means++ seeding, all subspaces */
+  double lloyd_ms;       /* Lloyd iterations, all subspaces */
+  double total_ms;       /* whole call on the device */
+  uint32_t iters_max;    /* largest iters_run over subspaces */
+  uint32_t iters_min;    /* smallest iters_run over subspaces */
+  uint32_t seed_fallbacks; /* k-means++ draws resolved by the exact serial chain */
+  uint32_t reseeds;      /* empty-cluster reseeds, summed over iterations */
+  double assign_ms;      /* summed device time of the Lloyd assignment kernel */
+  uint32_t assign_launches; /* launches of that kernel */
+  uint32_t launches;     /* all kernel launches of the call */
+} mvr_pq_train_stats;
+
+/* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`
+ * (src/index/pq.zig:158-164, per subspace `trainOneSubspace` :301-336).
+ * `pq_m` is the number of subspaces (the reference's comptime PQ_M; 32 in the
+ * stock build, 16 in the M=16x4 configuration). Each subspace runs
+ * kmeans.fit(k=256, max_iters, tol, seed +% m). The reference hard-codes
+ * max_iters=25, tol=1e-4 (pq.zig:319-325). Output: pq_m*256*(dim/pq_m)
+ * floats laid out codebook[m][c][k] (pq.zig:14-15). `stats` may be NULL. */
+int mvr_pq_train(mvr_ctx* ctx, const float* residuals, uint64_t residuals_len,
+                 uint32_t dim, uint64_t seed, uint32_t n_threads, uint32_t pq_m,
+                 uint32_t max_iters, float tol, float* codebooks_out,
+                 mvr_pq_train_stats* stats);
+
+/* As `mvr_pq_train`, with `d_residuals` and `d_codebooks_out` in device
+ * memory. Runs on the context's stream and returns when the result is
+ * ready. */
+int mvr_pq_train_device(mvr_ctx* ctx, const float* d_residuals,
+                        uint64_t residuals_len, uint32_t dim, uint64_t seed,
+                        uint32_t n_threads, uint32_t pq_m, uint32_t max_iters,
+                        float tol, float* d_codebooks_out,
+                        mvr_pq_train_stats* stats);
+
+/* Replaces the encode loop `storage.parallelTokenLoop(pqEncodeChunk)`
+ * (src/index/storage.zig:287-295, :389-400), i.e. `PQ.encode` per row
+ * (src/index/pq.zig:59-76): for each of the n rows and each subspace m, the
+ * first codeword of minimum exact squared L2 distance. `codebooks` is
+ * pq_m*256*(dim/pq_m) floats, `residuals` n*dim floats, `codes_out` n*pq_m
+ * bytes. */
+int mvr_pq_encode(mvr_ctx* ctx, const float* codebooks, uint32_t dim,
+                  uint32_t pq_m, const float* residuals, uint64_t n,
+                  uint8_t* codes_out);
+
+/* As `mvr_pq_encode`, all pointers in device memory; asynchronous on the
+ * context's stream (call `mvr_ctx_sync` before reading the codes). */
+int mvr_pq_encode_device(mvr_ctx* ctx, const float* d_codebooks, uint32_t dim,
+                         uint32_t pq_m, const float* d_residuals, uint64_t n,
+                         uint8_t* d_codes_out);
+
+/* Wait for all work on the context's stream; reports device-side errors. */
+int mvr_ctx_sync(mvr_ctx* ctx);
+
+/* Replaces `PQ.decode` (src/index/pq.zig:79-88) over a batch: rows of
+ * concatenated codewords. Host pointers; runs on the host (it is a copy). */
+int mvr_pq_decode(const float* codebooks, uint32_t dim, uint32_t pq_m,
+                  const uint8_t* codes, uint64_t n, float* out);
+
+/* ---- storage residuals ------------------------------------------------- */
+
+/* Replaces `residualsAndNormsChunk` over all rows
+ * (src/index/storage.zig:255-278): r = v - centroids[assign[i]];
+ * norm = sqrt(sum r^2) summed in coordinate order; r *= 1/norm if norm > 0.
+ * vectors n*dim, centroids kappa*dim, assignments n, residuals_out n*dim,
+ * norms_out n. Host pointers. */
+int mvr_residuals_norms(mvr_ctx* ctx, const float* vectors,
+                        const float* centroids, uint32_t kappa,
+                        const uint32_t* assignments, uint64_t n, uint32_t dim,
+                        float* residuals_out, float* norms_out);
+
+/* Device-pointer variant of `mvr_residuals_norms` (asynchronous). */
+int mvr_residuals_norms_device(mvr_ctx* ctx, const float* d_vectors,
+                               const float* d_centroids, uint32_t kappa,
+                               const uint32_t* d_assignments, uint64_t n,
+                               uint32_t dim, float* d_residuals_out,
+                               float* d_norms_out);
+
+/* ---- tac.clusterFlat --------------------------------------------------- */
+
+/* Mirrors `tac.ClusteringParams` (src/tac/tac.zig:35-57). Reference
+ * defaults: mu=128 tau=256 epsilon=4 theta=39 max_iters=25 tol=1e-4
+ * n_threads=1 (src/constants.zig:10-13). */
+typedef struct mvr_clustering_params {
+  uint32_t kappa_total;
+  uint32_t mu;
+  uint32_t tau;
+  uint32_t epsilon;
+  uint32_t theta;
+  uint32_t max_iters;
+  float tol;
+  uint64_t seed;
+  uint32_t n_threads;
+} mvr_clustering_params;
+
+/* Fill `p` with the reference defaults and the given budget and seed. */
+void mvr_clustering_params_default(mvr_clustering_params* p,
+                                   uint32_t kappa_total, uint64_t seed);
+
+/* Replaces `tac.clusterFlat(token_ids, vectors, dim, p, gpa)`
+ * (src/tac/tac.zig:563-838): per-token frequencies and CSR grouping,
+ * Welford spreads, budget phases 1-4 (tac.zig:97-402), then one
+ * kmeans.fit(k=kappa_j, seed ^ j) per token (runOneTokenKmeans,
+ * tac.zig:458-514), all per-token k-means on the GPU.
+ * Inputs: n_tokens ids, vectors_len = n_tokens*dim floats.
+ * Outputs: centroids_out kappa_total*dim floats (token-id order),
+ * assignments_out n_tokens global centroid ids, kappa_per_token_out with
+ * room for `kappa_per_token_cap` entries (the vocabulary size
+ * max(token_ids)+1 is written to *n_distinct_out; a smaller cap returns
+ * MVR_E_OUT_BUFFER_WRONG_SIZE), wcss_total_out summed in the reference's
+ * per-thread-chunk order for `p->n_threads`. */
+int mvr_tac_cluster_flat(mvr_ctx* ctx, const uint32_t* token_ids,
+                         uint64_t n_tokens, const float* vectors,
+                         uint64_t vectors_len, uint32_t dim,
+                         const mvr_clustering_params* p, float* centroids_out,
+                         uint32_t* assignments_out,
+                         uint32_t* kappa_per_token_out,
+                         uint64_t kappa_per_token_cap, uint64_t* n_distinct_out,
+                         float* wcss_total_out);
+
+/* Replaces `tac.allocateBudgets` (src/tac/tac.zig:390-402): phases 1-4 on
+ * per-token (freq, spread) arrays of length n. Host-only integer/float
+ * logic; `frac` is caller scratch of n floats. */
+int mvr_tac_allocate_budgets(const uint32_t* freqs, const float* spreads,
+                             uint32_t* kappa, float* frac, uint64_t n,
+                             uint32_t kappa_total,
+                             const mvr_clustering_params* p);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MVR_H */

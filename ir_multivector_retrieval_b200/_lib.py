@@ -1,0 +1,220 @@
+"""ctypes binding of ``libmvr_b200.so`` (the C ABI in ``include/mvr.h``).
+
+The shared library is the product; this module only declares its
+signatures. It fails loudly when the library is missing: there is no CPU
+fallback anywhere in the package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libmvr_b200.so"
+
+# Status codes of include/mvr.h, named after the reference's Zig errors.
+STATUS_NAMES = {
+    0: "Ok",
+    1: "KmeansBudgetTooSmall",
+    2: "EmptyVectorSet",
+    3: "DimMismatch",
+    4: "DimNotDivisibleByM",
+    5: "EmptyCorpus",
+    6: "OutBufferWrongSize",
+    7: "NQMismatch",
+    8: "EmptyDistribution",
+    9: "NonFinite",
+    10: "AllZero",
+    11: "BudgetTooSmall",
+    12: "BudgetTooLarge",
+    13: "InvalidThresholds",
+    14: "EmptyTokenDump",
+    15: "LengthMismatch",
+    16: "EmptyInput",
+    17: "OutOfMemory",
+    100: "CudaError",
+    101: "NcclError",
+    102: "Timeout",
+    103: "InvalidArgument",
+    104: "NoDevice",
+}
+CODES = {v: k for k, v in STATUS_NAMES.items()}
+
+
+class MvrError(Exception):
+    """A failing status from the library. ``name`` is the reference's Zig
+    error name (e.g. ``"DimNotDivisibleByM"``)."""
+
+    def __init__(self, code: int, message: str = ""):
+        self.code = int(code)
+        self.name = STATUS_NAMES.get(self.code, f"Status{code}")
+        super().__init__(f"{self.name}: {message}" if message else self.name)
+
+
+class PqTrainStats(C.Structure):
+    _fields_ = [
+        ("seed_ms", C.c_double),
+        ("lloyd_ms", C.c_double),
+        ("total_ms", C.c_double),
+        ("iters_max", C.c_uint32),
+        ("iters_min", C.c_uint32),
+        ("seed_fallbacks", C.c_uint32),
+        ("reseeds", C.c_uint32),
+        ("assign_ms", C.c_double),
+        ("assign_launches", C.c_uint32),
+        ("launches", C.c_uint32),
+    ]
+
+
+class ClusteringParams(C.Structure):
+    _fields_ = [
+        ("kappa_total", C.c_uint32),
+        ("mu", C.c_uint32),
+        ("tau", C.c_uint32),
+        ("epsilon", C.c_uint32),
+        ("theta", C.c_uint32),
+        ("max_iters", C.c_uint32),
+        ("tol", C.c_float),
+        ("seed", C.c_uint64),
+        ("n_threads", C.c_uint32),
+    ]
+
+
+_P = C.c_void_p
+_F = C.POINTER(C.c_float)
+_U8 = C.POINTER(C.c_uint8)
+_U32 = C.POINTER(C.c_uint32)
+_U64 = C.POINTER(C.c_uint64)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "mvr_ctx_create": (C.c_int, [C.c_int, C.POINTER(_P)]),
+    "mvr_ctx_destroy": (C.c_int, [_P]),
+    "mvr_last_error": (C.c_char_p, [_P]),
+    "mvr_status_name": (C.c_char_p, [C.c_int]),
+    "mvr_ctx_set_stream": (C.c_int, [_P, _P]),
+    "mvr_ctx_trim": (C.c_int, [_P]),
+    "mvr_ctx_sync": (C.c_int, [_P]),
+    "mvr_kmeans_fit": (
+        C.c_int,
+        [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,
+         C.c_uint32, _P, _P, _P, _P],
+    ),
+    "mvr_pq_train": (
+        C.c_int,
+        [_P, _P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+         C.c_float, _P, C.POINTER(PqTrainStats)],
+    ),
+    "mvr_pq_train_device": (
+        C.c_int,
+        [_P, _P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+         C.c_float, _P, C.POINTER(PqTrainStats)],
+    ),
+    "mvr_pq_encode": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, _P]),
+    "mvr_pq_encode_device": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, _P]),
+    "mvr_pq_decode": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_uint64, _P]),
+    "mvr_residuals_norms": (
+        C.c_int, [_P, _P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, _P]),
+    "mvr_residuals_norms_device": (
+        C.c_int, [_P, _P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, _P]),
+    "mvr_clustering_params_default": (None, [C.POINTER(ClusteringParams), C.c_uint32, C.c_uint64]),
+    "mvr_tac_cluster_flat": (
+        C.c_int,
+        [_P, _P, C.c_uint64, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams), _P, _P,
+         _P, C.c_uint64, _U64, _F],
+    ),
+    "mvr_tac_allocate_budgets": (
+        C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams)]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> C.CDLL:
+    """Load the shared library (once). Raises if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with "
+                    "`python -m ir_multivector_retrieval_b200.build` (there is no CPU fallback)"
+                )
+            lib = C.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def ptr(a) -> C.c_void_p:
+    """Raw address of a numpy array or a torch tensor (device or host)."""
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return C.c_void_p(a.ctypes.data)
+    if hasattr(a, "data_ptr"):
+        return C.c_void_p(a.data_ptr())
+    raise TypeError(f"cannot take the address of {type(a)!r}")
+
+
+class Context:
+    """A CUDA device context of the library (``mvr_ctx``)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        h = C.c_void_p()
+        st = self.lib.mvr_ctx_create(int(device), C.byref(h))
+        if st != 0:
+            raise MvrError(st, f"mvr_ctx_create(device={device})")
+        self.handle = h
+        self.device = device
+
+    def check(self, status: int, what: str = "") -> None:
+        if status != 0:
+            msg = self.lib.mvr_last_error(self.handle)
+            raise MvrError(status, (msg.decode() if msg else "") or what)
+
+    def set_stream(self, stream_handle: int | None) -> None:
+        self.check(self.lib.mvr_ctx_set_stream(self.handle, C.c_void_p(stream_handle or 0)))
+
+    def sync(self) -> None:
+        self.check(self.lib.mvr_ctx_sync(self.handle))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.mvr_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default: dict[int, Context] = {}
+
+
+def default_context(device: int | None = None) -> Context:
+    """Per-device shared context used by the reference-style functions."""
+    dev = int(os.environ.get("MVR_DEVICE", "0")) if device is None else int(device)
+    with _lock:
+        ctx = _default.get(dev)
+    if ctx is None:
+        ctx = Context(dev)
+        with _lock:
+            _default[dev] = ctx
+    return ctx

@@ -1,0 +1,431 @@
+// mvr_capi.cu — the extern "C" entry points declared in include/mvr.h.
+//
+// Host-pointer entry points stage inputs into context-owned device buffers,
+// run the device path and copy results back. There is no CPU fallback: a
+// missing or unusable GPU is reported as MVR_E_NO_DEVICE / MVR_E_CUDA.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/mvr.h"
+#include "mvr_internal.h"
+#include "pq_engine.h"
+#include "tac_engine.h"
+
+namespace mvr {
+
+int fail(Ctx* ctx, int status, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return status;
+}
+
+int cuda_fail(Ctx* ctx, cudaError_t e, const char* what) {
+  std::string msg = std::string(what) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) {
+    (void)cudaGetLastError();
+    return fail(ctx, MVR_E_OUT_OF_MEMORY, msg);
+  }
+  return fail(ctx, MVR_E_CUDA, msg);
+}
+
+int scratch(Ctx* ctx, int slot, size_t bytes, void** out) {
+  DevBuf& b = ctx->slots[slot];
+  if (bytes == 0) bytes = 256;
+  if (b.bytes < bytes) {
+    if (b.ptr) {
+      cudaError_t e = cudaStreamSynchronize(ctx->stream);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+      cudaFree(b.ptr);
+      b.ptr = nullptr;
+      b.bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&b.ptr, bytes);
+    if (e != cudaSuccess) {
+      b.ptr = nullptr;
+      return cuda_fail(ctx, e, "cudaMalloc(scratch)");
+    }
+    b.bytes = bytes;
+  }
+  *out = b.ptr;
+  return MVR_OK;
+}
+
+int pinned(Ctx* ctx, size_t bytes, void** out) {
+  if (ctx->pinned_bytes < bytes) {
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    ctx->pinned = nullptr;
+    ctx->pinned_bytes = 0;
+    cudaError_t e = cudaMallocHost(&ctx->pinned, bytes);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMallocHost");
+    ctx->pinned_bytes = bytes;
+  }
+  *out = ctx->pinned;
+  return MVR_OK;
+}
+
+namespace {
+
+int set_device(Ctx* c) {
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+  return MVR_OK;
+}
+
+int h2d(Ctx* c, void* d, const void* h, size_t bytes) {
+  if (bytes == 0) return MVR_OK;
+  MVR_CUDA(c, cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, c->stream));
+  return MVR_OK;
+}
+
+int d2h(Ctx* c, void* h, const void* d, size_t bytes) {
+  if (bytes == 0) return MVR_OK;
+  MVR_CUDA(c, cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, c->stream));
+  return MVR_OK;
+}
+
+// storage.residualsAndNormsChunk (src/index/storage.zig:255-278): one
+// thread per row, coordinates summed in order.
+__global__ void residuals_norms_kernel(const float* __restrict__ v, const float* __restrict__ cent,
+                                       const uint32_t* __restrict__ asg, uint64_t n, uint32_t dim,
+                                       float* __restrict__ res, float* __restrict__ norms) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const float* vi = v + i * dim;
+    const float* ci = cent + (uint64_t)asg[i] * dim;
+    float* ri = res + i * dim;
+    float sum = 0.f;
+    for (uint32_t d = 0; d < dim; ++d) {
+      const float diff = __fsub_rn(vi[d], ci[d]);
+      ri[d] = diff;
+      sum = __fadd_rn(sum, __fmul_rn(diff, diff));
+    }
+    const float norm = __fsqrt_rn(sum);
+    norms[i] = norm;
+    if (norm > 0.f) {
+      const float inv = __fdiv_rn(1.0f, norm);
+      for (uint32_t d = 0; d < dim; ++d) ri[d] = __fmul_rn(ri[d], inv);
+    }
+  }
+}
+
+int pq_validate(Ctx* c, uint64_t len, uint32_t dim, uint32_t pq_m) {
+  // pq.train validation order (src/index/pq.zig:165-168)
+  if (dim == 0) return fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (pq_m == 0 || dim % pq_m != 0) return fail(c, MVR_E_DIM_NOT_DIVISIBLE_BY_M, "dim % pq_m != 0");
+  if (len == 0) return fail(c, MVR_E_EMPTY_CORPUS, "empty residual set");
+  if (len % dim != 0) return fail(c, MVR_E_DIM_MISMATCH, "residuals_len % dim != 0");
+  return MVR_OK;
+}
+
+}  // namespace
+}  // namespace mvr
+
+using mvr::Ctx;
+
+extern "C" {
+
+const char* mvr_status_name(int s) {
+  switch (s) {
+    case MVR_OK: return "Ok";
+    case MVR_E_KMEANS_BUDGET_TOO_SMALL: return "KmeansBudgetTooSmall";
+    case MVR_E_EMPTY_VECTOR_SET: return "EmptyVectorSet";
+    case MVR_E_DIM_MISMATCH: return "DimMismatch";
+    case MVR_E_DIM_NOT_DIVISIBLE_BY_M: return "DimNotDivisibleByM";
+    case MVR_E_EMPTY_CORPUS: return "EmptyCorpus";
+    case MVR_E_OUT_BUFFER_WRONG_SIZE: return "OutBufferWrongSize";
+    case MVR_E_NQ_MISMATCH: return "NQMismatch";
+    case MVR_E_EMPTY_DISTRIBUTION: return "EmptyDistribution";
+    case MVR_E_NON_FINITE: return "NonFinite";
+    case MVR_E_ALL_ZERO: return "AllZero";
+    case MVR_E_BUDGET_TOO_SMALL: return "BudgetTooSmall";
+    case MVR_E_BUDGET_TOO_LARGE: return "BudgetTooLarge";
+    case MVR_E_INVALID_THRESHOLDS: return "InvalidThresholds";
+    case MVR_E_EMPTY_TOKEN_DUMP: return "EmptyTokenDump";
+    case MVR_E_LENGTH_MISMATCH: return "LengthMismatch";
+    case MVR_E_EMPTY_INPUT: return "EmptyInput";
+    case MVR_E_OUT_OF_MEMORY: return "OutOfMemory";
+    case MVR_E_CUDA: return "CudaError";
+    case MVR_E_NCCL: return "NcclError";
+    case MVR_E_TIMEOUT: return "Timeout";
+    case MVR_E_INVALID_ARGUMENT: return "InvalidArgument";
+    case MVR_E_NO_DEVICE: return "NoDevice";
+    default: return "Unknown";
+  }
+}
+
+int mvr_ctx_create(int device_ordinal, mvr_ctx** out) {
+  if (!out) return MVR_E_INVALID_ARGUMENT;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= device_ordinal || device_ordinal < 0) {
+    (void)cudaGetLastError();
+    return MVR_E_NO_DEVICE;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device_ordinal) != cudaSuccess) return MVR_E_NO_DEVICE;
+  if (prop.major < 10) return MVR_E_NO_DEVICE;  // built for sm_100a only
+  auto* h = new (std::nothrow) mvr_ctx;
+  if (!h) return MVR_E_OUT_OF_MEMORY;
+  Ctx* c = &h->impl;
+  c->device = device_ordinal;
+  c->sm_count = prop.multiProcessorCount;
+  if (cudaSetDevice(device_ordinal) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete h;
+    return MVR_E_CUDA;
+  }
+  c->stream = c->own_stream;
+  *out = h;
+  return MVR_OK;
+}
+
+int mvr_ctx_destroy(mvr_ctx* h) {
+  if (!h) return MVR_OK;
+  Ctx* c = &h->impl;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (auto& b : c->slots)
+    if (b.ptr) cudaFree(b.ptr);
+  if (c->pinned) cudaFreeHost(c->pinned);
+  for (auto& e : c->ev)
+    if (e) cudaEventDestroy(e);
+  if (c->own_stream) cudaStreamDestroy(c->own_stream);
+  delete h;
+  return MVR_OK;
+}
+
+const char* mvr_last_error(const mvr_ctx* h) { return h ? h->impl.last_error.c_str() : ""; }
+
+int mvr_ctx_set_stream(mvr_ctx* h, void* s) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.stream = s ? (cudaStream_t)s : h->impl.own_stream;
+  return MVR_OK;
+}
+
+int mvr_ctx_trim(mvr_ctx* h) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  MVR_TRY(mvr::set_device(c));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  for (auto& b : c->slots) {
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+  }
+  return MVR_OK;
+}
+
+int mvr_ctx_sync(mvr_ctx* h) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  MVR_CUDA(c, cudaGetLastError());
+  return MVR_OK;
+}
+
+// ---- pq.train -------------------------------------------------------------
+
+int mvr_pq_train_device(mvr_ctx* h, const float* d_res, uint64_t len, uint32_t dim, uint64_t seed,
+                        uint32_t n_threads, uint32_t pq_m, uint32_t max_iters, float tol,
+                        float* d_cb, mvr_pq_train_stats* stats) {
+  (void)n_threads;
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  MVR_TRY(mvr::pq_validate(c, len, dim, pq_m));
+  if (!d_res || !d_cb) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  mvr::PqJob job;
+  job.R = d_res;
+  job.N = len / dim;
+  job.D = (int)dim;
+  job.M = (int)pq_m;
+  job.S = (int)(dim / pq_m);
+  job.K = (int)MVR_PQ_CENTROIDS;
+  job.seed = seed;
+  job.max_iters = max_iters;
+  job.tol = tol;
+  mvr::PqOut out;
+  out.d_codebooks = d_cb;
+  out.stats = stats;
+  return mvr::pq_kmeans_device(c, job, out);
+}
+
+int mvr_pq_train(mvr_ctx* h, const float* res, uint64_t len, uint32_t dim, uint64_t seed,
+                 uint32_t n_threads, uint32_t pq_m, uint32_t max_iters, float tol, float* cb_out,
+                 mvr_pq_train_stats* stats) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  MVR_TRY(mvr::pq_validate(c, len, dim, pq_m));
+  if (!res || !cb_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  float* d_res = nullptr;
+  float* d_cb = nullptr;
+  const size_t cb_floats = (size_t)MVR_PQ_CENTROIDS * dim;  // pq_m * 256 * sub_dim
+  MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, len * sizeof(float), (void**)&d_res));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, cb_floats * sizeof(float), (void**)&d_cb));
+  MVR_TRY(mvr::h2d(c, d_res, res, len * sizeof(float)));
+  MVR_TRY(mvr_pq_train_device(h, d_res, len, dim, seed, n_threads, pq_m, max_iters, tol, d_cb, stats));
+  MVR_TRY(mvr::d2h(c, cb_out, d_cb, cb_floats * sizeof(float)));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MVR_OK;
+}
+
+// ---- PQ.encode / decode ---------------------------------------------------
+
+int mvr_pq_encode_device(mvr_ctx* h, const float* d_cb, uint32_t dim, uint32_t pq_m,
+                         const float* d_res, uint64_t n, uint8_t* d_codes) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (pq_m == 0 || dim % pq_m != 0) return mvr::fail(c, MVR_E_DIM_NOT_DIVISIBLE_BY_M, "dim % pq_m != 0");
+  if (n == 0) return MVR_OK;
+  if (!d_cb || !d_res || !d_codes) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  return mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes);
+}
+
+int mvr_pq_encode(mvr_ctx* h, const float* cb, uint32_t dim, uint32_t pq_m, const float* res,
+                  uint64_t n, uint8_t* codes_out) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (pq_m == 0 || dim % pq_m != 0) return mvr::fail(c, MVR_E_DIM_NOT_DIVISIBLE_BY_M, "dim % pq_m != 0");
+  if (n == 0) return MVR_OK;
+  if (!cb || !res || !codes_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  float* d_res = nullptr;
+  float* d_cb = nullptr;
+  uint8_t* d_codes = nullptr;
+  const size_t cb_floats = (size_t)MVR_PQ_CENTROIDS * dim;
+  MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, n * dim * sizeof(float), (void**)&d_res));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, cb_floats * sizeof(float), (void**)&d_cb));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotCodes, n * pq_m, (void**)&d_codes));
+  MVR_TRY(mvr::h2d(c, d_cb, cb, cb_floats * sizeof(float)));
+  MVR_TRY(mvr::h2d(c, d_res, res, n * dim * sizeof(float)));
+  MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes));
+  MVR_TRY(mvr::d2h(c, codes_out, d_codes, n * pq_m));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MVR_OK;
+}
+
+int mvr_pq_decode(const float* cb, uint32_t dim, uint32_t pq_m, const uint8_t* codes, uint64_t n,
+                  float* out) {
+  if (dim == 0) return MVR_E_DIM_MISMATCH;
+  if (pq_m == 0 || dim % pq_m != 0) return MVR_E_DIM_NOT_DIVISIBLE_BY_M;
+  if (n == 0) return MVR_OK;
+  if (!cb || !codes || !out) return MVR_E_INVALID_ARGUMENT;
+  const uint32_t s = dim / pq_m;
+  for (uint64_t i = 0; i < n; ++i)
+    for (uint32_t m = 0; m < pq_m; ++m)
+      std::memcpy(out + i * dim + (uint64_t)m * s,
+                  cb + ((uint64_t)m * MVR_PQ_CENTROIDS + codes[i * pq_m + m]) * s, sizeof(float) * s);
+  return MVR_OK;
+}
+
+// ---- kmeans.fit -----------------------------------------------------------
+
+int mvr_kmeans_fit(mvr_ctx* h, const float* vectors, uint64_t len, uint32_t dim, uint32_t k,
+                   uint32_t max_iters, float tol, uint64_t seed, uint32_t n_threads,
+                   float* centroids_out, uint32_t* assignments_out, float* wcss_out,
+                   uint32_t* iters_out) {
+  (void)n_threads;
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  // kmeans.fit validation order (src/tac/kmeans.zig:73-76)
+  if (k == 0) return mvr::fail(c, MVR_E_KMEANS_BUDGET_TOO_SMALL, "k == 0");
+  if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (len == 0) return mvr::fail(c, MVR_E_EMPTY_VECTOR_SET, "no vectors");
+  if (len % dim != 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "vectors_len % dim != 0");
+  if (!vectors || !centroids_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  const uint64_t n = len / dim;
+  float* d_v = nullptr;
+  float* d_cent = nullptr;
+  uint32_t* d_asg = nullptr;
+  MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, len * sizeof(float), (void**)&d_v));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, (size_t)k * dim * sizeof(float), (void**)&d_cent));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotAux0, n * sizeof(uint32_t), (void**)&d_asg));
+  MVR_TRY(mvr::h2d(c, d_v, vectors, len * sizeof(float)));
+  float wcss = 0.f;
+  uint32_t iters = 0;
+  if ((dim == 1 || dim == 2 || dim == 4) && k <= 256) {
+    mvr::PqJob job;
+    job.R = d_v;
+    job.N = n;
+    job.D = (int)dim;
+    job.M = 1;
+    job.S = (int)dim;
+    job.K = (int)k;
+    job.seed = seed;
+    job.max_iters = max_iters;
+    job.tol = tol;
+    mvr::PqOut out;
+    out.d_codebooks = d_cent;
+    out.d_assign = d_asg;
+    out.h_wcss = &wcss;
+    out.h_iters = &iters;
+    MVR_TRY(mvr::pq_kmeans_device(c, job, out));
+  } else {
+    MVR_TRY(mvr::kmeans_general_device(c, d_v, n, dim, k, max_iters, tol, seed, d_cent, d_asg, &wcss, &iters));
+  }
+  MVR_TRY(mvr::d2h(c, centroids_out, d_cent, (size_t)k * dim * sizeof(float)));
+  if (assignments_out) MVR_TRY(mvr::d2h(c, assignments_out, d_asg, n * sizeof(uint32_t)));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  if (wcss_out) *wcss_out = wcss;
+  if (iters_out) *iters_out = iters;
+  return MVR_OK;
+}
+
+// ---- residuals ------------------------------------------------------------
+
+int mvr_residuals_norms_device(mvr_ctx* h, const float* d_v, const float* d_cent, uint32_t kappa,
+                               const uint32_t* d_asg, uint64_t n, uint32_t dim, float* d_res,
+                               float* d_norms) {
+  (void)kappa;
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  if (n == 0) return MVR_OK;
+  if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (!d_v || !d_cent || !d_asg || !d_res || !d_norms)
+    return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  MVR_TRY(mvr::set_device(c));
+  const int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)c->sm_count * 16);
+  mvr::residuals_norms_kernel<<<grid, 256, 0, c->stream>>>(d_v, d_cent, d_asg, n, dim, d_res, d_norms);
+  MVR_CUDA(c, cudaGetLastError());
+  return MVR_OK;
+}
+
+int mvr_residuals_norms(mvr_ctx* h, const float* v, const float* cent, uint32_t kappa,
+                        const uint32_t* asg, uint64_t n, uint32_t dim, float* res_out,
+                        float* norms_out) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  if (n == 0) return MVR_OK;
+  if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (!v || !cent || !asg || !res_out || !norms_out)
+    return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  for (uint64_t i = 0; i < n; ++i)
+    if (asg[i] >= kappa) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "assignment >= kappa");
+  MVR_TRY(mvr::set_device(c));
+  float *d_v, *d_cent, *d_res, *d_norms;
+  uint32_t* d_asg;
+  MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, n * dim * sizeof(float), (void**)&d_v));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, (size_t)kappa * dim * sizeof(float), (void**)&d_cent));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotAux0, n * sizeof(uint32_t), (void**)&d_asg));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotSorted, n * dim * sizeof(float), (void**)&d_res));
+  MVR_TRY(mvr::scratch(c, mvr::kSlotAux1, n * sizeof(float), (void**)&d_norms));
+  MVR_TRY(mvr::h2d(c, d_v, v, n * dim * sizeof(float)));
+  MVR_TRY(mvr::h2d(c, d_cent, cent, (size_t)kappa * dim * sizeof(float)));
+  MVR_TRY(mvr::h2d(c, d_asg, asg, n * sizeof(uint32_t)));
+  MVR_TRY(mvr_residuals_norms_device(h, d_v, d_cent, kappa, d_asg, n, dim, d_res, d_norms));
+  MVR_TRY(mvr::d2h(c, res_out, d_res, n * dim * sizeof(float)));
+  MVR_TRY(mvr::d2h(c, norms_out, d_norms, n * sizeof(float)));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MVR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+// mvr_internal.h — context, scratch and error plumbing shared by the C-ABI
+// entry points and the kernel launchers. Not part of the public ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/mvr.h"
+
+namespace mvr {
+
+// Device buffer that only grows; freed by the context.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+enum ScratchSlot {
+  kSlotMinDist = 0,  // [M][N] f32: k-means++ D^2 weights, then Lloyd min_to_any
+  kSlotAssign,       // [M][N] u8 / u32 assignments
+  kSlotSorted,       // [M][N][S] f32 rows sorted by cluster (stable)
+  kSlotHist,         // [M][K][nblk] u32 per-block histograms -> scatter bases
+  kSlotChunk,        // [M][nchunk] double2 directed-rounding partial sums
+  kSlotSmall,        // per-subspace bookkeeping (counts, flags, draws ...)
+  kSlotResiduals,    // host-API staging of the input rows
+  kSlotCodebooks,    // host-API staging of codebooks
+  kSlotCodes,        // host-API staging of codes
+  kSlotAux0,
+  kSlotAux1,
+  kSlotAux2,
+  kSlotAux3,
+  kSlotCount
+};
+
+struct Ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string last_error;
+  DevBuf slots[kSlotCount];
+  void* pinned = nullptr;  // host staging for small device->host reads
+  size_t pinned_bytes = 0;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+};
+
+// Set the context's last error and return `status`.
+int fail(Ctx* ctx, int status, const std::string& msg);
+
+// Grow slot `slot` to at least `bytes` (contents are not preserved).
+int scratch(Ctx* ctx, int slot, size_t bytes, void** out);
+
+// Pinned host staging of at least `bytes`.
+int pinned(Ctx* ctx, size_t bytes, void** out);
+
+// Convert a CUDA error into MVR_E_CUDA with context.
+int cuda_fail(Ctx* ctx, cudaError_t e, const char* what);
+
+}  // namespace mvr
+
+struct mvr_ctx {
+  mvr::Ctx impl;
+};
+
+#define MVR_CUDA(ctx, call)                                   \
+  do {                                                        \
+    cudaError_t _e = (call);                                  \
+    if (_e != cudaSuccess) return ::mvr::cuda_fail((ctx), _e, #call); \
+  } while (0)
+
+#define MVR_TRY(expr)              \
+  do {                             \
+    int _s = (expr);               \
+    if (_s != MVR_OK) return _s;   \
+  } while (0)

@@ -1,0 +1,44 @@
+// pq_engine.h — batched k-means over PQ subspaces on one GPU.
+//
+// One "subspace problem" per m in [0, M): the rows R[i][m*S .. m*S+S) of a
+// row-major N x D matrix (D = M*S, S in {1,2,4}), clustered into K <= 256
+// centroids with the reference `kmeans.fit` semantics
+// (src/tac/kmeans.zig:67-232) and the PQ per-subspace seed `seed +% m`
+// (src/index/pq.zig:319-325). `mvr_kmeans_fit` for small dims is the M = 1
+// case of the same engine.
+#pragma once
+#include <cstdint>
+
+#include "mvr_internal.h"
+
+namespace mvr {
+
+struct PqJob {
+  const float* R = nullptr;  // device, N x D row-major, 4-byte aligned
+  uint64_t N = 0;
+  int D = 0;
+  int M = 0;
+  int S = 0;
+  int K = 256;
+  uint64_t seed = 0;  // subspace m uses seed + m
+  uint32_t max_iters = 25;
+  float tol = 1e-4f;
+};
+
+struct PqOut {
+  float* d_codebooks = nullptr;    // device [M][K][S] (required)
+  uint32_t* d_assign = nullptr;    // device [M][N] final assignments (optional)
+  float* h_wcss = nullptr;         // host [M] final WCSS (optional)
+  uint32_t* h_iters = nullptr;     // host [M] iterations run (optional)
+  mvr_pq_train_stats* stats = nullptr;
+};
+
+// Runs seeding + Lloyd for all M subspaces; returns the MVR status of the
+// smallest failing subspace, or MVR_OK. Synchronises the context stream.
+int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out);
+
+// PQ.encode of N rows (asynchronous on the context stream).
+int pq_encode_device(Ctx* ctx, const float* d_codebooks, int D, int M,
+                     const float* d_R, uint64_t N, uint8_t* d_codes);
+
+}  // namespace mvr

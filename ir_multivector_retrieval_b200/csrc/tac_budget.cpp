@@ -1,0 +1,171 @@
+// tac_budget.cpp — TAC budget phases 1-4 (host integer/float logic).
+//
+// Reference: src/tac/tac.zig:80-402 (classifyToken, allocateTail,
+// dampedWeight, dampedPhase2, boundPhase3, reconcilePhase4,
+// allocateBudgets). O(vocabulary) work that runs once per build between the
+// device spread pass and the device per-token k-means.
+#include <cmath>
+#include <cstdint>
+#include <vector>
+
+#include "../../include/mvr.h"
+#include "tac_engine.h"
+
+namespace mvr {
+namespace {
+
+enum Tier { kEmpty, kMicro, kSmall, kActive };
+
+inline Tier classify(uint32_t n, uint32_t mu, uint32_t tau) {
+  if (n == 0) return kEmpty;
+  if (n < mu) return kMicro;
+  if (n < tau) return kSmall;
+  return kActive;
+}
+
+}  // namespace
+
+int tac_allocate_budgets_host(const uint32_t* freqs, const float* spreads, uint32_t* kappa,
+                              float* frac, uint64_t n, uint32_t kappa_total, uint32_t mu,
+                              uint32_t tau, uint32_t eps, uint32_t theta) {
+  // Phase 1 — tail (tac.zig:97-125)
+  if (mu == 0 || tau == 0 || mu >= tau) return MVR_E_INVALID_THRESHOLDS;
+  uint32_t tail = 0;
+  for (uint64_t j = 0; j < n; ++j) {
+    switch (classify(freqs[j], mu, tau)) {
+      case kMicro: kappa[j] = 1; tail += 1; break;
+      case kSmall: kappa[j] = 2; tail += 2; break;
+      default: kappa[j] = 0; break;
+    }
+  }
+  if (tail > kappa_total) return MVR_E_BUDGET_TOO_SMALL;
+  const uint32_t budget = kappa_total - tail;
+
+  // Phase 2 — damped proportional allocation (tac.zig:157-210)
+  for (uint64_t j = 0; j < n; ++j) frac[j] = 0.f;
+  double sum_w = 0.0;
+  uint32_t n_active = 0;
+  for (uint64_t j = 0; j < n; ++j) {
+    if (classify(freqs[j], mu, tau) != kActive) continue;
+    const float w = std::sqrt((float)freqs[j]) * spreads[j];
+    if (!std::isfinite(w) || w < 0.f) return MVR_E_INVALID_THRESHOLDS;
+    sum_w += (double)w;
+    ++n_active;
+  }
+  if (n_active > 0) {
+    if (sum_w <= 0.0) {
+      const uint32_t base = budget / n_active;
+      uint32_t left = budget - base * n_active;
+      for (uint64_t j = 0; j < n; ++j) {
+        if (classify(freqs[j], mu, tau) != kActive) continue;
+        kappa[j] = base + (left > 0 ? 1u : 0u);
+        if (left > 0) --left;
+      }
+    } else {
+      const double bf = (double)budget;
+      for (uint64_t j = 0; j < n; ++j) {
+        if (classify(freqs[j], mu, tau) != kActive) continue;
+        const double w = (double)(std::sqrt((float)freqs[j]) * spreads[j]);
+        const double target = (w / sum_w) * bf;
+        const uint32_t fl = (uint32_t)std::floor(target);
+        kappa[j] = fl;
+        frac[j] = (float)(target - (double)fl);
+      }
+    }
+  }
+
+  // Phase 3 — floor and cap (tac.zig:228-248)
+  if (eps == 0 || theta == 0) return MVR_E_INVALID_THRESHOLDS;
+  if ((uint64_t)tau < (uint64_t)eps * theta) return MVR_E_INVALID_THRESHOLDS;
+  for (uint64_t j = 0; j < n; ++j) {
+    if (classify(freqs[j], mu, tau) != kActive) continue;
+    const uint32_t cap = freqs[j] / theta;
+    if (kappa[j] < eps) kappa[j] = eps;
+    if (kappa[j] > cap) kappa[j] = cap;
+  }
+
+  // Phase 4 — largest-remainder reconciliation (tac.zig:281-376)
+  uint64_t cur = 0;
+  for (uint64_t j = 0; j < n; ++j) cur += kappa[j];
+  if (cur == kappa_total) return MVR_OK;
+  if (cur < kappa_total) {
+    uint32_t remaining = (uint32_t)(kappa_total - cur);
+    while (remaining > 0) {
+      int64_t best = -1;
+      float bf = -INFINITY;
+      for (uint64_t j = 0; j < n; ++j) {
+        if (classify(freqs[j], mu, tau) != kActive) continue;
+        if (kappa[j] >= freqs[j] / theta) continue;
+        if (frac[j] > bf || (frac[j] == bf && best < 0)) {
+          best = (int64_t)j;
+          bf = frac[j];
+        }
+      }
+      if (best < 0) return MVR_E_BUDGET_TOO_LARGE;
+      ++kappa[best];
+      --remaining;
+    }
+    return MVR_OK;
+  }
+  uint32_t excess = (uint32_t)(cur - kappa_total);
+  while (excess > 0) {
+    int64_t best = -1;
+    float bf = INFINITY;
+    for (uint64_t j = 0; j < n; ++j) {
+      if (classify(freqs[j], mu, tau) != kActive || kappa[j] <= eps) continue;
+      if (frac[j] < bf) {
+        best = (int64_t)j;
+        bf = frac[j];
+      }
+    }
+    if (best >= 0) {
+      --kappa[best];
+      --excess;
+      continue;
+    }
+    int64_t found = -1;
+    for (uint64_t j = 0; j < n && found < 0; ++j)
+      if (classify(freqs[j], mu, tau) == kSmall && kappa[j] == 2) found = (int64_t)j;
+    if (found >= 0) {
+      kappa[found] = 1;
+      --excess;
+      continue;
+    }
+    for (uint64_t j = 0; j < n && found < 0; ++j)
+      if (classify(freqs[j], mu, tau) == kMicro && kappa[j] == 1) found = (int64_t)j;
+    if (found >= 0) {
+      kappa[found] = 0;
+      --excess;
+      continue;
+    }
+    return MVR_E_BUDGET_TOO_SMALL;
+  }
+  return MVR_OK;
+}
+
+}  // namespace mvr
+
+extern "C" {
+
+void mvr_clustering_params_default(mvr_clustering_params* p, uint32_t kappa_total, uint64_t seed) {
+  if (!p) return;
+  p->kappa_total = kappa_total;
+  p->mu = 128;   // constants.TAC_MU
+  p->tau = 256;  // constants.TAC_TAU
+  p->epsilon = 4;
+  p->theta = 39;
+  p->max_iters = 25;
+  p->tol = 1e-4f;
+  p->seed = seed;
+  p->n_threads = 1;
+}
+
+int mvr_tac_allocate_budgets(const uint32_t* freqs, const float* spreads, uint32_t* kappa,
+                             float* frac, uint64_t n, uint32_t kappa_total,
+                             const mvr_clustering_params* p) {
+  if (!p || (n > 0 && (!freqs || !spreads || !kappa || !frac))) return MVR_E_INVALID_ARGUMENT;
+  return mvr::tac_allocate_budgets_host(freqs, spreads, kappa, frac, n, kappa_total, p->mu, p->tau,
+                                        p->epsilon, p->theta);
+}
+
+}  // extern "C"

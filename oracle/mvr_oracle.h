@@ -1,0 +1,96 @@
+/*
+ * mvr_oracle.h — CPU restatement of the reference build path, used ONLY as
+ * the parity checker in tests/, in __graft_entry__.smoke() and as the timed
+ * CPU baseline in bench.py. Nothing in the product links or calls it.
+ *
+ * Every function follows a reference function (BleedingDev/
+ * ir-multivector-retrieval, Zig), cited as path:line beside its body in
+ * mvr_oracle.c. Status codes are the MVR_* values of include/mvr.h.
+ */
+#ifndef MVR_ORACLE_H
+#define MVR_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Order of the final 4-lane `@reduce(.Add)` in vec.l2sq for len 64/128.
+ * 0: ((a0+a1)+a2)+a3 (LLVM ordered reduction, the strict-mode lowering);
+ * 1: (a0+a1)+(a2+a3) (tree). Default 0. */
+void orc_set_reduce_tree(int tree);
+/* Lane count of vec.l2sqGeneric (`std.simd.suggestVectorLength(f32)`,
+ * 4 on the reference's Apple NEON hosts). Default 4. */
+void orc_set_lane_count(int lanes);
+
+float orc_l2sq(const float* a, const float* b, uint32_t len);
+int64_t orc_argmin(const float* v, uint64_t n);
+int64_t orc_argmax(const float* v, uint64_t n);
+
+typedef struct orc_rng {
+  uint64_t s[4];
+} orc_rng;
+void orc_rng_init(orc_rng* r, uint64_t seed);
+uint64_t orc_rng_next(orc_rng* r);
+uint64_t orc_rng_index(orc_rng* r, uint64_t n);
+double orc_rng_f64(orc_rng* r);
+float orc_rng_f32(orc_rng* r);
+int orc_weighted_sample(orc_rng* r, const float* w, uint64_t n, uint64_t* out);
+
+int orc_kmeans_fit(const float* vectors, uint64_t vectors_len, uint32_t dim,
+                   uint32_t k, uint32_t max_iters, float tol, uint64_t seed,
+                   uint32_t n_threads, float* centroids, uint32_t* assignments,
+                   float* wcss, uint32_t* iters_run, uint32_t* trace);
+
+int orc_pq_train(const float* residuals, uint64_t residuals_len, uint32_t dim,
+                 uint64_t seed, uint32_t n_threads, uint32_t pq_m,
+                 uint32_t max_iters, float tol, float* codebooks);
+int orc_pq_encode(const float* codebooks, uint32_t dim, uint32_t pq_m,
+                  const float* residuals, uint64_t n, uint8_t* codes,
+                  uint32_t n_threads);
+/* Timing helper for the CPU baseline: `iters` Lloyd iterations of every
+ * subspace starting from the given codebooks (no seeding), subspaces spread
+ * over n_threads like pq.train's work-stealing loop. */
+int orc_pq_lloyd_iters(const float* residuals, uint64_t n, uint32_t dim,
+                       uint32_t pq_m, uint32_t iters, uint32_t n_threads,
+                       float* codebooks_inout);
+
+int orc_residuals_norms(const float* vectors, const float* centroids,
+                        const uint32_t* assignments, uint64_t n, uint32_t dim,
+                        float* residuals, float* norms);
+
+int orc_tac_allocate_tail(const uint32_t* freqs, uint32_t* kappa, uint64_t n,
+                          uint32_t mu, uint32_t tau, uint32_t kappa_total,
+                          uint32_t* budget_out);
+int orc_tac_damped_phase2(const uint32_t* freqs, const float* spreads,
+                          uint32_t* kappa, float* frac, uint64_t n,
+                          uint32_t budget_active, uint32_t mu, uint32_t tau);
+int orc_tac_bound_phase3(const uint32_t* freqs, uint32_t* kappa, uint64_t n,
+                         uint32_t mu, uint32_t tau, uint32_t epsilon,
+                         uint32_t theta);
+int orc_tac_reconcile_phase4(const uint32_t* freqs, uint32_t* kappa,
+                             const float* frac, uint64_t n,
+                             uint32_t kappa_total, uint32_t mu, uint32_t tau,
+                             uint32_t epsilon, uint32_t theta);
+int orc_tac_allocate_budgets(const uint32_t* freqs, const float* spreads,
+                             uint32_t* kappa, float* frac, uint64_t n,
+                             uint32_t kappa_total, uint32_t mu, uint32_t tau,
+                             uint32_t epsilon, uint32_t theta);
+int orc_tac_spreads(const uint32_t* token_ids, uint64_t n_tokens,
+                    const float* vectors, uint32_t dim, uint64_t n_distinct,
+                    uint32_t* freqs_out, float* spreads_out);
+int orc_tac_cluster_flat(const uint32_t* token_ids, uint64_t n_tokens,
+                         const float* vectors, uint64_t vectors_len,
+                         uint32_t dim, uint32_t kappa_total, uint32_t mu,
+                         uint32_t tau, uint32_t epsilon, uint32_t theta,
+                         uint32_t max_iters, float tol, uint64_t seed,
+                         uint32_t n_threads, float* centroids,
+                         uint32_t* assignments, uint32_t* kappa_per_token,
+                         uint64_t kappa_cap, uint64_t* n_distinct_out,
+                         float* wcss_total);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

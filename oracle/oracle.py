@@ -1,0 +1,296 @@
+"""ctypes binding of the CPU parity oracle (``oracle/libmvr_oracle.so``).
+
+TEST INFRASTRUCTURE ONLY. Imported by tests/, ``__graft_entry__.smoke()``
+and the CPU-baseline leg of ``bench.py`` — never by the product package.
+The oracle restates the reference's algorithm in plain C (see the header of
+``mvr_oracle.c`` for what is pinned and what is not).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+import threading
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "libmvr_oracle.so"
+_lock = threading.Lock()
+_lib = None
+
+_P = C.c_void_p
+
+
+class OracleError(Exception):
+    def __init__(self, code: int, what: str = ""):
+        self.code = code
+        super().__init__(f"oracle status {code} {what}")
+
+
+def build(force: bool = False) -> Path:
+    srcs = [HERE / "mvr_oracle.c", HERE / "mvr_oracle.h", HERE.parent / "include" / "mvr.h"]
+    if force or not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in srcs):
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB
+
+
+def load() -> C.CDLL:
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB.exists():
+                build()
+            lib = C.CDLL(str(LIB))
+            sig = {
+                "orc_set_reduce_tree": (None, [C.c_int]),
+                "orc_set_lane_count": (None, [C.c_int]),
+                "orc_l2sq": (C.c_float, [_P, _P, C.c_uint32]),
+                "orc_argmin": (C.c_int64, [_P, C.c_uint64]),
+                "orc_argmax": (C.c_int64, [_P, C.c_uint64]),
+                "orc_rng_init": (None, [_P, C.c_uint64]),
+                "orc_rng_next": (C.c_uint64, [_P]),
+                "orc_rng_index": (C.c_uint64, [_P, C.c_uint64]),
+                "orc_rng_f64": (C.c_double, [_P]),
+                "orc_rng_f32": (C.c_float, [_P]),
+                "orc_weighted_sample": (C.c_int, [_P, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+                "orc_kmeans_fit": (C.c_int, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+                                             C.c_float, C.c_uint64, C.c_uint32, _P, _P, _P, _P, _P]),
+                "orc_pq_train": (C.c_int, [_P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32,
+                                           C.c_uint32, C.c_uint32, C.c_float, _P]),
+                "orc_pq_encode": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_uint64, _P, C.c_uint32]),
+                "orc_pq_lloyd_iters": (C.c_int, [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+                                                 C.c_uint32, _P]),
+                "orc_residuals_norms": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P, _P]),
+                "orc_tac_allocate_tail": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32,
+                                                    C.c_uint32, C.POINTER(C.c_uint32)]),
+                "orc_tac_damped_phase2": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint32,
+                                                    C.c_uint32, C.c_uint32]),
+                "orc_tac_bound_phase3": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32,
+                                                   C.c_uint32, C.c_uint32]),
+                "orc_tac_reconcile_phase4": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, C.c_uint32,
+                                                       C.c_uint32, C.c_uint32, C.c_uint32]),
+                "orc_tac_allocate_budgets": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint32,
+                                                       C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+                "orc_tac_spreads": (C.c_int, [_P, C.c_uint64, _P, C.c_uint32, C.c_uint64, _P, _P]),
+                "orc_tac_cluster_flat": (C.c_int, [_P, C.c_uint64, _P, C.c_uint64, C.c_uint32,
+                                                   C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                                   C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,
+                                                   C.c_uint32, _P, _P, _P, C.c_uint64,
+                                                   C.POINTER(C.c_uint64), C.POINTER(C.c_float)]),
+            }
+            for name, (res, args) in sig.items():
+                f = getattr(lib, name)
+                f.restype = res
+                f.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def _p(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint32).reshape(-1)
+
+
+def set_reduce_tree(tree: bool) -> None:
+    load().orc_set_reduce_tree(1 if tree else 0)
+
+
+def set_lane_count(n: int) -> None:
+    load().orc_set_lane_count(int(n))
+
+
+def l2sq(a, b) -> float:
+    a, b = _f32(a), _f32(b)
+    assert a.size == b.size
+    return float(np.float32(load().orc_l2sq(_p(a), _p(b), a.size)))
+
+
+def argmin(v) -> int:
+    v = _f32(v)
+    return int(load().orc_argmin(_p(v), v.size))
+
+
+def argmax(v) -> int:
+    v = _f32(v)
+    return int(load().orc_argmax(_p(v), v.size))
+
+
+class Rng:
+    """Restated Zig ``std.Random.DefaultPrng`` (Xoshiro256++)."""
+
+    def __init__(self, seed: int):
+        self.state = (C.c_uint64 * 4)()
+        load().orc_rng_init(self.state, seed & (2**64 - 1))
+
+    def next(self) -> int:
+        return int(load().orc_rng_next(self.state))
+
+    def index(self, n: int) -> int:
+        return int(load().orc_rng_index(self.state, n))
+
+    def f64(self) -> float:
+        return float(load().orc_rng_f64(self.state))
+
+    def f32(self) -> float:
+        return float(load().orc_rng_f32(self.state))
+
+    def weighted_sample(self, w) -> int:
+        w = _f32(w)
+        out = C.c_uint64(0)
+        st = load().orc_weighted_sample(self.state, _p(w), w.size, C.byref(out))
+        if st:
+            raise OracleError(st, "weighted_sample")
+        return int(out.value)
+
+
+@dataclass
+class KMeansResult:
+    centroids: np.ndarray
+    assignments: np.ndarray
+    wcss: float
+    iters_run: int
+    trace: np.ndarray | None = None
+
+
+def kmeans_fit(vectors, dim: int, k: int, seed: int, max_iters: int = 25, tol: float = 1e-4,
+               n_threads: int = 1, trace: bool = False) -> KMeansResult:
+    v = _f32(vectors)
+    n = v.size // dim if dim else 0
+    cent = np.zeros(max(k, 1) * max(dim, 1), dtype=np.float32)
+    asg = np.zeros(max(n, 1), dtype=np.uint32)
+    tr = np.zeros(max(max_iters, 1) * max(n, 1), dtype=np.uint32) if trace else None
+    w = C.c_float(0)
+    it = C.c_uint32(0)
+    st = load().orc_kmeans_fit(_p(v), v.size, dim, k, max_iters, C.c_float(tol), seed & (2**64 - 1),
+                               n_threads, _p(cent), _p(asg), C.byref(w), C.byref(it),
+                               _p(tr) if tr is not None else None)
+    if st:
+        raise OracleError(st, "kmeans_fit")
+    return KMeansResult(cent[: k * dim], asg[:n], float(w.value), int(it.value),
+                        tr.reshape(max_iters, n)[: it.value] if tr is not None else None)
+
+
+def pq_train(residuals, dim: int, seed: int, pq_m: int, n_threads: int = 1, max_iters: int = 25,
+             tol: float = 1e-4) -> np.ndarray:
+    r = _f32(residuals)
+    s = dim // pq_m if pq_m and dim % pq_m == 0 else 1
+    cb = np.zeros(max(pq_m, 1) * 256 * s, dtype=np.float32)
+    st = load().orc_pq_train(_p(r), r.size, dim, seed & (2**64 - 1), n_threads, pq_m, max_iters,
+                             C.c_float(tol), _p(cb))
+    if st:
+        raise OracleError(st, "pq_train")
+    return cb
+
+
+def pq_encode(codebooks, dim: int, pq_m: int, residuals, n_threads: int = 1) -> np.ndarray:
+    r = _f32(residuals)
+    n = r.size // dim
+    out = np.zeros((n, pq_m), dtype=np.uint8)
+    st = load().orc_pq_encode(_p(_f32(codebooks)), dim, pq_m, _p(r), n, _p(out), n_threads)
+    if st:
+        raise OracleError(st, "pq_encode")
+    return out
+
+
+def pq_lloyd_iters(residuals, dim: int, pq_m: int, iters: int, n_threads: int, codebooks) -> np.ndarray:
+    r = _f32(residuals)
+    cb = _f32(codebooks).copy()
+    st = load().orc_pq_lloyd_iters(_p(r), r.size // dim, dim, pq_m, iters, n_threads, _p(cb))
+    if st:
+        raise OracleError(st, "pq_lloyd_iters")
+    return cb
+
+
+def residuals_norms(vectors, centroids, assignments, dim: int):
+    v = _f32(vectors)
+    n = v.size // dim
+    res = np.zeros(n * dim, dtype=np.float32)
+    norms = np.zeros(n, dtype=np.float32)
+    load().orc_residuals_norms(_p(v), _p(_f32(centroids)), _p(_u32(assignments)), n, dim, _p(res), _p(norms))
+    return res, norms
+
+
+def _check(st, what):
+    if st:
+        raise OracleError(st, what)
+
+
+def tac_allocate_tail(freqs, kappa_total, mu, tau):
+    f = _u32(freqs)
+    k = np.zeros(f.size, dtype=np.uint32)
+    b = C.c_uint32(0)
+    _check(load().orc_tac_allocate_tail(_p(f), _p(k), f.size, mu, tau, kappa_total, C.byref(b)), "tail")
+    return k, int(b.value)
+
+
+def tac_damped_phase2(freqs, spreads, kappa, budget, mu, tau):
+    f, s, k = _u32(freqs), _f32(spreads), _u32(kappa).copy()
+    frac = np.zeros(f.size, dtype=np.float32)
+    _check(load().orc_tac_damped_phase2(_p(f), _p(s), _p(k), _p(frac), f.size, budget, mu, tau), "phase2")
+    return k, frac
+
+
+def tac_bound_phase3(freqs, kappa, mu, tau, eps, theta):
+    f, k = _u32(freqs), _u32(kappa).copy()
+    _check(load().orc_tac_bound_phase3(_p(f), _p(k), f.size, mu, tau, eps, theta), "phase3")
+    return k
+
+
+def tac_reconcile_phase4(freqs, kappa, frac, kappa_total, mu, tau, eps, theta):
+    f, k, fr = _u32(freqs), _u32(kappa).copy(), _f32(frac)
+    _check(load().orc_tac_reconcile_phase4(_p(f), _p(k), _p(fr), f.size, kappa_total, mu, tau, eps, theta),
+           "phase4")
+    return k
+
+
+def tac_allocate_budgets(freqs, spreads, kappa_total, mu=128, tau=256, eps=4, theta=39):
+    f, s = _u32(freqs), _f32(spreads)
+    k = np.zeros(f.size, dtype=np.uint32)
+    frac = np.zeros(f.size, dtype=np.float32)
+    _check(load().orc_tac_allocate_budgets(_p(f), _p(s), _p(k), _p(frac), f.size, kappa_total, mu, tau,
+                                           eps, theta), "allocate_budgets")
+    return k
+
+
+def tac_spreads(token_ids, vectors, dim: int):
+    ids = _u32(token_ids)
+    v = _f32(vectors)
+    nd = int(ids.max()) + 1
+    freqs = np.zeros(nd, dtype=np.uint32)
+    spreads = np.zeros(nd, dtype=np.float32)
+    load().orc_tac_spreads(_p(ids), ids.size, _p(v), dim, nd, _p(freqs), _p(spreads))
+    return freqs, spreads
+
+
+@dataclass
+class ClusterResult:
+    centroids: np.ndarray
+    assignments: np.ndarray
+    kappa_per_token: np.ndarray
+    wcss_total: float
+
+
+def tac_cluster_flat(token_ids, vectors, dim: int, kappa_total: int, seed: int, mu=128, tau=256,
+                     eps=4, theta=39, max_iters=25, tol=1e-4, n_threads=1) -> ClusterResult:
+    ids = _u32(token_ids)
+    v = _f32(vectors)
+    nd = int(ids.max()) + 1 if ids.size else 1
+    cent = np.zeros(max(kappa_total, 1) * max(dim, 1), dtype=np.float32)
+    asg = np.zeros(max(ids.size, 1), dtype=np.uint32)
+    kap = np.zeros(nd, dtype=np.uint32)
+    ndo = C.c_uint64(0)
+    w = C.c_float(0)
+    _check(load().orc_tac_cluster_flat(_p(ids), ids.size, _p(v), v.size, dim, kappa_total, mu, tau, eps,
+                                       theta, max_iters, C.c_float(tol), seed & (2**64 - 1), n_threads,
+                                       _p(cent), _p(asg), _p(kap), nd, C.byref(ndo), C.byref(w)),
+           "cluster_flat")
+    return ClusterResult(cent[: kappa_total * dim], asg[: ids.size], kap, float(w.value))

@@ -1,0 +1,199 @@
+"""GPU parity of PQ encode / pq.train / kmeans.fit against the CPU oracle.
+
+Bar: bit-exact. Codes and assignments are integers (exact equality); codebooks,
+centroids and WCSS are compared byte for byte, which is stricter than the
+1e-5 relative tolerance the specification allows for trained codebooks.
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+
+from ir_multivector_retrieval_b200 import kmeans, pq, synth
+from ir_multivector_retrieval_b200._lib import MvrError
+
+pytestmark = pytest.mark.gpu
+THREADS = max(1, os.cpu_count() or 1)
+
+
+def _rows(n, dim, seed):
+    return synth.unit_rows(n, dim, seed)
+
+
+@pytest.mark.parametrize("dim,m", [(64, 16), (64, 32), (32, 32), (128, 32), (12, 3), (8, 8)])
+def test_encode_bitexact(ctx, orc, dim, m):
+    rng = np.random.default_rng(dim * 100 + m)
+    cb = rng.standard_normal(m * 256 * (dim // m)).astype(np.float32)
+    x = _rows(10_007, dim, seed=m)
+    p = pq.PQ(dim=dim, sub_dim=dim // m, codebooks=cb, pq_m=m, ctx=ctx)
+    got = p.encode_batch(x)
+    want = orc.pq_encode(cb, dim, m, x, n_threads=THREADS)
+    assert np.array_equal(got, want)
+    assert np.array_equal(p.encode(x[5]), want[5])
+
+
+def test_encode_ties_and_exact_codewords(ctx, orc):
+    rng = np.random.default_rng(3)
+    cb = rng.standard_normal(16 * 256 * 4).astype(np.float32).reshape(16, 256, 4)
+    cb[:, 200] = cb[:, 5]  # duplicate codeword: the first index must win
+    cb[:, 17] = cb[:, 16]
+    cb = cb.reshape(-1)
+    p = pq.PQ(dim=64, sub_dim=4, codebooks=cb, pq_m=16, ctx=ctx)
+    codes = rng.integers(0, 256, size=(4096, 16), dtype=np.uint8)
+    x = p.decode(codes)
+    got = p.encode_batch(x)
+    want = orc.pq_encode(cb, 64, 16, x, n_threads=THREADS)
+    assert np.array_equal(got, want)
+    assert not np.any(got == 200) and not np.any(got == 17)
+    # idempotence: encode(decode(c)) == c where codewords are distinct
+    assert np.array_equal(p.encode_batch(p.decode(got)), got)
+
+
+def test_encode_nonfinite_rows(ctx, orc):
+    rng = np.random.default_rng(4)
+    cb = rng.standard_normal(16 * 256 * 4).astype(np.float32)
+    x = _rows(600, 64, 9)
+    x[3, 5] = np.nan
+    x[7, :] = np.inf
+    x[11, 0:4] = -np.inf
+    cbn = cb.copy()
+    cbn[4 * 3] = np.nan  # codeword 3 of subspace 0 has a NaN
+    for c in (cb, cbn):
+        got = pq.PQ(dim=64, sub_dim=4, codebooks=c, pq_m=16, ctx=ctx).encode_batch(x)
+        assert np.array_equal(got, orc.pq_encode(c, 64, 16, x))
+
+
+def test_encode_errors(ctx):
+    p = pq.PQ(dim=64, sub_dim=4, codebooks=np.zeros(16 * 256 * 4, np.float32), pq_m=16, ctx=ctx)
+    with pytest.raises(MvrError) as e:
+        p.encode(np.zeros(63, np.float32))
+    assert e.value.name == "DimMismatch"
+    assert p.encode_batch(np.zeros((0, 64), np.float32)).shape == (0, 16)
+
+
+@pytest.mark.parametrize("dim,m,n,iters,tol", [
+    (64, 16, 6000, 20, -math.inf),
+    (64, 16, 6000, 25, 1e-4),
+    (64, 32, 5000, 25, 1e-4),
+    (32, 32, 3000, 25, 1e-4),
+    (128, 32, 2500, 10, -math.inf),
+    (12, 3, 4096, 25, 1e-4),
+])
+def test_pq_train_bitexact(ctx, orc, dim, m, n, iters, tol):
+    x = _rows(n, dim, seed=n + m)
+    stats = {}
+    got = pq.train(x, dim, 0xA1B2C3D4 + 42, 1, pq_m=m, max_iters=iters, tol=tol, ctx=ctx, stats=stats)
+    want = orc.pq_train(x, dim, 0xA1B2C3D4 + 42, m, n_threads=THREADS, max_iters=iters, tol=tol)
+    assert got.codebooks.tobytes() == want.tobytes()
+    assert stats["iters_max"] <= iters
+    if tol == -math.inf:
+        assert stats["iters_min"] == iters
+
+
+@pytest.mark.parametrize("n", [1, 200, 256, 257, 300])
+def test_pq_train_small_corpora(ctx, orc, n):
+    x = _rows(n, 64, seed=n)
+    got = pq.train(x, 64, 7, pq_m=16, ctx=ctx)
+    assert got.codebooks.tobytes() == orc.pq_train(x, 64, 7, 16).tobytes()
+
+
+def test_pq_train_errors(ctx):
+    for args, name in (((np.zeros(33, np.float32), 33), "DimNotDivisibleByM"),
+                       ((np.zeros(0, np.float32), 32), "EmptyCorpus"),
+                       ((np.zeros(65, np.float32), 64), "DimMismatch")):
+        with pytest.raises(MvrError) as e:
+            pq.train(args[0], args[1], 1, pq_m=32 if args[1] != 64 else 16, ctx=ctx)
+        assert e.value.name == name
+    # fewer distinct sub-vectors than 256 with n > 256: k-means++ runs out of
+    # positive weights, weightedSample -> AllZero (src/util/rng.zig:65)
+    x = np.tile(_rows(10, 64, 1), (40, 1))
+    with pytest.raises(MvrError) as e:
+        pq.train(x, 64, 1, pq_m=16, ctx=ctx)
+    assert e.value.name == "AllZero"
+    x = _rows(400, 64, 2)
+    x[17, 3] = np.nan
+    with pytest.raises(MvrError) as e:
+        pq.train(x, 64, 1, pq_m=16, ctx=ctx)
+    assert e.value.name == "NonFinite"
+
+
+@pytest.mark.parametrize("dim", [1, 2, 4])
+@pytest.mark.parametrize("k", [1, 2, 7, 64, 256])
+def test_kmeans_fit_bitexact(ctx, orc, dim, k):
+    x = np.random.default_rng(dim * 1000 + k).standard_normal(3000 * dim).astype(np.float32)
+    for iters, tol in ((25, 1e-4), (12, 0.0), (7, -math.inf)):
+        got = kmeans.fit(x, dim, kmeans.KMeansParams(k=k, seed=99 + k, max_iters=iters, tol=tol), ctx=ctx)
+        want = orc.kmeans_fit(x, dim, k, 99 + k, max_iters=iters, tol=tol, n_threads=THREADS)
+        assert got.centroids.tobytes() == want.centroids.tobytes()
+        assert np.array_equal(got.assignments, want.assignments)
+        assert got.iters_run == want.iters_run
+        assert np.float32(got.wcss).tobytes() == np.float32(want.wcss).tobytes()
+
+
+def test_kmeans_reference_fixtures(ctx, orc):
+    # blobs (src/tac/kmeans.zig:409-447), collinear reseed (:535-543),
+    # early break (:666-708), degenerate k >= n (:391-407)
+    centers = [(0, 0), (10, 0), (0, 10)]
+    off = [(-0.05, 0.02), (0.03, -0.04), (-0.01, -0.02), (0.02, 0.05), (-0.03, 0.01), (0.04, -0.03)]
+    pts = np.array([(c[0] + o[0], c[1] + o[1]) for c in centers for o in off], np.float32)
+    cases = [(pts, 2, 3, 42, 50), (np.array([0, 0, 0.0001, 0, 100, 0], np.float32), 2, 3, 1, 10),
+             (np.array([1, 0, 0, 1], np.float32), 2, 4, 0, 25), (np.array([1, 0, 0, 1, 1, 1], np.float32), 2, 3, 0, 25)]
+    for x, dim, k, seed, iters in cases:
+        got = kmeans.fit(x, dim, kmeans.KMeansParams(k=k, seed=seed, max_iters=iters), ctx=ctx)
+        want = orc.kmeans_fit(x, dim, k, seed, max_iters=iters)
+        assert got.centroids.tobytes() == want.centroids.tobytes()
+        assert np.array_equal(got.assignments, want.assignments)
+        assert got.iters_run == want.iters_run and got.wcss == want.wcss
+
+
+def test_device_pointer_entry_points(ctx, orc):
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    from ir_multivector_retrieval_b200._lib import PqTrainStats
+
+    x = _rows(20_000, 64, 5)
+    dx = torch.from_numpy(x).cuda()
+    dcb = torch.empty(16 * 256 * 4, dtype=torch.float32, device="cuda")
+    st = PqTrainStats()
+    s = torch.cuda.current_stream()
+    ctx.set_stream(s.cuda_stream)
+    try:
+        ctx.check(ctx.lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), x.size, 64, 11, 1, 16,
+                                              8, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()), C.byref(st)))
+        codes = torch.empty((20_000, 16), dtype=torch.uint8, device="cuda")
+        ctx.check(ctx.lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), 64, 16,
+                                               C.c_void_p(dx.data_ptr()), 20_000, C.c_void_p(codes.data_ptr())))
+        ctx.sync()
+    finally:
+        ctx.set_stream(None)
+    cb = dcb.cpu().numpy()
+    want_cb = orc.pq_train(x, 64, 11, 16, n_threads=THREADS, max_iters=8, tol=-math.inf)
+    assert cb.tobytes() == want_cb.tobytes()
+    assert np.array_equal(codes.cpu().numpy(), orc.pq_encode(cb, 64, 16, x, n_threads=THREADS))
+    assert st.iters_max == 8 and st.total_ms > 0
+
+
+def test_full_size_train_and_encode(ctx, orc):
+    """BASELINE configs[1] shape: 1,521,797 x 64, M=16 x 4. Bit-exact against
+    the oracle for 2 Lloyd iterations (seeding included), plus size-free
+    properties after 20 iterations."""
+    n = 1_521_797
+    c = synth.make_corpus(n, 64, seed=42)
+    x = synth.anchor_residuals(c)
+    got = pq.train(x, 64, 42 + 0xA1B2C3D4, pq_m=16, max_iters=2, tol=-math.inf, ctx=ctx)
+    want = orc.pq_train(x, 64, 42 + 0xA1B2C3D4, 16, n_threads=THREADS, max_iters=2, tol=-math.inf)
+    assert got.codebooks.tobytes() == want.tobytes()
+    codes = got.encode_batch(x)
+    sample = np.random.default_rng(0).choice(n, 50_000, replace=False)
+    assert np.array_equal(codes[sample], orc.pq_encode(got.codebooks, 64, 16, x[sample], n_threads=THREADS))
+    stats = {}
+    p20 = pq.train(x, 64, 42 + 0xA1B2C3D4, pq_m=16, max_iters=20, tol=-math.inf, ctx=ctx, stats=stats)
+    assert stats["iters_min"] == 20 and np.isfinite(p20.codebooks).all()
+    codes = p20.encode_batch(x)
+    assert np.array_equal(p20.encode_batch(p20.decode(codes)), codes)
+    # Lloyd fixed point drift: 20 iterations never raise the quantisation error
+    def mse(p):
+        return float(np.mean((p.decode(p.encode_batch(x[sample])) - x[sample]) ** 2))
+    assert mse(p20) <= mse(got) + 1e-7
