@@ -59,7 +59,8 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def make_input(n: int = N_ROWS) -> np.ndarray:
+def make_input(n: int | None = None) -> np.ndarray:
+    n = N_ROWS if n is None else n
     from ir_multivector_retrieval_b200 import synth
 
     c = synth.make_corpus(n, DIM, seed=42)
@@ -196,13 +197,18 @@ def run_b200(args) -> None:
     from ir_multivector_retrieval_b200 import Context
     from ir_multivector_retrieval_b200._lib import PqTrainStats
 
-    x = make_input()
+    x = make_input(args.rows)
     n = x.shape[0]
     x_pin = torch.from_numpy(x).pin_memory()
     dx = x_pin.to(f"cuda:{local}", non_blocking=False)
     dcb = torch.empty(PQ_M * K * (DIM // PQ_M), dtype=torch.float32, device=f"cuda:{local}")
     dcodes = torch.empty((n, PQ_M), dtype=torch.uint8, device=f"cuda:{local}")
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the library and the timing events must share it
+    # (torch's default stream has handle 0, which the C ABI reads as "the
+    # context's own stream").
+    stream = torch.cuda.Stream(device=f"cuda:{local}")
+    torch.cuda.set_stream(stream)
+    torch.cuda.synchronize()
     ctx = Context(local)
     ctx.set_stream(stream.cuda_stream)
     lib = ctx.lib
@@ -344,6 +350,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-target-s", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -4,8 +4,8 @@
 // Exactness contract. The reference computes squared L2 distances in Zig's
 // strict float mode (no FMA contraction, IEEE round-to-nearest, denormals
 // kept). Every distance here uses __fadd_rn/__fmul_rn (or their sm_100
-// packed-pair forms __fadd2_rn/__fmul2_rn, which round each lane exactly
-// like the scalar ones) in the reference's summation order, so results are
+// packed-pair forms, arranged so that no product feeds an add; see
+// l2_small_pair) in the reference's summation order, so results are
 // bit-identical. The library is built with -fmad=false and without
 // --use_fast_math as a second guard.
 #pragma once
@@ -35,15 +35,24 @@ __device__ __forceinline__ float l2_small(const float* x, const float* c) {
 // Two distances at once: xx[k] = (x_k, x_k), nc[k] = (-ca_k, -cb_k).
 // x + (-c) is IEEE-identical to x - c, so lane 0 is l2_small(x, ca) and
 // lane 1 is l2_small(x, cb), bit for bit.
+//
+// The accumulation is written as fma(q, one, acc) with q = d*d already
+// rounded and `one` == 1.0f supplied at run time (a kernel argument):
+// fma(q, 1, acc) = round(acc + q), exactly the reference's add. Written as
+// a packed add of a packed product instead, the assembler contracts the
+// pair into one fused multiply-add (measured on sm_100a, even with
+// -fmad=false and explicit .rn), which rounds d*d away and breaks parity.
+// With `one` opaque there is no multiply feeding an add left to contract.
 template <int S>
 __device__ __forceinline__ float2 l2_small_pair(const float2 (&xx)[S],
-                                                const float2* nc) {
+                                                const float2* nc, float2 one) {
   float2 d = __fadd2_rn(xx[0], nc[0]);
   float2 acc = __fmul2_rn(d, d);
 #pragma unroll
   for (int k = 1; k < S; ++k) {
     d = __fadd2_rn(xx[k], nc[k]);
-    acc = __fadd2_rn(acc, __fmul2_rn(d, d));
+    const float2 q = __fmul2_rn(d, d);
+    acc = __ffma2_rn(q, one, acc);
   }
   return acc;
 }

@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kThreads)
 pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
                  const float* __restrict__ cb, uint8_t* __restrict__ codes,
                  uint8_t* __restrict__ asg, float* __restrict__ mind,
-                 uint32_t* __restrict__ hist, const uint8_t* __restrict__ state) {
+                 uint32_t* __restrict__ hist, const uint8_t* __restrict__ state, float one) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int KP = (K + 1) >> 1;
   float2* cbp = reinterpret_cast<float2*>(smem_raw);  // [M][KP][S]
@@ -97,6 +97,7 @@ pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
     ok[j] = row[j] < N;
   }
   uint32_t packed[kPtsPerThread] = {0u};
+  const float2 one2 = make_float2(one, one);  // 1.0f, opaque to the compiler
 
   for (int m = 0; m < M; ++m) {
     if (MODE == kModeLloyd && state[m] != kRunning) continue;
@@ -128,7 +129,7 @@ pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
       for (int k = 0; k < S; ++k) nc[k] = cm[p * S + k];
 #pragma unroll
       for (int j = 0; j < kPtsPerThread; ++j) {
-        const float2 dd = l2_small_pair<S>(xx[j], nc);
+        const float2 dd = l2_small_pair<S>(xx[j], nc, one2);
         if (p == 0) d0[j] = dd.x;
         if (dd.x < best[j]) { best[j] = dd.x; bi[j] = 2 * p; }
         if (dd.y < best[j]) { best[j] = dd.y; bi[j] = 2 * p + 1; }
@@ -733,11 +734,11 @@ int launch_assign(Ctx* ctx, int mode, const float* R, uint64_t N, int D, int M, 
   if (mode == kModeLloyd) {
     auto kern = pq_assign_kernel<S, kModeLloyd>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state);
+    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
   } else {
     auto kern = pq_assign_kernel<S, kModeEncode>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state);
+    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
   }
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;

@@ -154,15 +154,17 @@ def test_device_pointer_entry_points(ctx, orc):
     from ir_multivector_retrieval_b200._lib import PqTrainStats
 
     x = _rows(20_000, 64, 5)
-    dx = torch.from_numpy(x).cuda()
-    dcb = torch.empty(16 * 256 * 4, dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        dx = torch.from_numpy(x).cuda()
+        dcb = torch.empty(16 * 256 * 4, dtype=torch.float32, device="cuda")
     st = PqTrainStats()
-    s = torch.cuda.current_stream()
     ctx.set_stream(s.cuda_stream)
     try:
         ctx.check(ctx.lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), x.size, 64, 11, 1, 16,
                                               8, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()), C.byref(st)))
-        codes = torch.empty((20_000, 16), dtype=torch.uint8, device="cuda")
+        with torch.cuda.stream(s):
+            codes = torch.empty((20_000, 16), dtype=torch.uint8, device="cuda")
         ctx.check(ctx.lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), 64, 16,
                                                C.c_void_p(dx.data_ptr()), 20_000, C.c_void_p(codes.data_ptr())))
         ctx.sync()
@@ -197,3 +199,51 @@ def test_full_size_train_and_encode(ctx, orc):
     def mse(p):
         return float(np.mean((p.decode(p.encode_batch(x[sample])) - x[sample]) ** 2))
     assert mse(p20) <= mse(got) + 1e-7
+
+
+def _seq4(v):
+    q = (v.astype(np.float32) ** 2).astype(np.float32)
+    return np.float32(np.float32(np.float32(q[0] + q[1]) + q[2]) + q[3])
+
+
+def test_encode_rounding_order_sensitive_ties(ctx, orc):
+    """Codeword pairs whose ranking is decided only by the rounding order of
+    the distance sum: for the zero row, c_a = (p,q,r,s) and c_b = (r,s,p,q)
+    have the same exact distance and the same pairwise-tree sum, but their
+    left-fold sums (the reference order) differ. A kernel that sums in any
+    other order, or fuses the squares into FMAs, picks differently."""
+    rng = np.random.default_rng(17)
+    cases = []
+    while len(cases) < 16 * 48:
+        a = rng.standard_normal(4).astype(np.float32) * np.float32(rng.choice([1e-3, 1.0, 30.0]))
+        b = a[[2, 3, 0, 1]]
+        if _seq4(a) != _seq4(b):
+            cases.append((a, b))
+    x = np.zeros((3, 64), np.float32)
+    for call in range(48):
+        cb = np.full((16, 256, 4), 1e4, np.float32)
+        for m in range(16):
+            a, b = cases[call * 16 + m]
+            cb[m, 0], cb[m, 1] = a, b
+        cb = cb.reshape(-1)
+        got = pq.PQ(dim=64, sub_dim=4, codebooks=cb, pq_m=16, ctx=ctx).encode_batch(x)
+        want = orc.pq_encode(cb, 64, 16, x)
+        assert np.array_equal(got, want)
+        assert set(np.unique(want)) <= {0, 1} and len(np.unique(want)) == 2
+
+
+def test_encode_one_ulp_codewords(ctx, orc):
+    """Neighbouring codewords one ulp apart in one coordinate: distances that
+    differ only in their last bits."""
+    rng = np.random.default_rng(23)
+    base = rng.standard_normal((16, 128, 4)).astype(np.float32)
+    twin = base.copy()
+    k = rng.integers(0, 4, size=(16, 128))
+    for m in range(16):
+        for c in range(128):
+            twin[m, c, k[m, c]] = np.nextafter(twin[m, c, k[m, c]], np.float32(np.inf))
+    cb = np.stack([base, twin], axis=2).reshape(-1)  # codeword 2c and 2c+1 are twins
+    x = (base[:, rng.integers(0, 128, 50_000)].transpose(1, 0, 2)
+         + rng.standard_normal((50_000, 16, 4)).astype(np.float32) * np.float32(1e-3)).reshape(50_000, 64)
+    got = pq.PQ(dim=64, sub_dim=4, codebooks=cb, pq_m=16, ctx=ctx).encode_batch(x)
+    assert np.array_equal(got, orc.pq_encode(cb, 64, 16, x, n_threads=THREADS))
