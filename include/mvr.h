@@ -111,6 +111,42 @@ int mvr_kmeans_fit(mvr_ctx* ctx, const float* vectors, uint64_t vectors_len,
                    uint32_t* assignments_out, float* wcss_out,
                    uint32_t* iters_run_out);
 
+/* ---- kmeans.fit without device allocation ------------------------------- */
+
+/* Largest row count and the size of the fixed device scratch of
+ * `mvr_kmeans_fit_noalloc`. */
+#define MVR_NOALLOC_MAX_ROWS 65536u
+#define MVR_NOALLOC_SCRATCH_BYTES (1536u * 1024u)
+
+/* No counterpart in the reference: an extra entry point for hosts that
+ * cannot let a library allocate GPU memory (their own allocator owns the
+ * device, their memory budget is fixed up front, or cudaMalloc's implicit
+ * synchronisation is not acceptable on their path). Same result as
+ * `mvr_kmeans_fit` (bit for bit), but
+ *   - inputs and outputs are device pointers: `d_vectors` (vectors_len
+ *     floats), `d_centroids_out` (k*dim floats), `d_assignments_out`
+ *     (n u32, may be NULL); `wcss_out` / `iters_run_out` are host pointers
+ *     and may be NULL;
+ *   - work runs on `cuda_stream` (NULL = the legacy default stream) of the
+ *     current device, and the call returns when the result is ready;
+ *   - no context: it calls no cudaMalloc, cudaFree or other allocating
+ *     routine. All scratch lives in one fixed device array of
+ *     MVR_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU
+ *     that loads the library keeps until the process exits;
+ *   - limits: dim in {1, 2, 4}, k <= 256, n <= MVR_NOALLOC_MAX_ROWS rows;
+ *     larger inputs return MVR_E_INVALID_ARGUMENT before any GPU work.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any
+ * stream capture on the device. All calls share the one array, so calls that
+ * overlap on the GPU (other streams, other threads) race: serialise them.
+ * The array keeps the last call's contents; the call initialises everything
+ * it reads. */
+int mvr_kmeans_fit_noalloc(const float* d_vectors, uint64_t vectors_len,
+                           uint32_t dim, uint32_t k, uint32_t max_iters,
+                           float tol, uint64_t seed, float* d_centroids_out,
+                           uint32_t* d_assignments_out, float* wcss_out,
+                           uint32_t* iters_run_out, void* cuda_stream);
+
 /* ---- pq.train / PQ.encode ---------------------------------------------- */
 
 /* Per-call timing and iteration report of `mvr_pq_train*` (no reference

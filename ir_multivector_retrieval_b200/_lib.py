@@ -103,6 +103,10 @@ SIGNATURES = {
         [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,
          C.c_uint32, _P, _P, _P, _P],
     ),
+    "mvr_kmeans_fit_noalloc": (
+        C.c_int,
+        [_P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_uint64, _P, _P, _P, _P, _P],
+    ),
     "mvr_pq_train": (
         C.c_int,
         [_P, _P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,

@@ -727,31 +727,31 @@ size_t assign_smem(int M, int K, int mode) {
 }
 
 template <int S>
-int launch_assign(Ctx* ctx, int mode, const float* R, uint64_t N, int D, int M, int K,
+int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, uint64_t N, int D, int M, int K,
                   const float* cb, uint8_t* codes, uint8_t* asg, float* mind,
                   uint32_t* hist, const uint8_t* state, int nblk) {
   const size_t sm = assign_smem<S>(M, K, mode);
   if (mode == kModeLloyd) {
     auto kern = pq_assign_kernel<S, kModeLloyd>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
+    kern<<<nblk, kThreads, sm, st>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
   } else {
     auto kern = pq_assign_kernel<S, kModeEncode>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, ctx->stream>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
+    kern<<<nblk, kThreads, sm, st>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
   }
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
 }
 
 template <int S>
-int launch_chain(Ctx* ctx, const float* sorted, uint64_t N, int M, int K, const uint32_t* counts,
-                 const uint32_t* starts, float* cb, const uint8_t* state) {
+int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int M, int K,
+                 const uint32_t* counts, const uint32_t* starts, float* cb, const uint8_t* state) {
   const size_t sm = (size_t)kChainStages * 32 * (kChainCh + 1) * S * sizeof(float);
   auto kern = pq_chain_kernel<S>;
   MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const int grid = M * ((K + 31) / 32);
-  kern<<<grid, 32, sm, ctx->stream>>>(sorted, N, K, counts, starts, cb, state);
+  kern<<<grid, 32, sm, st>>>(sorted, N, K, counts, starts, cb, state);
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
 }
@@ -775,22 +775,59 @@ int pq_encode_device(Ctx* ctx, const float* d_cb, int D, int M, const float* d_R
   MVR_TRY(check_shape(ctx, D, M, S, 256));
   const int nblk = (int)((N + kTile - 1) / kTile);
   switch (S) {
-    case 1: return launch_assign<1>(ctx, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
-    case 2: return launch_assign<2>(ctx, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
-    default: return launch_assign<4>(ctx, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
+    case 1: return launch_assign<1>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
+    case 2: return launch_assign<2>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
+    default: return launch_assign<4>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
   }
 }
 
-int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
+PqLayout pq_layout(uint64_t N, int M, int S, int K) {
+  PqLayout L;
+  L.nblk = (int)((N + kTile - 1) / kTile);
+  L.nchunk = (int)((N + kSeedChunk - 1) / kSeedChunk);
+  size_t off = 0;
+  auto carve = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  // host-mirrored bookkeeping first, so one copy moves it both ways
+  L.o_draws = carve((size_t)M * K * 8);
+  L.o_chosen = carve((size_t)M * K * 8);
+  L.o_idx0 = carve((size_t)M * 8);
+  L.o_counts = carve((size_t)M * K * 4);
+  L.o_starts = carve((size_t)M * K * 4);
+  L.o_wcss = carve((size_t)M * 4);
+  L.o_prev = carve((size_t)M * 4);
+  L.o_status = carve((size_t)M * 4);
+  L.o_nonf = carve((size_t)M * 4);
+  L.o_iters = carve((size_t)M * 4);
+  L.o_fb = carve((size_t)M * 4);
+  L.o_rs = carve((size_t)M * 4);
+  L.o_state = carve((size_t)M);
+  L.small_bytes = off;
+  L.o_mind = carve((size_t)M * N * sizeof(float));
+  L.o_asg = carve((size_t)M * N);
+  L.o_sorted = carve((size_t)M * N * S * sizeof(float));
+  L.o_hist = carve((size_t)M * L.nblk * K * sizeof(uint32_t));
+  L.o_chunk = carve((size_t)M * L.nchunk * sizeof(double2));
+  L.total_bytes = off;
+  return L;
+}
+
+int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out, unsigned char* ws,
+                  unsigned char* hsmall) {
   const uint64_t N = job.N;
   const int D = job.D, M = job.M, S = job.S, K = job.K;
   MVR_TRY(check_shape(ctx, D, M, S, K));
   if (N == 0) return fail(ctx, MVR_E_EMPTY_VECTOR_SET, "no rows");
   if (N >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows per subspace");
-  cudaStream_t st = ctx->stream;
-  for (int e = 0; e < 4; ++e)
-    if (!ctx->ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ctx->ev[e]));
-  MVR_CUDA(ctx, cudaEventRecord(ctx->ev[0], st));
+  const bool timing = out.stats != nullptr && ctx != nullptr;
+  if (timing) {
+    for (int e = 0; e < 4; ++e)
+      if (!ctx->ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ctx->ev[e]));
+    MVR_CUDA(ctx, cudaEventRecord(ctx->ev[0], st));
+  }
 
   // ---- degenerate k >= n -------------------------------------------------
   if ((uint64_t)K >= N) {
@@ -805,59 +842,39 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
       if (out.h_wcss) out.h_wcss[m] = 0.f;
       if (out.h_iters) out.h_iters[m] = 0;
     }
-    if (out.stats) {
-      std::memset(out.stats, 0, sizeof(*out.stats));
-    }
+    if (out.stats) std::memset(out.stats, 0, sizeof(*out.stats));
     return MVR_OK;
   }
 
-  const int nblk = (int)((N + kTile - 1) / kTile);
-  const int nchunk = (int)((N + kSeedChunk - 1) / kSeedChunk);
+  const PqLayout L = pq_layout(N, M, S, K);
+  const int nblk = L.nblk, nchunk = L.nchunk;
+  float* mind = (float*)(ws + L.o_mind);
+  uint8_t* asg = (uint8_t*)(ws + L.o_asg);
+  float* sorted = (float*)(ws + L.o_sorted);
+  uint32_t* hist = (uint32_t*)(ws + L.o_hist);
+  double2* chunk = (double2*)(ws + L.o_chunk);
+  unsigned char* small = ws;  // bookkeeping lives at the start of the workspace
+  const size_t small_bytes = L.small_bytes;
+  double* d_draws = (double*)(small + L.o_draws);
+  uint64_t* d_chosen = (uint64_t*)(small + L.o_chosen);
+  uint64_t* d_idx0 = (uint64_t*)(small + L.o_idx0);
+  uint32_t* d_counts = (uint32_t*)(small + L.o_counts);
+  uint32_t* d_starts = (uint32_t*)(small + L.o_starts);
+  float* d_wcss = (float*)(small + L.o_wcss);
+  float* d_prev = (float*)(small + L.o_prev);
+  int* d_status = (int*)(small + L.o_status);
+  int* d_nonf = (int*)(small + L.o_nonf);
+  uint32_t* d_iters = (uint32_t*)(small + L.o_iters);
+  uint32_t* d_fb = (uint32_t*)(small + L.o_fb);
+  uint32_t* d_rs = (uint32_t*)(small + L.o_rs);
+  uint8_t* d_state = (uint8_t*)(small + L.o_state);
 
-  // ---- scratch ------------------------------------------------------------
-  float* mind = nullptr;
-  uint8_t* asg = nullptr;
-  float* sorted = nullptr;
-  uint32_t* hist = nullptr;
-  double2* chunk = nullptr;
-  unsigned char* small = nullptr;
-  MVR_TRY(scratch(ctx, kSlotMinDist, (size_t)M * N * sizeof(float), (void**)&mind));
-  MVR_TRY(scratch(ctx, kSlotAssign, (size_t)M * N, (void**)&asg));
-  MVR_TRY(scratch(ctx, kSlotSorted, (size_t)M * N * S * sizeof(float), (void**)&sorted));
-  MVR_TRY(scratch(ctx, kSlotHist, (size_t)M * nblk * K * sizeof(uint32_t), (void**)&hist));
-  MVR_TRY(scratch(ctx, kSlotChunk, (size_t)M * nchunk * sizeof(double2), (void**)&chunk));
-  // small: draws[M*K] f64 | chosen[M*K] u64 | idx0[M] u64 | counts[M*K] | starts[M*K]
-  //        | wcss[M] | prev[M] | status[M] | nonfinite[M] | iters[M] | fallbacks[M]
-  //        | reseeds[M] | state[M]
-  size_t off = 0;
-  auto carve = [&](size_t bytes) { size_t o = off; off = (off + bytes + 255) & ~(size_t)255; return o; };
-  const size_t o_draws = carve((size_t)M * K * 8), o_chosen = carve((size_t)M * K * 8),
-               o_idx0 = carve((size_t)M * 8), o_counts = carve((size_t)M * K * 4),
-               o_starts = carve((size_t)M * K * 4), o_wcss = carve((size_t)M * 4),
-               o_prev = carve((size_t)M * 4), o_status = carve((size_t)M * 4),
-               o_nonf = carve((size_t)M * 4), o_iters = carve((size_t)M * 4),
-               o_fb = carve((size_t)M * 4), o_rs = carve((size_t)M * 4), o_state = carve((size_t)M);
-  const size_t small_bytes = off;
-  MVR_TRY(scratch(ctx, kSlotSmall, small_bytes, (void**)&small));
-  double* d_draws = (double*)(small + o_draws);
-  uint64_t* d_chosen = (uint64_t*)(small + o_chosen);
-  uint64_t* d_idx0 = (uint64_t*)(small + o_idx0);
-  uint32_t* d_counts = (uint32_t*)(small + o_counts);
-  uint32_t* d_starts = (uint32_t*)(small + o_starts);
-  float* d_wcss = (float*)(small + o_wcss);
-  float* d_prev = (float*)(small + o_prev);
-  int* d_status = (int*)(small + o_status);
-  int* d_nonf = (int*)(small + o_nonf);
-  uint32_t* d_iters = (uint32_t*)(small + o_iters);
-  uint32_t* d_fb = (uint32_t*)(small + o_fb);
-  uint32_t* d_rs = (uint32_t*)(small + o_rs);
-  uint8_t* d_state = (uint8_t*)(small + o_state);
-
-  // ---- host RNG draws (data independent) --------------------------------
-  std::vector<unsigned char> hsmall(small_bytes, 0);
+  // ---- host RNG draws (data independent); the rest of the bookkeeping
+  // starts at zero (state = running, counters = 0) -------------------------
+  std::memset(hsmall, 0, small_bytes);
   {
-    double* hd = (double*)(hsmall.data() + o_draws);
-    uint64_t* hi0 = (uint64_t*)(hsmall.data() + o_idx0);
+    double* hd = (double*)(hsmall + L.o_draws);
+    uint64_t* hi0 = (uint64_t*)(hsmall + L.o_idx0);
     for (int m = 0; m < M; ++m) {
       Xoshiro256pp rng(job.seed + (uint64_t)m);
       hi0[m] = rng.below(N);
@@ -865,7 +882,7 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
       for (int c = 1; c < K; ++c) hd[(size_t)m * K + c] = rng.unit_f64();
     }
   }
-  MVR_CUDA(ctx, cudaMemcpyAsync(small, hsmall.data(), small_bytes, cudaMemcpyHostToDevice, st));
+  MVR_CUDA(ctx, cudaMemcpyAsync(small, hsmall, small_bytes, cudaMemcpyHostToDevice, st));
 
   float* cb = out.d_codebooks;
   pq_seed_init_kernel<<<M, 32, 0, st>>>(job.R, D, S, K, d_idx0, cb, d_chosen);
@@ -881,28 +898,31 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
                                                         d_draws, d_nonf, d_status, d_state, d_fb, d_chosen);
     MVR_CUDA(ctx, cudaGetLastError());
   }
-  MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
 
   // ---- Lloyd iterations ---------------------------------------------------
   const bool check = !(job.tol == -INFINITY) && !std::isnan(job.tol);
   uint32_t launches = 1 + 2 * (uint32_t)(K - 1);
   std::vector<cudaEvent_t> aev;  // assignment-kernel brackets (stats only)
-  if (out.stats) {
+  if (timing) {
     aev.resize(2 * (size_t)job.max_iters, nullptr);
     for (auto& e : aev) MVR_CUDA(ctx, cudaEventCreate(&e));
   }
   struct EvGuard {
     std::vector<cudaEvent_t>& v;
-    ~EvGuard() { for (auto e : v) if (e) cudaEventDestroy(e); }
+    ~EvGuard() {
+      for (auto e : v)
+        if (e) cudaEventDestroy(e);
+    }
   } ev_guard{aev};
   for (uint32_t it = 0; it < job.max_iters; ++it) {
-    if (out.stats) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it], st));
+    if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it], st));
     switch (S) {
-      case 1: MVR_TRY(launch_assign<1>(ctx, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
-      case 2: MVR_TRY(launch_assign<2>(ctx, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
-      default: MVR_TRY(launch_assign<4>(ctx, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
+      case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
+      case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
+      default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
     }
-    if (out.stats) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
+    if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
     launches += 5;
     const bool last = it + 1 == job.max_iters;
     if (check || (last && out.h_wcss)) {
@@ -919,50 +939,57 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
     }
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
-      case 1: MVR_TRY(launch_chain<1>(ctx, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
-      case 2: MVR_TRY(launch_chain<2>(ctx, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
-      default: MVR_TRY(launch_chain<4>(ctx, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
+      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
+      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
+      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
     }
     pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(job.R, N, D, S, K, d_counts, mind, cb, d_state, d_wcss,
                                                   d_prev, d_iters, d_rs, (int)it, check ? 1 : 0, job.tol);
     MVR_CUDA(ctx, cudaGetLastError());
-    // Converged subspaces keep the assignments of their last iteration; the
-    // final u32 copy for kmeans.fit callers happens when every subspace is
-    // finished, below.
   }
-  MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
-  MVR_CUDA(ctx, cudaMemcpyAsync(hsmall.data(), small, small_bytes, cudaMemcpyDeviceToHost, st));
-  MVR_CUDA(ctx, cudaStreamSynchronize(st));
-
-  const int* hstatus = (const int*)(hsmall.data() + o_status);
-  for (int m = 0; m < M; ++m)
-    if (hstatus[m] != MVR_OK) {
-      return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
-    }
-  const uint32_t* hiters = (const uint32_t*)(hsmall.data() + o_iters);
-  const float* hw = (const float*)(hsmall.data() + o_wcss);
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
   if (out.d_assign && job.max_iters > 0) {
-    // Early-stopped subspaces: their final assignments are the ones left in
-    // `asg` by their last iteration, which later iterations did not touch.
+    // Converged subspaces keep the assignments of their last iteration,
+    // which later iterations did not touch.
     u8_to_u32_kernel<<<1024, 256, 0, st>>>(asg, out.d_assign, (uint64_t)M * N);
     MVR_CUDA(ctx, cudaGetLastError());
-    MVR_CUDA(ctx, cudaStreamSynchronize(st));
+    ++launches;
   }
+  MVR_CUDA(ctx, cudaMemcpyAsync(hsmall, small, small_bytes, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+
+  const int* hstatus = (const int*)(hsmall + L.o_status);
+  for (int m = 0; m < M; ++m)
+    if (hstatus[m] != MVR_OK)
+      return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
+  const uint32_t* hiters = (const uint32_t*)(hsmall + L.o_iters);
+  const float* hw = (const float*)(hsmall + L.o_wcss);
   if (out.h_iters)
     for (int m = 0; m < M; ++m) out.h_iters[m] = job.max_iters ? hiters[m] : 0;
   if (out.h_wcss)
     for (int m = 0; m < M; ++m) out.h_wcss[m] = job.max_iters ? hw[m] : 0.f;
   if (out.stats) {
-    float t01 = 0, t12 = 0, t02 = 0;
-    cudaEventElapsedTime(&t01, ctx->ev[0], ctx->ev[1]);
-    cudaEventElapsedTime(&t12, ctx->ev[1], ctx->ev[2]);
-    cudaEventElapsedTime(&t02, ctx->ev[0], ctx->ev[2]);
-    out.stats->seed_ms = t01;
-    out.stats->lloyd_ms = t12;
-    out.stats->total_ms = t02;
+    std::memset(out.stats, 0, sizeof(*out.stats));
+    if (timing) {
+      float t01 = 0, t12 = 0, t02 = 0;
+      cudaEventElapsedTime(&t01, ctx->ev[0], ctx->ev[1]);
+      cudaEventElapsedTime(&t12, ctx->ev[1], ctx->ev[2]);
+      cudaEventElapsedTime(&t02, ctx->ev[0], ctx->ev[2]);
+      out.stats->seed_ms = t01;
+      out.stats->lloyd_ms = t12;
+      out.stats->total_ms = t02;
+      double am = 0.0;
+      for (uint32_t it = 0; it < job.max_iters; ++it) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, aev[2 * it], aev[2 * it + 1]);
+        am += t;
+      }
+      out.stats->assign_ms = am;
+      out.stats->assign_launches = job.max_iters;
+    }
     uint32_t mx = 0, mn = UINT32_MAX, fb = 0, rs = 0;
-    const uint32_t* hfb = (const uint32_t*)(hsmall.data() + o_fb);
-    const uint32_t* hrs = (const uint32_t*)(hsmall.data() + o_rs);
+    const uint32_t* hfb = (const uint32_t*)(hsmall + L.o_fb);
+    const uint32_t* hrs = (const uint32_t*)(hsmall + L.o_rs);
     for (int m = 0; m < M; ++m) {
       const uint32_t v = job.max_iters ? hiters[m] : 0;
       mx = std::max(mx, v);
@@ -974,17 +1001,18 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
     out.stats->iters_min = mn;
     out.stats->seed_fallbacks = fb;
     out.stats->reseeds = rs;
-    double am = 0.0;
-    for (uint32_t it = 0; it < job.max_iters; ++it) {
-      float t = 0.f;
-      cudaEventElapsedTime(&t, aev[2 * it], aev[2 * it + 1]);
-      am += t;
-    }
-    out.stats->assign_ms = am;
-    out.stats->assign_launches = job.max_iters;
-    out.stats->launches = launches + (out.d_assign ? 1u : 0u);
+    out.stats->launches = launches;
   }
   return MVR_OK;
+}
+
+int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
+  MVR_TRY(check_shape(ctx, job.D, job.M, job.S, job.K));
+  const PqLayout L = pq_layout(job.N, job.M, job.S, job.K);
+  unsigned char* ws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
+  std::vector<unsigned char> hsmall(L.small_bytes);
+  return pq_kmeans_run(ctx, ctx->stream, job, out, ws, hsmall.data());
 }
 
 }  // namespace mvr

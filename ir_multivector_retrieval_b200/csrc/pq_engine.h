@@ -33,8 +33,27 @@ struct PqOut {
   mvr_pq_train_stats* stats = nullptr;
 };
 
-// Runs seeding + Lloyd for all M subspaces; returns the MVR status of the
-// smallest failing subspace, or MVR_OK. Synchronises the context stream.
+// Byte offsets of the engine's device workspace. The bookkeeping block
+// [0, small_bytes) is mirrored on the host (RNG draws in, status out).
+struct PqLayout {
+  int nblk = 0, nchunk = 0;
+  size_t o_draws = 0, o_chosen = 0, o_idx0 = 0, o_counts = 0, o_starts = 0, o_wcss = 0, o_prev = 0,
+         o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_state = 0;
+  size_t small_bytes = 0;
+  size_t o_mind = 0, o_asg = 0, o_sorted = 0, o_hist = 0, o_chunk = 0;
+  size_t total_bytes = 0;
+};
+PqLayout pq_layout(uint64_t N, int M, int S, int K);
+
+// Runs seeding + Lloyd for all M subspaces on `stream`, with device
+// workspace `ws` (pq_layout(...).total_bytes, 256-byte aligned) and host
+// buffer `hsmall` (small_bytes). Allocates no device memory. `ctx` may be
+// null (then no timing and no error text). Returns the MVR status of the
+// smallest failing subspace, or MVR_OK; synchronises `stream`.
+int pq_kmeans_run(Ctx* ctx, cudaStream_t stream, const PqJob& job, const PqOut& out,
+                  unsigned char* ws, unsigned char* hsmall);
+
+// pq_kmeans_run with the workspace taken from the context's scratch.
 int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out);
 
 // PQ.encode of N rows (asynchronous on the context stream).
