@@ -116,7 +116,7 @@ int mvr_kmeans_fit(mvr_ctx* ctx, const float* vectors, uint64_t vectors_len,
 /* Largest row count and the size of the fixed device scratch of
  * `mvr_kmeans_fit_noalloc`. */
 #define MVR_NOALLOC_MAX_ROWS 65536u
-#define MVR_NOALLOC_SCRATCH_BYTES (1536u * 1024u)
+#define MVR_NOALLOC_SCRATCH_BYTES (3072u * 1024u)
 
 /* No counterpart in the reference: an extra entry point for hosts that
  * cannot let a library allocate GPU memory (their own allocator owns the

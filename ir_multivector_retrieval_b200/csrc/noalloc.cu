@@ -12,6 +12,7 @@
 // process exits.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <mutex>
 
@@ -78,7 +79,10 @@ extern "C" int mvr_kmeans_fit_noalloc(const float* d_vectors, uint64_t vectors_l
   job.seed = seed;
   job.max_iters = max_iters;
   job.tol = tol;
-  const mvr::PqLayout L = mvr::pq_layout(n, 1, (int)dim, (int)k);
+  // The grid (and with it the histogram part of the scratch) is sized for at
+  // most 160 SMs, which bounds the scratch for any device.
+  const int sms = std::min(mvr::sm_count_current_device(), 160);
+  const mvr::PqLayout L = mvr::pq_layout(n, 1, (int)dim, (int)k, sms);
   if (L.total_bytes > kScratchBytes || L.small_bytes > 16384) return MVR_E_INVALID_ARGUMENT;
 
   int device = 0;
@@ -98,7 +102,7 @@ extern "C" int mvr_kmeans_fit_noalloc(const float* d_vectors, uint64_t vectors_l
   out.d_assign = d_assignments_out;
   out.h_wcss = &wcss;
   out.h_iters = &iters;
-  const int rc = mvr::pq_kmeans_run(nullptr, static_cast<cudaStream_t>(cuda_stream), job, out, ws, hsmall);
+  const int rc = mvr::pq_kmeans_run(nullptr, static_cast<cudaStream_t>(cuda_stream), job, out, ws, hsmall, sms);
   if (rc != MVR_OK) return rc;
   if (wcss_out) *wcss_out = wcss;
   if (iters_run_out) *iters_run_out = iters;

@@ -8,7 +8,9 @@
 //   PQ.encode           src/index/pq.zig:59-76
 //
 // Data layout in HBM (N rows, M subspaces of S floats, K centroids):
-//   R        [N][D]      caller's rows, read in place (no transpose)
+//   R        [N][D]      caller's rows (read by the transpose and by encode)
+//   XT       [M][N][S]   subspace-major copy of R: every per-subspace pass
+//                        reads 32 consecutive rows as one contiguous segment
 //   codebook [M][K][S]   the reference layout codebook[m][c][k]
 //   minDist  [M][N] f32  k-means++ D^2 weights, then Lloyd min_to_any
 //   assign   [M][N] u8   Lloyd assignments (K <= 256)
@@ -25,9 +27,9 @@
 //     coordinate) reproduces that order exactly;
 //   * mean: sum * (1 / (float)count), both correctly rounded;
 //   * k-means++ draws: the reference's sequential f64 prefix sum is bounded
-//     rigorously with directed-rounding partial sums plus the recursive
-//     summation error bound; a draw whose outcome the bound cannot decide
-//     is recomputed with the exact sequential chain on the device.
+//     rigorously (directed-rounding partial sums plus an error bound on the
+//     sequential chain); a draw whose outcome the bound cannot decide is
+//     recomputed with the exact sequential chain on the device.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -42,40 +44,87 @@
 namespace mvr {
 namespace {
 
-constexpr int kThreads = 256;          // assign / scatter / seed-update CTA size
-constexpr int kPtsPerThread = 2;       // rows per thread in assign / scatter
-constexpr int kTile = kThreads * kPtsPerThread;  // rows per assign CTA
-constexpr int kSeedChunk = kThreads;   // rows per seed-update CTA
+constexpr int kAsgThreads = 512;            // assign / encode CTA size
+constexpr int kPtsPerThread = 2;            // rows per thread per assign pass
+constexpr int kAsgTile = kAsgThreads * kPtsPerThread;
+constexpr int kSeedThreads = 256;
+constexpr int kSeedRowsPerThread = 4;
+constexpr int kSeedChunk = kSeedThreads * kSeedRowsPerThread;  // rows per chunk
 constexpr int kSelectThreads = 1024;
-constexpr int kChainCh = 32;           // elements per cluster per pipeline stage
-constexpr int kChainStages = 6;
+static_assert(kSelectThreads == kSeedChunk, "the fine search maps one thread to one row");
+constexpr int kChainWarps = 4;              // warps per chain CTA
+constexpr int kChainE = 128;                // elements per cluster per ring stage
+constexpr int kChainStages = 3;
+constexpr int kMaxM = 32;                   // subspaces per call (scatter: one warp each)
+constexpr int kCrossingSlack = 300;         // binade crossings of a monotone f64 sum
 
 enum : uint8_t { kRunning = 0, kDone = 1, kFailed = 2 };
 enum { kModeEncode = 0, kModeLloyd = 1 };
 
 template <int S>
 __device__ __forceinline__ void load_sub(const float* __restrict__ p, float (&x)[S]) {
+  if constexpr (S == 4) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else if constexpr (S == 2) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(p));
+    x[0] = v.x; x[1] = v.y;
+  } else {
+    x[0] = __ldg(p);
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void load_sub_unaligned(const float* __restrict__ p, float (&x)[S]) {
 #pragma unroll
   for (int k = 0; k < S; ++k) x[k] = __ldg(p + k);
 }
 
 // ---------------------------------------------------------------------------
-// Assignment / encode: one thread handles kPtsPerThread rows across all M
-// subspaces; the M codebooks sit in shared memory as negated centroid pairs
-// so that two distances come out of each packed f32x2 instruction.
+// XT[m][r][:] = R[r][m*S : m*S+S]
+// ---------------------------------------------------------------------------
+template <int S>
+__global__ void __launch_bounds__(256)
+pq_transpose_kernel(const float* __restrict__ R, uint64_t N, int D, int M, float* __restrict__ XT) {
+  for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < N;
+       r += (uint64_t)gridDim.x * blockDim.x) {
+    const float* row = R + r * (uint64_t)D;
+    for (int m = 0; m < M; ++m) {
+      float x[S];
+      load_sub_unaligned<S>(row + m * S, x);
+      float* o = XT + ((size_t)m * N + r) * S;
+      if constexpr (S == 4) {
+        *reinterpret_cast<float4*>(o) = make_float4(x[0], x[1], x[2], x[3]);
+      } else if constexpr (S == 2) {
+        *reinterpret_cast<float2*>(o) = make_float2(x[0], x[1]);
+      } else {
+        o[0] = x[0];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Assignment / encode. Persistent CTAs: CTA b owns rows
+// [b*rows_per_cta, (b+1)*rows_per_cta), processed kAsgTile at a time, one
+// thread per kPtsPerThread rows across all M subspaces. The M codebooks sit
+// in shared memory as negated centroid pairs so that two distances come out
+// of each packed f32x2 instruction. Lloyd mode reads XT and writes
+// assignments, min distances and the CTA's cluster histogram; encode mode
+// reads R and writes codes.
 // ---------------------------------------------------------------------------
 template <int S, int MODE>
-__global__ void __launch_bounds__(kThreads)
-pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
-                 const float* __restrict__ cb, uint8_t* __restrict__ codes,
-                 uint8_t* __restrict__ asg, float* __restrict__ mind,
-                 uint32_t* __restrict__ hist, const uint8_t* __restrict__ state, float one) {
+__global__ void __launch_bounds__(kAsgThreads, 2)
+pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint64_t N, int D,
+                 int M, int K, const float* __restrict__ cb, uint8_t* __restrict__ codes,
+                 uint8_t* __restrict__ asg, float* __restrict__ mind, uint32_t* __restrict__ hist,
+                 const uint8_t* __restrict__ state, float one, uint64_t rows_per_cta) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int KP = (K + 1) >> 1;
   float2* cbp = reinterpret_cast<float2*>(smem_raw);  // [M][KP][S]
   uint32_t* h = reinterpret_cast<uint32_t*>(cbp + (size_t)M * KP * S);  // [M][K]
 
-  for (int e = threadIdx.x; e < M * KP * S; e += kThreads) {
+  for (int e = threadIdx.x; e < M * KP * S; e += kAsgThreads) {
     const int k = e % S;
     const int p = (e / S) % KP;
     const int m = e / (S * KP);
@@ -85,68 +134,73 @@ pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
     cbp[e] = make_float2(-a, -b);  // a NaN pad never wins a strict '<'
   }
   if (MODE == kModeLloyd)
-    for (int e = threadIdx.x; e < M * K; e += kThreads) h[e] = 0;
+    for (int e = threadIdx.x; e < M * K; e += kAsgThreads) h[e] = 0;
   __syncthreads();
 
-  const uint64_t base = (uint64_t)blockIdx.x * kTile;
-  uint64_t row[kPtsPerThread];
-  bool ok[kPtsPerThread];
-#pragma unroll
-  for (int j = 0; j < kPtsPerThread; ++j) {
-    row[j] = base + (uint64_t)j * kThreads + threadIdx.x;
-    ok[j] = row[j] < N;
-  }
-  uint32_t packed[kPtsPerThread] = {0u};
   const float2 one2 = make_float2(one, one);  // 1.0f, opaque to the compiler
-
-  for (int m = 0; m < M; ++m) {
-    if (MODE == kModeLloyd && state[m] != kRunning) continue;
-    float2 xx[kPtsPerThread][S];
+  const uint64_t lo = (uint64_t)blockIdx.x * rows_per_cta;
+  const uint64_t hi = min(N, lo + rows_per_cta);
+  for (uint64_t base = lo; base < hi; base += kAsgTile) {
+    uint64_t row[kPtsPerThread];
+    bool ok[kPtsPerThread];
 #pragma unroll
     for (int j = 0; j < kPtsPerThread; ++j) {
-      float x[S];
-      if (ok[j]) {
-        load_sub<S>(R + row[j] * (uint64_t)D + (uint64_t)m * S, x);
-      } else {
-#pragma unroll
-        for (int k = 0; k < S; ++k) x[k] = 0.f;
-      }
-#pragma unroll
-      for (int k = 0; k < S; ++k) xx[j][k] = make_float2(x[k], x[k]);
+      row[j] = base + (uint64_t)j * kAsgThreads + threadIdx.x;
+      ok[j] = row[j] < hi;
     }
-    float best[kPtsPerThread], d0[kPtsPerThread];
-    int bi[kPtsPerThread];
-#pragma unroll
-    for (int j = 0; j < kPtsPerThread; ++j) {
-      best[j] = __int_as_float(0x7f800000);
-      bi[j] = 0;
-      d0[j] = 0.f;
-    }
-    const float2* cm = cbp + (size_t)m * KP * S;
-    for (int p = 0; p < KP; ++p) {
-      float2 nc[S];
-#pragma unroll
-      for (int k = 0; k < S; ++k) nc[k] = cm[p * S + k];
+    // Tail of the CTA's range: whole warps without rows skip the tile.
+    if (!__any_sync(0xffffffffu, ok[0] || ok[kPtsPerThread - 1])) continue;
+    uint32_t packed[kPtsPerThread] = {0u};
+    for (int m = 0; m < M; ++m) {
+      if (MODE == kModeLloyd && state[m] != kRunning) continue;
+      float2 xx[kPtsPerThread][S];
 #pragma unroll
       for (int j = 0; j < kPtsPerThread; ++j) {
-        const float2 dd = l2_small_pair<S>(xx[j], nc, one2);
-        if (p == 0) d0[j] = dd.x;
-        if (dd.x < best[j]) { best[j] = dd.x; bi[j] = 2 * p; }
-        if (dd.y < best[j]) { best[j] = dd.y; bi[j] = 2 * p + 1; }
-      }
-    }
+        float x[S];
+        if (ok[j]) {
+          if (MODE == kModeLloyd)
+            load_sub<S>(XT + ((size_t)m * N + row[j]) * S, x);
+          else
+            load_sub_unaligned<S>(R + row[j] * (uint64_t)D + (uint64_t)m * S, x);
+        } else {
 #pragma unroll
-    for (int j = 0; j < kPtsPerThread; ++j) {
-      if (MODE == kModeLloyd) {
-        // vec.argmin starts from dists[0]: a NaN there wins by default.
-        if (isnan(d0[j])) { bi[j] = 0; best[j] = d0[j]; }
-        if (ok[j]) {
-          asg[(size_t)m * N + row[j]] = (uint8_t)bi[j];
-          mind[(size_t)m * N + row[j]] = best[j];
-          atomicAdd(&h[m * K + bi[j]], 1u);
+          for (int k = 0; k < S; ++k) x[k] = 0.f;
         }
-      } else {
-        if (ok[j]) {
+#pragma unroll
+        for (int k = 0; k < S; ++k) xx[j][k] = make_float2(x[k], x[k]);
+      }
+      float best[kPtsPerThread], d0[kPtsPerThread];
+      int bi[kPtsPerThread];
+#pragma unroll
+      for (int j = 0; j < kPtsPerThread; ++j) {
+        best[j] = __int_as_float(0x7f800000);
+        bi[j] = 0;
+        d0[j] = 0.f;
+      }
+      const float2* cm = cbp + (size_t)m * KP * S;
+      for (int p = 0; p < KP; ++p) {
+        float2 nc[S];
+#pragma unroll
+        for (int k = 0; k < S; ++k) nc[k] = cm[p * S + k];
+#pragma unroll
+        for (int j = 0; j < kPtsPerThread; ++j) {
+          const float2 dd = l2_small_pair<S>(xx[j], nc, one2);
+          if (p == 0) d0[j] = dd.x;
+          if (dd.x < best[j]) { best[j] = dd.x; bi[j] = 2 * p; }
+          if (dd.y < best[j]) { best[j] = dd.y; bi[j] = 2 * p + 1; }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPtsPerThread; ++j) {
+        if (MODE == kModeLloyd) {
+          // vec.argmin starts from dists[0]: a NaN there wins by default.
+          if (isnan(d0[j])) { bi[j] = 0; best[j] = d0[j]; }
+          if (ok[j]) {
+            asg[(size_t)m * N + row[j]] = (uint8_t)bi[j];
+            mind[(size_t)m * N + row[j]] = best[j];
+            atomicAdd(&h[m * K + bi[j]], 1u);
+          }
+        } else if (ok[j]) {
           packed[j] |= (uint32_t)bi[j] << (8 * (m & 3));
           if ((m & 3) == 3 || m == M - 1) {
             uint8_t* dst = codes + row[j] * (uint64_t)M + (m & ~3);
@@ -165,7 +219,7 @@ pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
   if (MODE == kModeLloyd) {
     __syncthreads();
     const int nblk = gridDim.x;
-    for (int e = threadIdx.x; e < M * K; e += kThreads) {
+    for (int e = threadIdx.x; e < M * K; e += kAsgThreads) {
       const int m = e / K, c = e % K;
       hist[((size_t)m * nblk + blockIdx.x) * K + c] = h[e];
     }
@@ -177,9 +231,8 @@ pq_assign_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
 // b = start[c] + sum_{b' < b} hist[b'][c].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K,
-               uint32_t* __restrict__ counts, uint32_t* __restrict__ starts,
-               const uint8_t* __restrict__ state) {
+pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K, uint32_t* __restrict__ counts,
+               uint32_t* __restrict__ starts, const uint8_t* __restrict__ state) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   __shared__ uint32_t tot[256];
@@ -190,8 +243,7 @@ pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K,
     for (int b = 0; b < nblk; ++b) total += hm[(size_t)b * K + c];
   tot[c] = c < K ? total : 0u;
   __syncthreads();
-  // exclusive scan over clusters (256 entries, Hillis-Steele)
-  for (int o = 1; o < 256; o <<= 1) {
+  for (int o = 1; o < 256; o <<= 1) {  // inclusive Hillis-Steele scan
     const uint32_t v = c >= o ? tot[c - o] : 0u;
     __syncthreads();
     tot[c] += v;
@@ -211,142 +263,132 @@ pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K,
 }
 
 // ---------------------------------------------------------------------------
-// Stable scatter of every subspace's rows into cluster order. Rows of a CTA
-// are ranked in row order: 16 groups of 32 consecutive rows, ranks within a
-// group from __match_any_sync, group prefixes per cluster in shared memory.
+// Stable scatter into cluster order. One warp per subspace walks the CTA's
+// row range 32 rows at a time: ranks inside the 32 from __match_any_sync,
+// per-cluster running offsets in shared memory owned by the warp. No block
+// barrier in the loop.
 // ---------------------------------------------------------------------------
 template <int S>
-__global__ void __launch_bounds__(kThreads)
-pq_scatter_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K,
-                  const uint8_t* __restrict__ asg, const uint32_t* __restrict__ bases,
-                  float* __restrict__ sorted, const uint8_t* __restrict__ state) {
-  constexpr int kGroups = kTile / 32;
-  __shared__ uint32_t gcnt[kGroups][256];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint64_t base = (uint64_t)blockIdx.x * kTile;
+__global__ void pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int M, int K,
+                                  const uint8_t* __restrict__ asg, const uint32_t* __restrict__ bases,
+                                  float* __restrict__ sorted, const uint8_t* __restrict__ state,
+                                  uint64_t rows_per_cta) {
+  __shared__ uint32_t run_all[kMaxM][256];
+  const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+  if (m >= M || state[m] != kRunning) return;
+  uint32_t* run = run_all[m];
   const int nblk = gridDim.x;
-  for (int m = 0; m < M; ++m) {
-    if (state[m] != kRunning) continue;
-    for (int e = threadIdx.x; e < kGroups * 256; e += kThreads) (&gcnt[0][0])[e] = 0u;
-    __syncthreads();
-    int cl[kPtsPerThread], rank[kPtsPerThread];
+  for (int c = lane; c < K; c += 32) run[c] = bases[((size_t)m * nblk + blockIdx.x) * K + c];
+  __syncwarp();
+  const uint64_t lo = (uint64_t)blockIdx.x * rows_per_cta;
+  const uint64_t hi = min(N, lo + rows_per_cta);
+  const uint8_t* am = asg + (size_t)m * N;
+  const float* xm = XT + (size_t)m * N * S;
+  float* sm = sorted + (size_t)m * N * S;
+  constexpr int kU = 4;  // 32-row groups loaded ahead
+  for (uint64_t base = lo; base < hi; base += 32 * kU) {
+    int cl[kU];
+    float x[kU][S];
 #pragma unroll
-    for (int j = 0; j < kPtsPerThread; ++j) {
-      const uint64_t r = base + (uint64_t)j * kThreads + threadIdx.x;
-      const bool ok = r < N;
-      cl[j] = ok ? (int)asg[(size_t)m * N + r] : 256 + lane;  // unique dummy keys
-      const uint32_t peers = __match_any_sync(0xffffffffu, cl[j]);
-      rank[j] = __popc(peers & lanemask_lt());
-      const int g = j * (kThreads / 32) + warp;
-      if (ok && rank[j] == 0) gcnt[g][cl[j]] = __popc(peers);
-    }
-    __syncthreads();
-    {  // exclusive prefix over groups, per cluster
-      const int c = threadIdx.x;
-      uint32_t run = 0;
-      for (int g = 0; g < kGroups; ++g) {
-        const uint32_t v = gcnt[g][c];
-        gcnt[g][c] = run;
-        run += v;
+    for (int u = 0; u < kU; ++u) {
+      const uint64_t r = base + (uint64_t)u * 32 + lane;
+      if (r < hi) {
+        cl[u] = am[r];
+        load_sub<S>(xm + r * S, x[u]);
+      } else {
+        cl[u] = 256 + lane;  // unique keys never match a real cluster
+#pragma unroll
+        for (int k = 0; k < S; ++k) x[u][k] = 0.f;
       }
     }
-    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < kPtsPerThread; ++j) {
-      const uint64_t r = base + (uint64_t)j * kThreads + threadIdx.x;
-      if (r < N) {
-        const int g = j * (kThreads / 32) + warp;
-        const uint32_t dst = bases[((size_t)m * nblk + blockIdx.x) * K + cl[j]] +
-                             gcnt[g][cl[j]] + (uint32_t)rank[j];
-        const float* src = R + r * (uint64_t)D + (uint64_t)m * S;
-        float* o = sorted + ((size_t)m * N + dst) * S;
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t peers = __match_any_sync(0xffffffffu, cl[u]);
+      const uint32_t rank = __popc(peers & lanemask_lt());
+      const bool ok = cl[u] < 256;
+      uint32_t dst = 0;
+      if (ok) dst = run[cl[u]] + rank;
+      __syncwarp();
+      if (ok && rank == 0) run[cl[u]] += __popc(peers);
+      __syncwarp();
+      if (ok) {
+        float* o = sm + (size_t)dst * S;
         if constexpr (S == 4) {
-          *reinterpret_cast<float4*>(o) = make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+          *reinterpret_cast<float4*>(o) = make_float4(x[u][0], x[u][1], x[u][2], x[u][3]);
         } else if constexpr (S == 2) {
-          *reinterpret_cast<float2*>(o) = make_float2(__ldg(src), __ldg(src + 1));
+          *reinterpret_cast<float2*>(o) = make_float2(x[u][0], x[u][1]);
         } else {
-          o[0] = __ldg(src);
+          o[0] = x[u][0];
         }
       }
     }
-    __syncthreads();
   }
 }
 
 // ---------------------------------------------------------------------------
-// Centroid sums in the reference order: one warp per 32 clusters of a
-// subspace, lane = cluster, S sequential f32 chains per lane. Cluster
-// members stream through a multi-stage cp.async ring in shared memory.
-// Empty clusters are left for the reseed kernel.
+// Centroid sums in the reference order. A warp covers 32/S clusters of one
+// subspace; lane = (cluster j, coordinate k) runs one sequential f32 chain.
+// Cluster members stream through a cp.async ring in shared memory
+// (kChainE elements per cluster per stage). Empty clusters are left for the
+// reseed kernel.
 // ---------------------------------------------------------------------------
 template <int S>
-__global__ void __launch_bounds__(32)
-pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int K,
+__global__ void __launch_bounds__(kChainWarps * 32)
+pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
                 const uint32_t* __restrict__ counts, const uint32_t* __restrict__ starts,
                 float* __restrict__ cb, const uint8_t* __restrict__ state) {
-  extern __shared__ __align__(16) float ring[];  // [stages][32][(CH+1)*S]
-  constexpr int kRow = (kChainCh + 1) * S;      // padded: conflict-free reads
-  constexpr int kStage = 32 * kRow;
-  const int wpm = (K + 31) / 32;
-  const int m = blockIdx.x / wpm;
-  const int c0 = (blockIdx.x % wpm) * 32;
+  constexpr int CPW = 32 / S;              // clusters per warp
+  constexpr int kRow = kChainE * S + S;    // padded: conflict-free reads
+  constexpr int kStage = CPW * kRow;
+  extern __shared__ __align__(16) float ring_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* ring = ring_all + (size_t)warp * kChainStages * kStage;
+  const int wpm = (K + CPW - 1) / CPW;
+  const int gw = blockIdx.x * kChainWarps + warp;
+  if (gw >= M * wpm) return;
+  const int m = gw / wpm;
   if (state[m] != kRunning) return;
-  const int lane = threadIdx.x;
-  const int c = c0 + lane;
+  const int j = lane / S, k = lane % S;
+  const int c = (gw % wpm) * CPW + j;
   const uint32_t cnt = c < K ? counts[(size_t)m * K + c] : 0u;
   const uint32_t st = c < K ? starts[(size_t)m * K + c] : 0u;
   uint32_t maxcnt = cnt;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) maxcnt = max(maxcnt, __shfl_xor_sync(0xffffffffu, maxcnt, o));
-  const int nst = (int)((maxcnt + kChainCh - 1) / kChainCh);
+  const int nst = (int)((maxcnt + kChainE - 1) / kChainE);
   const float* sm = sorted + (size_t)m * N * S;
 
   auto issue = [&](int t) {
     if (t < nst) {
       float* dstage = ring + (t % kChainStages) * kStage;
-      for (int j = 0; j < 32; ++j) {
-        const uint32_t cj = __shfl_sync(0xffffffffu, cnt, j);
-        const uint32_t sj = __shfl_sync(0xffffffffu, st, j);
-        const uint32_t e = (uint32_t)t * kChainCh + lane;
-        if (e < cj) cp_async<4 * S>(dstage + j * kRow + lane * S, sm + (size_t)(sj + e) * S);
+      for (int jj = 0; jj < CPW; ++jj) {
+        const uint32_t cj = __shfl_sync(0xffffffffu, cnt, jj * S);
+        const uint32_t sj = __shfl_sync(0xffffffffu, st, jj * S);
+        for (int e = lane; e < kChainE; e += 32) {
+          const uint32_t g = (uint32_t)t * kChainE + e;
+          if (g < cj) cp_async<4 * S>(dstage + jj * kRow + e * S, sm + (size_t)(sj + g) * S);
+        }
       }
     }
     cp_async_commit();
   };
 
-  float acc[S];
-#pragma unroll
-  for (int k = 0; k < S; ++k) acc[k] = 0.f;
+  float acc = 0.f;
   for (int t = 0; t < kChainStages - 1; ++t) issue(t);
   for (int t = 0; t < nst; ++t) {
     cp_async_wait<kChainStages - 2>();
     __syncwarp();
-    const float* src = ring + (t % kChainStages) * kStage + lane * kRow;
-    const uint32_t done = (uint32_t)t * kChainCh;
-    const int n = cnt > done ? (int)min((uint32_t)kChainCh, cnt - done) : 0;
-    for (int e = 0; e < n; ++e) {
-      if constexpr (S == 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src + e * 4);
-        acc[0] = __fadd_rn(acc[0], v.x);
-        acc[1] = __fadd_rn(acc[1], v.y);
-        acc[2] = __fadd_rn(acc[2], v.z);
-        acc[3] = __fadd_rn(acc[3], v.w);
-      } else if constexpr (S == 2) {
-        const float2 v = *reinterpret_cast<const float2*>(src + e * 2);
-        acc[0] = __fadd_rn(acc[0], v.x);
-        acc[1] = __fadd_rn(acc[1], v.y);
-      } else {
-        acc[0] = __fadd_rn(acc[0], src[e]);
-      }
-    }
+    const float* src = ring + (t % kChainStages) * kStage + j * kRow + k;
+    const uint32_t done = (uint32_t)t * kChainE;
+    const int n = cnt > done ? (int)min((uint32_t)kChainE, cnt - done) : 0;
+    for (int e = 0; e < n; ++e) acc = __fadd_rn(acc, src[e * S]);
     __syncwarp();
     issue(t + kChainStages - 1);
   }
   cp_async_wait<0>();
   if (c < K && cnt > 0) {
     const float inv = __fdiv_rn(1.0f, __uint2float_rn(cnt));
-#pragma unroll
-    for (int k = 0; k < S; ++k) cb[((size_t)m * K + c) * S + k] = __fmul_rn(acc[k], inv);
+    cb[((size_t)m * K + c) * S + k] = __fmul_rn(acc, inv);
   }
 }
 
@@ -413,7 +455,7 @@ __device__ uint64_t block_argmax_first(const float* v, uint64_t n) {
 // relative-WCSS convergence test (kmeans.zig:214-223).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
-pq_reseed_converge_kernel(const float* __restrict__ R, uint64_t N, int D, int S, int K,
+pq_reseed_converge_kernel(const float* __restrict__ XT, uint64_t N, int S, int K,
                           const uint32_t* __restrict__ counts, float* __restrict__ mind,
                           float* __restrict__ cb, uint8_t* __restrict__ state,
                           const float* __restrict__ wcss, float* __restrict__ prev_wcss,
@@ -433,7 +475,7 @@ pq_reseed_converge_kernel(const float* __restrict__ R, uint64_t N, int D, int S,
       if (counts[(size_t)m * K + c] != 0) continue;
       const uint64_t far = block_argmax_first(mm, N);
       if (threadIdx.x < (unsigned)S)
-        cb[((size_t)m * K + c) * S + threadIdx.x] = R[far * (uint64_t)D + (uint64_t)m * S + threadIdx.x];
+        cb[((size_t)m * K + c) * S + threadIdx.x] = XT[((size_t)m * N + far) * S + threadIdx.x];
       __syncthreads();
       if (threadIdx.x == 0) {
         mm[far] = -__int_as_float(0x7f800000);
@@ -460,57 +502,82 @@ pq_reseed_converge_kernel(const float* __restrict__ R, uint64_t N, int D, int S,
 // ---------------------------------------------------------------------------
 // k-means++ seeding
 // ---------------------------------------------------------------------------
-__global__ void pq_seed_init_kernel(const float* __restrict__ R, int D, int S, int K,
+__global__ void pq_seed_init_kernel(const float* __restrict__ XT, uint64_t N, int S, int K,
                                     const uint64_t* __restrict__ idx0, float* __restrict__ cb,
                                     uint64_t* __restrict__ chosen) {
   const int m = blockIdx.x;
   if (threadIdx.x < (unsigned)S)
-    cb[(size_t)m * K * S + threadIdx.x] = R[idx0[m] * (uint64_t)D + (uint64_t)m * S + threadIdx.x];
+    cb[(size_t)m * K * S + threadIdx.x] = XT[((size_t)m * N + idx0[m]) * S + threadIdx.x];
   if (threadIdx.x == 0) chosen[(size_t)m * K] = idx0[m];
 }
 
-// min_dist update with centroid `step` (kmeans.zig:117-135) fused with the
-// per-CTA directed-rounding partial sums of the new weights.
+// min_dist update with centroid `step` (kmeans.zig:117-135), fused with the
+// per-chunk directed-rounding sums of the new weights and the count of
+// non-zero weights below thr[m] (the weights whose f64 addition may round,
+// see pq_seed_select_kernel).
 template <int S>
-__global__ void __launch_bounds__(kThreads)
-pq_seed_update_kernel(const float* __restrict__ R, uint64_t N, int D, int M, int K, int step,
+__global__ void __launch_bounds__(kSeedThreads)
+pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, int step,
                       const float* __restrict__ cb, float* __restrict__ md,
-                      double2* __restrict__ chunk, int* __restrict__ nonfinite,
-                      const uint8_t* __restrict__ state) {
-  __shared__ double2 red[kThreads / 32];
+                      double2* __restrict__ chunk, uint32_t* __restrict__ chunk_cnt,
+                      int* __restrict__ nonfinite, const uint8_t* __restrict__ state,
+                      const double* __restrict__ thr) {
+  __shared__ double2 wp[kSeedThreads / 32][kMaxM];
+  __shared__ uint32_t wc[kSeedThreads / 32][kMaxM];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint64_t i = (uint64_t)blockIdx.x * kSeedChunk + threadIdx.x;
   const int nchunk = gridDim.x;
   for (int m = 0; m < M; ++m) {
     if (state[m] != kRunning) continue;
-    const float* c = cb + ((size_t)m * K + step) * S;
-    float w = 0.f;
-    if (i < N) {
-      float x[S], cc[S];
-      load_sub<S>(R + i * (uint64_t)D + (uint64_t)m * S, x);
+    float c[S];
 #pragma unroll
-      for (int k = 0; k < S; ++k) cc[k] = c[k];
-      const float d = l2_small<S>(x, cc);
-      float* slot = md + (size_t)m * N + i;
-      if (step == 0) {
-        w = d;
-      } else {
-        const float old = *slot;
-        w = d < old ? d : old;
+    for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
+    const double T = thr[m];
+    double lo = 0.0, hi = 0.0;
+    uint32_t cnt = 0;
+    bool bad = false;
+#pragma unroll
+    for (int u = 0; u < kSeedRowsPerThread; ++u) {
+      const uint64_t r = (uint64_t)blockIdx.x * kSeedChunk + (uint64_t)u * kSeedThreads + threadIdx.x;
+      if (r < N) {
+        float x[S];
+        load_sub<S>(XT + ((size_t)m * N + r) * S, x);
+        const float d = l2_small<S>(x, c);
+        float* slot = md + (size_t)m * N + r;
+        float w;
+        if (step == 0) {
+          w = d;
+        } else {
+          const float old = *slot;
+          w = d < old ? d : old;
+        }
+        *slot = w;
+        bad |= !isfinite(w) || w < 0.f;
+        lo = __dadd_rd(lo, (double)w);
+        hi = __dadd_ru(hi, (double)w);
+        cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
       }
-      *slot = w;
-      if (!isfinite(w) || w < 0.f) nonfinite[m] = 1;
     }
-    const double lo = warp_sum_rd((double)w);
-    const double hi = warp_sum_ru((double)w);
-    if (lane == 0) red[warp] = make_double2(lo, hi);
-    __syncthreads();
-    if (warp == 0) {
-      double2 v = lane < kThreads / 32 ? red[lane] : make_double2(0.0, 0.0);
-      const double l2 = warp_sum_rd(v.x), h2 = warp_sum_ru(v.y);
-      if (lane == 0) chunk[(size_t)m * nchunk + blockIdx.x] = make_double2(l2, h2);
+    if (bad) nonfinite[m] = 1;
+    lo = warp_sum_rd(lo);
+    hi = warp_sum_ru(hi);
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (lane == 0) {
+      wp[warp][m] = make_double2(lo, hi);
+      wc[warp][m] = cnt;
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  for (int m = threadIdx.x; m < M; m += kSeedThreads) {
+    if (state[m] != kRunning) continue;
+    double lo = 0.0, hi = 0.0;
+    uint32_t cnt = 0;
+    for (int w = 0; w < kSeedThreads / 32; ++w) {
+      lo = __dadd_rd(lo, wp[w][m].x);
+      hi = __dadd_ru(hi, wp[w][m].y);
+      cnt += wc[w][m];
+    }
+    chunk[(size_t)m * nchunk + blockIdx.x] = make_double2(lo, hi);
+    chunk_cnt[(size_t)m * nchunk + blockIdx.x] = cnt;
   }
 }
 
@@ -522,69 +589,114 @@ __device__ __forceinline__ double gamma_bound(uint64_t n) {
   return __ddiv_ru(g, __dsub_rd(1.0, g));
 }
 
-// Draw for centroid `step` (weightedSample, rng.zig:57-82): candidate from
-// the directed-rounding prefix bounds, accepted when the reference's
-// sequential f64 prefix provably selects the same row; otherwise the exact
-// sequential chain decides.
+// Draw for centroid `step` (weightedSample, rng.zig:57-82).
+//
+// The reference returns the first i with u < S_i, where S_i is the
+// sequential f64 sum of the first i+1 weights and u = fl(r * S_N). Here:
+//   * Lo_i <= E_i <= Hi_i bound the exact prefix E_i (directed rounding);
+//   * |S_i - E_i| <= B, with B the smaller of the classic gamma bound and a
+//     tighter one: an f64 add of a non-negative f32 weight w to a sum whose
+//     binade does not change is exact unless w has bits below the sum's
+//     ulp, which needs w < 2^23 * G with G = 2^(E-52) the largest ulp any
+//     prefix can have (E = exponent of an upper bound of S_N). So at most
+//     (#weights below 2^23 G) + (#binade crossings) adds round, each by at
+//     most G/2. The weights are counted below the previous draw's threshold
+//     (weights never grow between draws), and the tight bound is used only
+//     when that threshold covers the current one;
+//   * the candidate row is accepted when u's interval lies strictly between
+//     the intervals of S_{i-1} and S_i. Otherwise one thread runs the
+//     reference's sequential chain.
 __global__ void __launch_bounds__(kSelectThreads)
-pq_seed_select_kernel(const float* __restrict__ R, uint64_t N, int D, int S, int K, int step,
+pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, int step,
                       float* __restrict__ cb, const float* __restrict__ md,
-                      const double2* __restrict__ chunk, int nchunk,
-                      const double* __restrict__ draws, int* __restrict__ nonfinite,
+                      const double2* __restrict__ chunk, const uint32_t* __restrict__ chunk_cnt,
+                      int nchunk, const double* __restrict__ draws, int* __restrict__ nonfinite,
                       int* __restrict__ status, uint8_t* __restrict__ state,
-                      uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen) {
+                      uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen,
+                      double* __restrict__ thr) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kWarps = kSelectThreads / 32;
   __shared__ double2 wsum[kWarps];
+  __shared__ unsigned long long wcnt[kWarps];
   __shared__ double2 incl_all[kSelectThreads];
-  __shared__ double2 sh_excl;      // exclusive prefix of the found chunk
+  __shared__ double2 sh_excl;
   __shared__ int sh_chunk;
-  __shared__ double2 pre[kSeedChunk];  // element inclusive prefixes in the chunk
   __shared__ uint64_t sh_idx;
   __shared__ int sh_decided;
-  __shared__ float tile[4096];
-  __shared__ double sh_u;
 
   if (nonfinite[m]) {  // weightedSample validates every weight first
     if (tid == 0) { status[m] = MVR_E_NON_FINITE; state[m] = kFailed; }
     return;
   }
   const double2* ch = chunk + (size_t)m * nchunk;
+  const uint32_t* cc = chunk_cnt + (size_t)m * nchunk;
   const float* w = md + (size_t)m * N;
   const double r = draws[(size_t)m * K + step];
 
-  // 1. per-thread contiguous chunk ranges, then a block scan of the totals
+  // 1. contiguous chunk ranges per thread, block scan of the totals
   const int cpt = (nchunk + kSelectThreads - 1) / kSelectThreads;
   const int c_lo = min(nchunk, tid * cpt), c_hi = min(nchunk, c_lo + cpt);
   double tlo = 0.0, thi = 0.0;
-  for (int j = c_lo; j < c_hi; ++j) { tlo = __dadd_rd(tlo, ch[j].x); thi = __dadd_ru(thi, ch[j].y); }
-  double ilo = warp_scan_rd(tlo, lane), ihi = warp_scan_ru(thi, lane);
+  unsigned tcnt = 0;
+  for (int j = c_lo; j < c_hi; ++j) {
+    tlo = __dadd_rd(tlo, ch[j].x);
+    thi = __dadd_ru(thi, ch[j].y);
+    tcnt += cc[j];
+  }
+  const double ilo = warp_scan_rd(tlo, lane), ihi = warp_scan_ru(thi, lane);
+  const unsigned wc = __reduce_add_sync(0xffffffffu, tcnt);
   if (lane == 31) wsum[warp] = make_double2(ilo, ihi);
+  if (lane == 0) wcnt[warp] = wc;
   __syncthreads();
   if (warp == 0) {
-    double a = wsum[lane].x, b = wsum[lane].y;
-    a = warp_scan_rd(a, lane);
-    b = warp_scan_ru(b, lane);
+    const double a = warp_scan_rd(wsum[lane].x, lane);
+    const double b = warp_scan_ru(wsum[lane].y, lane);
+    unsigned long long cs = wcnt[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+    __syncwarp();
     wsum[lane] = make_double2(a, b);
+    wcnt[lane] = cs;
   }
   __syncthreads();
   const double wlo = warp > 0 ? wsum[warp - 1].x : 0.0, whi = warp > 0 ? wsum[warp - 1].y : 0.0;
   const double incl_lo = __dadd_rd(wlo, ilo), incl_hi = __dadd_ru(whi, ihi);
   const double Lo_N = wsum[kWarps - 1].x, Hi_N = wsum[kWarps - 1].y;
+  const unsigned long long C_N = wcnt[0];
   if (Hi_N <= 0.0) {  // every weight is exactly zero
     if (tid == 0) { status[m] = MVR_E_ALL_ZERO; state[m] = kFailed; }
     return;
   }
+
+  // 2. error bound of the sequential chain
+  const double gN = gamma_bound(N);
+  const double shi_classic = __dadd_ru(Hi_N, __dmul_ru(gN, Hi_N));
+  int e2 = 0;
+  (void)frexp(shi_classic, &e2);          // shi_classic < 2^e2
+  const double G = ldexp(1.0, e2 - 53);   // >= ulp of every prefix
+  const double thr_now = ldexp(G, 23);
+  const double B_tight = __dmul_ru(__ull2double_ru(C_N + kCrossingSlack), 0.5 * G);
+  const double thr_prev = thr[m];
+  const bool tight_ok = thr_now <= thr_prev;
+  auto bound_at = [&](uint64_t terms, double hi_prefix) {
+    const double bg = __dmul_ru(gamma_bound(terms), hi_prefix);
+    return tight_ok ? fmin(bg, B_tight) : bg;
+  };
+
   const double u_mid = r * (0.5 * (Lo_N + Hi_N));
   const bool past = !(u_mid < 0.5 * (incl_lo + incl_hi));
   incl_all[tid] = make_double2(incl_lo, incl_hi);
   const int n_before = __syncthreads_count(past);  // prefixes are monotone
-  if (tid == 0) { sh_decided = 0; sh_chunk = -1; }
+  if (tid == 0) {
+    sh_decided = 0;
+    sh_chunk = -1;
+    if (thr_now < thr_prev) thr[m] = thr_now;  // threshold for the next draw
+  }
   __syncthreads();
 
-  // 2. the first thread whose inclusive mid-prefix exceeds u_mid walks its
+  // 3. the first thread whose inclusive mid-prefix exceeds u_mid walks its
   //    chunks, starting from its predecessor's inclusive bounds.
   if (n_before < kSelectThreads && tid == n_before) {
     double lo = tid > 0 ? incl_all[tid - 1].x : 0.0;
@@ -593,105 +705,103 @@ pq_seed_select_kernel(const float* __restrict__ R, uint64_t N, int D, int S, int
     for (int j = c_lo; j < c_hi; ++j) {
       const double nlo = __dadd_rd(lo, ch[j].x), nhi = __dadd_ru(hi, ch[j].y);
       if (u_mid < 0.5 * (nlo + nhi)) { found = j; break; }
-      lo = nlo; hi = nhi;
+      lo = nlo;
+      hi = nhi;
     }
     sh_chunk = found;
     sh_excl = make_double2(lo, hi);
   }
   __syncthreads();
 
-  // 3. fine search inside the chunk (warp 0, 8 rows per lane)
-  if (sh_chunk >= 0 && warp == 0) {
-    const uint64_t cbase = (uint64_t)sh_chunk * kSeedChunk;
-    constexpr int kPer = kSeedChunk / 32;
-    double llo[kPer], lhi[kPer];
-    double slo = 0.0, shi = 0.0;
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      const uint64_t i = cbase + (uint64_t)lane * kPer + e;
-      const double v = i < N ? (double)w[i] : 0.0;
-      slo = __dadd_rd(slo, v); shi = __dadd_ru(shi, v);
-      llo[e] = slo; lhi[e] = shi;
+  // 4. fine search inside the chunk: one thread per row, block scan
+  const int fchunk = sh_chunk;
+  if (fchunk >= 0) {
+    const uint64_t i = (uint64_t)fchunk * kSeedChunk + tid;
+    const double v = i < N ? (double)w[i] : 0.0;
+    const double slo = warp_scan_rd(v, lane), shi = warp_scan_ru(v, lane);
+    if (lane == 31) wsum[warp] = make_double2(slo, shi);
+    __syncthreads();
+    if (warp == 0) {
+      const double a = warp_scan_rd(wsum[lane].x, lane);
+      const double b = warp_scan_ru(wsum[lane].y, lane);
+      __syncwarp();
+      wsum[lane] = make_double2(a, b);
     }
-    const double plo = warp_scan_rd(slo, lane), phi = warp_scan_ru(shi, lane);
-    double xlo = __shfl_up_sync(0xffffffffu, plo, 1), xhi = __shfl_up_sync(0xffffffffu, phi, 1);
-    if (lane == 0) { xlo = 0.0; xhi = 0.0; }
+    __syncthreads();
     const double2 ex = sh_excl;
-    const double blo = __dadd_rd(ex.x, xlo), bhi = __dadd_ru(ex.y, xhi);
-    int first = -1;
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      const double elo = __dadd_rd(blo, llo[e]), ehi = __dadd_ru(bhi, lhi[e]);
-      pre[lane * kPer + e] = make_double2(elo, ehi);
-      const uint64_t i = cbase + (uint64_t)lane * kPer + e;
-      if (first < 0 && i < N && u_mid < 0.5 * (elo + ehi)) first = e;
-    }
-    __syncwarp();
-    const uint32_t bal = __ballot_sync(0xffffffffu, first >= 0);
-    if (bal) {
-      const int fl = __ffs(bal) - 1;
-      const int fe = __shfl_sync(0xffffffffu, first, fl);
-      if (lane == 0) {
-        const int e = fl * kPer + fe;
-        const uint64_t istar = cbase + (uint64_t)e;
-        const double2 cur = pre[e];
-        const double2 prv = e > 0 ? pre[e - 1] : ex;
-        const double gN = gamma_bound(N);
-        const double SLoN = __dsub_rd(Lo_N, __dmul_ru(gN, Hi_N));
-        const double SHiN = __dadd_ru(Hi_N, __dmul_ru(gN, Hi_N));
-        // u = fl(r * S_N) lies between the directed roundings of r * S_N.
-        const double ULo = __dmul_rd(r, SLoN);
-        const double UHi = __dmul_ru(r, SHiN);
-        const double gi = gamma_bound(istar + 1);
-        const double SLoI = __dsub_rd(cur.x, __dmul_ru(gi, cur.y));
-        bool ok = UHi < SLoI;
-        if (istar > 0) {
-          const double gp = gamma_bound(istar);
-          const double SHiP = __dadd_ru(prv.y, __dmul_ru(gp, prv.y));
-          ok = ok && (ULo >= SHiP);
-        }
-        if (ok) { sh_idx = istar; sh_decided = 1; }
+    const double plo = warp > 0 ? wsum[warp - 1].x : 0.0, phi = warp > 0 ? wsum[warp - 1].y : 0.0;
+    const double elo = __dadd_rd(ex.x, __dadd_rd(plo, slo));
+    const double ehi = __dadd_ru(ex.y, __dadd_ru(phi, shi));
+    incl_all[tid] = make_double2(elo, ehi);
+    // Rows past N sort after every real row: counting them as hits keeps the
+    // hits a suffix, and a first hit past N means no candidate.
+    const bool hit = i >= N || u_mid < 0.5 * (elo + ehi);
+    const int first = __syncthreads_count(!hit);
+    if (first < kSelectThreads && tid == first && i < N) {
+      const uint64_t istar = i;
+      const double2 prv = tid > 0 ? incl_all[tid - 1] : ex;
+      const double BN = bound_at(N, Hi_N);
+      const double SLoN = __dsub_rd(Lo_N, BN);
+      const double SHiN = __dadd_ru(Hi_N, BN);
+      // u = fl(r * S_N) lies between the directed roundings of r * S_N.
+      const double ULo = __dmul_rd(r, SLoN);
+      const double UHi = __dmul_ru(r, SHiN);
+      const double SLoI = __dsub_rd(elo, bound_at(istar + 1, ehi));
+      bool ok = UHi < SLoI;
+      if (istar > 0) {
+        const double SHiP = __dadd_ru(prv.y, bound_at(istar, prv.y));
+        ok = ok && (ULo >= SHiP);
+      }
+      if (ok) {
+        sh_idx = istar;
+        sh_decided = 1;
       }
     }
   }
   __syncthreads();
 
-  // 4. undecided: the reference's sequential chain, verbatim.
-  if (!sh_decided) {
+  // 5. undecided: the reference's sequential chain, by one thread.
+  if (!sh_decided && tid == 0) {
     double total = 0.0;
     uint64_t last_pos = 0;
-    for (uint64_t t0 = 0; t0 < N; t0 += 4096) {
-      const uint32_t n = (uint32_t)min((uint64_t)4096, N - t0);
-      for (uint32_t e = tid; e < n; e += kSelectThreads) tile[e] = w[t0 + e];
-      __syncthreads();
-      if (tid == 0)
-        for (uint32_t e = 0; e < n; ++e) {
-          total = __dadd_rn(total, (double)tile[e]);
-          if (tile[e] != 0.f) last_pos = t0 + e;
-        }
-      __syncthreads();
+    uint64_t i = 0;
+    for (; i + 8 <= N; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = w[i + q];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        total = __dadd_rn(total, (double)v[q]);
+        if (v[q] != 0.f) last_pos = i + q;
+      }
     }
-    if (tid == 0) { sh_u = __dmul_rn(r, total); sh_idx = last_pos; }
-    __syncthreads();
-    const double u = sh_u;
+    for (; i < N; ++i) {
+      total = __dadd_rn(total, (double)w[i]);
+      if (w[i] != 0.f) last_pos = i;
+    }
+    const double u = __dmul_rn(r, total);
     double cum = 0.0;
-    for (uint64_t t0 = 0; t0 < N; t0 += 4096) {
-      const uint32_t n = (uint32_t)min((uint64_t)4096, N - t0);
-      for (uint32_t e = tid; e < n; e += kSelectThreads) tile[e] = w[t0 + e];
-      __syncthreads();
-      if (tid == 0 && !sh_decided)
-        for (uint32_t e = 0; e < n; ++e) {
-          cum = __dadd_rn(cum, (double)tile[e]);
-          if (u < cum) { sh_idx = t0 + e; sh_decided = 1; break; }
-        }
-      __syncthreads();
-      if (sh_decided) break;
+    uint64_t pick = last_pos;  // the reference's fallback: last positive weight
+    bool got = false;
+    for (i = 0; i + 8 <= N && !got; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = w[i + q];
+      for (int q = 0; q < 8; ++q) {
+        cum = __dadd_rn(cum, (double)v[q]);
+        if (u < cum) { pick = i + q; got = true; break; }
+      }
     }
-    if (tid == 0) fallbacks[m] += 1;
+    for (; i < N && !got; ++i) {
+      cum = __dadd_rn(cum, (double)w[i]);
+      if (u < cum) { pick = i; got = true; }
+    }
+    sh_idx = pick;
+    fallbacks[m] += 1;
   }
   __syncthreads();
   const uint64_t idx = sh_idx;
-  if (tid < S) cb[((size_t)m * K + step) * S + tid] = R[idx * (uint64_t)D + (uint64_t)m * S + tid];
+  if (tid < S) cb[((size_t)m * K + step) * S + tid] = XT[((size_t)m * N + idx) * S + tid];
   if (tid == 0) chosen[(size_t)m * K + step] = idx;
 }
 
@@ -718,27 +828,28 @@ __global__ void iota_u32_kernel(uint32_t* __restrict__ b, uint64_t N, int M) {
     b[i] = (uint32_t)(i % N);
 }
 
-template <int S>
-size_t assign_smem(int M, int K, int mode) {
-  const size_t kp = (size_t)(K + 1) / 2;
-  size_t b = (size_t)M * kp * S * sizeof(float2);
+// ---------------------------------------------------------------------------
+// host-side launch helpers
+// ---------------------------------------------------------------------------
+size_t assign_smem(int M, int K, int S, int mode) {
+  size_t b = (size_t)M * ((K + 1) / 2) * S * sizeof(float2);
   if (mode == kModeLloyd) b += (size_t)M * K * sizeof(uint32_t);
   return b;
 }
 
 template <int S>
-int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, uint64_t N, int D, int M, int K,
-                  const float* cb, uint8_t* codes, uint8_t* asg, float* mind,
-                  uint32_t* hist, const uint8_t* state, int nblk) {
-  const size_t sm = assign_smem<S>(M, K, mode);
+int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, const float* XT, uint64_t N,
+                  int D, int M, int K, const float* cb, uint8_t* codes, uint8_t* asg, float* mind,
+                  uint32_t* hist, const uint8_t* state, int nblk, uint64_t rows_per_cta) {
+  const size_t sm = assign_smem(M, K, S, mode);
   if (mode == kModeLloyd) {
     auto kern = pq_assign_kernel<S, kModeLloyd>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, st>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
+    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta);
   } else {
     auto kern = pq_assign_kernel<S, kModeEncode>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kThreads, sm, st>>>(R, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f);
+    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta);
   }
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
@@ -747,43 +858,72 @@ int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, uint64_t 
 template <int S>
 int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int M, int K,
                  const uint32_t* counts, const uint32_t* starts, float* cb, const uint8_t* state) {
-  const size_t sm = (size_t)kChainStages * 32 * (kChainCh + 1) * S * sizeof(float);
+  constexpr int CPW = 32 / S;
+  const size_t sm = (size_t)kChainWarps * kChainStages * CPW * (kChainE * S + S) * sizeof(float);
   auto kern = pq_chain_kernel<S>;
   MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-  const int grid = M * ((K + 31) / 32);
-  kern<<<grid, 32, sm, st>>>(sorted, N, K, counts, starts, cb, state);
+  const int warps = M * ((K + CPW - 1) / CPW);
+  const int grid = (warps + kChainWarps - 1) / kChainWarps;
+  kern<<<grid, kChainWarps * 32, sm, st>>>(sorted, N, M, K, counts, starts, cb, state);
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
 }
 
 int check_shape(Ctx* ctx, int D, int M, int S, int K) {
   if (M <= 0 || S <= 0 || D != M * S) return fail(ctx, MVR_E_INVALID_ARGUMENT, "D must equal M*S");
+  if (M > kMaxM) return fail(ctx, MVR_E_INVALID_ARGUMENT, "at most 32 subspaces per call");
   if (S != 1 && S != 2 && S != 4)
     return fail(ctx, MVR_E_INVALID_ARGUMENT, "sub-vector length must be 1, 2 or 4");
   if (K <= 0 || K > 256) return fail(ctx, MVR_E_INVALID_ARGUMENT, "K must be in [1, 256]");
-  const size_t sm = (size_t)M * ((K + 1) / 2) * S * sizeof(float2) + (size_t)M * K * 4;
-  if (sm > 200 * 1024) return fail(ctx, MVR_E_INVALID_ARGUMENT, "codebooks exceed shared memory");
+  // Up to ~100 KB two CTAs share an SM; larger codebook sets (e.g. D = 128)
+  // run one CTA per SM.
+  if (assign_smem(M, K, S, kModeLloyd) > 220 * 1024)
+    return fail(ctx, MVR_E_INVALID_ARGUMENT, "codebooks exceed shared memory");
   return MVR_OK;
 }
 
+// Persistent grid: two CTAs per SM, rows split evenly at warp granularity
+// (every CTA gets the same number of 32-row groups, +-1).
+void grid_for(uint64_t N, int sms, int* nblk, uint64_t* rows_per_cta) {
+  const uint64_t groups = (N + 31) / 32;
+  const uint64_t ctas = std::max<uint64_t>(1, std::min<uint64_t>(groups, (uint64_t)std::max(1, sms) * 2));
+  *rows_per_cta = ((groups + ctas - 1) / ctas) * 32;
+  *nblk = (int)((N + *rows_per_cta - 1) / *rows_per_cta);
+}
+
 }  // namespace
+
+int sm_count_current_device() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    return 148;
+  }
+  return n;
+}
 
 int pq_encode_device(Ctx* ctx, const float* d_cb, int D, int M, const float* d_R, uint64_t N,
                      uint8_t* d_codes) {
   if (N == 0) return MVR_OK;
   const int S = D / M;
   MVR_TRY(check_shape(ctx, D, M, S, 256));
-  const int nblk = (int)((N + kTile - 1) / kTile);
+  int nblk = 0;
+  uint64_t rpc = 0;
+  grid_for(N, ctx->sm_count, &nblk, &rpc);
+  cudaStream_t st = ctx->stream;
   switch (S) {
-    case 1: return launch_assign<1>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
-    case 2: return launch_assign<2>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
-    default: return launch_assign<4>(ctx, ctx->stream, kModeEncode, d_R, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk);
+    case 1: return launch_assign<1>(ctx, st, kModeEncode, d_R, nullptr, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk, rpc);
+    case 2: return launch_assign<2>(ctx, st, kModeEncode, d_R, nullptr, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk, rpc);
+    default: return launch_assign<4>(ctx, st, kModeEncode, d_R, nullptr, N, D, M, 256, d_cb, d_codes, nullptr, nullptr, nullptr, nullptr, nblk, rpc);
   }
 }
 
-PqLayout pq_layout(uint64_t N, int M, int S, int K) {
+PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   PqLayout L;
-  L.nblk = (int)((N + kTile - 1) / kTile);
+  uint64_t rpc = 0;
+  grid_for(N, sms, &L.nblk, &rpc);
+  L.rows_per_cta = rpc;
   L.nchunk = (int)((N + kSeedChunk - 1) / kSeedChunk);
   size_t off = 0;
   auto carve = [&](size_t bytes) {
@@ -795,6 +935,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K) {
   L.o_draws = carve((size_t)M * K * 8);
   L.o_chosen = carve((size_t)M * K * 8);
   L.o_idx0 = carve((size_t)M * 8);
+  L.o_thr = carve((size_t)M * 8);
   L.o_counts = carve((size_t)M * K * 4);
   L.o_starts = carve((size_t)M * K * 4);
   L.o_wcss = carve((size_t)M * 4);
@@ -806,17 +947,19 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K) {
   L.o_rs = carve((size_t)M * 4);
   L.o_state = carve((size_t)M);
   L.small_bytes = off;
+  L.o_xt = carve((size_t)M * N * S * sizeof(float));
   L.o_mind = carve((size_t)M * N * sizeof(float));
   L.o_asg = carve((size_t)M * N);
   L.o_sorted = carve((size_t)M * N * S * sizeof(float));
   L.o_hist = carve((size_t)M * L.nblk * K * sizeof(uint32_t));
   L.o_chunk = carve((size_t)M * L.nchunk * sizeof(double2));
+  L.o_chunk_cnt = carve((size_t)M * L.nchunk * sizeof(uint32_t));
   L.total_bytes = off;
   return L;
 }
 
 int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out, unsigned char* ws,
-                  unsigned char* hsmall) {
+                  unsigned char* hsmall, int sms) {
   const uint64_t N = job.N;
   const int D = job.D, M = job.M, S = job.S, K = job.K;
   MVR_TRY(check_shape(ctx, D, M, S, K));
@@ -846,18 +989,22 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     return MVR_OK;
   }
 
-  const PqLayout L = pq_layout(N, M, S, K);
+  const PqLayout L = pq_layout(N, M, S, K, sms);
   const int nblk = L.nblk, nchunk = L.nchunk;
+  const uint64_t rpc = L.rows_per_cta;
+  float* XT = (float*)(ws + L.o_xt);
   float* mind = (float*)(ws + L.o_mind);
   uint8_t* asg = (uint8_t*)(ws + L.o_asg);
   float* sorted = (float*)(ws + L.o_sorted);
   uint32_t* hist = (uint32_t*)(ws + L.o_hist);
   double2* chunk = (double2*)(ws + L.o_chunk);
+  uint32_t* chunk_cnt = (uint32_t*)(ws + L.o_chunk_cnt);
   unsigned char* small = ws;  // bookkeeping lives at the start of the workspace
   const size_t small_bytes = L.small_bytes;
   double* d_draws = (double*)(small + L.o_draws);
   uint64_t* d_chosen = (uint64_t*)(small + L.o_chosen);
   uint64_t* d_idx0 = (uint64_t*)(small + L.o_idx0);
+  double* d_thr = (double*)(small + L.o_thr);
   uint32_t* d_counts = (uint32_t*)(small + L.o_counts);
   uint32_t* d_starts = (uint32_t*)(small + L.o_starts);
   float* d_wcss = (float*)(small + L.o_wcss);
@@ -869,40 +1016,56 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   uint32_t* d_rs = (uint32_t*)(small + L.o_rs);
   uint8_t* d_state = (uint8_t*)(small + L.o_state);
 
-  // ---- host RNG draws (data independent); the rest of the bookkeeping
-  // starts at zero (state = running, counters = 0) -------------------------
+  // ---- host RNG draws (data independent); thresholds start at +inf; the
+  // rest of the bookkeeping starts at zero (state = running) ---------------
   std::memset(hsmall, 0, small_bytes);
   {
     double* hd = (double*)(hsmall + L.o_draws);
     uint64_t* hi0 = (uint64_t*)(hsmall + L.o_idx0);
+    double* ht = (double*)(hsmall + L.o_thr);
     for (int m = 0; m < M; ++m) {
       Xoshiro256pp rng(job.seed + (uint64_t)m);
       hi0[m] = rng.below(N);
       hd[(size_t)m * K] = 0.0;
       for (int c = 1; c < K; ++c) hd[(size_t)m * K + c] = rng.unit_f64();
+      ht[m] = HUGE_VAL;
     }
   }
   MVR_CUDA(ctx, cudaMemcpyAsync(small, hsmall, small_bytes, cudaMemcpyHostToDevice, st));
 
-  float* cb = out.d_codebooks;
-  pq_seed_init_kernel<<<M, 32, 0, st>>>(job.R, D, S, K, d_idx0, cb, d_chosen);
-  MVR_CUDA(ctx, cudaGetLastError());
-  for (int step = 0; step + 1 < K; ++step) {
+  uint32_t launches = 0;
+  {
+    const int grid = (int)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 8);
     switch (S) {
-      case 1: pq_seed_update_kernel<1><<<nchunk, kThreads, 0, st>>>(job.R, N, D, M, K, step, cb, mind, chunk, d_nonf, d_state); break;
-      case 2: pq_seed_update_kernel<2><<<nchunk, kThreads, 0, st>>>(job.R, N, D, M, K, step, cb, mind, chunk, d_nonf, d_state); break;
-      default: pq_seed_update_kernel<4><<<nchunk, kThreads, 0, st>>>(job.R, N, D, M, K, step, cb, mind, chunk, d_nonf, d_state); break;
+      case 1: pq_transpose_kernel<1><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      case 2: pq_transpose_kernel<2><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      default: pq_transpose_kernel<4><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
-    pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(job.R, N, D, S, K, step + 1, cb, mind, chunk, nchunk,
-                                                        d_draws, d_nonf, d_status, d_state, d_fb, d_chosen);
+    ++launches;
+  }
+
+  float* cb = out.d_codebooks;
+  pq_seed_init_kernel<<<M, 32, 0, st>>>(XT, N, S, K, d_idx0, cb, d_chosen);
+  MVR_CUDA(ctx, cudaGetLastError());
+  ++launches;
+  for (int step = 0; step + 1 < K; ++step) {
+    switch (S) {
+      case 1: pq_seed_update_kernel<1><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
+      case 2: pq_seed_update_kernel<2><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
+      default: pq_seed_update_kernel<4><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
+    }
     MVR_CUDA(ctx, cudaGetLastError());
+    pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(XT, N, S, K, step + 1, cb, mind, chunk, chunk_cnt,
+                                                        nchunk, d_draws, d_nonf, d_status, d_state, d_fb,
+                                                        d_chosen, d_thr);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 2;
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
 
   // ---- Lloyd iterations ---------------------------------------------------
   const bool check = !(job.tol == -INFINITY) && !std::isnan(job.tol);
-  uint32_t launches = 1 + 2 * (uint32_t)(K - 1);
   std::vector<cudaEvent_t> aev;  // assignment-kernel brackets (stats only)
   if (timing) {
     aev.resize(2 * (size_t)job.max_iters, nullptr);
@@ -918,9 +1081,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   for (uint32_t it = 0; it < job.max_iters; ++it) {
     if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it], st));
     switch (S) {
-      case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
-      case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
-      default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk)); break;
+      case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+      case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+      default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
     }
     if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
     launches += 5;
@@ -933,9 +1096,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
-      case 1: pq_scatter_kernel<1><<<nblk, kThreads, 0, st>>>(job.R, N, D, M, K, asg, hist, sorted, d_state); break;
-      case 2: pq_scatter_kernel<2><<<nblk, kThreads, 0, st>>>(job.R, N, D, M, K, asg, hist, sorted, d_state); break;
-      default: pq_scatter_kernel<4><<<nblk, kThreads, 0, st>>>(job.R, N, D, M, K, asg, hist, sorted, d_state); break;
+      case 1: pq_scatter_kernel<1><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
+      case 2: pq_scatter_kernel<2><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
+      default: pq_scatter_kernel<4><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
@@ -943,8 +1106,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
       default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
     }
-    pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(job.R, N, D, S, K, d_counts, mind, cb, d_state, d_wcss,
-                                                  d_prev, d_iters, d_rs, (int)it, check ? 1 : 0, job.tol);
+    pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, d_counts, mind, cb, d_state, d_wcss, d_prev,
+                                                  d_iters, d_rs, (int)it, check ? 1 : 0, job.tol);
     MVR_CUDA(ctx, cudaGetLastError());
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
@@ -1008,11 +1171,11 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
 
 int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
   MVR_TRY(check_shape(ctx, job.D, job.M, job.S, job.K));
-  const PqLayout L = pq_layout(job.N, job.M, job.S, job.K);
+  const PqLayout L = pq_layout(job.N, job.M, job.S, job.K, ctx->sm_count);
   unsigned char* ws = nullptr;
   MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
   std::vector<unsigned char> hsmall(L.small_bytes);
-  return pq_kmeans_run(ctx, ctx->stream, job, out, ws, hsmall.data());
+  return pq_kmeans_run(ctx, ctx->stream, job, out, ws, hsmall.data(), ctx->sm_count);
 }
 
 }  // namespace mvr

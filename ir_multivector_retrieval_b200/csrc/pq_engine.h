@@ -37,13 +37,19 @@ struct PqOut {
 // [0, small_bytes) is mirrored on the host (RNG draws in, status out).
 struct PqLayout {
   int nblk = 0, nchunk = 0;
-  size_t o_draws = 0, o_chosen = 0, o_idx0 = 0, o_counts = 0, o_starts = 0, o_wcss = 0, o_prev = 0,
-         o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_state = 0;
+  uint64_t rows_per_cta = 0;
+  size_t o_draws = 0, o_chosen = 0, o_idx0 = 0, o_thr = 0, o_counts = 0, o_starts = 0, o_wcss = 0,
+         o_prev = 0, o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_state = 0;
   size_t small_bytes = 0;
-  size_t o_mind = 0, o_asg = 0, o_sorted = 0, o_hist = 0, o_chunk = 0;
+  size_t o_xt = 0, o_mind = 0, o_asg = 0, o_sorted = 0, o_hist = 0, o_chunk = 0, o_chunk_cnt = 0;
   size_t total_bytes = 0;
 };
-PqLayout pq_layout(uint64_t N, int M, int S, int K);
+// Workspace layout for N rows, M subspaces of S floats, K centroids on a
+// device with `sms` streaming multiprocessors.
+PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms);
+
+// Multiprocessor count of the current device (148 if it cannot be read).
+int sm_count_current_device();
 
 // Runs seeding + Lloyd for all M subspaces on `stream`, with device
 // workspace `ws` (pq_layout(...).total_bytes, 256-byte aligned) and host
@@ -51,7 +57,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K);
 // null (then no timing and no error text). Returns the MVR status of the
 // smallest failing subspace, or MVR_OK; synchronises `stream`.
 int pq_kmeans_run(Ctx* ctx, cudaStream_t stream, const PqJob& job, const PqOut& out,
-                  unsigned char* ws, unsigned char* hsmall);
+                  unsigned char* ws, unsigned char* hsmall, int sms);
 
 // pq_kmeans_run with the workspace taken from the context's scratch.
 int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out);
