@@ -267,25 +267,43 @@ pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K, uint32_t* __restric
 // row range 32 rows at a time: ranks inside the 32 from __match_any_sync,
 // per-cluster running offsets in shared memory owned by the warp. No block
 // barrier in the loop.
+//
+// For S = 4 (16-byte elements) the two elements that share a 32-byte
+// sector are written back to back by the same thread, so L2 always sees
+// whole sectors (a lone half sector evicted before its partner arrives
+// costs a DRAM read-modify-write). The even element of a pair comes from
+// the previous lane of the same cluster in the group (shuffle) or, when it
+// arrived in an earlier group, from the warp's pending slot for that
+// cluster. Only the two ends of each (CTA, cluster) segment are written as
+// half sectors.
 // ---------------------------------------------------------------------------
 template <int S>
-__global__ void pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int M, int K,
+__global__ void __launch_bounds__(kMaxM * 32)
+pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int M, int K,
                                   const uint8_t* __restrict__ asg, const uint32_t* __restrict__ bases,
                                   float* __restrict__ sorted, const uint8_t* __restrict__ state,
                                   uint64_t rows_per_cta) {
-  __shared__ uint32_t run_all[kMaxM][256];
+  extern __shared__ __align__(16) unsigned char scat_smem[];
   const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+  // per warp: run[256] u32, seg0[256] u32, pend[256] float4
+  unsigned char* wbase = scat_smem + (size_t)m * (256 * 8 + (S == 4 ? 256 * 16 : 0));
+  uint32_t* run = reinterpret_cast<uint32_t*>(wbase);
+  uint32_t* seg0 = run + 256;
+  float4* pend = reinterpret_cast<float4*>(seg0 + 256);
   if (m >= M || state[m] != kRunning) return;
-  uint32_t* run = run_all[m];
   const int nblk = gridDim.x;
-  for (int c = lane; c < K; c += 32) run[c] = bases[((size_t)m * nblk + blockIdx.x) * K + c];
+  for (int c = lane; c < K; c += 32) {
+    const uint32_t b0 = bases[((size_t)m * nblk + blockIdx.x) * K + c];
+    run[c] = b0;
+    seg0[c] = b0;
+  }
   __syncwarp();
   const uint64_t lo = (uint64_t)blockIdx.x * rows_per_cta;
   const uint64_t hi = min(N, lo + rows_per_cta);
   const uint8_t* am = asg + (size_t)m * N;
   const float* xm = XT + (size_t)m * N * S;
   float* sm = sorted + (size_t)m * N * S;
-  constexpr int kU = 4;  // 32-row groups loaded ahead
+  constexpr int kU = 8;  // 32-row groups loaded ahead
   for (uint64_t base = lo; base < hi; base += 32 * kU) {
     int cl[kU];
     float x[kU][S];
@@ -293,8 +311,14 @@ __global__ void pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int 
     for (int u = 0; u < kU; ++u) {
       const uint64_t r = base + (uint64_t)u * 32 + lane;
       if (r < hi) {
-        cl[u] = am[r];
-        load_sub<S>(xm + r * S, x[u]);
+        cl[u] = __ldcs(am + r);
+        if constexpr (S == 4) {
+          const float4 v = __ldcs(reinterpret_cast<const float4*>(xm + r * 4));
+          x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
+        } else {
+#pragma unroll
+          for (int k = 0; k < S; ++k) x[u][k] = __ldcs(xm + r * S + k);
+        }
       } else {
         cl[u] = 256 + lane;  // unique keys never match a real cluster
 #pragma unroll
@@ -304,26 +328,65 @@ __global__ void pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int 
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const uint32_t peers = __match_any_sync(0xffffffffu, cl[u]);
-      const uint32_t rank = __popc(peers & lanemask_lt());
+      const uint32_t below = peers & lanemask_lt();
+      const uint32_t rank = __popc(below);
+      const uint32_t cnt = __popc(peers);
       const bool ok = cl[u] < 256;
-      uint32_t dst = 0;
-      if (ok) dst = run[cl[u]] + rank;
-      __syncwarp();
-      if (ok && rank == 0) run[cl[u]] += __popc(peers);
-      __syncwarp();
-      if (ok) {
-        float* o = sm + (size_t)dst * S;
-        if constexpr (S == 4) {
-          *reinterpret_cast<float4*>(o) = make_float4(x[u][0], x[u][1], x[u][2], x[u][3]);
-        } else if constexpr (S == 2) {
-          *reinterpret_cast<float2*>(o) = make_float2(x[u][0], x[u][1]);
-        } else {
-          o[0] = x[u][0];
+      const int c = ok ? cl[u] : 0;
+      const uint32_t p = ok ? run[c] + rank : 0u;
+      if constexpr (S == 4) {
+        const int prev_lane = below ? 31 - __clz(below) : lane;
+        float4 xv = make_float4(x[u][0], x[u][1], x[u][2], x[u][3]);
+        float4 xp;
+        xp.x = __shfl_sync(0xffffffffu, xv.x, prev_lane);
+        xp.y = __shfl_sync(0xffffffffu, xv.y, prev_lane);
+        xp.z = __shfl_sync(0xffffffffu, xv.z, prev_lane);
+        xp.w = __shfl_sync(0xffffffffu, xv.w, prev_lane);
+        // read phase: the pending even element, if this odd element's
+        // partner arrived in an earlier group of this segment
+        bool have_prev = false;
+        if (ok && (p & 1u)) {
+          if (rank > 0) {
+            have_prev = true;
+          } else if (p > seg0[c]) {
+            xp = pend[c];
+            have_prev = true;
+          }
         }
+        __syncwarp();
+        if (ok) {
+          float4* o = reinterpret_cast<float4*>(sm) + p;
+          if (p & 1u) {
+            if (have_prev) o[-1] = xp;  // same 32-byte sector, back to back
+            o[0] = xv;
+          } else if (rank + 1 == cnt) {
+            pend[c] = xv;  // partner comes later (or never: segment end)
+          }
+          if (rank == 0) run[c] += cnt;
+        }
+        __syncwarp();
+      } else {
+        if (ok) {
+          float* o = sm + (size_t)p * S;
+#pragma unroll
+          for (int k = 0; k < S; ++k) o[k] = x[u][k];
+        }
+        __syncwarp();
+        if (ok && rank == 0) run[c] += cnt;
+        __syncwarp();
       }
     }
   }
+  if constexpr (S == 4) {
+    // segment ends: a last element at an even position has no partner here
+    for (int c = lane; c < K; c += 32) {
+      const uint32_t r = run[c];
+      if (r > seg0[c] && ((r - 1) & 1u) == 0) reinterpret_cast<float4*>(sm)[r - 1] = pend[c];
+    }
+  }
 }
+
+size_t scatter_smem(int M, int S) { return (size_t)M * (256 * 8 + (S == 4 ? 256 * 16 : 0)); }
 
 // ---------------------------------------------------------------------------
 // Centroid sums in the reference order. A warp covers 32/S clusters of one
@@ -381,7 +444,15 @@ pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
     const float* src = ring + (t % kChainStages) * kStage + j * kRow + k;
     const uint32_t done = (uint32_t)t * kChainE;
     const int n = cnt > done ? (int)min((uint32_t)kChainE, cnt - done) : 0;
-    for (int e = 0; e < n; ++e) acc = __fadd_rn(acc, src[e * S]);
+    int e = 0;
+    for (; e + 8 <= n; e += 8) {  // loads first, then the dependent adds
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = src[(e + q) * S];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, v[q]);
+    }
+    for (; e < n; ++e) acc = __fadd_rn(acc, src[e * S]);
     __syncwarp();
     issue(t + kChainStages - 1);
   }
@@ -1096,9 +1167,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
-      case 1: pq_scatter_kernel<1><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
-      case 2: pq_scatter_kernel<2><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
-      default: pq_scatter_kernel<4><<<nblk, 32 * M, 0, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); break;
+      case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      default: { auto k = pq_scatter_kernel<4>; const size_t sm = scatter_smem(M, 4); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
