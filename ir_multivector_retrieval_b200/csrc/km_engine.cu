@@ -1,0 +1,917 @@
+// km_engine.cu — ragged batch of independent k-means problems, any dim.
+//
+// Reference: kmeans.fit (src/tac/kmeans.zig:67-232), rng.weightedSample
+// (src/util/rng.zig:57-82), vec.l2sq (src/util/vec.zig:109-175), and the
+// per-token driver runOneTokenKmeans (src/tac/tac.zig:458-514).
+//
+// Layout in HBM (R = rows of G, d = dim, KT = sum of k over problems):
+//   G      [R][d]   rows grouped by problem (the caller gathers them)
+//   C      [KT][d]  centroids, problem p at rows [coff_p, coff_p + k_p)
+//   md     [R]      k-means++ D^2 weights, then Lloyd min_to_any
+//   local  [R]      Lloyd assignment of each row, local to its problem
+//   keys/vals [R]   global cluster id / row, radix-sorted (stable) so that
+//                   each cluster's members follow in row order
+//   counts/starts [KT]
+//
+// Schedules:
+//   * seeding runs in lockstep over centroid index s; problems are ordered
+//     by k descending, so the problems (and their 1024-row chunks) that
+//     still draw at step s form a prefix;
+//   * Lloyd runs all problems together; converged problems are skipped.
+// Exactness follows pq_engine.cu: exact reference distance order, first-
+// index argmin, in-order sequential centroid sums, rigorous k-means++ draws.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#include "km_engine.h"
+#include "mvr_device.cuh"
+#include "mvr_rng.h"
+
+namespace mvr {
+namespace {
+
+constexpr int kChunk = 1024;       // seeding chunk; one select thread per row
+constexpr int kUpdT = 256;         // seed-update CTA
+constexpr int kSelT = 1024;        // select CTA
+constexpr int kAsgT = 128;         // assign CTA: one row per thread
+constexpr int kCT = 32;            // centroids per shared-memory tile
+constexpr int kRadixRows = 2048;   // rows per radix block (one warp)
+constexpr int kRadixWarps = 4;
+constexpr int kCrossingSlack = 300;
+
+enum : uint8_t { kRunning = 0, kDone = 1, kFailed = 2 };
+
+// vec.l2sq for any length with the 4-lane layout (vec.zig:128-175 with
+// lane_count 4): strided lane accumulators over whole groups of 4, the
+// ordered reduction, then the scalar tail. For lengths 1-4, 64 and 128 this
+// is the same arithmetic as the reference's specialisations.
+__device__ __forceinline__ float l2_gen(const float* __restrict__ x, const float* __restrict__ c, int d) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int i = 0;
+  for (; i + 4 <= d; i += 4) {
+    const float d0 = __fsub_rn(x[i], c[i]), d1 = __fsub_rn(x[i + 1], c[i + 1]);
+    const float d2 = __fsub_rn(x[i + 2], c[i + 2]), d3 = __fsub_rn(x[i + 3], c[i + 3]);
+    a0 = __fadd_rn(a0, __fmul_rn(d0, d0));
+    a1 = __fadd_rn(a1, __fmul_rn(d1, d1));
+    a2 = __fadd_rn(a2, __fmul_rn(d2, d2));
+    a3 = __fadd_rn(a3, __fmul_rn(d3, d3));
+  }
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  for (; i < d; ++i) {
+    const float t = __fsub_rn(x[i], c[i]);
+    s = __fadd_rn(s, __fmul_rn(t, t));
+  }
+  return s;
+}
+
+struct Prob {
+  const uint64_t* off;
+  const uint32_t* n;
+  const uint32_t* k;
+  const uint64_t* coff;
+  uint8_t* state;
+  int* status;
+  float* wcss;
+  float* prev;
+  uint32_t* iters;
+  double* thr;
+  uint32_t* fb;
+  int* nonf;
+};
+
+__device__ __forceinline__ double gamma_bound(uint64_t n) {
+  const double g = __dmul_ru(__ull2double_ru(n), 1.1102230246251565e-16);
+  return __ddiv_ru(g, __dsub_rd(1.0, g));
+}
+
+// ---------------------------------------------------------------------------
+// degenerate k >= n (kmeans.zig:88-104)
+// ---------------------------------------------------------------------------
+__global__ void km_degenerate_kernel(const float* __restrict__ G, int d, Prob P,
+                                     const uint32_t* __restrict__ list, float* __restrict__ C,
+                                     uint32_t* __restrict__ local, uint32_t* __restrict__ keys) {
+  const uint32_t p = list[blockIdx.x];
+  const uint64_t off = P.off[p];
+  const uint32_t n = P.n[p], k = P.k[p];
+  const uint64_t co = P.coff[p];
+  for (uint64_t e = threadIdx.x; e < (uint64_t)k * d; e += blockDim.x) {
+    const uint64_t c = e / d, j = e % d;
+    const uint64_t row = c < n ? c : n - 1;
+    C[(co + c) * d + j] = G[(off + row) * d + j];
+  }
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    local[off + i] = i;
+    keys[off + i] = (uint32_t)(co + i);  // every row carries a valid sort key
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k-means++ seeding
+// ---------------------------------------------------------------------------
+__global__ void km_seed_init_kernel(const float* __restrict__ G, int d, Prob P,
+                                    const uint32_t* __restrict__ list, const uint64_t* __restrict__ idx0,
+                                    float* __restrict__ C) {
+  const uint32_t p = list[blockIdx.x];
+  const uint64_t src = (P.off[p] + idx0[p]) * d, dst = P.coff[p] * d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) C[dst + j] = G[src + j];
+}
+
+// min_dist update with centroid `step` for the active chunks, plus per-chunk
+// directed-rounding sums and the count of non-zero weights below thr.
+__global__ void __launch_bounds__(kUpdT)
+km_seed_update_kernel(const float* __restrict__ G, int d, Prob P, int step,
+                      const uint32_t* __restrict__ ch_p, const uint64_t* __restrict__ ch_r0,
+                      const uint32_t* __restrict__ ch_len, const float* __restrict__ C,
+                      float* __restrict__ md, double2* __restrict__ ch_sum,
+                      uint32_t* __restrict__ ch_cnt) {
+  extern __shared__ float cen[];
+  __shared__ double2 wp[kUpdT / 32];
+  __shared__ uint32_t wc[kUpdT / 32];
+  const uint32_t p = ch_p[blockIdx.x];
+  if (P.state[p] != kRunning) return;
+  const uint64_t co = P.coff[p] + step;
+  for (int j = threadIdx.x; j < d; j += kUpdT) cen[j] = C[co * d + j];
+  __syncthreads();
+  const uint64_t r0 = ch_r0[blockIdx.x];
+  const uint32_t len = ch_len[blockIdx.x];
+  const double T = P.thr[p];
+  double lo = 0.0, hi = 0.0;
+  uint32_t cnt = 0;
+  bool bad = false;
+  for (uint32_t i = threadIdx.x; i < len; i += kUpdT) {
+    const uint64_t r = r0 + i;
+    const float dist = l2_gen(G + r * d, cen, d);
+    float w;
+    if (step == 0) {
+      w = dist;
+    } else {
+      const float old = md[r];
+      w = dist < old ? dist : old;
+    }
+    md[r] = w;
+    bad |= !isfinite(w) || w < 0.f;
+    lo = __dadd_rd(lo, (double)w);
+    hi = __dadd_ru(hi, (double)w);
+    cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+  }
+  if (bad) P.nonf[p] = 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  lo = warp_sum_rd(lo);
+  hi = warp_sum_ru(hi);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if (lane == 0) {
+    wp[warp] = make_double2(lo, hi);
+    wc[warp] = cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, b = 0.0;
+    uint32_t c = 0;
+    for (int w = 0; w < kUpdT / 32; ++w) {
+      a = __dadd_rd(a, wp[w].x);
+      b = __dadd_ru(b, wp[w].y);
+      c += wc[w];
+    }
+    ch_sum[blockIdx.x] = make_double2(a, b);
+    ch_cnt[blockIdx.x] = c;
+  }
+}
+
+// One weightedSample draw for each active problem (see pq_seed_select_kernel
+// in pq_engine.cu for the acceptance argument).
+__global__ void __launch_bounds__(kSelT)
+km_seed_select_kernel(const float* __restrict__ G, int d, Prob P, int step,
+                      const uint32_t* __restrict__ sel_p, const uint32_t* __restrict__ cfirst,
+                      const uint32_t* __restrict__ ccount, const uint64_t* __restrict__ ch_r0,
+                      const uint32_t* __restrict__ ch_len, const double2* __restrict__ ch_sum,
+                      const uint32_t* __restrict__ ch_cnt, const float* __restrict__ md,
+                      const double* __restrict__ draws, float* __restrict__ C) {
+  const uint32_t p = sel_p[blockIdx.x];
+  if (P.state[p] != kRunning) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = kSelT / 32;
+  __shared__ double2 wsum[kWarps];
+  __shared__ unsigned long long wcnt[kWarps];
+  __shared__ double2 incl_all[kSelT];
+  __shared__ double2 sh_excl;
+  __shared__ int sh_chunk;
+  __shared__ uint64_t sh_idx;
+  __shared__ int sh_decided;
+
+  if (P.nonf[p]) {
+    if (tid == 0) { P.status[p] = MVR_E_NON_FINITE; P.state[p] = kFailed; }
+    return;
+  }
+  const uint64_t off = P.off[p];
+  const uint64_t N = P.n[p];
+  const float* w = md + off;
+  const double r = draws[P.coff[p] + step];
+  const uint32_t cf = cfirst[p], cc = ccount[p];
+
+  const uint32_t cpt = (cc + kSelT - 1) / kSelT;
+  const uint32_t c_lo = min(cc, tid * cpt), c_hi = min(cc, c_lo + cpt);
+  double tlo = 0.0, thi = 0.0;
+  unsigned tcnt = 0;
+  for (uint32_t j = c_lo; j < c_hi; ++j) {
+    tlo = __dadd_rd(tlo, ch_sum[cf + j].x);
+    thi = __dadd_ru(thi, ch_sum[cf + j].y);
+    tcnt += ch_cnt[cf + j];
+  }
+  const double ilo = warp_scan_rd(tlo, lane), ihi = warp_scan_ru(thi, lane);
+  const unsigned wc = __reduce_add_sync(0xffffffffu, tcnt);
+  if (lane == 31) wsum[warp] = make_double2(ilo, ihi);
+  if (lane == 0) wcnt[warp] = wc;
+  __syncthreads();
+  if (warp == 0) {
+    const double a = warp_scan_rd(wsum[lane].x, lane);
+    const double b = warp_scan_ru(wsum[lane].y, lane);
+    unsigned long long cs = wcnt[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+    __syncwarp();
+    wsum[lane] = make_double2(a, b);
+    wcnt[lane] = cs;
+  }
+  __syncthreads();
+  const double wlo = warp > 0 ? wsum[warp - 1].x : 0.0, whi = warp > 0 ? wsum[warp - 1].y : 0.0;
+  const double incl_lo = __dadd_rd(wlo, ilo), incl_hi = __dadd_ru(whi, ihi);
+  const double Lo_N = wsum[kWarps - 1].x, Hi_N = wsum[kWarps - 1].y;
+  const unsigned long long C_N = wcnt[0];
+  if (Hi_N <= 0.0) {
+    if (tid == 0) { P.status[p] = MVR_E_ALL_ZERO; P.state[p] = kFailed; }
+    return;
+  }
+  const double gN = gamma_bound(N);
+  const double shi_classic = __dadd_ru(Hi_N, __dmul_ru(gN, Hi_N));
+  int e2 = 0;
+  (void)frexp(shi_classic, &e2);
+  const double Gu = ldexp(1.0, e2 - 53);
+  const double thr_now = ldexp(Gu, 23);
+  const double B_tight = __dmul_ru(__ull2double_ru(C_N + kCrossingSlack), 0.5 * Gu);
+  const double thr_prev = P.thr[p];
+  const bool tight_ok = thr_now <= thr_prev;
+  auto bound_at = [&](uint64_t terms, double hi_prefix) {
+    const double bg = __dmul_ru(gamma_bound(terms), hi_prefix);
+    return tight_ok ? fmin(bg, B_tight) : bg;
+  };
+  const double u_mid = r * (0.5 * (Lo_N + Hi_N));
+  const bool past = !(u_mid < 0.5 * (incl_lo + incl_hi));
+  incl_all[tid] = make_double2(incl_lo, incl_hi);
+  const int n_before = __syncthreads_count(past);
+  if (tid == 0) {
+    sh_decided = 0;
+    sh_chunk = -1;
+    if (thr_now < thr_prev) P.thr[p] = thr_now;
+  }
+  __syncthreads();
+  if (n_before < kSelT && tid == n_before) {
+    double lo = tid > 0 ? incl_all[tid - 1].x : 0.0;
+    double hi = tid > 0 ? incl_all[tid - 1].y : 0.0;
+    int found = -1;
+    for (uint32_t j = c_lo; j < c_hi; ++j) {
+      const double nlo = __dadd_rd(lo, ch_sum[cf + j].x), nhi = __dadd_ru(hi, ch_sum[cf + j].y);
+      if (u_mid < 0.5 * (nlo + nhi)) { found = (int)j; break; }
+      lo = nlo;
+      hi = nhi;
+    }
+    sh_chunk = found;
+    sh_excl = make_double2(lo, hi);
+  }
+  __syncthreads();
+  const int fchunk = sh_chunk;
+  if (fchunk >= 0) {
+    const uint64_t r0 = ch_r0[cf + fchunk] - off;  // row index within the problem
+    const uint32_t len = ch_len[cf + fchunk];
+    const uint64_t i = r0 + tid;
+    const double v = (uint32_t)tid < len ? (double)w[i] : 0.0;
+    const double slo = warp_scan_rd(v, lane), shi = warp_scan_ru(v, lane);
+    if (lane == 31) wsum[warp] = make_double2(slo, shi);
+    __syncthreads();
+    if (warp == 0) {
+      const double a = warp_scan_rd(wsum[lane].x, lane);
+      const double b = warp_scan_ru(wsum[lane].y, lane);
+      __syncwarp();
+      wsum[lane] = make_double2(a, b);
+    }
+    __syncthreads();
+    const double2 ex = sh_excl;
+    const double plo = warp > 0 ? wsum[warp - 1].x : 0.0, phi = warp > 0 ? wsum[warp - 1].y : 0.0;
+    const double elo = __dadd_rd(ex.x, __dadd_rd(plo, slo));
+    const double ehi = __dadd_ru(ex.y, __dadd_ru(phi, shi));
+    incl_all[tid] = make_double2(elo, ehi);
+    const bool valid = (uint32_t)tid < len;
+    const bool hit = !valid || u_mid < 0.5 * (elo + ehi);
+    const int first = __syncthreads_count(!hit);
+    if (first < kSelT && tid == first && valid) {
+      const double2 prv = tid > 0 ? incl_all[tid - 1] : ex;
+      const double BN = bound_at(N, Hi_N);
+      const double ULo = __dmul_rd(r, __dsub_rd(Lo_N, BN));
+      const double UHi = __dmul_ru(r, __dadd_ru(Hi_N, BN));
+      bool ok = UHi < __dsub_rd(elo, bound_at(i + 1, ehi));
+      if (i > 0) ok = ok && (ULo >= __dadd_ru(prv.y, bound_at(i, prv.y)));
+      if (ok) {
+        sh_idx = i;
+        sh_decided = 1;
+      }
+    }
+  }
+  __syncthreads();
+  if (!sh_decided && tid == 0) {  // the reference's sequential chain
+    double total = 0.0;
+    uint64_t last_pos = 0;
+    for (uint64_t q = 0; q < N; ++q) {
+      const float v = w[q];
+      total = __dadd_rn(total, (double)v);
+      if (v != 0.f) last_pos = q;
+    }
+    const double u = __dmul_rn(r, total);
+    double cum = 0.0;
+    uint64_t pick = last_pos;
+    for (uint64_t q = 0; q < N; ++q) {
+      cum = __dadd_rn(cum, (double)w[q]);
+      if (u < cum) { pick = q; break; }
+    }
+    sh_idx = pick;
+    P.fb[p] += 1;
+  }
+  __syncthreads();
+  const uint64_t idx = sh_idx;
+  const uint64_t dst = (P.coff[p] + step) * d, src = (off + idx) * d;
+  for (int j = tid; j < d; j += kSelT) C[dst + j] = G[src + j];
+}
+
+// ---------------------------------------------------------------------------
+// Lloyd assignment: one row per thread, centroids through shared memory in
+// tiles of kCT. DIM > 0 keeps the row in registers; DIM == 0 is the generic
+// path (row read through L1). Writes the local id, the min distance, the
+// global sort key and the cluster count.
+// ---------------------------------------------------------------------------
+template <int DIM>
+__global__ void __launch_bounds__(kAsgT)
+km_assign_kernel(const float* __restrict__ G, int d_rt, Prob P, const uint32_t* __restrict__ t_p,
+                 const uint64_t* __restrict__ t_r0, const uint32_t* __restrict__ t_len,
+                 const float* __restrict__ C, uint32_t* __restrict__ local, float* __restrict__ mind,
+                 uint32_t* __restrict__ keys) {
+  extern __shared__ __align__(16) float ct[];
+  const int d = DIM > 0 ? DIM : d_rt;
+  const uint32_t p = t_p[blockIdx.x];
+  if (P.state[p] != kRunning) return;
+  const uint32_t k = P.k[p];
+  const uint64_t co = P.coff[p];
+  const uint32_t len = t_len[blockIdx.x];
+  const uint64_t r = t_r0[blockIdx.x] + threadIdx.x;
+  const bool ok = threadIdx.x < len;
+  float xr[DIM > 0 ? DIM : 1];
+  const float* xg = G + (ok ? r : t_r0[blockIdx.x]) * d;
+  if constexpr (DIM > 0) {
+#pragma unroll
+    for (int j = 0; j < DIM; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xg + j));
+      xr[j] = v.x; xr[j + 1] = v.y; xr[j + 2] = v.z; xr[j + 3] = v.w;
+    }
+  }
+  float best = 0.f, d0 = 0.f;
+  uint32_t bi = 0;
+  for (uint32_t c0 = 0; c0 < k; c0 += kCT) {
+    const uint32_t nt = min((uint32_t)kCT, k - c0);
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < nt * (uint32_t)d; e += kAsgT) ct[e] = C[(co + c0) * d + e];
+    __syncthreads();
+    for (uint32_t j = 0; j < nt; ++j) {
+      float dist;
+      if constexpr (DIM > 0) dist = l2_wide<DIM>(xr, ct + j * DIM);
+      else dist = l2_gen(xg, ct + j * d, d);
+      const uint32_t c = c0 + j;
+      if (c == 0) {
+        best = dist;  // vec.argmin starts from dists[0]
+        d0 = dist;
+      } else if (dist < best) {
+        best = dist;
+        bi = c;
+      }
+    }
+  }
+  (void)d0;
+  if (ok) {
+    local[r] = bi;
+    mind[r] = best;
+    keys[r] = (uint32_t)(co + bi);
+  }
+}
+
+// Cluster sizes from the sort keys of all rows (rows of finished problems
+// keep their last keys), so counts and the radix order always agree.
+__global__ void km_count_kernel(const uint32_t* __restrict__ keys, uint64_t n, uint32_t* __restrict__ counts) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    atomicAdd(&counts[keys[i]], 1u);
+}
+
+// Sequential f32 WCSS per problem (kmeans.zig:179): one warp per problem,
+// rows staged through shared memory, lane 0 adds in row order.
+__global__ void __launch_bounds__(128)
+km_wcss_kernel(Prob P, uint32_t nprob, const float* __restrict__ mind) {
+  __shared__ __align__(16) float tile[4][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t p = blockIdx.x * 4 + warp;
+  if (p >= nprob || P.state[p] != kRunning) return;
+  const float* src = mind + P.off[p];
+  const uint32_t n = P.n[p];
+  float acc = 0.f;
+  for (uint32_t t0 = 0; t0 < n; t0 += 256) {
+    const uint32_t m = min(256u, n - t0);
+    for (uint32_t e = lane; e < m; e += 32) tile[warp][e] = src[t0 + e];
+    __syncwarp();
+    if (lane == 0)
+      for (uint32_t e = 0; e < m; ++e) acc = __fadd_rn(acc, tile[warp][e]);
+    __syncwarp();
+  }
+  if (lane == 0) P.wcss[p] = acc;
+}
+
+// Single-CTA exclusive scan of counts (n entries) into starts.
+__global__ void __launch_bounds__(1024)
+km_exclusive_scan_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out, uint64_t n) {
+  __shared__ uint32_t part[1024];
+  const uint64_t per = (n + 1023) / 1024;
+  const uint64_t lo = min(n, (uint64_t)threadIdx.x * per), hi = min(n, lo + per);
+  uint32_t s = 0;
+  for (uint64_t i = lo; i < hi; ++i) s += in[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const uint32_t v = threadIdx.x >= (unsigned)o ? part[threadIdx.x - o] : 0u;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  uint32_t run = part[threadIdx.x] - s;
+  for (uint64_t i = lo; i < hi; ++i) {
+    const uint32_t v = in[i];
+    out[i] = run;
+    run += v;
+  }
+}
+
+// Stable LSD radix pass (8-bit digit at `shift`) over (key, val) pairs.
+// Block b (one warp) owns rows [b*kRadixRows, ...). vals == nullptr means
+// val = row index (the first pass).
+__global__ void __launch_bounds__(kRadixWarps * 32)
+km_radix_hist_kernel(const uint32_t* __restrict__ keys, uint64_t n, int shift, int nblk,
+                     uint32_t* __restrict__ hist) {
+  __shared__ uint32_t h[kRadixWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * kRadixWarps + warp;
+  for (int e = lane; e < 256; e += 32) h[warp][e] = 0;
+  __syncwarp();
+  if (b < nblk) {
+    const uint64_t lo = (uint64_t)b * kRadixRows, hi = min(n, lo + kRadixRows);
+    for (uint64_t i = lo + lane; i < hi; i += 32) atomicAdd(&h[warp][(keys[i] >> shift) & 255u], 1u);
+    __syncwarp();
+    for (int e = lane; e < 256; e += 32) hist[(size_t)e * nblk + b] = h[warp][e];
+  }
+}
+
+__global__ void __launch_bounds__(kRadixWarps * 32)
+km_radix_scatter_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals,
+                        uint64_t n, int shift, int nblk, const uint32_t* __restrict__ base,
+                        uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out) {
+  __shared__ uint32_t run_all[kRadixWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * kRadixWarps + warp;
+  if (b >= nblk) return;
+  uint32_t* run = run_all[warp];
+  for (int e = lane; e < 256; e += 32) run[e] = base[(size_t)e * nblk + b];
+  __syncwarp();
+  const uint64_t lo = (uint64_t)b * kRadixRows, hi = min(n, lo + kRadixRows);
+  for (uint64_t i0 = lo; i0 < hi; i0 += 32) {
+    const uint64_t i = i0 + lane;
+    const bool ok = i < hi;
+    const uint32_t key = ok ? keys[i] : 0u, val = ok ? (vals ? vals[i] : (uint32_t)i) : 0u;
+    const int dig = ok ? (int)((key >> shift) & 255u) : 256 + lane;
+    const uint32_t peers = __match_any_sync(0xffffffffu, dig);
+    const uint32_t rank = __popc(peers & lanemask_lt());
+    uint32_t dst = 0;
+    if (ok) dst = run[dig] + rank;
+    __syncwarp();
+    if (ok && rank == 0) run[dig] += __popc(peers);
+    __syncwarp();
+    if (ok) {
+      keys_out[dst] = key;
+      vals_out[dst] = val;
+    }
+  }
+}
+
+// In-order centroid sums: one warp per global cluster, lane = coordinates
+// lane, lane+32, ...; members are the cluster's rows in row order.
+template <int DIM>
+__global__ void __launch_bounds__(256)
+km_chain_kernel(const float* __restrict__ G, int d_rt, Prob P, const uint32_t* __restrict__ cprob,
+                uint64_t KT, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ starts,
+                const uint32_t* __restrict__ vals, float* __restrict__ C) {
+  constexpr int Q = DIM > 0 ? (DIM + 31) / 32 : 8;  // coordinates per lane (generic: d <= 256)
+  const int d = DIM > 0 ? DIM : d_rt;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t g = (uint64_t)blockIdx.x * 8 + warp;
+  if (g >= KT) return;
+  if (P.state[cprob[g]] != kRunning) return;
+  const uint32_t cnt = counts[g];
+  if (cnt == 0) return;  // left for the reseed
+  const uint32_t st = starts[g];
+  float acc[Q];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) acc[q] = 0.f;
+  for (uint32_t b0 = 0; b0 < cnt; b0 += 32) {
+    const uint32_t m = min(32u, cnt - b0);
+    const uint32_t myrow = lane < (int)m ? vals[st + b0 + lane] : 0u;
+    for (uint32_t e = 0; e < m; ++e) {
+      const uint64_t row = __shfl_sync(0xffffffffu, myrow, e);
+      const float* x = G + row * d;
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const int j = lane + 32 * q;
+        if (j < d) acc[q] = __fadd_rn(acc[q], __ldg(x + j));
+      }
+    }
+  }
+  const float inv = __fdiv_rn(1.0f, __uint2float_rn(cnt));
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const int j = lane + 32 * q;
+    if (j < d) C[g * d + j] = __fmul_rn(acc[q], inv);
+  }
+}
+
+// First maximum of v[0..n) with vec.argmax semantics.
+__device__ uint64_t block_argmax_first(const float* v, uint64_t n) {
+  __shared__ float bv[32];
+  __shared__ uint64_t bi[32];
+  float best = -__int_as_float(0x7f800000);
+  uint64_t idx = n;
+  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = v[i];
+    if (x > best || (x == best && i < idx)) { best = x; idx = i; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const uint64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+  }
+  if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? bv[lane] : -__int_as_float(0x7f800000);
+    idx = lane < nw ? bi[lane] : n;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const uint64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+    }
+    if (lane == 0) bi[0] = (isnan(v[0]) || idx >= n) ? 0 : idx;
+  }
+  __syncthreads();
+  const uint64_t r = bi[0];
+  __syncthreads();
+  return r;
+}
+
+// Empty-cluster reseed in cluster order, then the convergence test.
+__global__ void __launch_bounds__(256)
+km_reseed_converge_kernel(const float* __restrict__ G, int d, Prob P, uint32_t nprob,
+                          const uint32_t* __restrict__ counts, float* __restrict__ mind,
+                          float* __restrict__ C, uint32_t* __restrict__ reseeds, int iter, int check,
+                          float tol) {
+  const uint32_t p = blockIdx.x;
+  if (p >= nprob || P.state[p] != kRunning) return;
+  const uint32_t k = P.k[p];
+  const uint64_t co = P.coff[p], off = P.off[p];
+  const uint32_t n = P.n[p];
+  __shared__ int any_empty;
+  if (threadIdx.x == 0) any_empty = 0;
+  __syncthreads();
+  for (uint32_t c = threadIdx.x; c < k; c += blockDim.x)
+    if (counts[co + c] == 0) any_empty = 1;
+  __syncthreads();
+  if (any_empty) {
+    float* mm = mind + off;
+    for (uint32_t c = 0; c < k; ++c) {
+      if (counts[co + c] != 0) continue;
+      const uint64_t far = block_argmax_first(mm, n);
+      for (int j = threadIdx.x; j < d; j += blockDim.x) C[(co + c) * d + j] = G[(off + far) * d + j];
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        mm[far] = -__int_as_float(0x7f800000);
+        reseeds[p] += 1;
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) {
+    P.iters[p] = (uint32_t)iter + 1;
+    if (check) {
+      const float w = P.wcss[p];
+      if (iter > 0) {
+        const float prev = P.prev[p];
+        const float denom = prev > 0.f ? prev : 1.0f;
+        if (__fdiv_rn(__fsub_rn(prev, w), denom) < tol) P.state[p] = kDone;
+      }
+      P.prev[p] = w;
+    }
+  }
+}
+
+struct Carver {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  }
+};
+
+template <typename T>
+T* at(unsigned char* base, size_t o) { return reinterpret_cast<T*>(base + o); }
+
+}  // namespace
+
+int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const KmBatch& b,
+                 uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res) {
+  const size_t NP = b.size();
+  res->status.assign(NP, MVR_OK);
+  res->wcss.assign(NP, 0.f);
+  res->iters.assign(NP, 0);
+  if (NP == 0) return MVR_OK;
+  if (dim == 0) return fail(ctx, MVR_E_DIM_MISMATCH, "dim == 0");
+  if (dim > 256) return fail(ctx, MVR_E_INVALID_ARGUMENT, "dim > 256 is not supported on the GPU path");
+  if (rows >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows");
+  cudaStream_t st = ctx->stream;
+  const uint64_t KT = b.coff.back() + b.k.back();
+  if (KT >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 centroids");
+
+  // ---- problem classes ---------------------------------------------------
+  std::vector<uint32_t> degen, live, seeders;
+  for (uint32_t p = 0; p < NP; ++p) {
+    if (b.k[p] == 0 || b.n[p] == 0) return fail(ctx, MVR_E_INVALID_ARGUMENT, "empty problem");
+    if (b.k[p] >= b.n[p]) {
+      degen.push_back(p);
+    } else {
+      live.push_back(p);
+      if (b.k[p] >= 2) seeders.push_back(p);
+    }
+  }
+  std::stable_sort(seeders.begin(), seeders.end(), [&](uint32_t a, uint32_t c) { return b.k[a] > b.k[c]; });
+  uint32_t kmax = 0;
+  for (uint32_t p : seeders) kmax = std::max(kmax, b.k[p]);
+
+  // seeding chunks, in seeder order
+  std::vector<uint32_t> ch_p, ch_len, cfirst(NP, 0), ccount(NP, 0);
+  std::vector<uint64_t> ch_r0;
+  std::vector<uint32_t> chunks_upto;  // chunks of seeders[0..i]
+  for (uint32_t p : seeders) {
+    cfirst[p] = (uint32_t)ch_p.size();
+    for (uint64_t r = 0; r < b.n[p]; r += kChunk) {
+      ch_p.push_back(p);
+      ch_r0.push_back(b.off[p] + r);
+      ch_len.push_back((uint32_t)std::min<uint64_t>(kChunk, b.n[p] - r));
+    }
+    ccount[p] = (uint32_t)ch_p.size() - cfirst[p];
+    chunks_upto.push_back((uint32_t)ch_p.size());
+  }
+  // assignment tiles of the live problems
+  std::vector<uint32_t> t_p, t_len;
+  std::vector<uint64_t> t_r0;
+  for (uint32_t p : live)
+    for (uint64_t r = 0; r < b.n[p]; r += kAsgT) {
+      t_p.push_back(p);
+      t_r0.push_back(b.off[p] + r);
+      t_len.push_back((uint32_t)std::min<uint64_t>(kAsgT, b.n[p] - r));
+    }
+  std::vector<uint32_t> cprob(KT);
+  for (uint32_t p = 0; p < NP; ++p)
+    for (uint32_t c = 0; c < b.k[p]; ++c) cprob[b.coff[p] + c] = p;
+
+  // ---- host RNG draws: draw s of problem p at draws[coff_p + s] -----------
+  std::vector<double> draws(KT, 0.0);
+  std::vector<uint64_t> idx0(NP, 0);
+  for (uint32_t p : live) {
+    Xoshiro256pp rng(b.seed[p]);
+    idx0[p] = rng.below(b.n[p]);
+    for (uint32_t s = 1; s < b.k[p]; ++s) draws[b.coff[p] + s] = rng.unit_f64();
+  }
+
+  // ---- workspace -------------------------------------------------------------
+  const int radix_nblk = (int)((rows + kRadixRows - 1) / kRadixRows);
+  int passes = 1;
+  while (passes < 4 && (KT >> (8 * passes)) > 0) ++passes;
+  Carver cv;
+  const size_t o_off = cv.take(NP * 8), o_n = cv.take(NP * 4), o_k = cv.take(NP * 4), o_coff = cv.take(NP * 8),
+               o_state = cv.take(NP), o_status = cv.take(NP * 4), o_wcss = cv.take(NP * 4),
+               o_prev = cv.take(NP * 4), o_iters = cv.take(NP * 4), o_thr = cv.take(NP * 8),
+               o_fb = cv.take(NP * 4), o_nonf = cv.take(NP * 4), o_rs = cv.take(NP * 4),
+               o_idx0 = cv.take(NP * 8), o_cfirst = cv.take(NP * 4), o_ccount = cv.take(NP * 4),
+               o_seeders = cv.take(std::max<size_t>(1, seeders.size()) * 4),
+               o_degen = cv.take(std::max<size_t>(1, degen.size()) * 4),
+               o_live = cv.take(std::max<size_t>(1, live.size()) * 4),
+               o_chp = cv.take(std::max<size_t>(1, ch_p.size()) * 4),
+               o_chr0 = cv.take(std::max<size_t>(1, ch_r0.size()) * 8),
+               o_chlen = cv.take(std::max<size_t>(1, ch_len.size()) * 4),
+               o_tp = cv.take(std::max<size_t>(1, t_p.size()) * 4),
+               o_tr0 = cv.take(std::max<size_t>(1, t_r0.size()) * 8),
+               o_tlen = cv.take(std::max<size_t>(1, t_len.size()) * 4), o_cprob = cv.take(KT * 4),
+               o_draws = cv.take(KT * 8);
+  const size_t host_bytes = cv.off;  // everything above is copied from the host
+  const size_t o_chsum = cv.take(std::max<size_t>(1, ch_p.size()) * sizeof(double2)),
+               o_chcnt = cv.take(std::max<size_t>(1, ch_p.size()) * 4), o_md = cv.take(rows * 4),
+               o_keys = cv.take(rows * 4), o_keys2 = cv.take(rows * 4), o_vals2 = cv.take(rows * 4),
+               o_keys3 = cv.take(rows * 4), o_vals3 = cv.take(rows * 4), o_counts = cv.take(KT * 4), o_starts = cv.take(KT * 4),
+               o_hist = cv.take((size_t)256 * radix_nblk * 4), o_base = cv.take((size_t)256 * radix_nblk * 4);
+  unsigned char* ws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotAux3, cv.off, (void**)&ws));
+  std::vector<unsigned char> hb(host_bytes, 0);
+  auto put = [&](size_t o, const void* src, size_t bytes) {
+    if (bytes) std::memcpy(hb.data() + o, src, bytes);
+  };
+  put(o_off, b.off.data(), NP * 8);
+  put(o_n, b.n.data(), NP * 4);
+  put(o_k, b.k.data(), NP * 4);
+  put(o_coff, b.coff.data(), NP * 8);
+  {
+    std::vector<uint8_t> st0(NP, kRunning);
+    for (uint32_t p : degen) st0[p] = kDone;
+    put(o_state, st0.data(), NP);
+    std::vector<double> thr0(NP, HUGE_VAL);
+    put(o_thr, thr0.data(), NP * 8);
+  }
+  put(o_idx0, idx0.data(), NP * 8);
+  put(o_cfirst, cfirst.data(), NP * 4);
+  put(o_ccount, ccount.data(), NP * 4);
+  put(o_seeders, seeders.data(), seeders.size() * 4);
+  put(o_degen, degen.data(), degen.size() * 4);
+  put(o_live, live.data(), live.size() * 4);
+  put(o_chp, ch_p.data(), ch_p.size() * 4);
+  put(o_chr0, ch_r0.data(), ch_r0.size() * 8);
+  put(o_chlen, ch_len.data(), ch_len.size() * 4);
+  put(o_tp, t_p.data(), t_p.size() * 4);
+  put(o_tr0, t_r0.data(), t_r0.size() * 8);
+  put(o_tlen, t_len.data(), t_len.size() * 4);
+  put(o_cprob, cprob.data(), KT * 4);
+  put(o_draws, draws.data(), KT * 8);
+  MVR_CUDA(ctx, cudaMemcpyAsync(ws, hb.data(), host_bytes, cudaMemcpyHostToDevice, st));
+
+  Prob P;
+  P.off = at<uint64_t>(ws, o_off);
+  P.n = at<uint32_t>(ws, o_n);
+  P.k = at<uint32_t>(ws, o_k);
+  P.coff = at<uint64_t>(ws, o_coff);
+  P.state = at<uint8_t>(ws, o_state);
+  P.status = at<int>(ws, o_status);
+  P.wcss = at<float>(ws, o_wcss);
+  P.prev = at<float>(ws, o_prev);
+  P.iters = at<uint32_t>(ws, o_iters);
+  P.thr = at<double>(ws, o_thr);
+  P.fb = at<uint32_t>(ws, o_fb);
+  P.nonf = at<int>(ws, o_nonf);
+  uint32_t* d_rs = at<uint32_t>(ws, o_rs);
+  const int d = (int)dim;
+  uint32_t launches = 0;
+
+  // every row carries a sort key below KT from the start (rows of problems
+  // that fail while seeding are never assigned)
+  MVR_CUDA(ctx, cudaMemsetAsync(at<uint32_t>(ws, o_keys), 0, rows * 4, st));
+
+  // ---- degenerate problems ------------------------------------------------
+  if (!degen.empty()) {
+    km_degenerate_kernel<<<(unsigned)degen.size(), 128, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_degen), d_C, d_local,
+                                                                 at<uint32_t>(ws, o_keys));
+    MVR_CUDA(ctx, cudaGetLastError());
+    ++launches;
+  }
+
+  // ---- seeding -----------------------------------------------------------------
+  if (!live.empty()) {
+    km_seed_init_kernel<<<(unsigned)live.size(), 64, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_live),
+                                                              at<uint64_t>(ws, o_idx0), d_C);
+    MVR_CUDA(ctx, cudaGetLastError());
+    ++launches;
+  }
+  for (uint32_t s = 1; s < kmax; ++s) {
+    // seeders with k > s form the prefix seeders[0 .. na)
+    const uint32_t na = (uint32_t)(std::partition_point(seeders.begin(), seeders.end(),
+                                                        [&](uint32_t p) { return b.k[p] > s; }) -
+                                   seeders.begin());
+    if (na == 0) break;
+    const uint32_t nch = chunks_upto[na - 1];
+    km_seed_update_kernel<<<nch, kUpdT, d * sizeof(float), st>>>(
+        d_G, d, P, (int)s - 1, at<uint32_t>(ws, o_chp), at<uint64_t>(ws, o_chr0), at<uint32_t>(ws, o_chlen),
+        d_C, at<float>(ws, o_md), at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt));
+    MVR_CUDA(ctx, cudaGetLastError());
+    km_seed_select_kernel<<<na, kSelT, 0, st>>>(
+        d_G, d, P, (int)s, at<uint32_t>(ws, o_seeders), at<uint32_t>(ws, o_cfirst), at<uint32_t>(ws, o_ccount),
+        at<uint64_t>(ws, o_chr0), at<uint32_t>(ws, o_chlen), at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt),
+        at<float>(ws, o_md), at<double>(ws, o_draws), d_C);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 2;
+  }
+
+  // ---- Lloyd iterations ---------------------------------------------------------
+  const bool check = !(tol == -INFINITY) && !std::isnan(tol);
+  float* mind = at<float>(ws, o_md);
+  uint32_t* keys = at<uint32_t>(ws, o_keys);
+  uint32_t* keys2 = at<uint32_t>(ws, o_keys2);
+  uint32_t* vals2 = at<uint32_t>(ws, o_vals2);
+  uint32_t* keys3 = at<uint32_t>(ws, o_keys3);
+  uint32_t* vals3 = at<uint32_t>(ws, o_vals3);
+  uint32_t* counts = at<uint32_t>(ws, o_counts);
+  uint32_t* starts = at<uint32_t>(ws, o_starts);
+  uint32_t* hist = at<uint32_t>(ws, o_hist);
+  uint32_t* base = at<uint32_t>(ws, o_base);
+  const unsigned ntiles = (unsigned)t_p.size();
+  const size_t asg_smem = (size_t)kCT * d * sizeof(float);
+  for (uint32_t it = 0; it < max_iters && !live.empty(); ++it) {
+    MVR_CUDA(ctx, cudaMemsetAsync(counts, 0, KT * 4, st));
+    if (d == 64) {
+      km_assign_kernel<64><<<ntiles, kAsgT, asg_smem, st>>>(d_G, d, P, at<uint32_t>(ws, o_tp), at<uint64_t>(ws, o_tr0),
+                                                             at<uint32_t>(ws, o_tlen), d_C, d_local, mind, keys);
+    } else if (d == 128) {
+      km_assign_kernel<128><<<ntiles, kAsgT, asg_smem, st>>>(d_G, d, P, at<uint32_t>(ws, o_tp), at<uint64_t>(ws, o_tr0),
+                                                              at<uint32_t>(ws, o_tlen), d_C, d_local, mind, keys);
+    } else {
+      km_assign_kernel<0><<<ntiles, kAsgT, asg_smem, st>>>(d_G, d, P, at<uint32_t>(ws, o_tp), at<uint64_t>(ws, o_tr0),
+                                                            at<uint32_t>(ws, o_tlen), d_C, d_local, mind, keys);
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+    km_count_kernel<<<1024, 256, 0, st>>>(keys, rows, counts);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 2;
+    const bool last = it + 1 == max_iters;
+    if (check || last) {
+      km_wcss_kernel<<<(unsigned)((NP + 3) / 4), 128, 0, st>>>(P, (uint32_t)NP, mind);
+      MVR_CUDA(ctx, cudaGetLastError());
+      ++launches;
+    }
+    km_exclusive_scan_kernel<<<1, 1024, 0, st>>>(counts, starts, KT);
+    MVR_CUDA(ctx, cudaGetLastError());
+    // stable radix sort of (global cluster, row); `keys` stays in row order
+    // (rows of finished problems keep their keys), the passes ping-pong
+    // between the 2 and 3 buffers
+    const uint32_t* ki = keys;
+    const uint32_t* vi = nullptr;
+    uint32_t *ko = keys2, *vo = vals2;
+    for (int pass = 0; pass < passes; ++pass) {
+      const int shift = 8 * pass;
+      const unsigned g = (unsigned)((radix_nblk + kRadixWarps - 1) / kRadixWarps);
+      km_radix_hist_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, rows, shift, radix_nblk, hist);
+      km_exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, base, (uint64_t)256 * radix_nblk);
+      km_radix_scatter_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, vi, rows, shift, radix_nblk, base, ko, vo);
+      MVR_CUDA(ctx, cudaGetLastError());
+      ki = ko;
+      vi = vo;
+      ko = ko == keys2 ? keys3 : keys2;
+      vo = vo == vals2 ? vals3 : vals2;
+      launches += 3;
+    }
+    const unsigned cgrid = (unsigned)((KT + 7) / 8);
+    if (d == 64)
+      km_chain_kernel<64><<<cgrid, 256, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_cprob), KT, counts, starts, vi, d_C);
+    else if (d == 128)
+      km_chain_kernel<128><<<cgrid, 256, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_cprob), KT, counts, starts, vi, d_C);
+    else
+      km_chain_kernel<0><<<cgrid, 256, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_cprob), KT, counts, starts, vi, d_C);
+    MVR_CUDA(ctx, cudaGetLastError());
+    km_reseed_converge_kernel<<<(unsigned)NP, 256, 0, st>>>(d_G, d, P, (uint32_t)NP, counts, mind, d_C, d_rs,
+                                                            (int)it, check ? 1 : 0, tol);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 3;
+  }
+
+  // ---- results ------------------------------------------------------------------
+  std::vector<int> hstatus(NP);
+  std::vector<uint32_t> hfb(NP);
+  MVR_CUDA(ctx, cudaMemcpyAsync(hstatus.data(), P.status, NP * 4, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaMemcpyAsync(res->wcss.data(), P.wcss, NP * 4, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaMemcpyAsync(res->iters.data(), P.iters, NP * 4, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaMemcpyAsync(hfb.data(), P.fb, NP * 4, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  res->status = hstatus;
+  res->seed_fallbacks = std::accumulate(hfb.begin(), hfb.end(), 0u);
+  res->launches = launches;
+  for (uint32_t p : degen) {
+    res->wcss[p] = 0.f;
+    res->iters[p] = 0;
+  }
+  if (max_iters == 0)
+    for (size_t p = 0; p < NP; ++p) {
+      res->wcss[p] = 0.f;
+      res->iters[p] = 0;
+    }
+  return MVR_OK;
+}
+
+}  // namespace mvr

@@ -1,0 +1,41 @@
+// km_engine.h — ragged batch of independent k-means problems of any
+// dimension on one GPU.
+//
+// Problem p clusters rows [off[p], off[p] + n[p]) of a row-major matrix G
+// (rows x dim) into k[p] centroids stored at rows [coff[p], coff[p] + k[p])
+// of C, with the reference `kmeans.fit` semantics (src/tac/kmeans.zig:67-232)
+// and RNG seed seed[p]. TAC uses one problem per token id (rows gathered in
+// token order, ascending original row inside a token; seed = seed ^ j,
+// src/tac/tac.zig:458-514); `mvr_kmeans_fit` for general dims is P = 1.
+#pragma once
+#include <cstdint>
+#include <vector>
+
+#include "mvr_internal.h"
+
+namespace mvr {
+
+struct KmBatch {
+  std::vector<uint64_t> off;   // first row of problem p in G
+  std::vector<uint32_t> n;     // rows of problem p
+  std::vector<uint32_t> k;     // centroids of problem p
+  std::vector<uint64_t> coff;  // first centroid row of problem p in C
+  std::vector<uint64_t> seed;  // RNG seed of problem p
+  size_t size() const { return n.size(); }
+};
+
+struct KmResult {
+  std::vector<int> status;      // MVR status per problem
+  std::vector<float> wcss;      // final WCSS per problem (0 for degenerate)
+  std::vector<uint32_t> iters;  // Lloyd iterations run per problem
+  uint32_t seed_fallbacks = 0;  // draws settled by the exact sequential chain
+  uint32_t launches = 0;
+};
+
+// Runs every problem to completion. d_G: rows x dim (device), d_C: sum(k) x
+// dim (device, output), d_local: rows u32 (device, output: local cluster id
+// of each row within its problem). Synchronises the context stream.
+int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const KmBatch& b,
+                 uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res);
+
+}  // namespace mvr
