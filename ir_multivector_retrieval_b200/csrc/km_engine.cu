@@ -90,6 +90,39 @@ __device__ __forceinline__ double gamma_bound(uint64_t n) {
 }
 
 // ---------------------------------------------------------------------------
+// Row gather and the group-major copy. CTA = 32 rows: rows are read whole
+// (V[idx[q]] or V[q]) into a shared tile whose row stride is 4 mod 32 words,
+// written back row-major to G (optional) and as float4 groups to GT, where
+// group g of rows q0..q0+31 is one contiguous 512-byte run. Coordinates past
+// d in the last group are zero.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+km_gather_groups_kernel(const float* __restrict__ V, const uint32_t* __restrict__ idx, uint64_t n, int d,
+                        int stride, float* __restrict__ G, float4* __restrict__ GT) {
+  extern __shared__ __align__(16) float tile[];
+  const uint64_t q0 = (uint64_t)blockIdx.x * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng4 = (d + 3) >> 2;
+  for (int i = warp; i < 32; i += 8) {
+    const uint64_t q = q0 + i;
+    if (q < n) {
+      const float* src = V + (idx ? (uint64_t)idx[q] : q) * d;
+      for (int e = lane; e < ng4 * 4; e += 32) {
+        const float v = e < d ? src[e] : 0.f;
+        tile[i * stride + e] = v;
+        if (G && e < d) G[q * d + e] = v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < ng4 * 32; t += 256) {
+    const int g = t >> 5, i = t & 31;
+    const uint64_t q = q0 + i;
+    if (q < n) GT[(uint64_t)g * n + q] = *reinterpret_cast<const float4*>(tile + i * stride + 4 * g);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // degenerate k >= n (kmeans.zig:88-104)
 // ---------------------------------------------------------------------------
 __global__ void km_degenerate_kernel(const float* __restrict__ G, int d, Prob P,
@@ -121,21 +154,64 @@ __global__ void km_seed_init_kernel(const float* __restrict__ G, int d, Prob P,
   for (int j = threadIdx.x; j < d; j += blockDim.x) C[dst + j] = G[src + j];
 }
 
+// l2_gen over the group-major copy GT (float4 group g of row r at
+// GT[g * R + r]): the same lane layout (coordinate 4g + l feeds lane l),
+// ordered reduction and scalar tail as l2_gen. NG = d / 4 when it is a
+// compile-time constant (64 -> 16, 128 -> 32), 0 for any d.
+template <int NG>
+__device__ __forceinline__ float l2_groups(const float4* __restrict__ GT, uint64_t R, uint64_t r,
+                                           const float4* __restrict__ c4, int d) {
+  const int ng = NG > 0 ? NG : d >> 2;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll(NG > 0 ? NG : 1)
+  for (int g = 0; g < ng; ++g) {
+    const float4 v = __ldg(GT + (uint64_t)g * R + r);
+    const float4 c = c4[g];
+    const float d0 = __fsub_rn(v.x, c.x), d1 = __fsub_rn(v.y, c.y);
+    const float d2 = __fsub_rn(v.z, c.z), d3 = __fsub_rn(v.w, c.w);
+    a0 = __fadd_rn(a0, __fmul_rn(d0, d0));
+    a1 = __fadd_rn(a1, __fmul_rn(d1, d1));
+    a2 = __fadd_rn(a2, __fmul_rn(d2, d2));
+    a3 = __fadd_rn(a3, __fmul_rn(d3, d3));
+  }
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  if (NG == 0 && (d & 3)) {
+    const float4 v = __ldg(GT + (uint64_t)ng * R + r);
+    const float4 c = c4[ng];
+    const float t0 = __fsub_rn(v.x, c.x);
+    s = __fadd_rn(s, __fmul_rn(t0, t0));
+    if ((d & 3) > 1) {
+      const float t1 = __fsub_rn(v.y, c.y);
+      s = __fadd_rn(s, __fmul_rn(t1, t1));
+    }
+    if ((d & 3) > 2) {
+      const float t2 = __fsub_rn(v.z, c.z);
+      s = __fadd_rn(s, __fmul_rn(t2, t2));
+    }
+  }
+  return s;
+}
+
 // min_dist update with centroid `step` for the active chunks, plus per-chunk
-// directed-rounding sums and the count of non-zero weights below thr.
+// directed-rounding sums and the count of non-zero weights below thr. Rows
+// come from the group-major copy, so each float4 load of a warp is one
+// contiguous 512-byte segment.
+template <int NG>
 __global__ void __launch_bounds__(kUpdT)
-km_seed_update_kernel(const float* __restrict__ G, int d, Prob P, int step,
+km_seed_update_kernel(const float4* __restrict__ GT, uint64_t R, int d, Prob P, int step,
                       const uint32_t* __restrict__ ch_p, const uint64_t* __restrict__ ch_r0,
                       const uint32_t* __restrict__ ch_len, const float* __restrict__ C,
                       float* __restrict__ md, double2* __restrict__ ch_sum,
                       uint32_t* __restrict__ ch_cnt) {
-  extern __shared__ float cen[];
+  extern __shared__ __align__(16) float4 cen4[];
   __shared__ double2 wp[kUpdT / 32];
   __shared__ uint32_t wc[kUpdT / 32];
   const uint32_t p = ch_p[blockIdx.x];
   if (P.state[p] != kRunning) return;
   const uint64_t co = P.coff[p] + step;
-  for (int j = threadIdx.x; j < d; j += kUpdT) cen[j] = C[co * d + j];
+  const int ng4 = (d + 3) >> 2;
+  float* cen = reinterpret_cast<float*>(cen4);
+  for (int j = threadIdx.x; j < ng4 * 4; j += kUpdT) cen[j] = j < d ? C[co * d + j] : 0.f;
   __syncthreads();
   const uint64_t r0 = ch_r0[blockIdx.x];
   const uint32_t len = ch_len[blockIdx.x];
@@ -143,21 +219,31 @@ km_seed_update_kernel(const float* __restrict__ G, int d, Prob P, int step,
   double lo = 0.0, hi = 0.0;
   uint32_t cnt = 0;
   bool bad = false;
-  for (uint32_t i = threadIdx.x; i < len; i += kUpdT) {
-    const uint64_t r = r0 + i;
-    const float dist = l2_gen(G + r * d, cen, d);
-    float w;
-    if (step == 0) {
-      w = dist;
-    } else {
-      const float old = md[r];
-      w = dist < old ? dist : old;
+  constexpr int kRowsPerThread = kChunk / kUpdT;
+  float dist[kRowsPerThread];
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const uint32_t i = threadIdx.x + u * kUpdT;
+    dist[u] = i < len ? l2_groups<NG>(GT, R, r0 + i, cen4, d) : 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < kRowsPerThread; ++u) {
+    const uint32_t i = threadIdx.x + u * kUpdT;
+    if (i < len) {
+      const uint64_t r = r0 + i;
+      float w;
+      if (step == 0) {
+        w = dist[u];
+      } else {
+        const float old = md[r];
+        w = dist[u] < old ? dist[u] : old;
+      }
+      md[r] = w;
+      bad |= !isfinite(w) || w < 0.f;
+      lo = __dadd_rd(lo, (double)w);
+      hi = __dadd_ru(hi, (double)w);
+      cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
     }
-    md[r] = w;
-    bad |= !isfinite(w) || w < 0.f;
-    lo = __dadd_rd(lo, (double)w);
-    hi = __dadd_ru(hi, (double)w);
-    cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
   }
   if (bad) P.nonf[p] = 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -411,49 +497,136 @@ __global__ void km_count_kernel(const uint32_t* __restrict__ keys, uint64_t n, u
     atomicAdd(&counts[keys[i]], 1u);
 }
 
-// Sequential f32 WCSS per problem (kmeans.zig:179): one warp per problem,
-// rows staged through shared memory, lane 0 adds in row order.
+// Sequential f32 WCSS per problem (kmeans.zig:179): one warp per problem.
+// The warp double-buffers 1024-value tiles of min_to_any in shared memory
+// with cp.async while lane 0 adds the current tile in row order, so the
+// dependent-add chain is the only serial part.
 __global__ void __launch_bounds__(128)
 km_wcss_kernel(Prob P, uint32_t nprob, const float* __restrict__ mind) {
-  __shared__ __align__(16) float tile[4][256];
+  __shared__ __align__(16) float tile[4][2][1024];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t p = blockIdx.x * 4 + warp;
   if (p >= nprob || P.state[p] != kRunning) return;
   const float* src = mind + P.off[p];
   const uint32_t n = P.n[p];
   float acc = 0.f;
-  for (uint32_t t0 = 0; t0 < n; t0 += 256) {
-    const uint32_t m = min(256u, n - t0);
-    for (uint32_t e = lane; e < m; e += 32) tile[warp][e] = src[t0 + e];
+  for (uint32_t e = lane; e < min(1024u, n); e += 32) cp_async<4>(&tile[warp][0][e], src + e);
+  cp_async_commit();
+  int buf = 0;
+  for (uint32_t t0 = 0; t0 < n; t0 += 1024) {
+    const uint32_t m = min(1024u, n - t0);
+    cp_async_wait<0>();
     __syncwarp();
-    if (lane == 0)
-      for (uint32_t e = 0; e < m; ++e) acc = __fadd_rn(acc, tile[warp][e]);
+    const uint32_t t1 = t0 + 1024;
+    if (t1 < n) {
+      const uint32_t m1 = min(1024u, n - t1);
+      for (uint32_t e = lane; e < m1; e += 32) cp_async<4>(&tile[warp][buf ^ 1][e], src + t1 + e);
+    }
+    cp_async_commit();
+    if (lane == 0) {
+      const float4* t4 = reinterpret_cast<const float4*>(tile[warp][buf]);
+      const uint32_t m4 = m >> 2;
+#pragma unroll 8
+      for (uint32_t e = 0; e < m4; ++e) {
+        const float4 v = t4[e];
+        acc = __fadd_rn(acc, v.x);
+        acc = __fadd_rn(acc, v.y);
+        acc = __fadd_rn(acc, v.z);
+        acc = __fadd_rn(acc, v.w);
+      }
+      for (uint32_t e = m4 * 4; e < m; ++e) acc = __fadd_rn(acc, tile[warp][buf][e]);
+    }
     __syncwarp();
+    buf ^= 1;
   }
+  cp_async_wait<0>();
   if (lane == 0) P.wcss[p] = acc;
 }
 
-// Single-CTA exclusive scan of counts (n entries) into starts.
-__global__ void __launch_bounds__(1024)
-km_exclusive_scan_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out, uint64_t n) {
-  __shared__ uint32_t part[1024];
-  const uint64_t per = (n + 1023) / 1024;
-  const uint64_t lo = min(n, (uint64_t)threadIdx.x * per), hi = min(n, lo + per);
+// Exclusive scan of n u32 in three launches: per-tile sums (tiles of
+// kScanTile), one CTA scanning the tile sums, per-tile scans plus offsets.
+constexpr int kScanT = 512;
+constexpr int kScanV = 8;
+constexpr int kScanTile = kScanT * kScanV;
+
+__device__ __forceinline__ uint32_t warp_incl_scan_u32(uint32_t x, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
+__global__ void __launch_bounds__(kScanT)
+km_scan_reduce_kernel(const uint32_t* __restrict__ in, uint64_t n, uint32_t* __restrict__ part) {
+  __shared__ uint32_t ws[kScanT / 32];
+  const uint64_t base = (uint64_t)blockIdx.x * kScanTile;
   uint32_t s = 0;
-  for (uint64_t i = lo; i < hi; ++i) s += in[i];
-  part[threadIdx.x] = s;
+#pragma unroll
+  for (int u = 0; u < kScanV; ++u) {
+    const uint64_t e = base + (uint64_t)u * kScanT + threadIdx.x;
+    if (e < n) s += in[e];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  s = __reduce_add_sync(0xffffffffu, s);
+  if (lane == 0) ws[warp] = s;
   __syncthreads();
-  for (int o = 1; o < 1024; o <<= 1) {
-    const uint32_t v = threadIdx.x >= (unsigned)o ? part[threadIdx.x - o] : 0u;
+  if (warp == 0) {
+    uint32_t v = lane < kScanT / 32 ? ws[lane] : 0u;
+    v = __reduce_add_sync(0xffffffffu, v);
+    if (lane == 0) part[blockIdx.x] = v;
+  }
+}
+
+__global__ void __launch_bounds__(1024)
+km_scan_partials_kernel(uint32_t* __restrict__ part, uint32_t np) {
+  __shared__ uint32_t ws[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t carry = 0;
+  for (uint32_t t0 = 0; t0 < np; t0 += 1024) {
+    const uint32_t e = t0 + threadIdx.x;
+    const uint32_t v = e < np ? part[e] : 0u;
+    const uint32_t x = warp_incl_scan_u32(v, lane);
+    if (lane == 31) ws[warp] = x;
     __syncthreads();
-    part[threadIdx.x] += v;
+    if (warp == 0) ws[lane] = warp_incl_scan_u32(ws[lane], lane);
+    __syncthreads();
+    const uint32_t incl = x + (warp > 0 ? ws[warp - 1] : 0u);
+    if (e < np) part[e] = carry + incl - v;
+    carry += ws[31];
     __syncthreads();
   }
-  uint32_t run = part[threadIdx.x] - s;
-  for (uint64_t i = lo; i < hi; ++i) {
-    const uint32_t v = in[i];
-    out[i] = run;
-    run += v;
+}
+
+__global__ void __launch_bounds__(kScanT)
+km_scan_apply_kernel(const uint32_t* __restrict__ in, uint64_t n, const uint32_t* __restrict__ part,
+                     uint32_t* __restrict__ out) {
+  __shared__ uint32_t ws[kScanT / 32];
+  const uint64_t base = (uint64_t)blockIdx.x * kScanTile + (uint64_t)threadIdx.x * kScanV;
+  uint32_t v[kScanV];
+  uint32_t s = 0;
+#pragma unroll
+  for (int u = 0; u < kScanV; ++u) {
+    v[u] = base + u < n ? in[base + u] : 0u;
+    s += v[u];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t x = warp_incl_scan_u32(s, lane);
+  if (lane == 31) ws[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = lane < kScanT / 32 ? ws[lane] : 0u;
+    const uint32_t wi = warp_incl_scan_u32(w, lane);
+    __syncwarp();
+    if (lane < kScanT / 32) ws[lane] = wi;
+  }
+  __syncthreads();
+  uint32_t run = part[blockIdx.x] + (x - s) + (warp > 0 ? ws[warp - 1] : 0u);
+#pragma unroll
+  for (int u = 0; u < kScanV; ++u) {
+    if (base + u < n) out[base + u] = run;
+    run += v[u];
   }
 }
 
@@ -641,7 +814,31 @@ T* at(unsigned char* base, size_t o) { return reinterpret_cast<T*>(base + o); }
 
 }  // namespace
 
-int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const KmBatch& b,
+int km_gather_groups(Ctx* ctx, const float* d_V, const uint32_t* d_idx, uint64_t n, uint32_t dim, float* d_G,
+                     float* d_GT) {
+  if (n == 0) return MVR_OK;
+  const int ng4 = (int)((dim + 3) / 4);
+  const int stride = 4 * ng4 + ((4 - 4 * ng4) % 32 + 32) % 32;  // 4 mod 32 words
+  const size_t smem = (size_t)32 * stride * sizeof(float);
+  km_gather_groups_kernel<<<(unsigned)((n + 31) / 32), 256, smem, ctx->stream>>>(
+      d_V, d_idx, n, (int)dim, stride, d_G, reinterpret_cast<float4*>(d_GT));
+  MVR_CUDA(ctx, cudaGetLastError());
+  return MVR_OK;
+}
+
+namespace {
+// Exclusive scan of n u32 (n >= 1); `part` holds ceil(n / kScanTile) u32.
+int scan_u32(Ctx* ctx, cudaStream_t st, const uint32_t* in, uint64_t n, uint32_t* part, uint32_t* out) {
+  const unsigned nt = (unsigned)((n + kScanTile - 1) / kScanTile);
+  km_scan_reduce_kernel<<<nt, kScanT, 0, st>>>(in, n, part);
+  km_scan_partials_kernel<<<1, 1024, 0, st>>>(part, nt);
+  km_scan_apply_kernel<<<nt, kScanT, 0, st>>>(in, n, part, out);
+  MVR_CUDA(ctx, cudaGetLastError());
+  return MVR_OK;
+}
+}  // namespace
+
+int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, uint32_t dim, const KmBatch& b,
                  uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res) {
   const size_t NP = b.size();
   res->status.assign(NP, MVR_OK);
@@ -731,7 +928,8 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
                o_chcnt = cv.take(std::max<size_t>(1, ch_p.size()) * 4), o_md = cv.take(rows * 4),
                o_keys = cv.take(rows * 4), o_keys2 = cv.take(rows * 4), o_vals2 = cv.take(rows * 4),
                o_keys3 = cv.take(rows * 4), o_vals3 = cv.take(rows * 4), o_counts = cv.take(KT * 4), o_starts = cv.take(KT * 4),
-               o_hist = cv.take((size_t)256 * radix_nblk * 4), o_base = cv.take((size_t)256 * radix_nblk * 4);
+               o_hist = cv.take((size_t)256 * radix_nblk * 4), o_base = cv.take((size_t)256 * radix_nblk * 4),
+               o_part = cv.take((std::max<uint64_t>(KT, (uint64_t)256 * radix_nblk) / kScanTile + 2) * 4);
   unsigned char* ws = nullptr;
   MVR_TRY(scratch(ctx, kSlotAux3, cv.off, (void**)&ws));
   std::vector<unsigned char> hb(host_bytes, 0);
@@ -808,9 +1006,14 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
                                    seeders.begin());
     if (na == 0) break;
     const uint32_t nch = chunks_upto[na - 1];
-    km_seed_update_kernel<<<nch, kUpdT, d * sizeof(float), st>>>(
-        d_G, d, P, (int)s - 1, at<uint32_t>(ws, o_chp), at<uint64_t>(ws, o_chr0), at<uint32_t>(ws, o_chlen),
-        d_C, at<float>(ws, o_md), at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt));
+    {
+      const float4* gt4 = reinterpret_cast<const float4*>(d_GT);
+      const size_t sm = (size_t)((d + 3) / 4) * sizeof(float4);
+      auto upd = d == 64 ? km_seed_update_kernel<16> : d == 128 ? km_seed_update_kernel<32> : km_seed_update_kernel<0>;
+      upd<<<nch, kUpdT, sm, st>>>(gt4, rows, d, P, (int)s - 1, at<uint32_t>(ws, o_chp), at<uint64_t>(ws, o_chr0),
+                                  at<uint32_t>(ws, o_chlen), d_C, at<float>(ws, o_md), at<double2>(ws, o_chsum),
+                                  at<uint32_t>(ws, o_chcnt));
+    }
     MVR_CUDA(ctx, cudaGetLastError());
     km_seed_select_kernel<<<na, kSelT, 0, st>>>(
         d_G, d, P, (int)s, at<uint32_t>(ws, o_seeders), at<uint32_t>(ws, o_cfirst), at<uint32_t>(ws, o_ccount),
@@ -832,6 +1035,9 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
   uint32_t* starts = at<uint32_t>(ws, o_starts);
   uint32_t* hist = at<uint32_t>(ws, o_hist);
   uint32_t* base = at<uint32_t>(ws, o_base);
+  uint32_t* part = at<uint32_t>(ws, o_part);
+  cudaStream_t side = nullptr;
+  MVR_TRY(side_stream(ctx, &side));
   const unsigned ntiles = (unsigned)t_p.size();
   const size_t asg_smem = (size_t)kCT * d * sizeof(float);
   for (uint32_t it = 0; it < max_iters && !live.empty(); ++it) {
@@ -851,13 +1057,16 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
     MVR_CUDA(ctx, cudaGetLastError());
     launches += 2;
     const bool last = it + 1 == max_iters;
-    if (check || last) {
-      km_wcss_kernel<<<(unsigned)((NP + 3) / 4), 128, 0, st>>>(P, (uint32_t)NP, mind);
+    const bool want_wcss = check || last;
+    if (want_wcss) {  // the serial WCSS overlaps the sort and the centroid sums
+      MVR_CUDA(ctx, cudaEventRecord(ctx->fork_ev, st));
+      MVR_CUDA(ctx, cudaStreamWaitEvent(side, ctx->fork_ev, 0));
+      km_wcss_kernel<<<(unsigned)((NP + 3) / 4), 128, 0, side>>>(P, (uint32_t)NP, mind);
       MVR_CUDA(ctx, cudaGetLastError());
+      MVR_CUDA(ctx, cudaEventRecord(ctx->join_ev, side));
       ++launches;
     }
-    km_exclusive_scan_kernel<<<1, 1024, 0, st>>>(counts, starts, KT);
-    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_TRY(scan_u32(ctx, st, counts, KT, part, starts));
     // stable radix sort of (global cluster, row); `keys` stays in row order
     // (rows of finished problems keep their keys), the passes ping-pong
     // between the 2 and 3 buffers
@@ -868,14 +1077,14 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
       const int shift = 8 * pass;
       const unsigned g = (unsigned)((radix_nblk + kRadixWarps - 1) / kRadixWarps);
       km_radix_hist_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, rows, shift, radix_nblk, hist);
-      km_exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, base, (uint64_t)256 * radix_nblk);
+      MVR_TRY(scan_u32(ctx, st, hist, (uint64_t)256 * radix_nblk, part, base));
       km_radix_scatter_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, vi, rows, shift, radix_nblk, base, ko, vo);
       MVR_CUDA(ctx, cudaGetLastError());
       ki = ko;
       vi = vo;
       ko = ko == keys2 ? keys3 : keys2;
       vo = vo == vals2 ? vals3 : vals2;
-      launches += 3;
+      launches += 5;
     }
     const unsigned cgrid = (unsigned)((KT + 7) / 8);
     if (d == 64)
@@ -885,10 +1094,11 @@ int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const 
     else
       km_chain_kernel<0><<<cgrid, 256, 0, st>>>(d_G, d, P, at<uint32_t>(ws, o_cprob), KT, counts, starts, vi, d_C);
     MVR_CUDA(ctx, cudaGetLastError());
+    if (want_wcss) MVR_CUDA(ctx, cudaStreamWaitEvent(st, ctx->join_ev, 0));
     km_reseed_converge_kernel<<<(unsigned)NP, 256, 0, st>>>(d_G, d, P, (uint32_t)NP, counts, mind, d_C, d_rs,
                                                             (int)it, check ? 1 : 0, tol);
     MVR_CUDA(ctx, cudaGetLastError());
-    launches += 3;
+    launches += 5;
   }
 
   // ---- results ------------------------------------------------------------------

@@ -32,10 +32,18 @@ struct KmResult {
   uint32_t launches = 0;
 };
 
-// Runs every problem to completion. d_G: rows x dim (device), d_C: sum(k) x
-// dim (device, output), d_local: rows u32 (device, output: local cluster id
-// of each row within its problem). Synchronises the context stream.
-int km_batch_run(Ctx* ctx, const float* d_G, uint64_t rows, uint32_t dim, const KmBatch& b,
+// Group-major copy of a row set: GT holds ceil(dim / 4) groups, group g of
+// row q (coordinates 4g .. 4g+3, zero past dim) as the float4 GT[g * n + q].
+// Row q is V[idx[q]] (or V[q] when idx is null); when G is not null the rows
+// are also written row-major to G. Enqueued on the context stream.
+int km_gather_groups(Ctx* ctx, const float* d_V, const uint32_t* d_idx, uint64_t n, uint32_t dim, float* d_G,
+                     float* d_GT);
+
+// Runs every problem to completion. d_G: rows x dim (device), d_GT: its
+// group-major copy (km_gather_groups), d_C: sum(k) x dim (device, output),
+// d_local: rows u32 (device, output: local cluster id of each row within its
+// problem). Synchronises the context stream.
+int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, uint32_t dim, const KmBatch& b,
                  uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res);
 
 }  // namespace mvr

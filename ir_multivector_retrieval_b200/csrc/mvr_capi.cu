@@ -54,6 +54,16 @@ int scratch(Ctx* ctx, int slot, size_t bytes, void** out) {
   return MVR_OK;
 }
 
+int side_stream(Ctx* ctx, cudaStream_t* out) {
+  if (!ctx->side) {
+    MVR_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking));
+    MVR_CUDA(ctx, cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming));
+    MVR_CUDA(ctx, cudaEventCreateWithFlags(&ctx->join_ev, cudaEventDisableTiming));
+  }
+  *out = ctx->side;
+  return MVR_OK;
+}
+
 int pinned(Ctx* ctx, size_t bytes, void** out) {
   if (ctx->pinned_bytes < bytes) {
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
@@ -193,6 +203,12 @@ int mvr_ctx_destroy(mvr_ctx* h) {
   if (c->pinned) cudaFreeHost(c->pinned);
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
+  if (c->side) {
+    cudaStreamSynchronize(c->side);
+    cudaStreamDestroy(c->side);
+  }
+  if (c->fork_ev) cudaEventDestroy(c->fork_ev);
+  if (c->join_ev) cudaEventDestroy(c->join_ev);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete h;
   return MVR_OK;

@@ -44,7 +44,14 @@ struct Ctx {
   void* pinned = nullptr;  // host staging for small device->host reads
   size_t pinned_bytes = 0;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // second stream for work that overlaps the main chain (created on first
+  // use), with its fork/join events
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 };
+
+// The context's side stream (created on first use on the current device).
+int side_stream(Ctx* ctx, cudaStream_t* out);
 
 // Set the context's last error and return `status`.
 int fail(Ctx* ctx, int status, const std::string& msg);

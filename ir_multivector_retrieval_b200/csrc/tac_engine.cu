@@ -16,71 +16,112 @@
 
 #include "../../include/mvr.h"
 #include "km_engine.h"
+#include "mvr_device.cuh"
 #include "mvr_internal.h"
 #include "tac_engine.h"
 
 namespace mvr {
 namespace {
 
-// G[q] = V[idx[q]]: one warp per row.
-__global__ void tac_gather_kernel(const float* __restrict__ V, const uint32_t* __restrict__ idx, uint64_t n,
-                                  uint32_t d, float* __restrict__ G) {
-  const uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint64_t stride = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-  for (uint64_t q = w; q < n; q += stride) {
-    const float* src = V + (uint64_t)idx[q] * d;
-    float* dst = G + q * d;
-    for (uint32_t j = lane; j < d; j += 32) dst[j] = src[j];
-  }
-}
-
 // Welford spread of one token per warp (tac.zig:609-644): f32 count,
 // inv = 1/count, per coordinate delta = x - mean; mean += delta*inv;
 // m2 += delta*(x - mean); trace = sum of m2 in coordinate order;
-// spread = trace / n. Coordinates j live in lane j % 32, slot j / 32.
-__global__ void __launch_bounds__(128)
+// spread = trace / n. Coordinate c lives in lane c % 32, slot c / 32 (Q
+// slots, d <= 32 Q). A token's rows are contiguous in G; they stream through
+// a per-warp ring of kSpStages shared-memory stages filled by cp.async, so
+// the dependent Welford chain, not load latency, sets the pace. The f32
+// count after q rows is min(q, 2^24) exactly (x + 1 rounds back to 2^24
+// there), so 32 lanes form 32 rows' 1/count at once.
+constexpr int kSpWarps = 4;
+constexpr int kSpStages = 3;
+constexpr int kSpStageFloats = 2048;
+
+template <int Q>
+__global__ void __launch_bounds__(kSpWarps * 32)
 tac_spread_kernel(const float* __restrict__ G, uint32_t d, const uint32_t* __restrict__ goff, uint64_t nd,
                   float* __restrict__ spreads) {
-  constexpr int Q = 8;  // d <= 256
-  const uint64_t j = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (j >= nd) return;
-  const uint32_t start = goff[j], end = goff[j + 1];
-  const uint32_t n = end - start;
-  if (n == 0) {
-    if (lane == 0) spreads[j] = 0.f;
-    return;
-  }
-  float mean[Q], m2[Q];
+  extern __shared__ __align__(16) float sp_stage[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* ring = sp_stage + (size_t)warp * kSpStages * kSpStageFloats;
+  const uint32_t rb = kSpStageFloats / d;  // rows per stage (>= 8)
+  const uint32_t sf = rb * d;
+  const bool vec = (d & 3) == 0;
+  for (uint64_t j = (uint64_t)blockIdx.x * kSpWarps + warp; j < nd; j += (uint64_t)gridDim.x * kSpWarps) {
+    const uint32_t start = goff[j], n = goff[j + 1] - start;
+    if (n == 0) {
+      if (lane == 0) spreads[j] = 0.f;
+      continue;
+    }
+    const float* src = G + (uint64_t)start * d;
+    const uint32_t nst = (n + rb - 1) / rb;
+    auto issue = [&](uint32_t stg) {
+      if (stg < nst) {
+        const uint32_t nf = min(rb, n - stg * rb) * d;
+        const float* s0 = src + (uint64_t)stg * sf;
+        float* d0 = ring + (stg % kSpStages) * kSpStageFloats;
+        if (vec) {
+          for (uint32_t e = lane * 4; e < nf; e += 128) cp_async<16>(d0 + e, s0 + e);
+        } else {
+          for (uint32_t e = lane; e < nf; e += 32) cp_async<4>(d0 + e, s0 + e);
+        }
+      }
+      cp_async_commit();
+    };
+    __syncwarp();  // the previous token's reads of the ring are done
 #pragma unroll
-  for (int q = 0; q < Q; ++q) { mean[q] = 0.f; m2[q] = 0.f; }
-  float count = 0.f;
-  for (uint32_t r = start; r < end; ++r) {
-    count = __fadd_rn(count, 1.0f);
-    const float inv = __fdiv_rn(1.0f, count);
-    const float* x = G + (uint64_t)r * d;
+    for (int q = 0; q < kSpStages - 1; ++q) issue(q);
+    float mean[Q], m2[Q];
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
-      const uint32_t c = lane + 32 * q;
-      if (c < d) {
-        const float xv = __ldg(x + c);
-        const float delta = __fsub_rn(xv, mean[q]);
-        mean[q] = __fadd_rn(mean[q], __fmul_rn(delta, inv));
-        m2[q] = __fadd_rn(m2[q], __fmul_rn(delta, __fsub_rn(xv, mean[q])));
+      mean[q] = 0.f;
+      m2[q] = 0.f;
+    }
+    for (uint32_t stg = 0; stg < nst; ++stg) {
+      cp_async_wait<kSpStages - 2>();
+      __syncwarp();
+      issue(stg + kSpStages - 1);
+      const float* x = ring + (stg % kSpStages) * kSpStageFloats;
+      const uint32_t rows = min(rb, n - stg * rb);
+      const uint32_t row0 = stg * rb;
+      float invl = 0.f;
+      for (uint32_t r = 0; r < rows; ++r) {
+        if ((r & 31) == 0) {
+          const uint32_t q = row0 + r + lane + 1;
+          invl = __fdiv_rn(1.0f, __uint2float_rn(min(q, 16777216u)));
+        }
+        const float inv = __shfl_sync(0xffffffffu, invl, r & 31);
+        const float* xr = x + r * d;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+          const uint32_t c = lane + 32 * q;
+          if (c < d) {
+            const float xv = xr[c];
+            const float delta = __fsub_rn(xv, mean[q]);
+            mean[q] = __fadd_rn(mean[q], __fmul_rn(delta, inv));
+            m2[q] = __fadd_rn(m2[q], __fmul_rn(delta, __fsub_rn(xv, mean[q])));
+          }
+        }
       }
     }
-  }
-  float trace = 0.f;
-  for (uint32_t c = 0; c < d; ++c) {
-    float v = 0.f;
+    cp_async_wait<0>();
+    float trace = 0.f;
 #pragma unroll
     for (int q = 0; q < Q; ++q)
-      if ((int)(c / 32) == q) v = m2[q];
-    v = __shfl_sync(0xffffffffu, v, c % 32);
-    trace = __fadd_rn(trace, v);
+      for (uint32_t l = 0; l < 32 && 32 * q + l < d; ++l)
+        trace = __fadd_rn(trace, __shfl_sync(0xffffffffu, m2[q], l));
+    if (lane == 0) spreads[j] = __fdiv_rn(trace, __uint2float_rn(n));
   }
-  if (lane == 0) spreads[j] = __fdiv_rn(trace, __uint2float_rn(n));
+}
+
+int launch_spreads(Ctx* c, const float* d_G, uint32_t d, const uint32_t* d_goff, uint64_t nd, float* d_sp) {
+  const size_t smem = (size_t)kSpWarps * kSpStages * kSpStageFloats * sizeof(float);
+  const unsigned grid = (unsigned)std::min<uint64_t>((nd + kSpWarps - 1) / kSpWarps, 1u << 20);
+  auto k = d <= 32 ? tac_spread_kernel<1> : d <= 64 ? tac_spread_kernel<2> : d <= 128 ? tac_spread_kernel<4>
+                                                                                     : tac_spread_kernel<8>;
+  MVR_CUDA(c, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<grid, kSpWarps * 32, smem, c->stream>>>(d_G, d, d_goff, nd, d_sp);
+  MVR_CUDA(c, cudaGetLastError());
+  return MVR_OK;
 }
 
 // assignments[idx[q]] = base[token of q] + local[q]
@@ -109,8 +150,12 @@ int kmeans_general_device(Ctx* ctx, const float* d_v, uint64_t n, uint32_t dim, 
   b.coff = {0};
   b.seed = {seed};
   if (n >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows");
+  if (dim > 256) return fail(ctx, MVR_E_INVALID_ARGUMENT, "dim > 256 is not supported on the GPU path");
+  float* d_GT = nullptr;
+  MVR_TRY(scratch(ctx, kSlotSorted, (size_t)n * ((dim + 3) / 4) * 4 * sizeof(float), (void**)&d_GT));
+  MVR_TRY(km_gather_groups(ctx, d_v, nullptr, n, dim, nullptr, d_GT));
   KmResult r;
-  MVR_TRY(km_batch_run(ctx, d_v, n, dim, b, max_iters, tol, d_centroids, d_assign, &r));
+  MVR_TRY(km_batch_run(ctx, d_v, d_GT, n, dim, b, max_iters, tol, d_centroids, d_assign, &r));
   if (r.status[0] != MVR_OK) return fail(ctx, r.status[0], mvr_status_name(r.status[0]));
   if (h_wcss) *h_wcss = r.wcss[0];
   if (h_iters) *h_iters = r.iters[0];
@@ -161,6 +206,8 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   const uint64_t rows = n_tokens;
   MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, rows * dim * sizeof(float), (void**)&d_V));
   MVR_TRY(mvr::scratch(c, mvr::kSlotSorted, rows * dim * sizeof(float), (void**)&d_G));
+  float* d_GT = nullptr;
+  MVR_TRY(mvr::scratch(c, mvr::kSlotMinDist, rows * ((dim + 3) / 4) * 4 * sizeof(float), (void**)&d_GT));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux0, rows * sizeof(uint32_t), (void**)&d_gidx));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux1, rows * sizeof(uint32_t), (void**)&d_local));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux2, rows * sizeof(uint32_t) * 2 + (nd + 1) * 4 * 2 + nd * 4 + 1024,
@@ -173,13 +220,8 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   MVR_CUDA(c, cudaMemcpyAsync(d_gidx, gidx.data(), rows * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_goff, goff.data(), (nd + 1) * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_rowtok, rowtok.data(), rows * 4, cudaMemcpyHostToDevice, st));
-  {
-    const int grid = (int)std::min<uint64_t>((rows * 32 + 255) / 256, (uint64_t)c->sm_count * 32);
-    mvr::tac_gather_kernel<<<grid, 256, 0, st>>>(d_V, d_gidx, rows, dim, d_G);
-    MVR_CUDA(c, cudaGetLastError());
-    mvr::tac_spread_kernel<<<(unsigned)((nd * 32 + 127) / 128), 128, 0, st>>>(d_G, dim, d_goff, nd, d_sp);
-    MVR_CUDA(c, cudaGetLastError());
-  }
+  MVR_TRY(mvr::km_gather_groups(c, d_V, d_gidx, rows, dim, d_G, d_GT));
+  MVR_TRY(mvr::launch_spreads(c, d_G, dim, d_goff, nd, d_sp));
   std::vector<float> spreads(nd);
   MVR_CUDA(c, cudaMemcpyAsync(spreads.data(), d_sp, nd * 4, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(c, cudaStreamSynchronize(st));
@@ -213,7 +255,7 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   }
   MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, (size_t)p->kappa_total * dim * sizeof(float), (void**)&d_C));
   mvr::KmResult r;
-  MVR_TRY(mvr::km_batch_run(c, d_G, rows, dim, b, p->max_iters, p->tol, d_C, d_local, &r));
+  MVR_TRY(mvr::km_batch_run(c, d_G, d_GT, rows, dim, b, p->max_iters, p->tol, d_C, d_local, &r));
   for (size_t q = 0; q < r.status.size(); ++q)  // the lowest failing token, as the serial reference reports
     if (r.status[q] != MVR_OK)
       return mvr::fail(c, r.status[q], std::string("token ") + std::to_string(pj[q]) + ": " +
