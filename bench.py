@@ -18,6 +18,12 @@ host memory every step. Encode throughput is reported beside it.
 (oracle/, multithreaded like the reference's work-stealing ``pq.train``) on
 this host's cores, on a bounded row sample of the same workload.
 
+``tac`` in the JSON line: ``tac.clusterFlat`` through the host-pointer C ABI
+on the same 1,521,797-row corpus with kappa = 32,768 and the paper-strict
+thresholds (mu 128, tau 256, eps 4, theta 39), with its device phases; and on
+configs[0]'s 117,645-row corpus (kappa 12,288, theta 10) beside the CPU
+restatement of the reference timed on one host core.
+
 Multi-GPU (``--gpus N`` under torchrun): each rank runs the full workload
 as an independent replica ("replicas only" in this round); the reported time
 is the max over ranks.
@@ -59,12 +65,67 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def make_input(n: int | None = None) -> np.ndarray:
-    n = N_ROWS if n is None else n
+def make_corpus(n: int | None = None):
     from ir_multivector_retrieval_b200 import synth
 
-    c = synth.make_corpus(n, DIM, seed=42)
-    return synth.anchor_residuals(c)
+    return synth.make_corpus(N_ROWS if n is None else n, DIM, seed=42)
+
+
+def make_input(n: int | None = None) -> np.ndarray:
+    from ir_multivector_retrieval_b200 import synth
+
+    return synth.anchor_residuals(make_corpus(n))
+
+
+TAC_KAPPA = 32_768
+TAC_SMALL = (117_645, 12_288, 10)  # configs[0] rows, kappa (10,240 leaves no room for the tail), theta
+
+
+def measure_tac(corpus, steps: int, cpu: bool) -> dict:
+    """clusterFlat through the host-pointer C ABI (e2e wall time, device
+    phases from mvr_tac_last_stats) on the full corpus and on configs[0]."""
+    from ir_multivector_retrieval_b200 import synth, tac
+
+    out = {"workload": (f"tac.clusterFlat {corpus.n:,} x {DIM}, kappa {TAC_KAPPA:,}, paper-strict "
+                        "(mu 128, tau 256, eps 4, theta 39), 25 iters, tol 1e-4")}
+    p = tac.ClusteringParams(kappa_total=TAC_KAPPA, seed=42)
+    tac.cluster_flat(corpus.token_ids, corpus.vectors, DIM, p)  # warm-up: grows buffers
+    walls, stats = [], []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        r = tac.cluster_flat(corpus.token_ids, corpus.vectors, DIM, p)
+        walls.append(time.perf_counter() - t0)
+        stats.append(tac.last_stats())
+    mid = sorted(range(len(walls)), key=walls.__getitem__)[len(walls) // 2]
+    st = stats[mid]
+    out.update({"e2e_ms": walls[mid] * 1e3,
+                "device_ms": st["spread_ms"] + st["seed_ms"] + st["lloyd_ms"],
+                "phases_ms": {k: st[k] for k in ("host_ms", "h2d_ms", "spread_ms", "seed_ms", "lloyd_ms",
+                                                 "d2h_ms")},
+                "tokens": st["problems"], "iters_max": st["iters_max"], "gpu_launches": st["launches"],
+                "wcss_total": r.wcss_total})
+    n0, k0, th0 = TAC_SMALL
+    c0 = synth.make_corpus(n0, DIM, seed=42)
+    p0 = tac.ClusteringParams(kappa_total=k0, seed=42, theta=th0)
+    tac.cluster_flat(c0.token_ids, c0.vectors, DIM, p0)
+    w0 = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        r0 = tac.cluster_flat(c0.token_ids, c0.vectors, DIM, p0)
+        w0.append(time.perf_counter() - t0)
+    small = {"workload": f"configs[0]: {n0:,} x {DIM}, kappa {k0:,}, theta {th0}", "e2e_ms": statistics.median(w0) * 1e3}
+    if cpu:
+        from oracle import oracle
+
+        oracle.build()
+        t0 = time.perf_counter()
+        rc = oracle.tac_cluster_flat(c0.token_ids, c0.vectors, DIM, k0, 42, theta=th0)
+        small["cpu_baseline"] = {"value_ms": (time.perf_counter() - t0) * 1e3, "cores": 1, "kind": "port",
+                                 "sample": "the whole configs[0] clusterFlat, single-threaded C restatement"}
+        small["bit_exact_vs_cpu"] = bool(np.array_equal(rc.assignments, r0.assignments)
+                                         and rc.centroids.tobytes() == r0.centroids.tobytes())
+    out["small"] = small
+    return out
 
 
 # ---------------------------------------------------------------- clocks
@@ -197,7 +258,10 @@ def run_b200(args) -> None:
     from ir_multivector_retrieval_b200 import Context
     from ir_multivector_retrieval_b200._lib import PqTrainStats
 
-    x = make_input(args.rows)
+    corpus = make_corpus(args.rows)
+    from ir_multivector_retrieval_b200 import synth
+
+    x = synth.anchor_residuals(corpus)
     n = x.shape[0]
     x_pin = torch.from_numpy(x).pin_memory()
     dx = x_pin.to(f"cuda:{local}", non_blocking=False)
@@ -328,6 +392,8 @@ def run_b200(args) -> None:
                     "d2h_bytes_per_step": int(cb_host.nbytes),
                     "encode_mvec_s": n / e2e_enc_s / 1e6},
         }
+        if not args.no_tac:
+            line["tac"] = measure_tac(corpus, 3, cpu=(world == 1 and not args.no_cpu))
         if world == 1 and not args.no_cpu:
             cpu = cpu_lloyd_seconds_per_iter(x, host_threads(), target_s=args.cpu_target_s)
             line["cpu_baseline"] = {
@@ -350,6 +416,7 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-target-s", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-tac", action="store_true", help="skip the clusterFlat measurement")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()

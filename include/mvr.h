@@ -202,6 +202,28 @@ int mvr_pq_encode_device(mvr_ctx* ctx, const float* d_codebooks, uint32_t dim,
                          uint32_t pq_m, const float* d_residuals, uint64_t n,
                          uint8_t* d_codes_out);
 
+/* Timing report of the most recent `mvr_tac_cluster_flat` call on the
+ * context (no reference counterpart; the reference prints `[stage]` lines,
+ * src/tac/tac.zig:660-680). Device times come from CUDA events on the
+ * context's stream, wall times from the host clock; milliseconds. */
+typedef struct mvr_tac_stats {
+  double total_ms;   /* wall time of the whole call */
+  double host_ms;    /* wall time of the host-side grouping and budgets */
+  double h2d_ms;     /* device: host->device copies of the inputs */
+  double spread_ms;  /* device: row gather, group-major copy, spreads */
+  double seed_ms;    /* device: k-means++ seeding of every token */
+  double lloyd_ms;   /* device: Lloyd iterations of every token */
+  double d2h_ms;     /* device: assignments and centroids back to the host */
+  uint32_t problems; /* tokens clustered (k_j > 0) */
+  uint32_t iters_max; /* largest iters_run over tokens */
+  uint32_t seed_fallbacks; /* k-means++ draws resolved by the exact serial chain */
+  uint32_t launches; /* kernel launches of the call */
+} mvr_tac_stats;
+
+/* Copies the report of the context's most recent `mvr_tac_cluster_flat`
+ * call (all zero before the first call). */
+int mvr_tac_last_stats(const mvr_ctx* ctx, mvr_tac_stats* out);
+
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);
 

@@ -69,6 +69,25 @@ class PqTrainStats(C.Structure):
     ]
 
 
+class TacStats(C.Structure):
+    _fields_ = [
+        ("total_ms", C.c_double),
+        ("host_ms", C.c_double),
+        ("h2d_ms", C.c_double),
+        ("spread_ms", C.c_double),
+        ("seed_ms", C.c_double),
+        ("lloyd_ms", C.c_double),
+        ("d2h_ms", C.c_double),
+        ("problems", C.c_uint32),
+        ("iters_max", C.c_uint32),
+        ("seed_fallbacks", C.c_uint32),
+        ("launches", C.c_uint32),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 class ClusteringParams(C.Structure):
     _fields_ = [
         ("kappa_total", C.c_uint32),
@@ -98,6 +117,7 @@ SIGNATURES = {
     "mvr_ctx_set_stream": (C.c_int, [_P, _P]),
     "mvr_ctx_trim": (C.c_int, [_P]),
     "mvr_ctx_sync": (C.c_int, [_P]),
+    "mvr_tac_last_stats": (C.c_int, [_P, C.POINTER(TacStats)]),
     "mvr_kmeans_fit": (
         C.c_int,
         [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,

@@ -980,6 +980,9 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
   const int d = (int)dim;
   uint32_t launches = 0;
 
+  cudaEvent_t* tev = nullptr;
+  MVR_TRY(tac_events(ctx, &tev));
+  MVR_CUDA(ctx, cudaEventRecord(tev[5], st));
   // every row carries a sort key below KT from the start (rows of problems
   // that fail while seeding are never assigned)
   MVR_CUDA(ctx, cudaMemsetAsync(at<uint32_t>(ws, o_keys), 0, rows * 4, st));
@@ -1023,6 +1026,7 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
     launches += 2;
   }
 
+  MVR_CUDA(ctx, cudaEventRecord(tev[6], st));
   // ---- Lloyd iterations ---------------------------------------------------------
   const bool check = !(tol == -INFINITY) && !std::isnan(tol);
   float* mind = at<float>(ws, o_md);
@@ -1101,6 +1105,7 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
     launches += 5;
   }
 
+  MVR_CUDA(ctx, cudaEventRecord(tev[7], st));
   // ---- results ------------------------------------------------------------------
   std::vector<int> hstatus(NP);
   std::vector<uint32_t> hfb(NP);
@@ -1110,6 +1115,13 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
   MVR_CUDA(ctx, cudaMemcpyAsync(hfb.data(), P.fb, NP * 4, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(ctx, cudaStreamSynchronize(st));
   res->status = hstatus;
+  {
+    float a = 0.f, b2 = 0.f;
+    cudaEventElapsedTime(&a, tev[5], tev[6]);
+    cudaEventElapsedTime(&b2, tev[6], tev[7]);
+    res->seed_ms = a;
+    res->lloyd_ms = b2;
+  }
   res->seed_fallbacks = std::accumulate(hfb.begin(), hfb.end(), 0u);
   res->launches = launches;
   for (uint32_t p : degen) {

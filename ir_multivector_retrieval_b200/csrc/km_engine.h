@@ -30,6 +30,8 @@ struct KmResult {
   std::vector<uint32_t> iters;  // Lloyd iterations run per problem
   uint32_t seed_fallbacks = 0;  // draws settled by the exact sequential chain
   uint32_t launches = 0;
+  double seed_ms = 0.0;   // device time of the seeding (degenerate copies included)
+  double lloyd_ms = 0.0;  // device time of the Lloyd iterations
 };
 
 // Group-major copy of a row set: GT holds ceil(dim / 4) groups, group g of

@@ -64,6 +64,13 @@ int side_stream(Ctx* ctx, cudaStream_t* out) {
   return MVR_OK;
 }
 
+int tac_events(Ctx* ctx, cudaEvent_t** out) {
+  for (auto& e : ctx->tev)
+    if (!e) MVR_CUDA(ctx, cudaEventCreate(&e));
+  *out = ctx->tev;
+  return MVR_OK;
+}
+
 int pinned(Ctx* ctx, size_t bytes, void** out) {
   if (ctx->pinned_bytes < bytes) {
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
@@ -85,17 +92,9 @@ int set_device(Ctx* c) {
   return MVR_OK;
 }
 
-int h2d(Ctx* c, void* d, const void* h, size_t bytes) {
-  if (bytes == 0) return MVR_OK;
-  MVR_CUDA(c, cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, c->stream));
-  return MVR_OK;
-}
+int h2d(Ctx* c, void* d, const void* h, size_t bytes) { return h2d_staged(c, d, h, bytes); }
 
-int d2h(Ctx* c, void* h, const void* d, size_t bytes) {
-  if (bytes == 0) return MVR_OK;
-  MVR_CUDA(c, cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, c->stream));
-  return MVR_OK;
-}
+int d2h(Ctx* c, void* h, const void* d, size_t bytes) { return d2h_staged(c, h, d, bytes); }
 
 // storage.residualsAndNormsChunk (src/index/storage.zig:255-278): one
 // thread per row, coordinates summed in order.
@@ -207,10 +206,19 @@ int mvr_ctx_destroy(mvr_ctx* h) {
     cudaStreamSynchronize(c->side);
     cudaStreamDestroy(c->side);
   }
+  mvr::destroy_host_io(c);
+  for (auto& e : c->tev)
+    if (e) cudaEventDestroy(e);
   if (c->fork_ev) cudaEventDestroy(c->fork_ev);
   if (c->join_ev) cudaEventDestroy(c->join_ev);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete h;
+  return MVR_OK;
+}
+
+int mvr_tac_last_stats(const mvr_ctx* h, mvr_tac_stats* out) {
+  if (!h || !out) return MVR_E_INVALID_ARGUMENT;
+  *out = h->impl.tac_stats;
   return MVR_OK;
 }
 

@@ -34,6 +34,8 @@ enum ScratchSlot {
   kSlotCount
 };
 
+class HostPool;
+
 struct Ctx {
   int device = 0;
   int sm_count = 0;
@@ -48,7 +50,24 @@ struct Ctx {
   // use), with its fork/join events
   cudaStream_t side = nullptr;
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  // timing events of the TAC path (created on first use) and its last report
+  cudaEvent_t tev[8] = {};
+  mvr_tac_stats tac_stats = {};
+  // host staging of large host<->device copies (host_io.cpp)
+  HostPool* io_pool = nullptr;
+  void* stage[2] = {nullptr, nullptr};
+  cudaEvent_t stage_ev[2] = {nullptr, nullptr};
 };
+
+// Host->device copy of a pageable host buffer through the pinned stages;
+// the source may be reused when it returns. Ordered on the context stream.
+int h2d_staged(Ctx* ctx, void* d, const void* h, size_t bytes);
+// Device->host copy through the pinned stages; complete when it returns.
+int d2h_staged(Ctx* ctx, void* h, const void* d, size_t bytes);
+void destroy_host_io(Ctx* ctx);
+
+// The context's TAC timing events (created on first use).
+int tac_events(Ctx* ctx, cudaEvent_t** out);
 
 // The context's side stream (created on first use on the current device).
 int side_stream(Ctx* ctx, cudaStream_t* out);

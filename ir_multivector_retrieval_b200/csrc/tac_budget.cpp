@@ -5,6 +5,7 @@
 // allocateBudgets). O(vocabulary) work that runs once per build between the
 // device spread pass and the device per-token k-means.
 #include <cmath>
+#include <algorithm>
 #include <cstdint>
 #include <vector>
 
@@ -84,63 +85,56 @@ int tac_allocate_budgets_host(const uint32_t* freqs, const float* spreads, uint3
     if (kappa[j] > cap) kappa[j] = cap;
   }
 
-  // Phase 4 — largest-remainder reconciliation (tac.zig:281-376)
+  // Phase 4 — largest-remainder reconciliation (tac.zig:281-376). The
+  // reference moves one unit per round to the arg-max (surplus) or arg-min
+  // (deficit) fractional remainder among the eligible active tokens, first
+  // index on ties. A round never changes frac, so the same token wins every
+  // round until it leaves the eligible set (reaches its cap, or its floor
+  // eps); visiting the eligible tokens once in (frac, index) order and
+  // moving all their units at once gives the same result in O(n log n).
   uint64_t cur = 0;
   for (uint64_t j = 0; j < n; ++j) cur += kappa[j];
   if (cur == kappa_total) return MVR_OK;
+  std::vector<uint32_t> order;
   if (cur < kappa_total) {
-    uint32_t remaining = (uint32_t)(kappa_total - cur);
-    while (remaining > 0) {
-      int64_t best = -1;
-      float bf = -INFINITY;
-      for (uint64_t j = 0; j < n; ++j) {
-        if (classify(freqs[j], mu, tau) != kActive) continue;
-        if (kappa[j] >= freqs[j] / theta) continue;
-        if (frac[j] > bf || (frac[j] == bf && best < 0)) {
-          best = (int64_t)j;
-          bf = frac[j];
-        }
-      }
-      if (best < 0) return MVR_E_BUDGET_TOO_LARGE;
-      ++kappa[best];
-      --remaining;
+    uint64_t remaining = kappa_total - cur;
+    for (uint64_t j = 0; j < n; ++j)
+      if (classify(freqs[j], mu, tau) == kActive && kappa[j] < freqs[j] / theta && !std::isnan(frac[j]))
+        order.push_back((uint32_t)j);
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return frac[a] > frac[b]; });
+    for (uint32_t j : order) {
+      if (remaining == 0) break;
+      const uint64_t room = freqs[j] / theta - kappa[j];
+      const uint64_t take = room < remaining ? room : remaining;
+      kappa[j] += (uint32_t)take;
+      remaining -= take;
     }
-    return MVR_OK;
+    return remaining == 0 ? MVR_OK : MVR_E_BUDGET_TOO_LARGE;
   }
-  uint32_t excess = (uint32_t)(cur - kappa_total);
-  while (excess > 0) {
-    int64_t best = -1;
-    float bf = INFINITY;
-    for (uint64_t j = 0; j < n; ++j) {
-      if (classify(freqs[j], mu, tau) != kActive || kappa[j] <= eps) continue;
-      if (frac[j] < bf) {
-        best = (int64_t)j;
-        bf = frac[j];
-      }
-    }
-    if (best >= 0) {
-      --kappa[best];
-      --excess;
-      continue;
-    }
-    int64_t found = -1;
-    for (uint64_t j = 0; j < n && found < 0; ++j)
-      if (classify(freqs[j], mu, tau) == kSmall && kappa[j] == 2) found = (int64_t)j;
-    if (found >= 0) {
-      kappa[found] = 1;
-      --excess;
-      continue;
-    }
-    for (uint64_t j = 0; j < n && found < 0; ++j)
-      if (classify(freqs[j], mu, tau) == kMicro && kappa[j] == 1) found = (int64_t)j;
-    if (found >= 0) {
-      kappa[found] = 0;
-      --excess;
-      continue;
-    }
-    return MVR_E_BUDGET_TOO_SMALL;
+  uint64_t excess = cur - kappa_total;
+  for (uint64_t j = 0; j < n; ++j)
+    if (classify(freqs[j], mu, tau) == kActive && kappa[j] > eps && frac[j] < INFINITY)
+      order.push_back((uint32_t)j);
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return frac[a] < frac[b]; });
+  for (uint32_t j : order) {
+    if (excess == 0) break;
+    const uint64_t room = kappa[j] - eps;
+    const uint64_t take = room < excess ? room : excess;
+    kappa[j] -= (uint32_t)take;
+    excess -= take;
   }
-  return MVR_OK;
+  // then small tokens 2 -> 1, then micro tokens 1 -> 0, in index order
+  for (uint64_t j = 0; j < n && excess > 0; ++j)
+    if (classify(freqs[j], mu, tau) == kSmall && kappa[j] == 2) {
+      kappa[j] = 1;
+      --excess;
+    }
+  for (uint64_t j = 0; j < n && excess > 0; ++j)
+    if (classify(freqs[j], mu, tau) == kMicro && kappa[j] == 1) {
+      kappa[j] = 0;
+      --excess;
+    }
+  return excess == 0 ? MVR_OK : MVR_E_BUDGET_TOO_SMALL;
 }
 
 }  // namespace mvr

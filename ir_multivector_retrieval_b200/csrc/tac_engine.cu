@@ -10,8 +10,10 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/mvr.h"
@@ -23,103 +25,182 @@
 namespace mvr {
 namespace {
 
-// Welford spread of one token per warp (tac.zig:609-644): f32 count,
+// Welford spread of one token per CTA (tac.zig:609-644): f32 count,
 // inv = 1/count, per coordinate delta = x - mean; mean += delta*inv;
 // m2 += delta*(x - mean); trace = sum of m2 in coordinate order;
-// spread = trace / n. Coordinate c lives in lane c % 32, slot c / 32 (Q
-// slots, d <= 32 Q). A token's rows are contiguous in G; they stream through
-// a per-warp ring of kSpStages shared-memory stages filled by cp.async, so
-// the dependent Welford chain, not load latency, sets the pace. The f32
-// count after q rows is min(q, 2^24) exactly (x + 1 rounds back to 2^24
-// there), so 32 lanes form 32 rows' 1/count at once.
-constexpr int kSpWarps = 4;
-constexpr int kSpStages = 3;
-constexpr int kSpStageFloats = 2048;
+// spread = trace / n. Thread c owns coordinate c (blockDim = d rounded up to
+// a warp); its Welford chain (sub -> mul -> add per row) is the critical
+// path. A token's rows are contiguous in G and stream through a ring of
+// kSpStages shared-memory stages: for d % 4 == 0 one thread issues a bulk
+// async copy (TMA) per stage that completes on the stage's mbarrier, so a
+// single CTA keeps several stages in flight; other d use 4-byte cp.async.
+// The f32 count after q rows is min(q, 2^24) exactly (x + 1 rounds back to
+// 2^24 there), so the threads form a whole stage's 1/count values at once.
+// Every mbarrier wait is bounded; on expiry the kernel raises *err and
+// leaves the token.
+constexpr int kSpStages = 6;
+constexpr int kSpStageFloats = 4096;
+constexpr int kSpMaxRows = 1024;  // rows per stage at most
+constexpr uint32_t kSpWaitLimit = 1u << 22;
 
-template <int Q>
-__global__ void __launch_bounds__(kSpWarps * 32)
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t it = 0; it < kSpWaitLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(256)
 tac_spread_kernel(const float* __restrict__ G, uint32_t d, const uint32_t* __restrict__ goff, uint64_t nd,
-                  float* __restrict__ spreads) {
-  extern __shared__ __align__(16) float sp_stage[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* ring = sp_stage + (size_t)warp * kSpStages * kSpStageFloats;
-  const uint32_t rb = kSpStageFloats / d;  // rows per stage (>= 8)
+                  float* __restrict__ spreads, int* __restrict__ err) {
+  extern __shared__ __align__(128) float sp_ring[];
+  __shared__ float sm2[256];
+  __shared__ __align__(8) uint64_t bars[kSpStages];
+  __shared__ float inv_s[kSpMaxRows];
+  const uint32_t tid = threadIdx.x, T = blockDim.x;
+  const uint32_t rb = min(kSpStageFloats / d, (uint32_t)kSpMaxRows);  // rows per stage (>= 16)
   const uint32_t sf = rb * d;
-  const bool vec = (d & 3) == 0;
-  for (uint64_t j = (uint64_t)blockIdx.x * kSpWarps + warp; j < nd; j += (uint64_t)gridDim.x * kSpWarps) {
+  const bool tma = (d & 3) == 0;
+  const bool own = tid < d;
+  if (tid == 0) {
+    for (int q = 0; q < kSpStages; ++q)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(&bars[q])));
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t issued = 0;  // stages issued by this CTA, across tokens
+  for (uint64_t j = blockIdx.x; j < nd; j += gridDim.x) {
     const uint32_t start = goff[j], n = goff[j + 1] - start;
     if (n == 0) {
-      if (lane == 0) spreads[j] = 0.f;
+      if (tid == 0) spreads[j] = 0.f;
       continue;
     }
     const float* src = G + (uint64_t)start * d;
     const uint32_t nst = (n + rb - 1) / rb;
-    auto issue = [&](uint32_t stg) {
+    const uint32_t first = issued;  // global stage number of this token's stage 0
+    auto issue = [&](uint32_t stg) {  // stg: token-local stage
+      const uint32_t slot = (first + stg) % kSpStages;
+      float* d0 = sp_ring + slot * kSpStageFloats;
       if (stg < nst) {
         const uint32_t nf = min(rb, n - stg * rb) * d;
         const float* s0 = src + (uint64_t)stg * sf;
-        float* d0 = ring + (stg % kSpStages) * kSpStageFloats;
-        if (vec) {
-          for (uint32_t e = lane * 4; e < nf; e += 128) cp_async<16>(d0 + e, s0 + e);
+        if (tma) {
+          if (tid == 0) {
+            const uint32_t bytes = nf * 4u;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(&bars[slot])),
+                         "r"(bytes)
+                         : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                    smem_u32(d0)),
+                "l"(s0), "r"(bytes), "r"(smem_u32(&bars[slot]))
+                : "memory");
+          }
         } else {
-          for (uint32_t e = lane; e < nf; e += 32) cp_async<4>(d0 + e, s0 + e);
+          for (uint32_t e = tid; e < nf; e += T) cp_async<4>(d0 + e, s0 + e);
         }
       }
-      cp_async_commit();
+      if (!tma) cp_async_commit();
     };
-    __syncwarp();  // the previous token's reads of the ring are done
-#pragma unroll
-    for (int q = 0; q < kSpStages - 1; ++q) issue(q);
-    float mean[Q], m2[Q];
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-      mean[q] = 0.f;
-      m2[q] = 0.f;
-    }
+    __syncthreads();  // the previous token's reads of the ring and sm2 are done
+    const uint32_t pre = min(nst, (uint32_t)kSpStages - 1);
+    for (uint32_t q = 0; q < kSpStages - 1; ++q) issue(q);
+    issued = first + pre;
+    float mean = 0.f, m2 = 0.f;
+    bool bad = false;
     for (uint32_t stg = 0; stg < nst; ++stg) {
-      cp_async_wait<kSpStages - 2>();
-      __syncwarp();
-      issue(stg + kSpStages - 1);
-      const float* x = ring + (stg % kSpStages) * kSpStageFloats;
+      const uint32_t g = first + stg, slot = g % kSpStages;
+      if (tma) {
+        if (!mbar_wait_bounded(&bars[slot], (g / kSpStages) & 1u)) bad = true;
+      } else {
+        cp_async_wait<kSpStages - 2>();
+      }
+      if (__syncthreads_or(bad)) {
+        bad = true;
+        break;
+      }
+      if (stg + kSpStages - 1 < nst) {
+        issue(stg + kSpStages - 1);
+        ++issued;
+      } else if (!tma) {
+        cp_async_commit();
+      }
+      const float* x = sp_ring + slot * kSpStageFloats + (own ? tid : 0);
       const uint32_t rows = min(rb, n - stg * rb);
       const uint32_t row0 = stg * rb;
-      float invl = 0.f;
-      for (uint32_t r = 0; r < rows; ++r) {
-        if ((r & 31) == 0) {
-          const uint32_t q = row0 + r + lane + 1;
-          invl = __fdiv_rn(1.0f, __uint2float_rn(min(q, 16777216u)));
-        }
-        const float inv = __shfl_sync(0xffffffffu, invl, r & 31);
-        const float* xr = x + r * d;
-#pragma unroll
-        for (int q = 0; q < Q; ++q) {
-          const uint32_t c = lane + 32 * q;
-          if (c < d) {
-            const float xv = xr[c];
-            const float delta = __fsub_rn(xv, mean[q]);
-            mean[q] = __fadd_rn(mean[q], __fmul_rn(delta, inv));
-            m2[q] = __fadd_rn(m2[q], __fmul_rn(delta, __fsub_rn(xv, mean[q])));
-          }
-        }
+      // 1/count of this stage's rows, once, by all threads
+      for (uint32_t r = tid; r < rows; r += T)
+        inv_s[r] = __fdiv_rn(1.0f, __uint2float_rn(min(row0 + r + 1, 16777216u)));
+      __syncthreads();
+      // groups of 8 rows, the next group's loads issued before this group's
+      // chain (two register sets, alternating)
+      const uint32_t ng = rows / 8;
+      float xa[8], ia[8], xb[8], ib[8];
+#define MVR_LOAD8(G8, XV, IV)                      \
+  _Pragma("unroll") for (int u = 0; u < 8; ++u) { \
+    XV[u] = x[((G8) * 8 + u) * d];                 \
+    IV[u] = inv_s[(G8) * 8 + u];                   \
+  }
+#define MVR_CHAIN8(XV, IV)                                          \
+  _Pragma("unroll") for (int u = 0; u < 8; ++u) {                  \
+    const float e = __fsub_rn(XV[u], mean);                         \
+    mean = __fadd_rn(mean, __fmul_rn(e, IV[u]));                    \
+    m2 = __fadd_rn(m2, __fmul_rn(e, __fsub_rn(XV[u], mean)));       \
+  }
+      if (ng > 0) { MVR_LOAD8(0u, xa, ia) }
+      uint32_t g8 = 0;
+      for (; g8 + 2 <= ng; g8 += 2) {
+        MVR_LOAD8(g8 + 1, xb, ib)
+        MVR_CHAIN8(xa, ia)
+        if (g8 + 2 < ng) { MVR_LOAD8(g8 + 2, xa, ia) }
+        MVR_CHAIN8(xb, ib)
+      }
+      if (g8 < ng) { MVR_CHAIN8(xa, ia) }
+#undef MVR_LOAD8
+#undef MVR_CHAIN8
+      for (uint32_t r = ng * 8; r < rows; ++r) {
+        const float xv = x[r * d];
+        const float e = __fsub_rn(xv, mean);
+        mean = __fadd_rn(mean, __fmul_rn(e, inv_s[r]));
+        m2 = __fadd_rn(m2, __fmul_rn(e, __fsub_rn(xv, mean)));
       }
     }
-    cp_async_wait<0>();
-    float trace = 0.f;
-#pragma unroll
-    for (int q = 0; q < Q; ++q)
-      for (uint32_t l = 0; l < 32 && 32 * q + l < d; ++l)
-        trace = __fadd_rn(trace, __shfl_sync(0xffffffffu, m2[q], l));
-    if (lane == 0) spreads[j] = __fdiv_rn(trace, __uint2float_rn(n));
+    if (!tma) cp_async_wait<0>();
+    if (bad) {
+      // drain: wait (bounded) for every stage still in flight, then leave
+      if (tma)
+        for (uint32_t g = first; g < issued; ++g) (void)mbar_wait_bounded(&bars[g % kSpStages], (g / kSpStages) & 1u);
+      if (tid == 0) atomicExch(err, 1);
+      break;
+    }
+    if (own) sm2[tid] = m2;
+    __syncthreads();
+    if (tid == 0) {
+      float trace = 0.f;
+      for (uint32_t c = 0; c < d; ++c) trace = __fadd_rn(trace, sm2[c]);
+      spreads[j] = __fdiv_rn(trace, __uint2float_rn(n));
+    }
   }
 }
 
-int launch_spreads(Ctx* c, const float* d_G, uint32_t d, const uint32_t* d_goff, uint64_t nd, float* d_sp) {
-  const size_t smem = (size_t)kSpWarps * kSpStages * kSpStageFloats * sizeof(float);
-  const unsigned grid = (unsigned)std::min<uint64_t>((nd + kSpWarps - 1) / kSpWarps, 1u << 20);
-  auto k = d <= 32 ? tac_spread_kernel<1> : d <= 64 ? tac_spread_kernel<2> : d <= 128 ? tac_spread_kernel<4>
-                                                                                     : tac_spread_kernel<8>;
-  MVR_CUDA(c, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k<<<grid, kSpWarps * 32, smem, c->stream>>>(d_G, d, d_goff, nd, d_sp);
+int launch_spreads(Ctx* c, const float* d_G, uint32_t d, const uint32_t* d_goff, uint64_t nd, float* d_sp,
+                   int* d_err) {
+  const size_t smem = (size_t)kSpStages * kSpStageFloats * sizeof(float);
+  const unsigned threads = (d + 31) / 32 * 32;
+  const unsigned grid = (unsigned)std::min<uint64_t>(nd, 1u << 30);
+  MVR_CUDA(c, cudaFuncSetAttribute(tac_spread_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tac_spread_kernel<<<grid, threads, smem, c->stream>>>(d_G, d, d_goff, nd, d_sp, d_err);
   MVR_CUDA(c, cudaGetLastError());
   return MVR_OK;
 }
@@ -182,6 +263,11 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   if (dim > 256) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "dim > 256 is not supported on the GPU path");
   if (n_tokens >= (1ull << 32)) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 tokens");
 
+  using clk = std::chrono::steady_clock;
+  const auto t_start = clk::now();
+  double host_ms = 0.0;
+  auto since = [](clk::time_point a) { return std::chrono::duration<double, std::milli>(clk::now() - a).count(); };
+  c->tac_stats = mvr_tac_stats{};
   // ---- step 0-1: vocabulary, frequencies, CSR grouping (host) -------------
   uint32_t max_id = 0;
   for (uint64_t i = 0; i < n_tokens; ++i) max_id = std::max(max_id, token_ids[i]);
@@ -189,17 +275,19 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   if (n_distinct_out) *n_distinct_out = nd;
   if (kappa_cap < nd) return mvr::fail(c, MVR_E_OUT_BUFFER_WRONG_SIZE, "kappa_per_token buffer too small");
   std::vector<uint32_t> freqs(nd, 0), goff(nd + 1, 0), gidx(n_tokens), rowtok(n_tokens);
-  for (uint64_t i = 0; i < n_tokens; ++i) ++freqs[token_ids[i]];
-  for (uint64_t j = 0; j < nd; ++j) goff[j + 1] = goff[j] + freqs[j];
-  {
+  auto group_rows = [&] {
+    for (uint64_t i = 0; i < n_tokens; ++i) ++freqs[token_ids[i]];
+    for (uint64_t j = 0; j < nd; ++j) goff[j + 1] = goff[j] + freqs[j];
     std::vector<uint32_t> cur(goff.begin(), goff.end() - 1);
     for (uint64_t i = 0; i < n_tokens; ++i) gidx[cur[token_ids[i]]++] = (uint32_t)i;
-  }
-  for (uint64_t j = 0; j < nd; ++j)
-    for (uint32_t q = goff[j]; q < goff[j + 1]; ++q) rowtok[q] = (uint32_t)j;
-
+    for (uint64_t j = 0; j < nd; ++j)
+      for (uint32_t q = goff[j]; q < goff[j + 1]; ++q) rowtok[q] = (uint32_t)j;
+  };
+  host_ms += since(t_start);
   MVR_TRY(mvr::set_device(c));
   cudaStream_t st = c->stream;
+  cudaEvent_t* tev = nullptr;
+  MVR_TRY(mvr::tac_events(c, &tev));
   float *d_V = nullptr, *d_G = nullptr, *d_sp = nullptr, *d_C = nullptr;
   uint32_t *d_gidx = nullptr, *d_goff = nullptr, *d_local = nullptr, *d_rowtok = nullptr, *d_goffc = nullptr,
            *d_asg = nullptr;
@@ -216,17 +304,34 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   d_goff = d_asg + rows;
   d_goffc = d_goff + (nd + 1);
   d_sp = reinterpret_cast<float*>(d_goffc + (nd + 1));
-  MVR_CUDA(c, cudaMemcpyAsync(d_V, vectors, rows * dim * sizeof(float), cudaMemcpyHostToDevice, st));
+  // the grouping runs on a second host thread while the rows stream in
+  MVR_CUDA(c, cudaEventRecord(tev[0], st));
+  {
+    std::thread grouper(group_rows);
+    const int s_v = mvr::h2d_staged(c, d_V, vectors, rows * dim * sizeof(float));
+    grouper.join();
+    MVR_TRY(s_v);
+  }
   MVR_CUDA(c, cudaMemcpyAsync(d_gidx, gidx.data(), rows * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_goff, goff.data(), (nd + 1) * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_rowtok, rowtok.data(), rows * 4, cudaMemcpyHostToDevice, st));
+  MVR_CUDA(c, cudaEventRecord(tev[1], st));
   MVR_TRY(mvr::km_gather_groups(c, d_V, d_gidx, rows, dim, d_G, d_GT));
-  MVR_TRY(mvr::launch_spreads(c, d_G, dim, d_goff, nd, d_sp));
-  std::vector<float> spreads(nd);
-  MVR_CUDA(c, cudaMemcpyAsync(spreads.data(), d_sp, nd * 4, cudaMemcpyDeviceToHost, st));
+  int* d_err = reinterpret_cast<int*>(d_sp + nd);
+  MVR_CUDA(c, cudaMemsetAsync(d_err, 0, sizeof(int), st));
+  MVR_TRY(mvr::launch_spreads(c, d_G, dim, d_goff, nd, d_sp, d_err));
+  MVR_CUDA(c, cudaEventRecord(tev[2], st));
+  std::vector<float> spreads(nd + 1);  // spreads, then the kernel's error flag
+  MVR_CUDA(c, cudaMemcpyAsync(spreads.data(), d_sp, (nd + 1) * 4, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(c, cudaStreamSynchronize(st));
+  {
+    int spread_err = 0;
+    std::memcpy(&spread_err, &spreads[nd], sizeof(int));
+    if (spread_err) return mvr::fail(c, MVR_E_TIMEOUT, "spread kernel: a bulk copy did not complete in time");
+  }
 
   // ---- step 3: budget phases 1-4 (host) ------------------------------------
+  const auto t_budget = clk::now();
   std::vector<float> frac(nd);
   std::vector<uint32_t> kap(nd);
   {
@@ -253,6 +358,7 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
     b.seed.push_back(p->seed ^ (uint64_t)j);
     pj.push_back((uint32_t)j);
   }
+  host_ms += since(t_budget);
   MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, (size_t)p->kappa_total * dim * sizeof(float), (void**)&d_C));
   mvr::KmResult r;
   MVR_TRY(mvr::km_batch_run(c, d_G, d_GT, rows, dim, b, p->max_iters, p->tol, d_C, d_local, &r));
@@ -268,10 +374,13 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
     mvr::tac_scatter_assign_kernel<<<grid, 256, 0, st>>>(d_gidx, d_rowtok, d_goffc, d_local, rows, d_asg);
     MVR_CUDA(c, cudaGetLastError());
   }
+  MVR_CUDA(c, cudaEventRecord(tev[3], st));
   MVR_CUDA(c, cudaMemcpyAsync(assignments_out, d_asg, rows * 4, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(c, cudaMemcpyAsync(centroids_out, d_C, (size_t)p->kappa_total * dim * sizeof(float),
                               cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(c, cudaEventRecord(tev[4], st));
   MVR_CUDA(c, cudaStreamSynchronize(st));
+  const auto t_tail = clk::now();
 
   // wcss_total: per-token WCSS summed in token order, per static thread chunk
   // when n_threads > 1 (tac.zig:685-825).
@@ -293,6 +402,24 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
     }
   }
   if (wcss_total_out) *wcss_total_out = total;
+  {
+    mvr_tac_stats& ts = c->tac_stats;
+    float h2d = 0.f, spr = 0.f, d2h = 0.f;
+    cudaEventElapsedTime(&h2d, tev[0], tev[1]);
+    cudaEventElapsedTime(&spr, tev[1], tev[2]);
+    cudaEventElapsedTime(&d2h, tev[3], tev[4]);
+    ts.h2d_ms = h2d;
+    ts.spread_ms = spr;
+    ts.d2h_ms = d2h;
+    ts.seed_ms = r.seed_ms;
+    ts.lloyd_ms = r.lloyd_ms;
+    ts.problems = (uint32_t)pj.size();
+    ts.iters_max = r.iters.empty() ? 0u : *std::max_element(r.iters.begin(), r.iters.end());
+    ts.seed_fallbacks = r.seed_fallbacks;
+    ts.launches = r.launches + 4;
+    ts.host_ms = host_ms + since(t_tail);
+    ts.total_ms = since(t_start);
+  }
   for (uint64_t i = 0; i < n_tokens; ++i)  // final invariant (tac.zig:827-830)
     if (assignments_out[i] >= p->kappa_total) return mvr::fail(c, MVR_E_INVALID_THRESHOLDS, "assignment out of range");
   return MVR_OK;

@@ -60,6 +60,14 @@ def allocate_budgets(freqs, spreads, kappa_total: int, p: ClusteringParams) -> n
     return k
 
 
+def last_stats(ctx=None) -> dict:
+    """Timing report of the context's most recent ``cluster_flat`` call."""
+    ctx = ctx or _lib.default_context()
+    st = _lib.TacStats()
+    ctx.check(ctx.lib.mvr_tac_last_stats(ctx.handle, C.byref(st)))
+    return st.as_dict()
+
+
 def cluster_flat(token_ids, vectors, dim: int, p: ClusteringParams, ctx=None) -> ClusteringResult:
     ids = np.ascontiguousarray(token_ids, dtype=np.uint32).reshape(-1)
     v = np.ascontiguousarray(vectors, dtype=np.float32).reshape(-1)

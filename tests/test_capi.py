@@ -84,6 +84,35 @@ def test_allocate_budgets_matches_oracle_on_random_vocab(lib, orc):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("seed", range(12))
+def test_allocate_budgets_reconcile_paths_match_oracle(lib, orc, seed):
+    """Surplus, deficit, degraded-tail and failing budgets: the host phase 4
+    (one pass in remainder order) against the oracle's one-unit rounds."""
+    from ir_multivector_retrieval_b200 import tac
+
+    rng = np.random.default_rng(100 + seed)
+    n = int(rng.integers(5, 400))
+    freqs = (np.minimum(rng.zipf(1.2, size=n), 400) * int(rng.integers(1, 40))).astype(np.uint32)
+    freqs[rng.random(n) < 0.1] = 0
+    spreads = rng.random(n).astype(np.float32)
+    spreads[rng.random(n) < 0.2] = 0.0
+    spreads[rng.random(n) < 0.1] = spreads[0]  # equal remainders
+    mu, tau, eps, theta = [(128, 256, 4, 39), (3, 40, 2, 10), (8, 64, 1, 4)][seed % 3]
+    tail = int(((freqs > 0) & (freqs < mu)).sum() + 2 * ((freqs >= mu) & (freqs < tau)).sum())
+    cap = int(sum(f // theta for f in freqs if f >= tau))
+    for kt in {max(1, tail // 2), max(1, tail - 3), tail + 1, tail + cap // 3, tail + cap, tail + cap + 7}:
+        p = tac.ClusteringParams(kappa_total=kt, seed=0, mu=mu, tau=tau, epsilon=eps, theta=theta)
+        try:
+            want = orc.tac_allocate_budgets(freqs, spreads, kt, mu, tau, eps, theta)
+        except Exception as e:
+            with pytest.raises(Exception) as g:
+                tac.allocate_budgets(freqs, spreads, kt, p)
+            assert g.value.code == e.code
+            continue
+        got = tac.allocate_budgets(freqs, spreads, kt, p)
+        assert np.array_equal(got, want), (kt, mu, tau, eps, theta)
+
+
 def test_no_gpu_fails_loudly_or_creates_context(lib):
     h = C.c_void_p()
     st = lib.mvr_ctx_create(0, C.byref(h))
