@@ -202,6 +202,37 @@ int mvr_pq_encode_device(mvr_ctx* ctx, const float* d_codebooks, uint32_t dim,
                          uint32_t pq_m, const float* d_residuals, uint64_t n,
                          uint8_t* d_codes_out);
 
+/* ---- several GPUs (one process per GPU) ------------------------------- */
+
+/* No counterpart in the reference (its pq.train runs on one host). An NCCL
+ * unique id (`mvr_comm_unique_id_bytes()` bytes) made by one process and
+ * handed to every rank by the caller (e.g. over torch.distributed), then
+ * `mvr_ctx_init_comm` on every rank joins its context to the communicator.
+ * NCCL is loaded at run time; MVR_E_NCCL when it is missing. */
+size_t mvr_comm_unique_id_bytes(void);
+int mvr_comm_unique_id(void* id_out, size_t id_bytes);
+int mvr_ctx_init_comm(mvr_ctx* ctx, int nranks, int rank, const void* id,
+                      size_t id_bytes);
+int mvr_ctx_comm_size(const mvr_ctx* ctx);
+int mvr_ctx_comm_rank(const mvr_ctx* ctx);
+
+/* Row-sharded `pq.train` (src/index/pq.zig:158-291) over the context's
+ * communicator: this rank holds rows [row0, row0 + n_local) of an n_total x
+ * dim matrix in device memory; the shards are non-empty and contiguous in
+ * rank order. Collective: every rank calls it with the same dim, seed,
+ * pq_m, max_iters and tol. Every rank receives the codebooks that
+ * `mvr_pq_train` computes on the whole matrix (identical bytes for any
+ * number of ranks); `d_assign_out` (optional, pq_m*n_local u32, [m][row])
+ * receives this rank's final assignments. Without a communicator the shard
+ * must be the whole matrix. Returns when the result is ready. */
+int mvr_pq_train_sharded_device(mvr_ctx* ctx, const float* d_rows,
+                                uint64_t n_local, uint64_t row0,
+                                uint64_t n_total, uint32_t dim, uint64_t seed,
+                                uint32_t n_threads, uint32_t pq_m,
+                                uint32_t max_iters, float tol,
+                                float* d_codebooks_out, uint32_t* d_assign_out,
+                                mvr_pq_train_stats* stats);
+
 /* Timing report of the most recent `mvr_tac_cluster_flat` call on the
  * context (no reference counterpart; the reference prints `[stage]` lines,
  * src/tac/tac.zig:660-680). Device times come from CUDA events on the
@@ -223,6 +254,12 @@ typedef struct mvr_tac_stats {
 /* Copies the report of the context's most recent `mvr_tac_cluster_flat`
  * call (all zero before the first call). */
 int mvr_tac_last_stats(const mvr_ctx* ctx, mvr_tac_stats* out);
+
+/* Verification mode (no reference counterpart): with `on` != 0 every
+ * k-means++ draw of the context is resolved by the reference's serial f64
+ * chain (rng.zig:57-82) instead of the interval-bounded parallel search.
+ * Results are identical either way; only the speed differs. */
+int mvr_ctx_set_serial_draws(mvr_ctx* ctx, int on);
 
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);

@@ -118,6 +118,17 @@ SIGNATURES = {
     "mvr_ctx_trim": (C.c_int, [_P]),
     "mvr_ctx_sync": (C.c_int, [_P]),
     "mvr_tac_last_stats": (C.c_int, [_P, C.POINTER(TacStats)]),
+    "mvr_ctx_set_serial_draws": (C.c_int, [_P, C.c_int]),
+    "mvr_comm_unique_id_bytes": (C.c_size_t, []),
+    "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),
+    "mvr_ctx_init_comm": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_size_t]),
+    "mvr_ctx_comm_size": (C.c_int, [_P]),
+    "mvr_ctx_comm_rank": (C.c_int, [_P]),
+    "mvr_pq_train_sharded_device": (
+        C.c_int,
+        [_P, _P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+         C.c_float, _P, _P, C.POINTER(PqTrainStats)],
+    ),
     "mvr_kmeans_fit": (
         C.c_int,
         [_P, _P, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,

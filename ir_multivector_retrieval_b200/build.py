@@ -27,6 +27,23 @@ LIB = PKG / "libmvr_b200.so"
 INCLUDE = PKG.parent / "include"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nccl_include() -> str:
+    """Header directory of the NCCL that PyTorch ships (the library itself is
+    loaded at run time), else the system one."""
+    try:
+        import nvidia.nccl as nn  # noqa: PLC0415
+
+        for p in nn.__path__:
+            inc = Path(p) / "include"
+            if (inc / "nccl.h").exists():
+                return str(inc)
+    except Exception:
+        pass
+    return "/usr/include"
+
+
 NVCC_FLAGS = [
     "-O3",
     "-lineinfo",
@@ -36,6 +53,7 @@ NVCC_FLAGS = [
     "-Xcompiler",
     "-fPIC,-ffp-contract=off,-O2",
     f"-I{INCLUDE}",
+    f"-I{nccl_include()}",
 ]
 
 
@@ -77,7 +95,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

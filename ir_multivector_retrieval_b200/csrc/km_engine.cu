@@ -276,7 +276,7 @@ km_seed_select_kernel(const float* __restrict__ G, int d, Prob P, int step,
                       const uint32_t* __restrict__ ccount, const uint64_t* __restrict__ ch_r0,
                       const uint32_t* __restrict__ ch_len, const double2* __restrict__ ch_sum,
                       const uint32_t* __restrict__ ch_cnt, const float* __restrict__ md,
-                      const double* __restrict__ draws, float* __restrict__ C) {
+                      const double* __restrict__ draws, float* __restrict__ C, int force_chain) {
   const uint32_t p = sel_p[blockIdx.x];
   if (P.state[p] != kRunning) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -400,7 +400,7 @@ km_seed_select_kernel(const float* __restrict__ G, int d, Prob P, int step,
       const double UHi = __dmul_ru(r, __dadd_ru(Hi_N, BN));
       bool ok = UHi < __dsub_rd(elo, bound_at(i + 1, ehi));
       if (i > 0) ok = ok && (ULo >= __dadd_ru(prv.y, bound_at(i, prv.y)));
-      if (ok) {
+      if (ok && !force_chain) {
         sh_idx = i;
         sh_decided = 1;
       }
@@ -1021,7 +1021,7 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
     km_seed_select_kernel<<<na, kSelT, 0, st>>>(
         d_G, d, P, (int)s, at<uint32_t>(ws, o_seeders), at<uint32_t>(ws, o_cfirst), at<uint32_t>(ws, o_ccount),
         at<uint64_t>(ws, o_chr0), at<uint32_t>(ws, o_chlen), at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt),
-        at<float>(ws, o_md), at<double>(ws, o_draws), d_C);
+        at<float>(ws, o_md), at<double>(ws, o_draws), d_C, ctx->serial_draws ? 1 : 0);
     MVR_CUDA(ctx, cudaGetLastError());
     launches += 2;
   }

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/mvr.h"
+#include "comm.h"
 #include "mvr_internal.h"
 #include "pq_engine.h"
 #include "tac_engine.h"
@@ -206,6 +207,7 @@ int mvr_ctx_destroy(mvr_ctx* h) {
     cudaStreamSynchronize(c->side);
     cudaStreamDestroy(c->side);
   }
+  mvr::destroy_comm(c);
   mvr::destroy_host_io(c);
   for (auto& e : c->tev)
     if (e) cudaEventDestroy(e);
@@ -213,6 +215,12 @@ int mvr_ctx_destroy(mvr_ctx* h) {
   if (c->join_ev) cudaEventDestroy(c->join_ev);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete h;
+  return MVR_OK;
+}
+
+int mvr_ctx_set_serial_draws(mvr_ctx* h, int on) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.serial_draws = on != 0;
   return MVR_OK;
 }
 
@@ -276,6 +284,39 @@ int mvr_pq_train_device(mvr_ctx* h, const float* d_res, uint64_t len, uint32_t d
   out.d_codebooks = d_cb;
   out.stats = stats;
   return mvr::pq_kmeans_device(c, job, out);
+}
+
+int mvr_pq_train_sharded_device(mvr_ctx* h, const float* d_rows, uint64_t n_local, uint64_t row0,
+                                uint64_t n_total, uint32_t dim, uint64_t seed, uint32_t n_threads, uint32_t pq_m,
+                                uint32_t max_iters, float tol, float* d_cb, uint32_t* d_assign_out,
+                                mvr_pq_train_stats* stats) {
+  (void)n_threads;
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  // pq.train's validation on the global shape (pq.zig:165-168)
+  MVR_TRY(mvr::pq_validate(c, n_total * (uint64_t)dim, dim, pq_m));
+  MVR_TRY(mvr::set_device(c));
+  mvr::PqJob job;
+  job.R = d_rows;
+  job.N = n_local;
+  job.D = (int)dim;
+  job.M = (int)pq_m;
+  job.S = (int)(dim / pq_m);
+  job.K = (int)MVR_PQ_CENTROIDS;
+  job.seed = seed;
+  job.max_iters = max_iters;
+  job.tol = tol;
+  mvr::PqOut out;
+  out.d_codebooks = d_cb;
+  out.d_assign = d_assign_out;
+  out.stats = stats;
+  if (!mvr::comm_active(c)) {  // one rank: the whole matrix
+    if (!d_rows || !d_cb) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+    if (row0 != 0 || n_local != n_total)
+      return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "without a communicator the shard is the whole matrix");
+    return mvr::pq_kmeans_device(c, job, out);
+  }
+  return mvr::pq_kmeans_run_dist(c, job, row0, n_total, out, d_rows && d_cb);
 }
 
 int mvr_pq_train(mvr_ctx* h, const float* res, uint64_t len, uint32_t dim, uint64_t seed,

@@ -35,6 +35,7 @@ enum ScratchSlot {
 };
 
 class HostPool;
+struct Comm;
 
 struct Ctx {
   int device = 0;
@@ -57,6 +58,10 @@ struct Ctx {
   HostPool* io_pool = nullptr;
   void* stage[2] = {nullptr, nullptr};
   cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+  // NCCL communicator for row-sharded training (comm.cpp); null = one GPU
+  Comm* comm = nullptr;
+  // resolve every k-means++ draw with the reference's serial chain
+  bool serial_draws = false;
 };
 
 // Host->device copy of a pageable host buffer through the pinned stages;

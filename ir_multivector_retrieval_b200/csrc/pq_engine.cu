@@ -35,14 +35,26 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "mvr_device.cuh"
 #include "mvr_rng.h"
 #include "pq_engine.h"
+#include "comm.h"
 
 namespace mvr {
 namespace {
+
+// Sequential 256-byte-aligned carving of a workspace.
+struct Carve {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  }
+};
 
 constexpr int kAsgThreads = 512;            // assign / encode CTA size
 constexpr int kPtsPerThread = 2;            // rows per thread per assign pass
@@ -399,7 +411,8 @@ template <int S>
 __global__ void __launch_bounds__(kChainWarps * 32)
 pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
                 const uint32_t* __restrict__ counts, const uint32_t* __restrict__ starts,
-                float* __restrict__ cb, const uint8_t* __restrict__ state) {
+                float* __restrict__ cb, const uint8_t* __restrict__ state,
+                const float* __restrict__ start_sums, int raw) {
   constexpr int CPW = 32 / S;              // clusters per warp
   constexpr int kRow = kChainE * S + S;    // padded: conflict-free reads
   constexpr int kStage = CPW * kRow;
@@ -436,7 +449,8 @@ pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
     cp_async_commit();
   };
 
-  float acc = 0.f;
+  // a row-sharded run continues the previous rank's running sums
+  float acc = (start_sums && c < K) ? start_sums[((size_t)m * K + c) * S + k] : 0.f;
   for (int t = 0; t < kChainStages - 1; ++t) issue(t);
   for (int t = 0; t < nst; ++t) {
     cp_async_wait<kChainStages - 2>();
@@ -457,7 +471,9 @@ pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
     issue(t + kChainStages - 1);
   }
   cp_async_wait<0>();
-  if (c < K && cnt > 0) {
+  if (c < K && raw) {
+    cb[((size_t)m * K + c) * S + k] = acc;  // running sums for the next rank
+  } else if (c < K && cnt > 0) {
     const float inv = __fdiv_rn(1.0f, __uint2float_rn(cnt));
     cb[((size_t)m * K + c) * S + k] = __fmul_rn(acc, inv);
   }
@@ -468,12 +484,12 @@ pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 pq_wcss_kernel(const float* __restrict__ mind, uint64_t N, float* __restrict__ wcss,
-               const uint8_t* __restrict__ state) {
+               const uint8_t* __restrict__ state, const float* __restrict__ start) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   __shared__ __align__(16) float tile[4096];
   const float* src = mind + (size_t)m * N;
-  float acc = 0.f;
+  float acc = start ? start[m] : 0.f;  // a row-sharded run continues the previous rank's sum
   for (uint64_t t0 = 0; t0 < N; t0 += 4096) {
     const uint64_t n = min((uint64_t)4096, N - t0);
     for (uint32_t e = threadIdx.x; e < n; e += 256) tile[e] = src[t0 + e];
@@ -531,14 +547,15 @@ pq_reseed_converge_kernel(const float* __restrict__ XT, uint64_t N, int S, int K
                           float* __restrict__ cb, uint8_t* __restrict__ state,
                           const float* __restrict__ wcss, float* __restrict__ prev_wcss,
                           uint32_t* __restrict__ iters_run, uint32_t* __restrict__ reseeds,
-                          int iter, int check, float tol) {
+                          int iter, int check, float tol, int do_reseed) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   __shared__ int any_empty;
   if (threadIdx.x == 0) any_empty = 0;
   __syncthreads();
-  for (int c = threadIdx.x; c < K; c += blockDim.x)
-    if (counts[(size_t)m * K + c] == 0) atomicOr(&any_empty, 1);
+  if (do_reseed)
+    for (int c = threadIdx.x; c < K; c += blockDim.x)
+      if (counts[(size_t)m * K + c] == 0) atomicOr(&any_empty, 1);
   __syncthreads();
   if (any_empty) {
     float* mm = mind + (size_t)m * N;
@@ -592,11 +609,11 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
                       const float* __restrict__ cb, float* __restrict__ md,
                       double2* __restrict__ chunk, uint32_t* __restrict__ chunk_cnt,
                       int* __restrict__ nonfinite, const uint8_t* __restrict__ state,
-                      const double* __restrict__ thr) {
+                      const double* __restrict__ thr, int chunk_stride) {
   __shared__ double2 wp[kSeedThreads / 32][kMaxM];
   __shared__ uint32_t wc[kSeedThreads / 32][kMaxM];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nchunk = gridDim.x;
+  const int nchunk = chunk_stride;  // chunk b of subspace m at m * chunk_stride + b
   for (int m = 0; m < M; ++m) {
     if (state[m] != kRunning) continue;
     float c[S];
@@ -684,7 +701,7 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
                       int nchunk, const double* __restrict__ draws, int* __restrict__ nonfinite,
                       int* __restrict__ status, uint8_t* __restrict__ state,
                       uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen,
-                      double* __restrict__ thr) {
+                      double* __restrict__ thr, int force_chain) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -823,7 +840,7 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
         const double SHiP = __dadd_ru(prv.y, bound_at(istar, prv.y));
         ok = ok && (ULo >= SHiP);
       }
-      if (ok) {
+      if (ok && !force_chain) {
         sh_idx = istar;
         sh_decided = 1;
       }
@@ -928,14 +945,15 @@ int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, const flo
 
 template <int S>
 int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int M, int K,
-                 const uint32_t* counts, const uint32_t* starts, float* cb, const uint8_t* state) {
+                 const uint32_t* counts, const uint32_t* starts, float* cb, const uint8_t* state,
+                 const float* start_sums = nullptr, int raw = 0) {
   constexpr int CPW = 32 / S;
   const size_t sm = (size_t)kChainWarps * kChainStages * CPW * (kChainE * S + S) * sizeof(float);
   auto kern = pq_chain_kernel<S>;
   MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const int warps = M * ((K + CPW - 1) / CPW);
   const int grid = (warps + kChainWarps - 1) / kChainWarps;
-  kern<<<grid, kChainWarps * 32, sm, st>>>(sorted, N, M, K, counts, starts, cb, state);
+  kern<<<grid, kChainWarps * 32, sm, st>>>(sorted, N, M, K, counts, starts, cb, state, start_sums, raw);
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
 }
@@ -960,6 +978,353 @@ void grid_for(uint64_t N, int sms, int* nblk, uint64_t* rows_per_cta) {
   const uint64_t ctas = std::max<uint64_t>(1, std::min<uint64_t>(groups, (uint64_t)std::max(1, sms) * 2));
   *rows_per_cta = ((groups + ctas - 1) / ctas) * 32;
   *nblk = (int)((N + *rows_per_cta - 1) / *rows_per_cta);
+}
+
+// ---------------------------------------------------------------------------
+// Row-sharded training: rank g holds global rows [row0_g, row0_g + N_g) in
+// rank order. Every rank ends with the same codebooks as the one-GPU run:
+//   * k-means++: per-chunk bounds of every rank are gathered, all ranks run
+//     the same coarse search, the rank owning the chosen chunk resolves the
+//     row and offers it (RowContrib) to the others;
+//   * Lloyd: counts are summed; the in-order centroid sums run rank after
+//     rank, each continuing the previous rank's running sums (the reference's
+//     serial loop split at shard borders), and the last rank scales and
+//     broadcasts; WCSS is continued the same way;
+//   * the rare paths (the exact draw chain, empty-cluster reseeds) gather the
+//     whole subspace and run the one-GPU logic on every rank.
+// ---------------------------------------------------------------------------
+struct RowContrib {
+  uint32_t flag;  // 0: nothing; 1: row below; 2: the owner could not settle the draw
+  uint32_t pad;
+  uint64_t gidx;  // global row index
+  float row[4];
+};
+
+// Offer row gidx[m] of subspace m when this rank holds it (want[m] != 0).
+__global__ void pq_dist_offer_kernel(const float* __restrict__ XT, uint64_t N, int S, int M, uint64_t row0,
+                                     const uint64_t* __restrict__ gidx, const uint32_t* __restrict__ want,
+                                     RowContrib* __restrict__ contrib) {
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    RowContrib rc;
+    rc.flag = 0;
+    rc.pad = 0;
+    rc.gidx = 0;
+    for (int k = 0; k < 4; ++k) rc.row[k] = 0.f;
+    const uint64_t g = gidx[m];
+    if ((!want || want[m]) && g >= row0 && g < row0 + N) {
+      rc.flag = 1;
+      rc.gidx = g;
+      for (int k = 0; k < S; ++k) rc.row[k] = XT[((size_t)m * N + (g - row0)) * S + k];
+    }
+    contrib[m] = rc;
+  }
+}
+
+// Take the offered rows as centroid `step`; flag 2 asks the host for the
+// exact chain.
+__global__ void pq_dist_take_kernel(const RowContrib* __restrict__ all, int G, int M, int S, int K, int step,
+                                    float* __restrict__ cb, uint64_t* __restrict__ chosen,
+                                    const uint8_t* __restrict__ state, uint32_t* __restrict__ need_chain) {
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    need_chain[m] = 0;
+    if (state[m] != kRunning) continue;
+    for (int r = 0; r < G; ++r) {
+      const RowContrib& rc = all[(size_t)r * M + m];
+      if (rc.flag == 1) {
+        for (int k = 0; k < S; ++k) cb[((size_t)m * K + step) * S + k] = rc.row[k];
+        chosen[(size_t)m * K + step] = rc.gidx;
+        break;
+      }
+      if (rc.flag == 2) {
+        need_chain[m] = 1;
+        break;
+      }
+    }
+  }
+}
+
+// Byte layout of one rank's seeding exchange block.
+struct SeedBlock {
+  size_t o_cnt, o_nonf, bytes;
+};
+__host__ __device__ inline SeedBlock seed_block(int M, int ncmax) {
+  SeedBlock b;
+  b.o_cnt = (size_t)M * ncmax * sizeof(double2);
+  b.o_nonf = b.o_cnt + (size_t)M * ncmax * sizeof(uint32_t);
+  b.bytes = (b.o_nonf + (size_t)M * sizeof(int) + 255) & ~(size_t)255;
+  return b;
+}
+
+// pq_seed_select_kernel over the gathered chunk bounds of all ranks (global
+// chunk j = rank j / ncmax, local chunk j % ncmax; padding chunks are empty).
+__global__ void __launch_bounds__(kSelectThreads)
+pq_seed_select_dist_kernel(const unsigned char* __restrict__ gath, int G, int ncmax,
+                           const uint64_t* __restrict__ rank_row0, int me, uint64_t N_total,
+                           const float* __restrict__ XT, uint64_t N, int S, int M, int K, int step,
+                           const float* __restrict__ md, const double* __restrict__ draws,
+                           int* __restrict__ status, uint8_t* __restrict__ state, double* __restrict__ thr,
+                           RowContrib* __restrict__ contrib, int force_chain) {
+  const int m = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    RowContrib z;
+    z.flag = 0;
+    z.pad = 0;
+    z.gidx = 0;
+    for (int k = 0; k < 4; ++k) z.row[k] = 0.f;
+    contrib[m] = z;
+  }
+  if (state[m] != kRunning) return;
+  constexpr int kWarps = kSelectThreads / 32;
+  __shared__ double2 wsum[kWarps];
+  __shared__ unsigned long long wcnt[kWarps];
+  __shared__ double2 incl_all[kSelectThreads];
+  __shared__ double2 sh_excl;
+  __shared__ int sh_chunk;
+  __shared__ uint64_t sh_idx;
+  __shared__ int sh_decided;
+  const SeedBlock sb = seed_block(M, ncmax);
+  const size_t bpr = sb.bytes;
+
+  bool nonf = false;
+  for (int r = 0; r < G; ++r) nonf |= reinterpret_cast<const int*>(gath + (size_t)r * bpr + sb.o_nonf)[m] != 0;
+  if (nonf) {
+    if (tid == 0) { status[m] = MVR_E_NON_FINITE; state[m] = kFailed; }
+    return;
+  }
+  auto CH = [&](int j) -> double2 {
+    const int r = j / ncmax, lc = j - r * ncmax;
+    return reinterpret_cast<const double2*>(gath + (size_t)r * bpr)[(size_t)m * ncmax + lc];
+  };
+  auto CC = [&](int j) -> uint32_t {
+    const int r = j / ncmax, lc = j - r * ncmax;
+    return reinterpret_cast<const uint32_t*>(gath + (size_t)r * bpr + sb.o_cnt)[(size_t)m * ncmax + lc];
+  };
+  const int nchunk = G * ncmax;
+  const float* w = md + (size_t)m * N;
+  const double r = draws[(size_t)m * K + step];
+
+  const int cpt = (nchunk + kSelectThreads - 1) / kSelectThreads;
+  const int c_lo = min(nchunk, tid * cpt), c_hi = min(nchunk, c_lo + cpt);
+  double tlo = 0.0, thi = 0.0;
+  unsigned tcnt = 0;
+  for (int j = c_lo; j < c_hi; ++j) {
+    const double2 v = CH(j);
+    tlo = __dadd_rd(tlo, v.x);
+    thi = __dadd_ru(thi, v.y);
+    tcnt += CC(j);
+  }
+  const double ilo = warp_scan_rd(tlo, lane), ihi = warp_scan_ru(thi, lane);
+  const unsigned wc = __reduce_add_sync(0xffffffffu, tcnt);
+  if (lane == 31) wsum[warp] = make_double2(ilo, ihi);
+  if (lane == 0) wcnt[warp] = wc;
+  __syncthreads();
+  if (warp == 0) {
+    const double a = warp_scan_rd(wsum[lane].x, lane);
+    const double b = warp_scan_ru(wsum[lane].y, lane);
+    unsigned long long cs = wcnt[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+    __syncwarp();
+    wsum[lane] = make_double2(a, b);
+    wcnt[lane] = cs;
+  }
+  __syncthreads();
+  const double wlo = warp > 0 ? wsum[warp - 1].x : 0.0, whi = warp > 0 ? wsum[warp - 1].y : 0.0;
+  const double incl_lo = __dadd_rd(wlo, ilo), incl_hi = __dadd_ru(whi, ihi);
+  const double Lo_N = wsum[kWarps - 1].x, Hi_N = wsum[kWarps - 1].y;
+  const unsigned long long C_N = wcnt[0];
+  if (Hi_N <= 0.0) {
+    if (tid == 0) { status[m] = MVR_E_ALL_ZERO; state[m] = kFailed; }
+    return;
+  }
+  const double gN = gamma_bound(N_total);
+  const double shi_classic = __dadd_ru(Hi_N, __dmul_ru(gN, Hi_N));
+  int e2 = 0;
+  (void)frexp(shi_classic, &e2);
+  const double Gu = ldexp(1.0, e2 - 53);
+  const double thr_now = ldexp(Gu, 23);
+  const double B_tight = __dmul_ru(__ull2double_ru(C_N + kCrossingSlack), 0.5 * Gu);
+  const double thr_prev = thr[m];
+  const bool tight_ok = thr_now <= thr_prev;
+  auto bound_at = [&](uint64_t terms, double hi_prefix) {
+    const double bg = __dmul_ru(gamma_bound(terms), hi_prefix);
+    return tight_ok ? fmin(bg, B_tight) : bg;
+  };
+  const double u_mid = r * (0.5 * (Lo_N + Hi_N));
+  const bool past = !(u_mid < 0.5 * (incl_lo + incl_hi));
+  incl_all[tid] = make_double2(incl_lo, incl_hi);
+  const int n_before = __syncthreads_count(past);
+  if (tid == 0) {
+    sh_decided = 0;
+    sh_chunk = -1;
+    if (thr_now < thr_prev) thr[m] = thr_now;
+  }
+  __syncthreads();
+  if (n_before < kSelectThreads && tid == n_before) {
+    double lo = tid > 0 ? incl_all[tid - 1].x : 0.0;
+    double hi = tid > 0 ? incl_all[tid - 1].y : 0.0;
+    int found = -1;
+    for (int j = c_lo; j < c_hi; ++j) {
+      const double2 v = CH(j);
+      const double nlo = __dadd_rd(lo, v.x), nhi = __dadd_ru(hi, v.y);
+      if (u_mid < 0.5 * (nlo + nhi)) { found = j; break; }
+      lo = nlo;
+      hi = nhi;
+    }
+    sh_chunk = found;
+    sh_excl = make_double2(lo, hi);
+  }
+  __syncthreads();
+  const int fchunk = sh_chunk;
+  if (fchunk < 0) {  // no candidate: the exact chain decides
+    if (me == 0 && tid == 0) contrib[m].flag = 2;
+    return;
+  }
+  const int owner = fchunk / ncmax, lc = fchunk - owner * ncmax;
+  if (owner != me) return;
+  const uint64_t li = (uint64_t)lc * kSeedChunk + tid;
+  const bool valid = li < N;
+  const double v = valid ? (double)w[li] : 0.0;
+  const double slo = warp_scan_rd(v, lane), shi = warp_scan_ru(v, lane);
+  if (lane == 31) wsum[warp] = make_double2(slo, shi);
+  __syncthreads();
+  if (warp == 0) {
+    const double a = warp_scan_rd(wsum[lane].x, lane);
+    const double b = warp_scan_ru(wsum[lane].y, lane);
+    __syncwarp();
+    wsum[lane] = make_double2(a, b);
+  }
+  __syncthreads();
+  const double2 ex = sh_excl;
+  const double plo = warp > 0 ? wsum[warp - 1].x : 0.0, phi = warp > 0 ? wsum[warp - 1].y : 0.0;
+  const double elo = __dadd_rd(ex.x, __dadd_rd(plo, slo));
+  const double ehi = __dadd_ru(ex.y, __dadd_ru(phi, shi));
+  incl_all[tid] = make_double2(elo, ehi);
+  const bool hit = !valid || u_mid < 0.5 * (elo + ehi);
+  const int first = __syncthreads_count(!hit);
+  if (first < kSelectThreads && tid == first && valid) {
+    const uint64_t gi = rank_row0[me] + li;
+    const double2 prv = tid > 0 ? incl_all[tid - 1] : ex;
+    const double BN = bound_at(N_total, Hi_N);
+    const double ULo = __dmul_rd(r, __dsub_rd(Lo_N, BN));
+    const double UHi = __dmul_ru(r, __dadd_ru(Hi_N, BN));
+    bool ok = UHi < __dsub_rd(elo, bound_at(gi + 1, ehi));
+    if (gi > 0) ok = ok && (ULo >= __dadd_ru(prv.y, bound_at(gi, prv.y)));
+    if (ok && !force_chain) {
+      sh_idx = gi;
+      sh_decided = 1;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    RowContrib rc;
+    rc.pad = 0;
+    for (int k = 0; k < 4; ++k) rc.row[k] = 0.f;
+    if (sh_decided) {
+      rc.flag = 1;
+      rc.gidx = sh_idx;
+      const uint64_t l = sh_idx - rank_row0[me];
+      for (int k = 0; k < S; ++k) rc.row[k] = XT[((size_t)m * N + l) * S + k];
+    } else {
+      rc.flag = 2;
+      rc.gidx = 0;
+    }
+    contrib[m] = rc;
+  }
+}
+
+// Subspace m's rows of this rank, padded to Nmax with `pad`, for a gather:
+// out[m][i] (weights / min distances) and, when xt_out is set, the rows.
+__global__ void pq_dist_pack_kernel(const float* __restrict__ src, const float* __restrict__ XT, uint64_t N,
+                                    uint64_t Nmax, int S, int m, float pad, float* __restrict__ out,
+                                    float* __restrict__ xt_out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < Nmax;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    out[i] = i < N ? src[(size_t)m * N + i] : pad;
+    if (xt_out)
+      for (int k = 0; k < S; ++k) xt_out[i * S + k] = i < N ? XT[((size_t)m * N + i) * S + k] : 0.f;
+  }
+}
+
+// The reference's sequential weightedSample chain over the gathered weights
+// of subspace m (rank-major, zero padding changes neither sum nor search).
+__global__ void pq_dist_chain_draw_kernel(const float* __restrict__ gw, int G, uint64_t Nmax,
+                                          const uint64_t* __restrict__ rank_row0, const double* __restrict__ draws,
+                                          int m, int K, int step, uint64_t* __restrict__ pick,
+                                          uint32_t* __restrict__ fallbacks) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t total_n = (uint64_t)G * Nmax;
+  double total = 0.0;
+  uint64_t last_pos = 0;
+  for (uint64_t p = 0; p < total_n; ++p) {
+    const float v = gw[p];
+    total = __dadd_rn(total, (double)v);
+    if (v != 0.f) last_pos = p;
+  }
+  const double u = __dmul_rn(draws[(size_t)m * K + step], total);
+  double cum = 0.0;
+  uint64_t hitp = last_pos;
+  for (uint64_t p = 0; p < total_n; ++p) {
+    cum = __dadd_rn(cum, (double)gw[p]);
+    if (u < cum) {
+      hitp = p;
+      break;
+    }
+  }
+  const uint64_t r = hitp / Nmax;
+  pick[m] = rank_row0[r] + (hitp - r * Nmax);
+  fallbacks[m] += 1;
+}
+
+// Centroids from the last rank's running sums and the summed counts.
+__global__ void pq_dist_scale_kernel(const float* __restrict__ sums, const uint32_t* __restrict__ gcounts,
+                                     float* __restrict__ cb, const uint8_t* __restrict__ state, int M, int K,
+                                     int S) {
+  const int n = M * K * S;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    const int m = e / (K * S), c = (e / S) % K;
+    if (state[m] != kRunning) continue;
+    const uint32_t cnt = gcounts[(size_t)m * K + c];
+    if (cnt > 0) cb[e] = __fmul_rn(sums[e], __fdiv_rn(1.0f, __uint2float_rn(cnt)));
+  }
+}
+
+// empty[m] = 1 when running subspace m has an empty cluster (summed counts)
+__global__ void pq_dist_empty_kernel(const uint32_t* __restrict__ gcounts, const uint8_t* __restrict__ state,
+                                     int M, int K, uint32_t* __restrict__ empty) {
+  const int m = blockIdx.x;
+  __shared__ int any;
+  if (threadIdx.x == 0) any = 0;
+  __syncthreads();
+  if (state[m] == kRunning)
+    for (int c = threadIdx.x; c < K; c += blockDim.x)
+      if (gcounts[(size_t)m * K + c] == 0) atomicOr(&any, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) empty[m] = (uint32_t)any;
+}
+
+// Empty-cluster reseed of subspace m over the gathered min distances and
+// rows (-inf padding never wins), identically on every rank; this rank also
+// marks its own copy of each chosen row.
+__global__ void __launch_bounds__(1024)
+pq_dist_reseed_kernel(float* __restrict__ gmind, const float* __restrict__ gxt, int G, uint64_t Nmax, int S, int K,
+                      int m, const uint32_t* __restrict__ gcounts, float* __restrict__ cb, float* __restrict__ mind,
+                      uint64_t N, int me, uint32_t* __restrict__ reseeds) {
+  const uint64_t total_n = (uint64_t)G * Nmax;
+  for (int c = 0; c < K; ++c) {
+    if (gcounts[(size_t)m * K + c] != 0) continue;
+    const uint64_t far = block_argmax_first(gmind, total_n);
+    if (threadIdx.x < (unsigned)S) cb[((size_t)m * K + c) * S + threadIdx.x] = gxt[far * S + threadIdx.x];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      gmind[far] = -__int_as_float(0x7f800000);
+      const uint64_t r = far / Nmax, l = far - r * Nmax;
+      if ((int)r == me && l < N) mind[(size_t)m * N + l] = -__int_as_float(0x7f800000);
+      reseeds[m] += 1;
+    }
+    __syncthreads();
+  }
 }
 
 }  // namespace
@@ -1122,14 +1487,14 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   ++launches;
   for (int step = 0; step + 1 < K; ++step) {
     switch (S) {
-      case 1: pq_seed_update_kernel<1><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
-      case 2: pq_seed_update_kernel<2><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
-      default: pq_seed_update_kernel<4><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr); break;
+      case 1: pq_seed_update_kernel<1><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+      case 2: pq_seed_update_kernel<2><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+      default: pq_seed_update_kernel<4><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
     pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(XT, N, S, K, step + 1, cb, mind, chunk, chunk_cnt,
                                                         nchunk, d_draws, d_nonf, d_status, d_state, d_fb,
-                                                        d_chosen, d_thr);
+                                                        d_chosen, d_thr, ctx && ctx->serial_draws ? 1 : 0);
     MVR_CUDA(ctx, cudaGetLastError());
     launches += 2;
   }
@@ -1160,7 +1525,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     launches += 5;
     const bool last = it + 1 == job.max_iters;
     if (check || (last && out.h_wcss)) {
-      pq_wcss_kernel<<<M, 256, 0, st>>>(mind, N, d_wcss, d_state);
+      pq_wcss_kernel<<<M, 256, 0, st>>>(mind, N, d_wcss, d_state, nullptr);
       MVR_CUDA(ctx, cudaGetLastError());
       ++launches;
     }
@@ -1178,7 +1543,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
     }
     pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, d_counts, mind, cb, d_state, d_wcss, d_prev,
-                                                  d_iters, d_rs, (int)it, check ? 1 : 0, job.tol);
+                                                  d_iters, d_rs, (int)it, check ? 1 : 0, job.tol, 1);
     MVR_CUDA(ctx, cudaGetLastError());
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
@@ -1247,6 +1612,314 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
   MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
   std::vector<unsigned char> hsmall(L.small_bytes);
   return pq_kmeans_run(ctx, ctx->stream, job, out, ws, hsmall.data(), ctx->sm_count);
+}
+
+int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_total, const PqOut& out,
+                       bool local_ok) {
+  cudaStream_t st = ctx->stream;
+  const int G = comm_size(ctx), me = comm_rank(ctx);
+  const uint64_t N = job.N;
+  const int D = job.D, M = job.M, S = job.S, K = job.K;
+  MVR_TRY(check_shape(ctx, D, M, S, K));  // same parameters on every rank
+  // rank-dependent checks travel with the rank table, so every rank fails
+  // together instead of leaving the others in a collective
+  local_ok = local_ok && N > 0 && N < (1ull << 32) && job.R && out.d_codebooks;
+  const int sms = ctx->sm_count;
+
+  // ---- dist bookkeeping (kSlotAux2) -----------------------------------------
+  // rank table first: every rank's (row0, N) -> contiguous shards in rank order
+  const size_t cb_floats = (size_t)M * K * S;
+  Carve dc;
+  const size_t o_tab_send = dc.take(16), o_tab = dc.take((size_t)G * 16), o_row0 = dc.take((size_t)G * 8);
+  unsigned char* dws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotAux2, dc.off + 64, (void**)&dws));
+  uint64_t* hp = nullptr;
+  MVR_TRY(pinned(ctx, std::max<size_t>((size_t)G * 16 + (size_t)M * 8, 4096), (void**)&hp));
+  hp[0] = row0;
+  hp[1] = local_ok ? N : 0;  // a zero row count marks a rank that cannot run
+  MVR_CUDA(ctx, cudaMemcpyAsync(dws + o_tab_send, hp, 16, cudaMemcpyHostToDevice, st));
+  MVR_TRY(comm_allgather(ctx, dws + o_tab_send, dws + o_tab, 16));
+  MVR_CUDA(ctx, cudaMemcpyAsync(hp, dws + o_tab, (size_t)G * 16, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  std::vector<uint64_t> r0(G), rn(G);
+  uint64_t expect = 0, Nmax = 0;
+  for (int r = 0; r < G; ++r) {
+    r0[r] = hp[2 * r];
+    rn[r] = hp[2 * r + 1];
+    if (rn[r] == 0)
+      return fail(ctx, MVR_E_INVALID_ARGUMENT,
+                  "rank " + std::to_string(r) + " cannot run (empty shard, null pointer or > 2^32-1 rows)");
+    if (r0[r] != expect) return fail(ctx, MVR_E_INVALID_ARGUMENT, "shards must be contiguous in rank order");
+    expect += rn[r];
+    Nmax = std::max(Nmax, rn[r]);
+  }
+  if (expect != N_total) return fail(ctx, MVR_E_INVALID_ARGUMENT, "the shards do not add up to n_total");
+  if ((uint64_t)K >= N_total) return fail(ctx, MVR_E_INVALID_ARGUMENT, "row-sharded training needs n_total > 256");
+  const int ncmax = (int)((Nmax + kSeedChunk - 1) / kSeedChunk);
+  const SeedBlock sb = seed_block(M, ncmax);
+  const size_t o_seed = dc.take(sb.bytes), o_seed_all = dc.take(sb.bytes * G),
+               o_con = dc.take((size_t)M * sizeof(RowContrib)), o_con_all = dc.take((size_t)G * M * sizeof(RowContrib)),
+               o_need = dc.take((size_t)M * 4), o_empty = dc.take((size_t)M * 4), o_pick = dc.take((size_t)M * 8),
+               o_sin = dc.take(cb_floats * 4), o_sout = dc.take(cb_floats * 4), o_gcnt = dc.take((size_t)M * K * 4),
+               o_wst = dc.take((size_t)M * 4);
+  MVR_TRY(scratch(ctx, kSlotAux2, dc.off, (void**)&dws));  // may move: re-derive everything below
+  {
+    for (int r = 0; r < G; ++r) hp[r] = r0[r];
+    MVR_CUDA(ctx, cudaMemcpyAsync(dws + o_row0, hp, (size_t)G * 8, cudaMemcpyHostToDevice, st));
+  }
+  const uint64_t* d_row0 = (const uint64_t*)(dws + o_row0);
+  unsigned char* seed_send = dws + o_seed;
+  unsigned char* seed_all = dws + o_seed_all;
+  RowContrib* con = (RowContrib*)(dws + o_con);
+  RowContrib* con_all = (RowContrib*)(dws + o_con_all);
+  uint32_t* d_need = (uint32_t*)(dws + o_need);
+  uint32_t* d_empty = (uint32_t*)(dws + o_empty);
+  uint64_t* d_pick = (uint64_t*)(dws + o_pick);
+  float* sums_in = (float*)(dws + o_sin);
+  float* sums_out = (float*)(dws + o_sout);
+  uint32_t* gcounts = (uint32_t*)(dws + o_gcnt);
+  float* wstart = (float*)(dws + o_wst);
+  MVR_CUDA(ctx, cudaMemsetAsync(seed_send, 0, sb.bytes, st));  // padding chunks stay empty
+
+  // ---- local engine workspace (kSlotMinDist) ---------------------------------
+  const PqLayout L = pq_layout(N, M, S, K, sms);
+  unsigned char* ws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
+  std::vector<unsigned char> hsmall_v(L.small_bytes);
+  unsigned char* hsmall = hsmall_v.data();
+  const int nblk = L.nblk, nchunk = L.nchunk;
+  const uint64_t rpc = L.rows_per_cta;
+  float* XT = (float*)(ws + L.o_xt);
+  float* mind = (float*)(ws + L.o_mind);
+  uint8_t* asg = (uint8_t*)(ws + L.o_asg);
+  float* sorted = (float*)(ws + L.o_sorted);
+  uint32_t* hist = (uint32_t*)(ws + L.o_hist);
+  unsigned char* small = ws;
+  double* d_draws = (double*)(small + L.o_draws);
+  uint64_t* d_chosen = (uint64_t*)(small + L.o_chosen);
+  uint64_t* d_idx0 = (uint64_t*)(small + L.o_idx0);
+  double* d_thr = (double*)(small + L.o_thr);
+  uint32_t* d_counts = (uint32_t*)(small + L.o_counts);
+  uint32_t* d_starts = (uint32_t*)(small + L.o_starts);
+  float* d_wcss = (float*)(small + L.o_wcss);
+  float* d_prev = (float*)(small + L.o_prev);
+  int* d_status = (int*)(small + L.o_status);
+  uint32_t* d_iters = (uint32_t*)(small + L.o_iters);
+  uint32_t* d_fb = (uint32_t*)(small + L.o_fb);
+  uint32_t* d_rs = (uint32_t*)(small + L.o_rs);
+  uint8_t* d_state = (uint8_t*)(small + L.o_state);
+  double2* chunk = (double2*)seed_send;
+  uint32_t* chunk_cnt = (uint32_t*)(seed_send + sb.o_cnt);
+  int* d_nonf = (int*)(seed_send + sb.o_nonf);
+
+  const bool timing = out.stats != nullptr;
+  if (timing) {
+    for (int e = 0; e < 4; ++e)
+      if (!ctx->ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ctx->ev[e]));
+    MVR_CUDA(ctx, cudaEventRecord(ctx->ev[0], st));
+  }
+  // host RNG draws over the global row count, as the one-GPU engine
+  std::memset(hsmall, 0, L.small_bytes);
+  {
+    double* hd = (double*)(hsmall + L.o_draws);
+    uint64_t* hi0 = (uint64_t*)(hsmall + L.o_idx0);
+    double* ht = (double*)(hsmall + L.o_thr);
+    for (int m = 0; m < M; ++m) {
+      Xoshiro256pp rng(job.seed + (uint64_t)m);
+      hi0[m] = rng.below(N_total);
+      hd[(size_t)m * K] = 0.0;
+      for (int c = 1; c < K; ++c) hd[(size_t)m * K + c] = rng.unit_f64();
+      ht[m] = HUGE_VAL;
+    }
+  }
+  MVR_CUDA(ctx, cudaMemcpyAsync(small, hsmall, L.small_bytes, cudaMemcpyHostToDevice, st));
+  uint32_t launches = 0;
+  {
+    const int grid = (int)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 8);
+    switch (S) {
+      case 1: pq_transpose_kernel<1><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      case 2: pq_transpose_kernel<2><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      default: pq_transpose_kernel<4><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+    ++launches;
+  }
+  float* cb = out.d_codebooks;
+  const size_t con_bytes = (size_t)M * sizeof(RowContrib);
+  auto exchange_rows = [&](int step) -> int {  // contrib -> every rank's centroid `step`
+    MVR_TRY(comm_allgather(ctx, con, con_all, con_bytes));
+    pq_dist_take_kernel<<<1, 32, 0, st>>>(con_all, G, M, S, K, step, cb, d_chosen, d_state, d_need);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 1;
+    return MVR_OK;
+  };
+  // rare paths: gathered copies of one subspace (kSlotAux3)
+  auto gather_subspace = [&](int m, const float* src, float pad, bool with_rows, float** gv, float** gx) -> int {
+    const size_t vb = (size_t)Nmax * 4, xb = with_rows ? (size_t)Nmax * S * 4 : 0;
+    Carve rc;
+    const size_t o_pv = rc.take(vb), o_px = rc.take(xb), o_gv = rc.take(vb * G), o_gx = rc.take(xb * G);
+    unsigned char* rws = nullptr;
+    MVR_TRY(scratch(ctx, kSlotAux3, rc.off, (void**)&rws));
+    float* pv = (float*)(rws + o_pv);
+    float* px = with_rows ? (float*)(rws + o_px) : nullptr;
+    const int grid = (int)std::min<uint64_t>((Nmax + 255) / 256, 4096);
+    pq_dist_pack_kernel<<<grid, 256, 0, st>>>(src, XT, N, Nmax, S, m, pad, pv, px);
+    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_TRY(comm_allgather(ctx, pv, rws + o_gv, vb));
+    if (with_rows) MVR_TRY(comm_allgather(ctx, px, rws + o_gx, xb));
+    *gv = (float*)(rws + o_gv);
+    *gx = with_rows ? (float*)(rws + o_gx) : nullptr;
+    launches += 1;
+    return MVR_OK;
+  };
+  uint32_t* hneed = (uint32_t*)hp;
+
+  // ---- k-means++ ----------------------------------------------------------------
+  pq_dist_offer_kernel<<<1, 32, 0, st>>>(XT, N, S, M, row0, d_idx0, nullptr, con);
+  MVR_CUDA(ctx, cudaGetLastError());
+  MVR_TRY(exchange_rows(0));
+  for (int step = 0; step + 1 < K; ++step) {
+    switch (S) {
+      case 1: pq_seed_update_kernel<1><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, ncmax); break;
+      case 2: pq_seed_update_kernel<2><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, ncmax); break;
+      default: pq_seed_update_kernel<4><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, ncmax); break;
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_TRY(comm_allgather(ctx, seed_send, seed_all, sb.bytes));
+    pq_seed_select_dist_kernel<<<M, kSelectThreads, 0, st>>>(seed_all, G, ncmax, d_row0, me, N_total, XT, N, S, M,
+                                                             K, step + 1, mind, d_draws, d_status, d_state, d_thr,
+                                                             con, ctx->serial_draws ? 1 : 0);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 2;
+    MVR_TRY(exchange_rows(step + 1));
+    MVR_CUDA(ctx, cudaMemcpyAsync(hneed, d_need, (size_t)M * 4, cudaMemcpyDeviceToHost, st));
+    MVR_CUDA(ctx, cudaStreamSynchronize(st));
+    bool any = false;
+    std::vector<uint32_t> need(hneed, hneed + M);
+    for (int m = 0; m < M; ++m) {
+      if (!need[m]) continue;
+      any = true;
+      float *gw = nullptr, *gx = nullptr;
+      MVR_TRY(gather_subspace(m, mind, 0.f, false, &gw, &gx));
+      pq_dist_chain_draw_kernel<<<1, 1, 0, st>>>(gw, G, Nmax, d_row0, d_draws, m, K, step + 1, d_pick, d_fb);
+      MVR_CUDA(ctx, cudaGetLastError());
+      ++launches;
+    }
+    if (any) {
+      MVR_CUDA(ctx, cudaMemcpyAsync(d_need, need.data(), (size_t)M * 4, cudaMemcpyHostToDevice, st));
+      pq_dist_offer_kernel<<<1, 32, 0, st>>>(XT, N, S, M, row0, d_pick, d_need, con);
+      MVR_CUDA(ctx, cudaGetLastError());
+      MVR_TRY(exchange_rows(step + 1));
+    }
+  }
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
+
+  // ---- Lloyd ------------------------------------------------------------------------
+  const bool check = !(job.tol == -INFINITY) && !std::isnan(job.tol);
+  for (uint32_t it = 0; it < job.max_iters; ++it) {
+    switch (S) {
+      case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+      case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+      default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+    }
+    pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
+    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_CUDA(ctx, cudaMemcpyAsync(gcounts, d_counts, (size_t)M * K * 4, cudaMemcpyDeviceToDevice, st));
+    MVR_TRY(comm_allreduce_sum_u32(ctx, gcounts, (size_t)M * K));
+    launches += 6;
+    const bool last = it + 1 == job.max_iters;
+    if (check || (last && out.h_wcss)) {  // WCSS continued rank after rank
+      if (me > 0) MVR_TRY(comm_recv(ctx, wstart, (size_t)M * 4, me - 1));
+      pq_wcss_kernel<<<M, 256, 0, st>>>(mind, N, d_wcss, d_state, me > 0 ? wstart : nullptr);
+      MVR_CUDA(ctx, cudaGetLastError());
+      if (me + 1 < G) MVR_TRY(comm_send(ctx, d_wcss, (size_t)M * 4, me + 1));
+      MVR_TRY(comm_broadcast(ctx, d_wcss, (size_t)M * 4, G - 1));
+      ++launches;
+    }
+    switch (S) {
+      case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      default: { auto k = pq_scatter_kernel<4>; const size_t sm = scatter_smem(M, 4); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+    // centroid sums continued rank after rank; the last rank scales
+    if (me > 0) MVR_TRY(comm_recv(ctx, sums_in, cb_floats * 4, me - 1));
+    const float* sstart = me > 0 ? sums_in : nullptr;
+    switch (S) {
+      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
+      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
+      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
+    }
+    if (me + 1 < G) {
+      MVR_TRY(comm_send(ctx, sums_out, cb_floats * 4, me + 1));
+    } else {
+      pq_dist_scale_kernel<<<(int)((cb_floats + 255) / 256), 256, 0, st>>>(sums_out, gcounts, cb, d_state, M, K, S);
+      MVR_CUDA(ctx, cudaGetLastError());
+    }
+    MVR_TRY(comm_broadcast(ctx, cb, cb_floats * 4, G - 1));
+    // empty clusters (same decision on every rank)
+    pq_dist_empty_kernel<<<M, 256, 0, st>>>(gcounts, d_state, M, K, d_empty);
+    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_CUDA(ctx, cudaMemcpyAsync(hneed, d_empty, (size_t)M * 4, cudaMemcpyDeviceToHost, st));
+    MVR_CUDA(ctx, cudaStreamSynchronize(st));
+    std::vector<uint32_t> empty(hneed, hneed + M);
+    for (int m = 0; m < M; ++m) {
+      if (!empty[m]) continue;
+      float *gv = nullptr, *gx = nullptr;
+      MVR_TRY(gather_subspace(m, mind, -__builtin_inff(), true, &gv, &gx));
+      pq_dist_reseed_kernel<<<1, 1024, 0, st>>>(gv, gx, G, Nmax, S, K, m, gcounts, cb, mind, N, me, d_rs);
+      MVR_CUDA(ctx, cudaGetLastError());
+      ++launches;
+    }
+    pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, gcounts, mind, cb, d_state, d_wcss, d_prev, d_iters,
+                                                  d_rs, (int)it, check ? 1 : 0, job.tol, 0);
+    MVR_CUDA(ctx, cudaGetLastError());
+    launches += 5;
+  }
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
+  if (out.d_assign && job.max_iters > 0) {
+    u8_to_u32_kernel<<<1024, 256, 0, st>>>(asg, out.d_assign, (uint64_t)M * N);
+    MVR_CUDA(ctx, cudaGetLastError());
+    ++launches;
+  }
+  MVR_CUDA(ctx, cudaMemcpyAsync(hsmall, small, L.small_bytes, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  const int* hstatus = (const int*)(hsmall + L.o_status);
+  for (int m = 0; m < M; ++m)
+    if (hstatus[m] != MVR_OK)
+      return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
+  const uint32_t* hiters = (const uint32_t*)(hsmall + L.o_iters);
+  const float* hw = (const float*)(hsmall + L.o_wcss);
+  if (out.h_iters)
+    for (int m = 0; m < M; ++m) out.h_iters[m] = job.max_iters ? hiters[m] : 0;
+  if (out.h_wcss)
+    for (int m = 0; m < M; ++m) out.h_wcss[m] = job.max_iters ? hw[m] : 0.f;
+  if (out.stats) {
+    std::memset(out.stats, 0, sizeof(*out.stats));
+    float t01 = 0, t12 = 0, t02 = 0;
+    cudaEventElapsedTime(&t01, ctx->ev[0], ctx->ev[1]);
+    cudaEventElapsedTime(&t12, ctx->ev[1], ctx->ev[2]);
+    cudaEventElapsedTime(&t02, ctx->ev[0], ctx->ev[2]);
+    out.stats->seed_ms = t01;
+    out.stats->lloyd_ms = t12;
+    out.stats->total_ms = t02;
+    uint32_t mx = 0, mn = UINT32_MAX, fb = 0, rs = 0;
+    const uint32_t* hfb = (const uint32_t*)(hsmall + L.o_fb);
+    const uint32_t* hrs = (const uint32_t*)(hsmall + L.o_rs);
+    for (int m = 0; m < M; ++m) {
+      const uint32_t v = job.max_iters ? hiters[m] : 0;
+      mx = std::max(mx, v);
+      mn = std::min(mn, v);
+      fb += hfb[m];
+      rs += hrs[m];
+    }
+    out.stats->iters_max = mx;
+    out.stats->iters_min = mn;
+    out.stats->seed_fallbacks = fb;
+    out.stats->reseeds = rs;
+    out.stats->launches = launches;
+  }
+  return MVR_OK;
 }
 
 }  // namespace mvr

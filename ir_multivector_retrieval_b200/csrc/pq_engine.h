@@ -62,6 +62,16 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t stream, const PqJob& job, const PqOut& 
 // pq_kmeans_run with the workspace taken from the context's scratch.
 int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out);
 
+// Row-sharded pq_kmeans_device: this rank holds rows [row0, row0 + job.N) of
+// an N_total-row matrix (shards contiguous in rank order, one per rank of the
+// context's communicator). Every rank ends with the codebooks the one-GPU
+// engine computes on the whole matrix; out.d_assign receives this rank's
+// rows. Collective: every rank calls it with the same job parameters.
+// local_ok = false makes every rank return MVR_E_INVALID_ARGUMENT (after the
+// first exchange) instead of leaving the other ranks waiting.
+int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_total, const PqOut& out,
+                       bool local_ok);
+
 // PQ.encode of N rows (asynchronous on the context stream).
 int pq_encode_device(Ctx* ctx, const float* d_codebooks, int D, int M,
                      const float* d_R, uint64_t N, uint8_t* d_codes);

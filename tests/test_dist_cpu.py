@@ -1,0 +1,104 @@
+"""Host logic of the row-sharded path on CPU: shard bounds, the NCCL id
+hand-off over a torch group, and the Lloyd exchange protocol (running f32
+sums carried rank to rank, counts summed) run by two gloo ranks against the
+single serial loop of the reference."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from ir_multivector_retrieval_b200 import dist as mdist
+
+
+def test_shard_rows_cover_contiguously():
+    for n in (1, 2, 7, 256, 1_521_797):
+        for world in (1, 2, 3, 4, 8):
+            if n < world:
+                continue
+            nxt, sizes = 0, []
+            for r in range(world):
+                row0, nl = mdist.shard_rows(n, world, r)
+                assert row0 == nxt and nl >= 1
+                nxt += nl
+                sizes.append(nl)
+            assert nxt == n and max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        mdist.shard_rows(10, 2, 2)
+
+
+def test_relay_order_equals_serial_sum():
+    rng = np.random.default_rng(0)
+    v = (rng.standard_normal(10_001) * 10.0 ** rng.integers(-6, 6, size=10_001)).astype(np.float32)
+    serial = np.float32(0)
+    for x in v:
+        serial = np.float32(serial + x)
+    for world in (1, 2, 3, 8):
+        shards = [v[mdist.shard_rows(v.size, world, r)[0]:][: mdist.shard_rows(v.size, world, r)[1]]
+                  for r in range(world)]
+        assert mdist.relay_order(shards).tobytes() == serial.tobytes()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, ret):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        uid = mdist.exchange_unique_id(lambda: bytes(range(128)))
+        ok_uid = uid == bytes(range(128))
+        # one Lloyd exchange for K clusters of S coordinates over sharded rows
+        rng = np.random.default_rng(42)
+        n, K, S = 5_003, 16, 4
+        rows = (rng.standard_normal((n, S)) * 100).astype(np.float32)
+        asg = rng.integers(0, K, size=n)
+        row0, nl = mdist.shard_rows(n, world, rank)
+        # the engine's order: counts summed by all ranks, then the relay
+        counts = torch.from_numpy(np.bincount(asg[row0:row0 + nl], minlength=K).astype(np.int64))
+        dist.all_reduce(counts)
+        sums = torch.zeros((K, S), dtype=torch.float32)
+        if rank > 0:
+            dist.recv(sums, src=rank - 1)
+        acc = sums.numpy().copy()
+        for i in range(row0, row0 + nl):
+            acc[asg[i]] = (acc[asg[i]] + rows[i]).astype(np.float32)
+        out = torch.from_numpy(acc)
+        if rank + 1 < world:
+            dist.send(out, dst=rank + 1)
+        dist.broadcast(out, src=world - 1)
+        if rank == 0:
+            want = np.zeros((K, S), np.float32)
+            for i in range(n):
+                want[asg[i]] = (want[asg[i]] + rows[i]).astype(np.float32)
+            ret.put((ok_uid, out.numpy().tobytes() == want.tobytes(),
+                     np.array_equal(counts.numpy(), np.bincount(asg, minlength=K))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_exchange_protocol():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    ok_uid, ok_sums, ok_counts = q.get(timeout=10)
+    assert ok_uid and ok_sums and ok_counts
