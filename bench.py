@@ -24,9 +24,13 @@ thresholds (mu 128, tau 256, eps 4, theta 39), with its device phases; and on
 configs[0]'s 117,645-row corpus (kappa 12,288, theta 10) beside the CPU
 restatement of the reference timed on one host core.
 
-Multi-GPU (``--gpus N`` under torchrun): each rank runs the full workload
-as an independent replica ("replicas only" in this round); the reported time
-is the max over ranks.
+Multi-GPU (``--gpus N`` under torchrun, configs[2]): the same 1,521,797 rows
+are split into N contiguous shards, one per GPU, and ``pq.train`` runs
+row-sharded (``mvr_pq_train_sharded_device``: NCCL exchanges inside the
+library, codebooks byte-identical to the one-GPU run for any N;
+``codebook_sha256`` in the line lets runs at different N be compared);
+``pq.encode`` runs on each shard. Strong scaling: the total work is fixed;
+times are the max over ranks.
 """
 from __future__ import annotations
 
@@ -259,10 +263,13 @@ def run_b200(args) -> None:
     from ir_multivector_retrieval_b200._lib import PqTrainStats
 
     corpus = make_corpus(args.rows)
+    from ir_multivector_retrieval_b200 import dist as mdist
     from ir_multivector_retrieval_b200 import synth
 
-    x = synth.anchor_residuals(corpus)
-    n = x.shape[0]
+    x_all = synth.anchor_residuals(corpus)
+    n_total = x_all.shape[0]
+    row0, n = mdist.shard_rows(n_total, world, rank)
+    x = np.ascontiguousarray(x_all[row0:row0 + n])
     x_pin = torch.from_numpy(x).pin_memory()
     dx = x_pin.to(f"cuda:{local}", non_blocking=False)
     dcb = torch.empty(PQ_M * K * (DIM // PQ_M), dtype=torch.float32, device=f"cuda:{local}")
@@ -276,10 +283,17 @@ def run_b200(args) -> None:
     ctx = Context(local)
     ctx.set_stream(stream.cuda_stream)
     lib = ctx.lib
+    if world > 1:
+        mdist.init_comm(ctx)
 
     def train_dev(st):
-        ctx.check(lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), x.size, DIM, SEED, 1, PQ_M,
-                                          ITERS, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()), C.byref(st)))
+        if world > 1:
+            ctx.check(lib.mvr_pq_train_sharded_device(ctx.handle, C.c_void_p(dx.data_ptr()), n, row0, n_total, DIM,
+                                                      SEED, 1, PQ_M, ITERS, C.c_float(-math.inf),
+                                                      C.c_void_p(dcb.data_ptr()), None, C.byref(st)))
+        else:
+            ctx.check(lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), x.size, DIM, SEED, 1, PQ_M,
+                                              ITERS, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()), C.byref(st)))
 
     def encode_dev():
         ctx.check(lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), DIM, PQ_M,
@@ -320,7 +334,7 @@ def run_b200(args) -> None:
     seed_ms = statistics.mean(s.seed_ms for s in stats)
     lloyd_ms = statistics.mean(s.lloyd_ms for s in stats)
     enc_ms = statistics.mean(a.elapsed_time(b) for a, b in enc_ev)
-    assign_ms = sum(s.assign_ms for s in stats) / sum(s.assign_launches for s in stats)
+    assign_ms = sum(s.assign_ms for s in stats) / max(1, sum(s.assign_launches for s in stats))
     launches = int(statistics.mean(s.launches for s in stats)) + 1
 
     def max_over_ranks(v: float) -> float:
@@ -340,10 +354,16 @@ def run_b200(args) -> None:
     codes_host = torch.empty((n, PQ_M), dtype=torch.uint8).pin_memory()
     e2e_train, e2e_enc = [], []
     for i in range(max(1, args.e2e_steps) + 1):
-        torch.cuda.synchronize()
+        barrier()
         t0 = time.perf_counter()
-        ctx.check(lib.mvr_pq_train(ctx.handle, C.c_void_p(x_pin.data_ptr()), x.size, DIM, SEED, 1, PQ_M, ITERS,
-                                   C.c_float(-math.inf), C.c_void_p(cb_host.ctypes.data), None))
+        if world > 1:  # the shard travels host -> device, codebooks come back
+            dx.copy_(x_pin, non_blocking=True)
+            train_dev(PqTrainStats())
+            torch.cuda.current_stream().synchronize()
+            cb_host[:] = dcb.cpu().numpy()
+        else:
+            ctx.check(lib.mvr_pq_train(ctx.handle, C.c_void_p(x_pin.data_ptr()), x.size, DIM, SEED, 1, PQ_M,
+                                       ITERS, C.c_float(-math.inf), C.c_void_p(cb_host.ctypes.data), None))
         t1 = time.perf_counter()
         ctx.check(lib.mvr_pq_encode(ctx.handle, C.c_void_p(cb_host.ctypes.data), DIM, PQ_M,
                                     C.c_void_p(x_pin.data_ptr()), n, C.c_void_p(codes_host.data_ptr())))
@@ -371,14 +391,17 @@ def run_b200(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows": n, "dim": DIM, "pq_m": PQ_M, "centroids": K,
-                       "lloyd_iters": ITERS, "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+            "config": {"workload": WORKLOAD, "rows": n_total, "rows_per_gpu": n, "dim": DIM, "pq_m": PQ_M,
+                       "centroids": K, "lloyd_iters": ITERS,
+                       "parallelism": f"row-sharded over {world} GPUs (NCCL)" if world > 1 else "1gpu",
                        "l2": "inputs (389 MB) > L2, no flush"},
+            "codebook_sha256": mdist.codebook_digest(cb_host),
             "pq_train_ms": train_ms, "seed_ms": seed_ms, "lloyd_ms": lloyd_ms,
             "lloyd_only_s_per_iter": lloyd_ms / 1e3 / ITERS,
-            "pq_encode_ms": enc_ms, "pq_encode_mvec_s": n / (enc_ms / 1e3) / 1e6,
+            "pq_encode_ms": enc_ms, "pq_encode_mvec_s": n_total / (enc_ms / 1e3) / 1e6,
             "seed_fallbacks": int(stats[-1].seed_fallbacks), "reseeds": int(stats[-1].reseeds),
             "gpu_launches": launches,
             "clocks": clk,
@@ -390,7 +413,7 @@ def run_b200(args) -> None:
                          "avg_launch_ms": assign_ms},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(cb_host.nbytes),
-                    "encode_mvec_s": n / e2e_enc_s / 1e6},
+                    "encode_mvec_s": n_total / e2e_enc_s / 1e6},
         }
         if not args.no_tac:
             line["tac"] = measure_tac(corpus, 3, cpu=(world == 1 and not args.no_cpu))

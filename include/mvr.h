@@ -224,7 +224,11 @@ int mvr_ctx_comm_rank(const mvr_ctx* ctx);
  * `mvr_pq_train` computes on the whole matrix (identical bytes for any
  * number of ranks); `d_assign_out` (optional, pq_m*n_local u32, [m][row])
  * receives this rank's final assignments. Without a communicator the shard
- * must be the whole matrix. Returns when the result is ready. */
+ * must be the whole matrix. With pq_m >= ranks each rank trains a range of
+ * whole subspaces over all rows (their columns are exchanged once before and
+ * the codebooks gathered after); with fewer subspaces than ranks the rows
+ * stay split and every k-means++ draw and Lloyd iteration exchanges bounds,
+ * counts and running sums. Returns when the result is ready. */
 int mvr_pq_train_sharded_device(mvr_ctx* ctx, const float* d_rows,
                                 uint64_t n_local, uint64_t row0,
                                 uint64_t n_total, uint32_t dim, uint64_t seed,

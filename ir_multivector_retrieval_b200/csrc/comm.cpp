@@ -23,6 +23,8 @@ struct NcclApi {
   ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -46,8 +48,10 @@ const NcclApi& api() {
     a.Send = (decltype(a.Send))sym("ncclSend");
     a.Recv = (decltype(a.Recv))sym("ncclRecv");
     a.GetErrorString = (decltype(a.GetErrorString))sym("ncclGetErrorString");
+    a.GroupStart = (decltype(a.GroupStart))sym("ncclGroupStart");
+    a.GroupEnd = (decltype(a.GroupEnd))sym("ncclGroupEnd");
     a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.AllGather && a.AllReduce && a.Broadcast &&
-           a.Send && a.Recv && a.GetErrorString;
+           a.Send && a.Recv && a.GetErrorString && a.GroupStart && a.GroupEnd;
     if (!a.ok) a.why = "libnccl.so.2 lacks a required symbol";
   });
   return a;
@@ -103,6 +107,14 @@ int comm_send(Ctx* ctx, const void* buf, size_t bytes, int peer) {
 }
 int comm_recv(Ctx* ctx, void* buf, size_t bytes, int peer) {
   MVR_NCCL(ctx, api().Recv(buf, bytes, ncclUint8, peer, ctx->comm->comm, ctx->stream));
+  return MVR_OK;
+}
+int comm_group_start(Ctx* ctx) {
+  MVR_NCCL(ctx, api().GroupStart());
+  return MVR_OK;
+}
+int comm_group_end(Ctx* ctx) {
+  MVR_NCCL(ctx, api().GroupEnd());
   return MVR_OK;
 }
 

@@ -28,5 +28,8 @@ int comm_allreduce_max_u64(Ctx* ctx, uint64_t* buf, size_t count);
 int comm_broadcast(Ctx* ctx, void* buf, size_t bytes, int root);
 int comm_send(Ctx* ctx, const void* buf, size_t bytes, int peer);
 int comm_recv(Ctx* ctx, void* buf, size_t bytes, int peer);
+// bracket point-to-point calls that must progress together (an exchange)
+int comm_group_start(Ctx* ctx);
+int comm_group_end(Ctx* ctx);
 
 }  // namespace mvr

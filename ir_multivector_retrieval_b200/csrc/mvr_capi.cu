@@ -316,6 +316,10 @@ int mvr_pq_train_sharded_device(mvr_ctx* h, const float* d_rows, uint64_t n_loca
       return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "without a communicator the shard is the whole matrix");
     return mvr::pq_kmeans_device(c, job, out);
   }
+  // subspaces are independent problems: with at least one per rank each rank
+  // trains whole subspaces (one exchange before, one gather after); with
+  // fewer subspaces than ranks the rows are split and every step exchanges
+  if ((int)pq_m >= mvr::comm_size(c)) return mvr::pq_kmeans_run_subspaces(c, job, row0, n_total, out, d_rows && d_cb);
   return mvr::pq_kmeans_run_dist(c, job, row0, n_total, out, d_rows && d_cb);
 }
 

@@ -1470,7 +1470,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   MVR_CUDA(ctx, cudaMemcpyAsync(small, hsmall, small_bytes, cudaMemcpyHostToDevice, st));
 
   uint32_t launches = 0;
-  {
+  if (!job.xt_ready) {
     const int grid = (int)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 8);
     switch (S) {
       case 1: pq_transpose_kernel<1><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
@@ -1816,12 +1816,26 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
 
   // ---- Lloyd ------------------------------------------------------------------------
   const bool check = !(job.tol == -INFINITY) && !std::isnan(job.tol);
+  std::vector<cudaEvent_t> aev;  // assignment-kernel brackets (stats only)
+  if (timing) {
+    aev.resize(2 * (size_t)job.max_iters, nullptr);
+    for (auto& e : aev) MVR_CUDA(ctx, cudaEventCreate(&e));
+  }
+  struct EvGuard {
+    std::vector<cudaEvent_t>& v;
+    ~EvGuard() {
+      for (auto e : v)
+        if (e) cudaEventDestroy(e);
+    }
+  } ev_guard{aev};
   for (uint32_t it = 0; it < job.max_iters; ++it) {
+    if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it], st));
     switch (S) {
       case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
       case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
       default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
     }
+    if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
     pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     MVR_CUDA(ctx, cudaMemcpyAsync(gcounts, d_counts, (size_t)M * K * 4, cudaMemcpyDeviceToDevice, st));
@@ -1903,6 +1917,14 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
     out.stats->seed_ms = t01;
     out.stats->lloyd_ms = t12;
     out.stats->total_ms = t02;
+    double am = 0.0;
+    for (uint32_t it = 0; it < job.max_iters; ++it) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, aev[2 * it], aev[2 * it + 1]);
+      am += t;
+    }
+    out.stats->assign_ms = am;
+    out.stats->assign_launches = job.max_iters;
     uint32_t mx = 0, mn = UINT32_MAX, fb = 0, rs = 0;
     const uint32_t* hfb = (const uint32_t*)(hsmall + L.o_fb);
     const uint32_t* hrs = (const uint32_t*)(hsmall + L.o_rs);
@@ -1918,6 +1940,168 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
     out.stats->seed_fallbacks = fb;
     out.stats->reseeds = rs;
     out.stats->launches = launches;
+  }
+  return MVR_OK;
+}
+
+int pq_kmeans_run_subspaces(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_total, const PqOut& out,
+                            bool local_ok) {
+  cudaStream_t st = ctx->stream;
+  const int G = comm_size(ctx), me = comm_rank(ctx);
+  const uint64_t N = job.N;
+  const int D = job.D, M = job.M, S = job.S, K = job.K;
+  MVR_TRY(check_shape(ctx, D, M, S, K));  // same parameters on every rank
+  local_ok = local_ok && N > 0 && N < (1ull << 32) && job.R && out.d_codebooks;
+  const int sms = ctx->sm_count;
+
+  // ---- rank table: contiguous non-empty shards in rank order -------------
+  Carve dc;
+  const size_t o_tab_send = dc.take(16), o_tab = dc.take((size_t)G * 16), o_stat = dc.take((size_t)G * 8);
+  unsigned char* dws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotAux2, dc.off, (void**)&dws));
+  uint64_t* hp = nullptr;
+  MVR_TRY(pinned(ctx, std::max<size_t>((size_t)G * 16, 4096), (void**)&hp));
+  hp[0] = row0;
+  hp[1] = local_ok ? N : 0;
+  MVR_CUDA(ctx, cudaMemcpyAsync(dws + o_tab_send, hp, 16, cudaMemcpyHostToDevice, st));
+  MVR_TRY(comm_allgather(ctx, dws + o_tab_send, dws + o_tab, 16));
+  MVR_CUDA(ctx, cudaMemcpyAsync(hp, dws + o_tab, (size_t)G * 16, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  std::vector<uint64_t> r0(G), rn(G);
+  uint64_t expect = 0;
+  for (int r = 0; r < G; ++r) {
+    r0[r] = hp[2 * r];
+    rn[r] = hp[2 * r + 1];
+    if (rn[r] == 0)
+      return fail(ctx, MVR_E_INVALID_ARGUMENT,
+                  "rank " + std::to_string(r) + " cannot run (empty shard, null pointer or > 2^32-1 rows)");
+    if (r0[r] != expect) return fail(ctx, MVR_E_INVALID_ARGUMENT, "shards must be contiguous in rank order");
+    expect += rn[r];
+  }
+  if (expect != N_total) return fail(ctx, MVR_E_INVALID_ARGUMENT, "the shards do not add up to n_total");
+  if ((uint64_t)K >= N_total) return fail(ctx, MVR_E_INVALID_ARGUMENT, "sharded training needs n_total > 256");
+  if (N_total >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows");
+  auto m_lo = [&](int g) { return (int)((int64_t)M * g / G); };
+  const int m0 = m_lo(me), m1 = m_lo(me + 1), Ml = m1 - m0;
+
+  const bool timing = out.stats != nullptr;
+  if (timing) {
+    for (int e = 0; e < 4; ++e)
+      if (!ctx->ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ctx->ev[e]));
+    MVR_CUDA(ctx, cudaEventRecord(ctx->ev[3], st));
+  }
+
+  // ---- this rank's rows, subspace-major (kSlotAux1) ---------------------------
+  float* XT_loc = nullptr;
+  MVR_TRY(scratch(ctx, kSlotAux1, (size_t)M * N * S * sizeof(float), (void**)&XT_loc));
+  {
+    const int grid = (int)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 8);
+    switch (S) {
+      case 1: pq_transpose_kernel<1><<<grid, 256, 0, st>>>(job.R, N, D, M, XT_loc); break;
+      case 2: pq_transpose_kernel<2><<<grid, 256, 0, st>>>(job.R, N, D, M, XT_loc); break;
+      default: pq_transpose_kernel<4><<<grid, 256, 0, st>>>(job.R, N, D, M, XT_loc); break;
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+  }
+  // ---- engine workspace for the owned subspaces over all rows ----------------
+  const PqLayout L = pq_layout(N_total, std::max(Ml, 1), S, K, sms);
+  unsigned char* ws = nullptr;
+  MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
+  float* XT_own = (float*)(ws + L.o_xt);
+  uint32_t* asg_own = nullptr;
+  if (out.d_assign) MVR_TRY(scratch(ctx, kSlotAux0, (size_t)std::max(Ml, 1) * N_total * 4, (void**)&asg_own));
+  // exchange: subspace m of rank g's rows goes to the owner of m
+  const size_t col = (size_t)S * sizeof(float);
+  MVR_TRY(comm_group_start(ctx));
+  for (int h = 0; h < G; ++h) {
+    if (h == me) continue;
+    for (int m = m_lo(h); m < m_lo(h + 1); ++m) MVR_TRY(comm_send(ctx, XT_loc + (size_t)m * N * S, N * col, h));
+  }
+  for (int g = 0; g < G; ++g) {
+    if (g == me) continue;
+    for (int m = m0; m < m1; ++m)
+      MVR_TRY(comm_recv(ctx, XT_own + ((size_t)(m - m0) * N_total + r0[g]) * S, rn[g] * col, g));
+  }
+  MVR_TRY(comm_group_end(ctx));
+  for (int m = m0; m < m1; ++m)
+    MVR_CUDA(ctx, cudaMemcpyAsync(XT_own + ((size_t)(m - m0) * N_total + row0) * S, XT_loc + (size_t)m * N * S,
+                                  N * col, cudaMemcpyDeviceToDevice, st));
+
+  // ---- the one-GPU engine on the owned subspaces ----------------------------------
+  int status = MVR_OK;
+  int fail_m = M;
+  mvr_pq_train_stats local_stats{};
+  if (Ml > 0) {
+    PqJob j2 = job;
+    j2.R = nullptr;
+    j2.N = N_total;
+    j2.M = Ml;
+    j2.seed = job.seed + (uint64_t)m0;  // subspace m0 + i uses seed +% (m0 + i)
+    j2.xt_ready = true;
+    PqOut o2;
+    o2.d_codebooks = out.d_codebooks + (size_t)m0 * K * S;
+    o2.d_assign = asg_own;
+    o2.stats = timing ? &local_stats : nullptr;
+    std::vector<unsigned char> hsmall(L.small_bytes);
+    status = pq_kmeans_run(ctx, st, j2, o2, ws, hsmall.data(), sms);
+    if (status != MVR_OK) {
+      // the engine names the first failing local subspace in the message
+      const std::string& e = ctx->last_error;
+      const size_t p = e.find("subspace ");
+      fail_m = m0 + (p == std::string::npos ? 0 : std::atoi(e.c_str() + p + 9));
+      if (status == MVR_E_CUDA || status == MVR_E_OUT_OF_MEMORY) return status;  // no collective can follow safely
+    }
+  }
+  // ---- statuses: every rank returns the first failing subspace's status -----
+  {
+    int64_t* hs = (int64_t*)hp;
+    hs[0] = ((int64_t)fail_m << 32) | (uint32_t)status;
+    MVR_CUDA(ctx, cudaMemcpyAsync(dws + o_tab_send, hs, 8, cudaMemcpyHostToDevice, st));
+    MVR_TRY(comm_allgather(ctx, dws + o_tab_send, dws + o_stat, 8));
+    MVR_CUDA(ctx, cudaMemcpyAsync(hs, dws + o_stat, (size_t)G * 8, cudaMemcpyDeviceToHost, st));
+    MVR_CUDA(ctx, cudaStreamSynchronize(st));
+    int best_m = M, best_s = MVR_OK;
+    for (int r = 0; r < G; ++r) {
+      const int s_r = (int)(uint32_t)(hs[r] & 0xffffffff), m_r = (int)(hs[r] >> 32);
+      if (s_r != MVR_OK && m_r < best_m) {
+        best_m = m_r;
+        best_s = s_r;
+      }
+    }
+    if (best_s != MVR_OK)
+      return fail(ctx, best_s, std::string("subspace ") + std::to_string(best_m) + ": " + mvr_status_name(best_s));
+  }
+  // ---- codebooks to every rank; assignments back to the row owners -------------
+  const size_t cb_sub = (size_t)K * S * sizeof(float);
+  MVR_TRY(comm_group_start(ctx));
+  for (int g = 0; g < G; ++g) {
+    const int lo = m_lo(g), hi = m_lo(g + 1);
+    if (hi > lo) MVR_TRY(comm_broadcast(ctx, out.d_codebooks + (size_t)lo * K * S, (size_t)(hi - lo) * cb_sub, g));
+  }
+  MVR_TRY(comm_group_end(ctx));
+  if (out.d_assign) {
+    MVR_TRY(comm_group_start(ctx));
+    for (int h = 0; h < G; ++h) {
+      if (h == me) continue;
+      for (int m = m0; m < m1; ++m)
+        MVR_TRY(comm_send(ctx, asg_own + (size_t)(m - m0) * N_total + r0[h], rn[h] * 4, h));
+    }
+    for (int g = 0; g < G; ++g) {
+      if (g == me) continue;
+      for (int m = m_lo(g); m < m_lo(g + 1); ++m) MVR_TRY(comm_recv(ctx, out.d_assign + (size_t)m * N, N * 4, g));
+    }
+    MVR_TRY(comm_group_end(ctx));
+    for (int m = m0; m < m1; ++m)
+      MVR_CUDA(ctx, cudaMemcpyAsync(out.d_assign + (size_t)m * N, asg_own + (size_t)(m - m0) * N_total + row0, N * 4,
+                                    cudaMemcpyDeviceToDevice, st));
+  }
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  if (out.stats) {
+    *out.stats = local_stats;  // seeding / Lloyd / assign: this rank's engine
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ctx->ev[3], ctx->ev[2]);
+    out.stats->total_ms = t;  // exchange, engine and gather
   }
   return MVR_OK;
 }

@@ -23,6 +23,9 @@ struct PqJob {
   uint64_t seed = 0;  // subspace m uses seed + m
   uint32_t max_iters = 25;
   float tol = 1e-4f;
+  // the workspace's subspace-major copy XT (pq_layout o_xt) already holds the
+  // rows; R is then not read
+  bool xt_ready = false;
 };
 
 struct PqOut {
@@ -71,6 +74,14 @@ int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out);
 // first exchange) instead of leaving the other ranks waiting.
 int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_total, const PqOut& out,
                        bool local_ok);
+
+// Subspace-sharded training, the default for pq_m >= ranks: rank g owns a
+// contiguous range of subspaces, receives those columns of every row (one
+// grouped exchange), runs the one-GPU engine on them with seeds seed + m,
+// and the codebooks are gathered on every rank. Same contract as
+// pq_kmeans_run_dist.
+int pq_kmeans_run_subspaces(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_total, const PqOut& out,
+                            bool local_ok);
 
 // PQ.encode of N rows (asynchronous on the context stream).
 int pq_encode_device(Ctx* ctx, const float* d_codebooks, int D, int M,

@@ -23,11 +23,25 @@ from ir_multivector_retrieval_b200 import Context, dist as mdist, synth  # noqa:
 from ir_multivector_retrieval_b200._lib import PqTrainStats  # noqa: E402
 
 
+def reseed_data(trial: int, S: int):
+    """Seeded data whose Lloyd iterations empty a cluster (found by search):
+    pq.train with pq_m = 1, seed = trial, tol = 0."""
+    rng = np.random.default_rng(trial)
+    n = int(rng.integers(260, 2000))
+    return (rng.uniform(-1, 1, size=(n, S)) ** 5).astype(np.float32)
+
+
 def case_data(name):
+    if name == "reseed4":
+        return reseed_data(1247, 4), 4, 1
+    if name == "reseed2":
+        return reseed_data(2902, 2), 2, 1
     if name == "dup":  # heavy duplication: zero weights, ties, possible empty clusters
         rng = np.random.default_rng(3)
         base = synth.unit_rows(300, 32, seed=4)
         return base[rng.integers(0, 300, size=12_000)], 32, 16
+    if name == "m3":  # three subspaces: uneven subspace ranges over 2 or 4 ranks
+        return synth.unit_rows(20_000, 12, seed=5), 12, 3
     if name == "s2":
         return synth.unit_rows(30_001, 32, seed=9), 32, 16
     return synth.unit_rows(50_000, 64, seed=7), 64, 16
@@ -43,7 +57,10 @@ def main() -> int:
     mdist.init_comm(ctx)
     assert ctx.lib.mvr_ctx_comm_size(ctx.handle) == world
     failures = []
-    cases = [("s4", 8, -math.inf, False), ("s2", 25, 1e-4, False), ("dup", 25, 1e-4, False), ("s4", 3, -math.inf, True)]
+    # pq_m >= ranks: subspace-sharded; pq_m = 1 (the reseed data): row-sharded
+    cases = [("s4", 8, -math.inf, False), ("s2", 25, 1e-4, False), ("dup", 25, 1e-4, False), ("m3", 10, 1e-4, False),
+             ("reseed4", 25, 0.0, False), ("reseed2", 25, 0.0, False), ("s4", 3, -math.inf, True),
+             ("reseed2", 4, -math.inf, True)]
     for name, iters, tol, serial in cases:
         x, dim, pq_m = case_data(name)
         n_total = x.shape[0]
@@ -54,7 +71,8 @@ def main() -> int:
         d_asg = torch.empty(pq_m * nl, dtype=torch.int32, device="cuda")
         ctx.check(ctx.lib.mvr_ctx_set_serial_draws(ctx.handle, 1 if serial else 0))
         torch.cuda.synchronize()
-        st = mdist.train_sharded(ctx, d_rows.data_ptr(), nl, row0, n_total, dim, 11, pq_m=pq_m, max_iters=iters,
+        seed = {"reseed4": 1247, "reseed2": 2902}.get(name, 11)
+        st = mdist.train_sharded(ctx, d_rows.data_ptr(), nl, row0, n_total, dim, seed, pq_m=pq_m, max_iters=iters,
                                  tol=tol, d_codebooks_ptr=d_cb.data_ptr(), d_assign_ptr=d_asg.data_ptr())
         cb = d_cb.cpu().numpy()
         asg = d_asg.cpu().numpy().view(np.uint32).reshape(pq_m, nl)
@@ -73,7 +91,7 @@ def main() -> int:
             torch.cuda.synchronize()
             st1 = PqTrainStats()
             ctx1.check(ctx1.lib.mvr_pq_train_sharded_device(
-                ctx1.handle, C.c_void_p(d_full.data_ptr()), n_total, 0, n_total, dim, 11, 1, pq_m, iters,
+                ctx1.handle, C.c_void_p(d_full.data_ptr()), n_total, 0, n_total, dim, seed, 1, pq_m, iters,
                 C.c_float(tol), C.c_void_p(d_cb1.data_ptr()), C.c_void_p(d_asg1.data_ptr()), C.byref(st1)))
             cb1 = d_cb1.cpu().numpy()
             asg1 = d_asg1.cpu().numpy().view(np.uint32).reshape(pq_m, n_total)
@@ -84,6 +102,8 @@ def main() -> int:
                 failures.append(f"{name}: sharded codebooks != one-GPU codebooks")
             if not np.array_equal(np.concatenate(allasg, axis=1), asg1):
                 failures.append(f"{name}: sharded assignments != one-GPU assignments")
+            if name.startswith("reseed") and not (st["reseeds"] > 0 and st1.reseeds == st["reseeds"]):
+                failures.append(f"{name}: expected the same non-zero reseed count")
             print(f"[dist] {name} world={world} iters={iters} tol={tol} serial={serial} "
                   f"fallbacks={st['seed_fallbacks']} reseeds={st['reseeds']} iters_run={st['iters_max']} "
                   f"one_gpu_fallbacks={st1.seed_fallbacks} one_gpu_reseeds={st1.reseeds} "

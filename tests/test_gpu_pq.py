@@ -247,3 +247,20 @@ def test_encode_one_ulp_codewords(ctx, orc):
          + rng.standard_normal((50_000, 16, 4)).astype(np.float32) * np.float32(1e-3)).reshape(50_000, 64)
     got = pq.PQ(dim=64, sub_dim=4, codebooks=cb, pq_m=16, ctx=ctx).encode_batch(x)
     assert np.array_equal(got, orc.pq_encode(cb, 64, 16, x, n_threads=THREADS))
+
+
+@pytest.mark.parametrize("trial,S", [(1247, 4), (2902, 2), (612, 1)])
+def test_empty_cluster_reseed_matches_oracle(ctx, orc, trial, S):
+    """Seeded data whose Lloyd iterations empty a cluster (kmeans.zig:199-211):
+    pq.train with pq_m = 1 reseeds it exactly as the oracle does."""
+    rng = np.random.default_rng(trial)
+    n = int(rng.integers(260, 2000))
+    if trial == 612:
+        x = rng.standard_normal((n, S)).astype(np.float32)
+    else:
+        x = (rng.uniform(-1, 1, size=(n, S)) ** 5).astype(np.float32)
+    st = {}
+    got = pq.train(x, S, trial, pq_m=1, max_iters=25, tol=0.0, ctx=ctx, stats=st)
+    want = orc.pq_train(x, S, trial, 1, n_threads=THREADS, max_iters=25, tol=0.0)
+    assert st["reseeds"] >= 1
+    assert got.codebooks.tobytes() == want.tobytes()
