@@ -26,11 +26,12 @@ restatement of the reference timed on one host core.
 
 Multi-GPU (``--gpus N`` under torchrun, configs[2]): the same 1,521,797 rows
 are split into N contiguous shards, one per GPU, and ``pq.train`` runs
-row-sharded (``mvr_pq_train_sharded_device``: NCCL exchanges inside the
-library, codebooks byte-identical to the one-GPU run for any N;
-``codebook_sha256`` in the line lets runs at different N be compared);
-``pq.encode`` runs on each shard. Strong scaling: the total work is fixed;
-times are the max over ranks.
+sharded (``mvr_pq_train_sharded_device``): with 16 subspaces and N <= 16 each
+GPU trains 16/N whole subspaces over all rows after one NCCL column exchange,
+then the codebooks are gathered; codebooks are byte-identical to the one-GPU
+run for any N (``codebook_sha256`` in the line lets runs at different N be
+compared). ``pq.encode`` runs on each shard. Strong scaling: the total work
+is fixed; times are the max over ranks.
 """
 from __future__ import annotations
 
@@ -396,7 +397,8 @@ def run_b200(args) -> None:
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows": n_total, "rows_per_gpu": n, "dim": DIM, "pq_m": PQ_M,
                        "centroids": K, "lloyd_iters": ITERS,
-                       "parallelism": f"row-sharded over {world} GPUs (NCCL)" if world > 1 else "1gpu",
+                       "parallelism": (("subspace-sharded" if PQ_M >= world else "row-sharded")
+                                       + f" over {world} GPUs (NCCL)") if world > 1 else "1gpu",
                        "l2": "inputs (389 MB) > L2, no flush"},
             "codebook_sha256": mdist.codebook_digest(cb_host),
             "pq_train_ms": train_ms, "seed_ms": seed_ms, "lloyd_ms": lloyd_ms,

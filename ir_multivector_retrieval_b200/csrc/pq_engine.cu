@@ -2036,6 +2036,7 @@ int pq_kmeans_run_subspaces(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t 
     j2.R = nullptr;
     j2.N = N_total;
     j2.M = Ml;
+    j2.D = Ml * S;  // the rows are read from XT only
     j2.seed = job.seed + (uint64_t)m0;  // subspace m0 + i uses seed +% (m0 + i)
     j2.xt_ready = true;
     PqOut o2;
