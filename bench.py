@@ -442,9 +442,14 @@ def main() -> int:
     ap.add_argument("--cpu-target-s", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-tac", action="store_true", help="skip the clusterFlat measurement")
+    ap.add_argument("--tac-only", action="store_true",
+                    help="only the clusterFlat measurement (one GPU; for profiling captures)")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()
+    if args.tac_only:
+        print(json.dumps({"tac": measure_tac(make_corpus(args.rows), args.steps, cpu=not args.no_cpu)}), flush=True)
+        return 0
     if args.impl == "reference":
         run_reference(args)
     else:
