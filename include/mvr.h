@@ -116,7 +116,7 @@ int mvr_kmeans_fit(mvr_ctx* ctx, const float* vectors, uint64_t vectors_len,
 /* Largest row count and the size of the fixed device scratch of
  * `mvr_kmeans_fit_noalloc`. */
 #define MVR_NOALLOC_MAX_ROWS 65536u
-#define MVR_NOALLOC_SCRATCH_BYTES (3072u * 1024u)
+#define MVR_NOALLOC_SCRATCH_BYTES (4096u * 1024u)
 
 /* No counterpart in the reference: an extra entry point for hosts that
  * cannot let a library allocate GPU memory (their own allocator owns the
@@ -264,6 +264,12 @@ int mvr_tac_last_stats(const mvr_ctx* ctx, mvr_tac_stats* out);
  * chain (rng.zig:57-82) instead of the interval-bounded parallel search.
  * Results are identical either way; only the speed differs. */
 int mvr_ctx_set_serial_draws(mvr_ctx* ctx, int on);
+
+/* Verification mode (no reference counterpart): with `on` != 0 every Lloyd
+ * assignment of pq.train computes all K distances of every row instead of
+ * skipping rows whose exact distance bounds prove their cluster unchanged.
+ * Results are identical either way; only the speed differs. */
+int mvr_ctx_set_exhaustive_assign(mvr_ctx* ctx, int on);
 
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);

@@ -119,6 +119,7 @@ SIGNATURES = {
     "mvr_ctx_sync": (C.c_int, [_P]),
     "mvr_tac_last_stats": (C.c_int, [_P, C.POINTER(TacStats)]),
     "mvr_ctx_set_serial_draws": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),
     "mvr_ctx_init_comm": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_size_t]),

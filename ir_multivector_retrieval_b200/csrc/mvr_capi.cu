@@ -224,6 +224,12 @@ int mvr_ctx_set_serial_draws(mvr_ctx* h, int on) {
   return MVR_OK;
 }
 
+int mvr_ctx_set_exhaustive_assign(mvr_ctx* h, int on) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.exhaustive_assign = on != 0;
+  return MVR_OK;
+}
+
 int mvr_tac_last_stats(const mvr_ctx* h, mvr_tac_stats* out) {
   if (!h || !out) return MVR_E_INVALID_ARGUMENT;
   *out = h->impl.tac_stats;

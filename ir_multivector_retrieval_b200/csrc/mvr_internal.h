@@ -62,6 +62,8 @@ struct Ctx {
   Comm* comm = nullptr;
   // resolve every k-means++ draw with the reference's serial chain
   bool serial_draws = false;
+  // compute every Lloyd distance (no bound pruning)
+  bool exhaustive_assign = false;
 };
 
 // Host->device copy of a pageable host buffer through the pinned stages;

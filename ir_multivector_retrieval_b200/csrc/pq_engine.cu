@@ -117,6 +117,29 @@ pq_transpose_kernel(const float* __restrict__ R, uint64_t N, int D, int M, float
 }
 
 // ---------------------------------------------------------------------------
+// Exact Hamerly bounds for the Lloyd assignment. An f32 distance of an
+// S <= 4 sub-vector is within (1 +- g) of the exact squared distance,
+// g = 2^-21 (at most six roundings of 2^-24 each touch any term). From the
+// winner's distance `best` and the runner-up's `sec`:
+//   ub = sqrt(best) / sqrt(1 - g)  >= the exact distance to the winner,
+//   lb = sqrt(sec)  / sqrt(1 + g)  <= the exact distance to every other,
+// rounded outwards. After a centroid update with drifts d_c (rounded up),
+// ub += d_a and lb -= max_c d_c keep both true (triangle inequality). When
+// ub * (1 + 2^-18) < lb and lb >= 2^-60, the winner's f32 distance is
+// strictly below every other f32 distance (the factor covers
+// sqrt((1+g)/(1-g)) and leaves an absolute margin far above subnormal
+// rounding), so the reference's first-index argmin is still the winner and
+// the row's distances need not be computed.
+// ---------------------------------------------------------------------------
+constexpr float kUbScale = 1.0f + 0x1p-21f;      // >= 1 / sqrt(1 - 2^-21)
+constexpr float kLbScale = 1.0f - 0x1p-21f;      // <= 1 / sqrt(1 + 2^-21)
+constexpr float kPruneMargin = 1.0f + 0x1p-18f;
+constexpr float kLbMin = 0x1p-60f;
+
+__device__ __forceinline__ float bound_upper(float best) { return __fmul_ru(__fsqrt_ru(best), kUbScale); }
+__device__ __forceinline__ float bound_lower(float sec) { return __fmul_rd(__fsqrt_rd(sec), kLbScale); }
+
+// ---------------------------------------------------------------------------
 // Assignment / encode. Persistent CTAs: CTA b owns rows
 // [b*rows_per_cta, (b+1)*rows_per_cta), processed kAsgTile at a time, one
 // thread per kPtsPerThread rows across all M subspaces. The M codebooks sit
@@ -125,12 +148,13 @@ pq_transpose_kernel(const float* __restrict__ R, uint64_t N, int D, int M, float
 // assignments, min distances and the CTA's cluster histogram; encode mode
 // reads R and writes codes.
 // ---------------------------------------------------------------------------
-template <int S, int MODE>
+template <int S, int MODE, bool BOUNDS>
 __global__ void __launch_bounds__(kAsgThreads, 2)
 pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint64_t N, int D,
                  int M, int K, const float* __restrict__ cb, uint8_t* __restrict__ codes,
                  uint8_t* __restrict__ asg, float* __restrict__ mind, uint32_t* __restrict__ hist,
-                 const uint8_t* __restrict__ state, float one, uint64_t rows_per_cta) {
+                 const uint8_t* __restrict__ state, float one, uint64_t rows_per_cta,
+                 float* __restrict__ ubnd, float* __restrict__ lbnd) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int KP = (K + 1) >> 1;
   float2* cbp = reinterpret_cast<float2*>(smem_raw);  // [M][KP][S]
@@ -181,11 +205,12 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
 #pragma unroll
         for (int k = 0; k < S; ++k) xx[j][k] = make_float2(x[k], x[k]);
       }
-      float best[kPtsPerThread], d0[kPtsPerThread];
+      float best[kPtsPerThread], d0[kPtsPerThread], sec[kPtsPerThread];
       int bi[kPtsPerThread];
 #pragma unroll
       for (int j = 0; j < kPtsPerThread; ++j) {
         best[j] = __int_as_float(0x7f800000);
+        sec[j] = __int_as_float(0x7f800000);
         bi[j] = 0;
         d0[j] = 0.f;
       }
@@ -198,8 +223,13 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
         for (int j = 0; j < kPtsPerThread; ++j) {
           const float2 dd = l2_small_pair<S>(xx[j], nc, one2);
           if (p == 0) d0[j] = dd.x;
-          if (dd.x < best[j]) { best[j] = dd.x; bi[j] = 2 * p; }
-          if (dd.y < best[j]) { best[j] = dd.y; bi[j] = 2 * p + 1; }
+          if (BOUNDS) {  // also the second smallest distance (a tie makes it equal the best)
+            if (dd.x < best[j]) { sec[j] = best[j]; best[j] = dd.x; bi[j] = 2 * p; } else { sec[j] = fminf(sec[j], dd.x); }
+            if (dd.y < best[j]) { sec[j] = best[j]; best[j] = dd.y; bi[j] = 2 * p + 1; } else { sec[j] = fminf(sec[j], dd.y); }
+          } else {
+            if (dd.x < best[j]) { best[j] = dd.x; bi[j] = 2 * p; }
+            if (dd.y < best[j]) { best[j] = dd.y; bi[j] = 2 * p + 1; }
+          }
         }
       }
 #pragma unroll
@@ -211,6 +241,10 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
             asg[(size_t)m * N + row[j]] = (uint8_t)bi[j];
             mind[(size_t)m * N + row[j]] = best[j];
             atomicAdd(&h[m * K + bi[j]], 1u);
+            if (BOUNDS) {
+              ubnd[(size_t)m * N + row[j]] = bound_upper(best[j]);
+              lbnd[(size_t)m * N + row[j]] = isnan(d0[j]) ? -__int_as_float(0x7f800000) : bound_lower(sec[j]);
+            }
           }
         } else if (ok[j]) {
           packed[j] |= (uint32_t)bi[j] << (8 * (m & 3));
@@ -235,6 +269,242 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
       const int m = e / K, c = e % K;
       hist[((size_t)m * nblk + blockIdx.x) * K + c] = h[e];
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pruned Lloyd iterations (after the first): drift of every centroid, a check
+// pass that keeps rows whose bounds prove the winner unchanged and lists the
+// others per subspace, a dense pass over the lists, and the per-CTA cluster
+// histograms of all rows for the stable sort.
+// ---------------------------------------------------------------------------
+// drift[m][c] >= |c_new - c_old| (exact Euclidean, rounded up). maxd[m] =
+// (largest drift, its centroid, second largest) as floats: a row's lower
+// bound drops by the largest drift among the centroids other than its own.
+__global__ void __launch_bounds__(256)
+pq_drift_kernel(const float* __restrict__ cb_old, const float* __restrict__ cb, int M, int K, int S,
+                const uint8_t* __restrict__ state, float* __restrict__ drift, float* __restrict__ maxd) {
+  const int m = blockIdx.x;
+  if (state[m] != kRunning) return;
+  __shared__ float sd[256];
+  for (int c = threadIdx.x; c < 256; c += blockDim.x) sd[c] = 0.f;
+  __syncthreads();
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    double d2 = 0.0;
+    for (int k = 0; k < S; ++k) {
+      const double a = cb[((size_t)m * K + c) * S + k], b = cb_old[((size_t)m * K + c) * S + k];
+      const double hi = __dsub_ru(a, b), lo = __dsub_rd(a, b);
+      const double t = fmax(fabs(hi), fabs(lo));  // >= |a - b|
+      d2 = __dadd_ru(d2, __dmul_ru(t, t));
+    }
+    const float d = __double2float_ru(__dsqrt_ru(d2));
+    drift[(size_t)m * K + c] = d;
+    sd[c] = d;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m1 = 0.f, m2 = 0.f;
+    int i1 = -1;
+    for (int c = 0; c < K; ++c) {
+      const float d = sd[c];
+      if (d > m1) { m2 = m1; m1 = d; i1 = c; } else if (d > m2) { m2 = d; }
+    }
+    maxd[3 * m] = m1;
+    maxd[3 * m + 1] = (float)i1;
+    maxd[3 * m + 2] = m2;
+  }
+}
+
+// Row r of subspace m (blockIdx.y): bounds moved by the drifts; a row whose
+// bounds still prove its winner keeps it (and, if need_mind, gets its f32
+// distance to it); every other row is appended to list[m]. One atomic per
+// CTA pass reserves the pass's list segment (warp offsets from a block scan).
+template <int S>
+__global__ void __launch_bounds__(256)
+pq_prune_check_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __restrict__ cb,
+                      const uint8_t* __restrict__ asg, float* __restrict__ ubnd, float* __restrict__ lbnd,
+                      const float* __restrict__ drift, const float* __restrict__ maxd,
+                      const uint8_t* __restrict__ state, uint32_t* __restrict__ list,
+                      uint32_t* __restrict__ list_cnt, float* __restrict__ mind, int need_mind) {
+  __shared__ uint32_t wcnt[8], wbase[8], bbase;
+  const int m = blockIdx.y;
+  if (state[m] != kRunning) return;
+  const float md1 = maxd[3 * m], md2 = maxd[3 * m + 2];
+  const uint32_t mi1 = (uint32_t)(int)maxd[3 * m + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < N; base += stride) {
+    const uint64_t r = base + threadIdx.x;
+    const bool ok = r < N;
+    bool keep = false;
+    if (ok) {
+      const size_t e = (size_t)m * N + r;
+      const uint32_t a = asg[e];
+      const float u = __fadd_ru(ubnd[e], drift[(size_t)m * K + a]);
+      const float l = __fsub_rd(lbnd[e], a == mi1 ? md2 : md1);
+      keep = l >= kLbMin && __fmul_ru(u, kPruneMargin) < l;
+      if (keep) {
+        ubnd[e] = u;
+        lbnd[e] = l;
+        if (need_mind) {
+          float x[S], c[S];
+          load_sub<S>(XT + e * S, x);
+#pragma unroll
+          for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + a) * S + k];
+          mind[e] = l2_small<S>(x, c);
+        }
+      }
+    }
+    const uint32_t need = __ballot_sync(0xffffffffu, ok && !keep);
+    if (lane == 0) wcnt[warp] = (uint32_t)__popc(need);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < 8; ++w) {
+        wbase[w] = t;
+        t += wcnt[w];
+      }
+      bbase = t ? atomicAdd(&list_cnt[m], t) : 0u;
+    }
+    __syncthreads();
+    if (ok && !keep) list[(size_t)m * N + bbase + wbase[warp] + __popc(need & lanemask_lt())] = (uint32_t)r;
+    __syncthreads();  // wcnt / wbase / bbase are reused by the next pass
+  }
+}
+
+// Dense assignment of the listed rows: work units of kAsgTile rows of one
+// subspace (all M codebooks in shared memory, as in pq_assign_kernel).
+template <int S>
+__global__ void __launch_bounds__(kAsgThreads, 2)
+pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, const float* __restrict__ cb,
+                      const uint32_t* __restrict__ list, const uint32_t* __restrict__ list_cnt,
+                      uint8_t* __restrict__ asg, float* __restrict__ mind, float* __restrict__ ubnd,
+                      float* __restrict__ lbnd, const uint8_t* __restrict__ state, float one) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint32_t upre[kMaxM + 1];
+  const int KP = (K + 1) >> 1;
+  float2* cbp = reinterpret_cast<float2*>(smem_raw);  // [M][KP][S]
+  for (int e = threadIdx.x; e < M * KP * S; e += kAsgThreads) {
+    const int k = e % S;
+    const int p = (e / S) % KP;
+    const int m = e / (S * KP);
+    const int ca = 2 * p, cbi = 2 * p + 1;
+    const float a = cb[((size_t)m * K + ca) * S + k];
+    const float b = cbi < K ? cb[((size_t)m * K + cbi) * S + k] : f32_nan();
+    cbp[e] = make_float2(-a, -b);
+  }
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (int m = 0; m < M; ++m) {
+      upre[m] = acc;
+      acc += state[m] == kRunning ? (list_cnt[m] + kAsgTile - 1) / kAsgTile : 0u;
+    }
+    upre[M] = acc;
+  }
+  __syncthreads();
+  const float2 one2 = make_float2(one, one);
+  const uint32_t units = upre[M];
+  for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+    int m = 0;
+    while (upre[m + 1] <= u) ++m;
+    const uint32_t i0 = (u - upre[m]) * kAsgTile, cnt = list_cnt[m];
+    uint64_t row[kPtsPerThread];
+    bool ok[kPtsPerThread];
+    float2 xx[kPtsPerThread][S];
+#pragma unroll
+    for (int j = 0; j < kPtsPerThread; ++j) {
+      const uint32_t i = i0 + (uint32_t)j * kAsgThreads + threadIdx.x;
+      ok[j] = i < cnt;
+      row[j] = ok[j] ? list[(size_t)m * N + i] : 0;
+      float x[S];
+      if (ok[j]) {
+        load_sub<S>(XT + ((size_t)m * N + row[j]) * S, x);
+      } else {
+#pragma unroll
+        for (int k = 0; k < S; ++k) x[k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < S; ++k) xx[j][k] = make_float2(x[k], x[k]);
+    }
+    if (!__any_sync(0xffffffffu, ok[0] || ok[kPtsPerThread - 1])) continue;
+    float best[kPtsPerThread], sec[kPtsPerThread], d0[kPtsPerThread];
+    int bi[kPtsPerThread];
+#pragma unroll
+    for (int j = 0; j < kPtsPerThread; ++j) {
+      best[j] = __int_as_float(0x7f800000);
+      sec[j] = __int_as_float(0x7f800000);
+      bi[j] = 0;
+      d0[j] = 0.f;
+    }
+    const float2* cm = cbp + (size_t)m * KP * S;
+    for (int p = 0; p < KP; ++p) {
+      float2 nc[S];
+#pragma unroll
+      for (int k = 0; k < S; ++k) nc[k] = cm[p * S + k];
+#pragma unroll
+      for (int j = 0; j < kPtsPerThread; ++j) {
+        const float2 dd = l2_small_pair<S>(xx[j], nc, one2);
+        if (p == 0) d0[j] = dd.x;
+        if (dd.x < best[j]) { sec[j] = best[j]; best[j] = dd.x; bi[j] = 2 * p; } else { sec[j] = fminf(sec[j], dd.x); }
+        if (dd.y < best[j]) { sec[j] = best[j]; best[j] = dd.y; bi[j] = 2 * p + 1; } else { sec[j] = fminf(sec[j], dd.y); }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPtsPerThread; ++j) {
+      if (isnan(d0[j])) { bi[j] = 0; best[j] = d0[j]; }
+      if (ok[j]) {
+        const size_t e = (size_t)m * N + row[j];
+        asg[e] = (uint8_t)bi[j];
+        mind[e] = best[j];
+        ubnd[e] = bound_upper(best[j]);
+        lbnd[e] = isnan(d0[j]) ? -__int_as_float(0x7f800000) : bound_lower(sec[j]);
+      }
+    }
+  }
+}
+
+// Per-CTA cluster histograms of all rows (the row ranges of pq_assign_kernel).
+__global__ void __launch_bounds__(512)
+pq_hist_kernel(const uint8_t* __restrict__ asg, uint64_t N, int M, int K, const uint8_t* __restrict__ state,
+               uint64_t rows_per_cta, uint32_t* __restrict__ hist) {
+  extern __shared__ uint32_t hh[];  // [M][K]
+  for (int e = threadIdx.x; e < M * K; e += blockDim.x) hh[e] = 0;
+  __syncthreads();
+  const uint64_t lo = (uint64_t)blockIdx.x * rows_per_cta, hi = min(N, lo + rows_per_cta);
+  for (int m = 0; m < M; ++m) {
+    if (state[m] != kRunning) continue;
+    const uint8_t* a = asg + (size_t)m * N;
+    for (uint64_t r = lo + threadIdx.x; r < hi; r += blockDim.x) atomicAdd(&hh[m * K + a[r]], 1u);
+  }
+  __syncthreads();
+  const int nblk = gridDim.x;
+  for (int e = threadIdx.x; e < M * K; e += blockDim.x) {
+    const int m = e / K, c = e % K;
+    hist[((size_t)m * nblk + blockIdx.x) * K + c] = hh[e];
+  }
+}
+
+// Before an empty-cluster reseed: f32 distances of every row to its winner
+// (rows kept by their bounds have no fresh value). Subspaces without an
+// empty cluster leave at once.
+template <int S>
+__global__ void __launch_bounds__(256)
+pq_mind_refresh_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __restrict__ cb,
+                       const uint8_t* __restrict__ asg, const uint32_t* __restrict__ counts,
+                       const uint8_t* __restrict__ state, float* __restrict__ mind) {
+  const int m = blockIdx.y;
+  if (state[m] != kRunning) return;
+  const bool empty = threadIdx.x < (unsigned)K && counts[(size_t)m * K + threadIdx.x] == 0;
+  if (!__syncthreads_or(empty)) return;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < N; r += stride) {
+    const size_t e = (size_t)m * N + r;
+    const uint32_t a = asg[e];
+    float x[S], c[S];
+    load_sub<S>(XT + e * S, x);
+#pragma unroll
+    for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + a) * S + k];
+    mind[e] = l2_small<S>(x, c);
   }
 }
 
@@ -928,16 +1198,24 @@ size_t assign_smem(int M, int K, int S, int mode) {
 template <int S>
 int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, const float* XT, uint64_t N,
                   int D, int M, int K, const float* cb, uint8_t* codes, uint8_t* asg, float* mind,
-                  uint32_t* hist, const uint8_t* state, int nblk, uint64_t rows_per_cta) {
+                  uint32_t* hist, const uint8_t* state, int nblk, uint64_t rows_per_cta,
+                  float* ubnd = nullptr, float* lbnd = nullptr) {
   const size_t sm = assign_smem(M, K, S, mode);
-  if (mode == kModeLloyd) {
-    auto kern = pq_assign_kernel<S, kModeLloyd>;
+  if (mode == kModeLloyd && ubnd) {
+    auto kern = pq_assign_kernel<S, kModeLloyd, true>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta);
+    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
+                                        ubnd, lbnd);
+  } else if (mode == kModeLloyd) {
+    auto kern = pq_assign_kernel<S, kModeLloyd, false>;
+    MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
+                                        nullptr, nullptr);
   } else {
-    auto kern = pq_assign_kernel<S, kModeEncode>;
+    auto kern = pq_assign_kernel<S, kModeEncode, false>;
     MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta);
+    kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
+                                        nullptr, nullptr);
   }
   MVR_CUDA(ctx, cudaGetLastError());
   return MVR_OK;
@@ -1390,6 +1668,13 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_hist = carve((size_t)M * L.nblk * K * sizeof(uint32_t));
   L.o_chunk = carve((size_t)M * L.nchunk * sizeof(double2));
   L.o_chunk_cnt = carve((size_t)M * L.nchunk * sizeof(uint32_t));
+  L.o_ub = carve((size_t)M * N * sizeof(float));
+  L.o_lb = carve((size_t)M * N * sizeof(float));
+  L.o_list = carve((size_t)M * N * sizeof(uint32_t));
+  L.o_lcnt = carve((size_t)M * sizeof(uint32_t));
+  L.o_cbold = carve((size_t)M * K * S * sizeof(float));
+  L.o_drift = carve((size_t)M * K * sizeof(float));
+  L.o_maxd = carve((size_t)M * 3 * sizeof(float));
   L.total_bytes = off;
   return L;
 }
@@ -1514,16 +1799,52 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         if (e) cudaEventDestroy(e);
     }
   } ev_guard{aev};
+  // Bound pruning (Hamerly) from the second iteration on; exact, see
+  // bound_upper / bound_lower.
+  const bool prune = !(ctx && ctx->exhaustive_assign);
+  float* ubnd = (float*)(ws + L.o_ub);
+  float* lbnd = (float*)(ws + L.o_lb);
+  uint32_t* plist = (uint32_t*)(ws + L.o_list);
+  uint32_t* lcnt = (uint32_t*)(ws + L.o_lcnt);
+  float* cb_old = (float*)(ws + L.o_cbold);
+  float* drift = (float*)(ws + L.o_drift);
+  float* maxd = (float*)(ws + L.o_maxd);
+  const unsigned pgx = (unsigned)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 4);
+  const size_t list_smem = assign_smem(M, K, S, kModeEncode);  // the codebooks only
   for (uint32_t it = 0; it < job.max_iters; ++it) {
+    const bool last = it + 1 == job.max_iters;
+    const bool need_mind = check || (last && out.h_wcss);
     if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it], st));
-    switch (S) {
-      case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
-      case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
-      default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
+    if (!prune || it == 0) {
+      float* ub_o = prune ? ubnd : nullptr;
+      float* lb_o = prune ? lbnd : nullptr;
+      switch (S) {
+        case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
+        case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
+        default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
+      }
+    } else {
+      pq_drift_kernel<<<M, 256, 0, st>>>(cb_old, cb, M, K, S, d_state, drift, maxd);
+      MVR_CUDA(ctx, cudaMemsetAsync(lcnt, 0, (size_t)M * sizeof(uint32_t), st));
+      const dim3 cg(pgx, (unsigned)M);
+      switch (S) {
+        case 1: pq_prune_check_kernel<1><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, ubnd, lbnd, drift, maxd, d_state, plist, lcnt, mind, need_mind ? 1 : 0); break;
+        case 2: pq_prune_check_kernel<2><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, ubnd, lbnd, drift, maxd, d_state, plist, lcnt, mind, need_mind ? 1 : 0); break;
+        default: pq_prune_check_kernel<4><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, ubnd, lbnd, drift, maxd, d_state, plist, lcnt, mind, need_mind ? 1 : 0); break;
+      }
+      MVR_CUDA(ctx, cudaGetLastError());
+      switch (S) {
+        case 1: { auto k = pq_assign_list_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+        case 2: { auto k = pq_assign_list_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+        default: { auto k = pq_assign_list_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+      }
+      MVR_CUDA(ctx, cudaGetLastError());
+      pq_hist_kernel<<<nblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, rpc, hist);
+      MVR_CUDA(ctx, cudaGetLastError());
+      launches += 5;
     }
     if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
     launches += 5;
-    const bool last = it + 1 == job.max_iters;
     if (check || (last && out.h_wcss)) {
       pq_wcss_kernel<<<M, 256, 0, st>>>(mind, N, d_wcss, d_state, nullptr);
       MVR_CUDA(ctx, cudaGetLastError());
@@ -1531,6 +1852,17 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     }
     pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
+    if (prune && it > 0 && !need_mind) {  // kept rows have no fresh distance: refresh where a reseed follows
+      const dim3 cg(pgx, (unsigned)M);
+      switch (S) {
+        case 1: pq_mind_refresh_kernel<1><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, d_counts, d_state, mind); break;
+        case 2: pq_mind_refresh_kernel<2><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, d_counts, d_state, mind); break;
+        default: pq_mind_refresh_kernel<4><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, d_counts, d_state, mind); break;
+      }
+      MVR_CUDA(ctx, cudaGetLastError());
+      ++launches;
+    }
+    if (prune) MVR_CUDA(ctx, cudaMemcpyAsync(cb_old, cb, (size_t)M * K * S * sizeof(float), cudaMemcpyDeviceToDevice, st));
     switch (S) {
       case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
       case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;

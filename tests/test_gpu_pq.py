@@ -264,3 +264,22 @@ def test_empty_cluster_reseed_matches_oracle(ctx, orc, trial, S):
     want = orc.pq_train(x, S, trial, 1, n_threads=THREADS, max_iters=25, tol=0.0)
     assert st["reseeds"] >= 1
     assert got.codebooks.tobytes() == want.tobytes()
+
+
+def test_bound_pruning_matches_exhaustive(ctx, orc):
+    """Lloyd iterations that skip rows by their distance bounds give the same
+    bytes as computing every distance, and as the oracle (fixed iterations,
+    tolerance mode and a reseeding case)."""
+    x = _rows(40_000, 32, 21)
+    for iters, tol in ((20, -math.inf), (25, 1e-4)):
+        st_p, st_e = {}, {}
+        pruned = pq.train(x, 32, 5, pq_m=8, max_iters=iters, tol=tol, ctx=ctx, stats=st_p)
+        ctx.check(ctx.lib.mvr_ctx_set_exhaustive_assign(ctx.handle, 1))
+        try:
+            full = pq.train(x, 32, 5, pq_m=8, max_iters=iters, tol=tol, ctx=ctx, stats=st_e)
+        finally:
+            ctx.check(ctx.lib.mvr_ctx_set_exhaustive_assign(ctx.handle, 0))
+        assert pruned.codebooks.tobytes() == full.codebooks.tobytes()
+        assert st_p["iters_max"] == st_e["iters_max"]
+        want = orc.pq_train(x, 32, 5, 8, n_threads=THREADS, max_iters=iters, tol=tol)
+        assert pruned.codebooks.tobytes() == want.tobytes()
