@@ -59,6 +59,7 @@ enum {
   MVR_E_LENGTH_MISMATCH = 15,        /* vec.VecError.LengthMismatch */
   MVR_E_EMPTY_INPUT = 16,            /* vec.VecError.EmptyInput */
   MVR_E_OUT_OF_MEMORY = 17,          /* Allocator.Error.OutOfMemory (host or device) */
+  MVR_E_BUFFER_TOO_SMALL = 18,       /* storage.StorageError.BufferTooSmall */
   /* B200-side failures with no reference counterpart */
   MVR_E_CUDA = 100,             /* a CUDA runtime call failed */
   MVR_E_NCCL = 101,             /* an NCCL call failed */
@@ -163,6 +164,10 @@ typedef struct mvr_pq_train_stats {
   double assign_ms;      /* summed device time of the Lloyd assignment kernel */
   uint32_t assign_launches; /* launches of that kernel */
   uint32_t launches;     /* all kernel launches of the call */
+  double assign_first_ms;   /* the first Lloyd assignment (every distance computed) */
+  uint64_t lloyd_rows_total; /* (row, subspace) assignments over all Lloyd iterations */
+  uint64_t lloyd_rows_exact; /* of those, the ones whose K distances were all computed
+                                (the rest kept their cluster by exact bounds) */
 } mvr_pq_train_stats;
 
 /* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`
@@ -236,6 +241,38 @@ int mvr_pq_train_sharded_device(mvr_ctx* ctx, const float* d_rows,
                                 uint32_t max_iters, float tol,
                                 float* d_codebooks_out, uint32_t* d_assign_out,
                                 mvr_pq_train_stats* stats);
+
+/* ---- .tac per-doc payload (storage.zig:705-749) -------------------------- */
+
+/* Bytes of the per-doc section of a .tac file: the doc index
+ * ((n_docs + 1) u64 payload offsets) followed by, per doc d with
+ * n_d = doc_offsets[d+1] - doc_offsets[d] tokens,
+ * [n_d u32 | n_d assignment u32 | n_d * pq_m code bytes | zero pad to 8]
+ * (storage.zig:506-508, docPayloadSize). `doc_offsets` is host memory. */
+int mvr_doc_layouts_bytes(const uint64_t* doc_offsets, uint64_t n_docs,
+                          uint32_t pq_m, uint64_t* bytes_out);
+
+/* Replaces storage.writeDocLayouts (src/index/storage.zig:705-749): writes
+ * the section above into `out` (out_len bytes; BufferTooSmall when short).
+ * `doc_offsets` (n_docs + 1 u64, non-decreasing, last = n_tokens) is host
+ * memory; `assignments` (n_tokens u32, TAC centroid ids), `codes`
+ * (n_tokens * pq_m bytes, token-major) and `out` are host memory here and
+ * device memory in the _device variant (asynchronous on the context
+ * stream). The bytes are identical to the reference's. */
+int mvr_write_doc_layouts(mvr_ctx* ctx, const uint64_t* doc_offsets,
+                          uint64_t n_docs, const uint32_t* assignments,
+                          const uint8_t* codes, uint64_t n_tokens,
+                          uint32_t pq_m, uint8_t* out, uint64_t out_len);
+int mvr_write_doc_layouts_device(mvr_ctx* ctx, const uint64_t* doc_offsets,
+                                 uint64_t n_docs, const uint32_t* d_assignments,
+                                 const uint8_t* d_codes, uint64_t n_tokens,
+                                 uint32_t pq_m, uint8_t* d_out,
+                                 uint64_t out_len);
+
+/* CRC-32 of the .tac footer (std.hash.Crc32: reflected polynomial
+ * 0xEDB88320, initial and final xor 0xFFFFFFFF, as zlib's crc32), over
+ * host memory; `crc` continues a previous value (0 to start). */
+uint32_t mvr_crc32(uint32_t crc, const void* data, uint64_t len);
 
 /* Timing report of the most recent `mvr_tac_cluster_flat` call on the
  * context (no reference counterpart; the reference prints `[stage]` lines,

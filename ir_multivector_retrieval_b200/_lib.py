@@ -35,6 +35,7 @@ STATUS_NAMES = {
     15: "LengthMismatch",
     16: "EmptyInput",
     17: "OutOfMemory",
+    18: "BufferTooSmall",
     100: "CudaError",
     101: "NcclError",
     102: "Timeout",
@@ -66,6 +67,9 @@ class PqTrainStats(C.Structure):
         ("assign_ms", C.c_double),
         ("assign_launches", C.c_uint32),
         ("launches", C.c_uint32),
+        ("assign_first_ms", C.c_double),
+        ("lloyd_rows_total", C.c_uint64),
+        ("lloyd_rows_exact", C.c_uint64),
     ]
 
 
@@ -119,6 +123,10 @@ SIGNATURES = {
     "mvr_ctx_sync": (C.c_int, [_P]),
     "mvr_tac_last_stats": (C.c_int, [_P, C.POINTER(TacStats)]),
     "mvr_ctx_set_serial_draws": (C.c_int, [_P, C.c_int]),
+    "mvr_doc_layouts_bytes": (C.c_int, [_P, C.c_uint64, C.c_uint32, C.POINTER(C.c_uint64)]),
+    "mvr_write_doc_layouts": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
+    "mvr_write_doc_layouts_device": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
+    "mvr_crc32": (C.c_uint32, [C.c_uint32, _P, C.c_uint64]),
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),

@@ -158,6 +158,7 @@ const char* mvr_status_name(int s) {
     case MVR_E_LENGTH_MISMATCH: return "LengthMismatch";
     case MVR_E_EMPTY_INPUT: return "EmptyInput";
     case MVR_E_OUT_OF_MEMORY: return "OutOfMemory";
+    case MVR_E_BUFFER_TOO_SMALL: return "BufferTooSmall";
     case MVR_E_CUDA: return "CudaError";
     case MVR_E_NCCL: return "NcclError";
     case MVR_E_TIMEOUT: return "Timeout";

@@ -353,6 +353,20 @@ pq_prune_check_kernel(const float* __restrict__ XT, uint64_t N, int K, const flo
           for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + a) * S + k];
           mind[e] = l2_small<S>(x, c);
         }
+      } else if (l >= kLbMin) {
+        // the drifts loosened ub: one exact distance to the winner tightens it
+        float x[S], c[S];
+        load_sub<S>(XT + e * S, x);
+#pragma unroll
+        for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + a) * S + k];
+        const float da = l2_small<S>(x, c);
+        const float ut = bound_upper(da);
+        if (__fmul_ru(ut, kPruneMargin) < l) {
+          keep = true;
+          ubnd[e] = ut;
+          lbnd[e] = l;
+          mind[e] = da;
+        }
       }
     }
     const uint32_t need = __ballot_sync(0xffffffffu, ok && !keep);
@@ -817,7 +831,8 @@ pq_reseed_converge_kernel(const float* __restrict__ XT, uint64_t N, int S, int K
                           float* __restrict__ cb, uint8_t* __restrict__ state,
                           const float* __restrict__ wcss, float* __restrict__ prev_wcss,
                           uint32_t* __restrict__ iters_run, uint32_t* __restrict__ reseeds,
-                          int iter, int check, float tol, int do_reseed) {
+                          int iter, int check, float tol, int do_reseed,
+                          const uint32_t* __restrict__ list_cnt, unsigned long long* __restrict__ exact) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   __shared__ int any_empty;
@@ -844,6 +859,8 @@ pq_reseed_converge_kernel(const float* __restrict__ XT, uint64_t N, int S, int K
   }
   if (threadIdx.x == 0) {
     iters_run[m] = (uint32_t)iter + 1;
+    // rows of this iteration whose distances were all computed (stats)
+    if (exact) exact[m] += list_cnt ? list_cnt[m] : N;
     if (check) {
       const float w = wcss[m];
       if (iter > 0) {
@@ -1659,6 +1676,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_iters = carve((size_t)M * 4);
   L.o_fb = carve((size_t)M * 4);
   L.o_rs = carve((size_t)M * 4);
+  L.o_exact = carve((size_t)M * 8);
   L.o_state = carve((size_t)M);
   L.small_bytes = off;
   L.o_xt = carve((size_t)M * N * S * sizeof(float));
@@ -1735,6 +1753,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   uint32_t* d_iters = (uint32_t*)(small + L.o_iters);
   uint32_t* d_fb = (uint32_t*)(small + L.o_fb);
   uint32_t* d_rs = (uint32_t*)(small + L.o_rs);
+  unsigned long long* d_exact = (unsigned long long*)(small + L.o_exact);
   uint8_t* d_state = (uint8_t*)(small + L.o_state);
 
   // ---- host RNG draws (data independent); thresholds start at +inf; the
@@ -1875,7 +1894,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
     }
     pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, d_counts, mind, cb, d_state, d_wcss, d_prev,
-                                                  d_iters, d_rs, (int)it, check ? 1 : 0, job.tol, 1);
+                                                  d_iters, d_rs, (int)it, check ? 1 : 0, job.tol, 1,
+                                                  (prune && it > 0) ? lcnt : nullptr, d_exact);
     MVR_CUDA(ctx, cudaGetLastError());
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
@@ -1917,10 +1937,20 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       }
       out.stats->assign_ms = am;
       out.stats->assign_launches = job.max_iters;
+      if (job.max_iters > 0) {
+        float t0 = 0.f;
+        cudaEventElapsedTime(&t0, aev[0], aev[1]);
+        out.stats->assign_first_ms = t0;
+      }
     }
     uint32_t mx = 0, mn = UINT32_MAX, fb = 0, rs = 0;
     const uint32_t* hfb = (const uint32_t*)(hsmall + L.o_fb);
     const uint32_t* hrs = (const uint32_t*)(hsmall + L.o_rs);
+    const unsigned long long* hex = (const unsigned long long*)(hsmall + L.o_exact);
+    for (int m = 0; m < M; ++m) {
+      out.stats->lloyd_rows_exact += hex[m];
+      out.stats->lloyd_rows_total += (uint64_t)(job.max_iters ? hiters[m] : 0) * N;
+    }
     for (int m = 0; m < M; ++m) {
       const uint32_t v = job.max_iters ? hiters[m] : 0;
       mx = std::max(mx, v);
@@ -2218,7 +2248,7 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
       ++launches;
     }
     pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, gcounts, mind, cb, d_state, d_wcss, d_prev, d_iters,
-                                                  d_rs, (int)it, check ? 1 : 0, job.tol, 0);
+                                                  d_rs, (int)it, check ? 1 : 0, job.tol, 0, nullptr, nullptr);
     MVR_CUDA(ctx, cudaGetLastError());
     launches += 5;
   }

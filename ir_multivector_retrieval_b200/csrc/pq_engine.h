@@ -42,7 +42,7 @@ struct PqLayout {
   int nblk = 0, nchunk = 0;
   uint64_t rows_per_cta = 0;
   size_t o_draws = 0, o_chosen = 0, o_idx0 = 0, o_thr = 0, o_counts = 0, o_starts = 0, o_wcss = 0,
-         o_prev = 0, o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_state = 0;
+         o_prev = 0, o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_exact = 0, o_state = 0;
   size_t small_bytes = 0;
   size_t o_xt = 0, o_mind = 0, o_asg = 0, o_sorted = 0, o_hist = 0, o_chunk = 0, o_chunk_cnt = 0;
   // Lloyd bound pruning: bounds [M][N] f32 x2, per-subspace row lists

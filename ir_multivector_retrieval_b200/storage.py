@@ -59,5 +59,36 @@ def build_codes(token_ids, vectors, dim: int, params: tac.ClusteringParams, *, p
     return BuildCodes(cl, res, norms, book, codes)
 
 
-__all__ = ["residuals_and_norms", "build_codes", "BuildCodes", "PQ_SEED_OFFSET"]
+def doc_layouts_bytes(doc_offsets, pq_m: int) -> int:
+    """Size of the .tac per-doc section (storage.zig:506-508)."""
+    off = np.ascontiguousarray(doc_offsets, dtype=np.uint64)
+    n = C.c_uint64(0)
+    st = _lib.load().mvr_doc_layouts_bytes(ptr(off), off.size - 1, pq_m, C.byref(n))
+    if st:
+        raise _lib.MvrError(st, "doc_layouts_bytes")
+    return int(n.value)
+
+
+def write_doc_layouts(doc_offsets, assignments, codes, pq_m: int, ctx=None) -> bytes:
+    """storage.writeDocLayouts (storage.zig:705-749) on the GPU: the doc
+    index plus one [n_d | assignments | codes | pad] block per doc."""
+    off = np.ascontiguousarray(doc_offsets, dtype=np.uint64)
+    a = np.ascontiguousarray(assignments, dtype=np.uint32).reshape(-1)
+    c = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1)
+    ctx = ctx or _lib.default_context()
+    n = doc_layouts_bytes(off, pq_m)
+    out = np.empty(n, dtype=np.uint8)
+    ctx.check(ctx.lib.mvr_write_doc_layouts(ctx.handle, ptr(off), off.size - 1, ptr(a), ptr(c), a.size, pq_m,
+                                            ptr(out), n))
+    return out.tobytes()
+
+
+def crc32(data: bytes, crc: int = 0) -> int:
+    """The .tac footer checksum (std.hash.Crc32, storage.zig:655-660)."""
+    buf = np.frombuffer(data, dtype=np.uint8)
+    return int(_lib.load().mvr_crc32(crc, ptr(buf) if buf.size else None, buf.size))
+
+
+__all__ = ["residuals_and_norms", "build_codes", "BuildCodes", "PQ_SEED_OFFSET", "doc_layouts_bytes",
+           "write_doc_layouts", "crc32"]
 _ = C  # ctypes kept for symmetry with the other modules

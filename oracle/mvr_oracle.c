@@ -998,3 +998,36 @@ done:
   free(token_wcss);
   return st;
 }
+
+/* ------------------------------------------------------------------------
+ * storage.zig — per-doc layouts (:705-749)
+ * ------------------------------------------------------------------------ */
+static uint64_t align_up8(uint64_t v) { return (v + 7u) & ~(uint64_t)7u; }
+
+uint64_t orc_write_doc_layouts(const uint64_t* doc_offsets, uint64_t n_docs,
+                               const uint32_t* assignments, const uint8_t* codes,
+                               uint32_t pq_m, uint8_t* out, uint64_t out_len) {
+  const uint64_t idx_bytes = (n_docs + 1) * 8;
+  if (out_len < idx_bytes) return 0;
+  uint64_t cur = idx_bytes, payload_off = 0;
+  for (uint64_t d = 0; d < n_docs; ++d) {
+    memcpy(out + d * 8, &payload_off, 8);
+    const uint64_t n_d = doc_offsets[d + 1] - doc_offsets[d];
+    const uint64_t tok_lo = doc_offsets[d];
+    const uint64_t unpadded = 4 + n_d * 4 + n_d * (uint64_t)pq_m;
+    const uint64_t this_doc = align_up8(unpadded);
+    if (out_len < cur + this_doc) return 0;
+    const uint32_t n32 = (uint32_t)n_d;
+    memcpy(out + cur, &n32, 4);
+    uint64_t w = cur + 4;
+    memcpy(out + w, assignments + tok_lo, n_d * 4);
+    w += n_d * 4;
+    memcpy(out + w, codes + tok_lo * pq_m, n_d * pq_m);
+    w += n_d * pq_m;
+    memset(out + w, 0, cur + this_doc - w);
+    payload_off += this_doc;
+    cur += this_doc;
+  }
+  memcpy(out + n_docs * 8, &payload_off, 8);
+  return cur;
+}

@@ -90,6 +90,13 @@ int orc_tac_cluster_flat(const uint32_t* token_ids, uint64_t n_tokens,
                          uint64_t kappa_cap, uint64_t* n_distinct_out,
                          float* wcss_total);
 
+/* storage.writeDocLayouts (src/index/storage.zig:705-749): doc index
+ * (n_docs + 1 u64 payload offsets) + per doc [n_d u32 | assignments u32 |
+ * codes u8 * n_d * pq_m | zero pad to 8]. Returns the bytes written, or 0
+ * when `out_len` is too small (BufferTooSmall). */
+uint64_t orc_write_doc_layouts(const uint64_t* doc_offsets, uint64_t n_docs,
+                               const uint32_t* assignments, const uint8_t* codes,
+                               uint32_t pq_m, uint8_t* out, uint64_t out_len);
 #ifdef __cplusplus
 }
 #endif

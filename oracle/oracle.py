@@ -294,3 +294,21 @@ def tac_cluster_flat(token_ids, vectors, dim: int, kappa_total: int, seed: int, 
                                        _p(cent), _p(asg), _p(kap), nd, C.byref(ndo), C.byref(w)),
            "cluster_flat")
     return ClusterResult(cent[: kappa_total * dim], asg[: ids.size], kap, float(w.value))
+
+
+def write_doc_layouts(doc_offsets, assignments, codes, pq_m: int) -> bytes:
+    """storage.writeDocLayouts restated (oracle/mvr_oracle.c)."""
+    off = np.ascontiguousarray(doc_offsets, dtype=np.uint64)
+    a = _u32(assignments)
+    c = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1)
+    n_docs = off.size - 1
+    cap = (n_docs + 1) * 8 + int(sum(((4 + int(off[d + 1] - off[d]) * (4 + pq_m)) + 7) // 8 * 8
+                                    for d in range(n_docs))) + 8
+    out = np.zeros(cap, dtype=np.uint8)
+    lib = load()
+    lib.orc_write_doc_layouts.restype = C.c_uint64
+    n = lib.orc_write_doc_layouts(_p(off), C.c_uint64(n_docs), _p(a), _p(c), C.c_uint32(pq_m), _p(out),
+                                  C.c_uint64(cap))
+    if n == 0:
+        raise OracleError(18, "write_doc_layouts")
+    return out[:n].tobytes()

@@ -120,3 +120,28 @@ def test_no_gpu_fails_loudly_or_creates_context(lib):
         lib.mvr_ctx_destroy(h)
     else:
         assert lib.mvr_status_name(st).decode() in ("NoDevice", "CudaError")
+
+
+def test_crc32_matches_the_standard(lib):
+    import zlib
+
+    from ir_multivector_retrieval_b200 import storage
+
+    assert storage.crc32(b"123456789") == 0xCBF43926  # the published CRC-32 check value
+    rng = np.random.default_rng(0)
+    for n in (0, 1, 7, 8, 9, 4097):
+        d = rng.integers(0, 256, size=n, dtype=np.uint8).tobytes()
+        assert storage.crc32(d) == zlib.crc32(d)
+        assert storage.crc32(d[n // 2:], storage.crc32(d[:n // 2])) == zlib.crc32(d)
+
+
+def test_doc_layout_size_matches_oracle(lib, orc):
+    from ir_multivector_retrieval_b200 import storage
+
+    rng = np.random.default_rng(3)
+    for m in (16, 32, 3):
+        n_d = rng.integers(0, 9, size=50)
+        off = np.concatenate([[0], np.cumsum(n_d)]).astype(np.uint64)
+        n = int(off[-1])
+        b = orc.write_doc_layouts(off, rng.integers(0, 1000, size=n), rng.integers(0, 256, size=n * m), m)
+        assert storage.doc_layouts_bytes(off, m) == len(b)

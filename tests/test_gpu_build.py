@@ -47,3 +47,45 @@ def test_build_chain_matches_oracle(ctx, orc, n, dim, kappa, pq_m):
     assert _same(got.pq.codebooks, cb)
     codes = orc.pq_encode(cb, dim, pq_m, res, n_threads=THREADS)
     assert np.array_equal(got.codes, codes)
+
+
+@pytest.mark.parametrize("m", [16, 32, 3])
+def test_doc_layouts_match_oracle(ctx, orc, m):
+    rng = np.random.default_rng(m)
+    n_d = rng.integers(0, 120, size=3_000)
+    n_d[::17] = 0  # empty docs
+    off = np.concatenate([[0], np.cumsum(n_d)]).astype(np.uint64)
+    n = int(off[-1])
+    asg = rng.integers(0, 2**32 - 1, size=n, dtype=np.uint64).astype(np.uint32)
+    codes = rng.integers(0, 256, size=(n, m), dtype=np.uint8)
+    got = storage.write_doc_layouts(off, asg, codes, m, ctx=ctx)
+    want = orc.write_doc_layouts(off, asg, codes, m)
+    assert got == want
+
+
+def test_doc_layouts_device_entry_and_short_buffer(ctx, orc):
+    torch = pytest.importorskip("torch")
+    import ctypes as C
+
+    from ir_multivector_retrieval_b200._lib import MvrError, ptr
+
+    rng = np.random.default_rng(2)
+    n_d = rng.integers(1, 60, size=500)
+    off = np.concatenate([[0], np.cumsum(n_d)]).astype(np.uint64)
+    n = int(off[-1])
+    asg = rng.integers(0, 30_000, size=n).astype(np.uint32)
+    codes = rng.integers(0, 256, size=(n, 16), dtype=np.uint8)
+    size = storage.doc_layouts_bytes(off, 16)
+    d_asg = torch.from_numpy(asg.view(np.int32)).cuda()
+    d_codes = torch.from_numpy(codes).cuda()
+    d_out = torch.empty(size, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ctx.check(ctx.lib.mvr_write_doc_layouts_device(ctx.handle, ptr(off), off.size - 1, ptr(d_asg), ptr(d_codes), n,
+                                                   16, ptr(d_out), size))
+    ctx.sync()
+    assert d_out.cpu().numpy().tobytes() == orc.write_doc_layouts(off, asg, codes, 16)
+    with pytest.raises(MvrError) as e:
+        ctx.check(ctx.lib.mvr_write_doc_layouts_device(ctx.handle, ptr(off), off.size - 1, ptr(d_asg),
+                                                       ptr(d_codes), n, 16, ptr(d_out), size - 1))
+    assert e.value.name == "BufferTooSmall"
+    _ = C

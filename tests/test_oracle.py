@@ -379,3 +379,32 @@ def test_residuals_norms(orc):
     r, n = orc.residuals_norms(v, c, [0, 1], 2)
     assert list(n) == [5.0, 0.0]
     assert abs(r[0] - 0.6) < 1e-6 and abs(r[1] - 0.8) < 1e-6 and r[2] == 0 and r[3] == 0
+
+
+def test_doc_layouts_round_trip(orc):
+    # storage.zig:1116-1194 (round-trip of every section), restated for the
+    # per-doc section: parse the index and each [n_d | ids | codes | pad]
+    rng = np.random.default_rng(11)
+    m = 16
+    n_d = [3, 0, 5, 1, 0, 8]
+    off = np.concatenate([[0], np.cumsum(n_d)]).astype(np.uint64)
+    n = int(off[-1])
+    asg = rng.integers(0, 2**32 - 1, size=n, dtype=np.uint64).astype(np.uint32)
+    codes = rng.integers(0, 256, size=(n, m), dtype=np.uint8)
+    b = orc.write_doc_layouts(off, asg, codes, m)
+    nd = len(n_d)
+    idx = np.frombuffer(b[: (nd + 1) * 8], dtype=np.uint64)
+    base = (nd + 1) * 8
+    for d in range(nd):
+        p = base + int(idx[d])
+        assert p % 8 == 0
+        k = int(np.frombuffer(b[p:p + 4], dtype=np.uint32)[0])
+        assert k == n_d[d]
+        ids = np.frombuffer(b[p + 4:p + 4 + 4 * k], dtype=np.uint32)
+        assert np.array_equal(ids, asg[off[d]:off[d + 1]])
+        cds = np.frombuffer(b[p + 4 + 4 * k:p + 4 + 4 * k + m * k], dtype=np.uint8)
+        assert np.array_equal(cds, codes[off[d]:off[d + 1]].reshape(-1))
+        end = base + int(idx[d + 1])
+        assert end - p == (4 + k * (4 + m) + 7) // 8 * 8
+        assert not any(b[p + 4 + k * (4 + m):end])
+    assert len(b) == base + int(idx[nd])
