@@ -60,6 +60,10 @@ enum {
   MVR_E_EMPTY_INPUT = 16,            /* vec.VecError.EmptyInput */
   MVR_E_OUT_OF_MEMORY = 17,          /* Allocator.Error.OutOfMemory (host or device) */
   MVR_E_BUFFER_TOO_SMALL = 18,       /* storage.StorageError.BufferTooSmall */
+  MVR_E_QUERY_SHAPE_MISMATCH = 19,   /* refine.RefineError.QueryShapeMismatch */
+  MVR_E_TABLE_SIZE_MISMATCH = 20,    /* refine.RefineError.TableSizeMismatch */
+  MVR_E_DOC_OUT_OF_RANGE = 21,       /* refine.RefineError.DocOutOfRange */
+  MVR_E_DOC_LAYOUT_CORRUPT = 22,     /* refine.RefineError.DocLayoutCorrupt */
   /* B200-side failures with no reference counterpart */
   MVR_E_CUDA = 100,             /* a CUDA runtime call failed */
   MVR_E_NCCL = 101,             /* an NCCL call failed */
@@ -258,7 +262,8 @@ int mvr_doc_layouts_bytes(const uint64_t* doc_offsets, uint64_t n_docs,
  * memory; `assignments` (n_tokens u32, TAC centroid ids), `codes`
  * (n_tokens * pq_m bytes, token-major) and `out` are host memory here and
  * device memory in the _device variant (asynchronous on the context
- * stream). The bytes are identical to the reference's. */
+ * stream; `d_out` 8-byte and `d_assignments` 4-byte aligned). The bytes
+ * are identical to the reference's. */
 int mvr_write_doc_layouts(mvr_ctx* ctx, const uint64_t* doc_offsets,
                           uint64_t n_docs, const uint32_t* assignments,
                           const uint8_t* codes, uint64_t n_tokens,
@@ -273,6 +278,52 @@ int mvr_write_doc_layouts_device(mvr_ctx* ctx, const uint64_t* doc_offsets,
  * 0xEDB88320, initial and final xor 0xFFFFFFFF, as zlib's crc32), over
  * host memory; `crc` continues a previous value (0 to start). */
 uint32_t mvr_crc32(uint32_t crc, const void* data, uint64_t len);
+
+/* ---- query side: PQ distance table and refine ------------------------- */
+
+/* Replaces PQ.buildDistanceTable (src/index/pq.zig:92-123): out[(m*256 + c)
+ * * n_q + i] = vec.dot(q_i[m*s .. m*s + s], codebook[m][c]) for the n_q
+ * query tokens (query: n_q * dim floats), out: pq_m * 256 * n_q floats.
+ * NQMismatch / OutBufferWrongSize as the reference. Host pointers here,
+ * device pointers (asynchronous) in the _device variant. */
+int mvr_pq_distance_table(mvr_ctx* ctx, const float* codebooks, uint32_t dim,
+                          uint32_t pq_m, const float* query, uint64_t query_len,
+                          uint32_t n_q, float* out, uint64_t out_len);
+int mvr_pq_distance_table_device(mvr_ctx* ctx, const float* d_codebooks,
+                                 uint32_t dim, uint32_t pq_m,
+                                 const float* d_query, uint64_t query_len,
+                                 uint32_t n_q, float* d_out, uint64_t out_len);
+
+/* Replaces refine.refine (src/retrieval/refine.zig:83-155) for n_cand
+ * candidate docs of one query: scores_out[c] = the exact MaxSim estimate
+ * S(q, doc_ids[c]) from the TAC centroids (kappa x dim), the per-doc
+ * section of mvr_write_doc_layouts (doc_section_len bytes, n_docs docs),
+ * the doc token offsets (n_docs + 1), the residual norms (n_tokens), the
+ * distance table and the query (n_q <= 128 tokens). The first failing
+ * candidate's status is returned (QueryShapeMismatch, TableSizeMismatch,
+ * DocOutOfRange, DocLayoutCorrupt; a centroid id >= kappa counts as a
+ * corrupt layout instead of reading past the centroids). Host pointers. */
+int mvr_refine_batch(mvr_ctx* ctx, const float* centroids, uint32_t kappa,
+                     uint32_t dim, uint32_t pq_m, const uint8_t* doc_section,
+                     uint64_t doc_section_len, uint64_t n_docs,
+                     const uint64_t* doc_token_offsets,
+                     const float* residual_norms, uint64_t n_tokens,
+                     const float* table, uint64_t table_len, const float* query,
+                     uint64_t query_len, uint32_t n_q, const uint32_t* doc_ids,
+                     uint64_t n_cand, float* scores_out);
+/* As mvr_refine_batch with every array in device memory (the index stays
+ * resident across queries; `d_doc_section` 8-byte aligned) and a per-
+ * candidate status array instead of a returned first failure;
+ * asynchronous on the context stream. */
+int mvr_refine_batch_device(mvr_ctx* ctx, const float* d_centroids,
+                            uint32_t kappa, uint32_t dim, uint32_t pq_m,
+                            const uint8_t* d_doc_section, uint64_t doc_section_len,
+                            uint64_t n_docs, const uint64_t* d_doc_token_offsets,
+                            const float* d_residual_norms, uint64_t n_tokens,
+                            const float* d_table, uint64_t table_len,
+                            const float* d_query, uint64_t query_len,
+                            uint32_t n_q, const uint32_t* d_doc_ids,
+                            uint64_t n_cand, float* d_scores, int* d_status);
 
 /* Timing report of the most recent `mvr_tac_cluster_flat` call on the
  * context (no reference counterpart; the reference prints `[stage]` lines,

@@ -36,6 +36,10 @@ STATUS_NAMES = {
     16: "EmptyInput",
     17: "OutOfMemory",
     18: "BufferTooSmall",
+    19: "QueryShapeMismatch",
+    20: "TableSizeMismatch",
+    21: "DocOutOfRange",
+    22: "DocLayoutCorrupt",
     100: "CudaError",
     101: "NcclError",
     102: "Timeout",
@@ -127,6 +131,19 @@ SIGNATURES = {
     "mvr_write_doc_layouts": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
     "mvr_write_doc_layouts_device": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
     "mvr_crc32": (C.c_uint32, [C.c_uint32, _P, C.c_uint64]),
+    "mvr_pq_distance_table": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
+    "mvr_pq_distance_table_device": (
+        C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
+    "mvr_refine_batch": (
+        C.c_int,
+        [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint64, _P, _P, C.c_uint64, _P, C.c_uint64,
+         _P, C.c_uint64, C.c_uint32, _P, C.c_uint64, _P],
+    ),
+    "mvr_refine_batch_device": (
+        C.c_int,
+        [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint64, _P, _P, C.c_uint64, _P, C.c_uint64,
+         _P, C.c_uint64, C.c_uint32, _P, C.c_uint64, _P, _P],
+    ),
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),

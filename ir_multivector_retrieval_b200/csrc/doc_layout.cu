@@ -40,7 +40,7 @@ int payload_offsets(const uint64_t* doc_offsets, uint64_t n_docs, uint32_t M, st
 __global__ void __launch_bounds__(256)
 doc_layout_kernel(const uint64_t* __restrict__ doc_off, const uint64_t* __restrict__ pay, uint64_t n_docs,
                   const uint32_t* __restrict__ asg, const uint8_t* __restrict__ codes, uint32_t M,
-                  uint8_t* __restrict__ out) {
+                  int words, uint8_t* __restrict__ out) {
   const uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const uint64_t stride = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -56,7 +56,7 @@ doc_layout_kernel(const uint64_t* __restrict__ doc_off, const uint64_t* __restri
     uint8_t* cdst = doc + 4 + 4 * n_d;
     const uint8_t* csrc = codes + tok_lo * (uint64_t)M;
     const uint64_t nc = n_d * (uint64_t)M;
-    if ((M & 3) == 0) {  // both ends 4-byte aligned
+    if (words) {  // M % 4 == 0 and a 4-byte aligned source: both ends aligned
       const uint32_t* s32 = reinterpret_cast<const uint32_t*>(csrc);
       uint32_t* d32 = reinterpret_cast<uint32_t*>(cdst);
       for (uint64_t i = lane; i < nc / 4; i += 32) d32[i] = s32[i];
@@ -89,7 +89,9 @@ int launch(Ctx* c, const uint64_t* doc_offsets, uint64_t n_docs, const std::vect
                               c->stream));
   const uint64_t warps = n_docs + 1;
   const unsigned grid = (unsigned)std::min<uint64_t>((warps * 32 + 255) / 256, (uint64_t)c->sm_count * 16);
-  doc_layout_kernel<<<grid, 256, 0, c->stream>>>(d_meta, d_meta + n_docs + 1, n_docs, d_asg, d_codes, pq_m, d_out);
+  const int words = (pq_m % 4 == 0) && (reinterpret_cast<uintptr_t>(d_codes) % 4 == 0);
+  doc_layout_kernel<<<grid, 256, 0, c->stream>>>(d_meta, d_meta + n_docs + 1, n_docs, d_asg, d_codes, pq_m, words,
+                                                 d_out);
   MVR_CUDA(c, cudaGetLastError());
   return MVR_OK;
 }
@@ -135,6 +137,8 @@ int mvr_write_doc_layouts_device(mvr_ctx* h, const uint64_t* doc_offsets, uint64
   std::vector<uint64_t> pay;
   MVR_TRY(mvr::check_args(c, doc_offsets, n_docs, n_tokens, pq_m, &pay, out_len));
   if (!d_out || (n_tokens && (!d_assignments || !d_codes))) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(d_out) % 8 || reinterpret_cast<uintptr_t>(d_assignments) % 4)
+    return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "out must be 8-byte and assignments 4-byte aligned");
   MVR_CUDA(c, cudaSetDevice(c->device));
   return mvr::launch(c, doc_offsets, n_docs, pay, d_assignments, d_codes, pq_m, d_out);
 }

@@ -159,6 +159,10 @@ const char* mvr_status_name(int s) {
     case MVR_E_EMPTY_INPUT: return "EmptyInput";
     case MVR_E_OUT_OF_MEMORY: return "OutOfMemory";
     case MVR_E_BUFFER_TOO_SMALL: return "BufferTooSmall";
+    case MVR_E_QUERY_SHAPE_MISMATCH: return "QueryShapeMismatch";
+    case MVR_E_TABLE_SIZE_MISMATCH: return "TableSizeMismatch";
+    case MVR_E_DOC_OUT_OF_RANGE: return "DocOutOfRange";
+    case MVR_E_DOC_LAYOUT_CORRUPT: return "DocLayoutCorrupt";
     case MVR_E_CUDA: return "CudaError";
     case MVR_E_NCCL: return "NcclError";
     case MVR_E_TIMEOUT: return "Timeout";

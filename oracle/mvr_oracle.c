@@ -1031,3 +1031,94 @@ uint64_t orc_write_doc_layouts(const uint64_t* doc_offsets, uint64_t n_docs,
   memcpy(out + n_docs * 8, &payload_off, 8);
   return cur;
 }
+
+/* ------------------------------------------------------------------------
+ * vec.dot, PQ.buildDistanceTable, refine.refine
+ * ------------------------------------------------------------------------ */
+float orc_dot(const float* a, const float* b, uint32_t len) {
+  if (len == 2) return a[0] * b[0] + a[1] * b[1]; /* vec.zig:50 */
+  if (len == 4) {                                 /* dotComptime, dim <= 4 */
+    float s = 0.0f;
+    for (int i = 0; i < 4; ++i) s += a[i] * b[i];
+    return s;
+  }
+  if (len == 64 || len == 128) { /* dotComptime: 4 lanes, ordered @reduce */
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (uint32_t off = 0; off < len; off += 4)
+      for (int l = 0; l < 4; ++l) acc[l] = acc[l] + a[off + l] * b[off + l];
+    return reduce_lanes(acc, 4);
+  }
+  const int L = g_lane_count; /* dotGeneric */
+  float acc[64] = {0.0f};
+  uint32_t i = 0;
+  while (i + (uint32_t)L <= len) {
+    for (int l = 0; l < L; ++l) acc[l] = acc[l] + a[i + l] * b[i + l];
+    i += (uint32_t)L;
+  }
+  float sum = reduce_lanes(acc, L);
+  while (i < len) {
+    sum += a[i] * b[i];
+    ++i;
+  }
+  return sum;
+}
+
+int orc_pq_distance_table(const float* codebooks, uint32_t dim, uint32_t pq_m,
+                          const float* query, uint64_t query_len, uint32_t n_q,
+                          float* out, uint64_t out_len) {
+  if (n_q == 0) return MVR_E_NQ_MISMATCH;
+  if (query_len != (uint64_t)n_q * dim) return MVR_E_NQ_MISMATCH;
+  if (out_len != (uint64_t)pq_m * 256u * n_q) return MVR_E_OUT_BUFFER_WRONG_SIZE;
+  const uint32_t s = dim / pq_m;
+  for (uint32_t m = 0; m < pq_m; ++m)
+    for (uint32_t c = 0; c < 256; ++c) {
+      const float* cv = codebooks + ((uint64_t)m * 256 + c) * s;
+      const uint64_t base = ((uint64_t)m * 256 + c) * n_q;
+      for (uint32_t i = 0; i < n_q; ++i)
+        out[base + i] = orc_dot(query + (uint64_t)i * dim + (uint64_t)m * s, cv, s);
+    }
+  return MVR_OK;
+}
+
+int orc_refine(const float* centroids, uint32_t dim, uint32_t pq_m,
+               const uint8_t* doc_section, uint64_t n_docs,
+               const uint64_t* doc_token_offsets, const float* residual_norms,
+               const float* table, uint64_t table_len, const float* query,
+               uint64_t query_len, uint32_t n_q, uint32_t doc_id, float* score) {
+  if (n_q == 0 || query_len != (uint64_t)n_q * dim) return MVR_E_QUERY_SHAPE_MISMATCH;
+  if (table_len != (uint64_t)pq_m * 256u * n_q) return MVR_E_TABLE_SIZE_MISMATCH;
+  if (doc_id >= n_docs) return MVR_E_DOC_OUT_OF_RANGE;
+  const uint64_t* idx = (const uint64_t*)doc_section;
+  const uint8_t* payload = doc_section + (n_docs + 1) * 8;
+  const uint64_t lo = idx[doc_id], hi = idx[doc_id + 1];
+  if (hi - lo < 4) return MVR_E_DOC_LAYOUT_CORRUPT;
+  uint32_t n_d;
+  memcpy(&n_d, payload + lo, 4);
+  if (hi - lo < 4 + (uint64_t)n_d * 4 + (uint64_t)n_d * pq_m) return MVR_E_DOC_LAYOUT_CORRUPT;
+  const uint64_t t_lo = doc_token_offsets[doc_id], t_hi = doc_token_offsets[doc_id + 1];
+  if (t_hi - t_lo != n_d) return MVR_E_DOC_LAYOUT_CORRUPT;
+  const uint8_t* ids = payload + lo + 4;
+  const uint8_t* codes = ids + (uint64_t)n_d * 4;
+  float* best = (float*)malloc(sizeof(float) * n_q);
+  for (uint32_t i = 0; i < n_q; ++i) best[i] = -INFINITY;
+  for (uint32_t k = 0; k < n_d; ++k) {
+    uint32_t cid;
+    memcpy(&cid, ids + (uint64_t)k * 4, 4);
+    const float* cv = centroids + (uint64_t)cid * dim;
+    const float norm_k = residual_norms[t_lo + k];
+    for (uint32_t i = 0; i < n_q; ++i) {
+      const float cent = orc_dot(query + (uint64_t)i * dim, cv, dim);
+      float res = 0.0f;
+      for (uint32_t m = 0; m < pq_m; ++m)
+        res += table[((uint64_t)m * 256 + codes[(uint64_t)k * pq_m + m]) * n_q + i];
+      const float sc = cent + norm_k * res;
+      if (sc > best[i]) best[i] = sc;
+    }
+  }
+  float sum = 0.0f;
+  if (n_d > 0)
+    for (uint32_t i = 0; i < n_q; ++i) sum += best[i];
+  free(best);
+  *score = sum;
+  return MVR_OK;
+}

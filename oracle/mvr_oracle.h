@@ -97,6 +97,25 @@ int orc_tac_cluster_flat(const uint32_t* token_ids, uint64_t n_tokens,
 uint64_t orc_write_doc_layouts(const uint64_t* doc_offsets, uint64_t n_docs,
                                const uint32_t* assignments, const uint8_t* codes,
                                uint32_t pq_m, uint8_t* out, uint64_t out_len);
+/* vec.dot (src/util/vec.zig:37-103): len 2 `a0*b0 + a1*b1`; len 4 left
+ * fold from +0; len 64/128 four lane accumulators from +0, then the
+ * ordered reduce; other lengths the lane-count loop plus the tail. */
+float orc_dot(const float* a, const float* b, uint32_t len);
+
+/* PQ.buildDistanceTable (src/index/pq.zig:92-123): out[(m*256+c)*n_q+i] =
+ * dot(q_i[m*s .. m*s+s], codebook[m][c]). Returns MVR status. */
+int orc_pq_distance_table(const float* codebooks, uint32_t dim, uint32_t pq_m,
+                          const float* query, uint64_t query_len, uint32_t n_q,
+                          float* out, uint64_t out_len);
+
+/* refine.refine (src/retrieval/refine.zig:83-155) for one candidate doc:
+ * `doc_section` is the writeDocLayouts section (index + payload). */
+int orc_refine(const float* centroids, uint32_t dim, uint32_t pq_m,
+               const uint8_t* doc_section, uint64_t n_docs,
+               const uint64_t* doc_token_offsets, const float* residual_norms,
+               const float* table, uint64_t table_len, const float* query,
+               uint64_t query_len, uint32_t n_q, uint32_t doc_id, float* score);
+
 #ifdef __cplusplus
 }
 #endif

@@ -312,3 +312,30 @@ def write_doc_layouts(doc_offsets, assignments, codes, pq_m: int) -> bytes:
     if n == 0:
         raise OracleError(18, "write_doc_layouts")
     return out[:n].tobytes()
+
+
+def dot(a, b) -> float:
+    a, b = _f32(a), _f32(b)
+    lib = load()
+    lib.orc_dot.restype = C.c_float
+    return float(lib.orc_dot(_p(a), _p(b), C.c_uint32(a.size)))
+
+
+def pq_distance_table(codebooks, dim: int, pq_m: int, query, n_q: int) -> np.ndarray:
+    q = _f32(query)
+    out = np.zeros(pq_m * 256 * n_q, dtype=np.float32)
+    _check(load().orc_pq_distance_table(_p(_f32(codebooks)), dim, pq_m, _p(q), C.c_uint64(q.size), n_q, _p(out),
+                                        C.c_uint64(out.size)), "pq_distance_table")
+    return out
+
+
+def refine(centroids, dim: int, pq_m: int, doc_section: bytes, n_docs: int, doc_token_offsets, norms, table,
+           query, n_q: int, doc_id: int) -> float:
+    sec = np.frombuffer(doc_section, dtype=np.uint8)
+    off = np.ascontiguousarray(doc_token_offsets, dtype=np.uint64)
+    t, q = _f32(table), _f32(query)
+    out = C.c_float(0)
+    _check(load().orc_refine(_p(_f32(centroids)), dim, pq_m, _p(np.ascontiguousarray(sec)), C.c_uint64(n_docs),
+                             _p(off), _p(_f32(norms)), _p(t), C.c_uint64(t.size), _p(q), C.c_uint64(q.size), n_q,
+                             doc_id, C.byref(out)), "refine")
+    return float(out.value)

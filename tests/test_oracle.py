@@ -408,3 +408,33 @@ def test_doc_layouts_round_trip(orc):
         assert end - p == (4 + k * (4 + m) + 7) // 8 * 8
         assert not any(b[p + 4 + k * (4 + m):end])
     assert len(b) == base + int(idx[nd])
+
+
+def test_dot_reference_kats(orc):
+    # src/util/vec.zig:334-358 and :497-509 (exact where the reference uses
+    # expectEqual), :521-575 (ramps, within the reference's 1e-5)
+    assert orc.dot([1, 2, 3], [4, -5, 6]) == 12.0
+    a = np.arange(1, 18, dtype=np.float32)
+    assert orc.dot(a, np.full(17, 2, np.float32)) == 306.0
+    assert orc.dot([1, 0, 0, 0], [0, 1, 0, 0]) == 0.0
+    assert orc.dot([1, 2], [3, 4]) == 11.0
+    assert orc.dot([1, 2, 3, 4], [5, 6, 7, 8]) == 70.0
+    i = np.arange(64, dtype=np.float32)
+    a, b = i * np.float32(0.01), (63 - i) * np.float32(0.02) + np.float32(0.5)
+    assert abs(orc.dot(a, b) - float(np.dot(a.astype(np.float64), b.astype(np.float64)))) < 1e-4
+    i = np.arange(128, dtype=np.float32)
+    a, b = i * np.float32(0.005) - np.float32(0.3), ((i * 13 + 1) % 128) * np.float32(0.01)
+    assert abs(orc.dot(a, b) - float(np.dot(a.astype(np.float64), b.astype(np.float64)))) < 1e-4
+
+
+def test_distance_table_layout(orc):
+    # src/index/pq.zig:344-349, :519-575: table[m][c][i] is the dot product of
+    # query token i's sub-vector m with codeword (m, c); bad sizes fail
+    rng = np.random.default_rng(1)
+    cb = rng.standard_normal(16 * 256 * 4).astype(np.float32)
+    q = rng.standard_normal((3, 64)).astype(np.float32)
+    t = orc.pq_distance_table(cb, 64, 16, q, 3).reshape(16, 256, 3)
+    for m, c, i in [(0, 0, 0), (5, 200, 2), (15, 255, 1)]:
+        assert t[m, c, i] == orc.dot(q[i, m * 4:(m + 1) * 4], cb.reshape(16, 256, 4)[m, c])
+    with pytest.raises(Exception):
+        orc.pq_distance_table(cb, 64, 16, q, 4)
