@@ -36,6 +36,7 @@ is fixed; times are the max over ranks.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import ctypes as C
 import json
 import math
@@ -86,39 +87,53 @@ TAC_KAPPA = 32_768
 TAC_SMALL = (117_645, 12_288, 10)  # configs[0] rows, kappa (10,240 leaves no room for the tail), theta
 
 
-def measure_tac(corpus, steps: int, cpu: bool) -> dict:
+def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=None) -> dict:
     """clusterFlat through the host-pointer C ABI (e2e wall time, device
-    phases from mvr_tac_last_stats) on the full corpus and on configs[0]."""
+    phases from mvr_tac_last_stats) on the full corpus and on configs[0].
+    With world > 1 every rank calls the token-sharded entry point on the
+    same inputs (a collective); times are the max over ranks (``reduce``)."""
     from ir_multivector_retrieval_b200 import synth, tac
 
+    sharded = world > 1
+    red = reduce or (lambda v: v)
     out = {"workload": (f"tac.clusterFlat {corpus.n:,} x {DIM}, kappa {TAC_KAPPA:,}, paper-strict "
-                        "(mu 128, tau 256, eps 4, theta 39), 25 iters, tol 1e-4")}
+                        "(mu 128, tau 256, eps 4, theta 39), 25 iters, tol 1e-4"),
+           "parallelism": f"token-sharded over {world} GPUs (NCCL)" if sharded else "1gpu"}
     p = tac.ClusteringParams(kappa_total=TAC_KAPPA, seed=42)
-    tac.cluster_flat(corpus.token_ids, corpus.vectors, DIM, p)  # warm-up: grows buffers
-    walls, stats = [], []
+
+    def call(ids, vec, prm):
+        return tac.cluster_flat(ids, vec, DIM, prm, ctx=ctx, sharded=sharded)
+
+    call(corpus.token_ids, corpus.vectors, p)  # warm-up: grows buffers
+    walls, stats, digests = [], [], set()
     for _ in range(max(1, steps)):
         t0 = time.perf_counter()
-        r = tac.cluster_flat(corpus.token_ids, corpus.vectors, DIM, p)
+        r = call(corpus.token_ids, corpus.vectors, p)
         walls.append(time.perf_counter() - t0)
-        stats.append(tac.last_stats())
+        stats.append(tac.last_stats(ctx))
+        digests.add(hashlib.sha256(r.centroids.tobytes() + r.assignments.tobytes()).hexdigest())
     mid = sorted(range(len(walls)), key=walls.__getitem__)[len(walls) // 2]
     st = stats[mid]
-    out.update({"e2e_ms": walls[mid] * 1e3,
-                "device_ms": st["spread_ms"] + st["seed_ms"] + st["lloyd_ms"],
+    out.update({"e2e_ms": red(walls[mid] * 1e3),
+                "device_ms": red(st["spread_ms"] + st["seed_ms"] + st["lloyd_ms"]),
                 "phases_ms": {k: st[k] for k in ("host_ms", "h2d_ms", "spread_ms", "seed_ms", "lloyd_ms",
                                                  "d2h_ms")},
                 "tokens": st["problems"], "iters_max": st["iters_max"], "gpu_launches": st["launches"],
-                "wcss_total": r.wcss_total})
+                "wcss_total": r.wcss_total, "outputs_sha256": sorted(digests)[0],
+                "repeatable": len(digests) == 1})
+    if sharded:
+        out["phases_ms_note"] = "phases and tokens of rank 0; e2e_ms and device_ms are the max over ranks"
     n0, k0, th0 = TAC_SMALL
     c0 = synth.make_corpus(n0, DIM, seed=42)
     p0 = tac.ClusteringParams(kappa_total=k0, seed=42, theta=th0)
-    tac.cluster_flat(c0.token_ids, c0.vectors, DIM, p0)
+    call(c0.token_ids, c0.vectors, p0)
     w0 = []
     for _ in range(max(1, steps)):
         t0 = time.perf_counter()
-        r0 = tac.cluster_flat(c0.token_ids, c0.vectors, DIM, p0)
+        r0 = call(c0.token_ids, c0.vectors, p0)
         w0.append(time.perf_counter() - t0)
-    small = {"workload": f"configs[0]: {n0:,} x {DIM}, kappa {k0:,}, theta {th0}", "e2e_ms": statistics.median(w0) * 1e3}
+    small = {"workload": f"configs[0]: {n0:,} x {DIM}, kappa {k0:,}, theta {th0}",
+             "e2e_ms": red(statistics.median(w0) * 1e3)}
     if cpu:
         from oracle import oracle
 
@@ -393,6 +408,11 @@ def run_b200(args) -> None:
         except Exception:
             traffic = None
 
+    tac_line = None
+    if not args.no_tac:  # collective when world > 1: every rank takes part
+        tac_line = measure_tac(corpus, 3, cpu=(world == 1 and not args.no_cpu), ctx=ctx, world=world,
+                               reduce=max_over_ranks)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -426,8 +446,8 @@ def run_b200(args) -> None:
                     "d2h_bytes_per_step": int(cb_host.nbytes),
                     "encode_mvec_s": n_total / e2e_enc_s / 1e6},
         }
-        if not args.no_tac:
-            line["tac"] = measure_tac(corpus, 3, cpu=(world == 1 and not args.no_cpu))
+        if tac_line is not None:
+            line["tac"] = tac_line
         if world == 1 and not args.no_cpu:
             cpu = cpu_lloyd_seconds_per_iter(x, host_threads(), target_s=args.cpu_target_s)
             line["cpu_baseline"] = {

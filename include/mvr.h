@@ -428,6 +428,35 @@ int mvr_tac_cluster_flat(mvr_ctx* ctx, const uint32_t* token_ids,
                          uint64_t kappa_per_token_cap, uint64_t* n_distinct_out,
                          float* wcss_total_out);
 
+/* Several GPUs (no reference counterpart; the reference runs the per-token
+ * k-means of tac.clusterFlat on host threads, src/tac/tac.zig:685-825):
+ * collective over the context's communicator (`mvr_ctx_init_comm`). Every
+ * rank passes the same inputs and receives the full outputs of
+ * `mvr_tac_cluster_flat`, bit for bit. Grouping, spreads and budgets run on
+ * every rank; the per-token k-means problems are split over the ranks by
+ * `mvr_tac_partition_tokens`, and the results are merged with one exact
+ * all-reduce (each value comes from exactly one rank). Without a
+ * communicator it is `mvr_tac_cluster_flat`. */
+int mvr_tac_cluster_flat_sharded(mvr_ctx* ctx, const uint32_t* token_ids,
+                                 uint64_t n_tokens, const float* vectors,
+                                 uint64_t vectors_len, uint32_t dim,
+                                 const mvr_clustering_params* p,
+                                 float* centroids_out,
+                                 uint32_t* assignments_out,
+                                 uint32_t* kappa_per_token_out,
+                                 uint64_t kappa_per_token_cap,
+                                 uint64_t* n_distinct_out,
+                                 float* wcss_total_out);
+
+/* The token split of `mvr_tac_cluster_flat_sharded` (host-only):
+ * longest-processing-time first over the work estimate n_j * (k_j + 1)
+ * (n_j when k_j >= n_j), heaviest token first (ties in token order), each to
+ * the least-loaded rank (ties: the lowest rank). owner_out[j] in
+ * [0, n_ranks); 0 for tokens without a problem (n_j = 0 or k_j = 0). */
+int mvr_tac_partition_tokens(const uint32_t* freqs, const uint32_t* kappa,
+                             uint64_t n, uint32_t n_ranks,
+                             uint32_t* owner_out);
+
 /* Replaces `tac.allocateBudgets` (src/tac/tac.zig:390-402): phases 1-4 on
  * per-token (freq, spread) arrays of length n. Host-only integer/float
  * logic; `frac` is caller scratch of n floats. */

@@ -187,6 +187,12 @@ SIGNATURES = {
         [_P, _P, C.c_uint64, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams), _P, _P,
          _P, C.c_uint64, _U64, _F],
     ),
+    "mvr_tac_cluster_flat_sharded": (
+        C.c_int,
+        [_P, _P, C.c_uint64, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams), _P, _P,
+         _P, C.c_uint64, _U64, _F],
+    ),
+    "mvr_tac_partition_tokens": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, _P]),
     "mvr_tac_allocate_budgets": (
         C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams)]),
 }

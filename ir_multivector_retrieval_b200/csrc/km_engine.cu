@@ -114,6 +114,7 @@ km_gather_groups_kernel(const float* __restrict__ V, const uint32_t* __restrict_
       }
     }
   }
+  if (!GT) return;
   __syncthreads();
   for (int t = threadIdx.x; t < ng4 * 32; t += 256) {
     const int g = t >> 5, i = t & 31;

@@ -37,7 +37,8 @@ struct KmResult {
 // Group-major copy of a row set: GT holds ceil(dim / 4) groups, group g of
 // row q (coordinates 4g .. 4g+3, zero past dim) as the float4 GT[g * n + q].
 // Row q is V[idx[q]] (or V[q] when idx is null); when G is not null the rows
-// are also written row-major to G. Enqueued on the context stream.
+// are also written row-major to G; GT may be null when only G is wanted.
+// Enqueued on the context stream.
 int km_gather_groups(Ctx* ctx, const float* d_V, const uint32_t* d_idx, uint64_t n, uint32_t dim, float* d_G,
                      float* d_GT);
 

@@ -137,6 +137,33 @@ int tac_allocate_budgets_host(const uint32_t* freqs, const float* spreads, uint3
   return excess == 0 ? MVR_OK : MVR_E_BUDGET_TOO_SMALL;
 }
 
+uint64_t tac_token_work(uint32_t n, uint32_t k) {
+  if (n == 0 || k == 0) return 0;
+  return k < n ? (uint64_t)n * ((uint64_t)k + 1) : (uint64_t)n;
+}
+
+void tac_partition_tokens_host(const uint32_t* freqs, const uint32_t* kappa, uint64_t n, uint32_t ranks,
+                               uint32_t* owner) {
+  std::vector<uint32_t> order;
+  for (uint64_t j = 0; j < n; ++j) {
+    owner[j] = 0;
+    if (tac_token_work(freqs[j], kappa[j]) > 0) order.push_back((uint32_t)j);
+  }
+  // heaviest first, ties in token order; each to the least-loaded rank
+  // (ties: the lowest rank)
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+    return tac_token_work(freqs[a], kappa[a]) > tac_token_work(freqs[b], kappa[b]);
+  });
+  std::vector<uint64_t> load(ranks, 0);
+  for (uint32_t j : order) {
+    uint32_t best = 0;
+    for (uint32_t r = 1; r < ranks; ++r)
+      if (load[r] < load[best]) best = r;
+    owner[j] = best;
+    load[best] += tac_token_work(freqs[j], kappa[j]);
+  }
+}
+
 }  // namespace mvr
 
 extern "C" {
@@ -160,6 +187,13 @@ int mvr_tac_allocate_budgets(const uint32_t* freqs, const float* spreads, uint32
   if (!p || (n > 0 && (!freqs || !spreads || !kappa || !frac))) return MVR_E_INVALID_ARGUMENT;
   return mvr::tac_allocate_budgets_host(freqs, spreads, kappa, frac, n, kappa_total, p->mu, p->tau,
                                         p->epsilon, p->theta);
+}
+
+int mvr_tac_partition_tokens(const uint32_t* freqs, const uint32_t* kappa, uint64_t n, uint32_t n_ranks,
+                             uint32_t* owner_out) {
+  if (n_ranks == 0 || (n > 0 && (!freqs || !kappa || !owner_out))) return MVR_E_INVALID_ARGUMENT;
+  mvr::tac_partition_tokens_host(freqs, kappa, n, n_ranks, owner_out);
+  return MVR_OK;
 }
 
 }  // extern "C"

@@ -7,6 +7,13 @@
 // side: the rows gathered in token order, the per-token Welford spreads
 // (tac.zig:609-644) and one k-means per token (runOneTokenKmeans,
 // tac.zig:458-514) through the ragged batch engine (km_engine.cu).
+//
+// Several GPUs (mvr_tac_cluster_flat_sharded): every rank groups the rows,
+// computes the spreads and the budgets (identical on every rank), then runs
+// only the tokens that the longest-processing-time split gives it, on a
+// compact copy of their rows. The per-token results, the centroids and the
+// assignments are merged with u32-sum all-reduces in which each value is
+// non-zero on at most one rank, so the merge is exact.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -17,6 +24,7 @@
 #include <vector>
 
 #include "../../include/mvr.h"
+#include "comm.h"
 #include "km_engine.h"
 #include "mvr_device.cuh"
 #include "mvr_internal.h"
@@ -213,6 +221,14 @@ __global__ void tac_scatter_assign_kernel(const uint32_t* __restrict__ idx, cons
     out[idx[q]] = goffc[rowtok[q]] + local[q];
 }
 
+// C[cmap[c]] = CL[c] for the local centroid rows c of one rank
+__global__ void tac_place_centroids_kernel(const float* __restrict__ CL, const uint32_t* __restrict__ cmap,
+                                           uint64_t nl, uint32_t d, float* __restrict__ C) {
+  const uint64_t total = nl * d;
+  for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x)
+    C[(uint64_t)cmap[e / d] * d + e % d] = CL[e];
+}
+
 int set_device(Ctx* c) {
   cudaError_t e = cudaSetDevice(c->device);
   if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
@@ -247,12 +263,18 @@ int kmeans_general_device(Ctx* ctx, const float* d_v, uint64_t n, uint32_t dim, 
 
 using mvr::Ctx;
 
-extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens, const float* vectors,
-                                    uint64_t vectors_len, uint32_t dim, const mvr_clustering_params* p,
-                                    float* centroids_out, uint32_t* assignments_out, uint32_t* kappa_out,
-                                    uint64_t kappa_cap, uint64_t* n_distinct_out, float* wcss_total_out) {
+namespace {
+
+// tac.clusterFlat on one GPU (sharded = false) or split over the ranks of
+// the context's communicator (sharded = true, more than one rank).
+int cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens, const float* vectors,
+                 uint64_t vectors_len, uint32_t dim, const mvr_clustering_params* p, float* centroids_out,
+                 uint32_t* assignments_out, uint32_t* kappa_out, uint64_t kappa_cap, uint64_t* n_distinct_out,
+                 float* wcss_total_out, bool sharded) {
   if (!h || !p) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  const int G = sharded ? mvr::comm_size(c) : 1;
+  const int me = G > 1 ? mvr::comm_rank(c) : 0;
   // clusterFlat's validation order (tac.zig:570-573)
   if (n_tokens == 0) return mvr::fail(c, MVR_E_EMPTY_TOKEN_DUMP, "no tokens");
   if (dim == 0) return mvr::fail(c, MVR_E_INVALID_THRESHOLDS, "dim == 0");
@@ -295,7 +317,7 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, rows * dim * sizeof(float), (void**)&d_V));
   MVR_TRY(mvr::scratch(c, mvr::kSlotSorted, rows * dim * sizeof(float), (void**)&d_G));
   float* d_GT = nullptr;
-  MVR_TRY(mvr::scratch(c, mvr::kSlotMinDist, rows * ((dim + 3) / 4) * 4 * sizeof(float), (void**)&d_GT));
+  if (G == 1) MVR_TRY(mvr::scratch(c, mvr::kSlotMinDist, rows * ((dim + 3) / 4) * 4 * sizeof(float), (void**)&d_GT));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux0, rows * sizeof(uint32_t), (void**)&d_gidx));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux1, rows * sizeof(uint32_t), (void**)&d_local));
   MVR_TRY(mvr::scratch(c, mvr::kSlotAux2, rows * sizeof(uint32_t) * 2 + (nd + 1) * 4 * 2 + nd * 4 + 1024,
@@ -316,10 +338,14 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   MVR_CUDA(c, cudaMemcpyAsync(d_goff, goff.data(), (nd + 1) * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_rowtok, rowtok.data(), rows * 4, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaEventRecord(tev[1], st));
-  MVR_TRY(mvr::km_gather_groups(c, d_V, d_gidx, rows, dim, d_G, d_GT));
+  // the sharded run gathers each rank's own tokens again below, so the
+  // full group-major copy is not needed there
+  MVR_TRY(mvr::km_gather_groups(c, d_V, d_gidx, rows, dim, d_G, G > 1 ? nullptr : d_GT));
   int* d_err = reinterpret_cast<int*>(d_sp + nd);
   MVR_CUDA(c, cudaMemsetAsync(d_err, 0, sizeof(int), st));
   MVR_TRY(mvr::launch_spreads(c, d_G, dim, d_goff, nd, d_sp, d_err));
+  // a rank whose spread pass timed out fails with all the others
+  if (G > 1) MVR_TRY(mvr::comm_allreduce_sum_u32(c, reinterpret_cast<uint32_t*>(d_err), 1));
   MVR_CUDA(c, cudaEventRecord(tev[2], st));
   std::vector<float> spreads(nd + 1);  // spreads, then the kernel's error flag
   MVR_CUDA(c, cudaMemcpyAsync(spreads.data(), d_sp, (nd + 1) * 4, cudaMemcpyDeviceToHost, st));
@@ -347,31 +373,108 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
   if (goffc[nd] != p->kappa_total) return mvr::fail(c, MVR_E_BUDGET_TOO_SMALL, "budgets do not sum to kappa_total");
 
   // ---- step 4: one k-means per token on the device -------------------------
+  // With several ranks each one runs the problems it owns on a compact copy
+  // of their rows (local row and centroid offsets).
+  std::vector<uint32_t> owner(nd, 0);
+  if (G > 1) mvr::tac_partition_tokens_host(freqs.data(), kap.data(), nd, (uint32_t)G, owner.data());
   mvr::KmBatch b;
   std::vector<uint32_t> pj;  // token id of each problem
+  uint64_t lrows = 0, lcent = 0;
   for (uint64_t j = 0; j < nd; ++j) {
-    if (kap[j] == 0 || freqs[j] == 0) continue;
-    b.off.push_back(goff[j]);
+    if (kap[j] == 0 || freqs[j] == 0 || owner[j] != (uint32_t)me) continue;
+    b.off.push_back(G > 1 ? lrows : goff[j]);
     b.n.push_back(freqs[j]);
     b.k.push_back(kap[j]);
-    b.coff.push_back(goffc[j]);
+    b.coff.push_back(G > 1 ? lcent : goffc[j]);
     b.seed.push_back(p->seed ^ (uint64_t)j);
     pj.push_back((uint32_t)j);
+    lrows += freqs[j];
+    lcent += kap[j];
+  }
+  std::vector<uint32_t> own_idx, own_tok, cmap;
+  if (G > 1) {
+    own_idx.resize(lrows);
+    own_tok.resize(lrows);
+    cmap.resize(lcent);
+    uint64_t q = 0, cc = 0;
+    for (uint32_t j : pj) {
+      for (uint32_t r = goff[j]; r < goff[j + 1]; ++r, ++q) {
+        own_idx[q] = gidx[r];
+        own_tok[q] = j;
+      }
+      for (uint32_t k = 0; k < kap[j]; ++k) cmap[cc++] = goffc[j] + k;
+    }
   }
   host_ms += since(t_budget);
   MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, (size_t)p->kappa_total * dim * sizeof(float), (void**)&d_C));
   mvr::KmResult r;
-  MVR_TRY(mvr::km_batch_run(c, d_G, d_GT, rows, dim, b, p->max_iters, p->tol, d_C, d_local, &r));
-  for (size_t q = 0; q < r.status.size(); ++q)  // the lowest failing token, as the serial reference reports
-    if (r.status[q] != MVR_OK)
-      return mvr::fail(c, r.status[q], std::string("token ") + std::to_string(pj[q]) + ": " +
-                                           mvr_status_name(r.status[q]));
+  float* d_CL = d_C;       // this rank's centroids (local rows when sharded)
+  uint32_t* d_oidx = nullptr;  // sharded: own rows' input positions, then their token ids
+  uint32_t* d_cmap = nullptr;  // sharded: global row of each local centroid, then the per-token info
+  if (G > 1) {
+    float *d_G2 = nullptr, *d_GT2 = nullptr;
+    MVR_TRY(mvr::scratch(c, mvr::kSlotAssign, std::max<uint64_t>(lrows * dim, 4) * sizeof(float), (void**)&d_G2));
+    MVR_TRY(mvr::scratch(c, mvr::kSlotHist, std::max<uint64_t>(lrows * ((dim + 3) / 4) * 4, 4) * sizeof(float),
+                         (void**)&d_GT2));
+    MVR_TRY(mvr::scratch(c, mvr::kSlotChunk, std::max<uint64_t>(2 * lrows, 4) * 4, (void**)&d_oidx));
+    MVR_TRY(mvr::scratch(c, mvr::kSlotCodes, std::max<uint64_t>(lcent * dim, 4) * sizeof(float), (void**)&d_CL));
+    MVR_TRY(mvr::scratch(c, mvr::kSlotSmall, (lcent + 3 * nd + 4) * 4, (void**)&d_cmap));
+    if (lrows) {
+      MVR_CUDA(c, cudaMemcpyAsync(d_oidx, own_idx.data(), lrows * 4, cudaMemcpyHostToDevice, st));
+      MVR_CUDA(c, cudaMemcpyAsync(d_oidx + lrows, own_tok.data(), lrows * 4, cudaMemcpyHostToDevice, st));
+      MVR_CUDA(c, cudaMemcpyAsync(d_cmap, cmap.data(), lcent * 4, cudaMemcpyHostToDevice, st));
+      MVR_TRY(mvr::km_gather_groups(c, d_V, d_oidx, lrows, dim, d_G2, d_GT2));
+    }
+    MVR_TRY(mvr::km_batch_run(c, d_G2, d_GT2, lrows, dim, b, p->max_iters, p->tol, d_CL, d_local, &r));
+  } else {
+    MVR_TRY(mvr::km_batch_run(c, d_G, d_GT, rows, dim, b, p->max_iters, p->tol, d_C, d_local, &r));
+  }
+
+  // per-token results of every rank: WCSS bits, status, iterations
+  std::vector<float> tw(nd, 0.f);
+  std::vector<uint32_t> tstat(nd, 0), titer(nd, 0);
+  for (size_t q = 0; q < pj.size(); ++q) {
+    tw[pj[q]] = r.wcss[q];
+    tstat[pj[q]] = (uint32_t)r.status[q];
+    titer[pj[q]] = r.iters[q];
+  }
+  MVR_CUDA(c, cudaMemcpyAsync(d_goffc, goffc.data(), (nd + 1) * 4, cudaMemcpyHostToDevice, st));
+  const int sgrid = (int)std::min<uint64_t>((rows + 255) / 256, (uint64_t)c->sm_count * 8);
+  if (G > 1) {
+    // every output value is written by exactly one rank and is zero on the
+    // others, so a u32 sum of the bit patterns merges them exactly
+    uint32_t* d_info = d_cmap + lcent;
+    std::vector<uint32_t> info(3 * nd);
+    std::memcpy(info.data(), tw.data(), nd * 4);
+    std::memcpy(info.data() + nd, tstat.data(), nd * 4);
+    std::memcpy(info.data() + 2 * nd, titer.data(), nd * 4);
+    MVR_CUDA(c, cudaMemcpyAsync(d_info, info.data(), 3 * nd * 4, cudaMemcpyHostToDevice, st));
+    MVR_TRY(mvr::comm_allreduce_sum_u32(c, d_info, 3 * nd));
+    MVR_CUDA(c, cudaMemcpyAsync(info.data(), d_info, 3 * nd * 4, cudaMemcpyDeviceToHost, st));
+    MVR_CUDA(c, cudaStreamSynchronize(st));
+    std::memcpy(tw.data(), info.data(), nd * 4);
+    std::memcpy(tstat.data(), info.data() + nd, nd * 4);
+    std::memcpy(titer.data(), info.data() + 2 * nd, nd * 4);
+  }
+  for (uint64_t j = 0; j < nd; ++j)  // the lowest failing token, as the serial reference reports
+    if (tstat[j] != MVR_OK)
+      return mvr::fail(c, (int)tstat[j], std::string("token ") + std::to_string(j) + ": " +
+                                             mvr_status_name((int)tstat[j]));
 
   // ---- outputs ----------------------------------------------------------------
-  MVR_CUDA(c, cudaMemcpyAsync(d_goffc, goffc.data(), (nd + 1) * 4, cudaMemcpyHostToDevice, st));
-  {
-    const int grid = (int)std::min<uint64_t>((rows + 255) / 256, (uint64_t)c->sm_count * 8);
-    mvr::tac_scatter_assign_kernel<<<grid, 256, 0, st>>>(d_gidx, d_rowtok, d_goffc, d_local, rows, d_asg);
+  if (G > 1) {
+    MVR_CUDA(c, cudaMemsetAsync(d_C, 0, (size_t)p->kappa_total * dim * sizeof(float), st));
+    MVR_CUDA(c, cudaMemsetAsync(d_asg, 0, rows * 4, st));
+    if (lrows) {
+      const int cgrid = (int)std::min<uint64_t>((lcent * dim + 255) / 256, (uint64_t)c->sm_count * 8);
+      mvr::tac_place_centroids_kernel<<<cgrid, 256, 0, st>>>(d_CL, d_cmap, lcent, dim, d_C);
+      mvr::tac_scatter_assign_kernel<<<sgrid, 256, 0, st>>>(d_oidx, d_oidx + lrows, d_goffc, d_local, lrows, d_asg);
+      MVR_CUDA(c, cudaGetLastError());
+    }
+    MVR_TRY(mvr::comm_allreduce_sum_u32(c, reinterpret_cast<uint32_t*>(d_C), (size_t)p->kappa_total * dim));
+    MVR_TRY(mvr::comm_allreduce_sum_u32(c, d_asg, rows));
+  } else {
+    mvr::tac_scatter_assign_kernel<<<sgrid, 256, 0, st>>>(d_gidx, d_rowtok, d_goffc, d_local, rows, d_asg);
     MVR_CUDA(c, cudaGetLastError());
   }
   MVR_CUDA(c, cudaEventRecord(tev[3], st));
@@ -384,8 +487,6 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
 
   // wcss_total: per-token WCSS summed in token order, per static thread chunk
   // when n_threads > 1 (tac.zig:685-825).
-  std::vector<float> tw(nd, 0.f);
-  for (size_t q = 0; q < pj.size(); ++q) tw[pj[q]] = r.wcss[q];
   float total = 0.f;
   const uint32_t nt = p->n_threads;
   if (nt <= 1) {
@@ -414,13 +515,33 @@ extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint6
     ts.seed_ms = r.seed_ms;
     ts.lloyd_ms = r.lloyd_ms;
     ts.problems = (uint32_t)pj.size();
-    ts.iters_max = r.iters.empty() ? 0u : *std::max_element(r.iters.begin(), r.iters.end());
+    ts.iters_max = 0;
+    for (uint64_t j = 0; j < nd; ++j) ts.iters_max = std::max(ts.iters_max, titer[j]);
     ts.seed_fallbacks = r.seed_fallbacks;
-    ts.launches = r.launches + 4;
+    ts.launches = r.launches + (G > 1 ? 6 : 4);
     ts.host_ms = host_ms + since(t_tail);
     ts.total_ms = since(t_start);
   }
   for (uint64_t i = 0; i < n_tokens; ++i)  // final invariant (tac.zig:827-830)
     if (assignments_out[i] >= p->kappa_total) return mvr::fail(c, MVR_E_INVALID_THRESHOLDS, "assignment out of range");
   return MVR_OK;
+}
+
+}  // namespace
+
+extern "C" int mvr_tac_cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens, const float* vectors,
+                                    uint64_t vectors_len, uint32_t dim, const mvr_clustering_params* p,
+                                    float* centroids_out, uint32_t* assignments_out, uint32_t* kappa_out,
+                                    uint64_t kappa_cap, uint64_t* n_distinct_out, float* wcss_total_out) {
+  return cluster_flat(h, token_ids, n_tokens, vectors, vectors_len, dim, p, centroids_out, assignments_out,
+                      kappa_out, kappa_cap, n_distinct_out, wcss_total_out, false);
+}
+
+extern "C" int mvr_tac_cluster_flat_sharded(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens,
+                                            const float* vectors, uint64_t vectors_len, uint32_t dim,
+                                            const mvr_clustering_params* p, float* centroids_out,
+                                            uint32_t* assignments_out, uint32_t* kappa_out, uint64_t kappa_cap,
+                                            uint64_t* n_distinct_out, float* wcss_total_out) {
+  return cluster_flat(h, token_ids, n_tokens, vectors, vectors_len, dim, p, centroids_out, assignments_out,
+                      kappa_out, kappa_cap, n_distinct_out, wcss_total_out, true);
 }

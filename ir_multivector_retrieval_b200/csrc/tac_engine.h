@@ -20,4 +20,15 @@ int tac_allocate_budgets_host(const uint32_t* freqs, const float* spreads, uint3
                               float* frac, uint64_t n, uint32_t kappa_total, uint32_t mu,
                               uint32_t tau, uint32_t eps, uint32_t theta);
 
+// Work estimate of one token's k-means: n * (k + 1) distance evaluations
+// per pass when k < n, n for the degenerate copy (k >= n), 0 without a
+// problem.
+uint64_t tac_token_work(uint32_t n, uint32_t k);
+
+// Longest-processing-time split of the per-token k-means problems over
+// `ranks` GPUs: owner[j] in [0, ranks) for every token (0 for tokens with
+// no problem).
+void tac_partition_tokens_host(const uint32_t* freqs, const uint32_t* kappa, uint64_t n, uint32_t ranks,
+                               uint32_t* owner);
+
 }  // namespace mvr

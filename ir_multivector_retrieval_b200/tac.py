@@ -68,7 +68,25 @@ def last_stats(ctx=None) -> dict:
     return st.as_dict()
 
 
-def cluster_flat(token_ids, vectors, dim: int, p: ClusteringParams, ctx=None) -> ClusteringResult:
+def partition_tokens(freqs, kappa, n_ranks: int) -> np.ndarray:
+    """Owner rank of every token's k-means in the sharded clusterFlat
+    (longest-processing-time split of the work n_j * (k_j + 1))."""
+    f = np.ascontiguousarray(freqs, dtype=np.uint32)
+    k = np.ascontiguousarray(kappa, dtype=np.uint32)
+    if f.size != k.size:
+        raise ValueError("freqs and kappa differ in length")
+    out = np.zeros(max(f.size, 1), dtype=np.uint32)
+    st = _lib.load().mvr_tac_partition_tokens(ptr(f), ptr(k), f.size, n_ranks, ptr(out))
+    if st:
+        raise _lib.MvrError(st, "partition_tokens")
+    return out[: f.size]
+
+
+def cluster_flat(token_ids, vectors, dim: int, p: ClusteringParams, ctx=None, *,
+                 sharded: bool = False) -> ClusteringResult:
+    """tac.clusterFlat (src/tac/tac.zig:563-838) on the GPU. With
+    ``sharded=True`` the call is collective over the context's communicator
+    (every rank passes the same inputs and gets the same full result)."""
     ids = np.ascontiguousarray(token_ids, dtype=np.uint32).reshape(-1)
     v = np.ascontiguousarray(vectors, dtype=np.float32).reshape(-1)
     ctx = ctx or _lib.default_context()
@@ -79,7 +97,7 @@ def cluster_flat(token_ids, vectors, dim: int, p: ClusteringParams, ctx=None) ->
     ndo = C.c_uint64(0)
     w = C.c_float(0)
     cp = p.to_c()
-    ctx.check(ctx.lib.mvr_tac_cluster_flat(ctx.handle, ptr(ids), ids.size, ptr(v), v.size, dim,
-                                           C.byref(cp), ptr(cent), ptr(asg), ptr(kap), nd, C.byref(ndo),
-                                           C.byref(w)))
+    fn = ctx.lib.mvr_tac_cluster_flat_sharded if sharded else ctx.lib.mvr_tac_cluster_flat
+    ctx.check(fn(ctx.handle, ptr(ids), ids.size, ptr(v), v.size, dim, C.byref(cp), ptr(cent), ptr(asg), ptr(kap), nd,
+                 C.byref(ndo), C.byref(w)))
     return ClusteringResult(cent[: p.kappa_total * dim], asg[: ids.size], kap[: ndo.value], float(w.value))

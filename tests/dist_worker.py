@@ -5,10 +5,13 @@ Every rank trains PQ codebooks on its contiguous row shard through
 ``mvr_pq_train_sharded_device``; rank 0 also trains on the whole matrix with
 the one-GPU entry point. The codebooks must be byte-identical on every rank
 and equal to the one-GPU result; the local assignments must equal the
-matching rows of the one-GPU assignments. Exit status 0 = pass.
+matching rows of the one-GPU assignments. Then every rank runs the
+token-sharded clusterFlat; its outputs must equal the one-GPU call's on every
+rank. Exit status 0 = pass.
 """
 import ctypes as C
 import datetime
+import hashlib
 import math
 import os
 import sys
@@ -19,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
-from ir_multivector_retrieval_b200 import Context, dist as mdist, synth  # noqa: E402
+from ir_multivector_retrieval_b200 import Context, dist as mdist, synth, tac  # noqa: E402
 from ir_multivector_retrieval_b200._lib import PqTrainStats  # noqa: E402
 
 
@@ -110,6 +113,43 @@ def main() -> int:
                   f"sharded_ms={st['total_ms']:.1f} one_gpu_ms={st1.total_ms:.1f}", flush=True)
         dist.barrier()
     ctx.check(ctx.lib.mvr_ctx_set_serial_draws(ctx.handle, 0))
+    # clusterFlat split over the ranks by token: the full outputs on every
+    # rank, equal to the one-GPU call (and, for the small case, the oracle)
+    tac_cases = [(60_000, 64, 8192, 10, 4, False), (20_000, 24, 3000, 10, 1, True), (3_000, 8, 600, 2, 1, False)]
+    for n, dim, kappa, theta, threads, with_oracle in tac_cases:
+        c = synth.make_corpus(n, dim, n_anchors=50 if n == 3_000 else 19221, seed=n + dim)
+        kw = dict(mu=8, tau=16, epsilon=2) if n == 3_000 else {}
+        p = tac.ClusteringParams(kappa, 42, theta=theta, n_threads=threads, **kw)
+        got = tac.cluster_flat(c.token_ids, c.vectors, dim, p, ctx=ctx, sharded=True)
+        st = tac.last_stats(ctx)
+        digest = hashlib.sha256(got.centroids.tobytes() + got.assignments.tobytes() +
+                                got.kappa_per_token.tobytes() + np.float32(got.wcss_total).tobytes()).hexdigest()
+        alld = [None] * world
+        dist.all_gather_object(alld, (digest, st["problems"]))
+        if rank == 0:
+            ctx1 = Context(local)
+            one = tac.cluster_flat(c.token_ids, c.vectors, dim, p, ctx=ctx1)
+            st1 = tac.last_stats(ctx1)
+            ctx1.close()
+            d1 = hashlib.sha256(one.centroids.tobytes() + one.assignments.tobytes() +
+                                one.kappa_per_token.tobytes() + np.float32(one.wcss_total).tobytes()).hexdigest()
+            if len({d for d, _ in alld}) != 1:
+                failures.append(f"tac {n}x{dim}: outputs differ across ranks")
+            if d1 != alld[0][0]:
+                failures.append(f"tac {n}x{dim}: sharded clusterFlat != one-GPU clusterFlat")
+            if sum(q for _, q in alld) != st1["problems"]:
+                failures.append(f"tac {n}x{dim}: problems split {[q for _, q in alld]} != {st1['problems']}")
+            if with_oracle:
+                from oracle import oracle as orc
+
+                want = orc.tac_cluster_flat(c.token_ids, c.vectors, dim, kappa, 42, mu=p.mu, tau=p.tau,
+                                            eps=p.epsilon, theta=p.theta, n_threads=threads)
+                if not (np.array_equal(got.assignments, want.assignments) and
+                        got.centroids.tobytes() == want.centroids.tobytes()):
+                    failures.append(f"tac {n}x{dim}: sharded clusterFlat != oracle")
+            print(f"[dist] tac {n}x{dim} kappa={kappa} world={world} problems={[q for _, q in alld]} "
+                  f"sharded_ms={st['total_ms']:.1f} one_gpu_ms={st1['total_ms']:.1f}", flush=True)
+        dist.barrier()
     ok = [not failures]
     dist.broadcast_object_list(ok, src=0)
     if rank == 0:

@@ -1,7 +1,8 @@
 """Host logic of the row-sharded path on CPU: shard bounds, the NCCL id
 hand-off over a torch group, and the Lloyd exchange protocol (running f32
 sums carried rank to rank, counts summed) run by two gloo ranks against the
-single serial loop of the reference."""
+single serial loop of the reference; the token split and the exact merge of
+the sharded clusterFlat."""
 import os
 import socket
 
@@ -102,3 +103,103 @@ def test_two_gloo_ranks_exchange_protocol():
     assert all(p.exitcode == 0 for p in procs)
     ok_uid, ok_sums, ok_counts = q.get(timeout=10)
     assert ok_uid and ok_sums and ok_counts
+
+
+def _lpt_model(freqs, kappa, world):
+    """Longest-processing-time split restated in Python."""
+    def work(n, k):
+        if n == 0 or k == 0:
+            return 0
+        return n * (k + 1) if k < n else n
+
+    owner = [0] * len(freqs)
+    order = sorted((j for j in range(len(freqs)) if work(int(freqs[j]), int(kappa[j])) > 0),
+                   key=lambda j: (-work(int(freqs[j]), int(kappa[j])), j))
+    load = [0] * world
+    for j in order:
+        r = min(range(world), key=lambda q: (load[q], q))
+        owner[j] = r
+        load[r] += work(int(freqs[j]), int(kappa[j]))
+    return np.array(owner, np.uint32), load
+
+
+def test_partition_tokens_is_lpt():
+    from ir_multivector_retrieval_b200 import tac
+
+    rng = np.random.default_rng(3)
+    for world in (1, 2, 3, 8):
+        freqs = rng.zipf(1.3, size=500).astype(np.uint32)
+        freqs[rng.integers(0, 500, size=40)] = 0
+        kappa = np.minimum(freqs, rng.integers(0, 40, size=500)).astype(np.uint32)
+        kappa[rng.integers(0, 500, size=10)] = 0
+        got = tac.partition_tokens(freqs, kappa, world)
+        want, load = _lpt_model(freqs, kappa, world)
+        assert np.array_equal(got, want)
+        assert int(got.max()) < world
+        # LPT bound: no rank exceeds the mean load by more than the largest item
+        biggest = max((int(f) * (int(k) + 1) if k < f else int(f)) for f, k in zip(freqs, kappa) if f and k)
+        assert max(load) <= sum(load) / world + biggest
+    assert tac.partition_tokens(np.zeros(0, np.uint32), np.zeros(0, np.uint32), 4).size == 0
+    with pytest.raises(Exception):
+        tac.partition_tokens([1, 2], [1, 1], 0)
+
+
+def _tac_worker(rank, world, port, ret):
+    """The sharded clusterFlat protocol on CPU: spreads and budgets on every
+    rank, the per-token k-means of the owned tokens only (oracle restatement),
+    outputs zero elsewhere, then one u32-sum all-reduce of the bit patterns."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ir_multivector_retrieval_b200 import synth, tac
+    from oracle import oracle as orc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        c = synth.make_corpus(4_000, 8, n_anchors=60, seed=11)
+        dim, kappa_total, seed, kw = 8, 700, 5, dict(mu=8, tau=16, eps=2, theta=4)
+        ids, vec = c.token_ids, c.vectors
+        freqs, spreads = orc.tac_spreads(ids, vec, dim)
+        kap = orc.tac_allocate_budgets(freqs, spreads, kappa_total, **kw)
+        goffc = np.concatenate([[0], np.cumsum(kap.astype(np.int64))])
+        owner = tac.partition_tokens(freqs, kap, world)
+        cent = np.zeros(kappa_total * dim, np.float32)
+        asg = np.zeros(ids.size, np.uint32)
+        for j in np.flatnonzero((freqs > 0) & (kap > 0) & (owner == rank)):
+            rows = np.flatnonzero(ids == j)
+            r = orc.kmeans_fit(vec[rows], dim, int(kap[j]), seed ^ int(j))
+            cent[goffc[j] * dim:(goffc[j] + kap[j]) * dim] = r.centroids
+            asg[rows] = goffc[j] + r.assignments
+        merged = torch.from_numpy(np.concatenate([cent.view(np.int32), asg.view(np.int32)]))
+        dist.all_reduce(merged)  # int32 sum == u32 sum of bit patterns here (no carries)
+        m = merged.numpy()
+        if rank == 0:
+            want = orc.tac_cluster_flat(ids, vec, dim, kappa_total, seed, **kw)
+            got_c = m[: cent.size].view(np.float32)
+            got_a = m[cent.size:].view(np.uint32)
+            ret.put((got_c.tobytes() == want.centroids.tobytes(), np.array_equal(got_a, want.assignments),
+                     len(set(owner[(freqs > 0) & (kap > 0)].tolist()))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_cluster_flat_merge():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tac_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    ok_c, ok_a, n_owners = q.get(timeout=10)
+    assert ok_c and ok_a and n_owners == 2
