@@ -172,6 +172,10 @@ typedef struct mvr_pq_train_stats {
   uint64_t lloyd_rows_total; /* (row, subspace) assignments over all Lloyd iterations */
   uint64_t lloyd_rows_exact; /* of those, the ones whose K distances were all computed
                                 (the rest kept their cluster by exact bounds) */
+  uint64_t filter_rows_rechecked; /* tensor-core filter: rows whose near-ties were
+                                     settled by exact distances */
+  uint32_t filter_violations;     /* winners outside the filter's error bound (then the
+                                     training ran again with exact scans); 0 expected */
 } mvr_pq_train_stats;
 
 /* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`
@@ -358,6 +362,20 @@ int mvr_ctx_set_serial_draws(mvr_ctx* ctx, int on);
  * skipping rows whose exact distance bounds prove their cluster unchanged.
  * Results are identical either way; only the speed differs. */
 int mvr_ctx_set_exhaustive_assign(mvr_ctx* ctx, int on);
+
+/* Verification mode (no reference counterpart): with `on` == 0 the Lloyd
+ * and encode assignments skip the tensor-core filter (a TF32 MMA chain that
+ * approximates every distance within a proven bound, after which only the
+ * near-ties get exact distances) and scan every centroid with the exact
+ * f32 arithmetic. Results are identical either way; on is the default. */
+int mvr_ctx_set_tensor_filter(mvr_ctx* ctx, int on);
+
+/* Counters of the filtered encode passes on this context since it was
+ * created: winners whose approximation fell outside the filter's error
+ * bound (0 expected; the host-pointer encode then re-runs exactly) and rows
+ * whose near-ties were settled by exact distances. Synchronises the
+ * context's stream; MVR_E_TIMEOUT if an MMA did not complete. */
+int mvr_ctx_filter_report(mvr_ctx* ctx, uint64_t* violations, uint64_t* rows_rechecked);
 
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);

@@ -74,6 +74,8 @@ class PqTrainStats(C.Structure):
         ("assign_first_ms", C.c_double),
         ("lloyd_rows_total", C.c_uint64),
         ("lloyd_rows_exact", C.c_uint64),
+        ("filter_rows_rechecked", C.c_uint64),
+        ("filter_violations", C.c_uint32),
     ]
 
 
@@ -145,6 +147,8 @@ SIGNATURES = {
          _P, C.c_uint64, C.c_uint32, _P, C.c_uint64, _P, _P],
     ),
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_set_tensor_filter": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_filter_report": (C.c_int, [_P, _U64, _U64]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),
     "mvr_ctx_init_comm": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_size_t]),

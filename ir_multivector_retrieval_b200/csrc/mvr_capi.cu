@@ -212,6 +212,7 @@ int mvr_ctx_destroy(mvr_ctx* h) {
     cudaStreamSynchronize(c->side);
     cudaStreamDestroy(c->side);
   }
+  if (c->tc_diag) cudaFree(c->tc_diag);
   mvr::destroy_comm(c);
   mvr::destroy_host_io(c);
   for (auto& e : c->tev)
@@ -227,6 +228,26 @@ int mvr_ctx_set_serial_draws(mvr_ctx* h, int on) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   h->impl.serial_draws = on != 0;
   return MVR_OK;
+}
+
+int mvr_ctx_set_tensor_filter(mvr_ctx* h, int on) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.tc_filter = on != 0;
+  return MVR_OK;
+}
+
+int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_rechecked) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  Ctx* c = &h->impl;
+  uint32_t dg[4] = {0, 0, 0, 0};
+  if (c->tc_diag) {
+    MVR_TRY(mvr::set_device(c));
+    MVR_CUDA(c, cudaMemcpyAsync(dg, c->tc_diag, sizeof(dg), cudaMemcpyDeviceToHost, c->stream));
+    MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  }
+  if (violations) *violations = dg[0];
+  if (rows_rechecked) *rows_rechecked = dg[1];
+  return dg[2] ? mvr::fail(c, MVR_E_TIMEOUT, "tensor-core filter: an MMA did not complete in time") : MVR_OK;
 }
 
 int mvr_ctx_set_exhaustive_assign(mvr_ctx* h, int on) {
@@ -387,6 +408,19 @@ int mvr_pq_encode(mvr_ctx* h, const float* cb, uint32_t dim, uint32_t pq_m, cons
   MVR_TRY(mvr::h2d(c, d_cb, cb, cb_floats * sizeof(float)));
   MVR_TRY(mvr::h2d(c, d_res, res, n * dim * sizeof(float)));
   MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes));
+  if (c->tc_filter && !c->exhaustive_assign && c->tc_diag) {
+    uint32_t dg[4] = {0, 0, 0, 0};
+    MVR_CUDA(c, cudaMemcpyAsync(dg, c->tc_diag, sizeof(dg), cudaMemcpyDeviceToHost, c->stream));
+    MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (dg[2]) return mvr::fail(c, MVR_E_TIMEOUT, "tensor-core filter: an MMA did not complete in time");
+    if (dg[0] > c->tc_viol_seen) {  // a winner broke the filter's error bound: encode again exactly
+      c->tc_viol_seen = dg[0];
+      c->tc_filter = false;
+      const int s2 = mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes);
+      c->tc_filter = true;
+      MVR_TRY(s2);
+    }
+  }
   MVR_TRY(mvr::d2h(c, codes_out, d_codes, n * pq_m));
   MVR_CUDA(c, cudaStreamSynchronize(c->stream));
   return MVR_OK;

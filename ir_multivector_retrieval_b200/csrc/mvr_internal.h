@@ -64,6 +64,12 @@ struct Ctx {
   bool serial_draws = false;
   // compute every Lloyd distance (no bound pruning)
   bool exhaustive_assign = false;
+  // tensor-core filtered assignment passes (off: the exact scans only)
+  bool tc_filter = true;
+  // device counters of the filtered encode passes (created on first use):
+  // [0] violations, [1] rows re-scanned, [2] timeouts
+  uint32_t* tc_diag = nullptr;
+  uint32_t tc_viol_seen = 0;  // violations already answered by an exact re-run
 };
 
 // Host->device copy of a pageable host buffer through the pinned stages;

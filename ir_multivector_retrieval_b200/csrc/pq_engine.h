@@ -26,6 +26,8 @@ struct PqJob {
   // the workspace's subspace-major copy XT (pq_layout o_xt) already holds the
   // rows; R is then not read
   bool xt_ready = false;
+  // assignment passes through the tensor-core filter (pq_tc_assign_kernel)
+  bool tc_filter = true;
 };
 
 struct PqOut {
@@ -48,6 +50,9 @@ struct PqLayout {
   // Lloyd bound pruning: bounds [M][N] f32 x2, per-subspace row lists
   // [M][N] u32 + counts, previous codebooks, drifts [M][K], max drift [M]
   size_t o_ub = 0, o_lb = 0, o_list = 0, o_lcnt = 0, o_cbold = 0, o_drift = 0, o_maxd = 0;
+  // tensor-core filter counters (in the bookkeeping block): violations,
+  // rows re-scanned, timeouts
+  size_t o_diag = 0;
   size_t total_bytes = 0;
 };
 // Workspace layout for N rows, M subspaces of S floats, K centroids on a

@@ -115,7 +115,7 @@ def main() -> int:
     ctx.check(ctx.lib.mvr_ctx_set_serial_draws(ctx.handle, 0))
     # clusterFlat split over the ranks by token: the full outputs on every
     # rank, equal to the one-GPU call (and, for the small case, the oracle)
-    tac_cases = [(60_000, 64, 8192, 10, 4, False), (20_000, 24, 3000, 10, 1, True), (3_000, 8, 600, 2, 1, False)]
+    tac_cases = [(20_000, 64, 4096, 10, 8, False), (25_000, 24, 5000, 10, 3, True), (3_000, 8, 600, 2, 1, False)]
     for n, dim, kappa, theta, threads, with_oracle in tac_cases:
         c = synth.make_corpus(n, dim, n_anchors=50 if n == 3_000 else 19221, seed=n + dim)
         kw = dict(mu=8, tau=16, epsilon=2) if n == 3_000 else {}

@@ -283,3 +283,56 @@ def test_bound_pruning_matches_exhaustive(ctx, orc):
         assert st_p["iters_max"] == st_e["iters_max"]
         want = orc.pq_train(x, 32, 5, 8, n_threads=THREADS, max_iters=iters, tol=tol)
         assert pruned.codebooks.tobytes() == want.tobytes()
+
+
+def _filter_report(ctx):
+    import ctypes as C
+
+    v, r = C.c_uint64(0), C.c_uint64(0)
+    ctx.check(ctx.lib.mvr_ctx_filter_report(ctx.handle, C.byref(v), C.byref(r)))
+    return v.value, r.value
+
+
+def _filter_datasets():
+    rng = np.random.default_rng(21)
+    base = synth.unit_rows(300, 32, seed=4)
+    yield "unit64", _rows(30_011, 64, seed=31), 64, 16
+    yield "unit32_s2", _rows(20_000, 32, seed=32), 32, 16
+    yield "unit8_s1", _rows(9_000, 8, seed=33), 8, 8
+    yield "dup", base[rng.integers(0, 300, size=12_000)], 32, 16  # exact ties, zero distances
+    yield "scaled_up", (_rows(8_000, 16, seed=34) * 1e3).astype(np.float32), 16, 4
+    yield "scaled_down", (_rows(8_000, 16, seed=35) * 1e-3).astype(np.float32), 16, 4
+    mixed = _rows(8_000, 16, seed=36)
+    mixed[::7] *= 1e4
+    mixed[3::11] *= 1e-5
+    yield "mixed", mixed.astype(np.float32), 16, 4
+    big = _rows(5_000, 16, seed=37)
+    big[::13] *= 1e15  # |x|^2 above 2^60: the exact scan takes these rows
+    yield "huge", big.astype(np.float32), 16, 4
+    q = (np.round(_rows(6_000, 16, seed=38) * 8) / 8).astype(np.float32)  # a coarse grid: many equal distances
+    yield "grid", q, 16, 4
+
+
+@pytest.mark.parametrize("name,x,dim,m", list(_filter_datasets()), ids=lambda v: v if isinstance(v, str) else "")
+def test_tensor_filter_matches_exact_scans(ctx, orc, name, x, dim, m):
+    """The tensor-core filtered assignment (default) and the exact scans give
+    the same codebooks and codes, equal to the oracle; no winner falls outside
+    the filter's error bound."""
+    st_f, st_e = {}, {}
+    f = pq.train(x, dim, 5, pq_m=m, max_iters=8, tol=1e-4, ctx=ctx, stats=st_f)
+    codes_f = f.encode_batch(x)
+    ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 0))
+    try:
+        e = pq.train(x, dim, 5, pq_m=m, max_iters=8, tol=1e-4, ctx=ctx, stats=st_e)
+        codes_e = e.encode_batch(x)
+    finally:
+        ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))
+    want = orc.pq_train(x, dim, 5, m, n_threads=THREADS, max_iters=8, tol=1e-4)
+    assert f.codebooks.tobytes() == want.tobytes()
+    assert e.codebooks.tobytes() == want.tobytes()
+    assert np.array_equal(codes_f, codes_e)
+    assert np.array_equal(codes_f, orc.pq_encode(want, dim, m, x, n_threads=THREADS))
+    assert st_f["filter_violations"] == 0 and st_e["filter_rows_rechecked"] == 0
+    viol, _ = _filter_report(ctx)
+    assert viol == 0
+
