@@ -119,6 +119,8 @@ def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=
                 "phases_ms": {k: st[k] for k in ("host_ms", "h2d_ms", "spread_ms", "seed_ms", "lloyd_ms",
                                                  "d2h_ms")},
                 "tokens": st["problems"], "iters_max": st["iters_max"], "gpu_launches": st["launches"],
+                "filter": {"rows_rechecked": st["filter_rows_rechecked"], "violations": st["filter_violations"],
+                           "rows_full_scan": st["filter_rows_full_scan"]},
                 "wcss_total": r.wcss_total, "outputs_sha256": sorted(digests)[0],
                 "repeatable": len(digests) == 1})
     if sharded:

@@ -345,6 +345,12 @@ typedef struct mvr_tac_stats {
   uint32_t iters_max; /* largest iters_run over tokens */
   uint32_t seed_fallbacks; /* k-means++ draws resolved by the exact serial chain */
   uint32_t launches; /* kernel launches of the call */
+  uint64_t filter_rows_rechecked; /* tensor-core filter: row assignments with several
+                                     candidates settled by exact distances */
+  uint32_t filter_violations;     /* winners outside the filter's bound (then the per-token
+                                     k-means ran again with exact scans); 0 expected */
+  uint64_t filter_rows_full_scan; /* row assignments whose candidate list overflowed and
+                                     took the exact scan over all centroids */
 } mvr_tac_stats;
 
 /* Copies the report of the context's most recent `mvr_tac_cluster_flat`

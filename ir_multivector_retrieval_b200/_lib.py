@@ -92,6 +92,9 @@ class TacStats(C.Structure):
         ("iters_max", C.c_uint32),
         ("seed_fallbacks", C.c_uint32),
         ("launches", C.c_uint32),
+        ("filter_rows_rechecked", C.c_uint64),
+        ("filter_violations", C.c_uint32),
+        ("filter_rows_full_scan", C.c_uint64),
     ]
 
     def as_dict(self) -> dict:

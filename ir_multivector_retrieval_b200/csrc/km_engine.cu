@@ -31,6 +31,7 @@
 #include "km_engine.h"
 #include "mvr_device.cuh"
 #include "mvr_rng.h"
+#include "tc_filter.cuh"
 
 namespace mvr {
 namespace {
@@ -491,6 +492,440 @@ km_assign_kernel(const float* __restrict__ G, int d_rt, Prob P, const uint32_t* 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core filtered Lloyd assignment for 64-dimensional rows (the TAC
+// path) and problems with at least kKmTcMinK centroids.
+//
+// For a 128-row tile of problem p, the centroids go through in blocks of
+// 256 columns; per block a chain of nine kind::tf32 MMAs (eight k-steps of
+// the rows' TF32 values against -2c, plus one carrying |c|^2 and the row
+// constant t) leaves a(c) = t + fl(|c|^2) - 2 x.c in a 256-column TMEM
+// accumulator. With TF32 truncation of both operands (< 2^-10 relative
+// each) and nine f32 accumulations,
+//   |a(c) - (t + fl(|c|^2) - 2 x.c)| <= E = 2^-7 |x| max|c| + 2^-9 max|c|^2
+//                                         + 2^-16 t + 2^-100,
+// about twice the worst case. The reference winner (first minimum of the
+// exact f32 distances, within 1 +- 2^-19 of the exact squared distances for
+// 64 coordinates) then has a(w) <= T = a(c1) + 2E + 2^-17 D(c1) + 2 delta,
+// delta = 2^-17 max|c|^2 bounding the f32 error of |c|^2. Each block's two
+// smallest keys (f32 bits, low 8 bits = column) are merged into the row's
+// running minimum; a block whose keys fall at or below the running T adds
+// its columns at or below it to the row's candidate list (a re-read of the
+// accumulator when there are several). T only shrinks as blocks go by, so
+// the list holds every column at or below the final T, in column order; the
+// exact 64-coordinate distances of the candidates decide, first minimum
+// first. Lists that overflow, non-finite or huge rows, and problems whose
+// centroids are non-finite or huge take the reference's full scan.
+//
+// One CTA per SM (two 256-column accumulators = all of TMEM): the block
+// b + 1 centroid tile arrives by one bulk copy and its MMA chain runs while
+// the four warps scan block b. Every wait is bounded; an expired wait sets
+// *err and the CTA stops.
+// ---------------------------------------------------------------------------
+constexpr int kKmTcMinK = 64;
+constexpr int kKmTcDim = 64;
+constexpr int kKmTcSteps = kKmTcDim / 8 + 1;                     // k-steps per MMA chain
+constexpr uint32_t kKmTcCols = 128;                              // centroids per block
+constexpr uint32_t kKmTcStepB = kKmTcCols * 32;                  // one k-step of a block
+constexpr uint32_t kKmTcBlockBytes = kKmTcSteps * kKmTcStepB;    // one 128-centroid block
+constexpr uint32_t kKmTcABytes = kKmTcSteps * tc::kTileBytesA;   // one 128-row tile
+constexpr int kKmTcList = 16;                                    // candidates per row
+constexpr int kKmTcRows = 256;                                   // rows per unit (two warpgroups)
+constexpr size_t kKmTcSmem = 2 * (size_t)kKmTcBlockBytes + 2 * (size_t)kKmTcABytes + kKmTcRows * kKmTcList * 8 + 1024;
+constexpr float kKmTcPad = 0x1p64f;
+constexpr float kKmTcHuge = 0x1p60f;
+
+// Centroid block (p, b) of the filter into Bg: k-step s < 8 holds
+// hi(-2 c[8s .. 8s+7]) of the 128 columns, step 8 holds (hi(fl(|c|^2)), 1);
+// columns past k get the padding |c|^2 = 2^64. cmx[p] = max over the
+// problem of |c|^2 rounded up (as f32 bits); bad[p] flags non-finite or
+// huge centroids.
+__global__ void __launch_bounds__(kKmTcCols)
+km_tc_prep_kernel(Prob P, const uint2* __restrict__ blocks, const float* __restrict__ C,
+                  unsigned char* __restrict__ Bg, uint32_t* __restrict__ cmx, uint32_t* __restrict__ bad) {
+  const uint2 pb = blocks[blockIdx.x];
+  const uint32_t p = pb.x, bk = pb.y;
+  if (P.state[p] != kRunning) return;
+  const uint32_t k = P.k[p], col = threadIdx.x, c = bk * kKmTcCols + col;
+  const bool real = c < k;
+  unsigned char* out = Bg + (size_t)blockIdx.x * kKmTcBlockBytes;
+  float cn = 0.f, cn_up = 0.f;
+  bool fin = true;
+  const float* cv = C + (P.coff[p] + (real ? c : 0)) * kKmTcDim;
+#pragma unroll
+  for (int s = 0; s < kKmTcDim / 8; ++s) {
+    float h[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float v = real ? cv[8 * s + q] : 0.f;
+      cn = __fadd_rn(cn, __fmul_rn(v, v));
+      cn_up = __fadd_ru(cn_up, __fmul_ru(v, v));
+      fin = fin && isfinite(v);
+      h[q] = __uint_as_float(__float_as_uint(__fmul_rn(-2.0f, v)) & 0xFFFFE000u);
+    }
+    unsigned char* t = out + (size_t)s * kKmTcStepB;
+    *reinterpret_cast<float4*>(t + tc::operand_offset(col, 0)) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(t + tc::operand_offset(col, 4)) = make_float4(h[4], h[5], h[6], h[7]);
+  }
+  const bool ok = fin && cn_up <= kKmTcHuge;
+  unsigned char* t = out + (size_t)(kKmTcSteps - 1) * kKmTcStepB;
+  *reinterpret_cast<float4*>(t + tc::operand_offset(col, 0)) =
+      (real && ok) ? make_float4(__uint_as_float(__float_as_uint(cn) & 0xFFFFE000u), 1.0f, 0.f, 0.f)
+                   : make_float4(kKmTcPad, 0.f, 0.f, 0.f);
+  *reinterpret_cast<float4*>(t + tc::operand_offset(col, 4)) = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (real) {
+    if (!ok) atomicOr(&bad[p], 1u);
+    else atomicMax(&cmx[p], __float_as_uint(cn_up));  // non-negative floats order as integers
+  }
+}
+
+// Reference order for the full scan: best starts at dists[0] (kmeans.zig
+// assignSlice), then the first strictly smaller distance.
+__device__ __noinline__ void km_tc_full_scan(const float* __restrict__ xg, const float* __restrict__ C, uint64_t co,
+                                             uint32_t k, float& best, uint32_t& bi) {
+  float x[kKmTcDim];
+#pragma unroll
+  for (int q = 0; q < kKmTcDim; q += 4) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(xg + q));
+    x[q] = v.x; x[q + 1] = v.y; x[q + 2] = v.z; x[q + 3] = v.w;
+  }
+  best = 0.f;
+  bi = 0;
+  for (uint32_t c = 0; c < k; ++c) {
+    float cl[kKmTcDim];
+#pragma unroll
+    for (int q = 0; q < kKmTcDim; q += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(C + (co + c) * kKmTcDim + q));
+      cl[q] = v.x; cl[q + 1] = v.y; cl[q + 2] = v.z; cl[q + 3] = v.w;
+    }
+    const float f = l2_wide<kKmTcDim>(x, cl);
+    if (c == 0) best = f;
+    else if (f < best) { best = f; bi = c; }
+  }
+}
+
+// Candidate list of one row: (column, key) pairs; a full list first drops
+// the entries that the current (smaller) threshold has ruled out.
+__device__ __forceinline__ void km_tc_push(uint2* l, int& nl, bool& ovf, uint32_t col, uint32_t key, uint32_t thr) {
+  if (nl == kKmTcList) {
+    int keep = 0;
+    for (int e = 0; e < nl; ++e) {
+      const uint2 en = l[e];
+      if (en.y <= thr) l[keep++] = en;
+    }
+    nl = keep;
+  }
+  if (nl < kKmTcList) l[nl++] = make_uint2(col, key);
+  else ovf = true;
+}
+
+// Units: up to 256 rows of one problem. Warps 0-3 and 4-7 (warpgroups 0 and
+// 1) own rows 0-127 and 128-255 of the unit, one row per thread (= TMEM
+// lane); warp 8 is the producer: it bulk-copies the centroid blocks (two
+// buffers) and issues, per block, one MMA chain per warpgroup into that
+// warpgroup's next accumulator slot (two 128-column slots each, so the chain
+// of block b + 1 runs while block b is scanned).
+__global__ void __launch_bounds__(288, 1)
+km_tc_assign_kernel(const float* __restrict__ G, Prob P, const uint32_t* __restrict__ u_p,
+                    const uint64_t* __restrict__ u_r0, const uint32_t* __restrict__ u_len, uint32_t nunits,
+                    const uint32_t* __restrict__ bbase, const unsigned char* __restrict__ Bg,
+                    const uint32_t* __restrict__ cmx, const uint32_t* __restrict__ bad,
+                    const float* __restrict__ C, uint32_t* __restrict__ local, float* __restrict__ mind,
+                    uint32_t* __restrict__ keys, uint32_t* __restrict__ diag) {
+  extern __shared__ unsigned char km_raw[];
+  unsigned char* base = km_raw + ((1024u - (tc::smem_addr(km_raw) & 1023u)) & 1023u);
+  unsigned char* sB0 = base;                                  // [2][kKmTcBlockBytes]
+  unsigned char* sA0 = base + 2 * kKmTcBlockBytes;            // [2 warpgroups][kKmTcABytes]
+  uint2* lst = reinterpret_cast<uint2*>(sA0 + 2 * kKmTcABytes);  // [256][kKmTcList] (column, key)
+  __shared__ __align__(8) uint64_t bfull[2], bfree[2], afull[2], accf[2][2], acce[2][2];
+  __shared__ uint32_t tslot, s_abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp == 0) tc::tmem_alloc(&tslot, 2 * tc::kCols);
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bfull[b], 1);
+      tc::mbar_init(&bfree[b], 1);
+      tc::mbar_init(&afull[b], 128);
+      for (int q = 0; q < 2; ++q) {
+        tc::mbar_init(&accf[b][q], 1);
+        tc::mbar_init(&acce[b][q], 128);
+      }
+    }
+    s_abort = 0u;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tslot;
+  auto aborted = [&]() { return *(volatile uint32_t*)&s_abort != 0u; };
+
+  if (warp == 8) {
+    // ============================ producer ===========================================
+    if (lane == 0) {
+      uint32_t gb = 0;          // blocks fetched by this CTA so far
+      uint32_t bc[2] = {0, 0};  // blocks chained per warpgroup
+      uint32_t ui = 0;          // units started
+      bool ok = true;
+      // fetch of the CTA's first block happens when its unit starts; the
+      // next block's fetch is issued before the current block's chains
+      for (uint32_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const uint32_t p = u_p[u];
+        if (P.state[p] != kRunning) continue;
+        const uint32_t nb = (P.k[p] + kKmTcCols - 1) / kKmTcCols, b0 = bbase[p];
+        for (int w = 0; w < 2 && ok; ++w) ok = tc::mbar_wait(&afull[w], ui & 1u);
+        ++ui;
+        if (!ok) break;
+        for (uint32_t bk = 0; bk < nb && ok; ++bk, ++gb) {
+          const int buf = (int)(gb & 1u);
+          if (bk == 0) {  // the unit's first block (the previous unit fetched nothing ahead)
+            if (gb >= 2) ok = tc::mbar_wait(&bfree[buf], ((gb >> 1) - 1u) & 1u);
+            if (!ok) break;
+            tc::bulk_load(sB0 + buf * kKmTcBlockBytes, Bg + (size_t)(b0 + bk) * kKmTcBlockBytes, kKmTcBlockBytes,
+                          &bfull[buf]);
+          }
+          if (bk + 1 < nb) {  // prefetch the next block into the other buffer
+            const uint32_t g1 = gb + 1;
+            if (g1 >= 2) ok = tc::mbar_wait(&bfree[g1 & 1u], ((g1 >> 1) - 1u) & 1u);
+            if (!ok) break;
+            tc::bulk_load(sB0 + (g1 & 1u) * kKmTcBlockBytes, Bg + (size_t)(b0 + bk + 1) * kKmTcBlockBytes,
+                          kKmTcBlockBytes, &bfull[g1 & 1u]);
+          }
+          ok = tc::mbar_wait(&bfull[buf], (gb >> 1) & 1u);
+          if (!ok) break;
+          for (int w = 0; w < 2 && ok; ++w) {
+            const uint32_t slot = bc[w] & 1u;
+            if (bc[w] >= 2) ok = tc::mbar_wait(&acce[w][slot], ((bc[w] >> 1) - 1u) & 1u);
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t d = tbase + (uint32_t)(w * 2 + (int)slot) * kKmTcCols;
+            unsigned char* sa = sA0 + w * kKmTcABytes;
+            unsigned char* sb = sB0 + buf * kKmTcBlockBytes;
+#pragma unroll
+            for (int s2 = 0; s2 < kKmTcSteps; ++s2)
+              tc::mma_tf32(d, tc::operand_desc(sa + s2 * tc::kTileBytesA), tc::operand_desc(sb + s2 * kKmTcStepB),
+                           s2 > 0 ? 1u : 0u, tc::kIdescTf32N128);
+            tc::mma_commit(&accf[w][slot]);
+            ++bc[w];
+          }
+          tc::mma_commit(&bfree[buf]);  // the buffer is free once both chains are done
+        }
+      }
+      if (!ok) atomicExch(&s_abort, 1u);
+    }
+    __syncwarp();
+  } else {
+    // ============================ epilogue warpgroups ================================
+    const int w = warp >> 2;                      // warpgroup
+    const int r = (warp & 3) * 32 + lane;         // row within the warpgroup's tile = TMEM lane
+    const int rr = w * 128 + r;                   // row within the unit
+    unsigned char* sa = sA0 + w * kKmTcABytes;
+    const uint32_t tlane = tbase + ((uint32_t)((warp & 3) * 32) << 16);
+    uint32_t bcount = 0;  // blocks scanned by this warpgroup
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      const uint32_t p = u_p[u];
+      if (P.state[p] != kRunning) continue;
+      const uint32_t k = P.k[p];
+      const uint64_t co = P.coff[p];
+      const uint32_t nb = (k + kKmTcCols - 1) / kKmTcCols;
+      const float cmax2 = __uint_as_float(cmx[p]);
+      const bool pbad = bad[p] != 0u;
+      const float cmax_up = __fsqrt_ru(cmax2), dl = __fmul_ru(0x1p-17f, cmax2);
+      const uint64_t row = u_r0[u] + (uint64_t)rr;
+      const bool valid = (uint32_t)rr < u_len[u];
+      float x[kKmTcDim];
+      {
+        const float* xg = G + (valid ? row : u_r0[u]) * kKmTcDim;
+#pragma unroll
+        for (int q = 0; q < kKmTcDim; q += 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(xg + q));
+          x[q] = v.x; x[q + 1] = v.y; x[q + 2] = v.z; x[q + 3] = v.w;
+        }
+      }
+      bool fin = true;
+      float xn2_up = 0.f, xn2_dn = 0.f;
+#pragma unroll
+      for (int q = 0; q < kKmTcDim; ++q) {
+        fin = fin && isfinite(x[q]);
+        xn2_up = __fadd_ru(xn2_up, __fmul_ru(x[q], x[q]));
+        xn2_dn = __fadd_rd(xn2_dn, __fmul_rd(x[q], x[q]));
+      }
+      const bool filt = valid && !pbad && fin && xn2_up <= kKmTcHuge;
+      float t = 1.0f, E = 0.f;
+      if (filt) {
+        const float xn_up = __fsqrt_ru(xn2_up);
+        const float eb = __fadd_ru(__fmul_ru(0x1p-7f, __fmul_ru(xn_up, cmax_up)), __fmul_ru(0x1p-9f, cmax2));
+        const float t0 = __fadd_ru(__fmul_ru(__fadd_ru(__fadd_ru(xn2_up, dl), eb), 1.0f + 0x1p-12f), 0x1p-100f);
+        t = tc::tf32_ceil_pos(t0);
+        E = __fadd_ru(__fadd_ru(eb, __fmul_ru(0x1p-16f, t)), 0x1p-100f);
+      }
+      // operand A (the previous unit's chains, which read it, are complete:
+      // this warpgroup has waited for every one of them)
+#pragma unroll
+      for (int s2 = 0; s2 < kKmTcDim / 8; ++s2) {
+        float h[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) h[q] = filt ? __uint_as_float(__float_as_uint(x[8 * s2 + q]) & 0xFFFFE000u) : 0.f;
+        unsigned char* ta = sa + s2 * tc::kTileBytesA;
+        *reinterpret_cast<float4*>(ta + tc::operand_offset(r, 0)) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(ta + tc::operand_offset(r, 4)) = make_float4(h[4], h[5], h[6], h[7]);
+      }
+      {
+        unsigned char* ta = sa + (kKmTcSteps - 1) * tc::kTileBytesA;
+        *reinterpret_cast<float4*>(ta + tc::operand_offset(r, 0)) = make_float4(1.0f, t, 0.f, 0.f);
+        *reinterpret_cast<float4*>(ta + tc::operand_offset(r, 4)) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      tc::fence_async_smem();
+      tc::mbar_arrive(&afull[w]);
+
+      uint32_t m1 = 0xFFFFFFFFu, m2 = 0xFFFFFFFFu;  // running smallest keys (value | in-block column)
+      uint32_t m1b = 0;                             // block of m1
+      int nl = 0;
+      bool ovf = false;
+      uint2* mylst = lst + rr * kKmTcList;
+      for (uint32_t bk = 0; bk < nb; ++bk, ++bcount) {
+        const uint32_t slot = bcount & 1u;
+        const bool got = tc::mbar_wait(&accf[w][slot], (bcount >> 1) & 1u);
+        if (!__all_sync(0xFFFFFFFFu, got) || __any_sync(0xFFFFFFFFu, aborted())) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t taddr = tlane + (uint32_t)(w * 2 + (int)slot) * kKmTcCols;
+        uint32_t q1 = 0xFFFFFFFFu, q2 = 0xFFFFFFFFu;
+#pragma unroll 1
+        for (int q = 0; q < 2; ++q) {
+          uint32_t v[64];
+          tc::tmem_ld64(taddr + (uint32_t)(q * 64), v);
+          tc::tmem_wait_ld();
+          float f1a = __int_as_float(0x7f800000), f2a = f1a, f1b = f1a, f2b = f1a;
+#pragma unroll
+          for (int jj = 0; jj < 64; jj += 4) {
+            const float k0 = __uint_as_float((v[jj] & 0xFFFFFF00u) | (uint32_t)jj);
+            const float k1 = __uint_as_float((v[jj + 1] & 0xFFFFFF00u) | (uint32_t)(jj + 1));
+            const float k2 = __uint_as_float((v[jj + 2] & 0xFFFFFF00u) | (uint32_t)(jj + 2));
+            const float k3 = __uint_as_float((v[jj + 3] & 0xFFFFFF00u) | (uint32_t)(jj + 3));
+            const float loa = fminf(k0, k1), hia = fmaxf(k0, k1);
+            f2a = tc::min3f(f2a, hia, fmaxf(f1a, loa));
+            f1a = fminf(f1a, loa);
+            const float lob = fminf(k2, k3), hib = fmaxf(k2, k3);
+            f2b = tc::min3f(f2b, hib, fmaxf(f1b, lob));
+            f1b = fminf(f1b, lob);
+          }
+          const uint32_t qb = (uint32_t)q << 6;
+          const uint32_t a1 = __float_as_uint(fminf(f1a, f1b)) | qb;
+          const uint32_t a2 = __float_as_uint(fminf(fmaxf(f1a, f1b), fminf(f2a, f2b))) | qb;
+          const uint32_t n2 = min(max(q1, a1), min(q2, a2));
+          q1 = min(q1, a1);
+          q2 = n2;
+        }
+        if (q1 < m1) {  // a tie keeps the earlier block
+          m2 = min(m1, q2);
+          m1 = q1;
+          m1b = bk;
+        } else {
+          m2 = min(m2, q1);
+        }
+        uint32_t thrkey = 0u;
+        bool need2 = false;
+        if (filt) {
+          const float a1hi = __uint_as_float(m1 | 0xFFu);
+          const float dup = fmaxf(__fadd_ru(__fadd_ru(__fsub_ru(__fadd_ru(a1hi, E), t), xn2_up), dl), 0.f);
+          const float T = __fadd_ru(__fadd_ru(__fadd_ru(a1hi, __fmul_ru(2.0f, E)), __fmul_ru(0x1p-17f, dup)),
+                                    __fmul_ru(2.0f, dl));
+          thrkey = __float_as_uint(T) | 0xFFu;
+          if (q1 <= thrkey) {
+            if (q2 <= thrkey) need2 = true;
+            else km_tc_push(mylst, nl, ovf, bk * kKmTcCols + (q1 & 0xFFu), q1, thrkey);
+          }
+        }
+        if (__any_sync(0xFFFFFFFFu, need2)) {  // several columns of this block at or below T
+#pragma unroll 1
+          for (int q = 0; q < 2; ++q) {
+            uint32_t v[64];
+            tc::tmem_ld64(taddr + (uint32_t)(q * 64), v);
+            tc::tmem_wait_ld();
+            if (need2) {
+              uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                lo |= (v[jj] <= thrkey ? 1u : 0u) << jj;
+                hi |= (v[jj + 32] <= thrkey ? 1u : 0u) << jj;
+              }
+              unsigned long long bits = ((unsigned long long)hi << 32) | lo;
+              while (bits) {  // in column order
+                const int jj = __ffsll((long long)bits) - 1;
+                bits &= bits - 1;
+                const uint32_t col = (uint32_t)(q * 64 + jj);
+                km_tc_push(mylst, nl, ovf, bk * kKmTcCols + col, (v[jj] & 0xFFFFFF00u) | col, thrkey);
+              }
+            }
+          }
+        }
+        tc::fence_before_sync();
+        tc::mbar_arrive(&acce[w][slot]);  // the slot may take the next chain
+      }
+      if (!ok) break;
+      // ---- the exact distances decide -------------------------------------------
+      uint32_t final_thr = 0xFFFFFFFFu;
+      if (filt) {
+        const float a1hi = __uint_as_float(m1 | 0xFFu);
+        const float dup = fmaxf(__fadd_ru(__fadd_ru(__fsub_ru(__fadd_ru(a1hi, E), t), xn2_up), dl), 0.f);
+        const float T = __fadd_ru(__fadd_ru(__fadd_ru(a1hi, __fmul_ru(2.0f, E)), __fmul_ru(0x1p-17f, dup)),
+                                  __fmul_ru(2.0f, dl));
+        final_thr = __float_as_uint(T) | 0xFFu;
+      }
+      int nfin = 0;
+      for (int e = 0; e < nl; ++e) nfin += mylst[e].y <= final_thr ? 1 : 0;
+      if (valid) {
+        uint32_t bi = 0;
+        float best = 0.f;
+        if (!filt || ovf || nl == 0) {
+          km_tc_full_scan(G + row * kKmTcDim, C, co, k, best, bi);
+        } else {
+          best = __int_as_float(0x7f800000);
+          for (int e = 0; e < nl; ++e) {
+            const uint2 en = mylst[e];
+            if (en.y > final_thr) continue;  // ruled out by the final threshold
+            const uint32_t c = en.x;
+            float cl[kKmTcDim];
+#pragma unroll
+            for (int q = 0; q < kKmTcDim; q += 4) {
+              const float4 v = __ldg(reinterpret_cast<const float4*>(C + (co + c) * kKmTcDim + q));
+              cl[q] = v.x; cl[q + 1] = v.y; cl[q + 2] = v.z; cl[q + 3] = v.w;
+            }
+            const float f = l2_wide<kKmTcDim>(x, cl);
+            if (f < best) {
+              best = f;
+              bi = c;
+            }
+          }
+          if (nfin == 1 && bi == m1b * kKmTcCols + (m1 & 0xFFu)) {  // canary on the single winner
+            const float a1lo = __uint_as_float(m1 & 0xFFFFFF00u), a1hi = __uint_as_float(m1 | 0xFFu);
+            const float phi =
+                __fadd_ru(__fadd_ru(__fadd_ru(__fsub_ru(t, xn2_dn), __fmul_ru(best, 1.0f + 0x1p-18f)), dl), E);
+            const float plo =
+                __fsub_rd(__fsub_rd(__fadd_rd(__fsub_rd(t, xn2_up), __fmul_rd(best, 1.0f - 0x1p-18f)), dl), E);
+            if (a1lo > phi || a1hi < plo) atomicAdd(&diag[0], 1u);
+          }
+        }
+        local[row] = bi;
+        mind[row] = best;
+        keys[row] = (uint32_t)(co + bi);
+      }
+      const uint32_t mm = __ballot_sync(0xFFFFFFFFu, valid && filt && nfin > 1);
+      if (mm && lane == 0) atomicAdd(&diag[1], (uint32_t)__popc(mm));
+      const uint32_t mo = __ballot_sync(0xFFFFFFFFu, valid && filt && ovf);
+      if (mo && lane == 0) atomicAdd(&diag[3], (uint32_t)__popc(mo));
+    }
+    if (!ok && lane == 0) atomicExch(&s_abort, 1u);
+  }
+  __syncthreads();
+  if (tid == 0 && s_abort) atomicExch(&diag[2], 1u);
+  tc::fence_after_sync();
+  if (warp == 0) tc::tmem_free(tbase, 2 * tc::kCols);
+}
+
 // Cluster sizes from the sort keys of all rows (rows of finished problems
 // keep their last keys), so counts and the radix order always agree.
 __global__ void km_count_kernel(const uint32_t* __restrict__ keys, uint64_t n, uint32_t* __restrict__ counts) {
@@ -882,15 +1317,31 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
     ccount[p] = (uint32_t)ch_p.size() - cfirst[p];
     chunks_upto.push_back((uint32_t)ch_p.size());
   }
-  // assignment tiles of the live problems
-  std::vector<uint32_t> t_p, t_len;
-  std::vector<uint64_t> t_r0;
-  for (uint32_t p : live)
+  // assignment tiles of the live problems: problems with many centroids (and
+  // 64-dim rows) go through the tensor-core filter, the rest through the
+  // exact scan
+  const bool tc_on = ctx->tc_filter && !ctx->exhaustive_assign && dim == (uint32_t)kKmTcDim;
+  std::vector<uint32_t> t_p, t_len, u_p, u_len, bbase(NP, 0);
+  std::vector<uint64_t> t_r0, u_r0;
+  std::vector<uint2> tcblocks;
+  for (uint32_t p : live) {
+    const bool filt = tc_on && b.k[p] >= (uint32_t)kKmTcMinK;
+    if (filt) {
+      bbase[p] = (uint32_t)tcblocks.size();
+      for (uint32_t bk = 0; bk < (b.k[p] + kKmTcCols - 1) / kKmTcCols; ++bk) tcblocks.push_back(make_uint2(p, bk));
+      for (uint64_t r = 0; r < b.n[p]; r += kKmTcRows) {
+        u_p.push_back(p);
+        u_r0.push_back(b.off[p] + r);
+        u_len.push_back((uint32_t)std::min<uint64_t>(kKmTcRows, b.n[p] - r));
+      }
+      continue;
+    }
     for (uint64_t r = 0; r < b.n[p]; r += kAsgT) {
       t_p.push_back(p);
       t_r0.push_back(b.off[p] + r);
       t_len.push_back((uint32_t)std::min<uint64_t>(kAsgT, b.n[p] - r));
     }
+  }
   std::vector<uint32_t> cprob(KT);
   for (uint32_t p = 0; p < NP; ++p)
     for (uint32_t c = 0; c < b.k[p]; ++c) cprob[b.coff[p] + c] = p;
@@ -923,14 +1374,19 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
                o_tp = cv.take(std::max<size_t>(1, t_p.size()) * 4),
                o_tr0 = cv.take(std::max<size_t>(1, t_r0.size()) * 8),
                o_tlen = cv.take(std::max<size_t>(1, t_len.size()) * 4), o_cprob = cv.take(KT * 4),
-               o_draws = cv.take(KT * 8);
+               o_draws = cv.take(KT * 8), o_up = cv.take(std::max<size_t>(1, u_p.size()) * 4),
+               o_ur0 = cv.take(std::max<size_t>(1, u_r0.size()) * 8),
+               o_ulen = cv.take(std::max<size_t>(1, u_len.size()) * 4), o_bbase = cv.take(NP * 4),
+               o_tcblk = cv.take(std::max<size_t>(1, tcblocks.size()) * 8);
   const size_t host_bytes = cv.off;  // everything above is copied from the host
   const size_t o_chsum = cv.take(std::max<size_t>(1, ch_p.size()) * sizeof(double2)),
                o_chcnt = cv.take(std::max<size_t>(1, ch_p.size()) * 4), o_md = cv.take(rows * 4),
                o_keys = cv.take(rows * 4), o_keys2 = cv.take(rows * 4), o_vals2 = cv.take(rows * 4),
                o_keys3 = cv.take(rows * 4), o_vals3 = cv.take(rows * 4), o_counts = cv.take(KT * 4), o_starts = cv.take(KT * 4),
                o_hist = cv.take((size_t)256 * radix_nblk * 4), o_base = cv.take((size_t)256 * radix_nblk * 4),
-               o_part = cv.take((std::max<uint64_t>(KT, (uint64_t)256 * radix_nblk) / kScanTile + 2) * 4);
+               o_part = cv.take((std::max<uint64_t>(KT, (uint64_t)256 * radix_nblk) / kScanTile + 2) * 4),
+               o_cmx = cv.take(NP * 4 * 2), o_diag = cv.take(16),
+               o_bg = cv.take(std::max<size_t>(1, tcblocks.size()) * (size_t)kKmTcBlockBytes);
   unsigned char* ws = nullptr;
   MVR_TRY(scratch(ctx, kSlotAux3, cv.off, (void**)&ws));
   std::vector<unsigned char> hb(host_bytes, 0);
@@ -962,6 +1418,11 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
   put(o_tlen, t_len.data(), t_len.size() * 4);
   put(o_cprob, cprob.data(), KT * 4);
   put(o_draws, draws.data(), KT * 8);
+  put(o_up, u_p.data(), u_p.size() * 4);
+  put(o_ur0, u_r0.data(), u_r0.size() * 8);
+  put(o_ulen, u_len.data(), u_len.size() * 4);
+  put(o_bbase, bbase.data(), NP * 4);
+  put(o_tcblk, tcblocks.data(), tcblocks.size() * 8);
   MVR_CUDA(ctx, cudaMemcpyAsync(ws, hb.data(), host_bytes, cudaMemcpyHostToDevice, st));
 
   Prob P;
@@ -1045,9 +1506,28 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
   MVR_TRY(side_stream(ctx, &side));
   const unsigned ntiles = (unsigned)t_p.size();
   const size_t asg_smem = (size_t)kCT * d * sizeof(float);
+  uint32_t* cmx = at<uint32_t>(ws, o_cmx);
+  uint32_t* d_diag = at<uint32_t>(ws, o_diag);
+  MVR_CUDA(ctx, cudaMemsetAsync(d_diag, 0, 16, st));
+  if (!u_p.empty())
+    MVR_CUDA(ctx, cudaFuncSetAttribute(km_tc_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kKmTcSmem));
   for (uint32_t it = 0; it < max_iters && !live.empty(); ++it) {
     MVR_CUDA(ctx, cudaMemsetAsync(counts, 0, KT * 4, st));
-    if (d == 64) {
+    if (!u_p.empty()) {  // filtered problems: operand tiles of the current centroids, then the filter
+      MVR_CUDA(ctx, cudaMemsetAsync(cmx, 0, NP * 4 * 2, st));
+      km_tc_prep_kernel<<<(unsigned)tcblocks.size(), kKmTcCols, 0, st>>>(P, at<uint2>(ws, o_tcblk), d_C,
+                                                                   at<unsigned char>(ws, o_bg), cmx, cmx + NP);
+      const unsigned g = (unsigned)std::min<size_t>(u_p.size(), (size_t)std::max(1, ctx->sm_count));
+      km_tc_assign_kernel<<<g, 288, kKmTcSmem, st>>>(d_G, P, at<uint32_t>(ws, o_up), at<uint64_t>(ws, o_ur0),
+                                                     at<uint32_t>(ws, o_ulen), (uint32_t)u_p.size(),
+                                                     at<uint32_t>(ws, o_bbase), at<unsigned char>(ws, o_bg), cmx,
+                                                     cmx + NP, d_C, d_local, mind, keys, d_diag);
+      MVR_CUDA(ctx, cudaGetLastError());
+      launches += 2;
+    }
+    if (ntiles == 0) {
+    } else if (d == 64) {
       km_assign_kernel<64><<<ntiles, kAsgT, asg_smem, st>>>(d_G, d, P, at<uint32_t>(ws, o_tp), at<uint64_t>(ws, o_tr0),
                                                              at<uint32_t>(ws, o_tlen), d_C, d_local, mind, keys);
     } else if (d == 128) {
@@ -1108,6 +1588,21 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
 
   MVR_CUDA(ctx, cudaEventRecord(tev[7], st));
   // ---- results ------------------------------------------------------------------
+  uint32_t hdiag[4] = {0, 0, 0, 0};
+  MVR_CUDA(ctx, cudaMemcpyAsync(hdiag, d_diag, 16, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(ctx, cudaStreamSynchronize(st));
+  if (hdiag[2]) return fail(ctx, MVR_E_TIMEOUT, "tensor-core filter: a bulk copy or an MMA did not complete in time");
+  if (hdiag[0]) {
+    // a winner's approximation broke its error bound: the whole batch again
+    // with the exact scans
+    ctx->tc_filter = false;
+    const int s2 = km_batch_run(ctx, d_G, d_GT, rows, dim, b, max_iters, tol, d_C, d_local, res);
+    ctx->tc_filter = true;
+    res->filter_violations = hdiag[0];
+    return s2;
+  }
+  res->filter_rows_rechecked = hdiag[1];
+  res->filter_rows_full_scan = hdiag[3];
   std::vector<int> hstatus(NP);
   std::vector<uint32_t> hfb(NP);
   MVR_CUDA(ctx, cudaMemcpyAsync(hstatus.data(), P.status, NP * 4, cudaMemcpyDeviceToHost, st));

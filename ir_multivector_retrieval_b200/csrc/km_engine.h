@@ -32,6 +32,9 @@ struct KmResult {
   uint32_t launches = 0;
   double seed_ms = 0.0;   // device time of the seeding (degenerate copies included)
   double lloyd_ms = 0.0;  // device time of the Lloyd iterations
+  uint64_t filter_rows_rechecked = 0;  // tensor-core filter: rows with several candidates
+  uint32_t filter_violations = 0;      // winners outside the filter's bound (then re-run exactly)
+  uint64_t filter_rows_full_scan = 0;  // rows whose candidate list overflowed (full exact scan)
 };
 
 // Group-major copy of a row set: GT holds ceil(dim / 4) groups, group g of

@@ -519,6 +519,9 @@ int cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens, const
     for (uint64_t j = 0; j < nd; ++j) ts.iters_max = std::max(ts.iters_max, titer[j]);
     ts.seed_fallbacks = r.seed_fallbacks;
     ts.launches = r.launches + (G > 1 ? 6 : 4);
+    ts.filter_rows_rechecked = r.filter_rows_rechecked;
+    ts.filter_violations = r.filter_violations;
+    ts.filter_rows_full_scan = r.filter_rows_full_scan;
     ts.host_ms = host_ms + since(t_tail);
     ts.total_ms = since(t_start);
   }

@@ -93,12 +93,31 @@ __device__ __forceinline__ void tmem_free(uint32_t base, uint32_t cols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
 }
 
-// One thread: D[tmem] (+)= A * B^T, M = 128, N = 256, K = 8.
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+// The same with N = 128.
+constexpr uint32_t kIdescTf32N128 =
+    (1u << 4) | (2u << 7) | (2u << 10) | ((128u >> 3) << 17) | ((kRowsPerTile >> 4) << 24);
+
+// One thread: D[tmem] (+)= A * B^T, M = 128, K = 8, N = 256 (or 128 with
+// idesc = kIdescTf32N128).
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate,
+                                         uint32_t idesc = kIdescTf32) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kIdescTf32), "r"(accumulate)
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// from global memory into shared memory, completing on *bar (which expects
+// the bytes through this same call's arrive).
+__device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_addr(smem)),
+      "l"(gmem), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
 // One thread: arrive on *bar once every MMA issued so far has completed.

@@ -195,3 +195,51 @@ def test_cluster_flat_errors(ctx, orc):
         assert e.value.code == w.value.code
     # the context stays usable
     _check_cluster(ctx, orc, bad.token_ids, bad.vectors, 8, 600, 0, mu=8, tau=16, epsilon=2, theta=2)
+
+
+# ----------------------------------------------- tensor-core filtered Lloyd
+def _km_filter_datasets():
+    rng = np.random.default_rng(8)
+    yield "unit", synth.unit_rows(9_000, 64, seed=41), 300
+    c = synth.make_corpus(30_000, 64, n_anchors=40, seed=3)
+    yield "anchors", c.vectors, 700
+    base = synth.unit_rows(150, 64, seed=42)
+    yield "dup", base[rng.integers(0, 150, size=6_000)], 100  # zero distances, equal centroids
+    yield "scaled_up", (synth.unit_rows(5_000, 64, seed=43) * 1e3).astype(np.float32), 128
+    yield "scaled_down", (synth.unit_rows(5_000, 64, seed=44) * 1e-3).astype(np.float32), 128
+    mixed = synth.unit_rows(6_000, 64, seed=45)
+    mixed[::5] *= 1e4
+    mixed[2::7] *= 1e-4
+    yield "mixed", mixed.astype(np.float32), 200
+    big = synth.unit_rows(4_000, 64, seed=46)
+    big[::9] *= 1e15  # |x|^2 above 2^60: these rows take the full scan
+    yield "huge", big.astype(np.float32), 64
+    grid = (np.round(synth.unit_rows(5_000, 64, seed=47) * 4) / 4).astype(np.float32)  # many equal distances
+    yield "grid", grid, 96
+
+
+@pytest.mark.parametrize("name,x,k", list(_km_filter_datasets()), ids=lambda v: v if isinstance(v, str) else "")
+def test_km_tensor_filter_matches_exact(ctx, orc, name, x, k):
+    """64-dim k-means with k >= 64 runs its Lloyd assignment through the
+    tensor-core filter; the exact scans and the oracle give the same bytes."""
+    got = _check_kmeans(ctx, orc, x, 64, k, seed=5, max_iters=8, tol=1e-4)
+    ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 0))
+    try:
+        ex = kmeans.fit(x, 64, kmeans.KMeansParams(k=k, seed=5, max_iters=8, tol=1e-4), ctx=ctx)
+    finally:
+        ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))
+    assert np.array_equal(got.assignments, ex.assignments)
+    assert _same_bytes(got.centroids, ex.centroids)
+
+
+def test_cluster_flat_tensor_filter_matches_exact(ctx, orc):
+    c = synth.make_corpus(117_645, 64, seed=42)
+    p = tac.ClusteringParams(12_288, 42, theta=10)
+    a = tac.cluster_flat(c.token_ids, c.vectors, 64, p, ctx=ctx)
+    ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 0))
+    try:
+        b = tac.cluster_flat(c.token_ids, c.vectors, 64, p, ctx=ctx)
+    finally:
+        ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))
+    assert np.array_equal(a.assignments, b.assignments) and _same_bytes(a.centroids, b.centroids)
+    assert np.float32(a.wcss_total).tobytes() == np.float32(b.wcss_total).tobytes()
