@@ -44,6 +44,7 @@ constexpr int kCT = 32;            // centroids per shared-memory tile
 constexpr int kRadixRows = 2048;   // rows per radix block (one warp)
 constexpr int kRadixWarps = 4;
 constexpr int kCrossingSlack = 300;
+constexpr uint32_t kWcssSeg = 32768;  // problems at least this long take the segmented WCSS sum
 
 enum : uint8_t { kRunning = 0, kDone = 1, kFailed = 2 };
 
@@ -942,7 +943,7 @@ km_wcss_kernel(Prob P, uint32_t nprob, const float* __restrict__ mind) {
   __shared__ __align__(16) float tile[4][2][1024];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t p = blockIdx.x * 4 + warp;
-  if (p >= nprob || P.state[p] != kRunning) return;
+  if (p >= nprob || P.state[p] != kRunning || P.n[p] >= kWcssSeg) return;  // long ones: km_wcss_seg_kernel
   const float* src = mind + P.off[p];
   const uint32_t n = P.n[p];
   float acc = 0.f;
@@ -977,6 +978,130 @@ km_wcss_kernel(Prob P, uint32_t nprob, const float* __restrict__ mind) {
   }
   cp_async_wait<0>();
   if (lane == 0) P.wcss[p] = acc;
+}
+
+// Sequential f32 WCSS of one long problem without the serial chain. For
+// non-negative addends the running sum s stays on one grid of spacing
+// u = 2^(max(e, -126) - 23) while it is inside its binade [2^e, 2^(e+1))
+// (zero and subnormal sums use u = 2^-149, which also covers the first
+// normal binade), and there fl(K*u + x) = (K + rne(x/u))*u with K = s/u an
+// integer: the rounding of each addend is independent of K except at exact
+// ties (x/u = m + 1/2), where the parity of K decides. So a CTA takes 8192
+// addends at a time: rounded quotients r_j, a block prefix sum, and the first
+// position where K + prefix reaches 2^24 (the sum enters the next binade);
+// that one addend is added with an f32 add and the grid is recomputed. A
+// chunk with a tie, or a problem with a non-finite value, is added serially
+// by one thread. The result is the reference's left-to-right f32 sum, bit
+// for bit.
+constexpr int kSegT = 1024, kSegV = 8, kSegChunk = kSegT * kSegV;
+
+__global__ void __launch_bounds__(kSegT)
+km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
+  const uint32_t p = blockIdx.x;
+  if (P.state[p] != kRunning || P.n[p] < kWcssSeg) return;
+  const float* x = mind + P.off[p];
+  const uint32_t n = P.n[p];
+  __shared__ float s_s;
+  __shared__ uint32_t s_i, s_cross;
+  __shared__ long long wtot[kSegT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  bool bad = false;
+  for (uint32_t j = tid; j < n; j += kSegT) bad = bad || !isfinite(x[j]);
+  if (__syncthreads_or(bad)) {
+    if (tid == 0) {
+      float a = 0.f;
+      for (uint32_t j = 0; j < n; ++j) a = __fadd_rn(a, x[j]);
+      P.wcss[p] = a;
+    }
+    return;
+  }
+  if (tid == 0) {  // the first addends serially: the sum's early binade changes come fast
+    float a = 0.f;
+    const uint32_t h = min(n, 1024u);
+    for (uint32_t j = 0; j < h; ++j) a = __fadd_rn(a, x[j]);
+    s_s = a;
+    s_i = h;
+  }
+  __syncthreads();
+  for (;;) {
+    const uint32_t i = s_i;
+    const float s = s_s;
+    __syncthreads();  // everyone has read the state
+    if (i >= n || !isfinite(s)) break;
+    const uint32_t eb = (__float_as_uint(s) >> 23) & 0xFFu;
+    const int ue = (eb == 0u ? -126 : (int)eb - 127) - 23;  // grid spacing 2^ue
+    const long long K = (long long)ldexp((double)s, -ue);   // exact, < 2^24
+    const uint32_t C = min((uint32_t)kSegChunk, n - i);
+    long long r[kSegV];
+    long long mine = 0;
+    bool tie = false;
+#pragma unroll
+    for (int v = 0; v < kSegV; ++v) {
+      const uint32_t j = (uint32_t)(kSegV * tid + v);
+      r[v] = 0;
+      if (j < C) {
+        const double y = ldexp((double)x[i + j], -ue);  // exact
+        if (y >= 0x1p40) {
+          r[v] = 1ll << 40;  // crosses the binade by itself
+        } else {
+          const double fl = floor(y), f = y - fl;
+          r[v] = (long long)fl + (f > 0.5 ? 1 : 0);
+          tie = tie || f == 0.5;
+        }
+        mine += r[v];
+      }
+    }
+    if (__syncthreads_or(tie)) {  // parity-dependent rounding in this chunk: add it serially
+      if (tid == 0) {
+        float a = s;
+        for (uint32_t j = 0; j < C; ++j) a = __fadd_rn(a, x[i + j]);
+        s_s = a;
+        s_i = i + C;
+      }
+      __syncthreads();
+      continue;
+    }
+    // block exclusive prefix of the per-thread sums
+    long long incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) wtot[warp] = incl;
+    if (tid == 0) s_cross = 0xFFFFFFFFu;
+    __syncthreads();
+    long long before = 0, total = 0;
+    for (int w = 0; w < kSegT / 32; ++w) {
+      if (w < warp) before += wtot[w];
+      total += wtot[w];
+    }
+    long long run = K + before + (incl - mine);
+    int cv = -1;
+#pragma unroll
+    for (int v = 0; v < kSegV; ++v) {
+      const uint32_t j = (uint32_t)(kSegV * tid + v);
+      if (cv < 0 && j < C) {
+        if (run + r[v] >= (1ll << 24)) cv = v;
+        else run += r[v];
+      }
+    }
+    if (cv >= 0) atomicMin(&s_cross, (uint32_t)(kSegV * tid + cv));
+    __syncthreads();
+    const uint32_t cj = s_cross;
+    if (cj == 0xFFFFFFFFu) {
+      if (tid == 0) {
+        s_s = (float)ldexp((double)(K + total), ue);
+        s_i = i + C;
+      }
+    } else if (cv >= 0 && (uint32_t)(kSegV * tid + cv) == cj) {
+      // the sum leaves its binade at addend cj: that one add in f32
+      s_s = __fadd_rn((float)ldexp((double)run, ue), x[i + cj]);
+      s_i = i + cj + 1;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) P.wcss[p] = s_s;
 }
 
 // Exclusive scan of n u32 in three launches: per-tile sums (tiles of
@@ -1506,6 +1631,8 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
   MVR_TRY(side_stream(ctx, &side));
   const unsigned ntiles = (unsigned)t_p.size();
   const size_t asg_smem = (size_t)kCT * d * sizeof(float);
+  bool long_problems = false;
+  for (uint32_t p : live) long_problems = long_problems || b.n[p] >= kWcssSeg;
   uint32_t* cmx = at<uint32_t>(ws, o_cmx);
   uint32_t* d_diag = at<uint32_t>(ws, o_diag);
   MVR_CUDA(ctx, cudaMemsetAsync(d_diag, 0, 16, st));
@@ -1548,6 +1675,11 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
       MVR_CUDA(ctx, cudaStreamWaitEvent(side, ctx->fork_ev, 0));
       km_wcss_kernel<<<(unsigned)((NP + 3) / 4), 128, 0, side>>>(P, (uint32_t)NP, mind);
       MVR_CUDA(ctx, cudaGetLastError());
+      if (long_problems) {
+        km_wcss_seg_kernel<<<(unsigned)NP, kSegT, 0, side>>>(P, mind);
+        MVR_CUDA(ctx, cudaGetLastError());
+        ++launches;
+      }
       MVR_CUDA(ctx, cudaEventRecord(ctx->join_ev, side));
       ++launches;
     }

@@ -243,3 +243,23 @@ def test_cluster_flat_tensor_filter_matches_exact(ctx, orc):
         ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))
     assert np.array_equal(a.assignments, b.assignments) and _same_bytes(a.centroids, b.centroids)
     assert np.float32(a.wcss_total).tobytes() == np.float32(b.wcss_total).tobytes()
+
+
+@pytest.mark.parametrize("kind", ["unit", "dup", "grid", "wide"])
+def test_kmeans_long_problem_wcss(ctx, orc, kind):
+    """Problems of 32,768 rows and more take the segmented exact WCSS sum;
+    the reported WCSS and the convergence decisions match the reference's
+    serial f32 sum."""
+    rng = np.random.default_rng(len(kind))
+    n, dim = 40_000, 8
+    if kind == "unit":
+        x = synth.unit_rows(n, dim, seed=2)
+    elif kind == "dup":  # zero distances: the sum stays 0 for a while
+        x = synth.unit_rows(60, dim, seed=3)[rng.integers(0, 60, size=n)]
+    elif kind == "grid":  # coarse values: many exact ties in the sum's rounding
+        x = (np.round(synth.unit_rows(n, dim, seed=4) * 4) / 4).astype(np.float32)
+    else:  # magnitudes over many binades
+        x = (synth.unit_rows(n, dim, seed=5) * 10.0 ** rng.integers(-6, 6, size=(n, 1))).astype(np.float32)
+    for k, tol, iters in ((12, 1e-4, 25), (40, 0.0, 6)):
+        _check_kmeans(ctx, orc, x, dim, k, seed=k, max_iters=iters, tol=tol)
+    _check_kmeans(ctx, orc, synth.unit_rows(36_000, 64, seed=6), 64, 80, seed=1, max_iters=10, tol=1e-4)
