@@ -985,15 +985,95 @@ km_wcss_kernel(Prob P, uint32_t nprob, const float* __restrict__ mind) {
 // u = 2^(max(e, -126) - 23) while it is inside its binade [2^e, 2^(e+1))
 // (zero and subnormal sums use u = 2^-149, which also covers the first
 // normal binade), and there fl(K*u + x) = (K + rne(x/u))*u with K = s/u an
-// integer: the rounding of each addend is independent of K except at exact
-// ties (x/u = m + 1/2), where the parity of K decides. So a CTA takes 8192
-// addends at a time: rounded quotients r_j, a block prefix sum, and the first
-// position where K + prefix reaches 2^24 (the sum enters the next binade);
-// that one addend is added with an f32 add and the grid is recomputed. A
-// chunk with a tie, or a problem with a non-finite value, is added serially
-// by one thread. The result is the reference's left-to-right f32 sum, bit
-// for bit.
+// integer: the rounding of an addend is independent of K except at exact
+// ties (x/u = m + 1/2), where round-half-even makes the new K even. So a tie
+// rounds up exactly when the sum of the grid values since the previous tie
+// (its own floor included) is odd; for the first tie of a chunk the chunk's
+// starting K counts too. A CTA takes 8192 addends at a time: grid values, a
+// block prefix sum, each tie's decision from the prefix at the previous tie,
+// the prefix of the round-ups, and the first position where K + prefix
+// reaches 2^24 (the sum enters the next binade); that one addend is added
+// with an f32 add and the grid is recomputed. A problem with a non-finite
+// value is added serially by one thread. The result is the reference's
+// left-to-right f32 sum, bit for bit.
 constexpr int kSegT = 1024, kSegV = 8, kSegChunk = kSegT * kSegV;
+
+// Block-wide exclusive prefix sum of one int64 per thread (1024 threads);
+// also returns the total. `sw` holds 33 int64 (warp totals, then their
+// exclusive prefixes and the total, written by warp 0).
+__device__ __forceinline__ long long seg_scan_excl(long long v, long long* sw, long long& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  __syncthreads();
+  if (lane == 31) sw[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const long long w = sw[lane];
+    long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long t = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    sw[lane] = wi - w;
+    if (lane == 31) sw[32] = wi;
+  }
+  __syncthreads();
+  total = sw[32];
+  return sw[warp] + inc - v;
+}
+
+// Block-wide "latest value" carry: for each thread the value of the last
+// thread before it with has = true (or `init` when none). `sw` holds 32
+// int64 and `sh` 32 int.
+__device__ __forceinline__ long long seg_carry_excl(bool has, long long v, long long init, long long* sw, int* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  bool h = has;
+  long long val = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long tv = __shfl_up_sync(0xFFFFFFFFu, val, o);
+    const bool th = __shfl_up_sync(0xFFFFFFFFu, h, o);
+    if (lane >= o && !h) {
+      h = th;
+      val = tv;
+    }
+  }
+  long long ev = __shfl_up_sync(0xFFFFFFFFu, val, 1);  // exclusive within the warp
+  bool eh = __shfl_up_sync(0xFFFFFFFFu, h, 1);
+  if (lane == 0) eh = false;
+  __syncthreads();
+  if (lane == 31) {
+    sw[warp] = val;
+    sh[warp] = h ? 1 : 0;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive carry over the warps
+    bool wh = sh[lane] != 0;
+    long long wv = sw[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long tv = __shfl_up_sync(0xFFFFFFFFu, wv, o);
+      const bool th = __shfl_up_sync(0xFFFFFFFFu, wh, o);
+      if (lane >= o && !wh) {
+        wh = th;
+        wv = tv;
+      }
+    }
+    long long xv = __shfl_up_sync(0xFFFFFFFFu, wv, 1);
+    bool xh = __shfl_up_sync(0xFFFFFFFFu, wh, 1);
+    if (lane == 0) xh = false;
+    __syncwarp();
+    sw[lane] = xh ? xv : init;
+  }
+  __syncthreads();
+  return eh ? ev : sw[warp];
+}
 
 __global__ void __launch_bounds__(kSegT)
 km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
@@ -1003,8 +1083,9 @@ km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
   const uint32_t n = P.n[p];
   __shared__ float s_s;
   __shared__ uint32_t s_i, s_cross;
-  __shared__ long long wtot[kSegT / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ long long sw[kSegT / 32 + 1];
+  __shared__ int sh[kSegT / 32];
+  const int tid = threadIdx.x;
   bool bad = false;
   for (uint32_t j = tid; j < n; j += kSegT) bad = bad || !isfinite(x[j]);
   if (__syncthreads_or(bad)) {
@@ -1015,9 +1096,9 @@ km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
     }
     return;
   }
-  if (tid == 0) {  // the first addends serially: the sum's early binade changes come fast
+  if (tid == 0) {  // the first addends serially: the sum changes binade often early on
     float a = 0.f;
-    const uint32_t h = min(n, 1024u);
+    const uint32_t h = min(n, 2048u);
     for (uint32_t j = 0; j < h; ++j) a = __fadd_rn(a, x[j]);
     s_s = a;
     s_i = h;
@@ -1032,58 +1113,74 @@ km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
     const int ue = (eb == 0u ? -126 : (int)eb - 127) - 23;  // grid spacing 2^ue
     const long long K = (long long)ldexp((double)s, -ue);   // exact, < 2^24
     const uint32_t C = min((uint32_t)kSegChunk, n - i);
-    long long r[kSegV];
+    long long val[kSegV];
+    bool tie[kSegV];
     long long mine = 0;
-    bool tie = false;
 #pragma unroll
     for (int v = 0; v < kSegV; ++v) {
       const uint32_t j = (uint32_t)(kSegV * tid + v);
-      r[v] = 0;
+      val[v] = 0;
+      tie[v] = false;
       if (j < C) {
         const double y = ldexp((double)x[i + j], -ue);  // exact
         if (y >= 0x1p40) {
-          r[v] = 1ll << 40;  // crosses the binade by itself
+          val[v] = 1ll << 40;  // crosses the binade by itself
         } else {
           const double fl = floor(y), f = y - fl;
-          r[v] = (long long)fl + (f > 0.5 ? 1 : 0);
-          tie = tie || f == 0.5;
+          tie[v] = f == 0.5;
+          val[v] = (long long)fl + (f > 0.5 ? 1 : 0);
         }
-        mine += r[v];
+        mine += val[v];
       }
     }
-    if (__syncthreads_or(tie)) {  // parity-dependent rounding in this chunk: add it serially
-      if (tid == 0) {
-        float a = s;
-        for (uint32_t j = 0; j < C; ++j) a = __fadd_rn(a, x[i + j]);
-        s_s = a;
-        s_i = i + C;
-      }
-      __syncthreads();
-      continue;
-    }
-    // block exclusive prefix of the per-thread sums
-    long long incl = mine;
+    long long total0 = 0;
+    const long long base0 = seg_scan_excl(mine, sw, total0);
+    // prefix P0 at each addend; the last tie's P0 inside this thread
+    long long p0[kSegV];
+    bool has = false;
+    long long lastp = 0;
+    {
+      long long run = base0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const long long t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += t;
+      for (int v = 0; v < kSegV; ++v) {
+        run += val[v];
+        p0[v] = run;
+        if (tie[v]) {
+          has = true;
+          lastp = run;
+        }
+      }
     }
-    if (lane == 31) wtot[warp] = incl;
+    const long long prev_in = seg_carry_excl(has, lastp, -K, sw, sh);
+    // round-ups at ties: the sum since the previous tie is odd
+    int ups = 0;
+    bool up[kSegV];
+    {
+      long long prev = prev_in;
+#pragma unroll
+      for (int v = 0; v < kSegV; ++v) {
+        up[v] = tie[v] && (((p0[v] - prev) & 1ll) != 0);
+        if (tie[v]) prev = p0[v];
+        ups += up[v] ? 1 : 0;
+      }
+    }
+    long long tot_up = 0;
+    const long long ubase = seg_scan_excl((long long)ups, sw, tot_up);
     if (tid == 0) s_cross = 0xFFFFFFFFu;
     __syncthreads();
-    long long before = 0, total = 0;
-    for (int w = 0; w < kSegT / 32; ++w) {
-      if (w < warp) before += wtot[w];
-      total += wtot[w];
-    }
-    long long run = K + before + (incl - mine);
+    // first addend at which the sum reaches the next binade
     int cv = -1;
+    long long before_c = 0;
+    {
+      long long u = ubase;
 #pragma unroll
-    for (int v = 0; v < kSegV; ++v) {
-      const uint32_t j = (uint32_t)(kSegV * tid + v);
-      if (cv < 0 && j < C) {
-        if (run + r[v] >= (1ll << 24)) cv = v;
-        else run += r[v];
+      for (int v = 0; v < kSegV; ++v) {
+        const uint32_t j = (uint32_t)(kSegV * tid + v);
+        u += up[v] ? 1 : 0;
+        if (cv < 0 && j < C && K + p0[v] + u >= (1ll << 24)) {
+          cv = v;
+          before_c = K + (p0[v] - val[v]) + (u - (up[v] ? 1 : 0));
+        }
       }
     }
     if (cv >= 0) atomicMin(&s_cross, (uint32_t)(kSegV * tid + cv));
@@ -1091,12 +1188,12 @@ km_wcss_seg_kernel(Prob P, const float* __restrict__ mind) {
     const uint32_t cj = s_cross;
     if (cj == 0xFFFFFFFFu) {
       if (tid == 0) {
-        s_s = (float)ldexp((double)(K + total), ue);
+        s_s = (float)ldexp((double)(K + total0 + tot_up), ue);
         s_i = i + C;
       }
     } else if (cv >= 0 && (uint32_t)(kSegV * tid + cv) == cj) {
       // the sum leaves its binade at addend cj: that one add in f32
-      s_s = __fadd_rn((float)ldexp((double)run, ue), x[i + cj]);
+      s_s = __fadd_rn((float)ldexp((double)before_c, ue), x[i + cj]);
       s_i = i + cj + 1;
     }
     __syncthreads();
