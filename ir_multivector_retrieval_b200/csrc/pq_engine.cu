@@ -1436,6 +1436,53 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
   }
 }
 
+// The same update with one warp per subspace (block = 32 x M threads, one
+// 1024-row chunk per CTA): lane l takes rows l, l + 32, ... of the chunk, so
+// each subspace's chunk sums need one warp reduction instead of one per warp
+// and per subspace, and every lane keeps 32 independent row loads in flight.
+// A non-finite weight shows up as a non-finite chunk bound (weights are sums
+// of squares, never negative).
+template <int S>
+__global__ void __launch_bounds__(kMaxM * 32)
+pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, int step,
+                        const float* __restrict__ cb, float* __restrict__ md, double2* __restrict__ chunk,
+                        uint32_t* __restrict__ chunk_cnt, int* __restrict__ nonfinite,
+                        const uint8_t* __restrict__ state, const double* __restrict__ thr, int chunk_stride) {
+  const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+  if (m >= M || state[m] != kRunning) return;
+  float c[S];
+#pragma unroll
+  for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
+  const double T = thr[m];
+  const uint64_t r0 = (uint64_t)blockIdx.x * kSeedChunk;
+  const float* xm = XT + (size_t)m * N * S;
+  float* mm = md + (size_t)m * N;
+  double lo = 0.0, hi = 0.0;
+  uint32_t cnt = 0;
+#pragma unroll 8
+  for (int q = 0; q < kSeedChunk / 32; ++q) {
+    const uint64_t r = r0 + (uint64_t)(q * 32 + lane);
+    if (r < N) {
+      float x[S];
+      load_sub<S>(xm + r * S, x);
+      const float d = l2_small<S>(x, c);
+      const float w = step == 0 ? d : fminf(d, mm[r]);  // the old weight when d is NaN
+      mm[r] = w;
+      lo = __dadd_rd(lo, (double)w);
+      hi = __dadd_ru(hi, (double)w);
+      cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+    }
+  }
+  lo = warp_sum_rd(lo);
+  hi = warp_sum_ru(hi);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if (lane == 0) {
+    chunk[(size_t)m * chunk_stride + blockIdx.x] = make_double2(lo, hi);
+    chunk_cnt[(size_t)m * chunk_stride + blockIdx.x] = cnt;
+    if (!isfinite(lo) || !isfinite(hi)) nonfinite[m] = 1;
+  }
+}
+
 // Upper bound of gamma_n = n u / (1 - n u), u = 2^-53: the recursive
 // summation error bound |S_n - E_n| <= gamma_{n-1} * sum |w_i| (Higham,
 // "Accuracy and Stability of Numerical Algorithms", 2nd ed., eq. 4.4).
@@ -2306,9 +2353,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   ++launches;
   for (int step = 0; step + 1 < K; ++step) {
     switch (S) {
-      case 1: pq_seed_update_kernel<1><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
-      case 2: pq_seed_update_kernel<2><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
-      default: pq_seed_update_kernel<4><<<nchunk, kSeedThreads, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+      case 1: pq_seed_update_w_kernel<1><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+      case 2: pq_seed_update_w_kernel<2><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+      default: pq_seed_update_w_kernel<4><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
     pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(XT, N, S, K, step + 1, cb, mind, chunk, chunk_cnt,
