@@ -83,6 +83,14 @@ def make_input(n: int | None = None) -> np.ndarray:
     return synth.anchor_residuals(make_corpus(n))
 
 
+def _hbm_peak() -> float:
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+    except Exception:
+        return 6650.0  # fallback measured on this pool earlier
+
+
+HBM_PEAK = _hbm_peak()
 TAC_KAPPA = 32_768
 TAC_SMALL = (117_645, 12_288, 10)  # configs[0] rows, kappa (10,240 leaves no room for the tail), theta
 
@@ -396,19 +404,29 @@ def run_b200(args) -> None:
     e2e_enc_s = max_over_ranks(statistics.median(e2e_enc))
     assert np.array_equal(cb_host, dcb.cpu().numpy()), "host and device entry points disagree"
 
-    # ---- roofline of the dominant kernel: the Lloyd assignment that computes
-    # every distance (the first iteration; later ones skip rows by bounds)
-    flops_per_launch = n * K * 3 * DIM  # 3 flops per coordinate per (row, centroid)
-    achieved = flops_per_launch / (first_ms / 1e3) / 1e12
-    sm_mhz = clk.get("sm_mhz") or 1965.0
-    peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # FP32 lanes x clock (one op per lane per cycle)
+    # ---- roofline of the dominant kernel: the k-means++ update (a third of the
+    # device time), one HBM pass per step over the subspace-major rows of this
+    # GPU's subspaces plus the weights read and written; its launches are
+    # sampled with CUDA events inside the engine (every 8th step)
+    upd_samples = sum(s.seed_update_samples for s in stats)
+    upd_ms = sum(s.seed_update_ms_sampled for s in stats) / max(1, upd_samples)
+    m_local = PQ_M // world if (world > 1 and PQ_M >= world) else PQ_M
+    n_rows = n_total if (world > 1 and PQ_M >= world) else n
+    bytes_per_launch = n_rows * m_local * (DIM // PQ_M) * 4 + 2 * n_rows * m_local * 4
+    achieved = bytes_per_launch / (max(upd_ms, 1e-9) / 1e3) / 1e9
+    peak = HBM_PEAK
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get("pq_assign_kernel_lloyd_bytes_per_launch")
+            t = json.loads(tfile.read_text()).get("pq_seed_update_bytes_per_launch")
+            traffic = t * (n_rows * m_local) / (N_ROWS * PQ_M) if t else None
         except Exception:
             traffic = None
+    # the FP32-bound Lloyd assignment beside it (first iteration: every distance)
+    flops_per_launch = n * K * 3 * DIM  # 3 flops per coordinate per (row, centroid)
+    sm_mhz = clk.get("sm_mhz") or 1965.0
+    fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # FP32 lanes x clock (one op per lane per cycle)
 
     tac_line = None
     if not args.no_tac:  # collective when world > 1: every rank takes part
@@ -437,13 +455,15 @@ def run_b200(args) -> None:
                              "rows_exact_fraction": rows_exact / max(1, rows_total),
                              "note": ("iterations after the first skip (row, subspace) pairs whose exact "
                                       "distance bounds prove the cluster unchanged")},
-            "roofline": {"kernel": "pq_assign_kernel<4,Lloyd,bounds> (first Lloyd iteration, every distance)",
-                         "bound": "fp32", "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": ("nominal FP32 issue rate, 148 SM x 128 lanes x median SM clock of "
-                                         "this run; MEASURED_PEAKS.json has no FP32 entry"),
-                         "algorithmic_flops_per_launch": flops_per_launch,
-                         "avg_launch_ms": first_ms},
+            "roofline": {"kernel": "pq_seed_update_w_kernel<4> (k-means++ weight update, 254 launches per training)",
+                         "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "avg_launch_ms": upd_ms, "sampled_launches": upd_samples},
+            "fp32_assign": {"kernel": "first Lloyd pass (pq_tc_assign_kernel + pq_hist_kernel)",
+                            "algorithmic_flops": flops_per_launch, "ms": first_ms,
+                            "tflops": flops_per_launch / (first_ms / 1e3) / 1e12, "fp32_issue_peak_tflops": fp32_peak},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(cb_host.nbytes),
                     "encode_mvec_s": n_total / e2e_enc_s / 1e6},

@@ -176,6 +176,9 @@ typedef struct mvr_pq_train_stats {
                                      settled by exact distances */
   uint32_t filter_violations;     /* winners outside the filter's error bound (then the
                                      training ran again with exact scans); 0 expected */
+  double seed_update_ms_sampled;  /* summed device time of every 8th k-means++ update
+                                     launch (steps >= 1) */
+  uint32_t seed_update_samples;   /* launches in that sum */
 } mvr_pq_train_stats;
 
 /* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`

@@ -76,6 +76,8 @@ class PqTrainStats(C.Structure):
         ("lloyd_rows_exact", C.c_uint64),
         ("filter_rows_rechecked", C.c_uint64),
         ("filter_violations", C.c_uint32),
+        ("seed_update_ms_sampled", C.c_double),
+        ("seed_update_samples", C.c_uint32),
     ]
 
 

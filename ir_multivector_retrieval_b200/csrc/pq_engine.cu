@@ -2351,13 +2351,30 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   pq_seed_init_kernel<<<M, 32, 0, st>>>(XT, N, S, K, d_idx0, cb, d_chosen);
   MVR_CUDA(ctx, cudaGetLastError());
   ++launches;
+  // every 8th update launch (step >= 1) bracketed by events: the sampled
+  // duration of the HBM-bound update kernel (stats only)
+  std::vector<cudaEvent_t> sev;
+  if (timing) {
+    sev.resize(2 * (size_t)((K - 2 + 7) / 8), nullptr);
+    for (auto& e : sev) MVR_CUDA(ctx, cudaEventCreate(&e));
+  }
+  struct SevGuard {
+    std::vector<cudaEvent_t>& v;
+    ~SevGuard() {
+      for (auto e : v)
+        if (e) cudaEventDestroy(e);
+    }
+  } sev_guard{sev};
   for (int step = 0; step + 1 < K; ++step) {
+    const bool sample = timing && step >= 1 && (step - 1) % 8 == 0 && (size_t)(2 * ((step - 1) / 8) + 1) < sev.size();
+    if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8)], st));
     switch (S) {
       case 1: pq_seed_update_w_kernel<1><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
       case 2: pq_seed_update_w_kernel<2><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
       default: pq_seed_update_w_kernel<4><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
+    if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8) + 1], st));
     pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(XT, N, S, K, step + 1, cb, mind, chunk, chunk_cnt,
                                                         nchunk, d_draws, d_nonf, d_status, d_state, d_fb,
                                                         d_chosen, d_thr, ctx && ctx->serial_draws ? 1 : 0);
@@ -2534,6 +2551,18 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         am += t;
       }
       out.stats->assign_ms = am;
+      double su = 0.0;
+      uint32_t ns = 0;
+      for (size_t q = 0; q + 1 < sev.size(); q += 2) {
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, sev[q], sev[q + 1]) == cudaSuccess) {
+          su += t;
+          ++ns;
+        }
+      }
+      (void)cudaGetLastError();
+      out.stats->seed_update_ms_sampled = su;
+      out.stats->seed_update_samples = ns;
       out.stats->assign_launches = job.max_iters;
       if (job.max_iters > 0) {
         float t0 = 0.f;
