@@ -4,7 +4,7 @@
 // driver's own bounce buffer at a fraction of the link rate. Large inputs
 // instead go through two context-owned pinned stages: worker threads copy
 // chunk i+1 into one stage while the DMA engine drains chunk i from the
-// other. The copy is complete from the caller's point of view (the source
+// other. Page-locked host buffers are copied directly. The copy is complete from the caller's point of view (the source
 // may be reused) when h2d_staged returns; the device side is ordered on the
 // context stream.
 #include <cuda_runtime.h>
@@ -91,6 +91,17 @@ class HostPool {
 };
 
 namespace {
+// Page-locked (pinned or registered) host memory goes to the DMA engine
+// directly; only pageable memory needs the stages.
+bool is_pinned(const void* h) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, h) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 constexpr size_t kStageBytes = 32u << 20;
 constexpr size_t kStagedMin = 8u << 20;  // smaller copies go straight to the driver
 constexpr size_t kPiece = 2u << 20;
@@ -110,7 +121,7 @@ int ensure_io(Ctx* c) {
 
 int h2d_staged(Ctx* c, void* d, const void* h, size_t bytes) {
   if (bytes == 0) return MVR_OK;
-  if (bytes < kStagedMin) {
+  if (bytes < kStagedMin || is_pinned(h)) {
     MVR_CUDA(c, cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, c->stream));
     return MVR_OK;
   }
@@ -137,7 +148,7 @@ int h2d_staged(Ctx* c, void* d, const void* h, size_t bytes) {
 
 int d2h_staged(Ctx* c, void* h, const void* d, size_t bytes) {
   if (bytes == 0) return MVR_OK;
-  if (bytes < kStagedMin) {
+  if (bytes < kStagedMin || is_pinned(h)) {
     MVR_CUDA(c, cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, c->stream));
     MVR_CUDA(c, cudaStreamSynchronize(c->stream));
     return MVR_OK;

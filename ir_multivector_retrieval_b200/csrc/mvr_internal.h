@@ -72,8 +72,10 @@ struct Ctx {
   uint32_t tc_viol_seen = 0;  // violations already answered by an exact re-run
 };
 
-// Host->device copy of a pageable host buffer through the pinned stages;
-// the source may be reused when it returns. Ordered on the context stream.
+// Host->device copy through the pinned stages (pageable sources: the source
+// may be reused when it returns) or directly (page-locked sources: complete
+// when the context stream reaches it; every host entry point synchronises
+// before it returns). Ordered on the context stream.
 int h2d_staged(Ctx* ctx, void* d, const void* h, size_t bytes);
 // Device->host copy through the pinned stages; complete when it returns.
 int d2h_staged(Ctx* ctx, void* h, const void* d, size_t bytes);
