@@ -131,6 +131,7 @@ def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=
                            "rows_full_scan": st["filter_rows_full_scan"]},
                 "wcss_total": r.wcss_total, "outputs_sha256": sorted(digests)[0],
                 "repeatable": len(digests) == 1})
+    out["_centroids"] = r.centroids
     if sharded:
         out["phases_ms_note"] = "phases and tokens of rank 0; e2e_ms and device_ms are the max over ranks"
     n0, k0, th0 = TAC_SMALL
@@ -155,6 +156,52 @@ def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=
         small["bit_exact_vs_cpu"] = bool(np.array_equal(rc.assignments, r0.assignments)
                                          and rc.centroids.tobytes() == r0.centroids.tobytes())
     out["small"] = small
+    return out
+
+
+def measure_hnsw(centroids, steps: int, cpu: bool, ctx=None) -> dict:
+    """hnsw.build over the clusterFlat centroids as the storage layer runs it
+    (storage.zig:404-424): the centroids normalised (vec.normalizeRowsInPlace,
+    on the GPU), then the chunked deferred-commit build (the reference's
+    10-thread path; the graph is the same for every thread count >= 2) with
+    M 32, efConstruction 1500 and seed 42 +% 0xdeadbeef. e2e_ms: the host
+    entry point (host centroids in, host CSR out); device_ms: the build's
+    CUDA-event time. One GPU: the build does not shard."""
+    from ir_multivector_retrieval_b200 import hnsw
+
+    seed = (42 + hnsw.STORAGE_SEED_OFFSET) & (2**64 - 1)
+    x = hnsw.normalize_rows(centroids, DIM, ctx=ctx)
+    kappa = x.size // DIM
+    hnsw.build(x[: DIM * 4096], DIM, seed, ctx=ctx)  # warm-up
+    walls, devs, digests, g = [], [], set(), None
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        g = hnsw.build(x, DIM, seed, ctx=ctx)
+        walls.append(time.perf_counter() - t0)
+        devs.append(g.device_ms)
+        digests.add(hashlib.sha256(b"".join(o.tobytes() + b.tobytes() for o, b in
+                                            zip(g.layer_offsets, g.layer_neighbours))).hexdigest())
+    out = {"workload": f"hnsw.build over the {kappa:,} clusterFlat centroids (dim {DIM}), M 32, efConstruction "
+                       "1500, chunked deferred-commit path",
+           "e2e_ms": statistics.median(walls) * 1e3, "device_ms": statistics.median(devs),
+           "gpu_launches": g.kernel_launches, "max_level": g.max_level,
+           "edges_per_layer": [int(b.size) for b in g.layer_neighbours],
+           "graph_sha256": sorted(digests)[0], "repeatable": len(digests) == 1,
+           "reference_published": {"value_s": 6.7, "note": "README: hnsw.build (parallel, 10 threads) on the "
+                                                         "full Jira corpus, Apple M-series; other hardware"}}
+    if cpu:
+        from oracle import oracle
+
+        oracle.build()
+        cores = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        o = oracle.hnsw_build(x, DIM, seed, n_threads=2, workers=cores)
+        out["cpu_baseline"] = {"value_ms": (time.perf_counter() - t0) * 1e3, "cores": cores, "kind": "port",
+                               "sample": "the whole build, the C restatement planning each chunk on every host "
+                                         "core (like the reference's worker threads)"}
+        out["bit_exact_vs_cpu"] = bool(o.entry_point == g.entry_point and all(
+            np.array_equal(a, b) for a, b in zip(o.layer_offsets + o.layer_neighbours,
+                                                 g.layer_offsets + g.layer_neighbours)))
     return out
 
 
@@ -432,6 +479,11 @@ def run_b200(args) -> None:
     if not args.no_tac:  # collective when world > 1: every rank takes part
         tac_line = measure_tac(corpus, 3, cpu=(world == 1 and not args.no_cpu), ctx=ctx, world=world,
                                reduce=max_over_ranks)
+    hnsw_line = None
+    if tac_line is not None:
+        cents = tac_line.pop("_centroids")
+        if world == 1 and not args.no_hnsw:  # one GPU: the graph build does not shard
+            hnsw_line = measure_hnsw(cents, 3, cpu=not args.no_cpu, ctx=ctx)
 
     if rank == 0:
         line = {
@@ -470,6 +522,8 @@ def run_b200(args) -> None:
         }
         if tac_line is not None:
             line["tac"] = tac_line
+        if hnsw_line is not None:
+            line["hnsw"] = hnsw_line
         if world == 1 and not args.no_cpu:
             cpu = cpu_lloyd_seconds_per_iter(x, host_threads(), target_s=args.cpu_target_s)
             line["cpu_baseline"] = {
@@ -493,13 +547,22 @@ def main() -> int:
     ap.add_argument("--cpu-target-s", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-tac", action="store_true", help="skip the clusterFlat measurement")
+    ap.add_argument("--no-hnsw", action="store_true", help="skip the hnsw.build measurement")
     ap.add_argument("--tac-only", action="store_true",
                     help="only the clusterFlat measurement (one GPU; for profiling captures)")
+    ap.add_argument("--hnsw-only", action="store_true",
+                    help="only clusterFlat and hnsw.build over its centroids (one GPU)")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()
-    if args.tac_only:
-        print(json.dumps({"tac": measure_tac(make_corpus(args.rows), args.steps, cpu=not args.no_cpu)}), flush=True)
+    if args.tac_only or args.hnsw_only:
+        t = measure_tac(make_corpus(args.rows), 1 if args.hnsw_only else args.steps,
+                        cpu=not args.no_cpu and args.tac_only)
+        cents = t.pop("_centroids")
+        out = {"tac": t}
+        if args.hnsw_only:
+            out["hnsw"] = measure_hnsw(cents, args.steps, cpu=not args.no_cpu)
+        print(json.dumps(out), flush=True)
         return 0
     if args.impl == "reference":
         run_reference(args)

@@ -69,7 +69,8 @@ enum {
   MVR_E_NCCL = 101,             /* an NCCL call failed */
   MVR_E_TIMEOUT = 102,          /* a bounded device wait ran out */
   MVR_E_INVALID_ARGUMENT = 103, /* null pointer, unsupported shape */
-  MVR_E_NO_DEVICE = 104         /* no CUDA device with sm_100 */
+  MVR_E_NO_DEVICE = 104,        /* no CUDA device with sm_100 */
+  MVR_E_DEVICE_LIMIT = 105      /* a device-side capacity was exceeded; nothing returned */
 };
 
 /* Number of centroids per PQ subspace (reference constants.PQ_CENTROIDS). */
@@ -491,6 +492,52 @@ int mvr_tac_allocate_budgets(const uint32_t* freqs, const float* spreads,
                              uint32_t* kappa, float* frac, uint64_t n,
                              uint32_t kappa_total,
                              const mvr_clustering_params* p);
+
+/* ------------------------------------------------------------------------
+ * HNSW over the TAC centroids (src/index/hnsw.zig)
+ * ------------------------------------------------------------------------ */
+
+/* A built graph: the reference's `Hnsw` (hnsw.zig:136-170) in host memory,
+ * owned by the library. */
+typedef struct mvr_hnsw mvr_hnsw;
+
+/* hnsw.build (hnsw.zig:314-475) on the GPU over `n_floats / dim` centroids,
+ * which the caller has L2-normalised (storage.zig:408-411 does that with
+ * vec.normalizeRowsInPlace; mvr_normalize_rows is its GPU form).
+ * n_threads <= 1 builds the reference's serial path (buildSerial,
+ * hnsw.zig:477-625); n_threads >= 2 its chunked deferred-commit path
+ * (buildParallel, hnsw.zig:639-946), whose graph is the same for every
+ * thread count >= 2, so the value only selects the path. Supported:
+ * 1 <= m <= 32, 1 <= ef_construction <= 4096, dim <= 256, at most 2^27
+ * centroids (MVR_E_INVALID_ARGUMENT otherwise). Equal similarities are
+ * ordered by node id where the reference's heaps leave the order to their
+ * layout. Errors: MVR_E_DIM_MISMATCH, MVR_E_EMPTY_CORPUS (the reference's
+ * HnswError), MVR_E_DEVICE_LIMIT when more than 512 beam entries tie
+ * exactly at the beam's minimum. */
+int mvr_hnsw_build(mvr_ctx* ctx, const float* centroids, uint64_t n_floats, uint32_t dim,
+                   uint64_t seed, uint32_t ef_construction, uint32_t m, uint32_t n_threads,
+                   mvr_hnsw** out);
+/* The same with the centroids in device memory (read only). */
+int mvr_hnsw_build_device(mvr_ctx* ctx, const float* d_centroids, uint64_t n_floats,
+                          uint32_t dim, uint64_t seed, uint32_t ef_construction, uint32_t m,
+                          uint32_t n_threads, mvr_hnsw** out);
+/* n, entry_point, max_level of a built graph; device time of the build in
+ * milliseconds and the number of kernels it launched. */
+void mvr_hnsw_info(const mvr_hnsw* g, uint32_t* n, uint32_t* entry_point, uint32_t* max_level,
+                   float* device_ms, uint64_t* kernel_launches);
+/* Top level of every node (n bytes). */
+const uint8_t* mvr_hnsw_node_levels(const mvr_hnsw* g);
+/* Layer `layer` as CSR: offsets (n + 1 entries, from 0) and the neighbour
+ * ids (offsets[n] entries); null when layer > max_level. */
+const uint32_t* mvr_hnsw_layer_offsets(const mvr_hnsw* g, uint32_t layer);
+const uint32_t* mvr_hnsw_layer_neighbours(const mvr_hnsw* g, uint32_t layer, uint64_t* count);
+void mvr_hnsw_free(mvr_hnsw* g);
+
+/* vec.normalizeRowsInPlace (src/util/vec.zig:185-253) on the GPU, in place
+ * on a host buffer: each row times 1 / sqrt(dot(row, row)), zero rows kept. */
+int mvr_normalize_rows(mvr_ctx* ctx, float* rows, uint64_t n_floats, uint32_t dim);
+/* The same on a device buffer, ordered on the context's stream. */
+int mvr_normalize_rows_device(mvr_ctx* ctx, float* d_rows, uint64_t n_floats, uint32_t dim);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -45,6 +45,7 @@ STATUS_NAMES = {
     102: "Timeout",
     103: "InvalidArgument",
     104: "NoDevice",
+    105: "DeviceLimit",
 }
 CODES = {v: k for k, v in STATUS_NAMES.items()}
 
@@ -202,6 +203,18 @@ SIGNATURES = {
          _P, C.c_uint64, _U64, _F],
     ),
     "mvr_tac_partition_tokens": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, _P]),
+    "mvr_hnsw_build": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+                                 C.POINTER(C.c_void_p)]),
+    "mvr_hnsw_build_device": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32,
+                                        C.c_uint32, C.POINTER(C.c_void_p)]),
+    "mvr_hnsw_info": (None, [_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                             C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
+    "mvr_hnsw_node_levels": (C.POINTER(C.c_uint8), [_P]),
+    "mvr_hnsw_layer_offsets": (C.POINTER(C.c_uint32), [_P, C.c_uint32]),
+    "mvr_hnsw_layer_neighbours": (C.POINTER(C.c_uint32), [_P, C.c_uint32, C.POINTER(C.c_uint64)]),
+    "mvr_hnsw_free": (None, [_P]),
+    "mvr_normalize_rows": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32]),
+    "mvr_normalize_rows_device": (C.c_int, [_P, _P, C.c_uint64, C.c_uint32]),
     "mvr_tac_allocate_budgets": (
         C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint32, C.POINTER(ClusteringParams)]),
 }

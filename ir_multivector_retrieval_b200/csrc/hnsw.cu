@@ -1,0 +1,1012 @@
+// hnsw.cu — HNSW over the TAC centroids on the GPU: hnsw.build
+// (src/index/hnsw.zig:314-946) and vec.normalizeRowsInPlace (vec.zig:185-253).
+//
+// The reference inserts nodes 1..n-1 in chunks (buildParallel, :639-946): for
+// a chunk of min(256, q_base) nodes it plans every node against the graph as
+// it stood at the chunk's start — greedy descent through the layers above
+// the node's level, then per layer a beam search of width efConstruction and
+// the heuristic neighbour selection — and then commits the plans in node
+// order: the node's own lists, and the node appended to each chosen
+// neighbour's list, which is shrunk by the heuristic when it exceeds its cap
+// (2M on layer 0, M above). The serial path (n_threads <= 1, :477-625) is the
+// same loop with chunks of one node.
+//
+// On the GPU, per chunk:
+//   hnsw_plan_kernel     one CTA per node of the chunk: the whole plan, with
+//                        the beam in shared memory
+//   hnsw_commit_own      the chunk's own lists, and one bit per (layer,
+//                        neighbour, node) marking every reverse edge
+//   hnsw_commit_reverse  one warp per (layer, neighbour) that received edges:
+//                        appends them in node order, shrinking as it goes.
+//                        The chosen neighbours of a chunk are all older nodes
+//                        (a chunk's nodes have no edges in the snapshot), and a
+//                        shrink reads only its own node's list, so the
+//                        neighbours are independent of one another and each
+//                        replays exactly the reference's sequence.
+// Levels come from the reference's RNG on the host (pickLevel draws one
+// nextFloat per node, in node order, and nothing else draws), so the host
+// knows every chunk's snapshot entry point and top level without waiting for
+// the device; a build is one asynchronous stream of launches.
+//
+// The beam search (searchLayer, :995-1043) as a sorted array. The reference
+// keeps a frontier max-heap C and a beam min-heap W of at most ef entries; a
+// neighbour e of the expanded node is pushed to both when |W| < ef or
+// sim(e) > min(W), and the worst of W is dropped when |W| > ef. Here:
+//   * W is kept sorted (higher similarity first, equal similarities by the
+//     smaller node id) with an "expanded" bit per entry.
+//   * Candidate j of an expansion (the unvisited neighbours in list order) is
+//     accepted iff fewer than ef of W ∪ {candidates before j} have similarity
+//     >= sim(j). That is the reference's sequential test: W's similarities
+//     are always the ef largest of everything offered so far, and a rejected
+//     candidate is never above the minimum it was tested against.
+//   * The new W is the first ef of the merge of W and the accepted set.
+//   * The frontier entries that can still be expanded are the unexpanded
+//     entries of W and those dropped from W with a similarity equal to W's
+//     minimum (the reference stops only at a candidate strictly below the
+//     minimum); anything lower never expands. Those ties are kept in a small
+//     list; all of W ranks above them, so the next expansion is the first
+//     unexpanded entry of W, else the tie with the smallest id.
+// Equal similarities: the reference's heaps order them by similarity alone,
+// so among exactly equal similarities its pop order follows the heap layout
+// of Zig's std.PriorityQueue; here they go by node id (the smaller id first
+// from the frontier and in the beam's output, the larger id first out of the
+// beam). Everything else — the comparisons (similarity alone), list orders,
+// the stable sorts of selectHeuristic, vec.dot's order — is the reference's.
+//
+// Arithmetic: vec.dot in the reference's order (len 64/128: four lane
+// accumulators from +0 over the 4-wide chunks, then ((a0+a1)+a2)+a3; other
+// lengths the same 4-lane loop plus the scalar tail; len 2 a0*b0 + a1*b1),
+// every operation __fmul_rn/__fadd_rn.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/mvr.h"
+#include "mvr_internal.h"
+#include "mvr_rng.h"
+
+namespace mvr {
+namespace {
+
+constexpr uint32_t kChunk = 256;                // CHUNK_SIZE (hnsw.zig:272)
+constexpr uint32_t kMaxLayers = 32;             // pickLevel caps levels at 31
+constexpr uint32_t kMaxM = 32;                  // M; lists hold <= 2M at rest
+constexpr uint32_t kMaxList = 2 * kMaxM + 1;    // cap + 1 during a commit
+constexpr uint32_t kListPad = kMaxList + 1;     // even: keeps 8-byte entries aligned
+constexpr uint32_t kPlanThreads = 256;
+constexpr uint32_t kTieCap = 512;
+constexpr uint32_t kExpanded = 0x80000000u;
+constexpr uint32_t kMaskWords = kChunk / 32;    // one bit per node of a chunk
+constexpr uint32_t kMaxEf = 4096;
+constexpr uint32_t kMaxDim = 256;
+constexpr size_t kSmemLimit = 226 * 1024;  // 227 KB per CTA less the static control block
+
+// device status bits
+constexpr uint32_t kErrTies = 1u, kErrLoop = 2u;
+
+struct DevGraph {
+  uint32_t n, dim, m;
+  uint32_t cap[kMaxLayers];
+  uint32_t* ids[kMaxLayers];  // n x (cap + 1) per layer
+  uint32_t* len[kMaxLayers];  // n per layer
+};
+
+struct Ent {
+  float sim;
+  uint32_t node;  // bit 31: expanded
+};
+
+__device__ __forceinline__ bool better(Ent a, Ent b) {
+  const uint32_t na = a.node & ~kExpanded, nb = b.node & ~kExpanded;
+  return a.sim > b.sim || (a.sim == b.sim && na < nb);
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// vec.dot(a, b) in the reference's order; a and b 16-byte aligned when dim
+// is a multiple of 4.
+__device__ __forceinline__ float dot_ref(const float* __restrict__ a, const float* __restrict__ b, uint32_t dim) {
+  if (dim == 2) return __fadd_rn(__fmul_rn(a[0], b[0]), __fmul_rn(a[1], b[1]));
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  uint32_t i = 0;
+  if ((dim & 3u) == 0) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    for (uint32_t c = 0; c < dim / 4; ++c) {
+      const float4 x = a4[c], y = b4[c];
+      a0 = __fadd_rn(a0, __fmul_rn(x.x, y.x));
+      a1 = __fadd_rn(a1, __fmul_rn(x.y, y.y));
+      a2 = __fadd_rn(a2, __fmul_rn(x.z, y.z));
+      a3 = __fadd_rn(a3, __fmul_rn(x.w, y.w));
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  }
+  for (; i + 4 <= dim; i += 4) {
+    a0 = __fadd_rn(a0, __fmul_rn(a[i], b[i]));
+    a1 = __fadd_rn(a1, __fmul_rn(a[i + 1], b[i + 1]));
+    a2 = __fadd_rn(a2, __fmul_rn(a[i + 2], b[i + 2]));
+    a3 = __fadd_rn(a3, __fmul_rn(a[i + 3], b[i + 3]));
+  }
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  for (; i < dim; ++i) s = __fadd_rn(s, __fmul_rn(a[i], b[i]));
+  return s;
+}
+
+// The same with b at a padded shared-memory row (scalar loads; the rows of
+// consecutive lanes sit in consecutive banks).
+__device__ __forceinline__ float dot_ref_scalar(const float* a, const float* b, uint32_t dim) {
+  if (dim == 2) return __fadd_rn(__fmul_rn(a[0], b[0]), __fmul_rn(a[1], b[1]));
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  uint32_t i = 0;
+  for (; i + 4 <= dim; i += 4) {
+    a0 = __fadd_rn(a0, __fmul_rn(a[i], b[i]));
+    a1 = __fadd_rn(a1, __fmul_rn(a[i + 1], b[i + 1]));
+    a2 = __fadd_rn(a2, __fmul_rn(a[i + 2], b[i + 2]));
+    a3 = __fadd_rn(a3, __fmul_rn(a[i + 3], b[i + 3]));
+  }
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+  for (; i < dim; ++i) s = __fadd_rn(s, __fmul_rn(a[i], b[i]));
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// plan
+// ---------------------------------------------------------------------------
+
+struct PlanLayout {  // byte offsets into dynamic shared memory
+  uint32_t qv, w0, w1, vis, cn, cs, as, ev, ties, rv, rid, cv;
+  uint32_t nwords, rstride, bytes;
+};
+
+struct PlanArgs {
+  DevGraph g;
+  PlanLayout lay;
+  const float* x;
+  const uint8_t* levels;
+  uint32_t q_base, snap_entry, snap_max, ef;
+  uint32_t* chosen;    // [kChunk][kMaxLayers][kMaxM]
+  uint32_t* n_chosen;  // [kChunk][kMaxLayers]
+  uint32_t* status;
+};
+
+struct PlanCtl {
+  uint32_t wn, hint, pop, done, nt, nev, newhint, cur, nr;
+  float tsim;
+  uint32_t bal[2], abal[2];
+};
+
+// greedySearchLayer (hnsw.zig:969-991), warp 0: the first strict maximum of
+// each list, while it improves.
+__device__ uint32_t greedy_layer(const PlanArgs& a, const float* qv, uint32_t L, uint32_t cur) {
+  const uint32_t lane = threadIdx.x & 31, dim = a.g.dim, cap = a.g.cap[L];
+  float cur_sim = dot_ref(qv, a.x + (size_t)cur * dim, dim);
+  for (uint32_t step = 0; step <= a.g.n; ++step) {
+    const uint32_t cnt = a.g.len[L][cur];
+    const uint32_t* list = a.g.ids[L] + (size_t)cur * (cap + 1);
+    float bs = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t i = lane; i < cnt; i += 32) {
+      const float s = dot_ref(qv, a.x + (size_t)list[i] * dim, dim);
+      if (bi == 0xFFFFFFFFu || s > bs) {  // first maximum of this lane's entries
+        bs = s;
+        bi = i;
+      }
+    }
+    for (int o = 16; o; o >>= 1) {
+      const float os = __shfl_xor_sync(~0u, bs, o);
+      const uint32_t oi = __shfl_xor_sync(~0u, bi, o);
+      if (oi != 0xFFFFFFFFu && (bi == 0xFFFFFFFFu || os > bs || (os == bs && oi < bi))) {
+        bs = os;
+        bi = oi;
+      }
+    }
+    if (bi == 0xFFFFFFFFu || !(bs > cur_sim)) return cur;
+    cur_sim = bs;
+    cur = list[bi];
+  }
+  return cur;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) hnsw_plan_kernel(PlanArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ PlanCtl ctl;
+  const PlanLayout& lay = a.lay;
+  float* qv = reinterpret_cast<float*>(sm + lay.qv);
+  Ent* const wb0 = reinterpret_cast<Ent*>(sm + lay.w0);
+  Ent* const wb1 = reinterpret_cast<Ent*>(sm + lay.w1);
+  uint32_t* vis = reinterpret_cast<uint32_t*>(sm + lay.vis);
+  uint32_t* cn = reinterpret_cast<uint32_t*>(sm + lay.cn);
+  float* cs = reinterpret_cast<float*>(sm + lay.cs);
+  Ent* as = reinterpret_cast<Ent*>(sm + lay.as);
+  Ent* ev = reinterpret_cast<Ent*>(sm + lay.ev);
+  uint32_t* ties = reinterpret_cast<uint32_t*>(sm + lay.ties);
+  float* rv = reinterpret_cast<float*>(sm + lay.rv);
+  uint32_t* rid = reinterpret_cast<uint32_t*>(sm + lay.rid);
+  float* cv = reinterpret_cast<float*>(sm + lay.cv);
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t qi = blockIdx.x, q = a.q_base + qi, dim = a.g.dim, ef = a.ef, m = a.g.m;
+  for (uint32_t i = tid; i < dim; i += blockDim.x) qv[i] = a.x[(size_t)q * dim + i];
+  const uint32_t l_new = a.levels[q];
+  __syncthreads();
+
+  // Phase A: greedy descent through the layers above l_new
+  if (warp == 0) {
+    uint32_t cur = a.snap_entry;
+    if (a.snap_max > l_new)
+      for (uint32_t L = a.snap_max; L > l_new; --L) cur = greedy_layer(a, qv, L, cur);
+    if (lane == 0) ctl.cur = cur;
+  }
+  __syncthreads();
+  const uint32_t top = a.snap_max < l_new ? a.snap_max : l_new;
+  uint32_t buf = 0;
+
+  for (int Ls = (int)top; Ls >= 0; --Ls) {
+    const uint32_t L = (uint32_t)Ls, cap = a.g.cap[L];
+    // ---- searchLayer from ctl.cur
+    for (uint32_t i = tid; i < lay.nwords; i += blockDim.x) vis[i] = 0;
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t e0 = ctl.cur;
+      (buf ? wb1 : wb0)[0] = Ent{dot_ref(qv, a.x + (size_t)e0 * dim, dim), e0};
+      vis[e0 >> 5] |= 1u << (e0 & 31);
+      ctl.wn = 1;
+      ctl.hint = 0;
+      ctl.nt = 0;
+      ctl.tsim = 0.f;
+    }
+    __syncthreads();
+    for (uint32_t it = 0;; ++it) {
+      Ent* W = buf ? wb1 : wb0;
+      const uint32_t wn = ctl.wn;
+      if (it > a.g.n) {  // every node expands at most once
+        if (tid == 0) atomicOr(a.status, kErrLoop);
+        break;
+      }
+      // the next expansion: first unexpanded entry of W, else the smallest tie
+      if (warp == 0) {
+        uint32_t p = wn;
+        for (uint32_t base = ctl.hint; base < wn; base += 32) {
+          const uint32_t i = base + lane;
+          const bool un = i < wn && !(W[i].node & kExpanded);
+          const uint32_t b = __ballot_sync(~0u, un);
+          if (b) {
+            p = base + __ffs(b) - 1;
+            break;
+          }
+        }
+        if (p < wn) {
+          if (lane == 0) {
+            ctl.pop = W[p].node;
+            W[p].node |= kExpanded;
+            ctl.hint = p;
+            ctl.done = 0;
+          }
+        } else {
+          const uint32_t nt = ctl.nt;
+          uint32_t best = 0xFFFFFFFFu, bi = 0;
+          for (uint32_t i = lane; i < nt; i += 32)
+            if (ties[i] < best) {
+              best = ties[i];
+              bi = i;
+            }
+          for (int o = 16; o; o >>= 1) {
+            const uint32_t ob = __shfl_xor_sync(~0u, best, o), oi = __shfl_xor_sync(~0u, bi, o);
+            if (ob < best) {
+              best = ob;
+              bi = oi;
+            }
+          }
+          if (lane == 0) {
+            if (nt == 0) {
+              ctl.done = 1;
+            } else {
+              ctl.pop = best;
+              ties[bi] = ties[nt - 1];
+              ctl.nt = nt - 1;
+              ctl.done = 0;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (ctl.done) break;
+      const uint32_t c = ctl.pop;
+      // unvisited neighbours of c, in list order (lists hold <= 2M <= 64 at rest)
+      const uint32_t cnt = a.g.len[L][c];
+      uint32_t e = 0;
+      bool fresh = false;
+      if (tid < cnt) {
+        e = a.g.ids[L][(size_t)c * (cap + 1) + tid];
+        const uint32_t bit = 1u << (e & 31);
+        fresh = !(atomicOr(&vis[e >> 5], bit) & bit);
+      }
+      if (warp < 2) {
+        const uint32_t b = __ballot_sync(~0u, fresh);
+        if (lane == 0) ctl.bal[warp] = b;
+      }
+      __syncthreads();
+      const uint32_t b0 = ctl.bal[0], b1 = ctl.bal[1];
+      const uint32_t k = __popc(b0) + __popc(b1);
+      if (k == 0) continue;
+      if (fresh) {
+        const uint32_t j = (warp == 0 ? 0u : (uint32_t)__popc(b0)) + __popc((warp == 0 ? b0 : b1) & lanemask_lt());
+        cn[j] = e;
+        cs[j] = dot_ref(qv, a.x + (size_t)e * dim, dim);
+      }
+      __syncthreads();
+      // acceptance
+      bool acc = false;
+      if (tid < k) {
+        const float sj = cs[tid];
+        uint32_t lo = 0, hi = wn;
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (W[mid].sim >= sj)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        uint32_t cp = 0;
+        for (uint32_t i = 0; i < tid; ++i) cp += cs[i] >= sj ? 1u : 0u;
+        acc = lo + cp < ef;
+      }
+      if (warp < 2) {
+        const uint32_t b = __ballot_sync(~0u, acc);
+        if (lane == 0) ctl.abal[warp] = b;
+      }
+      __syncthreads();
+      const uint32_t a0 = ctl.abal[0], a1 = ctl.abal[1];
+      const uint32_t na = __popc(a0) + __popc(a1);
+      if (na == 0) continue;
+      if (acc) {  // rank among the accepted, in the beam's order
+        const Ent me{cs[tid], cn[tid]};
+        uint32_t r = 0;
+        for (uint32_t i = 0; i < k; ++i) {
+          const bool ai = i < 32 ? ((a0 >> i) & 1u) : ((a1 >> (i - 32)) & 1u);
+          if (ai && better(Ent{cs[i], cn[i]}, me)) ++r;
+        }
+        as[r] = me;
+      }
+      if (tid == 0) {
+        ctl.newhint = 0xFFFFFFFFu;
+        ctl.nev = 0;
+      }
+      __syncthreads();
+      // merge W and the accepted entries into the other buffer, first ef kept
+      Ent* Wn = buf ? wb0 : wb1;
+      const uint32_t total = wn + na, hint = ctl.hint;
+      for (uint32_t i = tid; i < total; i += blockDim.x) {
+        Ent xe;
+        uint32_t pos;
+        if (i < wn) {
+          xe = W[i];
+          uint32_t lo = 0, hi = na;
+          while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (better(as[mid], xe))
+              lo = mid + 1;
+            else
+              hi = mid;
+          }
+          pos = i + lo;
+          if (i == hint) atomicMin(&ctl.newhint, pos);
+        } else {
+          const uint32_t r = i - wn;
+          xe = as[r];
+          uint32_t lo = 0, hi = wn;
+          while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (better(W[mid], xe))
+              lo = mid + 1;
+            else
+              hi = mid;
+          }
+          pos = r + lo;
+          if (r == 0) atomicMin(&ctl.newhint, pos);
+        }
+        if (pos < ef) {
+          Wn[pos] = xe;
+        } else if (!(xe.node & kExpanded)) {  // at most na <= 64 leave
+          const uint32_t v = atomicAdd(&ctl.nev, 1u);
+          ev[v] = xe;
+        }
+      }
+      __syncthreads();
+      if (warp == 0 && total > ef) {  // the beam is full: keep the live ties
+        const float mn = Wn[ef - 1].sim;
+        uint32_t nt = ctl.nt;
+        if (nt && ctl.tsim != mn) nt = 0;
+        const uint32_t nev = ctl.nev;
+        for (uint32_t base = 0; base < nev; base += 32) {
+          const uint32_t i = base + lane;
+          const bool t = i < nev && ev[i].sim == mn;
+          const uint32_t b = __ballot_sync(~0u, t);
+          if (t) {
+            const uint32_t slot = nt + __popc(b & lanemask_lt());
+            if (slot < kTieCap) ties[slot] = ev[i].node & ~kExpanded;
+          }
+          nt += __popc(b);
+        }
+        if (nt > kTieCap) {
+          nt = kTieCap;
+          if (lane == 0) atomicOr(a.status, kErrTies);
+        }
+        if (lane == 0) {
+          ctl.nt = nt;
+          ctl.tsim = mn;
+        }
+      }
+      if (tid == 0) {
+        const uint32_t nw = total < ef ? total : ef;
+        ctl.wn = nw;
+        ctl.hint = ctl.newhint < nw ? ctl.newhint : nw;
+      }
+      buf ^= 1u;
+      __syncthreads();
+    }
+    __syncthreads();
+    // ---- the beam, best first, is W[0 .. wn); next layer starts at its best
+    const Ent* W = buf ? wb1 : wb0;
+    const uint32_t wn = ctl.wn;
+    // ---- selectHeuristic (warp 0): keep a candidate unless a chosen
+    // neighbour is strictly more similar to it than the query is
+    if (warp == 0) {
+      uint32_t nr = 0;
+      for (uint32_t i = 0; i < wn && nr < m; ++i) {
+        const Ent ce = W[i];
+        const uint32_t cnode = ce.node & ~kExpanded;
+        for (uint32_t d = lane; d < dim; d += 32) cv[d] = a.x[(size_t)cnode * dim + d];
+        __syncwarp();
+        bool pr = false;
+        if (lane < nr) pr = dot_ref_scalar(cv, rv + (size_t)lane * lay.rstride, dim) > ce.sim;
+        const bool keep = __ballot_sync(~0u, pr) == 0;
+        if (keep) {
+          for (uint32_t d = lane; d < dim; d += 32) rv[(size_t)nr * lay.rstride + d] = cv[d];
+          if (lane == 0) rid[nr] = cnode;
+          ++nr;
+        }
+        __syncwarp();
+      }
+      uint32_t* out = a.chosen + ((size_t)qi * kMaxLayers + L) * kMaxM;
+      if (lane < nr) out[lane] = rid[lane];
+      if (lane == 0) {
+        a.n_chosen[(size_t)qi * kMaxLayers + L] = nr;
+        ctl.cur = wn ? (W[0].node & ~kExpanded) : ctl.cur;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// commit
+// ---------------------------------------------------------------------------
+
+struct CommitArgs {
+  DevGraph g;
+  const float* x;
+  const uint8_t* levels;
+  uint32_t q_base, chunk_len, snap_max;
+  const uint32_t* chosen;
+  const uint32_t* n_chosen;
+  uint32_t* mask;     // [layers][n][kMaskWords]
+  uint32_t* touched;  // [layers][n]
+  uint32_t* tlist;    // layer * n + node
+  uint32_t* tcount;
+  uint32_t warp_smem_floats;
+  uint32_t rstride;
+};
+
+// The chunk's own lists (each empty before: nothing links to a node of its
+// own chunk) and the reverse-edge marks. One warp per node of the chunk.
+__global__ void hnsw_commit_own(CommitArgs a) {
+  const uint32_t qi = blockIdx.x, lane = threadIdx.x, q = a.q_base + qi, n = a.g.n;
+  const uint32_t l_new = a.levels[q];
+  const uint32_t top = a.snap_max < l_new ? a.snap_max : l_new;
+  for (uint32_t L = 0; L <= top; ++L) {
+    const uint32_t nc = a.n_chosen[(size_t)qi * kMaxLayers + L], cap = a.g.cap[L];
+    if (lane < nc) {
+      const uint32_t r = a.chosen[((size_t)qi * kMaxLayers + L) * kMaxM + lane];
+      a.g.ids[L][(size_t)q * (cap + 1) + lane] = r;
+      const size_t key = (size_t)L * n + r;
+      atomicOr(&a.mask[key * kMaskWords + (qi >> 5)], 1u << (qi & 31));
+      if (atomicExch(&a.touched[key], 1u) == 0u) a.tlist[atomicAdd(a.tcount, 1u)] = (uint32_t)key;
+    }
+    if (lane == 0) a.g.len[L][q] = nc;
+  }
+}
+
+// shrinkNeighbours (hnsw.zig:1090-1107) of node r's list (len = cap + 1),
+// whole warp; returns the kept count. Shared scratch per warp: xr[dimp],
+// cv[dimp], rv[2M][rstride], ss[kListPad], sid[kListPad], so[kMaxList].
+__device__ uint32_t shrink_list(const CommitArgs& a, uint32_t* list, uint32_t len, uint32_t cap, float* xr,
+                                float* cv, float* rv, float* ss, uint32_t* sid, Ent* so) {
+  const uint32_t lane = threadIdx.x & 31, dim = a.g.dim;
+  for (uint32_t i = lane; i < len; i += 32) {
+    const uint32_t id = list[i];
+    sid[i] = id;
+    ss[i] = dot_ref(xr, a.x + (size_t)id * dim, dim);
+  }
+  __syncwarp();
+  // std.mem.sort by similarity, descending, stable
+  for (uint32_t i = lane; i < len; i += 32) {
+    const float s = ss[i];
+    uint32_t r = 0;
+    for (uint32_t j = 0; j < len; ++j) r += (ss[j] > s || (ss[j] == s && j < i)) ? 1u : 0u;
+    so[r] = Ent{s, sid[i]};
+  }
+  __syncwarp();
+  uint32_t nr = 0;
+  for (uint32_t i = 0; i < len && nr < cap; ++i) {
+    const Ent ce = so[i];
+    for (uint32_t d = lane; d < dim; d += 32) cv[d] = a.x[(size_t)ce.node * dim + d];
+    __syncwarp();
+    bool pr = false;
+    for (uint32_t j = lane; j < nr; j += 32) pr |= dot_ref_scalar(cv, rv + (size_t)j * a.rstride, dim) > ce.sim;
+    if (__ballot_sync(~0u, pr) == 0) {
+      for (uint32_t d = lane; d < dim; d += 32) rv[(size_t)nr * a.rstride + d] = cv[d];
+      if (lane == 0) sid[nr] = ce.node;  // sid[0 .. nr) is no longer read
+      ++nr;
+    }
+    __syncwarp();
+  }
+  for (uint32_t i = lane; i < nr; i += 32) list[i] = sid[i];
+  __syncwarp();
+  return nr;
+}
+
+// The reverse edges of the chunk: for each (layer, neighbour) that received
+// any, append the chunk's nodes in order, shrinking whenever the list
+// exceeds its cap (hnsw.zig:908-923). One warp per (layer, neighbour).
+__global__ void hnsw_commit_reverse(CommitArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const uint32_t dim = a.g.dim, dimp = (dim + 3u) & ~3u, n = a.g.n;
+  float* base = reinterpret_cast<float*>(sm) + (size_t)wib * a.warp_smem_floats;
+  float* xr = base;
+  float* cv = xr + dimp;
+  float* rv = cv + dimp;
+  float* ss = rv + (size_t)2 * kMaxM * a.rstride;
+  uint32_t* sid = reinterpret_cast<uint32_t*>(ss + kListPad);
+  Ent* so = reinterpret_cast<Ent*>(sid + kListPad);  // 8-byte aligned: every piece before is even
+  const uint32_t nent = *a.tcount;
+  const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+  for (uint32_t t = blockIdx.x * (blockDim.x >> 5) + wib; t < nent; t += warps) {
+    const uint32_t key = a.tlist[t];
+    const uint32_t L = key / n, r = key - L * n, cap = a.g.cap[L];
+    uint32_t* list = a.g.ids[L] + (size_t)r * (cap + 1);
+    uint32_t len = a.g.len[L][r];
+    for (uint32_t d = lane; d < dim; d += 32) xr[d] = a.x[(size_t)r * dim + d];
+    const uint32_t mw = lane < kMaskWords ? a.mask[(size_t)key * kMaskWords + lane] : 0u;
+    __syncwarp();
+    for (uint32_t w = 0; w < kMaskWords; ++w) {
+      uint32_t bits = __shfl_sync(~0u, mw, w);
+      while (bits) {
+        const uint32_t b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        if (lane == 0) list[len] = a.q_base + w * 32 + b;
+        ++len;
+        __syncwarp();
+        if (len > cap) len = shrink_list(a, list, len, cap, xr, cv, rv, ss, sid, so);
+      }
+    }
+    if (lane < kMaskWords) a.mask[(size_t)key * kMaskWords + lane] = 0u;
+    if (lane == 0) {
+      a.touched[key] = 0u;
+      a.g.len[L][r] = len;
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// freeze to CSR (hnsw.zig:427-462)
+// ---------------------------------------------------------------------------
+
+// offsets[i + 1] = offsets[i] + len[i]: one CTA, 1024 threads, sequential
+// blocks of 1024 nodes.
+__global__ void __launch_bounds__(1024) hnsw_offsets_kernel(const uint32_t* len, uint32_t n, uint32_t* offsets) {
+  __shared__ uint32_t wsum[32];
+  __shared__ uint32_t carry;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    carry = 0;
+    offsets[0] = 0;
+  }
+  __syncthreads();
+  for (uint32_t base = 0; base < n; base += 1024) {
+    const uint32_t i = base + tid;
+    const uint32_t v = i < n ? len[i] : 0u;
+    uint32_t s = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(~0u, s, o);
+      if (lane >= (uint32_t)o) s += y;
+    }
+    if (lane == 31) wsum[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t w = wsum[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(~0u, w, o);
+        if (lane >= (uint32_t)o) w += y;
+      }
+      wsum[lane] = w;
+    }
+    __syncthreads();
+    const uint32_t incl = carry + (warp ? wsum[warp - 1] : 0u) + s;
+    if (i < n) offsets[i + 1] = incl;
+    __syncthreads();
+    if (tid == 1023) carry = incl;
+    __syncthreads();
+  }
+}
+
+__global__ void hnsw_gather_kernel(const uint32_t* ids, const uint32_t* len, uint32_t n, uint32_t stride,
+                                   const uint32_t* offsets, uint32_t* out) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t node = (uint32_t)(t / stride), j = (uint32_t)(t % stride);
+  if (node < n && j < len[node]) out[offsets[node] + j] = ids[(size_t)node * stride + j];
+}
+
+// vec.normalizeRowsInPlace: one warp per row
+__global__ void normalize_rows_kernel(float* x, uint64_t n_rows, uint32_t dim) {
+  const uint64_t row = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  float* v = x + row * dim;
+  float ns = 0.f;
+  if (lane == 0) ns = dot_ref_scalar(v, v, dim);
+  ns = __shfl_sync(~0u, ns, 0);
+  if (ns == 0.0f) return;
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ns));
+  for (uint32_t d = lane; d < dim; d += 32) v[d] = __fmul_rn(v[d], inv);
+}
+
+// pickLevel (hnsw.zig:949-956)
+uint8_t pick_level(Xoshiro256pp& r, float m_l) {
+  const float u = 1.0f - r.unit_f32();
+  const float lvl = std::floor(-std::log(u) * m_l);
+  if (lvl < 0.0f) return 0;
+  if (lvl > 31.0f) return 31;
+  return (uint8_t)lvl;
+}
+
+struct DevAllocs {
+  std::vector<void*> ptrs;
+  ~DevAllocs() {
+    for (void* p : ptrs) cudaFree(p);
+  }
+  template <class T>
+  cudaError_t get(T** p, size_t bytes) {
+    void* v = nullptr;
+    const cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e == cudaSuccess) ptrs.push_back(v);
+    *p = static_cast<T*>(v);
+    return e;
+  }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+struct HnswGraphHost {
+  uint32_t n = 0, dim = 0, entry_point = 0, max_level = 0;
+  float device_ms = 0.f;
+  uint64_t launches = 0;
+  std::vector<uint8_t> levels;
+  std::vector<std::vector<uint32_t>> offsets, nbrs;
+};
+
+int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim, uint64_t seed, uint32_t ef,
+                      uint32_t m, uint32_t n_threads, HnswGraphHost* out) {
+  if (dim == 0 || n_floats % dim) return fail(c, MVR_E_DIM_MISMATCH, "hnsw.build: centroids.len % dim != 0");
+  const uint64_t n64 = n_floats / dim;
+  if (n64 == 0) return fail(c, MVR_E_EMPTY_CORPUS, "hnsw.build: no centroids");
+  if (n64 > (1ull << 27) || m == 0 || m > kMaxM || ef == 0 || ef > kMaxEf || dim > kMaxDim)
+    return fail(c, MVR_E_INVALID_ARGUMENT, "hnsw.build: unsupported n, m, ef_construction or dim");
+  if ((dim & 3u) == 0 && (reinterpret_cast<uintptr_t>(d_x) & 15u))
+    return fail(c, MVR_E_INVALID_ARGUMENT, "hnsw.build: centroids must be 16-byte aligned");
+  const uint32_t n = (uint32_t)n64;
+  const uint32_t dimp = (dim + 3u) & ~3u;
+  cudaStream_t st = c->stream;
+
+  // the plan kernel's shared memory
+  PlanLayout lay{};
+  {
+    uint32_t off = 0;
+    auto take = [&](uint32_t bytes) {
+      const uint32_t o = off;
+      off = (off + bytes + 15u) & ~15u;
+      return o;
+    };
+    lay.nwords = (n + 31) / 32;
+    lay.rstride = dim + 1;
+    lay.qv = take(dimp * 4);
+    lay.w0 = take(ef * 8);
+    lay.w1 = take(ef * 8);
+    lay.vis = take(lay.nwords * 4);
+    lay.cn = take(64 * 4);
+    lay.cs = take(64 * 4);
+    lay.as = take(64 * 8);
+    lay.ev = take(64 * 8);
+    lay.ties = take(kTieCap * 4);
+    lay.rv = take(kMaxM * lay.rstride * 4);
+    lay.rid = take(kMaxM * 4);
+    lay.cv = take(dimp * 4);
+    lay.bytes = off;
+  }
+  if (lay.bytes > kSmemLimit)
+    return fail(c, MVR_E_INVALID_ARGUMENT, "hnsw.build: search state exceeds one CTA's shared memory");
+  // the reverse-commit kernel's shared memory per warp
+  const uint32_t rstride = dim + 1;
+  const uint32_t warp_floats = 2 * dimp + 2 * kMaxM * rstride + 2 * kListPad + 2 * kMaxList;
+  const uint32_t warp_bytes = ((warp_floats * 4 + 15u) & ~15u);
+  uint32_t commit_warps = 4;
+  while (commit_warps > 1 && (size_t)commit_warps * warp_bytes > kSmemLimit) --commit_warps;
+  if ((size_t)warp_bytes > kSmemLimit) return fail(c, MVR_E_INVALID_ARGUMENT, "hnsw.build: dim too large");
+
+  // levels, in the reference's draw order (levels[0] first, then node order)
+  std::vector<uint8_t> levels(n);
+  Xoshiro256pp rng(seed);
+  const float m_l = 1.0f / std::log((float)m);
+  uint32_t top_level = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    levels[i] = pick_level(rng, m_l);
+    top_level = std::max<uint32_t>(top_level, levels[i]);
+  }
+  const uint32_t layers = top_level + 1;
+
+  DevAllocs al;
+  DevGraph g{};
+  g.n = n;
+  g.dim = dim;
+  g.m = m;
+  for (uint32_t L = 0; L < layers; ++L) {
+    g.cap[L] = L == 0 ? 2 * m : m;
+    MVR_CUDA(c, al.get(&g.ids[L], (size_t)n * (g.cap[L] + 1) * 4));
+    MVR_CUDA(c, al.get(&g.len[L], (size_t)n * 4));
+    MVR_CUDA(c, cudaMemsetAsync(g.len[L], 0, (size_t)n * 4, st));
+  }
+  uint8_t* d_levels = nullptr;
+  uint32_t *d_chosen = nullptr, *d_nchosen = nullptr, *d_mask = nullptr, *d_touched = nullptr, *d_tlist = nullptr,
+           *d_small = nullptr;
+  MVR_CUDA(c, al.get(&d_levels, n));
+  MVR_CUDA(c, al.get(&d_chosen, (size_t)kChunk * kMaxLayers * kMaxM * 4));
+  MVR_CUDA(c, al.get(&d_nchosen, (size_t)kChunk * kMaxLayers * 4));
+  MVR_CUDA(c, al.get(&d_mask, (size_t)layers * n * kMaskWords * 4));
+  MVR_CUDA(c, al.get(&d_touched, (size_t)layers * n * 4));
+  const size_t tl_cap = (size_t)kChunk * kMaxM * layers;
+  MVR_CUDA(c, al.get(&d_tlist, tl_cap * 4));
+  MVR_CUDA(c, al.get(&d_small, 64));  // [0] tcount, [1] status
+  MVR_CUDA(c, cudaMemsetAsync(d_mask, 0, (size_t)layers * n * kMaskWords * 4, st));
+  MVR_CUDA(c, cudaMemsetAsync(d_touched, 0, (size_t)layers * n * 4, st));
+  MVR_CUDA(c, cudaMemsetAsync(d_small, 0, 64, st));
+  MVR_CUDA(c, cudaMemcpyAsync(d_levels, levels.data(), n, cudaMemcpyHostToDevice, st));
+  MVR_CUDA(c, cudaFuncSetAttribute(hnsw_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.bytes));
+  MVR_CUDA(c, cudaFuncSetAttribute(hnsw_commit_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)(commit_warps * warp_bytes)));
+
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  MVR_CUDA(c, cudaEventCreate(&e0));
+  MVR_CUDA(c, cudaEventCreate(&e1));
+  struct EvGuard {
+    cudaEvent_t a, b;
+    ~EvGuard() {
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+    }
+  } evg{e0, e1};
+  MVR_CUDA(c, cudaEventRecord(e0, st));
+
+  uint64_t launches = 0;
+  uint32_t entry = 0, max_level = levels[0];
+  const uint32_t commit_grid = (uint32_t)std::max(1, c->sm_count) * 4;
+  for (uint32_t q_base = 1; q_base < n;) {
+    const uint32_t csz = n_threads <= 1 ? 1u : std::min(kChunk, q_base);
+    const uint32_t q_end = (uint32_t)std::min<uint64_t>((uint64_t)q_base + csz, n);
+    const uint32_t len = q_end - q_base;
+    PlanArgs pa{};
+    pa.g = g;
+    pa.lay = lay;
+    pa.x = d_x;
+    pa.levels = d_levels;
+    pa.q_base = q_base;
+    pa.snap_entry = entry;
+    pa.snap_max = max_level;
+    pa.ef = ef;
+    pa.chosen = d_chosen;
+    pa.n_chosen = d_nchosen;
+    pa.status = d_small + 1;
+    hnsw_plan_kernel<<<len, kPlanThreads, lay.bytes, st>>>(pa);
+    CommitArgs ca{};
+    ca.g = g;
+    ca.x = d_x;
+    ca.levels = d_levels;
+    ca.q_base = q_base;
+    ca.chunk_len = len;
+    ca.snap_max = max_level;
+    ca.chosen = d_chosen;
+    ca.n_chosen = d_nchosen;
+    ca.mask = d_mask;
+    ca.touched = d_touched;
+    ca.tlist = d_tlist;
+    ca.tcount = d_small;
+    ca.warp_smem_floats = warp_bytes / 4;
+    ca.rstride = rstride;
+    MVR_CUDA(c, cudaMemsetAsync(d_small, 0, 4, st));
+    hnsw_commit_own<<<len, 32, 0, st>>>(ca);
+    hnsw_commit_reverse<<<commit_grid, commit_warps * 32, commit_warps * warp_bytes, st>>>(ca);
+    launches += 3;
+    MVR_CUDA(c, cudaGetLastError());
+    for (uint32_t i = q_base; i < q_end; ++i)
+      if (levels[i] > max_level) {
+        max_level = levels[i];
+        entry = i;
+      }
+    q_base = q_end;
+  }
+
+  // freeze
+  std::vector<uint32_t*> d_off(layers), d_nb(layers);
+  for (uint32_t L = 0; L < layers && L <= max_level; ++L) {
+    MVR_CUDA(c, al.get(&d_off[L], ((size_t)n + 1) * 4));
+    hnsw_offsets_kernel<<<1, 1024, 0, st>>>(g.len[L], n, d_off[L]);
+    ++launches;
+  }
+  MVR_CUDA(c, cudaGetLastError());
+  std::vector<uint32_t> totals(layers, 0);
+  for (uint32_t L = 0; L <= max_level; ++L)
+    MVR_CUDA(c, cudaMemcpyAsync(&totals[L], d_off[L] + n, 4, cudaMemcpyDeviceToHost, st));
+  uint32_t hstatus = 0;
+  MVR_CUDA(c, cudaMemcpyAsync(&hstatus, d_small + 1, 4, cudaMemcpyDeviceToHost, st));
+  MVR_CUDA(c, cudaStreamSynchronize(st));
+  for (uint32_t L = 0; L <= max_level; ++L) {
+    MVR_CUDA(c, al.get(&d_nb[L], (size_t)totals[L] * 4));
+    const uint32_t stride = g.cap[L] + 1;
+    const uint64_t threads = (uint64_t)n * stride;
+    hnsw_gather_kernel<<<(uint32_t)((threads + 255) / 256), 256, 0, st>>>(g.ids[L], g.len[L], n, stride, d_off[L],
+                                                                         d_nb[L]);
+    ++launches;
+  }
+  MVR_CUDA(c, cudaGetLastError());
+  MVR_CUDA(c, cudaEventRecord(e1, st));
+  if (hstatus & kErrTies) return fail(c, MVR_E_DEVICE_LIMIT, "hnsw.build: more than 512 exact ties at the beam minimum");
+  if (hstatus & kErrLoop) return fail(c, MVR_E_DEVICE_LIMIT, "hnsw.build: search did not terminate");
+
+  out->n = n;
+  out->dim = dim;
+  out->entry_point = entry;
+  out->max_level = max_level;
+  out->levels = std::move(levels);
+  out->offsets.assign(max_level + 1, {});
+  out->nbrs.assign(max_level + 1, {});
+  for (uint32_t L = 0; L <= max_level; ++L) {
+    out->offsets[L].resize((size_t)n + 1);
+    out->nbrs[L].resize(std::max<uint32_t>(totals[L], 1));
+    MVR_TRY(d2h_staged(c, out->offsets[L].data(), d_off[L], ((size_t)n + 1) * 4));
+    MVR_TRY(d2h_staged(c, out->nbrs[L].data(), d_nb[L], (size_t)totals[L] * 4));
+    out->nbrs[L].resize(totals[L]);
+  }
+  MVR_CUDA(c, cudaEventSynchronize(e1));
+  MVR_CUDA(c, cudaEventElapsedTime(&out->device_ms, e0, e1));
+  out->launches = launches;
+  return MVR_OK;
+}
+
+int normalize_rows_device(Ctx* c, float* d, uint64_t n_floats, uint32_t dim) {
+  if (dim == 0) return fail(c, MVR_E_EMPTY_INPUT, "normalizeRowsInPlace: dim 0");
+  if (n_floats % dim) return fail(c, MVR_E_LENGTH_MISMATCH, "normalizeRowsInPlace: len % dim != 0");
+  const uint64_t rows = n_floats / dim;
+  if (rows == 0) return MVR_OK;
+  const uint64_t threads = rows * 32;
+  normalize_rows_kernel<<<(uint32_t)((threads + 255) / 256), 256, 0, c->stream>>>(d, rows, dim);
+  MVR_CUDA(c, cudaGetLastError());
+  return MVR_OK;
+}
+
+}  // namespace mvr
+
+struct mvr_hnsw {
+  mvr::HnswGraphHost g;
+};
+
+extern "C" {
+
+int mvr_hnsw_build_device(mvr_ctx* ctx, const float* d_centroids, uint64_t n_floats, uint32_t dim, uint64_t seed,
+                          uint32_t ef_construction, uint32_t m, uint32_t n_threads, mvr_hnsw** out) {
+  if (!ctx || !out || (!d_centroids && n_floats)) return MVR_E_INVALID_ARGUMENT;
+  *out = nullptr;
+  mvr::Ctx* c = &ctx->impl;
+  mvr_hnsw* h = new (std::nothrow) mvr_hnsw;
+  if (!h) return mvr::fail(c, MVR_E_OUT_OF_MEMORY, "hnsw.build: host allocation");
+  const int s = mvr::hnsw_build_device(c, d_centroids, n_floats, dim, seed, ef_construction, m, n_threads, &h->g);
+  if (s != MVR_OK) {
+    delete h;
+    return s;
+  }
+  *out = h;
+  return MVR_OK;
+}
+
+int mvr_hnsw_build(mvr_ctx* ctx, const float* centroids, uint64_t n_floats, uint32_t dim, uint64_t seed,
+                   uint32_t ef_construction, uint32_t m, uint32_t n_threads, mvr_hnsw** out) {
+  if (!ctx || !out || (!centroids && n_floats)) return MVR_E_INVALID_ARGUMENT;
+  *out = nullptr;
+  mvr::Ctx* c = &ctx->impl;
+  if (dim == 0 || n_floats % dim) return mvr::fail(c, MVR_E_DIM_MISMATCH, "hnsw.build: centroids.len % dim != 0");
+  if (n_floats == 0) return mvr::fail(c, MVR_E_EMPTY_CORPUS, "hnsw.build: no centroids");
+  float* d = nullptr;
+  MVR_CUDA(c, cudaMalloc(&d, n_floats * 4));
+  struct Free {
+    float* p;
+    ~Free() { cudaFree(p); }
+  } fr{d};
+  MVR_TRY(mvr::h2d_staged(c, d, centroids, n_floats * 4));
+  return mvr_hnsw_build_device(ctx, d, n_floats, dim, seed, ef_construction, m, n_threads, out);
+}
+
+void mvr_hnsw_info(const mvr_hnsw* h, uint32_t* n, uint32_t* entry_point, uint32_t* max_level, float* device_ms,
+                   uint64_t* kernel_launches) {
+  if (!h) return;
+  if (n) *n = h->g.n;
+  if (entry_point) *entry_point = h->g.entry_point;
+  if (max_level) *max_level = h->g.max_level;
+  if (device_ms) *device_ms = h->g.device_ms;
+  if (kernel_launches) *kernel_launches = h->g.launches;
+}
+
+const uint8_t* mvr_hnsw_node_levels(const mvr_hnsw* h) { return h ? h->g.levels.data() : nullptr; }
+
+const uint32_t* mvr_hnsw_layer_offsets(const mvr_hnsw* h, uint32_t layer) {
+  if (!h || layer > h->g.max_level) return nullptr;
+  return h->g.offsets[layer].data();
+}
+
+const uint32_t* mvr_hnsw_layer_neighbours(const mvr_hnsw* h, uint32_t layer, uint64_t* count) {
+  if (!h || layer > h->g.max_level) {
+    if (count) *count = 0;
+    return nullptr;
+  }
+  if (count) *count = h->g.nbrs[layer].size();
+  return h->g.nbrs[layer].data();
+}
+
+void mvr_hnsw_free(mvr_hnsw* h) { delete h; }
+
+int mvr_normalize_rows_device(mvr_ctx* ctx, float* d_rows, uint64_t n_floats, uint32_t dim) {
+  if (!ctx || (!d_rows && n_floats)) return MVR_E_INVALID_ARGUMENT;
+  return mvr::normalize_rows_device(&ctx->impl, d_rows, n_floats, dim);
+}
+
+int mvr_normalize_rows(mvr_ctx* ctx, float* rows, uint64_t n_floats, uint32_t dim) {
+  if (!ctx || (!rows && n_floats)) return MVR_E_INVALID_ARGUMENT;
+  mvr::Ctx* c = &ctx->impl;
+  if (dim == 0) return mvr::fail(c, MVR_E_EMPTY_INPUT, "normalizeRowsInPlace: dim 0");
+  if (n_floats % dim) return mvr::fail(c, MVR_E_LENGTH_MISMATCH, "normalizeRowsInPlace: len % dim != 0");
+  if (n_floats == 0) return MVR_OK;
+  float* d = nullptr;
+  MVR_CUDA(c, cudaMalloc(&d, n_floats * 4));
+  struct Free {
+    float* p;
+    ~Free() { cudaFree(p); }
+  } fr{d};
+  MVR_TRY(mvr::h2d_staged(c, d, rows, n_floats * 4));
+  MVR_TRY(mvr::normalize_rows_device(c, d, n_floats, dim));
+  MVR_TRY(mvr::d2h_staged(c, rows, d, n_floats * 4));
+  MVR_CUDA(c, cudaStreamSynchronize(c->stream));
+  return MVR_OK;
+}
+
+}  // extern "C"

@@ -168,6 +168,7 @@ const char* mvr_status_name(int s) {
     case MVR_E_TIMEOUT: return "Timeout";
     case MVR_E_INVALID_ARGUMENT: return "InvalidArgument";
     case MVR_E_NO_DEVICE: return "NoDevice";
+    case MVR_E_DEVICE_LIMIT: return "DeviceLimit";
     default: return "Unknown";
   }
 }

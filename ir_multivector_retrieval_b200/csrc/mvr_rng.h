@@ -88,6 +88,25 @@ struct Xoshiro256pp {
     std::memcpy(&d, &bits, 8);
     return d;
   }
+  // Random.float(f32) (Zig std): 23 random mantissa bits from the draw's low
+  // bits, exponent -1 - (leading zeros of the draw), extended by further
+  // draws when the top 41 bits are all zero.
+  float unit_f32() {
+    const uint64_t r = next();
+    uint32_t z = (uint32_t)lz(r);
+    if (z >= 41) {
+      z = 41 + (uint32_t)lz(next());
+      if (z == 41 + 64) {
+        const uint32_t x = (uint32_t)next() | 0x7FFu;
+        z += (uint32_t)__builtin_clz(x);
+      }
+    }
+    const uint32_t bits = ((126u - z) << 23) | ((uint32_t)r & 0x7FFFFFu);
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+  }
 };
+
 
 }  // namespace mvr

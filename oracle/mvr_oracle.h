@@ -116,6 +116,32 @@ int orc_refine(const float* centroids, uint32_t dim, uint32_t pq_m,
                const float* table, uint64_t table_len, const float* query,
                uint64_t query_len, uint32_t n_q, uint32_t doc_id, float* score);
 
+
+/* ---- HNSW over the centroids (src/index/hnsw.zig), hnsw_oracle.c ---- */
+typedef struct orc_hnsw orc_hnsw;
+typedef struct orc_hnsw_stats {
+  uint64_t searches, expansions, sims, accepted, heur_examined, heur_dots;
+} orc_hnsw_stats;
+/* hnsw.build: n_threads <= 1 the serial path, >= 2 the chunked
+ * deferred-commit path (identical for every count >= 2); `workers` host
+ * threads plan each chunk (any count gives the same graph). */
+int orc_hnsw_build(const float* centroids, uint64_t n_floats, uint32_t dim, uint64_t seed, uint32_t ef_c,
+                   uint32_t m, uint32_t n_threads, uint32_t workers, orc_hnsw** out);
+void orc_hnsw_free(orc_hnsw* h);
+void orc_hnsw_info(const orc_hnsw* h, uint32_t* n, uint32_t* entry_point, uint32_t* max_level);
+void orc_hnsw_levels(const orc_hnsw* h, uint8_t* out);
+uint64_t orc_hnsw_layer_size(const orc_hnsw* h, uint32_t L);
+void orc_hnsw_layer(const orc_hnsw* h, uint32_t L, uint32_t* offsets, uint32_t* nbrs);
+void orc_hnsw_last_stats(orc_hnsw_stats* out);
+/* hnsw.search over a frozen per-layer CSR graph */
+int orc_hnsw_search_csr(const float* centroids, uint32_t n, uint32_t dim, uint32_t entry_point, uint32_t max_level,
+                        const uint32_t* const* offsets, const uint32_t* const* nbrs, const float* query,
+                        uint32_t k, uint32_t ef, uint32_t* out, uint32_t* written);
+int orc_hnsw_search(const orc_hnsw* h, const float* query, uint32_t k, uint32_t ef, uint32_t* out,
+                    uint32_t* written);
+/* vec.normalizeRowsInPlace */
+void orc_normalize_rows(float* v, uint64_t n_rows, uint32_t dim);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,7 +30,7 @@ class OracleError(Exception):
 
 
 def build(force: bool = False) -> Path:
-    srcs = [HERE / "mvr_oracle.c", HERE / "mvr_oracle.h", HERE.parent / "include" / "mvr.h"]
+    srcs = [HERE / "mvr_oracle.c", HERE / "hnsw_oracle.c", HERE / "mvr_oracle.h", HERE.parent / "include" / "mvr.h"]
     if force or not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB
@@ -339,3 +339,94 @@ def refine(centroids, dim: int, pq_m: int, doc_section: bytes, n_docs: int, doc_
                              _p(off), _p(_f32(norms)), _p(t), C.c_uint64(t.size), _p(q), C.c_uint64(q.size), n_q,
                              doc_id, C.byref(out)), "refine")
     return float(out.value)
+
+
+# ---- HNSW over the centroids (hnsw_oracle.c, src/index/hnsw.zig) ----
+
+@dataclass
+class HnswGraph:
+    """Frozen per-layer CSR graph, the reference's ``Hnsw`` (hnsw.zig:136-170)."""
+    n: int
+    dim: int
+    entry_point: int
+    max_level: int
+    node_levels: np.ndarray  # u8[n]
+    layer_offsets: list  # per layer u32[n + 1]
+    layer_neighbours: list  # per layer u32[offsets[-1]]
+
+
+class _HnswStats(C.Structure):
+    _fields_ = [(f, C.c_uint64) for f in ("searches", "expansions", "sims", "accepted", "heur_examined",
+                                            "heur_dots")]
+
+
+def hnsw_build(centroids, dim: int, seed: int, ef_construction: int = 1500, m: int = 32, n_threads: int = 2,
+               workers: int = 0) -> HnswGraph:
+    """hnsw.build (hnsw.zig:314-475) on already normalised centroids."""
+    import os
+    x = _f32(centroids)
+    lib = load()
+    lib.orc_hnsw_build.restype = C.c_int
+    lib.orc_hnsw_build.argtypes = [_P, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32,
+                                   C.c_uint32, C.POINTER(C.c_void_p)]
+    h = C.c_void_p()
+    w = workers or (os.cpu_count() or 1)
+    _check(lib.orc_hnsw_build(_p(x), C.c_uint64(x.size), dim, C.c_uint64(seed & (2**64 - 1)), ef_construction, m,
+                              n_threads, w, C.byref(h)), "hnsw_build")
+    try:
+        n, ep, ml = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        lib.orc_hnsw_info.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                      C.POINTER(C.c_uint32)]
+        lib.orc_hnsw_info(h, C.byref(n), C.byref(ep), C.byref(ml))
+        levels = np.zeros(n.value, dtype=np.uint8)
+        lib.orc_hnsw_levels.argtypes = [C.c_void_p, _P]
+        lib.orc_hnsw_levels(h, _p(levels))
+        lib.orc_hnsw_layer_size.restype = C.c_uint64
+        lib.orc_hnsw_layer_size.argtypes = [C.c_void_p, C.c_uint32]
+        lib.orc_hnsw_layer.argtypes = [C.c_void_p, C.c_uint32, _P, _P]
+        offs, nbrs = [], []
+        for L in range(ml.value + 1):
+            o = np.zeros(n.value + 1, dtype=np.uint32)
+            b = np.zeros(max(1, lib.orc_hnsw_layer_size(h, L)), dtype=np.uint32)
+            lib.orc_hnsw_layer(h, L, _p(o), _p(b))
+            offs.append(o)
+            nbrs.append(b[: int(o[-1])])
+        return HnswGraph(n.value, dim, ep.value, ml.value, levels, offs, nbrs)
+    finally:
+        lib.orc_hnsw_free.argtypes = [C.c_void_p]
+        lib.orc_hnsw_free(h)
+
+
+def hnsw_last_stats() -> dict:
+    st = _HnswStats()
+    lib = load()
+    lib.orc_hnsw_last_stats.argtypes = [C.c_void_p]
+    lib.orc_hnsw_last_stats(C.byref(st))
+    return {f: int(getattr(st, f)) for f, _ in _HnswStats._fields_}
+
+
+def hnsw_search(g: HnswGraph, centroids, query, k: int, ef: int) -> np.ndarray:
+    """hnsw.search (hnsw.zig:1117-1150): top-k node ids, most similar first."""
+    x, q = _f32(centroids), _f32(query)
+    lib = load()
+    offs = [np.ascontiguousarray(o, dtype=np.uint32) for o in g.layer_offsets]
+    nbrs = [np.ascontiguousarray(b if b.size else np.zeros(1, np.uint32), dtype=np.uint32)
+            for b in g.layer_neighbours]
+    po = (C.c_void_p * len(offs))(*[o.ctypes.data for o in offs])
+    pn = (C.c_void_p * len(nbrs))(*[b.ctypes.data for b in nbrs])
+    out = np.zeros(max(k, 1), dtype=np.uint32)
+    wr = C.c_uint32()
+    lib.orc_hnsw_search_csr.argtypes = [_P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p,
+                                        C.c_void_p, _P, C.c_uint32, C.c_uint32, _P, C.POINTER(C.c_uint32)]
+    _check(lib.orc_hnsw_search_csr(_p(x), g.n, g.dim, g.entry_point, g.max_level, po, pn, _p(q), k, ef, _p(out),
+                                   C.byref(wr)), "hnsw_search")
+    return out[: wr.value].copy()
+
+
+def normalize_rows(v, dim: int) -> np.ndarray:
+    """vec.normalizeRowsInPlace (vec.zig:185-253) on a copy."""
+    x = _f32(v).copy()
+    lib = load()
+    lib.orc_normalize_rows.argtypes = [_P, C.c_uint64, C.c_uint32]
+    lib.orc_normalize_rows(_p(x), C.c_uint64(x.size // dim), dim)
+    return x
