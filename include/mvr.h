@@ -508,7 +508,7 @@ typedef struct mvr_hnsw mvr_hnsw;
  * hnsw.zig:477-625); n_threads >= 2 its chunked deferred-commit path
  * (buildParallel, hnsw.zig:639-946), whose graph is the same for every
  * thread count >= 2, so the value only selects the path. Supported:
- * 1 <= m <= 32, 1 <= ef_construction <= 4096, dim <= 256, at most 2^27
+ * 1 <= m <= 32, 1 <= ef_construction <= 2048, dim <= 256, at most 2^27
  * centroids (MVR_E_INVALID_ARGUMENT otherwise). Equal similarities are
  * ordered by node id where the reference's heaps leave the order to their
  * layout. Errors: MVR_E_DIM_MISMATCH, MVR_E_EMPTY_CORPUS (the reference's

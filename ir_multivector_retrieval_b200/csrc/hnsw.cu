@@ -46,6 +46,12 @@
 //     minimum); anything lower never expands. Those ties are kept in a small
 //     list; all of W ranks above them, so the next expansion is the first
 //     unexpanded entry of W, else the tie with the smallest id.
+// Latency: each expansion is a chain of dependent steps (pick, neighbour list,
+// rows, similarities, acceptance, merge), so the kernel overlaps the global
+// reads of the likely next expansion (the next unexpanded entry of W) with
+// the current one: its neighbours' rows are copied into shared memory with
+// cp.async while the current expansion proceeds, and the list of the one
+// after it is prefetched into L1. A wrong guess costs only the copies.
 // Equal similarities: the reference's heaps order them by similarity alone,
 // so among exactly equal similarities its pop order follows the heap layout
 // of Zig's std.PriorityQueue; here they go by node id (the smaller id first
@@ -81,7 +87,7 @@ constexpr uint32_t kPlanThreads = 256;
 constexpr uint32_t kTieCap = 512;
 constexpr uint32_t kExpanded = 0x80000000u;
 constexpr uint32_t kMaskWords = kChunk / 32;    // one bit per node of a chunk
-constexpr uint32_t kMaxEf = 4096;
+constexpr uint32_t kMaxEf = 2048;  // beam entries per CTA (8 per thread in a merge)
 constexpr uint32_t kMaxDim = 256;
 constexpr size_t kSmemLimit = 226 * 1024;  // 227 KB per CTA less the static control block
 
@@ -162,8 +168,8 @@ __device__ __forceinline__ float dot_ref_scalar(const float* a, const float* b, 
 // ---------------------------------------------------------------------------
 
 struct PlanLayout {  // byte offsets into dynamic shared memory
-  uint32_t qv, w0, w1, vis, cn, cs, as, ev, ties, rv, rid, cv;
-  uint32_t nwords, rstride, bytes;
+  uint32_t qv, w, vis, cn, cs, cacc, as, apos, ev, ties, rv, rid, cv, stg;
+  uint32_t nwords, rstride, stage_slots, bytes;
 };
 
 struct PlanArgs {
@@ -178,9 +184,10 @@ struct PlanArgs {
 };
 
 struct PlanCtl {
-  uint32_t wn, hint, pop, done, nt, nev, newhint, cur, nr;
-  float tsim;
-  uint32_t bal[2], abal[2];
+  uint32_t wn, hint, newhint, pop, spec, spec2, done, nt, nev, p0, full, cur;
+  float tsim, newmin;
+  uint32_t bal[2];
+  uint32_t stg_node[2], stg_mask[2][2];
 };
 
 // greedySearchLayer (hnsw.zig:969-991), warp 0: the first strict maximum of
@@ -215,22 +222,83 @@ __device__ uint32_t greedy_layer(const PlanArgs& a, const float* qv, uint32_t L,
   return cur;
 }
 
-__global__ void __launch_bounds__(kPlanThreads) hnsw_plan_kernel(PlanArgs a) {
+// vec.dot(q, x) for dim 64 / 128 with every load of the row issued before
+// the first add (the reference's order: lane accumulators over the 4-wide
+// chunks in order, then ((a0 + a1) + a2) + a3).
+template <int D>
+__device__ __forceinline__ float dot_fixed(const float* qv, const float* __restrict__ xr) {
+  const float4* q4 = reinterpret_cast<const float4*>(qv);
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int h = 0; h < D / 64; ++h) {
+    float4 v[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) v[c] = x4[h * 16 + c];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const float4 y = q4[h * 16 + c];
+      a0 = __fadd_rn(a0, __fmul_rn(y.x, v[c].x));
+      a1 = __fadd_rn(a1, __fmul_rn(y.y, v[c].y));
+      a2 = __fadd_rn(a2, __fmul_rn(y.z, v[c].z));
+      a3 = __fadd_rn(a3, __fmul_rn(y.w, v[c].w));
+    }
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+}
+
+__device__ __forceinline__ float dot_row(const float* qv, const float* __restrict__ xr, uint32_t dim) {
+  if (dim == 64) return dot_fixed<64>(qv, xr);
+  if (dim == 128) return dot_fixed<128>(qv, xr);
+  return dot_ref(qv, xr, dim);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
+// Number of leading entries of W[lo, hi) for which pred holds (pred is true
+// on a prefix: W is sorted). Whole warp, 32-way steps.
+template <class Pred>
+__device__ __forceinline__ uint32_t warp_boundary(const Ent* W, uint32_t lo, uint32_t hi, Pred pred) {
+  const uint32_t lane = threadIdx.x & 31;
+  while (lo < hi) {
+    const uint32_t stride = (hi - lo + 31) / 32, idx = lo + lane * stride;
+    const uint32_t c = __popc(__ballot_sync(~0u, idx < hi && pred(W[idx])));
+    if (c == 0) break;
+    const uint32_t nhi = lo + c * stride;
+    lo = lo + (c - 1) * stride + 1;
+    hi = nhi < hi ? nhi : hi;
+  }
+  return lo;
+}
+
+constexpr uint32_t kTail = kMaxEf / kPlanThreads;  // beam entries per thread in a merge
+
+__global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ PlanCtl ctl;
   const PlanLayout& lay = a.lay;
   float* qv = reinterpret_cast<float*>(sm + lay.qv);
-  Ent* const wb0 = reinterpret_cast<Ent*>(sm + lay.w0);
-  Ent* const wb1 = reinterpret_cast<Ent*>(sm + lay.w1);
+  Ent* W = reinterpret_cast<Ent*>(sm + lay.w);
   uint32_t* vis = reinterpret_cast<uint32_t*>(sm + lay.vis);
   uint32_t* cn = reinterpret_cast<uint32_t*>(sm + lay.cn);
   float* cs = reinterpret_cast<float*>(sm + lay.cs);
+  uint32_t* cacc = reinterpret_cast<uint32_t*>(sm + lay.cacc);
   Ent* as = reinterpret_cast<Ent*>(sm + lay.as);
+  uint32_t* apos = reinterpret_cast<uint32_t*>(sm + lay.apos);
   Ent* ev = reinterpret_cast<Ent*>(sm + lay.ev);
   uint32_t* ties = reinterpret_cast<uint32_t*>(sm + lay.ties);
   float* rv = reinterpret_cast<float*>(sm + lay.rv);
   uint32_t* rid = reinterpret_cast<uint32_t*>(sm + lay.rid);
   float* cv = reinterpret_cast<float*>(sm + lay.cv);
+  float* stg = reinterpret_cast<float*>(sm + lay.stg);
 
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t qi = blockIdx.x, q = a.q_base + qi, dim = a.g.dim, ef = a.ef, m = a.g.m;
@@ -247,51 +315,94 @@ __global__ void __launch_bounds__(kPlanThreads) hnsw_plan_kernel(PlanArgs a) {
   }
   __syncthreads();
   const uint32_t top = a.snap_max < l_new ? a.snap_max : l_new;
-  uint32_t buf = 0;
 
   for (int Ls = (int)top; Ls >= 0; --Ls) {
     const uint32_t L = (uint32_t)Ls, cap = a.g.cap[L];
+    const uint32_t* ids = a.g.ids[L];
+    const uint32_t* lens = a.g.len[L];
     // ---- searchLayer from ctl.cur
     for (uint32_t i = tid; i < lay.nwords; i += blockDim.x) vis[i] = 0;
     __syncthreads();
     if (tid == 0) {
       const uint32_t e0 = ctl.cur;
-      (buf ? wb1 : wb0)[0] = Ent{dot_ref(qv, a.x + (size_t)e0 * dim, dim), e0};
+      W[0] = Ent{dot_ref(qv, a.x + (size_t)e0 * dim, dim), e0};
       vis[e0 >> 5] |= 1u << (e0 & 31);
       ctl.wn = 1;
       ctl.hint = 0;
       ctl.nt = 0;
       ctl.tsim = 0.f;
+      ctl.full = 0;
+      ctl.nev = 0;
+      ctl.stg_node[0] = ctl.stg_node[1] = 0xFFFFFFFFu;
     }
     __syncthreads();
     for (uint32_t it = 0;; ++it) {
-      Ent* W = buf ? wb1 : wb0;
-      const uint32_t wn = ctl.wn;
       if (it > a.g.n) {  // every node expands at most once
         if (tid == 0) atomicOr(a.status, kErrLoop);
         break;
       }
-      // the next expansion: first unexpanded entry of W, else the smallest tie
+      // ---- P1 (warp 0): the ties evicted by the last merge, then the next
+      // expansion (first unexpanded entry of W, else the smallest tie) and
+      // two guesses of the ones after it (the next unexpanded entries of W),
+      // which only steer prefetches
       if (warp == 0) {
-        uint32_t p = wn;
-        for (uint32_t base = ctl.hint; base < wn; base += 32) {
-          const uint32_t i = base + lane;
-          const bool un = i < wn && !(W[i].node & kExpanded);
-          const uint32_t b = __ballot_sync(~0u, un);
-          if (b) {
-            p = base + __ffs(b) - 1;
-            break;
+        const uint32_t wn = ctl.wn;
+        uint32_t nt = ctl.nt;
+        if (ctl.full) {
+          const float mn = ctl.newmin;
+          if (nt && ctl.tsim != mn) nt = 0;
+          const uint32_t nev = ctl.nev;
+          for (uint32_t base = 0; base < nev; base += 32) {
+            const uint32_t i = base + lane;
+            const bool t = i < nev && ev[i].sim == mn;
+            const uint32_t b = __ballot_sync(~0u, t);
+            if (t) {
+              const uint32_t slot = nt + __popc(b & lanemask_lt());
+              if (slot < kTieCap) ties[slot] = ev[i].node & ~kExpanded;
+            }
+            nt += __popc(b);
           }
+          if (nt > kTieCap) {
+            nt = kTieCap;
+            if (lane == 0) atomicOr(a.status, kErrTies);
+          }
+          __syncwarp();
+          if (lane == 0) {
+            ctl.tsim = mn;
+            ctl.full = 0;
+          }
+        }
+        // chunks of 32 entries from the hint: the first unexpanded entry, then
+        // up to two more chunks for the guesses
+        uint32_t p = wn, p2 = wn, p3 = wn, nf = 0, extra = 0;
+        for (uint32_t base = ctl.hint; base < wn && nf < 3; base += 32) {
+          const uint32_t i = base + lane;
+          uint32_t b = __ballot_sync(~0u, i < wn && !(W[i].node & kExpanded));
+          while (b && nf < 3) {
+            const uint32_t idx = base + __ffs(b) - 1;
+            if (nf == 0)
+              p = idx;
+            else if (nf == 1)
+              p2 = idx;
+            else
+              p3 = idx;
+            ++nf;
+            b &= b - 1;
+          }
+          if (nf && ++extra > 2) break;
         }
         if (p < wn) {
           if (lane == 0) {
-            ctl.pop = W[p].node;
-            W[p].node |= kExpanded;
+            const uint32_t pop = W[p].node;
+            W[p].node = pop | kExpanded;
+            ctl.pop = pop;
             ctl.hint = p;
+            ctl.spec = p2 < wn ? (W[p2].node & ~kExpanded) : 0xFFFFFFFFu;
+            ctl.spec2 = p3 < wn ? (W[p3].node & ~kExpanded) : 0xFFFFFFFFu;
+            ctl.nt = nt;
             ctl.done = 0;
           }
         } else {
-          const uint32_t nt = ctl.nt;
           uint32_t best = 0xFFFFFFFFu, bi = 0;
           for (uint32_t i = lane; i < nt; i += 32)
             if (ties[i] < best) {
@@ -305,9 +416,13 @@ __global__ void __launch_bounds__(kPlanThreads) hnsw_plan_kernel(PlanArgs a) {
               bi = oi;
             }
           }
+          __syncwarp();
           if (lane == 0) {
+            ctl.spec = 0xFFFFFFFFu;
+            ctl.spec2 = 0xFFFFFFFFu;
             if (nt == 0) {
               ctl.done = 1;
+              ctl.nt = 0;
             } else {
               ctl.pop = best;
               ties[bi] = ties[nt - 1];
@@ -319,143 +434,157 @@ __global__ void __launch_bounds__(kPlanThreads) hnsw_plan_kernel(PlanArgs a) {
       }
       __syncthreads();
       if (ctl.done) break;
-      const uint32_t c = ctl.pop;
-      // unvisited neighbours of c, in list order (lists hold <= 2M <= 64 at rest)
-      const uint32_t cnt = a.g.len[L][c];
+      const uint32_t c = ctl.pop, spec = ctl.spec, spec2 = ctl.spec2;
+      // ---- P2: the unvisited neighbours of c in list order (threads < 64;
+      // the count and the ids are read together). Warps 2-3 stage the rows of
+      // the guessed next expansion's unvisited neighbours into shared memory
+      // with asynchronous copies that complete during the next iteration (a
+      // wrong guess costs only the copies); warp 4 prefetches the list of the
+      // guess after it into L1.
+      const uint32_t sbuf = it & 1u;  // staged now; the previous iteration's is sbuf ^ 1
       uint32_t e = 0;
       bool fresh = false;
-      if (tid < cnt) {
-        e = a.g.ids[L][(size_t)c * (cap + 1) + tid];
-        const uint32_t bit = 1u << (e & 31);
-        fresh = !(atomicOr(&vis[e >> 5], bit) & bit);
-      }
-      if (warp < 2) {
+      if (tid < 64) {
+        const uint32_t cnt = lens[c];
+        if (tid <= cap) e = ids[(size_t)c * (cap + 1) + tid];
+        if (tid < cnt) {
+          const uint32_t bit = 1u << (e & 31);
+          fresh = !(atomicOr(&vis[e >> 5], bit) & bit);
+        }
         const uint32_t b = __ballot_sync(~0u, fresh);
         if (lane == 0) ctl.bal[warp] = b;
+      } else if (warp < 4) {
+        cp_async_wait_all();  // this thread's copies of the previous iteration
+        const uint32_t u = tid - 64;
+        bool staged = false;
+        if (spec != 0xFFFFFFFFu && u < lay.stage_slots) {
+          const uint32_t cnt2 = lens[spec];
+          const uint32_t v = u <= cap ? ids[(size_t)spec * (cap + 1) + u] : 0u;
+          if (u < cnt2 && !((vis[v >> 5] >> (v & 31)) & 1u)) {
+            const char* src = reinterpret_cast<const char*>(a.x + (size_t)v * dim);
+            char* dst = reinterpret_cast<char*>(stg + ((size_t)sbuf * lay.stage_slots + u) * dim);
+            for (uint32_t o = 0; o < dim * 4; o += 16) cp_async16(dst + o, src + o);
+            staged = true;
+          }
+        }
+        cp_async_commit();
+        const uint32_t b = __ballot_sync(~0u, staged);
+        if (lane == 0) ctl.stg_mask[sbuf][warp - 2] = b;
+        if (u == 0) ctl.stg_node[sbuf] = spec;
+      } else if (warp == 4) {
+        if (spec2 != 0xFFFFFFFFu) {
+          const uint32_t lines = ((cap + 1) * 4 + 127) / 128;
+          if (lane < lines) prefetch_l1(reinterpret_cast<const char*>(ids + (size_t)spec2 * (cap + 1)) + lane * 128);
+          if (lane == lines) prefetch_l1(lens + spec2);
+        }
       }
       __syncthreads();
       const uint32_t b0 = ctl.bal[0], b1 = ctl.bal[1];
       const uint32_t k = __popc(b0) + __popc(b1);
-      if (k == 0) continue;
+      // ---- P3: similarity of each fresh neighbour, by the thread that read
+      // it: from the staged row when the previous iteration guessed c
       if (fresh) {
         const uint32_t j = (warp == 0 ? 0u : (uint32_t)__popc(b0)) + __popc((warp == 0 ? b0 : b1) & lanemask_lt());
+        const uint32_t pb = sbuf ^ 1u;
+        const bool hit = ctl.stg_node[pb] == c && tid < lay.stage_slots && ((ctl.stg_mask[pb][tid >> 5] >> (tid & 31)) & 1u);
         cn[j] = e;
-        cs[j] = dot_ref(qv, a.x + (size_t)e * dim, dim);
-      }
-      __syncthreads();
-      // acceptance
-      bool acc = false;
-      if (tid < k) {
-        const float sj = cs[tid];
-        uint32_t lo = 0, hi = wn;
-        while (lo < hi) {
-          const uint32_t mid = (lo + hi) >> 1;
-          if (W[mid].sim >= sj)
-            lo = mid + 1;
-          else
-            hi = mid;
-        }
-        uint32_t cp = 0;
-        for (uint32_t i = 0; i < tid; ++i) cp += cs[i] >= sj ? 1u : 0u;
-        acc = lo + cp < ef;
-      }
-      if (warp < 2) {
-        const uint32_t b = __ballot_sync(~0u, acc);
-        if (lane == 0) ctl.abal[warp] = b;
-      }
-      __syncthreads();
-      const uint32_t a0 = ctl.abal[0], a1 = ctl.abal[1];
-      const uint32_t na = __popc(a0) + __popc(a1);
-      if (na == 0) continue;
-      if (acc) {  // rank among the accepted, in the beam's order
-        const Ent me{cs[tid], cn[tid]};
-        uint32_t r = 0;
-        for (uint32_t i = 0; i < k; ++i) {
-          const bool ai = i < 32 ? ((a0 >> i) & 1u) : ((a1 >> (i - 32)) & 1u);
-          if (ai && better(Ent{cs[i], cn[i]}, me)) ++r;
-        }
-        as[r] = me;
+        cs[j] = dot_row(qv, hit ? stg + ((size_t)pb * lay.stage_slots + tid) * dim : a.x + (size_t)e * dim, dim);
       }
       if (tid == 0) {
+        ctl.p0 = 0xFFFFFFFFu;
         ctl.newhint = 0xFFFFFFFFu;
         ctl.nev = 0;
       }
       __syncthreads();
-      // merge W and the accepted entries into the other buffer, first ef kept
-      Ent* Wn = buf ? wb0 : wb1;
-      const uint32_t total = wn + na, hint = ctl.hint;
-      for (uint32_t i = tid; i < total; i += blockDim.x) {
-        Ent xe;
-        uint32_t pos;
-        if (i < wn) {
-          xe = W[i];
-          uint32_t lo = 0, hi = na;
-          while (lo < hi) {
-            const uint32_t mid = (lo + hi) >> 1;
-            if (better(as[mid], xe))
-              lo = mid + 1;
-            else
-              hi = mid;
-          }
-          pos = i + lo;
-          if (i == hint) atomicMin(&ctl.newhint, pos);
-        } else {
-          const uint32_t r = i - wn;
-          xe = as[r];
-          uint32_t lo = 0, hi = wn;
-          while (lo < hi) {
-            const uint32_t mid = (lo + hi) >> 1;
-            if (better(W[mid], xe))
-              lo = mid + 1;
-            else
-              hi = mid;
-          }
-          pos = r + lo;
-          if (r == 0) atomicMin(&ctl.newhint, pos);
-        }
-        if (pos < ef) {
-          Wn[pos] = xe;
-        } else if (!(xe.node & kExpanded)) {  // at most na <= 64 leave
-          const uint32_t v = atomicAdd(&ctl.nev, 1u);
-          ev[v] = xe;
+      if (k == 0) continue;
+      // ---- P4: acceptance of candidate j: fewer than ef of W and the
+      // candidates before j are at least as similar. One warp per candidate;
+      // the count in W by 32-way steps (W's similarities never increase).
+      const uint32_t wn = ctl.wn;
+      for (uint32_t j = warp; j < k; j += kPlanThreads / 32) {
+        const float sj = cs[j];
+        const uint32_t inw = warp_boundary(W, 0, wn, [sj](Ent w) { return w.sim >= sj; });
+        const uint32_t cp = __popc(__ballot_sync(~0u, lane < j && cs[lane] >= sj)) +
+                            __popc(__ballot_sync(~0u, lane + 32 < j && cs[lane + 32] >= sj));
+        if (lane == 0) cacc[j] = (inw + cp < ef) ? 1u : 0u;
+      }
+      __syncthreads();
+      const uint32_t a0 = __ballot_sync(~0u, lane < k && cacc[lane]);
+      const uint32_t a1 = __ballot_sync(~0u, lane + 32 < k && cacc[lane + 32]);
+      const uint32_t na = __popc(a0) + __popc(a1);
+      if (na == 0) continue;
+      // ---- P5: rank among the accepted (beam order) and the place in W,
+      // one warp per accepted candidate
+      for (uint32_t j = warp; j < k; j += kPlanThreads / 32) {
+        if (!((j < 32 ? (a0 >> j) : (a1 >> (j - 32))) & 1u)) continue;
+        const Ent me{cs[j], cn[j]};
+        const uint32_t r =
+            __popc(__ballot_sync(~0u, ((a0 >> lane) & 1u) && better(Ent{cs[lane], cn[lane]}, me))) +
+            __popc(__ballot_sync(~0u, ((a1 >> lane) & 1u) && better(Ent{cs[lane + 32], cn[lane + 32]}, me)));
+        const uint32_t pw = warp_boundary(W, 0, wn, [me](Ent w) { return better(w, me); });
+        if (lane == 0) {
+          as[r] = me;
+          apos[r] = r + pw;
+          atomicMin(&ctl.p0, pw);
+          if (r == 0) atomicMin(&ctl.newhint, pw);
         }
       }
       __syncthreads();
-      if (warp == 0 && total > ef) {  // the beam is full: keep the live ties
-        const float mn = Wn[ef - 1].sim;
-        uint32_t nt = ctl.nt;
-        if (nt && ctl.tsim != mn) nt = 0;
-        const uint32_t nev = ctl.nev;
-        for (uint32_t base = 0; base < nev; base += 32) {
-          const uint32_t i = base + lane;
-          const bool t = i < nev && ev[i].sim == mn;
-          const uint32_t b = __ballot_sync(~0u, t);
-          if (t) {
-            const uint32_t slot = nt + __popc(b & lanemask_lt());
-            if (slot < kTieCap) ties[slot] = ev[i].node & ~kExpanded;
+      // ---- P6/P7: merge in place: entries of W from p0 on move down by the
+      // number of accepted entries ahead of them; the first ef are kept.
+      // Every move is read before any is written.
+      const uint32_t p0 = ctl.p0, hint = ctl.hint, total = wn + na;
+      Ent te[kTail];
+      uint32_t tp[kTail];
+#pragma unroll
+      for (uint32_t t = 0; t < kTail; ++t) {
+        const uint32_t i = p0 + tid + t * kPlanThreads;
+        tp[t] = 0xFFFFFFFFu;
+        if (i < wn) {
+          te[t] = W[i];
+          uint32_t lo = 0, hi = na;
+          while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (better(as[mid], te[t]))
+              lo = mid + 1;
+            else
+              hi = mid;
           }
-          nt += __popc(b);
+          tp[t] = i + lo;
+          if (i == hint) atomicMin(&ctl.newhint, tp[t]);
         }
-        if (nt > kTieCap) {
-          nt = kTieCap;
-          if (lane == 0) atomicOr(a.status, kErrTies);
+      }
+      __syncthreads();
+#pragma unroll
+      for (uint32_t t = 0; t < kTail; ++t) {
+        if (tp[t] == 0xFFFFFFFFu) continue;
+        if (tp[t] < ef) {
+          W[tp[t]] = te[t];
+          if (tp[t] == ef - 1) ctl.newmin = te[t].sim;
+        } else if (!(te[t].node & kExpanded)) {  // at most na <= 64 leave
+          ev[atomicAdd(&ctl.nev, 1u)] = te[t];
         }
-        if (lane == 0) {
-          ctl.nt = nt;
-          ctl.tsim = mn;
+      }
+      if (tid < na) {
+        const uint32_t np = apos[tid];
+        if (np < ef) {
+          W[np] = as[tid];
+          if (np == ef - 1) ctl.newmin = as[tid].sim;
+        } else {
+          ev[atomicAdd(&ctl.nev, 1u)] = as[tid];
         }
       }
       if (tid == 0) {
         const uint32_t nw = total < ef ? total : ef;
         ctl.wn = nw;
-        ctl.hint = ctl.newhint < nw ? ctl.newhint : nw;
+        ctl.hint = hint < p0 ? hint : (ctl.newhint < nw ? ctl.newhint : nw);
+        ctl.full = total > ef ? 1u : 0u;  // the next P1 keeps the live ties
       }
-      buf ^= 1u;
       __syncthreads();
     }
+    cp_async_wait_all();
     __syncthreads();
     // ---- the beam, best first, is W[0 .. wn); next layer starts at its best
-    const Ent* W = buf ? wb1 : wb0;
     const uint32_t wn = ctl.wn;
     // ---- selectHeuristic (warp 0): keep a candidate unless a chosen
     // neighbour is strictly more similar to it than the query is
@@ -734,17 +863,21 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
     lay.nwords = (n + 31) / 32;
     lay.rstride = dim + 1;
     lay.qv = take(dimp * 4);
-    lay.w0 = take(ef * 8);
-    lay.w1 = take(ef * 8);
+    lay.w = take(ef * 8);
     lay.vis = take(lay.nwords * 4);
     lay.cn = take(64 * 4);
     lay.cs = take(64 * 4);
+    lay.cacc = take(64 * 4);
     lay.as = take(64 * 8);
+    lay.apos = take(64 * 4);
     lay.ev = take(64 * 8);
     lay.ties = take(kTieCap * 4);
     lay.rv = take(kMaxM * lay.rstride * 4);
     lay.rid = take(kMaxM * 4);
     lay.cv = take(dimp * 4);
+    // staged rows of the guessed next expansion: 16 KB per buffer, whole rows
+    lay.stage_slots = (dim & 3u) == 0 ? std::min<uint32_t>(64, 16384 / (dim * 4)) : 0u;
+    lay.stg = take(2 * lay.stage_slots * dim * 4);
     lay.bytes = off;
   }
   if (lay.bytes > kSmemLimit)
@@ -795,6 +928,10 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
   MVR_CUDA(c, cudaMemsetAsync(d_small, 0, 64, st));
   MVR_CUDA(c, cudaMemcpyAsync(d_levels, levels.data(), n, cudaMemcpyHostToDevice, st));
   MVR_CUDA(c, cudaFuncSetAttribute(hnsw_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.bytes));
+  {  // shared memory for two CTAs per SM; the rest of the unified L1 stays cache
+    const int pct = (int)std::min<size_t>(100, (2 * (lay.bytes + 1024) * 100 + 228 * 1024 - 1) / (228 * 1024));
+    MVR_CUDA(c, cudaFuncSetAttribute(hnsw_plan_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, pct));
+  }
   MVR_CUDA(c, cudaFuncSetAttribute(hnsw_commit_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)(commit_warps * warp_bytes)));
 
