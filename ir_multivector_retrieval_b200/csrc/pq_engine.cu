@@ -1441,7 +1441,9 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
 // each subspace's chunk sums need one warp reduction instead of one per warp
 // and per subspace, and every lane keeps 32 independent row loads in flight.
 // A non-finite weight shows up as a non-finite chunk bound (weights are sums
-// of squares, never negative).
+// of squares, never negative). Odd steps walk the chunks in reverse order, so
+// each pass starts on the rows and weights the previous pass left in L2
+// (every chunk still writes its own sums: the results do not depend on it).
 template <int S>
 __global__ void __launch_bounds__(kMaxM * 32)
 pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, int step,
@@ -1454,7 +1456,8 @@ pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, 
 #pragma unroll
   for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
   const double T = thr[m];
-  const uint64_t r0 = (uint64_t)blockIdx.x * kSeedChunk;
+  const uint32_t ch = (step & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x;
+  const uint64_t r0 = (uint64_t)ch * kSeedChunk;
   const float* xm = XT + (size_t)m * N * S;
   float* mm = md + (size_t)m * N;
   double lo = 0.0, hi = 0.0;
@@ -1477,8 +1480,8 @@ pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, 
   hi = warp_sum_ru(hi);
   cnt = __reduce_add_sync(0xffffffffu, cnt);
   if (lane == 0) {
-    chunk[(size_t)m * chunk_stride + blockIdx.x] = make_double2(lo, hi);
-    chunk_cnt[(size_t)m * chunk_stride + blockIdx.x] = cnt;
+    chunk[(size_t)m * chunk_stride + ch] = make_double2(lo, hi);
+    chunk_cnt[(size_t)m * chunk_stride + ch] = cnt;
     if (!isfinite(lo) || !isfinite(hi)) nonfinite[m] = 1;
   }
 }
