@@ -96,8 +96,9 @@ TAC_SMALL = (117_645, 12_288, 10)  # configs[0] rows, kappa (10,240 leaves no ro
 
 
 def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=None) -> dict:
-    """clusterFlat through the host-pointer C ABI (e2e wall time, device
-    phases from mvr_tac_last_stats) on the full corpus and on configs[0].
+    """clusterFlat through the host-pointer C ABI (e2e wall time with the
+    inputs in page-locked host memory, device phases from mvr_tac_last_stats)
+    on the full corpus and on configs[0].
     With world > 1 every rank calls the token-sharded entry point on the
     same inputs (a collective); times are the max over ranks (``reduce``)."""
     from ir_multivector_retrieval_b200 import synth, tac
@@ -112,11 +113,17 @@ def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=
     def call(ids, vec, prm):
         return tac.cluster_flat(ids, vec, DIM, prm, ctx=ctx, sharded=sharded)
 
-    call(corpus.token_ids, corpus.vectors, p)  # warm-up: grows buffers
+    def pinned(a):  # inputs in page-locked host memory, like the pq.train e2e leg
+        import torch
+
+        return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+
+    ids_h, vec_h = pinned(corpus.token_ids), pinned(corpus.vectors)
+    call(ids_h, vec_h, p)  # warm-up: grows buffers
     walls, stats, digests = [], [], set()
     for _ in range(max(1, steps)):
         t0 = time.perf_counter()
-        r = call(corpus.token_ids, corpus.vectors, p)
+        r = call(ids_h, vec_h, p)
         walls.append(time.perf_counter() - t0)
         stats.append(tac.last_stats(ctx))
         digests.add(hashlib.sha256(r.centroids.tobytes() + r.assignments.tobytes()).hexdigest())
@@ -137,11 +144,12 @@ def measure_tac(corpus, steps: int, cpu: bool, ctx=None, world: int = 1, reduce=
     n0, k0, th0 = TAC_SMALL
     c0 = synth.make_corpus(n0, DIM, seed=42)
     p0 = tac.ClusteringParams(kappa_total=k0, seed=42, theta=th0)
-    call(c0.token_ids, c0.vectors, p0)
+    ids0, vec0 = pinned(c0.token_ids), pinned(c0.vectors)
+    call(ids0, vec0, p0)
     w0 = []
     for _ in range(max(1, steps)):
         t0 = time.perf_counter()
-        r0 = call(c0.token_ids, c0.vectors, p0)
+        r0 = call(ids0, vec0, p0)
         w0.append(time.perf_counter() - t0)
     small = {"workload": f"configs[0]: {n0:,} x {DIM}, kappa {k0:,}, theta {th0}",
              "e2e_ms": red(statistics.median(w0) * 1e3)}
