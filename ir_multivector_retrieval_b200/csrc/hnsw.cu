@@ -809,20 +809,6 @@ uint8_t pick_level(Xoshiro256pp& r, float m_l) {
   return (uint8_t)lvl;
 }
 
-struct DevAllocs {
-  std::vector<void*> ptrs;
-  ~DevAllocs() {
-    for (void* p : ptrs) cudaFree(p);
-  }
-  template <class T>
-  cudaError_t get(T** p, size_t bytes) {
-    void* v = nullptr;
-    const cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
-    if (e == cudaSuccess) ptrs.push_back(v);
-    *p = static_cast<T*>(v);
-    return e;
-  }
-};
 
 }  // namespace
 
@@ -901,28 +887,47 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
   }
   const uint32_t layers = top_level + 1;
 
-  DevAllocs al;
+  // one workspace for the whole build, carved from the context's grow-only
+  // scratch (a repeated build allocates nothing)
   DevGraph g{};
   g.n = n;
   g.dim = dim;
   g.m = m;
+  const size_t tl_cap = (size_t)kChunk * kMaxM * layers;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  size_t o_ids[kMaxLayers], o_len[kMaxLayers], o_off[kMaxLayers], o_nb[kMaxLayers];
   for (uint32_t L = 0; L < layers; ++L) {
     g.cap[L] = L == 0 ? 2 * m : m;
-    MVR_CUDA(c, al.get(&g.ids[L], (size_t)n * (g.cap[L] + 1) * 4));
-    MVR_CUDA(c, al.get(&g.len[L], (size_t)n * 4));
+    o_ids[L] = take((size_t)n * (g.cap[L] + 1) * 4);
+    o_len[L] = take((size_t)n * 4);
+    o_off[L] = take(((size_t)n + 1) * 4);
+    o_nb[L] = take((size_t)n * g.cap[L] * 4);  // lists hold at most cap entries at rest
+  }
+  const size_t o_levels = take(n), o_chosen = take((size_t)kChunk * kMaxLayers * kMaxM * 4),
+               o_nchosen = take((size_t)kChunk * kMaxLayers * 4), o_mask = take((size_t)layers * n * kMaskWords * 4),
+               o_touched = take((size_t)layers * n * 4), o_tlist = take(tl_cap * 4), o_small = take(64);
+  unsigned char* ws = nullptr;
+  MVR_TRY(scratch(c, kSlotAux3, off, (void**)&ws));
+  std::vector<uint32_t*> d_off(layers), d_nb(layers);
+  for (uint32_t L = 0; L < layers; ++L) {
+    g.ids[L] = reinterpret_cast<uint32_t*>(ws + o_ids[L]);
+    g.len[L] = reinterpret_cast<uint32_t*>(ws + o_len[L]);
+    d_off[L] = reinterpret_cast<uint32_t*>(ws + o_off[L]);
+    d_nb[L] = reinterpret_cast<uint32_t*>(ws + o_nb[L]);
     MVR_CUDA(c, cudaMemsetAsync(g.len[L], 0, (size_t)n * 4, st));
   }
-  uint8_t* d_levels = nullptr;
-  uint32_t *d_chosen = nullptr, *d_nchosen = nullptr, *d_mask = nullptr, *d_touched = nullptr, *d_tlist = nullptr,
-           *d_small = nullptr;
-  MVR_CUDA(c, al.get(&d_levels, n));
-  MVR_CUDA(c, al.get(&d_chosen, (size_t)kChunk * kMaxLayers * kMaxM * 4));
-  MVR_CUDA(c, al.get(&d_nchosen, (size_t)kChunk * kMaxLayers * 4));
-  MVR_CUDA(c, al.get(&d_mask, (size_t)layers * n * kMaskWords * 4));
-  MVR_CUDA(c, al.get(&d_touched, (size_t)layers * n * 4));
-  const size_t tl_cap = (size_t)kChunk * kMaxM * layers;
-  MVR_CUDA(c, al.get(&d_tlist, tl_cap * 4));
-  MVR_CUDA(c, al.get(&d_small, 64));  // [0] tcount, [1] status
+  uint8_t* d_levels = ws + o_levels;
+  uint32_t* d_chosen = reinterpret_cast<uint32_t*>(ws + o_chosen);
+  uint32_t* d_nchosen = reinterpret_cast<uint32_t*>(ws + o_nchosen);
+  uint32_t* d_mask = reinterpret_cast<uint32_t*>(ws + o_mask);
+  uint32_t* d_touched = reinterpret_cast<uint32_t*>(ws + o_touched);
+  uint32_t* d_tlist = reinterpret_cast<uint32_t*>(ws + o_tlist);
+  uint32_t* d_small = reinterpret_cast<uint32_t*>(ws + o_small);  // [0] tcount, [1] status
   MVR_CUDA(c, cudaMemsetAsync(d_mask, 0, (size_t)layers * n * kMaskWords * 4, st));
   MVR_CUDA(c, cudaMemsetAsync(d_touched, 0, (size_t)layers * n * 4, st));
   MVR_CUDA(c, cudaMemsetAsync(d_small, 0, 64, st));
@@ -996,9 +1001,7 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
   }
 
   // freeze
-  std::vector<uint32_t*> d_off(layers), d_nb(layers);
   for (uint32_t L = 0; L < layers && L <= max_level; ++L) {
-    MVR_CUDA(c, al.get(&d_off[L], ((size_t)n + 1) * 4));
     hnsw_offsets_kernel<<<1, 1024, 0, st>>>(g.len[L], n, d_off[L]);
     ++launches;
   }
@@ -1010,7 +1013,6 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
   MVR_CUDA(c, cudaMemcpyAsync(&hstatus, d_small + 1, 4, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(c, cudaStreamSynchronize(st));
   for (uint32_t L = 0; L <= max_level; ++L) {
-    MVR_CUDA(c, al.get(&d_nb[L], (size_t)totals[L] * 4));
     const uint32_t stride = g.cap[L] + 1;
     const uint64_t threads = (uint64_t)n * stride;
     hnsw_gather_kernel<<<(uint32_t)((threads + 255) / 256), 256, 0, st>>>(g.ids[L], g.len[L], n, stride, d_off[L],
@@ -1084,12 +1086,8 @@ int mvr_hnsw_build(mvr_ctx* ctx, const float* centroids, uint64_t n_floats, uint
   mvr::Ctx* c = &ctx->impl;
   if (dim == 0 || n_floats % dim) return mvr::fail(c, MVR_E_DIM_MISMATCH, "hnsw.build: centroids.len % dim != 0");
   if (n_floats == 0) return mvr::fail(c, MVR_E_EMPTY_CORPUS, "hnsw.build: no centroids");
-  float* d = nullptr;
-  MVR_CUDA(c, cudaMalloc(&d, n_floats * 4));
-  struct Free {
-    float* p;
-    ~Free() { cudaFree(p); }
-  } fr{d};
+  float* d = nullptr;  // staged in the context's scratch (the build's workspace uses another slot)
+  MVR_TRY(mvr::scratch(c, mvr::kSlotAux2, n_floats * 4, (void**)&d));
   MVR_TRY(mvr::h2d_staged(c, d, centroids, n_floats * 4));
   return mvr_hnsw_build_device(ctx, d, n_floats, dim, seed, ef_construction, m, n_threads, out);
 }
@@ -1134,11 +1132,7 @@ int mvr_normalize_rows(mvr_ctx* ctx, float* rows, uint64_t n_floats, uint32_t di
   if (n_floats % dim) return mvr::fail(c, MVR_E_LENGTH_MISMATCH, "normalizeRowsInPlace: len % dim != 0");
   if (n_floats == 0) return MVR_OK;
   float* d = nullptr;
-  MVR_CUDA(c, cudaMalloc(&d, n_floats * 4));
-  struct Free {
-    float* p;
-    ~Free() { cudaFree(p); }
-  } fr{d};
+  MVR_TRY(mvr::scratch(c, mvr::kSlotAux2, n_floats * 4, (void**)&d));
   MVR_TRY(mvr::h2d_staged(c, d, rows, n_floats * 4));
   MVR_TRY(mvr::normalize_rows_device(c, d, n_floats, dim));
   MVR_TRY(mvr::d2h_staged(c, rows, d, n_floats * 4));
