@@ -199,6 +199,7 @@ __device__ __forceinline__ float l2_groups(const float4* __restrict__ GT, uint64
 // directed-rounding sums and the count of non-zero weights below thr. Rows
 // come from the group-major copy, so each float4 load of a warp is one
 // contiguous 512-byte segment.
+
 template <int NG>
 __global__ void __launch_bounds__(kUpdT)
 km_seed_update_kernel(const float4* __restrict__ GT, uint64_t R, int d, Prob P, int step,
@@ -209,6 +210,7 @@ km_seed_update_kernel(const float4* __restrict__ GT, uint64_t R, int d, Prob P, 
   extern __shared__ __align__(16) float4 cen4[];
   __shared__ double2 wp[kUpdT / 32];
   __shared__ uint32_t wc[kUpdT / 32];
+  grid_dependency_wait();  // launched early (programmatic dependent launch): the last step completes first
   const uint32_t p = ch_p[blockIdx.x];
   if (P.state[p] != kRunning) return;
   const uint64_t co = P.coff[p] + step;
@@ -280,6 +282,7 @@ km_seed_select_kernel(const float* __restrict__ G, int d, Prob P, int step,
                       const uint32_t* __restrict__ ch_len, const double2* __restrict__ ch_sum,
                       const uint32_t* __restrict__ ch_cnt, const float* __restrict__ md,
                       const double* __restrict__ draws, float* __restrict__ C, int force_chain) {
+  grid_dependency_wait();
   const uint32_t p = sel_p[blockIdx.x];
   if (P.state[p] != kRunning) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1697,16 +1700,17 @@ int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, u
       const float4* gt4 = reinterpret_cast<const float4*>(d_GT);
       const size_t sm = (size_t)((d + 3) / 4) * sizeof(float4);
       auto upd = d == 64 ? km_seed_update_kernel<16> : d == 128 ? km_seed_update_kernel<32> : km_seed_update_kernel<0>;
-      upd<<<nch, kUpdT, sm, st>>>(gt4, rows, d, P, (int)s - 1, at<uint32_t>(ws, o_chp), at<uint64_t>(ws, o_chr0),
-                                  at<uint32_t>(ws, o_chlen), d_C, at<float>(ws, o_md), at<double2>(ws, o_chsum),
-                                  at<uint32_t>(ws, o_chcnt));
+      MVR_CUDA(ctx, launch_pdl(upd, dim3(nch), dim3(kUpdT), sm, st, gt4, rows, d, P, (int)s - 1,
+                               (const uint32_t*)at<uint32_t>(ws, o_chp), (const uint64_t*)at<uint64_t>(ws, o_chr0),
+                               (const uint32_t*)at<uint32_t>(ws, o_chlen), (const float*)d_C, at<float>(ws, o_md),
+                               at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt)));
     }
-    MVR_CUDA(ctx, cudaGetLastError());
-    km_seed_select_kernel<<<na, kSelT, 0, st>>>(
-        d_G, d, P, (int)s, at<uint32_t>(ws, o_seeders), at<uint32_t>(ws, o_cfirst), at<uint32_t>(ws, o_ccount),
-        at<uint64_t>(ws, o_chr0), at<uint32_t>(ws, o_chlen), at<double2>(ws, o_chsum), at<uint32_t>(ws, o_chcnt),
-        at<float>(ws, o_md), at<double>(ws, o_draws), d_C, ctx->serial_draws ? 1 : 0);
-    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_CUDA(ctx, launch_pdl(km_seed_select_kernel, dim3(na), dim3(kSelT), 0, st, (const float*)d_G, d, P, (int)s,
+                             (const uint32_t*)at<uint32_t>(ws, o_seeders), (const uint32_t*)at<uint32_t>(ws, o_cfirst),
+                             (const uint32_t*)at<uint32_t>(ws, o_ccount), (const uint64_t*)at<uint64_t>(ws, o_chr0),
+                             (const uint32_t*)at<uint32_t>(ws, o_chlen), (const double2*)at<double2>(ws, o_chsum),
+                             (const uint32_t*)at<uint32_t>(ws, o_chcnt), (const float*)at<float>(ws, o_md),
+                             (const double*)at<double>(ws, o_draws), d_C, ctx->serial_draws ? 1 : 0));
     launches += 2;
   }
 

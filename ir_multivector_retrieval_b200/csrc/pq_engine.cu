@@ -1450,6 +1450,7 @@ pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, 
                         const float* __restrict__ cb, float* __restrict__ md, double2* __restrict__ chunk,
                         uint32_t* __restrict__ chunk_cnt, int* __restrict__ nonfinite,
                         const uint8_t* __restrict__ state, const double* __restrict__ thr, int chunk_stride) {
+  grid_dependency_wait();  // launched early (programmatic dependent launch): the last step completes first
   const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
   if (m >= M || state[m] != kRunning) return;
   float c[S];
@@ -1519,6 +1520,7 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
                       int* __restrict__ status, uint8_t* __restrict__ state,
                       uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen,
                       double* __restrict__ thr, int force_chain) {
+  grid_dependency_wait();
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2371,17 +2373,17 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   for (int step = 0; step + 1 < K; ++step) {
     const bool sample = timing && step >= 1 && (step - 1) % 8 == 0 && (size_t)(2 * ((step - 1) / 8) + 1) < sev.size();
     if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8)], st));
-    switch (S) {
-      case 1: pq_seed_update_w_kernel<1><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
-      case 2: pq_seed_update_w_kernel<2><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
-      default: pq_seed_update_w_kernel<4><<<nchunk, 32 * M, 0, st>>>(XT, N, M, K, step, cb, mind, chunk, chunk_cnt, d_nonf, d_state, d_thr, nchunk); break;
+    {
+      auto upd = S == 1 ? pq_seed_update_w_kernel<1> : S == 2 ? pq_seed_update_w_kernel<2> : pq_seed_update_w_kernel<4>;
+      MVR_CUDA(ctx, launch_pdl(upd, dim3(nchunk), dim3(32 * M), 0, st, (const float*)XT, N, M, K, step,
+                               (const float*)cb, mind, chunk, chunk_cnt, d_nonf, (const uint8_t*)d_state,
+                               (const double*)d_thr, nchunk));
     }
-    MVR_CUDA(ctx, cudaGetLastError());
     if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8) + 1], st));
-    pq_seed_select_kernel<<<M, kSelectThreads, 0, st>>>(XT, N, S, K, step + 1, cb, mind, chunk, chunk_cnt,
-                                                        nchunk, d_draws, d_nonf, d_status, d_state, d_fb,
-                                                        d_chosen, d_thr, ctx && ctx->serial_draws ? 1 : 0);
-    MVR_CUDA(ctx, cudaGetLastError());
+    MVR_CUDA(ctx, launch_pdl(pq_seed_select_kernel, dim3(M), dim3(kSelectThreads), 0, st, (const float*)XT, N, S, K,
+                             step + 1, cb, (const float*)mind, (const double2*)chunk, (const uint32_t*)chunk_cnt,
+                             nchunk, (const double*)d_draws, d_nonf, d_status, d_state, d_fb, d_chosen, d_thr,
+                             ctx && ctx->serial_draws ? 1 : 0));
     launches += 2;
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
