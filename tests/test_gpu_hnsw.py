@@ -101,3 +101,14 @@ def test_errors(ctx):
     with pytest.raises(MvrError) as e:
         hnsw.normalize_rows(np.ones(10, np.float32), 3, ctx=ctx)
     assert e.value.name == "LengthMismatch"
+
+
+def test_thread_count_contract(ctx, orc):
+    """build_determinism_test.zig / hnsw.zig:1401: the graph is the same for
+    every n_threads >= 2 and differs on the serial path (n_threads 1)."""
+    base, _ = rng_rows(orc, 20260501, 600, 16)
+    g2 = hnsw.build(base, 16, 17, ef_construction=64, m=8, n_threads=2, ctx=ctx)
+    g10 = hnsw.build(base, 16, 17, ef_construction=64, m=8, n_threads=10, ctx=ctx)
+    g1 = hnsw.build(base, 16, 17, ef_construction=64, m=8, n_threads=1, ctx=ctx)
+    _same(g2, g10)
+    assert any(not np.array_equal(a, b) for a, b in zip(g1.layer_neighbours, g2.layer_neighbours))
