@@ -188,6 +188,7 @@ struct PlanCtl {
   float tsim, newmin;
   uint32_t bal[2];
   uint32_t stg_node[2], stg_mask[2][2];
+  uint32_t hk[kPlanThreads / 32], hp[kPlanThreads / 32], hslot[kPlanThreads / 32], hkept, nr;
 };
 
 // greedySearchLayer (hnsw.zig:969-991), warp 0: the first strict maximum of
@@ -586,25 +587,57 @@ __global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) 
     __syncthreads();
     // ---- the beam, best first, is W[0 .. wn); next layer starts at its best
     const uint32_t wn = ctl.wn;
-    // ---- selectHeuristic (warp 0): keep a candidate unless a chosen
-    // neighbour is strictly more similar to it than the query is
-    if (warp == 0) {
-      uint32_t nr = 0;
-      for (uint32_t i = 0; i < wn && nr < m; ++i) {
-        const Ent ce = W[i];
+    // ---- selectHeuristic: keep a candidate unless a chosen neighbour is
+    // strictly more similar to it than the query is. Eight candidates per
+    // round, one per warp: each is tested against the neighbours chosen
+    // before the round and against the earlier candidates of the round, then
+    // one thread keeps them in order — the reference's sequential rule.
+    constexpr uint32_t kHB = kPlanThreads / 32;
+    if (tid == 0) ctl.nr = 0;
+    __syncthreads();
+    for (uint32_t b = 0; b < wn; b += kHB) {
+      const uint32_t nr = ctl.nr;
+      if (nr >= m) break;
+      const uint32_t i = b + warp;
+      float* cvw = cv + (size_t)warp * lay.rstride;
+      Ent ce{0.f, 0u};
+      if (i < wn) {
+        ce = W[i];
         const uint32_t cnode = ce.node & ~kExpanded;
-        for (uint32_t d = lane; d < dim; d += 32) cv[d] = a.x[(size_t)cnode * dim + d];
-        __syncwarp();
-        bool pr = false;
-        if (lane < nr) pr = dot_ref_scalar(cv, rv + (size_t)lane * lay.rstride, dim) > ce.sim;
-        const bool keep = __ballot_sync(~0u, pr) == 0;
-        if (keep) {
-          for (uint32_t d = lane; d < dim; d += 32) rv[(size_t)nr * lay.rstride + d] = cv[d];
-          if (lane == 0) rid[nr] = cnode;
-          ++nr;
-        }
-        __syncwarp();
+        for (uint32_t d = lane; d < dim; d += 32) cvw[d] = a.x[(size_t)cnode * dim + d];
       }
+      __syncthreads();
+      if (i < wn) {
+        bool pk = false, pp = false;
+        if (lane < nr) pk = dot_ref_scalar(cvw, rv + (size_t)lane * lay.rstride, dim) > ce.sim;
+        if (lane < warp) pp = dot_ref_scalar(cvw, cv + (size_t)lane * lay.rstride, dim) > ce.sim;
+        const uint32_t bk = __ballot_sync(~0u, pk), bp = __ballot_sync(~0u, pp);
+        if (lane == 0) {
+          ctl.hk[warp] = bk;
+          ctl.hp[warp] = bp;
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t n = nr, kept = 0;
+        for (uint32_t w = 0; w < kHB && b + w < wn && n < m; ++w)
+          if (ctl.hk[w] == 0 && (ctl.hp[w] & kept) == 0) {
+            kept |= 1u << w;
+            rid[n] = W[b + w].node & ~kExpanded;
+            ctl.hslot[w] = n++;
+          }
+        ctl.hkept = kept;
+        ctl.nr = n;
+      }
+      __syncthreads();
+      if ((ctl.hkept >> warp) & 1u) {
+        float* dst = rv + (size_t)ctl.hslot[warp] * lay.rstride;
+        for (uint32_t d = lane; d < dim; d += 32) dst[d] = cvw[d];
+      }
+      __syncthreads();
+    }
+    if (warp == 0) {
+      const uint32_t nr = ctl.nr;
       uint32_t* out = a.chosen + ((size_t)qi * kMaxLayers + L) * kMaxM;
       if (lane < nr) out[lane] = rid[lane];
       if (lane == 0) {
@@ -860,7 +893,7 @@ int hnsw_build_device(Ctx* c, const float* d_x, uint64_t n_floats, uint32_t dim,
     lay.ties = take(kTieCap * 4);
     lay.rv = take(kMaxM * lay.rstride * 4);
     lay.rid = take(kMaxM * 4);
-    lay.cv = take(dimp * 4);
+    lay.cv = take((kPlanThreads / 32) * lay.rstride * 4);  // one candidate row per warp
     // staged rows of the guessed next expansion: 16 KB per buffer, whole rows
     lay.stage_slots = (dim & 3u) == 0 ? std::min<uint32_t>(64, 16384 / (dim * 4)) : 0u;
     lay.stg = take(2 * lay.stage_slots * dim * 4);
