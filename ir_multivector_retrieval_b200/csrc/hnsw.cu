@@ -184,7 +184,8 @@ struct PlanArgs {
 };
 
 struct PlanCtl {
-  uint32_t wn, hint, newhint, pop, spec, spec2, done, nt, nev, p0, full, cur;
+  uint32_t wn, hint, newhint, pop, nt, nev, p0, full, cur;
+  uint32_t scan[kPlanThreads / 32];
   float tsim, newmin;
   uint32_t bal[2];
   uint32_t stg_node[2], stg_mask[2][2];
@@ -342,45 +343,50 @@ __global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) 
         if (tid == 0) atomicOr(a.status, kErrLoop);
         break;
       }
-      // ---- P1 (warp 0): the ties evicted by the last merge, then the next
-      // expansion (first unexpanded entry of W, else the smallest tie) and
-      // two guesses of the ones after it (the next unexpanded entries of W),
-      // which only steer prefetches
-      if (warp == 0) {
-        const uint32_t wn = ctl.wn;
+      // ---- P1: the next expansion. All warps scan 256 entries of W from
+      // the hint (one ballot each); the first unexpanded entry is the next
+      // expansion and the two after it are guesses that only steer the
+      // copies below. Meanwhile the last warp keeps the ties the last merge
+      // evicted: entries dropped with similarity equal to the new minimum
+      // stay expandable (the reference stops only strictly below it).
+      const uint32_t wn = ctl.wn, hint0 = ctl.hint;
+      if (warp == kPlanThreads / 32 - 1 && ctl.full) {
         uint32_t nt = ctl.nt;
-        if (ctl.full) {
-          const float mn = ctl.newmin;
-          if (nt && ctl.tsim != mn) nt = 0;
-          const uint32_t nev = ctl.nev;
-          for (uint32_t base = 0; base < nev; base += 32) {
-            const uint32_t i = base + lane;
-            const bool t = i < nev && ev[i].sim == mn;
-            const uint32_t b = __ballot_sync(~0u, t);
-            if (t) {
-              const uint32_t slot = nt + __popc(b & lanemask_lt());
-              if (slot < kTieCap) ties[slot] = ev[i].node & ~kExpanded;
-            }
-            nt += __popc(b);
-          }
-          if (nt > kTieCap) {
-            nt = kTieCap;
-            if (lane == 0) atomicOr(a.status, kErrTies);
-          }
-          __syncwarp();
-          if (lane == 0) {
-            ctl.tsim = mn;
-            ctl.full = 0;
-          }
-        }
-        // chunks of 32 entries from the hint: the first unexpanded entry, then
-        // up to two more chunks for the guesses
-        uint32_t p = wn, p2 = wn, p3 = wn, nf = 0, extra = 0;
-        for (uint32_t base = ctl.hint; base < wn && nf < 3; base += 32) {
+        const float mn = ctl.newmin;
+        if (nt && ctl.tsim != mn) nt = 0;
+        const uint32_t nev = ctl.nev;
+        for (uint32_t base = 0; base < nev; base += 32) {
           const uint32_t i = base + lane;
-          uint32_t b = __ballot_sync(~0u, i < wn && !(W[i].node & kExpanded));
-          while (b && nf < 3) {
-            const uint32_t idx = base + __ffs(b) - 1;
+          const bool tt = i < nev && ev[i].sim == mn;
+          const uint32_t bt = __ballot_sync(~0u, tt);
+          if (tt) {
+            const uint32_t slot = nt + __popc(bt & lanemask_lt());
+            if (slot < kTieCap) ties[slot] = ev[i].node & ~kExpanded;
+          }
+          nt += __popc(bt);
+        }
+        if (nt > kTieCap) {
+          nt = kTieCap;
+          if (lane == 0) atomicOr(a.status, kErrTies);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          ctl.nt = nt;
+          ctl.tsim = mn;
+          ctl.full = 0;
+        }
+      }
+      uint32_t p = wn, p2 = wn, p3 = wn;
+      for (uint32_t base = hint0;;) {  // uniform: every thread reads the same words
+        const uint32_t i = base + 32 * warp + lane;
+        const uint32_t bw = __ballot_sync(~0u, i < wn && !(W[i].node & kExpanded));
+        if (lane == 0) ctl.scan[warp] = bw;
+        __syncthreads();
+        uint32_t nf = 0;
+        for (uint32_t w = 0; w < kPlanThreads / 32 && nf < 3; ++w) {
+          uint32_t bb = ctl.scan[w];
+          while (bb && nf < 3) {
+            const uint32_t idx = base + 32 * w + __ffs(bb) - 1;
             if (nf == 0)
               p = idx;
             else if (nf == 1)
@@ -388,22 +394,26 @@ __global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) 
             else
               p3 = idx;
             ++nf;
-            b &= b - 1;
+            bb &= bb - 1;
           }
-          if (nf && ++extra > 2) break;
         }
-        if (p < wn) {
-          if (lane == 0) {
-            const uint32_t pop = W[p].node;
-            W[p].node = pop | kExpanded;
-            ctl.pop = pop;
-            ctl.hint = p;
-            ctl.spec = p2 < wn ? (W[p2].node & ~kExpanded) : 0xFFFFFFFFu;
-            ctl.spec2 = p3 < wn ? (W[p3].node & ~kExpanded) : 0xFFFFFFFFu;
-            ctl.nt = nt;
-            ctl.done = 0;
-          }
-        } else {
+        if (nf || base + kPlanThreads >= wn) break;
+        base += kPlanThreads;
+        __syncthreads();  // the words are rewritten by the next window
+      }
+      uint32_t c, spec = 0xFFFFFFFFu, spec2 = 0xFFFFFFFFu;
+      if (p < wn) {
+        c = W[p].node & ~kExpanded;
+        if (p2 < wn) spec = W[p2].node & ~kExpanded;
+        if (p3 < wn) spec2 = W[p3].node & ~kExpanded;
+        if (tid == 0) {
+          W[p].node = c | kExpanded;
+          ctl.hint = p;
+        }
+      } else {  // W is exhausted: the tie with the smallest id, if any
+        const uint32_t nt = ctl.nt;
+        if (nt == 0) break;
+        if (warp == 0) {
           uint32_t best = 0xFFFFFFFFu, bi = 0;
           for (uint32_t i = lane; i < nt; i += 32)
             if (ties[i] < best) {
@@ -419,23 +429,14 @@ __global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) 
           }
           __syncwarp();
           if (lane == 0) {
-            ctl.spec = 0xFFFFFFFFu;
-            ctl.spec2 = 0xFFFFFFFFu;
-            if (nt == 0) {
-              ctl.done = 1;
-              ctl.nt = 0;
-            } else {
-              ctl.pop = best;
-              ties[bi] = ties[nt - 1];
-              ctl.nt = nt - 1;
-              ctl.done = 0;
-            }
+            ctl.pop = best;
+            ties[bi] = ties[nt - 1];
+            ctl.nt = nt - 1;
           }
         }
+        __syncthreads();
+        c = ctl.pop;
       }
-      __syncthreads();
-      if (ctl.done) break;
-      const uint32_t c = ctl.pop, spec = ctl.spec, spec2 = ctl.spec2;
       // ---- P2: the unvisited neighbours of c in list order (threads < 64;
       // the count and the ids are read together). Warps 2-3 stage the rows of
       // the guessed next expansion's unvisited neighbours into shared memory
@@ -501,7 +502,6 @@ __global__ void __launch_bounds__(kPlanThreads, 2) hnsw_plan_kernel(PlanArgs a) 
       // ---- P4: acceptance of candidate j: fewer than ef of W and the
       // candidates before j are at least as similar. One warp per candidate;
       // the count in W by 32-way steps (W's similarities never increase).
-      const uint32_t wn = ctl.wn;
       for (uint32_t j = warp; j < k; j += kPlanThreads / 32) {
         const float sj = cs[j];
         const uint32_t inw = warp_boundary(W, 0, wn, [sj](Ent w) { return w.sim >= sj; });
