@@ -98,6 +98,9 @@ def test_errors(ctx):
     with pytest.raises(MvrError) as e:
         hnsw.build(np.ones(64, np.float32), 4, 1, m=33, ctx=ctx)
     assert e.value.name == "InvalidArgument"
+    with pytest.raises(MvrError) as e:  # the beam lives in one CTA's shared memory
+        hnsw.build(np.ones(64, np.float32), 4, 1, ef_construction=2049, ctx=ctx)
+    assert e.value.name == "InvalidArgument"
     with pytest.raises(MvrError) as e:
         hnsw.normalize_rows(np.ones(10, np.float32), 3, ctx=ctx)
     assert e.value.name == "LengthMismatch"
