@@ -458,6 +458,11 @@ def run_b200(args) -> None:
     e2e_value = max_over_ranks(statistics.median(e2e_train)) / ITERS
     e2e_enc_s = max_over_ranks(statistics.median(e2e_enc))
     assert np.array_equal(cb_host, dcb.cpu().numpy()), "host and device entry points disagree"
+    if world == 1:
+        encode_dev()
+        torch.cuda.synchronize()
+        assert np.array_equal(codes_host.numpy().reshape(-1), dcodes.cpu().numpy().reshape(-1)), \
+            "host and device encodes disagree"
 
     # ---- roofline of the dominant kernel: the k-means++ update (a third of the
     # device time), one HBM pass per step over the subspace-major rows of this

@@ -208,7 +208,8 @@ int mvr_pq_train_device(mvr_ctx* ctx, const float* d_residuals,
  * (src/index/pq.zig:59-76): for each of the n rows and each subspace m, the
  * first codeword of minimum exact squared L2 distance. `codebooks` is
  * pq_m*256*(dim/pq_m) floats, `residuals` n*dim floats, `codes_out` n*pq_m
- * bytes. */
+ * bytes. Page-locked `residuals` of 524,288 rows or more are copied in chunks
+ * that overlap the encoding of the chunks already on the device. */
 int mvr_pq_encode(mvr_ctx* ctx, const float* codebooks, uint32_t dim,
                   uint32_t pq_m, const float* residuals, uint64_t n,
                   uint8_t* codes_out);

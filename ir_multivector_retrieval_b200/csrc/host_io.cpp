@@ -119,6 +119,8 @@ int ensure_io(Ctx* c) {
 }
 }  // namespace
 
+bool host_is_pinned(const void* h) { return is_pinned(h); }
+
 int h2d_staged(Ctx* c, void* d, const void* h, size_t bytes) {
   if (bytes == 0) return MVR_OK;
   if (bytes < kStagedMin || is_pinned(h)) {

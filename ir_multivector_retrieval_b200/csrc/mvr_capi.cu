@@ -407,8 +407,41 @@ int mvr_pq_encode(mvr_ctx* h, const float* cb, uint32_t dim, uint32_t pq_m, cons
   MVR_TRY(mvr::scratch(c, mvr::kSlotCodebooks, cb_floats * sizeof(float), (void**)&d_cb));
   MVR_TRY(mvr::scratch(c, mvr::kSlotCodes, n * pq_m, (void**)&d_codes));
   MVR_TRY(mvr::h2d(c, d_cb, cb, cb_floats * sizeof(float)));
-  MVR_TRY(mvr::h2d(c, d_res, res, n * dim * sizeof(float)));
-  MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes));
+  constexpr uint64_t kPipeRows = 1ull << 18;
+  if (n >= 2 * kPipeRows && mvr::host_is_pinned(res)) {
+    // page-locked rows: copied in up to 8 chunks on the side stream, each
+    // chunk encoded on the context stream as soon as it has landed (every
+    // row's code is independent of the others)
+    cudaStream_t s2 = nullptr;
+    MVR_TRY(mvr::side_stream(c, &s2));
+    const uint64_t nch = std::min<uint64_t>(8, (n + kPipeRows - 1) / kPipeRows);
+    const uint64_t per = (n + nch - 1) / nch;
+    cudaEvent_t evs[9] = {};
+    struct EvFree {
+      cudaEvent_t* e;
+      ~EvFree() {
+        for (int i = 0; i < 9; ++i)
+          if (e[i]) cudaEventDestroy(e[i]);
+      }
+    } evfree{evs};
+    for (uint64_t i = 0; i <= nch; ++i) MVR_CUDA(c, cudaEventCreateWithFlags(&evs[i], cudaEventDisableTiming));
+    MVR_CUDA(c, cudaEventRecord(evs[nch], c->stream));  // the side stream follows the context stream's earlier work
+    MVR_CUDA(c, cudaStreamWaitEvent(s2, evs[nch], 0));
+    for (uint64_t i = 0; i < nch; ++i) {
+      const uint64_t off = i * per, cnt = std::min(per, n - off);
+      MVR_CUDA(c, cudaMemcpyAsync(d_res + off * dim, res + off * dim, cnt * dim * sizeof(float),
+                                  cudaMemcpyHostToDevice, s2));
+      MVR_CUDA(c, cudaEventRecord(evs[i], s2));
+    }
+    for (uint64_t i = 0; i < nch; ++i) {
+      const uint64_t off = i * per, cnt = std::min(per, n - off);
+      MVR_CUDA(c, cudaStreamWaitEvent(c->stream, evs[i], 0));
+      MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res + off * dim, cnt, d_codes + off * pq_m));
+    }
+  } else {
+    MVR_TRY(mvr::h2d(c, d_res, res, n * dim * sizeof(float)));
+    MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes));
+  }
   if (c->tc_filter && !c->exhaustive_assign && c->tc_diag) {
     uint32_t dg[4] = {0, 0, 0, 0};
     MVR_CUDA(c, cudaMemcpyAsync(dg, c->tc_diag, sizeof(dg), cudaMemcpyDeviceToHost, c->stream));

@@ -77,6 +77,8 @@ struct Ctx {
 // when the context stream reaches it; every host entry point synchronises
 // before it returns). Ordered on the context stream.
 int h2d_staged(Ctx* ctx, void* d, const void* h, size_t bytes);
+// True for page-locked (pinned or registered) host memory.
+bool host_is_pinned(const void* h);
 // Device->host copy through the pinned stages; complete when it returns.
 int d2h_staged(Ctx* ctx, void* h, const void* d, size_t bytes);
 void destroy_host_io(Ctx* ctx);

@@ -336,3 +336,28 @@ def test_tensor_filter_matches_exact_scans(ctx, orc, name, x, dim, m):
     viol, _ = _filter_report(ctx)
     assert viol == 0
 
+
+
+def test_host_encode_chunked_matches_device(ctx):
+    """mvr_pq_encode with page-locked rows (copied and encoded in chunks that
+    overlap) and with pageable rows returns the device entry point's codes."""
+    import ctypes as C
+
+    import torch
+
+    n, dim, m = 600_000, 64, 16
+    x = synth.unit_rows(n, dim, seed=77).reshape(-1)
+    cb = (np.random.default_rng(5).standard_normal(m * 256 * 4) * 0.3).astype(np.float32)
+    x_pin = torch.from_numpy(x).pin_memory()
+    out_pin = torch.empty(n * m, dtype=torch.uint8).pin_memory()
+    ctx.check(ctx.lib.mvr_pq_encode(ctx.handle, C.c_void_p(cb.ctypes.data), dim, m, C.c_void_p(x_pin.data_ptr()),
+                                    n, C.c_void_p(out_pin.data_ptr())))
+    dx, dcb = x_pin.cuda(), torch.from_numpy(cb).cuda()
+    dcodes = torch.empty(n * m, dtype=torch.uint8, device="cuda")
+    ctx.check(ctx.lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), dim, m, C.c_void_p(dx.data_ptr()),
+                                           n, C.c_void_p(dcodes.data_ptr())))
+    ctx.sync()
+    want = dcodes.cpu().numpy()
+    assert np.array_equal(out_pin.numpy(), want)
+    p = pq.PQ(dim=dim, sub_dim=4, codebooks=cb, pq_m=m)
+    assert np.array_equal(p.encode_batch(x.reshape(n, dim)).reshape(-1), want)
