@@ -16,7 +16,11 @@ host memory every step. Encode throughput is reported beside it.
 
 ``--impl reference`` times the CPU restatement of the reference
 (oracle/, multithreaded like the reference's work-stealing ``pq.train``) on
-this host's cores, on a bounded row sample of the same workload.
+this host's cores: one whole pq.train (seeding + 20 Lloyd iterations, the GPU
+value's basis) over a bounded row sample, scaled linearly to all rows. The
+one-GPU line also checks the benched codebooks and codes against the
+restatement run on all rows (``pq_bit_exact_vs_cpu``, after timing) and ends
+with a short ``codebook_sha256`` line for comparing runs at different N.
 
 ``tac`` in the JSON line: ``tac.clusterFlat`` through the host-pointer C ABI
 on the same 1,521,797-row corpus with kappa = 32,768 and the paper-strict
@@ -64,6 +68,15 @@ UNIT = "s/iter"
 WORKLOAD = "configs[1]: synthetic 1,521,797 x 64 f32, PQ M=16x4, 256 centroids, k-means++ + 20 Lloyd iters, + pq.encode"
 
 
+def config_dict(world: int, rows_per_gpu: int | None = None) -> dict:
+    """The workload description both arms print (same keys, same values)."""
+    return {"workload": WORKLOAD, "rows": N_ROWS, "rows_per_gpu": rows_per_gpu or N_ROWS, "dim": DIM,
+            "pq_m": PQ_M, "centroids": K, "lloyd_iters": ITERS,
+            "parallelism": (("subspace-sharded" if PQ_M >= world else "row-sharded")
+                            + f" over {world} GPUs (NCCL)") if world > 1 else "1gpu",
+            "l2": "inputs (389 MB) > L2, no flush"}
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -87,7 +100,7 @@ def _hbm_peak() -> float:
     try:
         return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
     except Exception:
-        return 6650.0  # fallback measured on this pool earlier
+        return 6650.0  # fallback copy bandwidth when the measured file is absent
 
 
 HBM_PEAK = _hbm_peak()
@@ -296,27 +309,52 @@ def cpu_lloyd_seconds_per_iter(x: np.ndarray, threads: int, target_s: float = 15
     return {"s_per_iter": dt * N_ROWS / n_sample, "rows": n_sample, "wall_s": dt}
 
 
+def cpu_train_seconds_per_iter(x: np.ndarray, threads: int, target_s: float = 15.0) -> dict:
+    """The GPU value's basis on the host: one whole pq.train (k-means++
+    seeding + ITERS Lloyd iterations, tol = -inf) by the C restatement on all
+    host threads (work-stealing over the subspaces like pq.zig:192-284), on a
+    row sample sized for ~target_s, scaled linearly to N_ROWS (seeding and
+    Lloyd are both linear in the rows) and divided by ITERS."""
+    from oracle import oracle
+
+    oracle.build()
+    n_probe = min(len(x), 10_000)
+    t0 = time.perf_counter()
+    oracle.pq_train(x[:n_probe], DIM, SEED, PQ_M, n_threads=threads, max_iters=ITERS, tol=-math.inf)
+    probe = time.perf_counter() - t0
+    n_sample = int(min(len(x), max(n_probe, n_probe * target_s / max(probe, 1e-6))))
+    t0 = time.perf_counter()
+    oracle.pq_train(x[:n_sample], DIM, SEED, PQ_M, n_threads=threads, max_iters=ITERS, tol=-math.inf)
+    dt = time.perf_counter() - t0
+    return {"s_per_iter": dt * N_ROWS / n_sample / ITERS, "rows": n_sample, "wall_s": dt,
+            "sample": (f"one whole pq.train (k-means++ seeding + {ITERS} Lloyd iterations, all {PQ_M} subspaces) "
+                       f"over the first {n_sample:,} rows (of {N_ROWS:,}), time scaled linearly to all rows "
+                       f"and divided by {ITERS}; C restatement of pq.train on {threads} threads")}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = host_threads()
     x = make_input()
-    vals = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = cpu_lloyd_seconds_per_iter(x, threads, target_s=args.cpu_target_s)
-        if i >= args.warmup:
-            vals.append(info["s_per_iter"])
+    # each timed step is a bounded sample; the whole run stays within a few minutes
+    target = min(args.cpu_target_s, 150.0 / max(1, args.steps))
+    for _ in range(args.warmup):
+        cpu_train_seconds_per_iter(x, threads, target_s=1.0)
+    vals, info = [], None
+    for _ in range(args.steps):
+        info = cpu_train_seconds_per_iter(x, threads, target_s=target)
+        vals.append(info["s_per_iter"])
     v = statistics.median(vals)
-    sample = (f"1 Lloyd iteration of all 16 subspaces over the first {info['rows']} rows "
-              f"(of {N_ROWS}), scaled linearly to all rows; C restatement of pq.train's Lloyd loop")
+    lloyd = cpu_lloyd_seconds_per_iter(x, threads, target_s=min(target, 10.0))
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "parallelism": "cpu", "l2": "inputs > L2"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.gpus, N_ROWS // max(1, args.gpus)),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": info["sample"]},
+        "lloyd_only_s_per_iter": lloyd["s_per_iter"],
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -464,29 +502,84 @@ def run_b200(args) -> None:
         assert np.array_equal(codes_host.numpy().reshape(-1), dcodes.cpu().numpy().reshape(-1)), \
             "host and device encodes disagree"
 
-    # ---- roofline of the dominant kernel: the k-means++ update (a third of the
-    # device time), one HBM pass per step over the subspace-major rows of this
-    # GPU's subspaces plus the weights read and written; its launches are
-    # sampled with CUDA events inside the engine (every 8th step)
+    # ---- encode through each assignment kernel (one GPU): the exact f32 scan
+    # and the tensor-core filter, both bit-identical; the line reports both
+    enc_paths = {}
+    if world == 1:
+        for name, on in (("exact_f32_scan", 0), ("tcgen05_filter", 1)):
+            ctx.check(lib.mvr_ctx_set_tensor_filter(ctx.handle, on))
+            encode_dev()
+            ts = []
+            for _ in range(5):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                encode_dev()
+                e1.record(stream)
+                ts.append((e0, e1))
+            torch.cuda.synchronize()
+            enc_paths[name] = statistics.median(a.elapsed_time(b) for a, b in ts)
+            assert np.array_equal(codes_host.numpy().reshape(-1), dcodes.cpu().numpy().reshape(-1)), \
+                f"encode through {name} differs"
+        ctx.check(lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))  # the library default
+
+    # ---- rooflines. (1) the k-means++ weight update: one HBM pass per step
+    # over the subspace-major rows of this GPU's subspaces plus the weights
+    # read and written; launches sampled with CUDA events inside the engine
+    # (every 8th step). (2) the pruned Lloyd passes (iterations >= 1): exact
+    # (row, centroid) distances actually computed x 12 flops (3 per
+    # coordinate, SURVEY's convention) against the FP32 lanes x sampled clock.
+    # The line's "roofline" is the one with more device time per training.
     upd_samples = sum(s.seed_update_samples for s in stats)
     upd_ms = sum(s.seed_update_ms_sampled for s in stats) / max(1, upd_samples)
     m_local = PQ_M // world if (world > 1 and PQ_M >= world) else PQ_M
     n_rows = n_total if (world > 1 and PQ_M >= world) else n
     bytes_per_launch = n_rows * m_local * (DIM // PQ_M) * 4 + 2 * n_rows * m_local * 4
     achieved = bytes_per_launch / (max(upd_ms, 1e-9) / 1e3) / 1e9
-    peak = HBM_PEAK
-    traffic = None
+    traffic_json = {}
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         try:
-            t = json.loads(tfile.read_text()).get("pq_seed_update_bytes_per_launch")
-            traffic = t * (n_rows * m_local) / (N_ROWS * PQ_M) if t else None
+            traffic_json = json.loads(tfile.read_text())
         except Exception:
-            traffic = None
-    # the FP32-bound Lloyd assignment beside it (first iteration: every distance)
-    flops_per_launch = n * K * 3 * DIM  # 3 flops per coordinate per (row, centroid)
+            traffic_json = {}
+    t = traffic_json.get("pq_seed_update_bytes_per_launch")
+    traffic = t * (n_rows * m_local) / (N_ROWS * PQ_M) if t else None
     sm_mhz = clk.get("sm_mhz") or 1965.0
     fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # FP32 lanes x clock (one op per lane per cycle)
+    seed_upd_total_ms = upd_ms * (K - 1)
+    roof_hbm = {"kernel": "pq_seed_update_w_kernel<4> (k-means++ weight update, 255 launches per training)",
+                "bound": "hbm", "achieved": achieved, "peak": HBM_PEAK, "unit": "GB/s",
+                "frac": achieved / HBM_PEAK, "traffic": traffic,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth), of measured",
+                "algorithmic_bytes_per_launch": bytes_per_launch, "avg_launch_ms": upd_ms,
+                "sampled_launches": upd_samples, "device_ms_per_training": seed_upd_total_ms}
+    list_launches = sum(s.list_launches for s in stats)
+    list_ms = sum(s.list_ms for s in stats) / max(1, list_launches)
+    list_dist = sum(s.list_distances for s in stats) / max(1, list_launches)
+    list_flops = list_dist * 3 * (DIM // PQ_M)
+    list_tf = list_flops / (max(list_ms, 1e-9) / 1e3) / 1e12
+    tl = traffic_json.get("pq_list_pass_bytes_per_launch")
+    roof_fp32 = {"kernel": "pruned Lloyd pass (iterations >= 1: bound check + exact scans of the unsettled rows)",
+                 "bound": "fp32", "achieved": list_tf, "peak": fp32_peak, "unit": "TFLOP/s",
+                 "frac": list_tf / fp32_peak,
+                 "traffic": tl * (n_rows * m_local) / (N_ROWS * PQ_M) if tl else None,
+                 "peak_source": ("nominal FP32 issue rate: 148 SMs x 128 lanes x the sampled SM clock "
+                                 "(MEASURED_PEAKS.json has no FP32 figure)"),
+                 "algorithmic_flops_per_launch": list_flops, "distances_per_launch": list_dist,
+                 "avg_launch_ms": list_ms, "launches": list_launches,
+                 "device_ms_per_training": list_ms * max(1, list_launches) / max(1, len(stats))}
+    if roof_fp32["device_ms_per_training"] > seed_upd_total_ms:
+        roofline, roofline_other = roof_fp32, roof_hbm
+    else:
+        roofline, roofline_other = roof_hbm, roof_fp32
+    enc_flops = n * K * 3 * DIM
+    enc_bytes = n * (4 * DIM + PQ_M)
+    encode_roofline = {
+        "kernel": "pq.encode (default path)", "ms": enc_ms, "algorithmic_flops": enc_flops,
+        "fp32_tflops": enc_flops / (enc_ms / 1e3) / 1e12, "fp32_frac": enc_flops / (enc_ms / 1e3) / 1e12 / fp32_peak,
+        "hbm_bytes": enc_bytes, "hbm_gbs": enc_bytes / (enc_ms / 1e3) / 1e9,
+        "hbm_frac": enc_bytes / (enc_ms / 1e3) / 1e9 / HBM_PEAK, "paths_ms": enc_paths}
 
     tac_line = None
     if not args.no_tac:  # collective when world > 1: every rank takes part
@@ -502,13 +595,9 @@ def run_b200(args) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False,
-            "scaling": "strong" if world > 1 else "weak",
+            "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows": n_total, "rows_per_gpu": n, "dim": DIM, "pq_m": PQ_M,
-                       "centroids": K, "lloyd_iters": ITERS,
-                       "parallelism": (("subspace-sharded" if PQ_M >= world else "row-sharded")
-                                       + f" over {world} GPUs (NCCL)") if world > 1 else "1gpu",
-                       "l2": "inputs (389 MB) > L2, no flush"},
+            "config": config_dict(world, n),
             "codebook_sha256": mdist.codebook_digest(cb_host),
             "pq_train_ms": train_ms, "seed_ms": seed_ms, "lloyd_ms": lloyd_ms,
             "lloyd_only_s_per_iter": lloyd_ms / 1e3 / ITERS,
@@ -520,15 +609,8 @@ def run_b200(args) -> None:
                              "rows_exact_fraction": rows_exact / max(1, rows_total),
                              "note": ("iterations after the first skip (row, subspace) pairs whose exact "
                                       "distance bounds prove the cluster unchanged")},
-            "roofline": {"kernel": "pq_seed_update_w_kernel<4> (k-means++ weight update, 254 launches per training)",
-                         "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
-                         "algorithmic_bytes_per_launch": bytes_per_launch,
-                         "avg_launch_ms": upd_ms, "sampled_launches": upd_samples},
-            "fp32_assign": {"kernel": "first Lloyd pass (pq_tc_assign_kernel + pq_hist_kernel)",
-                            "algorithmic_flops": flops_per_launch, "ms": first_ms,
-                            "tflops": flops_per_launch / (first_ms / 1e3) / 1e12, "fp32_issue_peak_tflops": fp32_peak},
+            "roofline": roofline, "roofline_secondary": roofline_other, "encode_roofline": encode_roofline,
+            "pruned_passes": {"launches": list_launches, "avg_ms": list_ms, "distances_per_launch": list_dist},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(cb_host.nbytes),
                     "encode_mvec_s": n_total / e2e_enc_s / 1e6},
@@ -538,12 +620,30 @@ def run_b200(args) -> None:
         if hnsw_line is not None:
             line["hnsw"] = hnsw_line
         if world == 1 and not args.no_cpu:
-            cpu = cpu_lloyd_seconds_per_iter(x, host_threads(), target_s=args.cpu_target_s)
-            line["cpu_baseline"] = {
-                "value": cpu["s_per_iter"], "unit": UNIT, "cores": host_threads(), "kind": "port",
-                "sample": (f"1 Lloyd iteration of all 16 subspaces over {cpu['rows']} rows, scaled to "
-                           f"{N_ROWS}; Lloyd only (seeding excluded, GPU value includes it)")}
+            threads = host_threads()
+            cpu = cpu_train_seconds_per_iter(x, threads, target_s=args.cpu_target_s)
+            lloyd = cpu_lloyd_seconds_per_iter(x, threads, target_s=min(args.cpu_target_s, 10.0))
+            line["cpu_baseline"] = {"value": cpu["s_per_iter"], "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": cpu["sample"], "lloyd_only_s_per_iter": lloyd["s_per_iter"]}
+        if world == 1 and not args.no_parity:
+            # the benched codebooks and codes against the C restatement of the
+            # reference on the same rows (after timing; all host threads)
+            from oracle import oracle
+
+            oracle.build()
+            t0 = time.perf_counter()
+            want_cb = oracle.pq_train(x, DIM, SEED, PQ_M, n_threads=host_threads(), max_iters=ITERS,
+                                      tol=-math.inf)
+            want_codes = oracle.pq_encode(want_cb, DIM, PQ_M, x, n_threads=host_threads())
+            line["pq_bit_exact_vs_cpu"] = {
+                "codebooks": bool(want_cb.tobytes() == cb_host.tobytes()),
+                "codes": bool(np.array_equal(want_codes.reshape(-1), codes_host.numpy().reshape(-1))),
+                "rows": int(n), "cpu_wall_s": time.perf_counter() - t0,
+                "what": (f"oracle pq.train ({ITERS} Lloyd iterations, all rows) + PQ.encode of all rows vs "
+                         "the benched codebooks and codes")}
         print(json.dumps(line), flush=True)
+        # one short line that survives a tail: digests to compare across GPU counts
+        print(f"codebook_sha256 {line['codebook_sha256']} n_gpus {world} value {value:.6g}", flush=True)
     ctx.close()
     if dist is not None:
         dist.barrier()
@@ -559,6 +659,8 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-target-s", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the full-size check of the benched codebooks and codes against the oracle")
     ap.add_argument("--no-tac", action="store_true", help="skip the clusterFlat measurement")
     ap.add_argument("--no-hnsw", action="store_true", help="skip the hnsw.build measurement")
     ap.add_argument("--tac-only", action="store_true",

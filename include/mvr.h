@@ -141,9 +141,12 @@ int mvr_kmeans_fit(mvr_ctx* ctx, const float* vectors, uint64_t vectors_len,
  *     that loads the library keeps until the process exits;
  *   - limits: dim in {1, 2, 4}, k <= 256, n <= MVR_NOALLOC_MAX_ROWS rows;
  *     larger inputs return MVR_E_INVALID_ARGUMENT before any GPU work.
- * The first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any
- * stream capture on the device. All calls share the one array, so calls that
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture on the
+ * device. The address belongs to the device's CUDA context: a call made
+ * under another context (after cudaDeviceReset, or with a context made
+ * current through the driver API) looks it up again. Devices other than
+ * sm_100 return MVR_E_NO_DEVICE. All calls share the one array, so calls that
  * overlap on the GPU (other streams, other threads) race: serialise them.
  * The array keeps the last call's contents; the call initialises everything
  * it reads. */
@@ -180,6 +183,12 @@ typedef struct mvr_pq_train_stats {
   double seed_update_ms_sampled;  /* summed device time of every 8th k-means++ update
                                      launch (steps >= 1) */
   uint32_t seed_update_samples;   /* launches in that sum */
+  double list_ms;                 /* summed device time of the pruned Lloyd passes
+                                     (iterations >= 1: bound checks and the distance
+                                     scans of the rows the bounds did not settle) */
+  uint32_t list_launches;         /* pruned passes timed in list_ms */
+  uint64_t list_distances;        /* exact (row, centroid) distances those passes
+                                     computed */
 } mvr_pq_train_stats;
 
 /* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`
@@ -387,6 +396,15 @@ int mvr_ctx_set_tensor_filter(mvr_ctx* ctx, int on);
  * whose near-ties were settled by exact distances. Synchronises the
  * context's stream; MVR_E_TIMEOUT if an MMA did not complete. */
 int mvr_ctx_filter_report(mvr_ctx* ctx, uint64_t* violations, uint64_t* rows_rechecked);
+
+/* Polls of a bounded device wait before it gives up: the stage waits of the
+ * clusterFlat spread kernel's bulk-copy ring. No reference counterpart; for
+ * tests of the expiry path. `polls` = 0 gives up at the first wait (the call
+ * then returns MVR_E_TIMEOUT after the kernel has waited, with the default
+ * limit, for its copies still in flight); MVR_WAIT_LIMIT_DEFAULT restores
+ * the normal limit. */
+#define MVR_WAIT_LIMIT_DEFAULT 4194304u
+int mvr_ctx_set_wait_limit(mvr_ctx* ctx, uint32_t polls);
 
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);

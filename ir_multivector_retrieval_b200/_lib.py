@@ -16,6 +16,8 @@ import numpy as np
 LIB_PATH = Path(__file__).resolve().parent / "libmvr_b200.so"
 
 # Status codes of include/mvr.h, named after the reference's Zig errors.
+WAIT_LIMIT_DEFAULT = 4194304  # MVR_WAIT_LIMIT_DEFAULT in include/mvr.h
+
 STATUS_NAMES = {
     0: "Ok",
     1: "KmeansBudgetTooSmall",
@@ -79,6 +81,9 @@ class PqTrainStats(C.Structure):
         ("filter_violations", C.c_uint32),
         ("seed_update_ms_sampled", C.c_double),
         ("seed_update_samples", C.c_uint32),
+        ("list_ms", C.c_double),
+        ("list_launches", C.c_uint32),
+        ("list_distances", C.c_uint64),
     ]
 
 
@@ -154,6 +159,7 @@ SIGNATURES = {
     ),
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_tensor_filter": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_set_wait_limit": (C.c_int, [_P, C.c_uint32]),
     "mvr_ctx_filter_report": (C.c_int, [_P, _U64, _U64]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),

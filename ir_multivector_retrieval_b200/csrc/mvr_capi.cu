@@ -237,6 +237,12 @@ int mvr_ctx_set_tensor_filter(mvr_ctx* h, int on) {
   return MVR_OK;
 }
 
+int mvr_ctx_set_wait_limit(mvr_ctx* h, uint32_t polls) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.wait_limit = polls;
+  return MVR_OK;
+}
+
 int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_rechecked) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;

@@ -70,6 +70,9 @@ struct Ctx {
   // [0] violations, [1] rows re-scanned, [2] timeouts
   uint32_t* tc_diag = nullptr;
   uint32_t tc_viol_seen = 0;  // violations already answered by an exact re-run
+  // polls of the clusterFlat spread kernel's stage waits before it gives up
+  // (MVR_WAIT_LIMIT_DEFAULT; tests lower it to make the wait run out)
+  uint32_t wait_limit = MVR_WAIT_LIMIT_DEFAULT;
 };
 
 // Host->device copy through the pinned stages (pageable sources: the source

@@ -10,6 +10,7 @@
 // scratch comes from `g_noalloc_scratch`, a fixed array compiled into this
 // library. Every GPU that loads the library holds that array until the
 // process exits.
+#include <cuda.h>  // driver types only: the two driver calls below come from cudaGetDriverEntryPointByVersion
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -31,24 +32,83 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device, looked up once
-// per device (the first call on a device does this; it should come before
-// any stream capture on that device).
+// The array's device address belongs to the CUDA context that loaded this
+// module, not to the device number: after cudaDeviceReset, or when a host
+// makes another context current through the driver API, the old address is
+// gone. Each device slot therefore remembers the unique id of the context
+// its address was looked up in, and a call made under another context looks
+// it up again.
+struct ScratchSlot {
+  unsigned long long ctx_id = 0;  // 0: not looked up (or no context id available)
+  void* addr = nullptr;
+  int arch_ok = -1;               // -1 unknown, 0 not an sm_100 device, 1 sm_100
+};
+ScratchSlot g_slot[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult(CUDAAPI*)(CUcontext*);
+using CtxGetIdFn = CUresult(CUDAAPI*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context, 0 when there is none or
+// the driver does not provide the calls (then every call looks the address
+// up again, which is always correct). Caller holds g_setup_mutex.
+unsigned long long current_context_id() {
+  static bool looked_up = false;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  if (!looked_up) {
+    looked_up = true;
+    cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", reinterpret_cast<void**>(&get_current), 12000,
+                                         cudaEnableDefault, &q1) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess)
+      get_current = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", reinterpret_cast<void**>(&get_id), 12000, cudaEnableDefault,
+                                         &q2) != cudaSuccess ||
+        q2 != cudaDriverEntryPointSuccess)
+      get_id = nullptr;
+    (void)cudaGetLastError();
+  }
+  if (!get_current || !get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch in the current device's current
+// context. Looked up on the first call on a device (that call should come
+// before any stream capture on the device) and again whenever the current
+// context is not the one of the cached address. The device must be an
+// sm_100 GPU, the only architecture this library is built for.
 int scratch_address(int device, unsigned char** out) {
   if (device < 0 || device >= kMaxDevices) return MVR_E_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_addr[device]) {
+  ScratchSlot& s = g_slot[device];
+  if (s.arch_ok < 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return MVR_E_NO_DEVICE;
+    }
+    s.arch_ok = (major == 10 && minor == 0) ? 1 : 0;
+  }
+  if (!s.arch_ok) return MVR_E_NO_DEVICE;
+  const unsigned long long id = current_context_id();
+  if (id == 0 || s.addr == nullptr || s.ctx_id != id) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
       (void)cudaGetLastError();
+      s.addr = nullptr;
+      s.ctx_id = 0;
       return MVR_E_CUDA;
     }
-    g_scratch_addr[device] = p;
+    s.addr = p;
+    s.ctx_id = current_context_id();  // the lookup binds the device's context if none was current
   }
-  *out = static_cast<unsigned char*>(g_scratch_addr[device]);
+  *out = static_cast<unsigned char*>(s.addr);
   return MVR_OK;
 }
 

@@ -2402,6 +2402,13 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         if (e) cudaEventDestroy(e);
     }
   } ev_guard{aev};
+  std::vector<cudaEvent_t> lev;  // pruned-pass brackets (stats only)
+  if (timing) {
+    lev.resize(2 * (size_t)job.max_iters, nullptr);
+    for (auto& e : lev) MVR_CUDA(ctx, cudaEventCreate(&e));
+  }
+  EvGuard lev_guard{lev};
+  uint32_t list_passes = 0;
   // Bound pruning (Hamerly) from the second iteration on; exact, see
   // bound_upper / bound_lower.
   const bool prune = !(ctx && ctx->exhaustive_assign);
@@ -2444,6 +2451,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     } else {
       pq_drift_kernel<<<M, 256, 0, st>>>(cb_old, cb, M, K, S, d_state, drift, maxd);
       MVR_CUDA(ctx, cudaMemsetAsync(lcnt, 0, (size_t)M * sizeof(uint32_t), st));
+      if (timing) MVR_CUDA(ctx, cudaEventRecord(lev[2 * list_passes], st));
       const dim3 cg(pgx, (unsigned)M);
       switch (S) {
         case 1: pq_prune_check_kernel<1><<<cg, 256, 0, st>>>(XT, N, K, cb, asg, ubnd, lbnd, drift, maxd, d_state, plist, lcnt, mind, need_mind ? 1 : 0); break;
@@ -2465,6 +2473,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         }
       }
       MVR_CUDA(ctx, cudaGetLastError());
+      if (timing) MVR_CUDA(ctx, cudaEventRecord(lev[2 * list_passes + 1], st));
+      ++list_passes;
       pq_hist_kernel<<<nblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, rpc, hist);
       MVR_CUDA(ctx, cudaGetLastError());
       launches += 5;
@@ -2569,6 +2579,14 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       out.stats->seed_update_ms_sampled = su;
       out.stats->seed_update_samples = ns;
       out.stats->assign_launches = job.max_iters;
+      double lm = 0.0;
+      for (uint32_t q = 0; q < list_passes; ++q) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, lev[2 * q], lev[2 * q + 1]);
+        lm += t;
+      }
+      out.stats->list_ms = lm;
+      out.stats->list_launches = list_passes;
       if (job.max_iters > 0) {
         float t0 = 0.f;
         cudaEventElapsedTime(&t0, aev[0], aev[1]);
@@ -2583,6 +2601,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       out.stats->lloyd_rows_exact += hex[m];
       out.stats->lloyd_rows_total += (uint64_t)(job.max_iters ? hiters[m] : 0) * N;
     }
+    // the first pass scans every row of every subspace; the rest were listed
+    if (prune && job.max_iters > 1 && out.stats->lloyd_rows_exact >= (uint64_t)M * N)
+      out.stats->list_distances = (out.stats->lloyd_rows_exact - (uint64_t)M * N) * (uint64_t)K;
     for (int m = 0; m < M; ++m) {
       const uint32_t v = job.max_iters ? hiters[m] : 0;
       mx = std::max(mx, v);

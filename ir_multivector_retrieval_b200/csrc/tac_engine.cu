@@ -44,20 +44,21 @@ namespace {
 // single CTA keeps several stages in flight; other d use 4-byte cp.async.
 // The f32 count after q rows is min(q, 2^24) exactly (x + 1 rounds back to
 // 2^24 there), so the threads form a whole stage's 1/count values at once.
-// Every mbarrier wait is bounded; on expiry the kernel raises *err and
-// leaves the token.
+// Every mbarrier wait is bounded (kSpWaitLimit polls, or the context's
+// test-only limit for the stage waits); on expiry the kernel waits for its
+// copies still in flight, raises *err and leaves.
 constexpr int kSpStages = 6;
 constexpr int kSpStageFloats = 4096;
 constexpr int kSpMaxRows = 1024;  // rows per stage at most
-constexpr uint32_t kSpWaitLimit = 1u << 22;
+constexpr uint32_t kSpWaitLimit = MVR_WAIT_LIMIT_DEFAULT;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = kSpWaitLimit) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t it = 0; it < kSpWaitLimit; ++it) {
+  for (uint32_t it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -71,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 __global__ void __launch_bounds__(256)
 tac_spread_kernel(const float* __restrict__ G, uint32_t d, const uint32_t* __restrict__ goff, uint64_t nd,
-                  float* __restrict__ spreads, int* __restrict__ err) {
+                  float* __restrict__ spreads, int* __restrict__ err, uint32_t wait_limit) {
   extern __shared__ __align__(128) float sp_ring[];
   __shared__ float sm2[256];
   __shared__ __align__(8) uint64_t bars[kSpStages];
@@ -130,7 +131,7 @@ tac_spread_kernel(const float* __restrict__ G, uint32_t d, const uint32_t* __res
     for (uint32_t stg = 0; stg < nst; ++stg) {
       const uint32_t g = first + stg, slot = g % kSpStages;
       if (tma) {
-        if (!mbar_wait_bounded(&bars[slot], (g / kSpStages) & 1u)) bad = true;
+        if (!mbar_wait_bounded(&bars[slot], (g / kSpStages) & 1u, wait_limit)) bad = true;
       } else {
         cp_async_wait<kSpStages - 2>();
       }
@@ -186,7 +187,9 @@ tac_spread_kernel(const float* __restrict__ G, uint32_t d, const uint32_t* __res
     }
     if (!tma) cp_async_wait<0>();
     if (bad) {
-      // drain: wait (bounded) for every stage still in flight, then leave
+      // drain: wait for every stage still in flight (with the full limit,
+      // whatever the first wait's limit was), then leave: no bulk copy may
+      // land in shared memory after the CTA has exited
       if (tma)
         for (uint32_t g = first; g < issued; ++g) (void)mbar_wait_bounded(&bars[g % kSpStages], (g / kSpStages) & 1u);
       if (tid == 0) atomicExch(err, 1);
@@ -208,7 +211,7 @@ int launch_spreads(Ctx* c, const float* d_G, uint32_t d, const uint32_t* d_goff,
   const unsigned threads = (d + 31) / 32 * 32;
   const unsigned grid = (unsigned)std::min<uint64_t>(nd, 1u << 30);
   MVR_CUDA(c, cudaFuncSetAttribute(tac_spread_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  tac_spread_kernel<<<grid, threads, smem, c->stream>>>(d_G, d, d_goff, nd, d_sp, d_err);
+  tac_spread_kernel<<<grid, threads, smem, c->stream>>>(d_G, d, d_goff, nd, d_sp, d_err, c->wait_limit);
   MVR_CUDA(c, cudaGetLastError());
   return MVR_OK;
 }

@@ -336,6 +336,50 @@ static float lloyd_step(const float* vectors, uint64_t n, uint64_t d,
   return wcss;
 }
 
+/* The k-means++ weight update of one step (kmeans.zig:128-135): per row,
+ * independent of the others, so static row chunks on n_threads threads give
+ * the same bytes as the serial loop (the reference runs it serially). */
+typedef struct seed_job {
+  const float* vectors;
+  const float* cc;
+  float* min_dist;
+  uint64_t lo, hi, d;
+} seed_job;
+
+static void seed_slice(const seed_job* j) {
+  for (uint64_t i = j->lo; i < j->hi; ++i) {
+    const float dist = orc_l2sq(j->vectors + i * j->d, j->cc, (uint32_t)j->d);
+    if (dist < j->min_dist[i]) j->min_dist[i] = dist;
+  }
+}
+
+static void* seed_thread(void* p) {
+  seed_slice((const seed_job*)p);
+  return NULL;
+}
+
+static void seed_update(const float* vectors, uint64_t n, uint64_t d, const float* cc, float* min_dist,
+                        uint32_t n_threads) {
+  uint64_t t = n_threads <= 1 || n < 8192 ? 1 : (n_threads < n ? n_threads : n);
+  if (t <= 1) {
+    seed_job j = {vectors, cc, min_dist, 0, n, d};
+    seed_slice(&j);
+    return;
+  }
+  seed_job jobs[64];
+  pthread_t th[64];
+  if (t > 64) t = 64;
+  const uint64_t chunk = (n + t - 1) / t;
+  for (uint64_t i = 0; i < t; ++i) {
+    uint64_t lo = i * chunk, hi = lo + chunk;
+    if (lo > n) lo = n;
+    if (hi > n) hi = n;
+    jobs[i] = (seed_job){vectors, cc, min_dist, lo, hi, d};
+    pthread_create(&th[i], NULL, seed_thread, &jobs[i]);
+  }
+  for (uint64_t i = 0; i < t; ++i) pthread_join(th[i], NULL);
+}
+
 /* kmeans.fit (src/tac/kmeans.zig:67-232). `trace`, if not NULL, receives
  * the assignments of every Lloyd iteration (max_iters * n u32). */
 int orc_kmeans_fit(const float* vectors, uint64_t vectors_len, uint32_t dim,
@@ -376,11 +420,7 @@ int orc_kmeans_fit(const float* vectors, uint64_t vectors_len, uint32_t dim,
       return st;
     }
     memcpy(centroids + c * d, vectors + idx * d, sizeof(float) * d);
-    const float* cc = centroids + c * d;
-    for (uint64_t i = 0; i < n; ++i) {
-      const float dist = orc_l2sq(vectors + i * d, cc, dim);
-      if (dist < min_dist[i]) min_dist[i] = dist;
-    }
+    seed_update(vectors, n, d, centroids + c * d, min_dist, n_threads);
   }
   free(min_dist);
 
@@ -887,6 +927,143 @@ int orc_tac_spreads(const uint32_t* token_ids, uint64_t n_tokens,
   return MVR_OK;
 }
 
+static int g_workers = 1;
+void orc_set_workers(int n) { g_workers = n > 1 ? n : 1; }
+
+/* runOneTokenKmeans (src/tac/tac.zig:458-514): gather the token's rows in
+ * index order, kmeans.fit(k_j, seed ^ j), scatter centroids and global
+ * assignments. */
+static int cluster_one_token(const float* vectors, uint32_t dim, uint64_t j, const uint32_t* offsets,
+                             const uint32_t* indices, const uint32_t* kappa_per_token, const uint32_t* goff,
+                             uint32_t max_iters, float tol, uint64_t seed, uint32_t inner, float* gather,
+                             float* cent, uint32_t* asg, float* centroids, uint32_t* assignments, float* w) {
+  const uint32_t k_j = kappa_per_token[j];
+  const uint32_t n_j = offsets[j + 1] - offsets[j];
+  *w = 0.0f;
+  if (k_j == 0 || n_j == 0) return MVR_OK;
+  for (uint32_t q = 0; q < n_j; ++q)
+    memcpy(gather + (uint64_t)q * dim, vectors + (uint64_t)indices[offsets[j] + q] * dim, sizeof(float) * dim);
+  const int st = orc_kmeans_fit(gather, (uint64_t)n_j * dim, dim, k_j, max_iters, tol, seed ^ (uint64_t)j, inner,
+                                cent, asg, w, NULL, NULL);
+  if (st) return st;
+  memcpy(centroids + (uint64_t)goff[j] * dim, cent, sizeof(float) * (uint64_t)k_j * dim);
+  for (uint32_t q = 0; q < n_j; ++q) assignments[indices[offsets[j] + q]] = goff[j] + asg[q];
+  return MVR_OK;
+}
+
+typedef struct token_pool {
+  const float* vectors;
+  uint32_t dim;
+  const uint32_t* offsets;
+  const uint32_t* indices;
+  const uint32_t* kappa;
+  const uint32_t* goff;
+  uint32_t max_iters;
+  float tol;
+  uint64_t seed;
+  const uint64_t* order;
+  uint64_t count;
+  uint64_t next;
+  uint32_t max_n, max_k;
+  float* centroids;
+  uint32_t* assignments;
+  float* token_wcss;
+  int status;
+  pthread_mutex_t mu;
+} token_pool;
+
+static void* token_worker(void* p) {
+  token_pool* tp = (token_pool*)p;
+  float* gather = (float*)malloc(sizeof(float) * (uint64_t)(tp->max_n ? tp->max_n : 1) * tp->dim);
+  float* cent = (float*)malloc(sizeof(float) * (uint64_t)(tp->max_k ? tp->max_k : 1) * tp->dim);
+  uint32_t* asg = (uint32_t*)malloc(sizeof(uint32_t) * (tp->max_n ? tp->max_n : 1));
+  for (;;) {
+    pthread_mutex_lock(&tp->mu);
+    const uint64_t q = tp->next++;
+    const int stop = tp->status != MVR_OK;
+    pthread_mutex_unlock(&tp->mu);
+    if (stop || q >= tp->count) break;
+    const uint64_t j = tp->order[q];
+    float w = 0.0f;
+    const int st = cluster_one_token(tp->vectors, tp->dim, j, tp->offsets, tp->indices, tp->kappa, tp->goff,
+                                     tp->max_iters, tp->tol, tp->seed, 1, gather, cent, asg, tp->centroids,
+                                     tp->assignments, &w);
+    tp->token_wcss[j] = w;
+    if (st) {
+      pthread_mutex_lock(&tp->mu);
+      if (tp->status == MVR_OK) tp->status = st;
+      pthread_mutex_unlock(&tp->mu);
+    }
+  }
+  free(gather);
+  free(cent);
+  free(asg);
+  return NULL;
+}
+
+static const uint64_t* g_sort_work;
+static int cmp_work_desc(const void* a, const void* b) {
+  const uint64_t x = g_sort_work[*(const uint64_t*)a], y = g_sort_work[*(const uint64_t*)b];
+  if (x != y) return x > y ? -1 : 1;
+  const uint64_t i = *(const uint64_t*)a, k = *(const uint64_t*)b;
+  return i < k ? -1 : (i > k);
+}
+
+static int cluster_tokens_parallel(const float* vectors, uint32_t dim, uint64_t nd, const uint32_t* freqs,
+                                   const uint32_t* offsets, const uint32_t* indices, const uint32_t* kappa,
+                                   const uint32_t* goff, uint32_t max_iters, float tol, uint64_t seed,
+                                   float* centroids, uint32_t* assignments, float* token_wcss) {
+  uint64_t* work = (uint64_t*)calloc(nd ? nd : 1, sizeof(uint64_t));
+  uint64_t* order = (uint64_t*)malloc(sizeof(uint64_t) * (nd ? nd : 1));
+  uint64_t total = 0, cnt = 0;
+  uint32_t max_n = 0, max_k = 0;
+  for (uint64_t j = 0; j < nd; ++j) {
+    if (!freqs[j] || !kappa[j]) continue;
+    work[j] = (uint64_t)freqs[j] * ((uint64_t)kappa[j] + 1);
+    total += work[j];
+    order[cnt++] = j;
+  }
+  g_sort_work = work;
+  qsort(order, cnt, sizeof(uint64_t), cmp_work_desc);
+  int st = MVR_OK;
+  uint64_t first_small = 0;
+  /* big tokens one at a time with all workers inside kmeans.fit */
+  while (first_small < cnt && work[order[first_small]] * (uint64_t)g_workers >= total) {
+    const uint64_t j = order[first_small++];
+    const uint32_t n_j = offsets[j + 1] - offsets[j];
+    float* gather = (float*)malloc(sizeof(float) * (uint64_t)n_j * dim);
+    float* cent = (float*)malloc(sizeof(float) * (uint64_t)kappa[j] * dim);
+    uint32_t* asg = (uint32_t*)malloc(sizeof(uint32_t) * n_j);
+    float w = 0.0f;
+    st = cluster_one_token(vectors, dim, j, offsets, indices, kappa, goff, max_iters, tol, seed,
+                           (uint32_t)g_workers, gather, cent, asg, centroids, assignments, &w);
+    token_wcss[j] = w;
+    free(gather);
+    free(cent);
+    free(asg);
+    if (st) break;
+  }
+  if (st == MVR_OK && first_small < cnt) {
+    for (uint64_t q = first_small; q < cnt; ++q) {
+      const uint64_t j = order[q];
+      const uint32_t n_j = offsets[j + 1] - offsets[j];
+      if (n_j > max_n) max_n = n_j;
+      if (kappa[j] > max_k) max_k = kappa[j];
+    }
+    token_pool tp = {vectors, dim, offsets, indices, kappa, goff, max_iters, tol, seed, order + first_small,
+                     cnt - first_small, 0, max_n, max_k, centroids, assignments, token_wcss, MVR_OK,
+                     PTHREAD_MUTEX_INITIALIZER};
+    pthread_t th[256];
+    const int t = g_workers < 256 ? g_workers : 256;
+    for (int i = 0; i < t; ++i) pthread_create(&th[i], NULL, token_worker, &tp);
+    for (int i = 0; i < t; ++i) pthread_join(th[i], NULL);
+    st = tp.status;
+  }
+  free(work);
+  free(order);
+  return st;
+}
+
 /* clusterFlat (src/tac/tac.zig:563-838) with runOneTokenKmeans
  * (:458-514). wcss_total follows the reference's static per-thread token
  * chunks (:712-825) when n_threads > 1. */
@@ -942,24 +1119,26 @@ int orc_tac_cluster_flat(const uint32_t* token_ids, uint64_t n_tokens,
     if (freqs[j] > max_n) max_n = freqs[j];
     if (kappa_per_token[j] > max_k) max_k = kappa_per_token[j];
   }
-  gather = (float*)malloc(sizeof(float) * (uint64_t)max_n * dim);
-  cent = (float*)malloc(sizeof(float) * (uint64_t)(max_k ? max_k : 1) * dim);
-  asg = (uint32_t*)malloc(sizeof(uint32_t) * (max_n ? max_n : 1));
   token_wcss = (float*)calloc(nd, sizeof(float));
-  for (uint64_t j = 0; j < nd; ++j) {
-    const uint32_t k_j = kappa_per_token[j];
-    const uint32_t n_j = offsets[j + 1] - offsets[j];
-    if (k_j == 0 || n_j == 0) continue;
-    for (uint32_t q = 0; q < n_j; ++q)
-      memcpy(gather + (uint64_t)q * dim,
-             vectors + (uint64_t)indices[offsets[j] + q] * dim, sizeof(float) * dim);
-    float w = 0.0f;
-    st = orc_kmeans_fit(gather, (uint64_t)n_j * dim, dim, k_j, max_iters, tol,
-                        seed ^ (uint64_t)j, 1, cent, asg, &w, NULL, NULL);
+  if (g_workers > 1) {
+    /* Test-speed path, same bytes: tokens are independent k-means problems
+     * writing disjoint outputs, so they run on g_workers threads; a token
+     * with a large share of the work runs alone with its assignment and
+     * seeding loops split over all workers (per-row work: identical). */
+    st = cluster_tokens_parallel(vectors, dim, nd, freqs, offsets, indices, kappa_per_token, goff,
+                                 max_iters, tol, seed, centroids, assignments, token_wcss);
     if (st) goto done;
-    memcpy(centroids + (uint64_t)goff[j] * dim, cent, sizeof(float) * (uint64_t)k_j * dim);
-    for (uint32_t q = 0; q < n_j; ++q) assignments[indices[offsets[j] + q]] = goff[j] + asg[q];
-    token_wcss[j] = w;
+  } else {
+    gather = (float*)malloc(sizeof(float) * (uint64_t)max_n * dim);
+    cent = (float*)malloc(sizeof(float) * (uint64_t)(max_k ? max_k : 1) * dim);
+    asg = (uint32_t*)malloc(sizeof(uint32_t) * (max_n ? max_n : 1));
+    for (uint64_t j = 0; j < nd; ++j) {
+      float w = 0.0f;
+      st = cluster_one_token(vectors, dim, j, offsets, indices, kappa_per_token, goff, max_iters, tol, seed, 1,
+                             gather, cent, asg, centroids, assignments, &w);
+      if (st) goto done;
+      token_wcss[j] = w;
+    }
   }
   {
     float total = 0.0f;

@@ -23,6 +23,9 @@ void orc_set_reduce_tree(int tree);
 /* Lane count of vec.l2sqGeneric (`std.simd.suggestVectorLength(f32)`,
  * 4 on the reference's Apple NEON hosts). Default 4. */
 void orc_set_lane_count(int lanes);
+/* Worker threads of orc_tac_cluster_flat (tokens in parallel; results are
+ * the same bytes for any count; 1 = the serial loop). Test speed only. */
+void orc_set_workers(int n);
 
 float orc_l2sq(const float* a, const float* b, uint32_t len);
 int64_t orc_argmin(const float* v, uint64_t n);

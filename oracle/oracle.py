@@ -46,6 +46,7 @@ def load() -> C.CDLL:
             sig = {
                 "orc_set_reduce_tree": (None, [C.c_int]),
                 "orc_set_lane_count": (None, [C.c_int]),
+                "orc_set_workers": (None, [C.c_int]),
                 "orc_l2sq": (C.c_float, [_P, _P, C.c_uint32]),
                 "orc_argmin": (C.c_int64, [_P, C.c_uint64]),
                 "orc_argmax": (C.c_int64, [_P, C.c_uint64]),
@@ -280,7 +281,11 @@ class ClusterResult:
 
 
 def tac_cluster_flat(token_ids, vectors, dim: int, kappa_total: int, seed: int, mu=128, tau=256,
-                     eps=4, theta=39, max_iters=25, tol=1e-4, n_threads=1) -> ClusterResult:
+                     eps=4, theta=39, max_iters=25, tol=1e-4, n_threads=1, workers: int = 1) -> ClusterResult:
+    """clusterFlat restated. `n_threads` is the reference's thread count (it
+    only changes how wcss_total is chunked, tac.zig:712-825); `workers` runs
+    the per-token k-means on that many host threads (same bytes)."""
+    load().orc_set_workers(int(workers))
     ids = _u32(token_ids)
     v = _f32(vectors)
     nd = int(ids.max()) + 1 if ids.size else 1

@@ -177,30 +177,6 @@ def test_device_pointer_entry_points(ctx, orc):
     assert st.iters_max == 8 and st.total_ms > 0
 
 
-def test_full_size_train_and_encode(ctx, orc):
-    """BASELINE configs[1] shape: 1,521,797 x 64, M=16 x 4. Bit-exact against
-    the oracle for 2 Lloyd iterations (seeding included), plus size-free
-    properties after 20 iterations."""
-    n = 1_521_797
-    c = synth.make_corpus(n, 64, seed=42)
-    x = synth.anchor_residuals(c)
-    got = pq.train(x, 64, 42 + 0xA1B2C3D4, pq_m=16, max_iters=2, tol=-math.inf, ctx=ctx)
-    want = orc.pq_train(x, 64, 42 + 0xA1B2C3D4, 16, n_threads=THREADS, max_iters=2, tol=-math.inf)
-    assert got.codebooks.tobytes() == want.tobytes()
-    codes = got.encode_batch(x)
-    sample = np.random.default_rng(0).choice(n, 50_000, replace=False)
-    assert np.array_equal(codes[sample], orc.pq_encode(got.codebooks, 64, 16, x[sample], n_threads=THREADS))
-    stats = {}
-    p20 = pq.train(x, 64, 42 + 0xA1B2C3D4, pq_m=16, max_iters=20, tol=-math.inf, ctx=ctx, stats=stats)
-    assert stats["iters_min"] == 20 and np.isfinite(p20.codebooks).all()
-    codes = p20.encode_batch(x)
-    assert np.array_equal(p20.encode_batch(p20.decode(codes)), codes)
-    # Lloyd fixed point drift: 20 iterations never raise the quantisation error
-    def mse(p):
-        return float(np.mean((p.decode(p.encode_batch(x[sample])) - x[sample]) ** 2))
-    assert mse(p20) <= mse(got) + 1e-7
-
-
 def _seq4(v):
     q = (v.astype(np.float32) ** 2).astype(np.float32)
     return np.float32(np.float32(np.float32(q[0] + q[1]) + q[2]) + q[3])

@@ -263,3 +263,22 @@ def test_kmeans_long_problem_wcss(ctx, orc, kind):
     for k, tol, iters in ((12, 1e-4, 25), (40, 0.0, 6)):
         _check_kmeans(ctx, orc, x, dim, k, seed=k, max_iters=iters, tol=tol)
     _check_kmeans(ctx, orc, synth.unit_rows(36_000, 64, seed=6), 64, 80, seed=1, max_iters=10, tol=1e-4)
+
+
+def test_spread_wait_expiry_reports_timeout(ctx, orc):
+    """The bounded mbarrier wait of the spread kernel's bulk-copy ring, made
+    to run out (the test-only limit of 0 polls): the call fails with
+    MVR_E_TIMEOUT after the kernel has waited for its copies still in
+    flight, and the context stays usable: the next call is bit-exact."""
+    from ir_multivector_retrieval_b200 import _lib
+
+    c = synth.make_corpus(20_000, 64, seed=20_064)
+    p = tac.ClusteringParams(4096, 42, theta=10)
+    ctx.check(ctx.lib.mvr_ctx_set_wait_limit(ctx.handle, 0))
+    try:
+        with pytest.raises(MvrError) as e:
+            tac.cluster_flat(c.token_ids, c.vectors, 64, p, ctx=ctx)
+        assert e.value.code == 102  # MVR_E_TIMEOUT
+    finally:
+        ctx.check(ctx.lib.mvr_ctx_set_wait_limit(ctx.handle, _lib.WAIT_LIMIT_DEFAULT))
+    _check_cluster(ctx, orc, c.token_ids, c.vectors, 64, 4096, 42, theta=10)
