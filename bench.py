@@ -546,7 +546,12 @@ def run_b200(args) -> None:
     t = traffic_json.get("pq_seed_update_bytes_per_launch")
     traffic = t * (n_rows * m_local) / (N_ROWS * PQ_M) if t else None
     sm_mhz = clk.get("sm_mhz") or 1965.0
-    fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12  # FP32 lanes x clock (one op per lane per cycle)
+    fp32_nominal = 148 * 128 * sm_mhz * 1e6 / 1e12  # scalar FP32 lanes x clock
+    # measured packed f32x2 add/mul issue rate of this GPU (the exact distance
+    # kernels' instructions; about twice the scalar rate on B200)
+    rate = C.c_double(0.0)
+    ctx.check(lib.mvr_measure_f32x2_rate(ctx.handle, C.byref(rate)))
+    fp32_peak = rate.value / 1e12
     seed_upd_total_ms = upd_ms * (K - 1)
     roof_hbm = {"kernel": "pq_seed_update_w_kernel<4> (k-means++ weight update, 255 launches per training)",
                 "bound": "hbm", "achieved": achieved, "peak": HBM_PEAK, "unit": "GB/s",
@@ -564,8 +569,10 @@ def run_b200(args) -> None:
                  "bound": "fp32", "achieved": list_tf, "peak": fp32_peak, "unit": "TFLOP/s",
                  "frac": list_tf / fp32_peak,
                  "traffic": tl * (n_rows * m_local) / (N_ROWS * PQ_M) if tl else None,
-                 "peak_source": ("nominal FP32 issue rate: 148 SMs x 128 lanes x the sampled SM clock "
-                                 "(MEASURED_PEAKS.json has no FP32 figure)"),
+                 "peak_source": ("measured on this GPU in this run: packed f32x2 add/mul lane operations per "
+                                 "second (mvr_measure_f32x2_rate; MEASURED_PEAKS.json has no FP32 figure), "
+                                 "of measured; one algorithmic flop counted per lane operation"),
+                 "scalar_fp32_nominal_tflops": fp32_nominal,
                  "algorithmic_flops_per_launch": list_flops, "distances_per_launch": list_dist,
                  "avg_launch_ms": list_ms, "launches": list_launches,
                  "device_ms_per_training": list_ms * max(1, list_launches) / max(1, len(stats))}

@@ -383,6 +383,13 @@ int mvr_ctx_set_serial_draws(mvr_ctx* ctx, int on);
  * Results are identical either way; only the speed differs. */
 int mvr_ctx_set_exhaustive_assign(mvr_ctx* ctx, int on);
 
+/* Verification mode (no reference counterpart): with `on` == 0 the pruned
+ * Lloyd passes of pq.train scan all K centroids of every row whose bounds
+ * fail; by default (`on` != 0) such a row scans only the centroids whose
+ * distance from its current centroid is within twice its distance bound
+ * (the rest provably cannot win). Results are identical either way. */
+int mvr_ctx_set_candidate_scan(mvr_ctx* ctx, int on);
+
 /* Verification mode (no reference counterpart): with `on` == 0 the Lloyd
  * and encode assignments skip the tensor-core filter (a TF32 MMA chain that
  * approximates every distance within a proven bound, after which only the
@@ -405,6 +412,13 @@ int mvr_ctx_filter_report(mvr_ctx* ctx, uint64_t* violations, uint64_t* rows_rec
  * the normal limit. */
 #define MVR_WAIT_LIMIT_DEFAULT 4194304u
 int mvr_ctx_set_wait_limit(mvr_ctx* ctx, uint32_t polls);
+
+/* Measured FP32 issue rate of the context's GPU, in lane operations per
+ * second: independent chains of packed f32x2 adds and multiplies (the
+ * instructions of the exact distance kernels) on every SM, best of two runs
+ * after a warm-up. No reference counterpart; the benchmark's FP32 rooflines
+ * divide by it. Synchronises the context's stream. */
+int mvr_measure_f32x2_rate(mvr_ctx* ctx, double* lane_ops_per_s);
 
 /* Wait for all work on the context's stream; reports device-side errors. */
 int mvr_ctx_sync(mvr_ctx* ctx);

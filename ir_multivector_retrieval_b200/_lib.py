@@ -160,6 +160,8 @@ SIGNATURES = {
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_tensor_filter": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_wait_limit": (C.c_int, [_P, C.c_uint32]),
+    "mvr_ctx_set_candidate_scan": (C.c_int, [_P, C.c_int]),
+    "mvr_measure_f32x2_rate": (C.c_int, [_P, C.POINTER(C.c_double)]),
     "mvr_ctx_filter_report": (C.c_int, [_P, _U64, _U64]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),
     "mvr_comm_unique_id": (C.c_int, [_P, C.c_size_t]),

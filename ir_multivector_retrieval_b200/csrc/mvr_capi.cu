@@ -257,6 +257,12 @@ int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_reche
   return dg[2] ? mvr::fail(c, MVR_E_TIMEOUT, "tensor-core filter: an MMA did not complete in time") : MVR_OK;
 }
 
+int mvr_ctx_set_candidate_scan(mvr_ctx* h, int on) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.cand_scan = on != 0;
+  return MVR_OK;
+}
+
 int mvr_ctx_set_exhaustive_assign(mvr_ctx* h, int on) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   h->impl.exhaustive_assign = on != 0;

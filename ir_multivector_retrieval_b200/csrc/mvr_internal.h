@@ -66,6 +66,9 @@ struct Ctx {
   bool exhaustive_assign = false;
   // tensor-core filtered assignment passes (off: the exact scans only)
   bool tc_filter = true;
+  // pruned Lloyd passes scan only the candidate centroids near the current
+  // one (off: the bound check + full scans of the failing rows)
+  bool cand_scan = true;
   // device counters of the filtered encode passes (created on first use):
   // [0] violations, [1] rows re-scanned, [2] timeouts
   uint32_t* tc_diag = nullptr;

@@ -261,6 +261,35 @@ def test_bound_pruning_matches_exhaustive(ctx, orc):
         assert pruned.codebooks.tobytes() == want.tobytes()
 
 
+def test_candidate_scan_matches_full_scans(ctx, orc):
+    """Pruned Lloyd passes that scan only the centroids near a row's current
+    one give the same bytes as full scans of the failing rows and as the
+    oracle, on adversarial sets (exact duplicates, quantised grids with many
+    equal distances, magnitudes over many binades, non-finite-free but huge
+    rows) and with fewer centroids than the neighbour table (kmeans.fit)."""
+    for name, x, dim, m in _filter_datasets():
+        for iters, tol in ((12, -math.inf), (25, 1e-4)):
+            st_c, st_f = {}, {}
+            got = pq.train(x, dim, 9, pq_m=m, max_iters=iters, tol=tol, ctx=ctx, stats=st_c)
+            ctx.check(ctx.lib.mvr_ctx_set_candidate_scan(ctx.handle, 0))
+            try:
+                full = pq.train(x, dim, 9, pq_m=m, max_iters=iters, tol=tol, ctx=ctx, stats=st_f)
+            finally:
+                ctx.check(ctx.lib.mvr_ctx_set_candidate_scan(ctx.handle, 1))
+            assert got.codebooks.tobytes() == full.codebooks.tobytes(), name
+            assert st_c["iters_max"] == st_f["iters_max"], name
+            want = orc.pq_train(x, dim, 9, m, n_threads=THREADS, max_iters=iters, tol=tol)
+            assert got.codebooks.tobytes() == want.tobytes(), name
+    for dim, k in ((4, 9), (2, 31), (4, 33), (1, 256)):
+        xs = synth.unit_rows(7_000, dim, seed=k) if dim > 1 else \
+            np.random.default_rng(k).standard_normal(7_000).astype(np.float32)
+        g = kmeans.fit(xs, dim, kmeans.KMeansParams(k=k, seed=k, max_iters=15, tol=-math.inf), ctx=ctx)
+        w = orc.kmeans_fit(xs, dim, k, k, max_iters=15, tol=-math.inf)
+        assert np.array_equal(g.assignments, w.assignments)
+        assert g.centroids.tobytes() == np.ascontiguousarray(w.centroids, dtype=np.float32).tobytes()
+        assert np.float32(g.wcss).tobytes() == np.float32(w.wcss).tobytes()
+
+
 def _filter_report(ctx):
     import ctypes as C
 
