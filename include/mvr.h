@@ -64,6 +64,12 @@ enum {
   MVR_E_TABLE_SIZE_MISMATCH = 20,    /* refine.RefineError.TableSizeMismatch */
   MVR_E_DOC_OUT_OF_RANGE = 21,       /* refine.RefineError.DocOutOfRange */
   MVR_E_DOC_LAYOUT_CORRUPT = 22,     /* refine.RefineError.DocLayoutCorrupt */
+  MVR_E_INVALID_INDEX = 23,          /* storage.StorageError.InvalidIndex */
+  MVR_E_UNSUPPORTED_VERSION = 24,    /* storage.StorageError.UnsupportedVersion */
+  MVR_E_INDEX_CORRUPT = 25,          /* storage.StorageError.IndexCorrupt */
+  MVR_E_ASSIGNMENT_OUT_OF_RANGE = 26, /* inverted_list.InvertedListError.AssignmentOutOfRange */
+  MVR_E_DOC_OFFSETS_BAD = 27,        /* inverted_list.InvertedListError.DocOffsetsBad */
+  MVR_E_KAPPA_ZERO = 28,             /* inverted_list.InvertedListError.KappaZero */
   /* B200-side failures with no reference counterpart */
   MVR_E_CUDA = 100,             /* a CUDA runtime call failed */
   MVR_E_NCCL = 101,             /* an NCCL call failed */
@@ -525,6 +531,68 @@ int mvr_tac_allocate_budgets(const uint32_t* freqs, const float* spreads,
                              uint32_t* kappa, float* frac, uint64_t n,
                              uint32_t kappa_total,
                              const mvr_clustering_params* p);
+
+/* ------------------------------------------------------------------------
+ * Inverted lists and the .tac index image (src/index/inverted_list.zig,
+ * src/index/storage.zig)
+ * ------------------------------------------------------------------------ */
+
+/* Replaces `inverted_list.build(assignments, doc_offsets, kappa, gpa)`
+ * (src/index/inverted_list.zig:54-150) on the GPU: for each centroid j the
+ * ascending ids of the documents with at least one token assigned to j
+ * (one entry per document). `doc_offsets` has `doc_offsets_len` = n_docs + 1
+ * entries (CSR token ranges). Outputs: `offsets_out` kappa + 1 u64 (from 0),
+ * `payload_out` the doc ids, `payload_cap` entries available (n_tokens
+ * always suffices); `payload_len_out` = offsets_out[kappa]. Errors in the
+ * reference's order: MVR_E_KAPPA_ZERO, MVR_E_DOC_OFFSETS_BAD (empty
+ * offsets, more than 2^32 - 1 docs, last offset != n_tokens, first != 0,
+ * decreasing), MVR_E_ASSIGNMENT_OUT_OF_RANGE; MVR_E_BUFFER_TOO_SMALL when
+ * the payload does not fit. All pointers are host memory. */
+int mvr_inverted_lists_build(mvr_ctx* ctx, const uint32_t* assignments, uint64_t n_tokens,
+                             const uint64_t* doc_offsets, uint64_t doc_offsets_len, uint32_t kappa,
+                             uint64_t* offsets_out, uint32_t* payload_out, uint64_t payload_cap,
+                             uint64_t* payload_len_out);
+
+/* The parts of a built index, the reference's `BuildOutput`
+ * (storage.zig:127-148), as plain host arrays. `pq_m` is the subspace count
+ * (the reference's comptime PQ_M; the header records it and a reader checks
+ * it). The HNSW graph is given as the reference's `Hnsw` fields
+ * (hnsw.zig:136-170): `hnsw_layer_offsets[L]` (n + 1 u32) and
+ * `hnsw_layer_neighbours[L]` (offsets[L][n] u32) for L = 0 .. max_level. */
+typedef struct mvr_tac_parts {
+  uint32_t dim, kappa, sub_dim, pq_m;
+  uint64_t n_docs, n_tokens;
+  const float* centroids;          /* kappa * dim (normalised, as storage.build stores them) */
+  const uint32_t* assignments;     /* n_tokens */
+  const uint8_t* pq_codes;         /* n_tokens * pq_m */
+  const uint64_t* doc_offsets;     /* n_docs + 1 */
+  const float* codebooks;          /* pq_m * 256 * sub_dim */
+  uint32_t hnsw_n, hnsw_entry_point, hnsw_max_level;
+  const uint8_t* hnsw_node_levels; /* hnsw_n */
+  const uint32_t* const* hnsw_layer_offsets;
+  const uint32_t* const* hnsw_layer_neighbours;
+  const uint64_t* ilist_offsets;   /* kappa + 1 */
+  const uint32_t* ilist_payload;   /* ilist_offsets[kappa] */
+  const float* residual_norms;     /* n_tokens */
+} mvr_tac_parts;
+
+/* On-disk header region (storage.zig:75-77): the 112-byte Header padded to
+ * 128 bytes. Magic "TAC_IDX1", version 2 (constants.zig:43-45). */
+#define MVR_TAC_HEADER_REGION 128u
+#define MVR_TAC_VERSION 2u
+
+/* Replaces `storage.computeSize` (storage.zig:495-528): bytes of the image. */
+int mvr_tac_file_size(const mvr_tac_parts* parts, uint64_t* bytes_out);
+
+/* Replaces `storage.serialise` (storage.zig:560-665) with `writeHnsw`
+ * (:667-703) and `writeDocLayouts` (:705-749): header, centroids, HNSW, PQ
+ * codebooks, inverted lists, per-doc layouts (interleaved on the GPU),
+ * doc token offsets, residual norms, each section padded to 8 bytes, then
+ * the footer CRC-32 of everything before it (std.hash.Crc32) and 4 zero
+ * bytes. `buf` (host, `buf_len` >= mvr_tac_file_size) receives the image;
+ * MVR_E_BUFFER_TOO_SMALL otherwise. */
+int mvr_tac_serialise(mvr_ctx* ctx, const mvr_tac_parts* parts, void* buf, uint64_t buf_len,
+                      uint64_t* written_out);
 
 /* ------------------------------------------------------------------------
  * HNSW over the TAC centroids (src/index/hnsw.zig)

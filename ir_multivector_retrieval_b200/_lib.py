@@ -42,6 +42,12 @@ STATUS_NAMES = {
     20: "TableSizeMismatch",
     21: "DocOutOfRange",
     22: "DocLayoutCorrupt",
+    23: "InvalidIndex",
+    24: "UnsupportedVersion",
+    25: "IndexCorrupt",
+    26: "AssignmentOutOfRange",
+    27: "DocOffsetsBad",
+    28: "KappaZero",
     100: "CudaError",
     101: "NcclError",
     102: "Timeout",

@@ -163,6 +163,12 @@ const char* mvr_status_name(int s) {
     case MVR_E_TABLE_SIZE_MISMATCH: return "TableSizeMismatch";
     case MVR_E_DOC_OUT_OF_RANGE: return "DocOutOfRange";
     case MVR_E_DOC_LAYOUT_CORRUPT: return "DocLayoutCorrupt";
+    case MVR_E_INVALID_INDEX: return "InvalidIndex";
+    case MVR_E_UNSUPPORTED_VERSION: return "UnsupportedVersion";
+    case MVR_E_INDEX_CORRUPT: return "IndexCorrupt";
+    case MVR_E_ASSIGNMENT_OUT_OF_RANGE: return "AssignmentOutOfRange";
+    case MVR_E_DOC_OFFSETS_BAD: return "DocOffsetsBad";
+    case MVR_E_KAPPA_ZERO: return "KappaZero";
     case MVR_E_CUDA: return "CudaError";
     case MVR_E_NCCL: return "NcclError";
     case MVR_E_TIMEOUT: return "Timeout";

@@ -480,39 +480,43 @@ pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, co
 
 // ---------------------------------------------------------------------------
 // Candidate-pruned Lloyd pass (iterations >= 1): the bound check above fused
-// with a scan of only the centroids that can still win.
+// with a scan of only the centroids near the row's current one.
 //
-// For a row x whose bounds fail, with current cluster a and
+// pq_nbr_kernel lists, for every centroid a, its kCandL nearest other
+// centroids in increasing v_j, v_j <= |c_a - c_j| a lower bound (f64 with
+// directed rounding). A row x whose bounds fail, with current cluster a and
 // ut = bound_upper(f_a) >= |x - c_a| (f_a its exact f32 distance to c_a),
-// every centroid c_j satisfies |x - c_j| >= |c_a - c_j| - ut >= v_j - ut,
-// v_j <= |c_a - c_j| a lower bound from pq_nbr_kernel. The row scans the
-// neighbours of c_a in increasing v_j while v_j <= T with
-//   T = RU(RU(ut (2 + 2^-18)) + 2^-50).
-// A centroid left out has v_j > T, so sqrt(D_j) > ut (1 + 2^-18) + 2^-50 with
-// D_j its exact squared distance: D_j > D_a (1 + 2^-17) and D_j > 2^-100.
-// The f32 distances are within (1 +- g) of D (g = 2^-21, plus absolute
-// underflow terms below 2^-145), so f_j > f_a >= f_w for the scanned winner
-// w: no left-out centroid can be the minimum or tie with it, and the first
-// minimum among the scanned centroids (smallest index on equal values) is
-// the reference's first-index argmin over all K. Lower bound for the next
-// iteration: the smaller of bound_lower(second smallest scanned distance)
-// and RD(v_next - ut), v_next the first neighbour left out.
+// gets the exact f32 distances to all kCandL listed neighbours. Every
+// centroid c_j off the list has v_j >= v_last (the list's last entry) and
+//   |x - c_j| >= |c_a - c_j| - |x - c_a| >= v_last - ut.
+// When v_last > T = RU(RU(ut (2 + 2^-18)) + 2^-50), that is
+// |x - c_j| > ut (1 + 2^-18) + 2^-50: the exact squared distance D_j exceeds
+// D_a (1 + 2^-17) and 2^-100, and since the f32 distances are within
+// (1 +- g) of D (g = 2^-21, plus underflow terms below 2^-145), f_j > f_a >=
+// f_w for the winner w among the scanned centroids. No centroid off the
+// list can be the minimum or tie with it, so the first minimum among a and
+// the listed neighbours (smallest index on equal values) is the reference's
+// first-index argmin over all K. Otherwise (v_last <= T), or when x, f_a or
+// a codeword is not finite, the row gets the full scan of all K in index
+// order (a NaN distance to centroid 0 wins, as vec.argmin starts from
+// dists[0]). Lower bound for the next iteration: the smaller of
+// bound_lower(second smallest scanned distance) and RD(v_last - ut).
 //
-// The neighbour table keeps the kCandL nearest centroids of each centroid;
-// a row whose cutoff lies beyond the table, or whose values are not finite,
-// or a subspace with a non-finite codeword, takes the full scan of all K
-// (one warp per row, the reference's first-index rule; a NaN distance to
-// centroid 0 wins, as vec.argmin starts from dists[0]).
-//
-// A CTA owns one subspace (blockIdx.y): codebook and neighbour table in
-// shared memory, rows in chunks of kCandThreads. Phase A checks the bounds
-// (one thread per row) and compacts the rows that need a scan into a
-// shared-memory queue; phase B scans them with one lane per queued row.
+// Work layout: each warp checks the bounds of 32 rows at a time (one lane
+// per row) and appends the rows that need a scan to a warp-private queue in
+// shared memory; whenever the queue holds 4 rows, the warp scans them with
+// 8 lanes per row (4 listed neighbours per lane, then a 3-step shuffle
+// reduction of (best, index, runner-up)). No block barrier after the
+// codebook and neighbour table are staged.
 // ---------------------------------------------------------------------------
 constexpr int kCandThreads = 256;
-constexpr int kCandL = 32;                       // neighbours per centroid in the table
+constexpr int kCandWarps = kCandThreads / 32;
+constexpr int kCandL = 32;                       // listed neighbours per centroid (8 lanes x 4)
+constexpr int kCandStride = kCandL + 1;          // shared-memory row stride of the table
+constexpr int kCandQ = 40;                       // warp queue capacity (< 4 left + 32 new)
 constexpr float kCandCut = 2.0f + 0x1p-18f;      // 1 + kPruneMargin
 constexpr float kCandFloor = 0x1p-50f;
+constexpr uint32_t kNoKey = 0xFFFFFFFFu;
 
 // Lower bound of |a - b| (f64, a and b floats): 0 when the sign is unsure.
 __device__ __forceinline__ double abs_diff_rd(double a, double b) {
@@ -527,13 +531,13 @@ __device__ __forceinline__ uint32_t nbr_key(float v, int j) {
   return (b >= 0x200u ? ((b & ~0xFFu) - 0x100u) : 0u) | (uint32_t)j;
 }
 
-// nbr[m][a][0..L): the L smallest keys of centroid a's neighbours (itself
-// included, at distance 0). One warp per (m, a); each lane holds 8
-// candidates sorted in registers, L rounds of a warp minimum pop them.
+// nbr[m][a][0..kCandL): keys of the min(kCandL, K - 1) nearest centroids
+// other than a, ascending; unused slots hold kNoKey. One warp per (m, a);
+// each lane holds 8 candidates sorted in registers, rounds of a warp
+// minimum pop them in order.
 template <int S>
 __global__ void __launch_bounds__(256)
-pq_nbr_kernel(const float* __restrict__ cb, int K, int L, const uint8_t* __restrict__ state,
-              uint32_t* __restrict__ nbr) {
+pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ state, uint32_t* __restrict__ nbr) {
   const int m = blockIdx.y;
   if (state[m] != kRunning) return;
   const int lane = threadIdx.x & 31, a = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -546,8 +550,8 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, int L, const uint8_t* __restr
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int j = lane * 8 + q;
-    key[q] = 0xFFFFFFFFu;
-    if (j < K) {
+    key[q] = kNoKey;
+    if (j < K && j != a) {
       double d2 = 0.0;
 #pragma unroll
       for (int k = 0; k < S; ++k) {
@@ -555,11 +559,10 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, int L, const uint8_t* __restr
         d2 = __dadd_rd(d2, __dmul_rd(t, t));
       }
       float v = __double2float_rd(__dsqrt_rd(d2));
-      if (!(v >= 0.f) || j == a) v = 0.f;  // non-finite codewords: the scan kernel takes full scans
+      if (!(v >= 0.f)) v = 0.f;  // non-finite codewords: the scan kernel takes full scans
       key[q] = nbr_key(v, j);
     }
   }
-  // sort the lane's 8 keys (insertion; small and branch-free enough)
 #pragma unroll
   for (int i = 1; i < 8; ++i)
 #pragma unroll
@@ -568,21 +571,18 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, int L, const uint8_t* __restr
       key[k - 1] = lo;
       key[k] = hi;
     }
-  uint32_t mine[2] = {0xFFFFFFFFu, 0xFFFFFFFFu};
+  uint32_t mine = kNoKey;
+  const int L = min(kCandL, K - 1);
   for (int i = 0; i < L; ++i) {
     const uint32_t mn = __reduce_min_sync(0xffffffffu, key[0]);
     if (key[0] == mn) {  // keys are unique (the index is in the low bits): one lane pops
 #pragma unroll
       for (int q = 0; q < 7; ++q) key[q] = key[q + 1];
-      key[7] = 0xFFFFFFFFu;
+      key[7] = kNoKey;
     }
-    if (lane == (i & 31)) mine[i >> 5] = mn;
+    if (lane == i) mine = mn;
   }
-  uint32_t* out = nbr + ((size_t)m * K + a) * L;
-  for (int h = 0; h < 2; ++h) {
-    const int i = lane + 32 * h;
-    if (i < L) out[i] = mine[h];
-  }
+  nbr[((size_t)m * K + a) * kCandL + lane] = mine;
 }
 
 template <int S>
@@ -596,33 +596,54 @@ __device__ __forceinline__ void load_centroid(const float* sC, int j, float (&c)
   }
 }
 
-size_t cand_smem(int K, int L, int S) {
+// (best, index, runner-up) of one lane merged into its 8-lane group; equal
+// values keep the smaller index, the loser's best joins the runner-up.
+__device__ __forceinline__ void group_merge(float& b, int& bi, float& sc, unsigned gmask) {
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(gmask, b, o);
+    const int oi = __shfl_xor_sync(gmask, bi, o);
+    const float os = __shfl_xor_sync(gmask, sc, o);
+    if (ob < b || (ob == b && oi < bi)) {
+      sc = fminf(fminf(sc, b), os);
+      b = ob;
+      bi = oi;
+    } else {
+      sc = fminf(fminf(sc, ob), os);
+    }
+  }
+}
+
+size_t cand_smem(int K, int S) {
   const size_t cbytes = ((size_t)K * S * 4 + 15) & ~(size_t)15;
-  const size_t tbytes = (((size_t)K * (L + 1) * 4) + 15) & ~(size_t)15;
-  return cbytes + tbytes + (size_t)kCandThreads * (16 + 12);
+  const size_t tbytes = (((size_t)K * kCandStride * 4) + 15) & ~(size_t)15;
+  const size_t dbytes = ((size_t)K * 4 + 15) & ~(size_t)15;
+  return cbytes + tbytes + dbytes + (size_t)kCandWarps * kCandQ * (16 + 12);
 }
 
 template <int S>
-__global__ void __launch_bounds__(kCandThreads)
-pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, int L, const float* __restrict__ cb,
+__global__ void __launch_bounds__(kCandThreads, 4)
+pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __restrict__ cb,
                const uint32_t* __restrict__ nbr, uint8_t* __restrict__ asg, float* __restrict__ ubnd,
                float* __restrict__ lbnd, const float* __restrict__ drift, const float* __restrict__ maxd,
                const uint8_t* __restrict__ state, float* __restrict__ mind, int need_mind,
                uint32_t* __restrict__ list_cnt, unsigned long long* __restrict__ dist_cnt) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ uint32_t s_qn;
   __shared__ int s_bad;
   const int m = blockIdx.y;
   if (state[m] != kRunning) return;
   const size_t cbytes = ((size_t)K * S * 4 + 15) & ~(size_t)15;
-  const size_t tbytes = (((size_t)K * (L + 1) * 4) + 15) & ~(size_t)15;
-  float* sC = reinterpret_cast<float*>(smem_raw);                              // [K][S]
-  uint32_t* sT = reinterpret_cast<uint32_t*>(smem_raw + cbytes);              // [K][L+1]
-  float4* qx = reinterpret_cast<float4*>(smem_raw + cbytes + tbytes);          // [kCandThreads]
-  float* qd = reinterpret_cast<float*>(qx + kCandThreads);                     // exact distance to c_a
-  uint32_t* qr = reinterpret_cast<uint32_t*>(qd + kCandThreads);               // row
-  uint32_t* qa = qr + kCandThreads;                                            // current cluster
+  const size_t tbytes = (((size_t)K * kCandStride * 4) + 15) & ~(size_t)15;
+  const size_t dbytes = ((size_t)K * 4 + 15) & ~(size_t)15;
+  float* sC = reinterpret_cast<float*>(smem_raw);                                // [K][S]
+  uint32_t* sT = reinterpret_cast<uint32_t*>(smem_raw + cbytes);                // [K][kCandStride]
+  float* sD = reinterpret_cast<float*>(smem_raw + cbytes + tbytes);             // drifts [K]
+  unsigned char* qbase = smem_raw + cbytes + tbytes + dbytes;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float4* qx = reinterpret_cast<float4*>(qbase) + warp * kCandQ;                // rows of the queue
+  float* qd = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 16) + warp * kCandQ;
+  uint32_t* qr = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 20) + warp * kCandQ;
+  uint32_t* qa = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 24) + warp * kCandQ;
   if (tid == 0) s_bad = 0;
   __syncthreads();
   {
@@ -632,195 +653,167 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, int L, const flo
       sC[e] = v;
       bad |= !isfinite(v);
     }
-    for (int e = tid; e < K * L; e += kCandThreads) sT[(e / L) * (L + 1) + e % L] = nbr[(size_t)m * K * L + e];
+    for (int e = tid; e < K * kCandL; e += kCandThreads)
+      sT[(e / kCandL) * kCandStride + e % kCandL] = nbr[(size_t)m * K * kCandL + e];
+    for (int c = tid; c < K; c += kCandThreads) sD[c] = drift[(size_t)m * K + c];
     if (bad) atomicOr(&s_bad, 1);
   }
+  __syncthreads();
+  const bool bad_cb = s_bad != 0;
+  const int L = min(kCandL, K - 1);  // listed neighbours; L < kCandL: every centroid is listed
   const float md1 = maxd[3 * m], md2 = maxd[3 * m + 2];
   const uint32_t mi1 = (uint32_t)(int)maxd[3 * m + 1];
-  const float* dm = drift + (size_t)m * K;
-  uint32_t listed = 0;
+  const int g = lane >> 3, gl = lane & 7;
+  const unsigned gmask = 0xFFu << (lane & ~7);
+  uint32_t qn = 0, listed = 0;
   unsigned long long dists = 0;
-  for (uint64_t base = (uint64_t)blockIdx.x * kCandThreads; base < N; base += (uint64_t)gridDim.x * kCandThreads) {
-    if (tid == 0) s_qn = 0;
-    __syncthreads();  // also: the tables are in place, the previous chunk's queue is consumed
-    // ---- phase A: bounds, then one exact distance, else queue the row
-    {
-      const uint64_t r = base + tid;
-      bool queue = false;
-      float x[S];
-      float da = 0.f;
-      uint32_t a = 0;
-      if (r < N) {
-        const size_t e = (size_t)m * N + r;
-        a = asg[e];
-        const float u = __fadd_ru(ubnd[e], dm[a]);
-        const float l = __fsub_rd(lbnd[e], a == mi1 ? md2 : md1);
-        if (l >= kLbMin && __fmul_ru(u, kPruneMargin) < l) {
-          ubnd[e] = u;
-          lbnd[e] = l;
-          if (need_mind) {
-            float c[S];
-            load_sub<S>(XT + e * S, x);
-            load_centroid<S>(sC, (int)a, c);
-            mind[e] = l2_small<S>(x, c);
-          }
+
+  // Scan `cnt` (1..4) rows at the end of the queue, 8 lanes per row.
+  auto scan_rows = [&](uint32_t cnt) {
+    const uint32_t e = qn - cnt + min((uint32_t)g, cnt - 1);
+    const bool act = (uint32_t)g < cnt;
+    const float4 v = qx[e];
+    float x[S];
+    x[0] = v.x;
+    if constexpr (S > 1) x[1] = v.y;
+    if constexpr (S > 2) { x[2] = v.z; x[3] = v.w; }
+    const float da = qd[e];
+    const uint32_t a = qa[e], r = qr[e];
+    float b = gl == 0 ? da : __int_as_float(0x7f800000);
+    int bi = gl == 0 ? (int)a : 0x7fffffff;
+    float sc = __int_as_float(0x7f800000);
+    const uint32_t* row = sT + (size_t)a * kCandStride;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t key = row[gl + 8 * q];
+      if (key != kNoKey) {
+        const int j = (int)(key & 0xFFu);
+        float c[S];
+        load_centroid<S>(sC, j, c);
+        const float f = l2_small<S>(x, c);
+        if (f < b || (f == b && j < bi)) {
+          sc = fminf(sc, b);
+          b = f;
+          bi = j;
         } else {
+          sc = fminf(sc, f);
+        }
+      }
+    }
+    group_merge(b, bi, sc, gmask);
+    const float ut = bound_upper(da);
+    const float vlast = L == kCandL ? __uint_as_float(row[kCandL - 1]) : __int_as_float(0x7f800000);
+    const float T = __fadd_ru(__fmul_ru(ut, kCandCut), kCandFloor);
+    // the listed neighbours decide unless the cutoff reaches past the list
+    const bool full = bad_cb || !(ut <= 3.0e38f) || (L == kCandL && !(vlast > T));
+    float lb;
+    unsigned long long cnt_d = (unsigned long long)L;
+    if (full) {  // every distance, in index order, 32 centroids per lane
+      float fb = __int_as_float(0x7f800000), fs = __int_as_float(0x7f800000), d0 = 0.f;
+      int fi = 0x7fffffff;
+      for (int j = gl * 32; j < min(K, gl * 32 + 32); ++j) {
+        float c[S];
+        load_centroid<S>(sC, j, c);
+        const float f = l2_small<S>(x, c);
+        if (j == 0) d0 = f;
+        const float fk = isnan(f) ? __int_as_float(0x7f800000) : f;
+        if (fk < fb || fi == 0x7fffffff) {
+          fs = fminf(fs, fb);
+          fb = fk;
+          fi = j;
+        } else {
+          fs = fminf(fs, fk);
+        }
+      }
+      group_merge(fb, fi, fs, gmask);
+      d0 = __shfl_sync(gmask, d0, lane & ~7);
+      if (isnan(d0)) {  // vec.argmin starts from dists[0]: a NaN there wins
+        b = d0;
+        bi = 0;
+        lb = -__int_as_float(0x7f800000);
+      } else {
+        b = fb;
+        bi = fi;
+        lb = bound_lower(fs);
+      }
+      cnt_d = (unsigned long long)K;
+    } else {
+      const float lc = L == kCandL ? __fsub_rd(vlast, ut) : __int_as_float(0x7f800000);
+      lb = fminf(bound_lower(sc), lc);
+    }
+    if (act && gl == 0) {
+      const size_t eo = (size_t)m * N + r;
+      asg[eo] = (uint8_t)bi;
+      mind[eo] = b;
+      ubnd[eo] = bound_upper(b);
+      lbnd[eo] = lb;
+      dists += cnt_d + 1;
+    }
+    qn -= cnt;
+    __syncwarp();
+  };
+
+  const uint64_t wstride = (uint64_t)gridDim.x * kCandWarps * 32;
+  for (uint64_t base = ((uint64_t)blockIdx.x * kCandWarps + warp) * 32; base < N; base += wstride) {
+    // ---- bounds of 32 rows; one exact distance when they fail; queue the rest
+    const uint64_t r = base + lane;
+    bool queue = false;
+    float x[S];
+    float da = 0.f;
+    uint32_t a = 0;
+    if (r < N) {
+      const size_t e = (size_t)m * N + r;
+      a = asg[e];
+      const float u = __fadd_ru(ubnd[e], sD[a]);
+      const float l = __fsub_rd(lbnd[e], a == mi1 ? md2 : md1);
+      if (l >= kLbMin && __fmul_ru(u, kPruneMargin) < l) {
+        ubnd[e] = u;
+        lbnd[e] = l;
+        if (need_mind) {
           float c[S];
           load_sub<S>(XT + e * S, x);
           load_centroid<S>(sC, (int)a, c);
-          da = l2_small<S>(x, c);
-          const float ut = bound_upper(da);
-          if (l >= kLbMin && __fmul_ru(ut, kPruneMargin) < l) {
-            ubnd[e] = ut;
-            lbnd[e] = l;
-            mind[e] = da;
-          } else {
-            queue = true;
-          }
+          mind[e] = l2_small<S>(x, c);
         }
-      }
-      const uint32_t qb = __ballot_sync(0xffffffffu, queue);
-      uint32_t wbase = 0;
-      if (lane == 0 && qb) wbase = atomicAdd(&s_qn, (uint32_t)__popc(qb));
-      wbase = __shfl_sync(0xffffffffu, wbase, 0);
-      if (queue) {
-        const uint32_t q = wbase + __popc(qb & lanemask_lt());
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        v.x = x[0];
-        if constexpr (S > 1) v.y = x[1];
-        if constexpr (S > 2) { v.z = x[2]; v.w = x[3]; }
-        qx[q] = v;
-        qd[q] = da;
-        qr[q] = (uint32_t)r;
-        qa[q] = a;
+      } else {
+        float c[S];
+        load_sub<S>(XT + e * S, x);
+        load_centroid<S>(sC, (int)a, c);
+        da = l2_small<S>(x, c);
+        const float ut = bound_upper(da);
+        if (l >= kLbMin && __fmul_ru(ut, kPruneMargin) < l) {
+          ubnd[e] = ut;
+          lbnd[e] = l;
+          mind[e] = da;
+        } else {
+          queue = true;
+        }
       }
     }
-    __syncthreads();
-    const uint32_t qn = s_qn;
-    if (tid == 0) listed += qn;
-    // ---- phase B: one lane per queued row (warps past the queue idle)
-    if ((uint32_t)(warp * 32) < qn) {
-      const bool act = (uint32_t)tid < qn;
-      float x[S], best = 0.f, sec = __int_as_float(0x7f800000), lb = 0.f;
-      int bi = 0;
-      uint32_t r = 0;
-      bool full = false;
-      unsigned long long cnt = 0;
-      if (act) {
-        const float4 v = qx[tid];
-        x[0] = v.x;
-        if constexpr (S > 1) x[1] = v.y;
-        if constexpr (S > 2) { x[2] = v.z; x[3] = v.w; }
-        const uint32_t a = qa[tid];
-        r = qr[tid];
-        best = qd[tid];
-        bi = (int)a;
-        cnt = 1;
-        const float ut = bound_upper(best);
-        full = s_bad || !(ut <= 3.0e38f);  // NaN or inf: the reference's full loop decides
-        float knext = __int_as_float(0x7f800000);
-        if (!full) {
-          const float T = __fadd_ru(__fmul_ru(ut, kCandCut), kCandFloor);
-          const uint32_t* row = sT + (size_t)a * (L + 1);
-          int i = 0;
-          for (; i < L; ++i) {
-            const uint32_t key = row[i];
-            const float kv = __uint_as_float(key);
-            if (kv > T) {
-              knext = kv;
-              break;
-            }
-            const int j = (int)(key & 0xFFu);
-            if (j == (int)a) continue;
-            float c[S];
-            load_centroid<S>(sC, j, c);
-            const float f = l2_small<S>(x, c);
-            ++cnt;
-            if (f < best || (f == best && j < bi)) {
-              sec = best;
-              best = f;
-              bi = j;
-            } else {
-              sec = fminf(sec, f);
-            }
-          }
-          if (i == L && L < K) full = true;  // cutoff beyond the table
-        }
-        if (!full) {
-          const float lc = knext <= 3.0e38f ? __fsub_rd(knext, ut) : __int_as_float(0x7f800000);
-          lb = fminf(bound_lower(sec), lc);
-        }
-      }
-      // rows that need every distance: the warp scans them one at a time
-      unsigned fm = __ballot_sync(0xffffffffu, act && full);
-      while (fm) {
-        const int src = __ffs(fm) - 1;
-        fm &= fm - 1;
-        float xs[S];
-#pragma unroll
-        for (int k = 0; k < S; ++k) xs[k] = __shfl_sync(0xffffffffu, x[k], src);
-        float b = __int_as_float(0x7f800000), sc = __int_as_float(0x7f800000), d0 = 0.f;
-        int ib = 0x7fffffff;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int j = lane * 8 + q;
-          if (j < K) {
-            float c[S];
-            load_centroid<S>(sC, j, c);
-            const float f = l2_small<S>(xs, c);
-            if (j == 0) d0 = f;
-            const float fk = isnan(f) ? __int_as_float(0x7f800000) : f;
-            if (fk < b || ib == 0x7fffffff) {
-              sc = fminf(sc, b);
-              b = fk;
-              ib = j;
-            } else {
-              sc = fminf(sc, fk);
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ob = __shfl_xor_sync(0xffffffffu, b, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, ib, o);
-          const float os = __shfl_xor_sync(0xffffffffu, sc, o);
-          if (ob < b || (ob == b && oi < ib)) {
-            sc = fminf(fminf(sc, b), os);
-            b = ob;
-            ib = oi;
-          } else {
-            sc = fminf(fminf(sc, ob), os);
-          }
-        }
-        d0 = __shfl_sync(0xffffffffu, d0, 0);
-        if (lane == src) {
-          if (isnan(d0)) {  // vec.argmin starts from dists[0]: a NaN there wins
-            best = d0;
-            bi = 0;
-            lb = -__int_as_float(0x7f800000);
-          } else {
-            best = b;
-            bi = ib;
-            lb = bound_lower(sc);
-          }
-          cnt = (unsigned long long)K;
-        }
-      }
-      if (act) {
-        const size_t e = (size_t)m * N + r;
-        asg[e] = (uint8_t)bi;
-        mind[e] = best;
-        ubnd[e] = bound_upper(best);
-        lbnd[e] = lb;
-      }
-      dists += cnt;
+    const uint32_t qb = __ballot_sync(0xffffffffu, queue);
+    if (queue) {
+      const uint32_t q = qn + __popc(qb & lanemask_lt());
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      v.x = x[0];
+      if constexpr (S > 1) v.y = x[1];
+      if constexpr (S > 2) { v.z = x[2]; v.w = x[3]; }
+      qx[q] = v;
+      qd[q] = da;
+      qr[q] = (uint32_t)r;
+      qa[q] = a;
     }
+    qn += __popc(qb);
+    listed += __popc(qb);
+    __syncwarp();
+    while (qn >= 4) scan_rows(4);
   }
-  // per-CTA totals (statistics)
+  if (qn > 0) scan_rows(qn);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) dists += __shfl_xor_sync(0xffffffffu, dists, o);
-  if (lane == 0 && dists) atomicAdd(&dist_cnt[m], dists);
-  if (tid == 0 && listed) atomicAdd(&list_cnt[m], listed);
+  if (lane == 0) {
+    if (dists) atomicAdd(&dist_cnt[m], dists);
+    if (listed) atomicAdd(&list_cnt[m], listed);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2605,7 +2598,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_cbold = carve((size_t)M * K * S * sizeof(float));
   L.o_drift = carve((size_t)M * K * sizeof(float));
   L.o_maxd = carve((size_t)M * 3 * sizeof(float));
-  L.o_nbr = carve((size_t)M * K * std::min(K, kCandL) * sizeof(uint32_t));
+  L.o_nbr = carve((size_t)M * K * kCandL * sizeof(uint32_t));
   L.total_bytes = off;
   return L;
 }
@@ -2768,12 +2761,11 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   // Candidate scans (pq_cand_kernel) replace the check + full-scan list
   // passes unless the context asks for the latter (verification).
   const bool cand = prune && !(ctx && !ctx->cand_scan);
-  const int candL = std::min(K, kCandL);
   uint32_t* nbr = (uint32_t*)(ws + L.o_nbr);
   unsigned long long* d_ldist = (unsigned long long*)(small + L.o_ldist);
-  const size_t csmem = cand_smem(K, candL, S);
+  const size_t csmem = cand_smem(K, S);
   const unsigned cgx = (unsigned)std::max<uint64_t>(
-      1, std::min<uint64_t>((N + kCandThreads - 1) / kCandThreads, (uint64_t)(std::max(1, sms) * 6 + M - 1) / M));
+      1, std::min<uint64_t>((N + kCandThreads - 1) / kCandThreads, (uint64_t)(std::max(1, sms) * 4 + M - 1) / M));
   float* ubnd = (float*)(ws + L.o_ub);
   float* lbnd = (float*)(ws + L.o_lb);
   uint32_t* plist = (uint32_t*)(ws + L.o_list);
@@ -2813,15 +2805,15 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         const dim3 ng((unsigned)((K + 7) / 8), (unsigned)M), cgrid(cgx, (unsigned)M);
         const int nm = need_mind ? 1 : 0;
         switch (S) {
-          case 1: pq_nbr_kernel<1><<<ng, 256, 0, st>>>(cb, K, candL, d_state, nbr); break;
-          case 2: pq_nbr_kernel<2><<<ng, 256, 0, st>>>(cb, K, candL, d_state, nbr); break;
-          default: pq_nbr_kernel<4><<<ng, 256, 0, st>>>(cb, K, candL, d_state, nbr); break;
+          case 1: pq_nbr_kernel<1><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
+          case 2: pq_nbr_kernel<2><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
+          default: pq_nbr_kernel<4><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
         }
         MVR_CUDA(ctx, cudaGetLastError());
         switch (S) {
-          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, candL, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, candL, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, candL, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
         }
         MVR_CUDA(ctx, cudaGetLastError());
       } else {

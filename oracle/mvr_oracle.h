@@ -12,6 +12,10 @@
 
 #include <stdint.h>
 
+/* status codes and the shared parts struct of the .tac image (types only:
+ * the oracle links nothing of the product) */
+#include "../include/mvr.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -144,6 +148,31 @@ int orc_hnsw_search(const orc_hnsw* h, const float* query, uint32_t k, uint32_t 
                     uint32_t* written);
 /* vec.normalizeRowsInPlace */
 void orc_normalize_rows(float* v, uint64_t n_rows, uint32_t dim);
+
+
+/* ---- .tac image and inverted lists (tac_file_oracle.c) ---- */
+uint32_t orc_crc32(const uint8_t* p, uint64_t len);
+int orc_inverted_lists_build(const uint32_t* assignments, uint64_t n_assign, const uint64_t* doc_offsets,
+                             uint64_t doc_offsets_len, uint32_t kappa, uint64_t* offsets, uint32_t* payload,
+                             uint64_t payload_cap, uint64_t* total_out);
+uint64_t orc_tac_file_size(const mvr_tac_parts* p);
+int orc_tac_serialise(const mvr_tac_parts* p, uint8_t* buf, uint64_t len, uint64_t* written);
+
+/* What orc_tac_parse finds: header fields and the byte offset of every
+ * array in the image (HNSW: up to max_level + 1 <= 256 layers). */
+typedef struct orc_tac_view {
+  uint32_t version, dim, kappa, pq_m, pq_bits, sub_dim;
+  uint64_t n_docs, n_tokens;
+  uint64_t centroids_off;
+  uint32_t hnsw_n, hnsw_entry_point, hnsw_max_level;
+  uint64_t hnsw_levels_off;
+  uint64_t hnsw_layer_offsets_off[256], hnsw_layer_neighbours_off[256], hnsw_layer_edges[256];
+  uint64_t pq_off;
+  uint64_t ilist_offsets_off, ilist_payload_off, ilist_total;
+  uint64_t doc_index_off, doc_payload_off, doc_payload_len;
+  uint64_t doc_tok_off, norms_off, footer_off;
+} orc_tac_view;
+int orc_tac_parse(const uint8_t* b, uint64_t len, uint32_t reader_pq_m, orc_tac_view* v);
 
 #ifdef __cplusplus
 }

@@ -80,6 +80,12 @@ def load() -> C.CDLL:
                                                    C.c_uint32, C.c_uint32, C.c_float, C.c_uint64,
                                                    C.c_uint32, _P, _P, _P, C.c_uint64,
                                                    C.POINTER(C.c_uint64), C.POINTER(C.c_float)]),
+                "orc_crc32": (C.c_uint32, [_P, C.c_uint64]),
+                "orc_inverted_lists_build": (C.c_int, [_P, C.c_uint64, _P, C.c_uint64, C.c_uint32, _P, _P,
+                                                       C.c_uint64, C.POINTER(C.c_uint64)]),
+                "orc_tac_file_size": (C.c_uint64, [_P]),
+                "orc_tac_serialise": (C.c_int, [_P, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+                "orc_tac_parse": (C.c_int, [_P, C.c_uint64, C.c_uint32, _P]),
             }
             for name, (res, args) in sig.items():
                 f = getattr(lib, name)
@@ -435,3 +441,132 @@ def normalize_rows(v, dim: int) -> np.ndarray:
     lib.orc_normalize_rows.argtypes = [_P, C.c_uint64, C.c_uint32]
     lib.orc_normalize_rows(_p(x), C.c_uint64(x.size // dim), dim)
     return x
+
+
+# ---------------------------------------------------------------- .tac image
+
+class TacParts(C.Structure):
+    """Mirror of mvr_tac_parts (include/mvr.h): the reference's BuildOutput."""
+
+    _fields_ = [("dim", C.c_uint32), ("kappa", C.c_uint32), ("sub_dim", C.c_uint32), ("pq_m", C.c_uint32),
+                ("n_docs", C.c_uint64), ("n_tokens", C.c_uint64),
+                ("centroids", C.c_void_p), ("assignments", C.c_void_p), ("pq_codes", C.c_void_p),
+                ("doc_offsets", C.c_void_p), ("codebooks", C.c_void_p),
+                ("hnsw_n", C.c_uint32), ("hnsw_entry_point", C.c_uint32), ("hnsw_max_level", C.c_uint32),
+                ("hnsw_node_levels", C.c_void_p), ("hnsw_layer_offsets", C.c_void_p),
+                ("hnsw_layer_neighbours", C.c_void_p), ("ilist_offsets", C.c_void_p),
+                ("ilist_payload", C.c_void_p), ("residual_norms", C.c_void_p)]
+
+
+class TacView(C.Structure):
+    _fields_ = [("version", C.c_uint32), ("dim", C.c_uint32), ("kappa", C.c_uint32), ("pq_m", C.c_uint32),
+                ("pq_bits", C.c_uint32), ("sub_dim", C.c_uint32), ("n_docs", C.c_uint64),
+                ("n_tokens", C.c_uint64), ("centroids_off", C.c_uint64), ("hnsw_n", C.c_uint32),
+                ("hnsw_entry_point", C.c_uint32), ("hnsw_max_level", C.c_uint32), ("hnsw_levels_off", C.c_uint64),
+                ("hnsw_layer_offsets_off", C.c_uint64 * 256), ("hnsw_layer_neighbours_off", C.c_uint64 * 256),
+                ("hnsw_layer_edges", C.c_uint64 * 256), ("pq_off", C.c_uint64), ("ilist_offsets_off", C.c_uint64),
+                ("ilist_payload_off", C.c_uint64), ("ilist_total", C.c_uint64), ("doc_index_off", C.c_uint64),
+                ("doc_payload_off", C.c_uint64), ("doc_payload_len", C.c_uint64), ("doc_tok_off", C.c_uint64),
+                ("norms_off", C.c_uint64), ("footer_off", C.c_uint64)]
+
+
+def crc32(data: bytes) -> int:
+    b = np.frombuffer(data, dtype=np.uint8)
+    return int(load().orc_crc32(_p(b) if b.size else None, b.size))
+
+
+def inverted_lists_build(assignments, doc_offsets, kappa: int):
+    """inverted_list.build restated: (offsets kappa+1 u64, payload u32)."""
+    a = _u32(assignments)
+    off = np.ascontiguousarray(doc_offsets, dtype=np.uint64)
+    offsets = np.zeros(int(kappa) + 1, dtype=np.uint64)
+    payload = np.zeros(max(1, a.size), dtype=np.uint32)
+    total = C.c_uint64(0)
+    _check(load().orc_inverted_lists_build(_p(a) if a.size else None, a.size, _p(off) if off.size else None,
+                                           off.size, int(kappa), _p(offsets), _p(payload), payload.size,
+                                           C.byref(total)), "inverted_lists_build")
+    return offsets, payload[: total.value].copy()
+
+
+def tac_parts(*, dim, kappa, sub_dim, pq_m, centroids, assignments, pq_codes, doc_offsets, codebooks,
+              hnsw_entry_point, hnsw_node_levels, hnsw_layer_offsets, hnsw_layer_neighbours, ilist_offsets,
+              ilist_payload, residual_norms):
+    """A TacParts plus the arrays it points into (keep both alive)."""
+    keep = {
+        "centroids": np.ascontiguousarray(centroids, dtype=np.float32).reshape(-1),
+        "assignments": np.ascontiguousarray(assignments, dtype=np.uint32).reshape(-1),
+        "pq_codes": np.ascontiguousarray(pq_codes, dtype=np.uint8).reshape(-1),
+        "doc_offsets": np.ascontiguousarray(doc_offsets, dtype=np.uint64),
+        "codebooks": np.ascontiguousarray(codebooks, dtype=np.float32).reshape(-1),
+        "levels": np.ascontiguousarray(hnsw_node_levels, dtype=np.uint8),
+        "offs": [np.ascontiguousarray(o, dtype=np.uint32) for o in hnsw_layer_offsets],
+        "nbrs": [np.ascontiguousarray(o, dtype=np.uint32) for o in hnsw_layer_neighbours],
+        "ilo": np.ascontiguousarray(ilist_offsets, dtype=np.uint64),
+        "ilp": np.ascontiguousarray(ilist_payload, dtype=np.uint32),
+        "norms": np.ascontiguousarray(residual_norms, dtype=np.float32).reshape(-1),
+    }
+    L = len(keep["offs"])
+    keep["offp"] = (C.c_void_p * L)(*[o.ctypes.data for o in keep["offs"]])
+    keep["nbrp"] = (C.c_void_p * L)(*[(o.ctypes.data if o.size else keep["offs"][0].ctypes.data)
+                                      for o in keep["nbrs"]])
+    p = TacParts()
+    p.dim, p.kappa, p.sub_dim, p.pq_m = dim, kappa, sub_dim, pq_m
+    p.n_docs = keep["doc_offsets"].size - 1
+    p.n_tokens = keep["assignments"].size
+    p.centroids = keep["centroids"].ctypes.data
+    p.assignments = keep["assignments"].ctypes.data
+    p.pq_codes = keep["pq_codes"].ctypes.data
+    p.doc_offsets = keep["doc_offsets"].ctypes.data
+    p.codebooks = keep["codebooks"].ctypes.data
+    p.hnsw_n = keep["levels"].size
+    p.hnsw_entry_point = hnsw_entry_point
+    p.hnsw_max_level = L - 1
+    p.hnsw_node_levels = keep["levels"].ctypes.data
+    p.hnsw_layer_offsets = C.cast(keep["offp"], C.c_void_p)
+    p.hnsw_layer_neighbours = C.cast(keep["nbrp"], C.c_void_p)
+    p.ilist_offsets = keep["ilo"].ctypes.data
+    p.ilist_payload = keep["ilp"].ctypes.data if keep["ilp"].size else keep["ilo"].ctypes.data
+    p.residual_norms = keep["norms"].ctypes.data
+    return p, keep
+
+
+def tac_serialise(parts_and_keep) -> bytes:
+    """storage.serialise restated: the whole image (computeSize bytes)."""
+    p, _keep = parts_and_keep
+    lib = load()
+    n = int(lib.orc_tac_file_size(C.byref(p)))
+    buf = np.zeros(n, dtype=np.uint8)
+    w = C.c_uint64(0)
+    _check(lib.orc_tac_serialise(C.byref(p), _p(buf), n, C.byref(w)), "tac_serialise")
+    return buf[: w.value].tobytes()
+
+
+def tac_parse(image: bytes, reader_pq_m: int) -> dict:
+    """storage.parse restated: every section as numpy arrays (copies).
+    Raises OracleError with the reference's StorageError code."""
+    b = np.frombuffer(image, dtype=np.uint8)
+    v = TacView()
+    _check(load().orc_tac_parse(_p(b) if b.size else None, b.size, int(reader_pq_m), C.byref(v)), "tac_parse")
+
+    def arr(off, dtype, count):
+        return np.frombuffer(image, dtype=dtype, count=int(count), offset=int(off)).copy()
+
+    n = v.hnsw_n
+    layers_off = [arr(v.hnsw_layer_offsets_off[L], np.uint32, n + 1) for L in range(v.hnsw_max_level + 1)]
+    layers_nbr = [arr(v.hnsw_layer_neighbours_off[L], np.uint32, v.hnsw_layer_edges[L])
+                  for L in range(v.hnsw_max_level + 1)]
+    return {
+        "header": {k: getattr(v, k) for k in ("version", "dim", "kappa", "pq_m", "pq_bits", "sub_dim", "n_docs",
+                                             "n_tokens")},
+        "centroids": arr(v.centroids_off, np.float32, v.kappa * v.dim),
+        "hnsw": {"n": n, "entry_point": v.hnsw_entry_point, "max_level": v.hnsw_max_level,
+                 "node_levels": arr(v.hnsw_levels_off, np.uint8, n), "layer_offsets": layers_off,
+                 "layer_neighbours": layers_nbr},
+        "codebooks": arr(v.pq_off, np.float32, v.pq_m * 256 * v.sub_dim),
+        "ilist_offsets": arr(v.ilist_offsets_off, np.uint64, v.kappa + 1),
+        "ilist_payload": arr(v.ilist_payload_off, np.uint32, v.ilist_total),
+        "doc_index": arr(v.doc_index_off, np.uint64, v.n_docs + 1),
+        "doc_section": bytes(image[v.doc_index_off: v.doc_payload_off + v.doc_payload_len]),
+        "doc_token_offsets": arr(v.doc_tok_off, np.uint64, v.n_docs + 1),
+        "residual_norms": arr(v.norms_off, np.float32, v.n_tokens),
+    }
