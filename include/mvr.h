@@ -303,6 +303,12 @@ int mvr_write_doc_layouts_device(mvr_ctx* ctx, const uint64_t* doc_offsets,
  * host memory; `crc` continues a previous value (0 to start). */
 uint32_t mvr_crc32(uint32_t crc, const void* data, uint64_t len);
 
+/* CRC-32 of A || B from crc(A), crc(B) and the length of B (the GF(2)
+ * combination zlib calls crc32_combine); the footer checksum of
+ * mvr_tac_serialise is computed in chunks on host threads and joined this
+ * way. No reference counterpart. */
+uint32_t mvr_crc32_combine(uint32_t crc1, uint32_t crc2, uint64_t len2);
+
 /* ---- query side: PQ distance table and refine ------------------------- */
 
 /* Replaces PQ.buildDistanceTable (src/index/pq.zig:92-123): out[(m*256 + c)

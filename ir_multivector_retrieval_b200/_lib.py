@@ -93,6 +93,19 @@ class PqTrainStats(C.Structure):
     ]
 
 
+class TacParts(C.Structure):
+    """Mirror of mvr_tac_parts (include/mvr.h): the reference's BuildOutput."""
+
+    _fields_ = [("dim", C.c_uint32), ("kappa", C.c_uint32), ("sub_dim", C.c_uint32), ("pq_m", C.c_uint32),
+                ("n_docs", C.c_uint64), ("n_tokens", C.c_uint64),
+                ("centroids", C.c_void_p), ("assignments", C.c_void_p), ("pq_codes", C.c_void_p),
+                ("doc_offsets", C.c_void_p), ("codebooks", C.c_void_p),
+                ("hnsw_n", C.c_uint32), ("hnsw_entry_point", C.c_uint32), ("hnsw_max_level", C.c_uint32),
+                ("hnsw_node_levels", C.c_void_p), ("hnsw_layer_offsets", C.c_void_p),
+                ("hnsw_layer_neighbours", C.c_void_p), ("ilist_offsets", C.c_void_p),
+                ("ilist_payload", C.c_void_p), ("residual_norms", C.c_void_p)]
+
+
 class TacStats(C.Structure):
     _fields_ = [
         ("total_ms", C.c_double),
@@ -150,6 +163,11 @@ SIGNATURES = {
     "mvr_write_doc_layouts": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
     "mvr_write_doc_layouts_device": (C.c_int, [_P, _P, C.c_uint64, _P, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
     "mvr_crc32": (C.c_uint32, [C.c_uint32, _P, C.c_uint64]),
+    "mvr_crc32_combine": (C.c_uint32, [C.c_uint32, C.c_uint32, C.c_uint64]),
+    "mvr_inverted_lists_build": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64, C.c_uint32, _P, _P, C.c_uint64,
+                                           C.POINTER(C.c_uint64)]),
+    "mvr_tac_file_size": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
+    "mvr_tac_serialise": (C.c_int, [_P, _P, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "mvr_pq_distance_table": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),
     "mvr_pq_distance_table_device": (
         C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint32, _P, C.c_uint64]),

@@ -1499,6 +1499,49 @@ int scan_u32(Ctx* ctx, cudaStream_t st, const uint32_t* in, uint64_t n, uint32_t
 }
 }  // namespace
 
+size_t scan_part_words(uint64_t n) { return (size_t)(n / kScanTile + 2); }
+
+int exclusive_scan_u32(Ctx* ctx, cudaStream_t st, const uint32_t* in, uint64_t n, uint32_t* part, uint32_t* out) {
+  if (n == 0) return MVR_OK;
+  return scan_u32(ctx, st, in, n, part, out);
+}
+
+size_t radix_pairs_scratch_words(uint64_t n) {
+  const uint64_t nblk = (n + kRadixRows - 1) / kRadixRows;
+  return (size_t)(2 * 256 * nblk) + scan_part_words(256 * nblk);
+}
+
+int radix_sort_pairs(Ctx* ctx, cudaStream_t st, const uint32_t* keys, const uint32_t* vals, uint64_t n, int key_bits,
+                     uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, uint32_t* scratch,
+                     const uint32_t** keys_out, const uint32_t** vals_out) {
+  *keys_out = keys;
+  *vals_out = vals;
+  if (n == 0) return MVR_OK;
+  const int nblk = (int)((n + kRadixRows - 1) / kRadixRows);
+  uint32_t* hist = scratch;
+  uint32_t* base = scratch + (size_t)256 * nblk;
+  uint32_t* part = base + (size_t)256 * nblk;
+  const uint32_t* ki = keys;
+  const uint32_t* vi = vals;
+  uint32_t *ko = k0, *vo = v0;
+  const int passes = std::max(1, (key_bits + 7) / 8);
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = 8 * pass;
+    const unsigned g = (unsigned)((nblk + kRadixWarps - 1) / kRadixWarps);
+    km_radix_hist_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, n, shift, nblk, hist);
+    MVR_TRY(scan_u32(ctx, st, hist, (uint64_t)256 * nblk, part, base));
+    km_radix_scatter_kernel<<<g, kRadixWarps * 32, 0, st>>>(ki, vi, n, shift, nblk, base, ko, vo);
+    MVR_CUDA(ctx, cudaGetLastError());
+    ki = ko;
+    vi = vo;
+    ko = ko == k0 ? k1 : k0;
+    vo = vo == v0 ? v1 : v0;
+  }
+  *keys_out = ki;
+  *vals_out = vi;
+  return MVR_OK;
+}
+
 int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, uint32_t dim, const KmBatch& b,
                  uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res) {
   const size_t NP = b.size();

@@ -52,4 +52,17 @@ int km_gather_groups(Ctx* ctx, const float* d_V, const uint32_t* d_idx, uint64_t
 int km_batch_run(Ctx* ctx, const float* d_G, const float* d_GT, uint64_t rows, uint32_t dim, const KmBatch& b,
                  uint32_t max_iters, float tol, float* d_C, uint32_t* d_local, KmResult* res);
 
+// Exclusive prefix sums of n u32 on `st`; `part` holds scan_part_words(n).
+size_t scan_part_words(uint64_t n);
+int exclusive_scan_u32(Ctx* ctx, cudaStream_t st, const uint32_t* in, uint64_t n, uint32_t* part, uint32_t* out);
+
+// Stable LSD radix sort of (key, val) pairs by the low `key_bits` bits of the
+// keys (8 bits per pass; vals == nullptr sorts the row indices), ping-pong
+// between (k0, v0) and (k1, v1); the sorted pairs are at *keys_out /
+// *vals_out. `scratch` holds radix_pairs_scratch_words(n) u32.
+size_t radix_pairs_scratch_words(uint64_t n);
+int radix_sort_pairs(Ctx* ctx, cudaStream_t st, const uint32_t* keys, const uint32_t* vals, uint64_t n, int key_bits,
+                     uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, uint32_t* scratch,
+                     const uint32_t** keys_out, const uint32_t** vals_out);
+
 }  // namespace mvr
