@@ -484,11 +484,11 @@ pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, co
 //
 // pq_nbr_kernel lists, for every centroid a, its kCandL nearest other
 // centroids in increasing v_j, v_j <= |c_a - c_j| a lower bound (f64 with
-// directed rounding). A row x whose bounds fail, with current cluster a and
-// ut = bound_upper(f_a) >= |x - c_a| (f_a its exact f32 distance to c_a),
-// gets the exact f32 distances to all kCandL listed neighbours. Every
-// centroid c_j off the list has v_j >= v_last (the list's last entry) and
-//   |x - c_j| >= |c_a - c_j| - |x - c_a| >= v_last - ut.
+// directed rounding), and v_last, the bound of the last one listed. A row x
+// whose bounds fail, with current cluster a and ut = bound_upper(f_a) >=
+// |x - c_a| (f_a its exact f32 distance to c_a), gets the exact f32
+// distances to all listed neighbours. Every centroid c_j off the list has
+// v_j >= v_last and |x - c_j| >= |c_a - c_j| - |x - c_a| >= v_last - ut.
 // When v_last > T = RU(RU(ut (2 + 2^-18)) + 2^-50), that is
 // |x - c_j| > ut (1 + 2^-18) + 2^-50: the exact squared distance D_j exceeds
 // D_a (1 + 2^-17) and 2^-100, and since the f32 distances are within
@@ -504,19 +504,18 @@ pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, co
 //
 // Work layout: each warp checks the bounds of 32 rows at a time (one lane
 // per row) and appends the rows that need a scan to a warp-private queue in
-// shared memory; whenever the queue holds 4 rows, the warp scans them with
-// 8 lanes per row (4 listed neighbours per lane, then a 3-step shuffle
-// reduction of (best, index, runner-up)). No block barrier after the
-// codebook and neighbour table are staged.
+// shared memory; whenever 32 rows are queued, each lane scans one of them
+// through its fixed window of kCandL neighbours (no divergence). Rows that
+// need the full scan are then done one at a time by the whole warp (8
+// centroids per lane, index order, shuffle reduction). No block barrier
+// after the codebook and neighbour table are staged.
 // ---------------------------------------------------------------------------
 constexpr int kCandThreads = 256;
 constexpr int kCandWarps = kCandThreads / 32;
-constexpr int kCandL = 32;                       // listed neighbours per centroid (8 lanes x 4)
-constexpr int kCandStride = kCandL + 1;          // shared-memory row stride of the table
-constexpr int kCandQ = 40;                       // warp queue capacity (< 4 left + 32 new)
+constexpr int kCandL = 32;                       // listed neighbours per centroid
+constexpr int kCandQ = 64;                       // warp queue capacity (< 32 left + 32 new)
 constexpr float kCandCut = 2.0f + 0x1p-18f;      // 1 + kPruneMargin
 constexpr float kCandFloor = 0x1p-50f;
-constexpr uint32_t kNoKey = 0xFFFFFFFFu;
 
 // Lower bound of |a - b| (f64, a and b floats): 0 when the sign is unsure.
 __device__ __forceinline__ double abs_diff_rd(double a, double b) {
@@ -531,13 +530,14 @@ __device__ __forceinline__ uint32_t nbr_key(float v, int j) {
   return (b >= 0x200u ? ((b & ~0xFFu) - 0x100u) : 0u) | (uint32_t)j;
 }
 
-// nbr[m][a][0..kCandL): keys of the min(kCandL, K - 1) nearest centroids
-// other than a, ascending; unused slots hold kNoKey. One warp per (m, a);
-// each lane holds 8 candidates sorted in registers, rounds of a warp
-// minimum pop them in order.
+// nbr_idx[m][a][0..kCandL): the min(kCandL, K - 1) nearest centroids other
+// than a, by increasing key; nbr_last[m][a]: the value of the last key when
+// kCandL are listed. One warp per (m, a); each lane holds 8 candidates
+// sorted in registers, rounds of a warp minimum pop them in order.
 template <int S>
 __global__ void __launch_bounds__(256)
-pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ state, uint32_t* __restrict__ nbr) {
+pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ state, uint8_t* __restrict__ nbr_idx,
+              float* __restrict__ nbr_last) {
   const int m = blockIdx.y;
   if (state[m] != kRunning) return;
   const int lane = threadIdx.x & 31, a = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -550,7 +550,7 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ s
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int j = lane * 8 + q;
-    key[q] = kNoKey;
+    key[q] = 0xFFFFFFFFu;
     if (j < K && j != a) {
       double d2 = 0.0;
 #pragma unroll
@@ -571,18 +571,19 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ s
       key[k - 1] = lo;
       key[k] = hi;
     }
-  uint32_t mine = kNoKey;
+  uint32_t mine = 0xFFFFFFFFu;
   const int L = min(kCandL, K - 1);
   for (int i = 0; i < L; ++i) {
     const uint32_t mn = __reduce_min_sync(0xffffffffu, key[0]);
     if (key[0] == mn) {  // keys are unique (the index is in the low bits): one lane pops
 #pragma unroll
       for (int q = 0; q < 7; ++q) key[q] = key[q + 1];
-      key[7] = kNoKey;
+      key[7] = 0xFFFFFFFFu;
     }
     if (lane == i) mine = mn;
   }
-  nbr[((size_t)m * K + a) * kCandL + lane] = mine;
+  nbr_idx[((size_t)m * K + a) * kCandL + lane] = (uint8_t)(mine & 0xFFu);
+  if (lane == L - 1) nbr_last[(size_t)m * K + a] = __uint_as_float(mine);
 }
 
 template <int S>
@@ -596,54 +597,38 @@ __device__ __forceinline__ void load_centroid(const float* sC, int j, float (&c)
   }
 }
 
-// (best, index, runner-up) of one lane merged into its 8-lane group; equal
-// values keep the smaller index, the loser's best joins the runner-up.
-__device__ __forceinline__ void group_merge(float& b, int& bi, float& sc, unsigned gmask) {
-#pragma unroll
-  for (int o = 4; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(gmask, b, o);
-    const int oi = __shfl_xor_sync(gmask, bi, o);
-    const float os = __shfl_xor_sync(gmask, sc, o);
-    if (ob < b || (ob == b && oi < bi)) {
-      sc = fminf(fminf(sc, b), os);
-      b = ob;
-      bi = oi;
-    } else {
-      sc = fminf(fminf(sc, ob), os);
-    }
-  }
-}
-
 size_t cand_smem(int K, int S) {
   const size_t cbytes = ((size_t)K * S * 4 + 15) & ~(size_t)15;
-  const size_t tbytes = (((size_t)K * kCandStride * 4) + 15) & ~(size_t)15;
-  const size_t dbytes = ((size_t)K * 4 + 15) & ~(size_t)15;
-  return cbytes + tbytes + dbytes + (size_t)kCandWarps * kCandQ * (16 + 12);
+  const size_t ibytes = (size_t)K * kCandL;                   // multiple of 16
+  const size_t fbytes = ((size_t)K * 4 + 15) & ~(size_t)15;   // per-centroid floats
+  return cbytes + ibytes + 2 * fbytes + (size_t)kCandWarps * kCandQ * 32;
 }
 
 template <int S>
 __global__ void __launch_bounds__(kCandThreads, 4)
 pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __restrict__ cb,
-               const uint32_t* __restrict__ nbr, uint8_t* __restrict__ asg, float* __restrict__ ubnd,
-               float* __restrict__ lbnd, const float* __restrict__ drift, const float* __restrict__ maxd,
-               const uint8_t* __restrict__ state, float* __restrict__ mind, int need_mind,
-               uint32_t* __restrict__ list_cnt, unsigned long long* __restrict__ dist_cnt) {
+               const uint8_t* __restrict__ nbr_idx, const float* __restrict__ nbr_last, uint8_t* __restrict__ asg,
+               float* __restrict__ ubnd, float* __restrict__ lbnd, const float* __restrict__ drift,
+               const float* __restrict__ maxd, const uint8_t* __restrict__ state, float* __restrict__ mind,
+               int need_mind, uint32_t* __restrict__ list_cnt, unsigned long long* __restrict__ dist_cnt) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ int s_bad;
   const int m = blockIdx.y;
   if (state[m] != kRunning) return;
   const size_t cbytes = ((size_t)K * S * 4 + 15) & ~(size_t)15;
-  const size_t tbytes = (((size_t)K * kCandStride * 4) + 15) & ~(size_t)15;
-  const size_t dbytes = ((size_t)K * 4 + 15) & ~(size_t)15;
-  float* sC = reinterpret_cast<float*>(smem_raw);                                // [K][S]
-  uint32_t* sT = reinterpret_cast<uint32_t*>(smem_raw + cbytes);                // [K][kCandStride]
-  float* sD = reinterpret_cast<float*>(smem_raw + cbytes + tbytes);             // drifts [K]
-  unsigned char* qbase = smem_raw + cbytes + tbytes + dbytes;
+  const size_t ibytes = (size_t)K * kCandL;
+  const size_t fbytes = ((size_t)K * 4 + 15) & ~(size_t)15;
+  float* sC = reinterpret_cast<float*>(smem_raw);                                   // [K][S]
+  uint8_t* sI = smem_raw + cbytes;                                                   // [K][kCandL] neighbours
+  float* sV = reinterpret_cast<float*>(smem_raw + cbytes + ibytes);                 // [K] v_last
+  float* sD = reinterpret_cast<float*>(smem_raw + cbytes + ibytes + fbytes);        // [K] drifts
+  unsigned char* qbase = smem_raw + cbytes + ibytes + 2 * fbytes;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float4* qx = reinterpret_cast<float4*>(qbase) + warp * kCandQ;                // rows of the queue
-  float* qd = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 16) + warp * kCandQ;
-  uint32_t* qr = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 20) + warp * kCandQ;
-  uint32_t* qa = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 24) + warp * kCandQ;
+  float4* qx = reinterpret_cast<float4*>(qbase) + warp * kCandQ;                    // rows
+  float* qd = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 16) + warp * kCandQ;  // f_a
+  float* qu = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 20) + warp * kCandQ;  // ut
+  uint32_t* qr = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 24) + warp * kCandQ;
+  uint32_t* qa = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 28) + warp * kCandQ;
   if (tid == 0) s_bad = 0;
   __syncthreads();
   {
@@ -653,9 +638,12 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
       sC[e] = v;
       bad |= !isfinite(v);
     }
-    for (int e = tid; e < K * kCandL; e += kCandThreads)
-      sT[(e / kCandL) * kCandStride + e % kCandL] = nbr[(size_t)m * K * kCandL + e];
-    for (int c = tid; c < K; c += kCandThreads) sD[c] = drift[(size_t)m * K + c];
+    const uint4* gi = reinterpret_cast<const uint4*>(nbr_idx + (size_t)m * K * kCandL);
+    for (int e = tid; e < K * kCandL / 16; e += kCandThreads) reinterpret_cast<uint4*>(sI)[e] = gi[e];
+    for (int c = tid; c < K; c += kCandThreads) {
+      sV[c] = nbr_last[(size_t)m * K + c];
+      sD[c] = drift[(size_t)m * K + c];
+    }
     if (bad) atomicOr(&s_bad, 1);
   }
   __syncthreads();
@@ -663,91 +651,112 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
   const int L = min(kCandL, K - 1);  // listed neighbours; L < kCandL: every centroid is listed
   const float md1 = maxd[3 * m], md2 = maxd[3 * m + 2];
   const uint32_t mi1 = (uint32_t)(int)maxd[3 * m + 1];
-  const int g = lane >> 3, gl = lane & 7;
-  const unsigned gmask = 0xFFu << (lane & ~7);
   uint32_t qn = 0, listed = 0;
   unsigned long long dists = 0;
 
-  // Scan `cnt` (1..4) rows at the end of the queue, 8 lanes per row.
+  // Scan the last `cnt` (1..32) queued rows, one per lane.
   auto scan_rows = [&](uint32_t cnt) {
-    const uint32_t e = qn - cnt + min((uint32_t)g, cnt - 1);
-    const bool act = (uint32_t)g < cnt;
+    const bool act = (uint32_t)lane < cnt;
+    const uint32_t e = qn - cnt + (act ? (uint32_t)lane : 0u);
     const float4 v = qx[e];
     float x[S];
     x[0] = v.x;
     if constexpr (S > 1) x[1] = v.y;
     if constexpr (S > 2) { x[2] = v.z; x[3] = v.w; }
-    const float da = qd[e];
-    const uint32_t a = qa[e], r = qr[e];
-    float b = gl == 0 ? da : __int_as_float(0x7f800000);
-    int bi = gl == 0 ? (int)a : 0x7fffffff;
-    float sc = __int_as_float(0x7f800000);
-    const uint32_t* row = sT + (size_t)a * kCandStride;
+    const uint32_t a = qa[e];
+    const float ut = qu[e];
+    float b = qd[e], sc = __int_as_float(0x7f800000);
+    int bi = (int)a;
+    // the listed neighbours, 16 per 128-bit load of indices
+    const uint4* ip = reinterpret_cast<const uint4*>(sI + (size_t)a * kCandL);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t key = row[gl + 8 * q];
-      if (key != kNoKey) {
-        const int j = (int)(key & 0xFFu);
-        float c[S];
-        load_centroid<S>(sC, j, c);
-        const float f = l2_small<S>(x, c);
-        if (f < b || (f == b && j < bi)) {
-          sc = fminf(sc, b);
-          b = f;
-          bi = j;
-        } else {
-          sc = fminf(sc, f);
+    for (int h = 0; h < kCandL / 16; ++h) {
+      const uint4 w = ip[h];
+      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        if (h * 16 + q < L) {
+          const int j = (int)((wd[q >> 2] >> (8 * (q & 3))) & 0xFFu);
+          float c[S];
+          load_centroid<S>(sC, j, c);
+          const float f = l2_small<S>(x, c);
+          if (f < b || (f == b && j < bi)) {
+            sc = fminf(sc, b);
+            b = f;
+            bi = j;
+          } else {
+            sc = fminf(sc, f);
+          }
         }
       }
     }
-    group_merge(b, bi, sc, gmask);
-    const float ut = bound_upper(da);
-    const float vlast = L == kCandL ? __uint_as_float(row[kCandL - 1]) : __int_as_float(0x7f800000);
+    const float vlast = sV[a];
     const float T = __fadd_ru(__fmul_ru(ut, kCandCut), kCandFloor);
-    // the listed neighbours decide unless the cutoff reaches past the list
-    const bool full = bad_cb || !(ut <= 3.0e38f) || (L == kCandL && !(vlast > T));
-    float lb;
-    unsigned long long cnt_d = (unsigned long long)L;
-    if (full) {  // every distance, in index order, 32 centroids per lane
+    const bool full = act && (bad_cb || !(ut <= 3.0e38f) || (L == kCandL && !(vlast > T)));
+    float lb = fminf(bound_lower(sc), L == kCandL ? __fsub_rd(vlast, ut) : __int_as_float(0x7f800000));
+    unsigned long long cnt_d = (unsigned long long)L + 1;
+    // rows whose cutoff reaches past the list: the warp scans all K, one row at a time
+    unsigned fm = __ballot_sync(0xffffffffu, full);
+    while (fm) {
+      const int src = __ffs(fm) - 1;
+      fm &= fm - 1;
+      float xs[S];
+#pragma unroll
+      for (int k = 0; k < S; ++k) xs[k] = __shfl_sync(0xffffffffu, x[k], src);
       float fb = __int_as_float(0x7f800000), fs = __int_as_float(0x7f800000), d0 = 0.f;
       int fi = 0x7fffffff;
-      for (int j = gl * 32; j < min(K, gl * 32 + 32); ++j) {
-        float c[S];
-        load_centroid<S>(sC, j, c);
-        const float f = l2_small<S>(x, c);
-        if (j == 0) d0 = f;
-        const float fk = isnan(f) ? __int_as_float(0x7f800000) : f;
-        if (fk < fb || fi == 0x7fffffff) {
-          fs = fminf(fs, fb);
-          fb = fk;
-          fi = j;
-        } else {
-          fs = fminf(fs, fk);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int j = lane * 8 + q;
+        if (j < K) {
+          float c[S];
+          load_centroid<S>(sC, j, c);
+          const float f = l2_small<S>(xs, c);
+          if (j == 0) d0 = f;
+          const float fk = isnan(f) ? __int_as_float(0x7f800000) : f;
+          if (fk < fb || fi == 0x7fffffff) {
+            fs = fminf(fs, fb);
+            fb = fk;
+            fi = j;
+          } else {
+            fs = fminf(fs, fk);
+          }
         }
       }
-      group_merge(fb, fi, fs, gmask);
-      d0 = __shfl_sync(gmask, d0, lane & ~7);
-      if (isnan(d0)) {  // vec.argmin starts from dists[0]: a NaN there wins
-        b = d0;
-        bi = 0;
-        lb = -__int_as_float(0x7f800000);
-      } else {
-        b = fb;
-        bi = fi;
-        lb = bound_lower(fs);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, fb, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, fi, o);
+        const float os = __shfl_xor_sync(0xffffffffu, fs, o);
+        if (ob < fb || (ob == fb && oi < fi)) {
+          fs = fminf(fminf(fs, fb), os);
+          fb = ob;
+          fi = oi;
+        } else {
+          fs = fminf(fminf(fs, ob), os);
+        }
       }
-      cnt_d = (unsigned long long)K;
-    } else {
-      const float lc = L == kCandL ? __fsub_rd(vlast, ut) : __int_as_float(0x7f800000);
-      lb = fminf(bound_lower(sc), lc);
+      d0 = __shfl_sync(0xffffffffu, d0, 0);
+      if (lane == src) {
+        if (isnan(d0)) {  // vec.argmin starts from dists[0]: a NaN there wins
+          b = d0;
+          bi = 0;
+          lb = -__int_as_float(0x7f800000);
+        } else {
+          b = fb;
+          bi = fi;
+          lb = bound_lower(fs);
+        }
+        cnt_d = (unsigned long long)K;
+      }
     }
-    if (act && gl == 0) {
-      const size_t eo = (size_t)m * N + r;
+    if (act) {
+      const size_t eo = (size_t)m * N + qr[e];
       asg[eo] = (uint8_t)bi;
       mind[eo] = b;
       ubnd[eo] = bound_upper(b);
       lbnd[eo] = lb;
-      dists += cnt_d + 1;
+      dists += cnt_d;
     }
     qn -= cnt;
     __syncwarp();
@@ -759,7 +768,7 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
     const uint64_t r = base + lane;
     bool queue = false;
     float x[S];
-    float da = 0.f;
+    float da = 0.f, ut = 0.f;
     uint32_t a = 0;
     if (r < N) {
       const size_t e = (size_t)m * N + r;
@@ -780,7 +789,7 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
         load_sub<S>(XT + e * S, x);
         load_centroid<S>(sC, (int)a, c);
         da = l2_small<S>(x, c);
-        const float ut = bound_upper(da);
+        ut = bound_upper(da);
         if (l >= kLbMin && __fmul_ru(ut, kPruneMargin) < l) {
           ubnd[e] = ut;
           lbnd[e] = l;
@@ -799,13 +808,14 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
       if constexpr (S > 2) { v.z = x[2]; v.w = x[3]; }
       qx[q] = v;
       qd[q] = da;
+      qu[q] = ut;
       qr[q] = (uint32_t)r;
       qa[q] = a;
     }
     qn += __popc(qb);
     listed += __popc(qb);
     __syncwarp();
-    while (qn >= 4) scan_rows(4);
+    if (qn >= 32) scan_rows(32);
   }
   if (qn > 0) scan_rows(qn);
 #pragma unroll
@@ -2598,7 +2608,8 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_cbold = carve((size_t)M * K * S * sizeof(float));
   L.o_drift = carve((size_t)M * K * sizeof(float));
   L.o_maxd = carve((size_t)M * 3 * sizeof(float));
-  L.o_nbr = carve((size_t)M * K * kCandL * sizeof(uint32_t));
+  L.o_nbr = carve((size_t)M * K * kCandL);
+  L.o_nbr_last = carve((size_t)M * K * sizeof(float));
   L.total_bytes = off;
   return L;
 }
@@ -2761,7 +2772,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   // Candidate scans (pq_cand_kernel) replace the check + full-scan list
   // passes unless the context asks for the latter (verification).
   const bool cand = prune && !(ctx && !ctx->cand_scan);
-  uint32_t* nbr = (uint32_t*)(ws + L.o_nbr);
+  uint8_t* nbr_idx = (uint8_t*)(ws + L.o_nbr);
+  float* nbr_last = (float*)(ws + L.o_nbr_last);
   unsigned long long* d_ldist = (unsigned long long*)(small + L.o_ldist);
   const size_t csmem = cand_smem(K, S);
   const unsigned cgx = (unsigned)std::max<uint64_t>(
@@ -2805,15 +2817,15 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         const dim3 ng((unsigned)((K + 7) / 8), (unsigned)M), cgrid(cgx, (unsigned)M);
         const int nm = need_mind ? 1 : 0;
         switch (S) {
-          case 1: pq_nbr_kernel<1><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
-          case 2: pq_nbr_kernel<2><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
-          default: pq_nbr_kernel<4><<<ng, 256, 0, st>>>(cb, K, d_state, nbr); break;
+          case 1: pq_nbr_kernel<1><<<ng, 256, 0, st>>>(cb, K, d_state, nbr_idx, nbr_last); break;
+          case 2: pq_nbr_kernel<2><<<ng, 256, 0, st>>>(cb, K, d_state, nbr_idx, nbr_last); break;
+          default: pq_nbr_kernel<4><<<ng, 256, 0, st>>>(cb, K, d_state, nbr_idx, nbr_last); break;
         }
         MVR_CUDA(ctx, cudaGetLastError());
         switch (S) {
-          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
         }
         MVR_CUDA(ctx, cudaGetLastError());
       } else {

@@ -50,9 +50,10 @@ struct PqLayout {
   // Lloyd bound pruning: bounds [M][N] f32 x2, per-subspace row lists
   // [M][N] u32 + counts, previous codebooks, drifts [M][K], max drift [M]
   size_t o_ub = 0, o_lb = 0, o_list = 0, o_lcnt = 0, o_cbold = 0, o_drift = 0, o_maxd = 0;
-  // candidate scans: neighbour tables [M][K][L] u32; distances computed by
+  // candidate scans: neighbour lists [M][K][32] u8 and the bound of each
+  // list's last entry [M][K] f32; distances computed by
   // the pruned passes [M] u64 (in the bookkeeping block)
-  size_t o_nbr = 0, o_ldist = 0;
+  size_t o_nbr = 0, o_nbr_last = 0, o_ldist = 0;
   // tensor-core filter counters (in the bookkeeping block): violations,
   // rows re-scanned, timeouts
   size_t o_diag = 0;
