@@ -657,6 +657,160 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- configs[4]
+
+C4_ROWS, C4_DIM, C4_M, C4_ITERS = 50_000_000, 128, 32, 25
+C4_WORKLOAD = ("configs[4]: synthetic 50,000,000 x 128 f32 (made on the GPU), PQ M=32x4, 256 centroids, "
+               "k-means++ + 25 Lloyd iters, + pq.encode")
+
+
+def run_configs4(args) -> None:
+    """BASELINE configs[4]'s PQ stage: pq.train (M = 32 x 4, 25 iterations)
+    and pq.encode of 50M x 128 rows made on the GPU (synth.device_residuals),
+    at N GPUs: subspace-sharded training over NCCL, each rank encoding its
+    row shard. Same metric as the default line; a row sample of the codes is
+    checked against the oracle given the trained codebooks (one GPU)."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+    from ir_multivector_retrieval_b200 import Context
+    from ir_multivector_retrieval_b200 import dist as mdist
+    from ir_multivector_retrieval_b200 import synth
+    from ir_multivector_retrieval_b200._lib import PqTrainStats
+
+    n_total = args.rows or C4_ROWS
+    row0, n = mdist.shard_rows(n_total, world, rank)
+    dev = f"cuda:{local}"
+    dx, _ids = synth.device_residuals(n_total, C4_DIM, seed=42, device=dev, row0=row0, n_rows=n)
+    del _ids
+    S = C4_DIM // C4_M
+    dcb = torch.empty(C4_M * K * S, dtype=torch.float32, device=dev)
+    dcodes = torch.empty((n, C4_M), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    torch.cuda.synchronize()
+    ctx = Context(local)
+    ctx.set_stream(stream.cuda_stream)
+    lib = ctx.lib
+    if world > 1:
+        mdist.init_comm(ctx)
+    seed = SEED
+
+    def train_dev(st):
+        if world > 1:
+            ctx.check(lib.mvr_pq_train_sharded_device(ctx.handle, C.c_void_p(dx.data_ptr()), n, row0, n_total, C4_DIM,
+                                                      seed, 1, C4_M, C4_ITERS, C.c_float(-math.inf),
+                                                      C.c_void_p(dcb.data_ptr()), None, C.byref(st)))
+        else:
+            ctx.check(lib.mvr_pq_train_device(ctx.handle, C.c_void_p(dx.data_ptr()), n * C4_DIM, C4_DIM, seed, 1,
+                                              C4_M, C4_ITERS, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()),
+                                              C.byref(st)))
+
+    def encode_dev():
+        ctx.check(lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), C4_DIM, C4_M,
+                                           C.c_void_p(dx.data_ptr()), n, C.c_void_p(dcodes.data_ptr())))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        train_dev(PqTrainStats())
+        encode_dev()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    stats, enc = [], []
+    t0e = torch.cuda.Event(enable_timing=True)
+    t1e = torch.cuda.Event(enable_timing=True)
+    t0e.record(stream)
+    for _ in range(args.steps):
+        st = PqTrainStats()
+        train_dev(st)
+        stats.append(st)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        encode_dev()
+        e1.record(stream)
+        enc.append((e0, e1))
+    t1e.record(stream)
+    barrier()
+    clk = clocks.stop()
+    train_ms = max_over_ranks(statistics.mean(s.total_ms for s in stats))
+    enc_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in enc))
+    step_ms = max_over_ranks(t0e.elapsed_time(t1e) / args.steps)
+    cb_host = dcb.cpu().numpy()
+    line = None
+    if rank == 0:
+        lst = stats[-1]
+        line = {
+            "metric": METRIC, "value": train_ms / 1e3 / C4_ITERS, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (generated on the GPU)",
+            "config": {"workload": C4_WORKLOAD, "rows": n_total, "rows_per_gpu": n, "dim": C4_DIM, "pq_m": C4_M,
+                       "centroids": K, "lloyd_iters": C4_ITERS,
+                       "parallelism": f"subspace-sharded over {world} GPUs (NCCL)" if world > 1 else "1gpu",
+                       "l2": "inputs (25.6 GB) > L2, no flush"},
+            "codebook_sha256": mdist.codebook_digest(cb_host),
+            "pq_train_ms": train_ms, "seed_ms": lst.seed_ms, "lloyd_ms": lst.lloyd_ms,
+            "pq_encode_ms": enc_ms, "pq_encode_mvec_s": n_total / (enc_ms / 1e3) / 1e6,
+            "pruned_passes": {"launches": lst.list_launches,
+                              "avg_ms": lst.list_ms / max(1, lst.list_launches),
+                              "distances_per_launch": lst.list_distances / max(1, lst.list_launches)},
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu:
+            from oracle import oracle
+
+            oracle.build()
+            threads = host_threads()
+            xs = dx[: min(n, 4000)].cpu().numpy()
+            t0 = time.perf_counter()
+            oracle.pq_train(xs, C4_DIM, seed, C4_M, n_threads=threads, max_iters=C4_ITERS, tol=-math.inf)
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {
+                "value": dt * n_total / xs.shape[0] / C4_ITERS, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": (f"one whole pq.train (seeding + {C4_ITERS} Lloyd iterations, {C4_M} subspaces) over "
+                           f"the first {xs.shape[0]:,} rows, time scaled linearly to {n_total:,} rows, / {C4_ITERS}")}
+        if world == 1 and not args.no_parity:
+            from oracle import oracle
+
+            oracle.build()
+            idx = torch.from_numpy(np.sort(np.random.default_rng(7).choice(n, 200_000, replace=False))).to(dev)
+            xs = dx[idx].cpu().numpy()
+            want = oracle.pq_encode(cb_host, C4_DIM, C4_M, xs, n_threads=host_threads())
+            got = dcodes[idx].cpu().numpy()
+            line["pq_encode_bit_exact_vs_cpu"] = {
+                "codes": bool(np.array_equal(want.reshape(-1), got.reshape(-1))), "rows": 200_000,
+                "what": "oracle PQ.encode of a seeded 200,000-row sample with the trained codebooks"}
+            line["codebooks_finite"] = bool(np.isfinite(cb_host).all())
+        print(json.dumps(line), flush=True)
+        print(f"codebook_sha256 {line['codebook_sha256']} n_gpus {world} value {line['value']:.6g}", flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -674,6 +828,8 @@ def main() -> int:
                     help="only the clusterFlat measurement (one GPU; for profiling captures)")
     ap.add_argument("--hnsw-only", action="store_true",
                     help="only clusterFlat and hnsw.build over its centroids (one GPU)")
+    ap.add_argument("--workload", choices=["configs1", "configs4"], default="configs1",
+                    help="configs1 (default, the headline line) or configs4 (50M x 128, M=32, 25 iterations)")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -688,6 +844,8 @@ def main() -> int:
         return 0
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "configs4":
+        run_configs4(args)
     else:
         run_b200(args)
     return 0

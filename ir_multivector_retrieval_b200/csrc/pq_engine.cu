@@ -507,7 +507,8 @@ pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, co
 // shared memory; whenever 32 rows are queued, each lane scans one of them
 // through its fixed window of kCandL neighbours (no divergence). Rows that
 // need the full scan are then done one at a time by the whole warp (8
-// centroids per lane, index order, shuffle reduction). No block barrier
+// centroids per lane, then a shuffle reduction that keeps the smallest index
+// among equal distances). No block barrier
 // after the codebook and neighbour table are staged.
 // ---------------------------------------------------------------------------
 constexpr int kCandThreads = 256;
@@ -705,9 +706,12 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
       for (int k = 0; k < S; ++k) xs[k] = __shfl_sync(0xffffffffu, x[k], src);
       float fb = __int_as_float(0x7f800000), fs = __int_as_float(0x7f800000), d0 = 0.f;
       int fi = 0x7fffffff;
+      // lane l takes centroids l, l + 32, ... (consecutive lanes read
+      // consecutive codewords: no bank conflicts); equal distances across
+      // lanes are settled by index in the reduction
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int j = lane * 8 + q;
+        const int j = lane + 32 * q;
         if (j < K) {
           float c[S];
           load_centroid<S>(sC, j, c);

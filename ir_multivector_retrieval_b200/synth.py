@@ -67,3 +67,46 @@ def unit_rows(n: int, dim: int, seed: int = 0) -> np.ndarray:
     """n unit-norm Gaussian rows (float32)."""
     rng = np.random.default_rng(seed)
     return _normalize_rows(rng.standard_normal((n, dim), dtype=np.float32))
+
+
+def device_residuals(n_tokens: int, dim: int, *, n_anchors: int = 19221, zipf_s: float = 1.1, noise: float = 0.35,
+                     seed: int = 42, device: str = "cuda", row0: int = 0, n_rows: int | None = None,
+                     chunk: int = 1 << 22):
+    """The same generator run on the GPU for corpora too large to make on the
+    host (BASELINE configs[3] and [4]): anchors uniform on the sphere, token
+    id = Zipf(zipf_s) rank, vector = normalize(anchor + noise N(0, I)), and
+    the PQ input row = normalize(vector - anchor), the unit residual from
+    the token's anchor (standing in for its TAC centroid). Rows
+    [row0, row0 + n_rows) of the n_tokens-row corpus are made; each block of
+    `chunk` rows has its own seeded torch Philox stream, so any shard of the
+    corpus comes out the same whichever process makes it. The values differ
+    from make_corpus at equal seeds; the distributions are the same. Returns
+    (residuals n_rows x dim f32, token ids int64), both on `device`."""
+    import torch
+
+    n_rows = n_tokens - row0 if n_rows is None else n_rows
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    anchors = torch.randn((n_anchors, dim), generator=g, device=device, dtype=torch.float32)
+    anchors /= anchors.norm(dim=1, keepdim=True)
+    w = 1.0 / torch.arange(1, n_anchors + 1, device=device, dtype=torch.float64) ** zipf_s
+    cdf = torch.cumsum(w / w.sum(), 0)
+    res = torch.empty((n_rows, dim), device=device, dtype=torch.float32)
+    ids = torch.empty(n_rows, device=device, dtype=torch.int64)
+    lo, hi = row0, row0 + n_rows
+    for c in range(lo // chunk, (hi + chunk - 1) // chunk):
+        c0, c1 = c * chunk, min(n_tokens, (c + 1) * chunk)
+        gc = torch.Generator(device=device)
+        gc.manual_seed(int(seed) * 1_000_003 + 7 + c)
+        u = torch.rand(c1 - c0, generator=gc, device=device, dtype=torch.float64)
+        t = torch.clamp(torch.searchsorted(cdf, u, right=True), max=n_anchors - 1)
+        v = anchors[t] + noise * torch.randn((c1 - c0, dim), generator=gc, device=device, dtype=torch.float32)
+        v /= v.norm(dim=1, keepdim=True).clamp_min(1e-30)
+        r = v - anchors[t]
+        nr = r.norm(dim=1, keepdim=True)
+        r = torch.where(nr > 0, r / nr.clamp_min(1e-30), r)
+        a, b = max(lo, c0), min(hi, c1)
+        res[a - lo:b - lo] = r[a - c0:b - c0]
+        ids[a - lo:b - lo] = t[a - c0:b - c0]
+        del u, t, v, r, nr
+    return res, ids

@@ -50,3 +50,21 @@ def test_cluster_flat_full_size(ctx, orc, corpus):
     assert np.array_equal(got.assignments, want.assignments)
     assert got.centroids.tobytes() == np.ascontiguousarray(want.centroids, dtype=np.float32).tobytes()
     assert np.float32(got.wcss_total).tobytes() == np.float32(want.wcss_total).tobytes()
+
+
+def test_configs4_shape_on_a_row_sample(ctx, orc):
+    """BASELINE configs[4]'s PQ shape (dim 128, M = 32 x 4, 256 centroids,
+    25 Lloyd iterations) on a seeded 150,000-row block of its 50M-row corpus
+    (made on the GPU): codebooks byte for byte, then the codes of the block."""
+    import torch
+
+    from ir_multivector_retrieval_b200 import synth
+
+    xd, _ = synth.device_residuals(50_000_000, 128, seed=42, device="cuda", row0=12_000_000, n_rows=150_000)
+    x = xd.cpu().numpy()
+    got = pq.train(x, 128, SEED, pq_m=32, max_iters=25, tol=-math.inf, ctx=ctx)
+    want = orc.pq_train(x, 128, SEED, 32, n_threads=THREADS, max_iters=25, tol=-math.inf)
+    assert got.codebooks.tobytes() == want.tobytes()
+    assert np.array_equal(got.encode_batch(x), orc.pq_encode(want, 128, 32, x, n_threads=THREADS))
+    del xd
+    torch.cuda.empty_cache()
