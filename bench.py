@@ -503,11 +503,12 @@ def run_b200(args) -> None:
             "host and device encodes disagree"
 
     # ---- encode through each assignment kernel (one GPU): the exact f32 scan
-    # and the tensor-core filter, both bit-identical; the line reports both
+    # (the PQ default) and the tensor-core filter, both bit-identical; the
+    # line reports both
     enc_paths = {}
     if world == 1:
         for name, on in (("exact_f32_scan", 0), ("tcgen05_filter", 1)):
-            ctx.check(lib.mvr_ctx_set_tensor_filter(ctx.handle, on))
+            ctx.check(lib.mvr_ctx_set_pq_tensor_filter(ctx.handle, on))
             encode_dev()
             ts = []
             for _ in range(5):
@@ -521,7 +522,7 @@ def run_b200(args) -> None:
             enc_paths[name] = statistics.median(a.elapsed_time(b) for a, b in ts)
             assert np.array_equal(codes_host.numpy().reshape(-1), dcodes.cpu().numpy().reshape(-1)), \
                 f"encode through {name} differs"
-        ctx.check(lib.mvr_ctx_set_tensor_filter(ctx.handle, 1))  # the library default
+        ctx.check(lib.mvr_ctx_set_pq_tensor_filter(ctx.handle, 0))  # the library default for PQ
 
     # ---- rooflines. (1) the k-means++ weight update: one HBM pass per step
     # over the subspace-major rows of this GPU's subspaces plus the weights

@@ -404,10 +404,18 @@ int mvr_ctx_set_candidate_scan(mvr_ctx* ctx, int on);
 
 /* Verification mode (no reference counterpart): with `on` == 0 the Lloyd
  * and encode assignments skip the tensor-core filter (a TF32 MMA chain that
- * approximates every distance within a proven bound, after which only the
+ * approximates every distance within an error bound, after which only the
  * near-ties get exact distances) and scan every centroid with the exact
- * f32 arithmetic. Results are identical either way; on is the default. */
+ * f32 arithmetic. Results are identical either way; on is the default, and
+ * it applies to the 64-dim k-means of tac.clusterFlat. */
 int mvr_ctx_set_tensor_filter(mvr_ctx* ctx, int on);
+
+/* The tensor-core filter for pq.train's first Lloyd pass and PQ.encode
+ * too (`on` != 0; needs mvr_ctx_set_tensor_filter on as well). Off by
+ * default: for 4-float sub-vectors the exact f32 scans measured as fast as
+ * the filter (whose accumulator read-out costs about as much as the exact
+ * distance). No reference counterpart; results are identical either way. */
+int mvr_ctx_set_pq_tensor_filter(mvr_ctx* ctx, int on);
 
 /* Counters of the filtered encode passes on this context since it was
  * created: winners whose approximation fell outside the filter's error

@@ -183,6 +183,7 @@ SIGNATURES = {
     ),
     "mvr_ctx_set_exhaustive_assign": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_tensor_filter": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_set_pq_tensor_filter": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_wait_limit": (C.c_int, [_P, C.c_uint32]),
     "mvr_ctx_set_candidate_scan": (C.c_int, [_P, C.c_int]),
     "mvr_measure_f32x2_rate": (C.c_int, [_P, C.POINTER(C.c_double)]),

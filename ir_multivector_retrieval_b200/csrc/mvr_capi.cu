@@ -249,6 +249,12 @@ int mvr_ctx_set_wait_limit(mvr_ctx* h, uint32_t polls) {
   return MVR_OK;
 }
 
+int mvr_ctx_set_pq_tensor_filter(mvr_ctx* h, int on) {
+  if (!h) return MVR_E_INVALID_ARGUMENT;
+  h->impl.pq_tc_filter = on != 0;
+  return MVR_OK;
+}
+
 int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_rechecked) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
@@ -460,7 +466,7 @@ int mvr_pq_encode(mvr_ctx* h, const float* cb, uint32_t dim, uint32_t pq_m, cons
     MVR_TRY(mvr::h2d(c, d_res, res, n * dim * sizeof(float)));
     MVR_TRY(mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes));
   }
-  if (c->tc_filter && !c->exhaustive_assign && c->tc_diag) {
+  if (c->tc_filter && c->pq_tc_filter && !c->exhaustive_assign && c->tc_diag) {
     uint32_t dg[4] = {0, 0, 0, 0};
     MVR_CUDA(c, cudaMemcpyAsync(dg, c->tc_diag, sizeof(dg), cudaMemcpyDeviceToHost, c->stream));
     MVR_CUDA(c, cudaStreamSynchronize(c->stream));

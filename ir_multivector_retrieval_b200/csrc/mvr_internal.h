@@ -66,6 +66,9 @@ struct Ctx {
   bool exhaustive_assign = false;
   // tensor-core filtered assignment passes (off: the exact scans only)
   bool tc_filter = true;
+  // ... also for the PQ passes (4-float sub-vectors), where the filter
+  // measured no faster than the exact scans: off by default
+  bool pq_tc_filter = false;
   // pruned Lloyd passes scan only the candidate centroids near the current
   // one (off: the bound check + full scans of the failing rows)
   bool cand_scan = true;

@@ -2549,7 +2549,7 @@ int pq_encode_device(Ctx* ctx, const float* d_cb, int D, int M, const float* d_R
   uint64_t rpc = 0;
   grid_for(N, ctx->sm_count, &nblk, &rpc);
   cudaStream_t st = ctx->stream;
-  if (ctx->tc_filter && !ctx->exhaustive_assign) {
+  if (ctx->tc_filter && ctx->pq_tc_filter && !ctx->exhaustive_assign) {
     if (!ctx->tc_diag) {
       MVR_CUDA(ctx, cudaMalloc(&ctx->tc_diag, 4 * sizeof(uint32_t)));
       MVR_CUDA(ctx, cudaMemsetAsync(ctx->tc_diag, 0, 4 * sizeof(uint32_t), st));
@@ -2767,7 +2767,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   // Bound pruning (Hamerly) from the second iteration on; exact, see
   // bound_upper / bound_lower.
   const bool prune = !(ctx && ctx->exhaustive_assign);
-  const bool use_tc = prune && job.tc_filter && !(ctx && !ctx->tc_filter);
+  // The tensor-core filter for the first pass only when the context asks for
+  // it on PQ (the exact scan measured as fast for 4-float sub-vectors).
+  const bool use_tc = prune && job.tc_filter && ctx && ctx->tc_filter && ctx->pq_tc_filter;
   // The pruned passes (row lists) stay on the exact kernel: for 4-float
   // sub-vectors the filter's accumulator read-out per (row, centroid) costs
   // about as much as the exact distance, and the exact list pass measured

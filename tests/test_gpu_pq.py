@@ -320,12 +320,16 @@ def _filter_datasets():
 
 @pytest.mark.parametrize("name,x,dim,m", list(_filter_datasets()), ids=lambda v: v if isinstance(v, str) else "")
 def test_tensor_filter_matches_exact_scans(ctx, orc, name, x, dim, m):
-    """The tensor-core filtered assignment (default) and the exact scans give
-    the same codebooks and codes, equal to the oracle; no winner falls outside
-    the filter's error bound."""
+    """The tensor-core filtered assignment (switched on for PQ) and the exact
+    scans (the PQ default) give the same codebooks and codes, equal to the
+    oracle; no winner falls outside the filter's error bound."""
     st_f, st_e = {}, {}
-    f = pq.train(x, dim, 5, pq_m=m, max_iters=8, tol=1e-4, ctx=ctx, stats=st_f)
-    codes_f = f.encode_batch(x)
+    ctx.check(ctx.lib.mvr_ctx_set_pq_tensor_filter(ctx.handle, 1))
+    try:
+        f = pq.train(x, dim, 5, pq_m=m, max_iters=8, tol=1e-4, ctx=ctx, stats=st_f)
+        codes_f = f.encode_batch(x)
+    finally:
+        ctx.check(ctx.lib.mvr_ctx_set_pq_tensor_filter(ctx.handle, 0))
     ctx.check(ctx.lib.mvr_ctx_set_tensor_filter(ctx.handle, 0))
     try:
         e = pq.train(x, dim, 5, pq_m=m, max_iters=8, tol=1e-4, ctx=ctx, stats=st_e)
