@@ -773,6 +773,7 @@ def run_configs4(args) -> None:
                        "l2": "inputs (25.6 GB) > L2, no flush"},
             "codebook_sha256": mdist.codebook_digest(cb_host),
             "pq_train_ms": train_ms, "seed_ms": lst.seed_ms, "lloyd_ms": lst.lloyd_ms,
+            "seed_fallbacks": int(lst.seed_fallbacks),
             "pq_encode_ms": enc_ms, "pq_encode_mvec_s": n_total / (enc_ms / 1e3) / 1e6,
             "pruned_passes": {"launches": lst.list_launches,
                               "avg_ms": lst.list_ms / max(1, lst.list_launches),

@@ -1847,6 +1847,171 @@ __device__ __forceinline__ double gamma_bound(uint64_t n) {
   return __ddiv_ru(g, __dsub_rd(1.0, g));
 }
 
+// ---------------------------------------------------------------------------
+// The reference's sequential f64 sum of the weights, exactly, by one CTA
+// (weightedSample, rng.zig:57-82), for draws the interval bounds cannot
+// decide when N is large (the bounds widen with N; one thread running the
+// chain over tens of millions of weights takes a large fraction of a
+// second).
+//
+// A running f64 sum S in the binade [2^e, 2^(e+1)) is a multiple of its
+// ulp u = 2^(e-52), and while S + w stays in that binade, fl(S + w) =
+// S + g u with g = w / u rounded to nearest: a function of w and e alone,
+// except when w's part below u is exactly u / 2 (a tie, decided by the
+// parity of S / u). A chunk of rows whose sums provably stay in one binade
+// (the directed-rounding prefix bounds widened by the classic recursive-sum
+// error bound gamma_N sum w) and hold no tie therefore moves S by exactly
+// G u, G = sum of g: the CTA's warps form every clean chunk's G in
+// parallel, then one thread walks the chunks adding G u (exact) or, for
+// the few chunks that cross a binade or hold a tie, the chunk's weights one
+// by one in the reference's order. The exact chunk-end sums then locate the
+// first row with u_draw < S_i.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kExactChunkedMinRows = 1u << 18;  // smaller N: the one-thread chain
+
+// g for adding w >= 0 to a sum in binade e (ulps of 2^(e-52), rounded to
+// nearest); `tie` when the part below the ulp is exactly half of it.
+__device__ __forceinline__ uint64_t grid_steps(float w, int e, bool& tie) {
+  const uint32_t b = __float_as_uint(w);
+  const int be = (int)(b >> 23);
+  const uint64_t mant = be ? (uint64_t)((b & 0x7FFFFFu) | 0x800000u) : (uint64_t)(b & 0x7FFFFFu);
+  const int E = be ? be - 127 : -126;  // w = mant * 2^(E - 23)
+  const int sh = E - 23 + 52 - e;      // w / u = mant * 2^sh
+  tie = false;
+  if (mant == 0) return 0;
+  if (sh >= 0) return mant << sh;      // the chunk stays below 2^(e+1): mant << sh < 2^53
+  const int rs = -sh;
+  if (rs > 25) return 0;               // w / u < 1/4
+  const uint64_t q = mant >> rs;
+  const uint64_t frac = mant & ((1ull << rs) - 1);
+  const uint64_t half = 1ull << (rs - 1);
+  if (frac > half) return q + 1;
+  tie = frac == half;
+  return q;
+}
+
+// Called by all kSelectThreads threads of the CTA of subspace m. ex_lo /
+// ex_hi: this thread's exclusive prefix bounds at chunk c_lo. Returns the
+// reference's pick (valid in every thread).
+__device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, uint64_t N, const double2* __restrict__ ch,
+                                                  int nchunk, int c_lo, int c_hi, double ex_lo, double ex_hi,
+                                                  double B, double r, double2* __restrict__ xpre,
+                                                  unsigned long long* __restrict__ xg, int* __restrict__ xe) {
+  __shared__ unsigned long long s_last;
+  __shared__ int s_first;
+  __shared__ double s_total;
+  __shared__ uint64_t s_pick;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    s_last = 0;
+    s_first = nchunk;
+  }
+  // 1a. exclusive prefix bounds of every chunk
+  {
+    double lo = ex_lo, hi = ex_hi;
+    for (int c = c_lo; c < c_hi; ++c) {
+      xpre[c] = make_double2(lo, hi);
+      lo = __dadd_rd(lo, ch[c].x);
+      hi = __dadd_ru(hi, ch[c].y);
+    }
+  }
+  __syncthreads();
+  // 1b. per chunk (one warp each): its binade if it provably stays in one,
+  // G, ties; and the last non-zero weight
+  unsigned long long last = 0;
+  for (int c = warp; c < nchunk; c += kSelectThreads / 32) {
+    const double2 pre = xpre[c];
+    const double lo_s = __dsub_rd(pre.x, B);
+    const double hi_e = __dadd_ru(__dadd_ru(pre.y, ch[c].y), B);
+    int e = INT_MIN;
+    if (lo_s >= 0x1p-1022) {
+      const int e0 = ilogb(lo_s);
+      if (hi_e < ldexp(1.0, e0 + 1)) e = e0;
+    }
+    const uint64_t r0 = (uint64_t)c * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
+    unsigned long long G = 0;
+    bool tie = false;
+    for (uint64_t i = r0 + lane; i < r1; i += 32) {
+      const float v = w[i];
+      if (v != 0.f) last = max(last, (unsigned long long)i);
+      if (e != INT_MIN) {
+        bool t;
+        G += grid_steps(v, e, t);
+        tie |= t;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) G += __shfl_xor_sync(0xffffffffu, G, o);
+    if (__any_sync(0xffffffffu, tie)) e = INT_MIN;
+    if (lane == 0) {
+      xg[c] = G;
+      xe[c] = e;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+  if (lane == 0) atomicMax(&s_last, last);
+  __syncthreads();
+  // 2. one thread: exact chunk-end sums (xpre[c].x), in the reference's
+  //    order; the per-chunk terms are staged in shared memory a tile at a time
+  constexpr int kTile = 2048;
+  __shared__ double s_step[kTile];  // G u of a clean chunk, NaN for a chunk to chain
+  double S = 0.0;
+  for (int t0 = 0; t0 < nchunk; t0 += kTile) {
+    const int tn = min(kTile, nchunk - t0);
+    for (int q = tid; q < tn; q += kSelectThreads) {
+      const int e = xe[t0 + q];
+      s_step[q] = e != INT_MIN ? ldexp((double)xg[t0 + q], e - 52) : __longlong_as_double(0x7ff8000000000000ll);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int q = 0; q < tn; ++q) {
+        const double g = s_step[q];
+        if (!isnan(g)) {
+          S = __dadd_rn(S, g);  // exact: same binade, a multiple of its ulp
+        } else {
+          const uint64_t r0 = (uint64_t)(t0 + q) * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
+          uint64_t i = r0;
+          for (; i + 8 <= r1; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = w[i + k];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) S = __dadd_rn(S, (double)v[k]);
+          }
+          for (; i < r1; ++i) S = __dadd_rn(S, (double)w[i]);
+        }
+        xpre[t0 + q].x = S;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) s_total = S;
+  __syncthreads();
+  // 3. the first chunk whose end sum exceeds u, then its rows in order
+  const double u = __dmul_rn(r, s_total);
+  int first = nchunk;
+  for (int c = c_lo; c < c_hi; ++c)
+    if (u < xpre[c].x) { first = c; break; }
+  if (first < nchunk) atomicMin(&s_first, first);
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t pick = s_last;  // the reference's fallback: last positive weight
+    const int c = s_first;
+    if (c < nchunk) {
+      double S = c > 0 ? xpre[c - 1].x : 0.0;
+      const uint64_t r0 = (uint64_t)c * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
+      for (uint64_t i = r0; i < r1; ++i) {
+        S = __dadd_rn(S, (double)w[i]);
+        if (u < S) { pick = i; break; }
+      }
+    }
+    s_pick = pick;
+  }
+  __syncthreads();
+  return s_pick;
+}
+
 // Draw for centroid `step` (weightedSample, rng.zig:57-82).
 //
 // The reference returns the first i with u < S_i, where S_i is the
@@ -1871,7 +2036,8 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
                       int nchunk, const double* __restrict__ draws, int* __restrict__ nonfinite,
                       int* __restrict__ status, uint8_t* __restrict__ state,
                       uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen,
-                      double* __restrict__ thr, int force_chain) {
+                      double* __restrict__ thr, int force_chain, double2* __restrict__ xpre,
+                      unsigned long long* __restrict__ xg, int* __restrict__ xe) {
   grid_dependency_wait();
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
@@ -1948,6 +2114,8 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
   const bool past = !(u_mid < 0.5 * (incl_lo + incl_hi));
   incl_all[tid] = make_double2(incl_lo, incl_hi);
   const int n_before = __syncthreads_count(past);  // prefixes are monotone
+  // this thread's exclusive prefix bounds (incl_all is reused below)
+  const double ex_lo = tid > 0 ? incl_all[tid - 1].x : 0.0, ex_hi = tid > 0 ? incl_all[tid - 1].y : 0.0;
   if (tid == 0) {
     sh_decided = 0;
     sh_chunk = -1;
@@ -2019,8 +2187,17 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
   }
   __syncthreads();
 
-  // 5. undecided: the reference's sequential chain, by one thread.
-  if (!sh_decided && tid == 0) {
+  // 5. undecided: the reference's sequential chain, exactly: chunked by the
+  //    whole CTA for large N, by one thread otherwise.
+  if (!sh_decided && N >= kExactChunkedMinRows) {
+    const uint64_t pick = exact_chain_draw(w, N, ch, nchunk, c_lo, c_hi, ex_lo, ex_hi,
+                                           __dmul_ru(gamma_bound(N), Hi_N), r, xpre + (size_t)m * nchunk,
+                                           xg + (size_t)m * nchunk, xe + (size_t)m * nchunk);
+    if (tid == 0) {
+      sh_idx = pick;
+      fallbacks[m] += 1;
+    }
+  } else if (!sh_decided && tid == 0) {
     double total = 0.0;
     uint64_t last_pos = 0;
     uint64_t i = 0;
@@ -2605,6 +2782,10 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_hist = carve((size_t)M * L.nblk * K * sizeof(uint32_t));
   L.o_chunk = carve((size_t)M * L.nchunk * sizeof(double2));
   L.o_chunk_cnt = carve((size_t)M * L.nchunk * sizeof(uint32_t));
+  // exact chained draws (large N): chunk prefix bounds / end sums, G, binade
+  L.o_xpre = carve((size_t)M * L.nchunk * sizeof(double2));
+  L.o_xg = carve((size_t)M * L.nchunk * sizeof(unsigned long long));
+  L.o_xe = carve((size_t)M * L.nchunk * sizeof(int));
   L.o_ub = carve((size_t)M * N * sizeof(float));
   L.o_lb = carve((size_t)M * N * sizeof(float));
   L.o_list = carve((size_t)M * N * sizeof(uint32_t));
@@ -2738,7 +2919,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     MVR_CUDA(ctx, launch_pdl(pq_seed_select_kernel, dim3(M), dim3(kSelectThreads), 0, st, (const float*)XT, N, S, K,
                              step + 1, cb, (const float*)mind, (const double2*)chunk, (const uint32_t*)chunk_cnt,
                              nchunk, (const double*)d_draws, d_nonf, d_status, d_state, d_fb, d_chosen, d_thr,
-                             ctx && ctx->serial_draws ? 1 : 0));
+                             ctx && ctx->serial_draws ? 1 : 0, (double2*)(ws + L.o_xpre),
+                             (unsigned long long*)(ws + L.o_xg), (int*)(ws + L.o_xe)));
     launches += 2;
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));

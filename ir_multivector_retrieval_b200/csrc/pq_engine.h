@@ -47,6 +47,7 @@ struct PqLayout {
          o_prev = 0, o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_exact = 0, o_state = 0;
   size_t small_bytes = 0;
   size_t o_xt = 0, o_mind = 0, o_asg = 0, o_sorted = 0, o_hist = 0, o_chunk = 0, o_chunk_cnt = 0;
+  size_t o_xpre = 0, o_xg = 0, o_xe = 0;  // exact chained draws (large N)
   // Lloyd bound pruning: bounds [M][N] f32 x2, per-subspace row lists
   // [M][N] u32 + counts, previous codebooks, drifts [M][K], max drift [M]
   size_t o_ub = 0, o_lb = 0, o_list = 0, o_lcnt = 0, o_cbold = 0, o_drift = 0, o_maxd = 0;

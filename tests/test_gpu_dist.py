@@ -15,6 +15,8 @@ import pytest
 from ir_multivector_retrieval_b200 import synth
 from ir_multivector_retrieval_b200._lib import MvrError, PqTrainStats
 
+THREADS = max(1, os.cpu_count() or 1)
+
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -58,6 +60,31 @@ def test_serial_draws_mode_matches(ctx, orc):
     assert st_serial["seed_fallbacks"] == 16 * 255 and st_fast["seed_fallbacks"] == 0
     assert fast.codebooks.tobytes() == serial.codebooks.tobytes()
     assert serial.codebooks.tobytes() == orc.pq_train(x, 32, 3, 16, n_threads=8, max_iters=10).tobytes()
+
+
+def test_serial_draws_mode_matches_large_n(ctx, orc):
+    """Above 2^18 rows an undecided draw runs the reference's sequential f64
+    chain chunk by chunk (binade-exact steps for clean chunks, the weights one
+    by one for the others): every draw through it gives the same bytes as
+    the interval-bounded draws and the oracle, including data with many
+    equal and zero weights and sums that cross many binades."""
+    from ir_multivector_retrieval_b200 import pq
+
+    rng = np.random.default_rng(5)
+    x = synth.unit_rows(300_000, 16, seed=4)
+    x[rng.integers(0, 300_000, 40_000)] = x[7]            # exact duplicates: zero weights
+    x[::97] *= np.float32(1e-3)                              # small weights over many binades
+    for fast_first in (True, False):
+        st = {}
+        ctx.check(ctx.lib.mvr_ctx_set_serial_draws(ctx.handle, 0 if fast_first else 1))
+        try:
+            got = pq.train(x, 16, 9, pq_m=4, max_iters=3, tol=-math.inf, ctx=ctx, stats=st)
+        finally:
+            ctx.check(ctx.lib.mvr_ctx_set_serial_draws(ctx.handle, 0))
+        if not fast_first:
+            assert st["seed_fallbacks"] == 4 * 255
+        want = orc.pq_train(x, 16, 9, 4, n_threads=THREADS, max_iters=3, tol=-math.inf)
+        assert got.codebooks.tobytes() == want.tobytes()
 
 
 def test_sharded_training_on_several_gpus():
