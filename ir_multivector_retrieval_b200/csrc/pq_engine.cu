@@ -1517,6 +1517,131 @@ pq_scatter_kernel(const float* __restrict__ XT, uint64_t N, int M, int K,
 size_t scatter_smem(int M, int S) { return (size_t)M * (256 * 8 + (S == 4 ? 256 * 16 : 0)); }
 
 // ---------------------------------------------------------------------------
+// Stable scatter into cluster order, tiled: block (b, m) walks row range b
+// (the pq_hist_kernel ranges) of subspace m in tiles of kScatTile rows. Each
+// warp ranks its kScatTile / kScatWarps consecutive rows within their
+// clusters (__match_any_sync per 32 rows plus a warp-private running count),
+// one scan across the warps gives every row its slot in the tile's cluster
+// order, the rows are staged there in shared memory and written out by
+// consecutive threads, so each cluster's part of the tile leaves as one
+// contiguous run of its segment. Row order inside a cluster is kept (warps
+// hold consecutive rows, lanes and groups are in row order).
+// ---------------------------------------------------------------------------
+constexpr int kScatT = 256;
+constexpr int kScatWarps = kScatT / 32;
+constexpr int kScatTile = 4096;
+constexpr int kScatPerWarp = kScatTile / kScatWarps;  // 512 rows: 16 groups of 32
+
+template <int S> struct RowT;
+template <> struct RowT<1> { using T = float; };
+template <> struct RowT<2> { using T = float2; };
+template <> struct RowT<4> { using T = float4; };
+
+size_t scatter_tile_smem(int S) {
+  return (size_t)kScatTile * (S * 4 + 1) + (size_t)kScatWarps * 256 * 4 + 3 * 256 * 4;
+}
+
+template <int S>
+__global__ void __launch_bounds__(kScatT)
+pq_scatter_tile_kernel(const float* __restrict__ XT, uint64_t N, int K, const uint8_t* __restrict__ asg,
+                       const uint32_t* __restrict__ bases, float* __restrict__ sorted,
+                       const uint8_t* __restrict__ state, uint64_t rows_per_cta) {
+  using T = typename RowT<S>::T;
+  extern __shared__ __align__(16) unsigned char scat_smem[];
+  T* srow = reinterpret_cast<T*>(scat_smem);                                   // [kScatTile] rows, tile order
+  uint32_t* wcnt = reinterpret_cast<uint32_t*>(srow + kScatTile);              // [kScatWarps][256]
+  uint32_t* run = wcnt + kScatWarps * 256;                                     // [256] next global slot
+  uint32_t* tstart = run + 256;                                                // [256] tile-local start
+  uint32_t* ttot = tstart + 256;                                               // [256] tile count
+  uint8_t* scl = reinterpret_cast<uint8_t*>(ttot + 256);                       // [kScatTile] cluster per slot
+  const int m = blockIdx.y, b = blockIdx.x, nblk = gridDim.x;
+  if (state[m] != kRunning) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int c = tid; c < 256; c += kScatT) run[c] = c < K ? bases[((size_t)m * nblk + b) * K + c] : 0u;
+  const uint64_t lo = (uint64_t)b * rows_per_cta, hi = min(N, lo + rows_per_cta);
+  const uint8_t* am = asg + (size_t)m * N;
+  const T* xm = reinterpret_cast<const T*>(XT + (size_t)m * N * S);
+  T* sm = reinterpret_cast<T*>(sorted + (size_t)m * N * S);
+  uint32_t* myc = wcnt + warp * 256;
+  for (uint64_t t0 = lo; t0 < hi; t0 += kScatTile) {
+    for (int e = tid; e < kScatWarps * 256; e += kScatT) wcnt[e] = 0;
+    __syncthreads();
+    // ranks inside the warp's rows, in row order
+    constexpr int kG = kScatPerWarp / 32;
+    int cl[kG];
+    uint32_t rk[kG];
+    const uint64_t w0 = t0 + (uint64_t)warp * kScatPerWarp;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const uint64_t r = w0 + (uint64_t)g * 32 + lane;
+      cl[g] = r < hi ? (int)__ldcs(am + r) : 256 + lane;  // 256 + lane: unique, never a cluster
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const uint32_t peers = __match_any_sync(0xffffffffu, cl[g]);
+      const uint32_t below = __popc(peers & lanemask_lt());
+      const bool ok = cl[g] < 256;
+      rk[g] = ok ? myc[cl[g]] + below : 0u;
+      __syncwarp();
+      if (ok && below == 0) myc[cl[g]] += __popc(peers);
+      __syncwarp();
+    }
+    __syncthreads();
+    // per cluster: exclusive offsets of the warps, tile totals, tile starts
+    uint32_t tot = 0;
+    if (tid < 256) {
+      for (int w = 0; w < kScatWarps; ++w) {
+        const uint32_t v = wcnt[w * 256 + tid];
+        wcnt[w * 256 + tid] = tot;
+        tot += v;
+      }
+      ttot[tid] = tot;
+    }
+    __syncthreads();
+    if (tid < 32) {  // exclusive scan of the 256 tile totals, 8 per lane
+      uint32_t v[8], sum = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[q] = ttot[tid * 8 + q];
+        sum += v[q];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      uint32_t acc = incl - sum;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        tstart[tid * 8 + q] = acc;
+        acc += v[q];
+      }
+    }
+    __syncthreads();
+    // stage every row at its slot of the tile's cluster order
+#pragma unroll 4
+    for (int g = 0; g < kG; ++g) {
+      if (cl[g] < 256) {
+        const uint32_t slot = tstart[cl[g]] + wcnt[warp * 256 + cl[g]] + rk[g];
+        srow[slot] = __ldcs(xm + w0 + (uint64_t)g * 32 + lane);
+        scl[slot] = (uint8_t)cl[g];
+      }
+    }
+    __syncthreads();
+    // write out: consecutive threads, consecutive slots of a cluster's run
+    const uint32_t nt = (uint32_t)min((uint64_t)kScatTile, hi - t0);
+    for (uint32_t i = tid; i < nt; i += kScatT) {
+      const int c = scl[i];
+      sm[run[c] + (i - tstart[c])] = srow[i];
+    }
+    __syncthreads();
+    if (tid < 256) run[tid] += tot;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Centroid sums in the reference order. A warp covers 32/S clusters of one
 // subspace; lane = (cluster j, coordinate k) runs one sequential f32 chain.
 // Cluster members stream through a cp.async ring in shared memory
@@ -3064,10 +3189,14 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       ++launches;
     }
     if (prune) MVR_CUDA(ctx, cudaMemcpyAsync(cb_old, cb, (size_t)M * K * S * sizeof(float), cudaMemcpyDeviceToDevice, st));
-    switch (S) {
-      case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
-      case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
-      default: { auto k = pq_scatter_kernel<4>; const size_t sm = scatter_smem(M, 4); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+    {
+      const size_t sm = scatter_tile_smem(S);
+      const dim3 sg((unsigned)nblk, (unsigned)M);
+      switch (S) {
+        case 1: { auto k = pq_scatter_tile_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        case 2: { auto k = pq_scatter_tile_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        default: { auto k = pq_scatter_tile_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+      }
     }
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
