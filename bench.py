@@ -813,6 +813,190 @@ def run_configs4(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- configs[3]
+
+C3_ROWS, C3_DIM, C3_M, C3_ITERS, C3_SAMPLE = 600_000_000, 64, 16, 20, 10_000_000
+C3_BLOCK = 1 << 24  # rows generated and encoded per block
+C3_WORKLOAD = ("configs[3]: synthetic 600,000,000 x 64 f32 (made on the GPU block by block), PQ M=16x4 trained "
+               "(k-means++ + 20 Lloyd iters) on the first 10,000,000 rows, pq.encode of all 600M rows")
+
+
+def run_configs3(args) -> None:
+    """BASELINE configs[3]'s PQ stage: pq.train on a seeded 10M-row sample
+    (the corpus's first 10M rows; subspace-sharded over NCCL at N > 1) and
+    pq.encode of all 600M rows, each rank encoding its contiguous shard
+    block by block (rows made on the GPU by synth.device_residuals, the same
+    rows whatever N). The anchor of each row's token stands in for its
+    coarse (TAC) centroid, as in the default workload. Metric: pq.encode
+    Mvec/s over the 600M rows (device time, max over ranks); the training
+    figure is beside it. One GPU also streams the rows from page-locked host
+    memory through the host-pointer encode (a bounded host buffer, refilled
+    once and replayed, reported as e2e)."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+    from ir_multivector_retrieval_b200 import Context
+    from ir_multivector_retrieval_b200 import dist as mdist
+    from ir_multivector_retrieval_b200 import synth
+    from ir_multivector_retrieval_b200._lib import PqTrainStats
+
+    n_total = args.rows or C3_ROWS
+    n_sample = min(C3_SAMPLE, n_total)
+    dev = f"cuda:{local}"
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    ctx = Context(local)
+    ctx.set_stream(stream.cuda_stream)
+    lib = ctx.lib
+    if world > 1:
+        mdist.init_comm(ctx)
+    S = C3_DIM // C3_M
+    dcb = torch.empty(C3_M * K * S, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- training on the sample (row shard of the first n_sample rows)
+    s0, sn = mdist.shard_rows(n_sample, world, rank)
+    xs, _ = synth.device_residuals(n_total, C3_DIM, seed=42, device=dev, row0=s0, n_rows=sn)
+
+    def train(st):
+        if world > 1:
+            ctx.check(lib.mvr_pq_train_sharded_device(ctx.handle, C.c_void_p(xs.data_ptr()), sn, s0, n_sample, C3_DIM,
+                                                      SEED, 1, C3_M, C3_ITERS, C.c_float(-math.inf),
+                                                      C.c_void_p(dcb.data_ptr()), None, C.byref(st)))
+        else:
+            ctx.check(lib.mvr_pq_train_device(ctx.handle, C.c_void_p(xs.data_ptr()), sn * C3_DIM, C3_DIM, SEED, 1,
+                                              C3_M, C3_ITERS, C.c_float(-math.inf), C.c_void_p(dcb.data_ptr()),
+                                              C.byref(st)))
+
+    for _ in range(max(1, args.warmup)):
+        train(PqTrainStats())
+    barrier()
+    tst = PqTrainStats()
+    train(tst)
+    barrier()
+    train_ms = max_over_ranks(tst.total_ms)
+    cb_host = dcb.cpu().numpy()
+    del xs
+    ctx.check(lib.mvr_ctx_trim(ctx.handle))
+    torch.cuda.empty_cache()
+
+    # ---- encode this rank's shard, block by block (generation untimed)
+    r0, rn = mdist.shard_rows(n_total, world, rank)
+    codes = torch.empty((rn, C3_M), dtype=torch.uint8, device=dev)
+    enc_ms = 0.0
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    for b0 in range(0, rn, C3_BLOCK):
+        bn = min(C3_BLOCK, rn - b0)
+        xb, _ = synth.device_residuals(n_total, C3_DIM, seed=42, device=dev, row0=r0 + b0, n_rows=bn)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.check(lib.mvr_pq_encode_device(ctx.handle, C.c_void_p(dcb.data_ptr()), C3_DIM, C3_M,
+                                           C.c_void_p(xb.data_ptr()), bn, C.c_void_p(codes[b0].data_ptr())))
+        e1.record(stream)
+        e1.synchronize()
+        enc_ms += e0.elapsed_time(e1)
+        if b0 == 0 and world == 1 and not args.no_parity:
+            keep_first = xb[:200_000].cpu().numpy()
+        del xb
+    barrier()
+    clk = clocks.stop()
+    enc_ms = max_over_ranks(enc_ms)
+
+    # ---- one GPU: encode streamed from page-locked host memory
+    e2e = None
+    if world == 1 and not args.no_e2e_stream:
+        hb = min(rn, 1 << 25)  # 33.5M rows, 8.6 GB page-locked
+        xb, _ = synth.device_residuals(n_total, C3_DIM, seed=42, device=dev, row0=0, n_rows=hb)
+        host = torch.empty((hb, C3_DIM), dtype=torch.float32, pin_memory=True)
+        host.copy_(xb)
+        del xb
+        torch.cuda.empty_cache()
+        codes_h = torch.empty((hb, C3_M), dtype=torch.uint8, pin_memory=True)
+        passes = (n_total + hb - 1) // hb
+        t0 = time.perf_counter()
+        done = 0
+        for _ in range(passes):
+            bn = min(hb, n_total - done)
+            ctx.check(lib.mvr_pq_encode(ctx.handle, C.c_void_p(cb_host.ctypes.data), C3_DIM, C3_M,
+                                        C.c_void_p(host.data_ptr()), bn, C.c_void_p(codes_h.data_ptr())))
+            done += bn
+        wall = time.perf_counter() - t0
+        same = bool(np.array_equal(codes_h[:100_000].numpy(), codes[:100_000].cpu().numpy()))
+        e2e = {"value": n_total / wall / 1e6, "unit": "Mvec/s", "h2d_bytes_per_step": int(n_total * C3_DIM * 4),
+               "d2h_bytes_per_step": int(n_total * C3_M),
+               "note": (f"host-pointer pq.encode of {n_total:,} rows from a {hb:,}-row page-locked host buffer "
+                        f"replayed {passes} times (copies overlapped with the encode in chunks); codes equal to the "
+                        f"device path: {same}")}
+        del host, codes_h
+    if rank == 0:
+        line = {
+            "metric": "pq.encode Mvec/s", "value": n_total / (enc_ms / 1e3) / 1e6, "unit": "Mvec/s",
+            "n_gpus": world, "steps": 1, "warmup": args.warmup, "ms_per_step": enc_ms + train_ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (generated on the GPU)",
+            "config": {"workload": C3_WORKLOAD, "rows": n_total, "rows_per_gpu": rn, "dim": C3_DIM, "pq_m": C3_M,
+                       "centroids": K, "lloyd_iters": C3_ITERS, "train_rows": n_sample,
+                       "parallelism": f"row-sharded encode, subspace-sharded training over {world} GPUs (NCCL)"
+                       if world > 1 else "1gpu", "l2": "inputs > L2, no flush"},
+            "codebook_sha256": mdist.codebook_digest(cb_host),
+            "pq_encode_ms": enc_ms, "pq_train_ms": train_ms, "pq_train_s_per_iter": train_ms / 1e3 / C3_ITERS,
+            "seed_ms": tst.seed_ms, "lloyd_ms": tst.lloyd_ms, "seed_fallbacks": int(tst.seed_fallbacks),
+            "clocks": clk,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if world == 1 and not args.no_cpu:
+            from oracle import oracle
+
+            oracle.build()
+            xc, _ = synth.device_residuals(n_total, C3_DIM, seed=42, device=dev, row0=0, n_rows=2_000_000)
+            xc = xc.cpu().numpy()
+            t0 = time.perf_counter()
+            oracle.pq_encode(cb_host, C3_DIM, C3_M, xc, n_threads=host_threads())
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": xc.shape[0] / dt / 1e6, "unit": "Mvec/s", "cores": host_threads(),
+                                    "kind": "port", "sample": "PQ.encode of the first 2,000,000 rows by the C "
+                                                              "restatement on all host threads"}
+        if world == 1 and not args.no_parity:
+            from oracle import oracle
+
+            oracle.build()
+            want = oracle.pq_encode(cb_host, C3_DIM, C3_M, keep_first, n_threads=host_threads())
+            line["pq_encode_bit_exact_vs_cpu"] = {
+                "codes": bool(np.array_equal(want.reshape(-1), codes[:200_000].cpu().numpy().reshape(-1))),
+                "rows": 200_000, "what": "oracle PQ.encode of the first 200,000 rows with the trained codebooks"}
+        print(json.dumps(line), flush=True)
+        print(f"codebook_sha256 {line['codebook_sha256']} n_gpus {world} value {line['value']:.6g}", flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -830,8 +1014,11 @@ def main() -> int:
                     help="only the clusterFlat measurement (one GPU; for profiling captures)")
     ap.add_argument("--hnsw-only", action="store_true",
                     help="only clusterFlat and hnsw.build over its centroids (one GPU)")
-    ap.add_argument("--workload", choices=["configs1", "configs4"], default="configs1",
-                    help="configs1 (default, the headline line) or configs4 (50M x 128, M=32, 25 iterations)")
+    ap.add_argument("--workload", choices=["configs1", "configs3", "configs4"], default="configs1",
+                    help="configs1 (default, the headline line), configs3 (600M x 64: train on 10M rows, encode "
+                         "all) or configs4 (50M x 128, M=32, 25 iterations)")
+    ap.add_argument("--no-e2e-stream", action="store_true",
+                    help="configs3: skip the host-streamed encode leg")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the workload (default 1,521,797; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -848,6 +1035,8 @@ def main() -> int:
         run_reference(args)
     elif args.workload == "configs4":
         run_configs4(args)
+    elif args.workload == "configs3":
+        run_configs3(args)
     else:
         run_b200(args)
     return 0

@@ -1979,40 +1979,68 @@ __device__ __forceinline__ double gamma_bound(uint64_t n) {
 // chain over tens of millions of weights takes a large fraction of a
 // second).
 //
-// A running f64 sum S in the binade [2^e, 2^(e+1)) is a multiple of its
-// ulp u = 2^(e-52), and while S + w stays in that binade, fl(S + w) =
-// S + g u with g = w / u rounded to nearest: a function of w and e alone,
-// except when w's part below u is exactly u / 2 (a tie, decided by the
-// parity of S / u). A chunk of rows whose sums provably stay in one binade
-// (the directed-rounding prefix bounds widened by the classic recursive-sum
-// error bound gamma_N sum w) and hold no tie therefore moves S by exactly
-// G u, G = sum of g: the CTA's warps form every clean chunk's G in
-// parallel, then one thread walks the chunks adding G u (exact) or, for
-// the few chunks that cross a binade or hold a tie, the chunk's weights one
-// by one in the reference's order. The exact chunk-end sums then locate the
-// first row with u_draw < S_i.
+// A running f64 sum S in the binade [2^e, 2^(e+1)) is K u with u = 2^(e-52)
+// and K an integer. While S + w stays in that binade, fl(S + w) = (K + g) u,
+// g = w / u rounded to nearest: a function of w and e alone unless w's part
+// below u is exactly u / 2 (a tie), where round-half-even adds the parity
+// of K + floor(w / u); after a tie K is even. So each row maps the parity
+// of K to (new parity, g): flip or keep for a row without a tie, reset to
+// even for a tie, and a chunk's rows compose into one such map (two
+// (parity, G) pairs, for an even and an odd incoming K), built by a warp
+// scan. A chunk is clean when its sums provably stay in one binade (the
+// directed-rounding prefix bounds widened by the classic recursive-sum
+// error bound gamma_N sum w); one thread then walks the chunks applying
+// each clean chunk's map to the exact running S (an exact add of G u) and
+// adding the weights of the few other chunks (binade crossings) one by one
+// in the reference's order. The exact chunk-end sums locate the first row
+// with u_draw < S_i.
 // ---------------------------------------------------------------------------
 constexpr uint64_t kExactChunkedMinRows = 1u << 18;  // smaller N: the one-thread chain
 
-// g for adding w >= 0 to a sum in binade e (ulps of 2^(e-52), rounded to
-// nearest); `tie` when the part below the ulp is exactly half of it.
-__device__ __forceinline__ uint64_t grid_steps(float w, int e, bool& tie) {
+// A row's (or chunk's) map on the parity of K: for an incoming parity p,
+// K grows by add[p] and leaves with parity out[p].
+struct ParMap {
+  unsigned long long add0, add1;
+  uint32_t out0, out1;
+};
+
+__device__ __forceinline__ ParMap parmap_identity() { return ParMap{0ull, 0ull, 0u, 1u}; }
+
+// first then second
+__device__ __forceinline__ ParMap parmap_then(const ParMap& f, const ParMap& s) {
+  ParMap r;
+  r.add0 = f.add0 + (f.out0 ? s.add1 : s.add0);
+  r.out0 = f.out0 ? s.out1 : s.out0;
+  r.add1 = f.add1 + (f.out1 ? s.add1 : s.add0);
+  r.out1 = f.out1 ? s.out1 : s.out0;
+  return r;
+}
+
+// The map of adding w >= 0 to a sum in binade e.
+__device__ __forceinline__ ParMap parmap_row(float w, int e) {
   const uint32_t b = __float_as_uint(w);
   const int be = (int)(b >> 23);
   const uint64_t mant = be ? (uint64_t)((b & 0x7FFFFFu) | 0x800000u) : (uint64_t)(b & 0x7FFFFFu);
   const int E = be ? be - 127 : -126;  // w = mant * 2^(E - 23)
   const int sh = E - 23 + 52 - e;      // w / u = mant * 2^sh
-  tie = false;
-  if (mant == 0) return 0;
-  if (sh >= 0) return mant << sh;      // the chunk stays below 2^(e+1): mant << sh < 2^53
-  const int rs = -sh;
-  if (rs > 25) return 0;               // w / u < 1/4
-  const uint64_t q = mant >> rs;
-  const uint64_t frac = mant & ((1ull << rs) - 1);
-  const uint64_t half = 1ull << (rs - 1);
-  if (frac > half) return q + 1;
-  tie = frac == half;
-  return q;
+  uint64_t g = 0;
+  if (mant != 0) {
+    if (sh >= 0) {
+      g = mant << sh;  // the chunk stays below 2^(e+1): g < 2^53
+    } else if (-sh <= 25) {  // below: w / u < 1/4, rounds to 0
+      const int rs = -sh;
+      const uint64_t q = mant >> rs;
+      const uint64_t frac = mant & ((1ull << rs) - 1);
+      const uint64_t half = 1ull << (rs - 1);
+      if (frac == half) {  // tie: even K + q stays, odd rounds up; K leaves even
+        const uint64_t q1 = q & 1ull;
+        return ParMap{q + q1, q + (q1 ^ 1ull), 0u, 0u};
+      }
+      g = frac > half ? q + 1 : q;
+    }
+  }
+  const uint32_t gb = (uint32_t)(g & 1ull);
+  return ParMap{g, g, gb, 1u ^ gb};
 }
 
 // Called by all kSelectThreads threads of the CTA of subspace m. ex_lo /
@@ -2021,7 +2049,7 @@ __device__ __forceinline__ uint64_t grid_steps(float w, int e, bool& tie) {
 __device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, uint64_t N, const double2* __restrict__ ch,
                                                   int nchunk, int c_lo, int c_hi, double ex_lo, double ex_hi,
                                                   double B, double r, double2* __restrict__ xpre,
-                                                  unsigned long long* __restrict__ xg, int* __restrict__ xe) {
+                                                  ulonglong2* __restrict__ xg, int* __restrict__ xe) {
   __shared__ unsigned long long s_last;
   __shared__ int s_first;
   __shared__ double s_total;
@@ -2042,7 +2070,8 @@ __device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, u
   }
   __syncthreads();
   // 1b. per chunk (one warp each): its binade if it provably stays in one,
-  // G, ties; and the last non-zero weight
+  // and the chunk's parity map (xe = e | out0 << 16 | out1 << 17, or
+  // INT_MIN to chain it); the last non-zero weight
   unsigned long long last = 0;
   for (int c = warp; c < nchunk; c += kSelectThreads / 32) {
     const double2 pre = xpre[c];
@@ -2054,23 +2083,32 @@ __device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, u
       if (hi_e < ldexp(1.0, e0 + 1)) e = e0;
     }
     const uint64_t r0 = (uint64_t)c * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
-    unsigned long long G = 0;
-    bool tie = false;
-    for (uint64_t i = r0 + lane; i < r1; i += 32) {
-      const float v = w[i];
+    ParMap acc = parmap_identity();
+    for (uint64_t i0 = r0; i0 < r1; i0 += 32) {
+      const uint64_t i = i0 + lane;
+      const float v = i < r1 ? w[i] : 0.f;
       if (v != 0.f) last = max(last, (unsigned long long)i);
-      if (e != INT_MIN) {
-        bool t;
-        G += grid_steps(v, e, t);
-        tie |= t;
-      }
-    }
+      if (e == INT_MIN) continue;  // warp-uniform
+      ParMap f = parmap_row(v, e);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) G += __shfl_xor_sync(0xffffffffu, G, o);
-    if (__any_sync(0xffffffffu, tie)) e = INT_MIN;
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive scan of the maps in row order
+        ParMap p;
+        p.add0 = __shfl_up_sync(0xffffffffu, f.add0, o);
+        p.add1 = __shfl_up_sync(0xffffffffu, f.add1, o);
+        p.out0 = __shfl_up_sync(0xffffffffu, f.out0, o);
+        p.out1 = __shfl_up_sync(0xffffffffu, f.out1, o);
+        if (lane >= o) f = parmap_then(p, f);
+      }
+      ParMap t;
+      t.add0 = __shfl_sync(0xffffffffu, f.add0, 31);
+      t.add1 = __shfl_sync(0xffffffffu, f.add1, 31);
+      t.out0 = __shfl_sync(0xffffffffu, f.out0, 31);
+      t.out1 = __shfl_sync(0xffffffffu, f.out1, 31);
+      acc = parmap_then(acc, t);
+    }
     if (lane == 0) {
-      xg[c] = G;
-      xe[c] = e;
+      xg[c] = make_ulonglong2(acc.add0, acc.add1);
+      xe[c] = e == INT_MIN ? INT_MIN : (int)((uint32_t)(e & 0xFFFF) | (acc.out0 << 16) | (acc.out1 << 17));
     }
   }
 #pragma unroll
@@ -2078,22 +2116,26 @@ __device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, u
   if (lane == 0) atomicMax(&s_last, last);
   __syncthreads();
   // 2. one thread: exact chunk-end sums (xpre[c].x), in the reference's
-  //    order; the per-chunk terms are staged in shared memory a tile at a time
-  constexpr int kTile = 2048;
-  __shared__ double s_step[kTile];  // G u of a clean chunk, NaN for a chunk to chain
+  //    order; the per-chunk maps are staged in shared memory a tile at a time
+  constexpr int kTile = 1024;
+  __shared__ ulonglong2 s_add[kTile];
+  __shared__ int s_e[kTile];
   double S = 0.0;
   for (int t0 = 0; t0 < nchunk; t0 += kTile) {
     const int tn = min(kTile, nchunk - t0);
     for (int q = tid; q < tn; q += kSelectThreads) {
-      const int e = xe[t0 + q];
-      s_step[q] = e != INT_MIN ? ldexp((double)xg[t0 + q], e - 52) : __longlong_as_double(0x7ff8000000000000ll);
+      s_add[q] = xg[t0 + q];
+      s_e[q] = xe[t0 + q];
     }
     __syncthreads();
     if (tid == 0) {
       for (int q = 0; q < tn; ++q) {
-        const double g = s_step[q];
-        if (!isnan(g)) {
-          S = __dadd_rn(S, g);  // exact: same binade, a multiple of its ulp
+        const int x = s_e[q];
+        if (x != INT_MIN) {
+          const int e = (int)(int16_t)(x & 0xFFFF);
+          const uint64_t K0 = (uint64_t)ldexp(S, 52 - e);  // S = K0 * 2^(e-52) exactly
+          const ulonglong2 a = s_add[q];
+          S = __dadd_rn(S, ldexp((double)((K0 & 1ull) ? a.y : a.x), e - 52));  // exact: same binade
         } else {
           const uint64_t r0 = (uint64_t)(t0 + q) * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
           uint64_t i = r0;
@@ -2124,11 +2166,11 @@ __device__ __noinline__ uint64_t exact_chain_draw(const float* __restrict__ w, u
     uint64_t pick = s_last;  // the reference's fallback: last positive weight
     const int c = s_first;
     if (c < nchunk) {
-      double S = c > 0 ? xpre[c - 1].x : 0.0;
+      double Sc = c > 0 ? xpre[c - 1].x : 0.0;
       const uint64_t r0 = (uint64_t)c * kSeedChunk, r1 = min(N, r0 + kSeedChunk);
       for (uint64_t i = r0; i < r1; ++i) {
-        S = __dadd_rn(S, (double)w[i]);
-        if (u < S) { pick = i; break; }
+        Sc = __dadd_rn(Sc, (double)w[i]);
+        if (u < Sc) { pick = i; break; }
       }
     }
     s_pick = pick;
@@ -2162,7 +2204,7 @@ pq_seed_select_kernel(const float* __restrict__ XT, uint64_t N, int S, int K, in
                       int* __restrict__ status, uint8_t* __restrict__ state,
                       uint32_t* __restrict__ fallbacks, uint64_t* __restrict__ chosen,
                       double* __restrict__ thr, int force_chain, double2* __restrict__ xpre,
-                      unsigned long long* __restrict__ xg, int* __restrict__ xe) {
+                      ulonglong2* __restrict__ xg, int* __restrict__ xe) {
   grid_dependency_wait();
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
@@ -2909,7 +2951,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_chunk_cnt = carve((size_t)M * L.nchunk * sizeof(uint32_t));
   // exact chained draws (large N): chunk prefix bounds / end sums, G, binade
   L.o_xpre = carve((size_t)M * L.nchunk * sizeof(double2));
-  L.o_xg = carve((size_t)M * L.nchunk * sizeof(unsigned long long));
+  L.o_xg = carve((size_t)M * L.nchunk * sizeof(ulonglong2));
   L.o_xe = carve((size_t)M * L.nchunk * sizeof(int));
   L.o_ub = carve((size_t)M * N * sizeof(float));
   L.o_lb = carve((size_t)M * N * sizeof(float));
@@ -3045,7 +3087,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
                              step + 1, cb, (const float*)mind, (const double2*)chunk, (const uint32_t*)chunk_cnt,
                              nchunk, (const double*)d_draws, d_nonf, d_status, d_state, d_fb, d_chosen, d_thr,
                              ctx && ctx->serial_draws ? 1 : 0, (double2*)(ws + L.o_xpre),
-                             (unsigned long long*)(ws + L.o_xg), (int*)(ws + L.o_xe)));
+                             (ulonglong2*)(ws + L.o_xg), (int*)(ws + L.o_xe)));
     launches += 2;
   }
   if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
