@@ -838,10 +838,14 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
 // exact value, where (all bounds rounded outwards)
 //   E = 2^-17 (2 |x| max|c| + max|c|^2 + t) + 2^-100.
 // The dropped lo*lo terms and the TF32 truncation of the lo parts add at
-// most 3 * 2^-20 * sum|x_k y_k| (y = -2c) + 2^-20 |c|^2, and the
-// accumulation of three MMAs at most 3 * 2^-21 of the summed magnitudes
-// (taken as four f32 ulps per MMA; the measured error is about one), so E
-// holds with a factor of about two to spare. The row
+// most 3 * 2^-20 * sum|x_k y_k| (y = -2c) + 2^-20 |c|^2. The accumulation
+// is bounded as an f32 accumulator that rounds (or truncates) once per
+// addition: the three MMAs add at most 27 terms, each addition off by at
+// most 2^-23 of the running magnitude, so at most 27 * 2^-23 < 2^-18.2 of
+// the summed magnitudes (NVIDIA does not document the order or width of the
+// tensor core's internal sums; the measured error is about one ulp per
+// MMA). Both stay below 2^-17.3 of (2 |x| max|c| + max|c|^2 + t), so E
+// holds. The row
 // constant t (TF32-exact, >= |x|^2 + E + ...) keeps every a(c) positive, so
 // the f32 bit patterns order like the values; the low 8 bits are replaced
 // by the column index, and integer min/max per column track the smallest
