@@ -1362,34 +1362,87 @@ pq_mind_refresh_kernel(const float* __restrict__ XT, uint64_t N, int K, const fl
 // Per-cluster counts and stable scatter bases: for each (m, c), base of CTA
 // b = start[c] + sum_{b' < b} hist[b'][c].
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+constexpr int kScanThreads = 1024;
+constexpr int kScanWarps = kScanThreads / 32;
+
+// One CTA per subspace: warp w sums the histogram rows of its range of CTAs
+// (nblk split in kScanWarps contiguous ranges, lane = cluster within a group
+// of 32), the per-cluster totals and the ranges' exclusive offsets come from
+// the shared partial sums, one scan over the clusters gives the starts, and
+// each warp rewrites its rows as running bases. Every histogram element is
+// read twice by independent loads (no serial walk over nblk per thread).
+__global__ void __launch_bounds__(kScanThreads)
 pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K, uint32_t* __restrict__ counts,
                uint32_t* __restrict__ starts, const uint8_t* __restrict__ state) {
   const int m = blockIdx.x;
   if (state[m] != kRunning) return;
-  __shared__ uint32_t tot[256];
-  const int c = threadIdx.x;
+  __shared__ uint32_t part[kScanWarps][256];  // range sums, then the ranges' exclusive offsets
+  __shared__ uint32_t cstart[256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* hm = hist + (size_t)m * nblk * K;
-  uint32_t total = 0;
-  if (c < K)
-    for (int b = 0; b < nblk; ++b) total += hm[(size_t)b * K + c];
-  tot[c] = c < K ? total : 0u;
-  __syncthreads();
-  for (int o = 1; o < 256; o <<= 1) {  // inclusive Hillis-Steele scan
-    const uint32_t v = c >= o ? tot[c - o] : 0u;
-    __syncthreads();
-    tot[c] += v;
-    __syncthreads();
+  const int b0 = (int)((int64_t)nblk * warp / kScanWarps), b1 = (int)((int64_t)nblk * (warp + 1) / kScanWarps);
+  uint32_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // clusters lane, lane + 32, ...
+#pragma unroll 2
+  for (int b = b0; b < b1; ++b) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q * 32 + lane < K) sum[q] += hm[(size_t)b * K + q * 32 + lane];
   }
-  const uint32_t start = tot[c] - (c < K ? total : 0u);
-  if (c < K) {
-    counts[(size_t)m * K + c] = total;
-    starts[(size_t)m * K + c] = start;
-    uint32_t run = start;
-    for (int b = 0; b < nblk; ++b) {
-      const uint32_t v = hm[(size_t)b * K + c];
-      hm[(size_t)b * K + c] = run;
-      run += v;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) part[warp][q * 32 + lane] = sum[q];
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t tot = 0;
+    for (int w = 0; w < kScanWarps; ++w) {
+      const uint32_t v = part[w][tid];
+      part[w][tid] = tot;
+      tot += v;
+    }
+    cstart[tid] = tid < K ? tot : 0u;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan of the 256 totals, 8 per lane
+    uint32_t v[8], sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[q] = cstart[lane * 8 + q];
+      sum += v[q];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    uint32_t acc = incl - sum;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int c = lane * 8 + q;
+      if (c < K) {
+        counts[(size_t)m * K + c] = v[q];
+        starts[(size_t)m * K + c] = acc;
+      }
+      cstart[c] = acc;
+      acc += v[q];
+    }
+  }
+  __syncthreads();
+  uint32_t run[8], v[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) run[q] = cstart[q * 32 + lane] + part[warp][q * 32 + lane];
+  if (b0 < b1) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = q * 32 + lane < K ? hm[(size_t)b0 * K + q * 32 + lane] : 0u;
+  }
+  for (int b = b0; b < b1; ++b) {
+    uint32_t nx[8];  // the next row's loads go out before this row's stores
+#pragma unroll
+    for (int q = 0; q < 8; ++q) nx[q] = (b + 1 < b1 && q * 32 + lane < K) ? hm[(size_t)(b + 1) * K + q * 32 + lane] : 0u;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q * 32 + lane < K) hm[(size_t)b * K + q * 32 + lane] = run[q];
+      run[q] += v[q];
+      v[q] = nx[q];
     }
   }
 }
@@ -1724,6 +1777,155 @@ pq_chain_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
   }
 }
 
+// The same chains for 16-byte sub-vectors (S = 4), fed by bulk copies from a
+// producer warp. A CTA is one consumer warp (8 clusters of one subspace, lane
+// = (cluster j, coordinate k), one sequential f32 chain per lane, members
+// added in the order of the sorted copy, as pq_chain_kernel adds them) and
+// one producer warp. A cluster's members are one contiguous run of 16-byte
+// rows in the sorted copy, so a ring stage of a cluster (kChainE members) is
+// one cp.async.bulk; the producer's lane 0 announces each stage's bytes on
+// the stage's `full` mbarrier and issues the stage's copies, and waits on the
+// stage's `empty` mbarrier (released by the consumer) before it refills a
+// slot. The copies thus never hold up the sequential adds, which read full
+// stages through a fully unrolled loop. Every wait is bounded: a wait that
+// expires sets diag[3], the consumer leaves without writing its clusters,
+// and the producer waits (bounded) for the copies it issued before it leaves.
+constexpr int kChainBulkMaxStages = 13;
+constexpr int kChainBulkRow = kChainE * 4 + 4;                  // floats per cluster per stage (+16 B: banks)
+constexpr int kChainBulkStage = 8 * kChainBulkRow;              // floats per stage (8 clusters)
+constexpr int kChainBulkBarBytes = 2 * kChainBulkMaxStages * 8 + 16;  // full, empty, abort flag (16 B aligned)
+
+__device__ __forceinline__ void mbar_expect_arrive(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc::smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* smem, const void* gmem, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          tc::smem_addr(smem)),
+      "l"(gmem), "r"(bytes), "r"(tc::smem_addr(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(64)
+pq_chain_bulk_kernel(const float* __restrict__ sorted, uint64_t N, int M, int K,
+                     const uint32_t* __restrict__ counts, const uint32_t* __restrict__ starts,
+                     float* __restrict__ cb, const uint8_t* __restrict__ state,
+                     const float* __restrict__ start_sums, int raw, int stages, uint32_t* __restrict__ diag) {
+  constexpr int S = 4, CPW = 8;
+  extern __shared__ __align__(128) unsigned char chain_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(chain_smem);
+  uint64_t* empty = full + kChainBulkMaxStages;
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(empty + kChainBulkMaxStages);
+  float* ring = reinterpret_cast<float*>(chain_smem + kChainBulkBarBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpm = (K + CPW - 1) / CPW;
+  const int gw = blockIdx.x;
+  if (gw >= M * wpm) return;  // whole CTA
+  const int m = gw / wpm;
+  if (state[m] != kRunning) return;  // whole CTA
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < stages; ++q) {
+      tc::mbar_init(&full[q], 1);
+      tc::mbar_init(&empty[q], 1);
+    }
+    *abort_flag = 0u;
+  }
+  __syncthreads();
+  const int c0 = (gw % wpm) * CPW;
+
+  if (warp == 1) {  // producer: lane 0 issues every copy
+    if (lane != 0) return;
+    uint32_t cj[CPW], sj[CPW], maxcnt = 0;
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) {
+      cj[q] = c0 + q < K ? counts[(size_t)m * K + c0 + q] : 0u;
+      sj[q] = c0 + q < K ? starts[(size_t)m * K + c0 + q] : 0u;
+      maxcnt = max(maxcnt, cj[q]);
+    }
+    const int nst = (int)((maxcnt + kChainE - 1) / kChainE);
+    const float* sm = sorted + (size_t)m * N * S;
+    int slot = 0, issued = 0;
+    uint32_t phase = 0;
+    for (int t = 0; t < nst; ++t) {
+      if (*abort_flag) break;
+      if (t >= stages && !tc::mbar_wait(&empty[slot], phase ^ 1u)) {
+        atomicExch(&diag[3], 1u);
+        break;
+      }
+      const uint32_t g0 = (uint32_t)t * kChainE;
+      uint32_t total = 0;
+#pragma unroll
+      for (int q = 0; q < CPW; ++q) total += cj[q] > g0 ? min((uint32_t)kChainE, cj[q] - g0) * 16u : 0u;
+      mbar_expect_arrive(&full[slot], total);
+      float* dst = ring + (size_t)slot * kChainBulkStage;
+#pragma unroll
+      for (int q = 0; q < CPW; ++q)
+        if (cj[q] > g0)
+          bulk_g2s(dst + q * kChainBulkRow, sm + (size_t)(sj[q] + g0) * S, min((uint32_t)kChainE, cj[q] - g0) * 16u,
+                   &full[slot]);
+      ++issued;
+      if (++slot == stages) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    // the last copies of each slot have landed before the CTA may leave
+    for (int u = max(0, issued - stages); u < issued; ++u)
+      if (!tc::mbar_wait(&full[u % stages], (uint32_t)(u / stages) & 1u)) atomicExch(&diag[3], 1u);
+    return;
+  }
+
+  // consumer
+  const int j = lane >> 2, k = lane & 3;
+  const int c = c0 + j;
+  const uint32_t cnt = c < K ? counts[(size_t)m * K + c] : 0u;
+  const uint32_t maxcnt = __reduce_max_sync(0xffffffffu, cnt);
+  const int nst = (int)((maxcnt + kChainE - 1) / kChainE);
+  // a row-sharded run continues the previous rank's running sums
+  float acc = (start_sums && c < K) ? start_sums[((size_t)m * K + c) * S + k] : 0.f;
+  int slot = 0;
+  uint32_t phase = 0;
+  for (int t = 0; t < nst; ++t) {
+    if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[slot], phase))) {
+      if (lane == 0) {
+        atomicExch(&diag[3], 1u);
+        *abort_flag = 1u;
+      }
+      return;
+    }
+    const float* src = ring + (size_t)slot * kChainBulkStage + j * kChainBulkRow + k;
+    const uint32_t done = (uint32_t)t * kChainE;
+    const int n = cnt > done ? (int)min((uint32_t)kChainE, cnt - done) : 0;
+    if (n == kChainE) {
+#pragma unroll
+      for (int e = 0; e < kChainE; ++e) acc = __fadd_rn(acc, src[e * S]);
+    } else {
+      int e = 0;
+      for (; e + 8 <= n; e += 8) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = src[(e + q) * S];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, v[q]);
+      }
+      for (; e < n; ++e) acc = __fadd_rn(acc, src[e * S]);
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[slot]);
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+  if (c < K && raw) {
+    cb[((size_t)m * K + c) * S + k] = acc;  // running sums for the next rank
+  } else if (c < K && cnt > 0) {
+    const float inv = __fdiv_rn(1.0f, __uint2float_rn(cnt));
+    cb[((size_t)m * K + c) * S + k] = __fmul_rn(acc, inv);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Sequential f32 WCSS of one subspace (kmeans.zig:179), row order.
 // ---------------------------------------------------------------------------
@@ -1917,54 +2119,102 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
   }
 }
 
-// The same update with one warp per subspace (block = 32 x M threads, one
-// 1024-row chunk per CTA): lane l takes rows l, l + 32, ... of the chunk, so
-// each subspace's chunk sums need one warp reduction instead of one per warp
-// and per subspace, and every lane keeps 32 independent row loads in flight.
+// The same update with W warps per subspace (block = 32 x M x W threads, one
+// 1024-row chunk per CTA): warp w of a subspace takes the chunk's rows
+// w x 1024/W .. (w + 1) x 1024/W - 1, lane l of it rows l, l + 32, ..., so
+// each subspace's chunk sums need one warp reduction per warp and, for W > 1,
+// a second one over the W partial sums. W > 1 serves the few-subspace case
+// (a GPU that trains 1 or 2 subspaces of a subspace-sharded training): more
+// warps in flight per chunk for the same 1024-row chunk sums. The partial
+// sums are directed-rounding bounds, valid in any summation order.
 // A non-finite weight shows up as a non-finite chunk bound (weights are sums
 // of squares, never negative). Odd steps walk the chunks in reverse order, so
 // each pass starts on the rows and weights the previous pass left in L2
 // (every chunk still writes its own sums: the results do not depend on it).
-template <int S>
+template <int S, int W>
 __global__ void __launch_bounds__(kMaxM * 32)
 pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, int step,
                         const float* __restrict__ cb, float* __restrict__ md, double2* __restrict__ chunk,
                         uint32_t* __restrict__ chunk_cnt, int* __restrict__ nonfinite,
                         const uint8_t* __restrict__ state, const double* __restrict__ thr, int chunk_stride) {
+  static_assert(W == 1 || W == 2 || W == 4 || W == 8, "warps per subspace");
+  constexpr int kRowsPerWarp = kSeedChunk / W;
   grid_dependency_wait();  // launched early (programmatic dependent launch): the last step completes first
-  const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
-  if (m >= M || state[m] != kRunning) return;
-  float c[S];
-#pragma unroll
-  for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
-  const double T = thr[m];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = warp / W, part = warp % W;
+  const bool live = m < M && state[m] == kRunning;
   const uint32_t ch = (step & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x;
-  const uint64_t r0 = (uint64_t)ch * kSeedChunk;
-  const float* xm = XT + (size_t)m * N * S;
-  float* mm = md + (size_t)m * N;
   double lo = 0.0, hi = 0.0;
   uint32_t cnt = 0;
+  if (live) {
+    float c[S];
+#pragma unroll
+    for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
+    const double T = thr[m];
+    const uint64_t r0 = (uint64_t)ch * kSeedChunk + (uint64_t)part * kRowsPerWarp;
+    const float* xm = XT + (size_t)m * N * S;
+    float* mm = md + (size_t)m * N;
 #pragma unroll 8
-  for (int q = 0; q < kSeedChunk / 32; ++q) {
-    const uint64_t r = r0 + (uint64_t)(q * 32 + lane);
-    if (r < N) {
-      float x[S];
-      load_sub<S>(xm + r * S, x);
-      const float d = l2_small<S>(x, c);
-      const float w = step == 0 ? d : fminf(d, mm[r]);  // the old weight when d is NaN
-      mm[r] = w;
-      lo = __dadd_rd(lo, (double)w);
-      hi = __dadd_ru(hi, (double)w);
-      cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+    for (int q = 0; q < kRowsPerWarp / 32; ++q) {
+      const uint64_t r = r0 + (uint64_t)(q * 32 + lane);
+      if (r < N) {
+        float x[S];
+        load_sub<S>(xm + r * S, x);
+        const float d = l2_small<S>(x, c);
+        const float w = step == 0 ? d : fminf(d, mm[r]);  // the old weight when d is NaN
+        mm[r] = w;
+        lo = __dadd_rd(lo, (double)w);
+        hi = __dadd_ru(hi, (double)w);
+        cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+      }
     }
+    lo = warp_sum_rd(lo);
+    hi = warp_sum_ru(hi);
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
   }
-  lo = warp_sum_rd(lo);
-  hi = warp_sum_ru(hi);
-  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if constexpr (W > 1) {
+    __shared__ double s_lo[kMaxM * 32 / 32], s_hi[kMaxM * 32 / 32];
+    __shared__ uint32_t s_cnt[kMaxM * 32 / 32];
+    if (lane == 0) {
+      s_lo[warp] = lo;
+      s_hi[warp] = hi;
+      s_cnt[warp] = cnt;
+    }
+    __syncthreads();
+    if (!live || part != 0) return;
+    lo = lane < W ? s_lo[warp + lane] : 0.0;  // adding +0 is exact in either rounding
+    hi = lane < W ? s_hi[warp + lane] : 0.0;
+    cnt = lane < W ? s_cnt[warp + lane] : 0u;
+    lo = warp_sum_rd(lo);
+    hi = warp_sum_ru(hi);
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+  } else {
+    if (!live) return;
+  }
   if (lane == 0) {
     chunk[(size_t)m * chunk_stride + ch] = make_double2(lo, hi);
     chunk_cnt[(size_t)m * chunk_stride + ch] = cnt;
     if (!isfinite(lo) || !isfinite(hi)) nonfinite[m] = 1;
+  }
+}
+
+// Warps per subspace of the weight update: enough warps over the grid to
+// keep about 48 per SM busy when the subspaces alone do not, with the block
+// inside kMaxM x 32 threads.
+static int seed_update_split(uint64_t nchunk, int M, int sms) {
+  const uint64_t want = (uint64_t)std::max(1, sms) * 48;
+  int w = 1;
+  while (w < 8 && nchunk * (uint64_t)M * w < want && M * w * 2 <= kMaxM) w *= 2;
+  return w;
+}
+
+template <int S>
+static decltype(&pq_seed_update_w_kernel<S, 1>) seed_update_kernel(int w) {
+  switch (w) {
+    case 8: return pq_seed_update_w_kernel<S, 8>;
+    case 4: return pq_seed_update_w_kernel<S, 4>;
+    case 2: return pq_seed_update_w_kernel<S, 2>;
+    default: return pq_seed_update_w_kernel<S, 1>;
   }
 }
 
@@ -2495,8 +2745,23 @@ int launch_tc_assign(Ctx* ctx, cudaStream_t st, int mode, bool use_list, const f
 template <int S>
 int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int M, int K,
                  const uint32_t* counts, const uint32_t* starts, float* cb, const uint8_t* state,
-                 const float* start_sums = nullptr, int raw = 0) {
+                 uint32_t* diag, int sm_count, const float* start_sums = nullptr, int raw = 0) {
   constexpr int CPW = 32 / S;
+  if constexpr (S == 4) {
+    // one consumer warp (+ its producer warp) per CTA; the ring is as deep as
+    // the shared memory of the CTAs an SM must hold at once allows
+    const int ctas = M * ((K + CPW - 1) / CPW);
+    const int per_sm = std::max(1, (ctas + std::max(1, sm_count) - 1) / std::max(1, sm_count));
+    const size_t stage_bytes = (size_t)kChainBulkStage * sizeof(float);
+    const size_t fit = (227 * 1024 / (size_t)per_sm - kChainBulkBarBytes) / stage_bytes;
+    const int stages = (int)std::max<size_t>(2, std::min<size_t>(kChainBulkMaxStages, fit));
+    const size_t sm = kChainBulkBarBytes + (size_t)stages * stage_bytes;
+    MVR_CUDA(ctx, cudaFuncSetAttribute(pq_chain_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    pq_chain_bulk_kernel<<<ctas, 64, sm, st>>>(sorted, N, M, K, counts, starts, cb, state, start_sums, raw, stages,
+                                               diag);
+    MVR_CUDA(ctx, cudaGetLastError());
+    return MVR_OK;
+  }
   const size_t sm = (size_t)kChainWarps * kChainStages * CPW * (kChainE * S + S) * sizeof(float);
   auto kern = pq_chain_kernel<S>;
   MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
@@ -3077,12 +3342,13 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         if (e) cudaEventDestroy(e);
     }
   } sev_guard{sev};
+  const int split = seed_update_split((uint64_t)nchunk, M, sms);
   for (int step = 0; step + 1 < K; ++step) {
     const bool sample = timing && step >= 1 && (step - 1) % 8 == 0 && (size_t)(2 * ((step - 1) / 8) + 1) < sev.size();
     if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8)], st));
     {
-      auto upd = S == 1 ? pq_seed_update_w_kernel<1> : S == 2 ? pq_seed_update_w_kernel<2> : pq_seed_update_w_kernel<4>;
-      MVR_CUDA(ctx, launch_pdl(upd, dim3(nchunk), dim3(32 * M), 0, st, (const float*)XT, N, M, K, step,
+      auto upd = S == 1 ? seed_update_kernel<1>(split) : S == 2 ? seed_update_kernel<2>(split) : seed_update_kernel<4>(split);
+      MVR_CUDA(ctx, launch_pdl(upd, dim3(nchunk), dim3(32 * M * split), 0, st, (const float*)XT, N, M, K, step,
                                (const float*)cb, mind, chunk, chunk_cnt, d_nonf, (const uint8_t*)d_state,
                                (const double*)d_thr, nchunk));
     }
@@ -3222,7 +3488,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       MVR_CUDA(ctx, cudaGetLastError());
       ++launches;
     }
-    pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
+    pq_scan_kernel<<<M, kScanThreads, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     if (prune && it > 0 && !need_mind) {  // kept rows have no fresh distance: refresh where a reseed follows
       const dim3 cg(pgx, (unsigned)M);
@@ -3246,9 +3512,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     }
     MVR_CUDA(ctx, cudaGetLastError());
     switch (S) {
-      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
-      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
-      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state)); break;
+      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state, d_diag, sms)); break;
+      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state, d_diag, sms)); break;
+      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, cb, d_state, d_diag, sms)); break;
     }
     pq_reseed_converge_kernel<<<M, 1024, 0, st>>>(XT, N, S, K, d_counts, mind, cb, d_state, d_wcss, d_prev,
                                                   d_iters, d_rs, (int)it, check ? 1 : 0, job.tol, 1,
@@ -3270,6 +3536,8 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   for (int m = 0; m < M; ++m)
     if (hstatus[m] != MVR_OK)
       return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
+  if (((const uint32_t*)(hsmall + L.o_diag))[3])
+    return fail(ctx, MVR_E_TIMEOUT, "centroid sums: a bulk copy of cluster members did not complete in time");
   const uint32_t* hdiag = (const uint32_t*)(hsmall + L.o_diag);
   if (hdiag[2]) return fail(ctx, MVR_E_TIMEOUT, "tensor-core filter: an MMA did not complete in time");
   if (use_tc && hdiag[0] > 0) {
@@ -3470,6 +3738,7 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
   uint32_t* d_fb = (uint32_t*)(small + L.o_fb);
   uint32_t* d_rs = (uint32_t*)(small + L.o_rs);
   uint8_t* d_state = (uint8_t*)(small + L.o_state);
+  uint32_t* d_diag = (uint32_t*)(small + L.o_diag);
   double2* chunk = (double2*)seed_send;
   uint32_t* chunk_cnt = (uint32_t*)(seed_send + sb.o_cnt);
   int* d_nonf = (int*)(seed_send + sb.o_nonf);
@@ -3598,7 +3867,7 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
       default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc)); break;
     }
     if (timing) MVR_CUDA(ctx, cudaEventRecord(aev[2 * it + 1], st));
-    pq_scan_kernel<<<M, 256, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
+    pq_scan_kernel<<<M, kScanThreads, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     MVR_CUDA(ctx, cudaMemcpyAsync(gcounts, d_counts, (size_t)M * K * 4, cudaMemcpyDeviceToDevice, st));
     MVR_TRY(comm_allreduce_sum_u32(ctx, gcounts, (size_t)M * K));
@@ -3622,9 +3891,9 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
     if (me > 0) MVR_TRY(comm_recv(ctx, sums_in, cb_floats * 4, me - 1));
     const float* sstart = me > 0 ? sums_in : nullptr;
     switch (S) {
-      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
-      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
-      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, sstart, 1)); break;
+      case 1: MVR_TRY(launch_chain<1>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, d_diag, sms, sstart, 1)); break;
+      case 2: MVR_TRY(launch_chain<2>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, d_diag, sms, sstart, 1)); break;
+      default: MVR_TRY(launch_chain<4>(ctx, st, sorted, N, M, K, d_counts, d_starts, sums_out, d_state, d_diag, sms, sstart, 1)); break;
     }
     if (me + 1 < G) {
       MVR_TRY(comm_send(ctx, sums_out, cb_floats * 4, me + 1));
@@ -3664,6 +3933,8 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
   for (int m = 0; m < M; ++m)
     if (hstatus[m] != MVR_OK)
       return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
+  if (((const uint32_t*)(hsmall + L.o_diag))[3])
+    return fail(ctx, MVR_E_TIMEOUT, "centroid sums: a bulk copy of cluster members did not complete in time");
   const uint32_t* hiters = (const uint32_t*)(hsmall + L.o_iters);
   const float* hw = (const float*)(hsmall + L.o_wcss);
   if (out.h_iters)
