@@ -526,8 +526,9 @@ def run_b200(args) -> None:
 
     # ---- rooflines. (1) the k-means++ weight update: one HBM pass per step
     # over the subspace-major rows of this GPU's subspaces plus the weights
-    # read and written; launches sampled with CUDA events inside the engine
-    # (every 8th step). (2) the pruned Lloyd passes (iterations >= 1): exact
+    # read (a weight is written back only where the new centroid lowers it:
+    # those few writes are not counted); launches sampled with CUDA events
+    # inside the engine (every 8th step). (2) the pruned Lloyd passes (iterations >= 1): exact
     # (row, centroid) distances actually computed x 12 flops (3 per
     # coordinate, SURVEY's convention) against the FP32 lanes x sampled clock.
     # The line's "roofline" is the one with more device time per training.
@@ -535,7 +536,7 @@ def run_b200(args) -> None:
     upd_ms = sum(s.seed_update_ms_sampled for s in stats) / max(1, upd_samples)
     m_local = PQ_M // world if (world > 1 and PQ_M >= world) else PQ_M
     n_rows = n_total if (world > 1 and PQ_M >= world) else n
-    bytes_per_launch = n_rows * m_local * (DIM // PQ_M) * 4 + 2 * n_rows * m_local * 4
+    bytes_per_launch = n_rows * m_local * (DIM // PQ_M) * 4 + n_rows * m_local * 4
     achieved = bytes_per_launch / (max(upd_ms, 1e-9) / 1e3) / 1e9
     traffic_json = {}
     tfile = ROOT / "profiles" / "traffic.json"

@@ -1599,7 +1599,7 @@ size_t scatter_tile_smem(int S) {
 }
 
 template <int S>
-__global__ void __launch_bounds__(kScatT)
+__global__ void __launch_bounds__(kScatT, 2)
 pq_scatter_tile_kernel(const float* __restrict__ XT, uint64_t N, int K, const uint8_t* __restrict__ asg,
                        const uint32_t* __restrict__ bases, float* __restrict__ sorted,
                        const uint8_t* __restrict__ state, uint64_t rows_per_cta) {
@@ -1627,11 +1627,13 @@ pq_scatter_tile_kernel(const float* __restrict__ XT, uint64_t N, int K, const ui
     constexpr int kG = kScatPerWarp / 32;
     int cl[kG];
     uint32_t rk[kG];
+    T xr[kG];  // the rows themselves, loaded with the assignments: their latency overlaps the ranking
     const uint64_t w0 = t0 + (uint64_t)warp * kScatPerWarp;
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
       const uint64_t r = w0 + (uint64_t)g * 32 + lane;
       cl[g] = r < hi ? (int)__ldcs(am + r) : 256 + lane;  // 256 + lane: unique, never a cluster
+      if (r < hi) xr[g] = __ldcs(xm + r);
     }
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
@@ -1677,17 +1679,18 @@ pq_scatter_tile_kernel(const float* __restrict__ XT, uint64_t N, int K, const ui
     }
     __syncthreads();
     // stage every row at its slot of the tile's cluster order
-#pragma unroll 4
+#pragma unroll
     for (int g = 0; g < kG; ++g) {
       if (cl[g] < 256) {
         const uint32_t slot = tstart[cl[g]] + wcnt[warp * 256 + cl[g]] + rk[g];
-        srow[slot] = __ldcs(xm + w0 + (uint64_t)g * 32 + lane);
+        srow[slot] = xr[g];
         scl[slot] = (uint8_t)cl[g];
       }
     }
     __syncthreads();
     // write out: consecutive threads, consecutive slots of a cluster's run
     const uint32_t nt = (uint32_t)min((uint64_t)kScatTile, hi - t0);
+#pragma unroll 4
     for (uint32_t i = tid; i < nt; i += kScatT) {
       const int c = scl[i];
       sm[run[c] + (i - tstart[c])] = srow[i];
@@ -2084,11 +2087,12 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
         float w;
         if (step == 0) {
           w = d;
+          *slot = w;
         } else {
           const float old = *slot;
           w = d < old ? d : old;
+          if (__float_as_uint(w) != __float_as_uint(old)) *slot = w;  // stored only when it changes
         }
-        *slot = w;
         bad |= !isfinite(w) || w < 0.f;
         lo = __dadd_rd(lo, (double)w);
         hi = __dadd_ru(hi, (double)w);
@@ -2154,18 +2158,33 @@ pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, 
     const uint64_t r0 = (uint64_t)ch * kSeedChunk + (uint64_t)part * kRowsPerWarp;
     const float* xm = XT + (size_t)m * N * S;
     float* mm = md + (size_t)m * N;
-#pragma unroll 8
-    for (int q = 0; q < kRowsPerWarp / 32; ++q) {
-      const uint64_t r = r0 + (uint64_t)(q * 32 + lane);
-      if (r < N) {
-        float x[S];
-        load_sub<S>(xm + r * S, x);
-        const float d = l2_small<S>(x, c);
-        const float w = step == 0 ? d : fminf(d, mm[r]);  // the old weight when d is NaN
-        mm[r] = w;
-        lo = __dadd_rd(lo, (double)w);
-        hi = __dadd_ru(hi, (double)w);
-        cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+    // batches of 8 rows per lane: every load of the batch goes out before
+    // the first (conditional) store
+    constexpr int kBmax = S == 4 ? 4 : 8;  // registers: a block of up to 1024 threads
+    constexpr int kB = kRowsPerWarp / 32 < kBmax ? kRowsPerWarp / 32 : kBmax;
+    for (int q0 = 0; q0 < kRowsPerWarp / 32; q0 += kB) {
+      float x[kB][S], old[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
+        if (r < N) {
+          load_sub<S>(xm + r * S, x[b]);
+          old[b] = step == 0 ? 0.f : mm[r];
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
+        if (r < N) {
+          const float d = l2_small<S>(x[b], c);
+          const float w = step == 0 ? d : fminf(d, old[b]);  // the old weight when d is NaN
+          // stored only when it changes: after the first steps few rows
+          // move to the new centroid, so most of the pass only reads
+          if (step == 0 || __float_as_uint(w) != __float_as_uint(old[b])) mm[r] = w;
+          lo = __dadd_rd(lo, (double)w);
+          hi = __dadd_ru(hi, (double)w);
+          cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+        }
       }
     }
     lo = warp_sum_rd(lo);
