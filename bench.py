@@ -536,7 +536,9 @@ def run_b200(args) -> None:
     upd_ms = sum(s.seed_update_ms_sampled for s in stats) / max(1, upd_samples)
     m_local = PQ_M // world if (world > 1 and PQ_M >= world) else PQ_M
     n_rows = n_total if (world > 1 and PQ_M >= world) else n
-    bytes_per_launch = n_rows * m_local * (DIM // PQ_M) * 4 + n_rows * m_local * 4
+    groups = max(1, max(int(s.groups) for s in stats))  # subspace groups trained side by side
+    m_launch = m_local / groups  # subspaces one update launch covers
+    bytes_per_launch = int(n_rows * m_launch * ((DIM // PQ_M) * 4 + 4))
     achieved = bytes_per_launch / (max(upd_ms, 1e-9) / 1e3) / 1e9
     traffic_json = {}
     tfile = ROOT / "profiles" / "traffic.json"
@@ -546,7 +548,7 @@ def run_b200(args) -> None:
         except Exception:
             traffic_json = {}
     t = traffic_json.get("pq_seed_update_bytes_per_launch")
-    traffic = t * (n_rows * m_local) / (N_ROWS * PQ_M) if t else None
+    traffic = t * (n_rows * m_launch) / (N_ROWS * PQ_M) if t else None
     sm_mhz = clk.get("sm_mhz") or 1965.0
     fp32_nominal = 148 * 128 * sm_mhz * 1e6 / 1e12  # scalar FP32 lanes x clock
     # measured packed f32x2 add/mul issue rate of this GPU (the exact distance
@@ -554,8 +556,9 @@ def run_b200(args) -> None:
     rate = C.c_double(0.0)
     ctx.check(lib.mvr_measure_f32x2_rate(ctx.handle, C.byref(rate)))
     fp32_peak = rate.value / 1e12
-    seed_upd_total_ms = upd_ms * (K - 1)
-    roof_hbm = {"kernel": "pq_seed_update_w_kernel<4> (k-means++ weight update, 255 launches per training)",
+    seed_upd_total_ms = upd_ms * (K - 1) * groups
+    roof_hbm = {"kernel": (f"pq_seed_update_w_kernel<4> (k-means++ weight update, {(K - 1) * groups} launches per "
+                           f"training of {m_launch:g} subspaces each)"),
                 "bound": "hbm", "achieved": achieved, "peak": HBM_PEAK, "unit": "GB/s",
                 "frac": achieved / HBM_PEAK, "traffic": traffic,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth), of measured",

@@ -195,6 +195,12 @@ typedef struct mvr_pq_train_stats {
   uint32_t list_launches;         /* pruned passes timed in list_ms */
   uint64_t list_distances;        /* exact (row, centroid) distances those passes
                                      computed */
+  uint32_t groups;                /* subspace groups trained side by side on two
+                                     streams (1 or 2): each k-means++ update and
+                                     each pruned-pass launch covers pq_m / groups
+                                     subspaces */
+  double host_enqueue_ms;         /* host time spent issuing the work (the longest
+                                     group), against total_ms on the device */
 } mvr_pq_train_stats;
 
 /* Replaces `pq.train(residuals, dim, seed, n_threads, gpa)`
@@ -401,6 +407,12 @@ int mvr_ctx_set_exhaustive_assign(mvr_ctx* ctx, int on);
  * distance from its current centroid is within twice its distance bound
  * (the rest provably cannot win). Results are identical either way. */
 int mvr_ctx_set_candidate_scan(mvr_ctx* ctx, int on);
+
+/* Tuning switch (no reference counterpart): pq.train runs its subspaces in
+ * `groups` groups side by side, each on its own stream (1 or 2; default 2,
+ * used when there are two or more subspaces). Results are identical either
+ * way. */
+int mvr_ctx_set_pq_groups(mvr_ctx* ctx, int groups);
 
 /* Verification mode (no reference counterpart): with `on` == 0 the Lloyd
  * and encode assignments skip the tensor-core filter (a TF32 MMA chain that

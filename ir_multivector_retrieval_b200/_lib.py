@@ -90,6 +90,8 @@ class PqTrainStats(C.Structure):
         ("list_ms", C.c_double),
         ("list_launches", C.c_uint32),
         ("list_distances", C.c_uint64),
+        ("groups", C.c_uint32),
+        ("host_enqueue_ms", C.c_double),
     ]
 
 
@@ -186,6 +188,7 @@ SIGNATURES = {
     "mvr_ctx_set_pq_tensor_filter": (C.c_int, [_P, C.c_int]),
     "mvr_ctx_set_wait_limit": (C.c_int, [_P, C.c_uint32]),
     "mvr_ctx_set_candidate_scan": (C.c_int, [_P, C.c_int]),
+    "mvr_ctx_set_pq_groups": (C.c_int, [_P, C.c_int]),
     "mvr_measure_f32x2_rate": (C.c_int, [_P, C.POINTER(C.c_double)]),
     "mvr_ctx_filter_report": (C.c_int, [_P, _U64, _U64]),
     "mvr_comm_unique_id_bytes": (C.c_size_t, []),

@@ -3,11 +3,14 @@
 // Host-pointer entry points stage inputs into context-owned device buffers,
 // run the device path and copy results back. There is no CPU fallback: a
 // missing or unusable GPU is reported as MVR_E_NO_DEVICE / MVR_E_CUDA.
+#include <cuda.h>  // driver types only: the driver calls come from cudaGetDriverEntryPointByVersion
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -19,8 +22,68 @@
 
 namespace mvr {
 
+namespace {
+thread_local std::string* tl_error_sink = nullptr;
+
+using CtxGetCurrentFn = CUresult(CUDAAPI*)(CUcontext*);
+using CtxGetIdFn = CUresult(CUDAAPI*)(CUcontext, unsigned long long*);
+std::mutex g_ctx_id_mu;
+std::mutex g_smem_mu;
+std::map<std::pair<const void*, unsigned long long>, size_t> g_smem_set;
+}  // namespace
+
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_ctx_id_mu);
+    static bool looked_up = false;
+    if (!looked_up) {
+      looked_up = true;
+      cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
+      if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", reinterpret_cast<void**>(&get_current), 12000,
+                                           cudaEnableDefault, &q1) != cudaSuccess ||
+          q1 != cudaDriverEntryPointSuccess)
+        get_current = nullptr;
+      if (cudaGetDriverEntryPointByVersion("cuCtxGetId", reinterpret_cast<void**>(&get_id), 12000,
+                                           cudaEnableDefault, &q2) != cudaSuccess ||
+          q2 != cudaDriverEntryPointSuccess)
+        get_id = nullptr;
+      (void)cudaGetLastError();
+    }
+  }
+  if (!get_current || !get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+cudaError_t raise_smem_limit(const void* func, size_t bytes) {
+  const unsigned long long id = current_context_id();
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  if (id == 0) {  // no context id: ask the function itself
+    cudaFuncAttributes a{};
+    const cudaError_t q = cudaFuncGetAttributes(&a, func);
+    if (q != cudaSuccess) return q;
+    if ((size_t)a.maxDynamicSharedSizeBytes >= bytes) return cudaSuccess;
+    return cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  }
+  size_t& have = g_smem_set[{func, id}];
+  if (have >= bytes) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
+
+ErrorSink::ErrorSink(std::string* msg) : prev(tl_error_sink) { tl_error_sink = msg; }
+ErrorSink::~ErrorSink() { tl_error_sink = prev; }
+
 int fail(Ctx* ctx, int status, const std::string& msg) {
-  if (ctx) ctx->last_error = msg;
+  if (tl_error_sink)
+    *tl_error_sink = msg;
+  else if (ctx)
+    ctx->last_error = msg;
   return status;
 }
 
@@ -215,6 +278,13 @@ int mvr_ctx_destroy(mvr_ctx* h) {
   if (c->pinned) cudaFreeHost(c->pinned);
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
+  for (auto& t : c->pq_timing) {
+    for (auto& e : t.phase)
+      if (e) cudaEventDestroy(e);
+    for (auto e : t.pool) cudaEventDestroy(e);
+  }
+  for (auto& e : c->pev)
+    if (e) cudaEventDestroy(e);
   if (c->side) {
     cudaStreamSynchronize(c->side);
     cudaStreamDestroy(c->side);
@@ -272,6 +342,12 @@ int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_reche
 int mvr_ctx_set_candidate_scan(mvr_ctx* h, int on) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   h->impl.cand_scan = on != 0;
+  return MVR_OK;
+}
+
+int mvr_ctx_set_pq_groups(mvr_ctx* h, int groups) {
+  if (!h || groups < 1 || groups > 2) return MVR_E_INVALID_ARGUMENT;
+  h->impl.pq_groups = groups;
   return MVR_OK;
 }
 

@@ -37,6 +37,13 @@ enum ScratchSlot {
 class HostPool;
 struct Comm;
 
+// Timing events of one pq.train engine run: the phase marks (start, end of
+// seeding, end of Lloyd) and a pool for the sampled kernel brackets.
+struct PqTiming {
+  cudaEvent_t phase[3] = {nullptr, nullptr, nullptr};
+  std::vector<cudaEvent_t> pool;
+};
+
 struct Ctx {
   int device = 0;
   int sm_count = 0;
@@ -47,6 +54,10 @@ struct Ctx {
   void* pinned = nullptr;  // host staging for small device->host reads
   size_t pinned_bytes = 0;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // pq.train timing events, one set per subspace group (created on first
+  // use), and the whole call's start / end with two groups
+  PqTiming pq_timing[2];
+  cudaEvent_t pev[2] = {nullptr, nullptr};
   // second stream for work that overlaps the main chain (created on first
   // use), with its fork/join events
   cudaStream_t side = nullptr;
@@ -72,6 +83,8 @@ struct Ctx {
   // pruned Lloyd passes scan only the candidate centroids near the current
   // one (off: the bound check + full scans of the failing rows)
   bool cand_scan = true;
+  // pq.train subspace groups run side by side on two streams (1 or 2)
+  int pq_groups = 2;
   // device counters of the filtered encode passes (created on first use):
   // [0] violations, [1] rows re-scanned, [2] timeouts
   uint32_t* tc_diag = nullptr;
@@ -100,6 +113,27 @@ int side_stream(Ctx* ctx, cudaStream_t* out);
 
 // Set the context's last error and return `status`.
 int fail(Ctx* ctx, int status, const std::string& msg);
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId), 0
+// when there is none or the driver does not provide the calls.
+unsigned long long current_context_id();
+
+// Raises `func`'s dynamic shared-memory limit to at least `bytes` in the
+// current CUDA context; never lowers it, and calls cudaFuncSetAttribute only
+// when the limit must grow (the call costs host time at launch sites inside
+// loops). Thread-safe.
+cudaError_t raise_smem_limit(const void* func, size_t bytes);
+
+// While one is alive on a thread, fail() and cuda_fail() on that thread write
+// their message to *msg instead of the context (engine work that runs on
+// several host threads at once; the caller reports one message afterwards).
+struct ErrorSink {
+  explicit ErrorSink(std::string* msg);
+  ~ErrorSink();
+  ErrorSink(const ErrorSink&) = delete;
+  ErrorSink& operator=(const ErrorSink&) = delete;
+  std::string* prev;
+};
 
 // Grow slot `slot` to at least `bytes` (contents are not preserved).
 int scratch(Ctx* ctx, int slot, size_t bytes, void** out);

@@ -10,7 +10,6 @@
 // scratch comes from `g_noalloc_scratch`, a fixed array compiled into this
 // library. Every GPU that loads the library holds that array until the
 // process exits.
-#include <cuda.h>  // driver types only: the two driver calls below come from cudaGetDriverEntryPointByVersion
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -46,36 +45,6 @@ struct ScratchSlot {
 };
 ScratchSlot g_slot[kMaxDevices];
 
-using CtxGetCurrentFn = CUresult(CUDAAPI*)(CUcontext*);
-using CtxGetIdFn = CUresult(CUDAAPI*)(CUcontext, unsigned long long*);
-
-// Unique id of the calling thread's current context, 0 when there is none or
-// the driver does not provide the calls (then every call looks the address
-// up again, which is always correct). Caller holds g_setup_mutex.
-unsigned long long current_context_id() {
-  static bool looked_up = false;
-  static CtxGetCurrentFn get_current = nullptr;
-  static CtxGetIdFn get_id = nullptr;
-  if (!looked_up) {
-    looked_up = true;
-    cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", reinterpret_cast<void**>(&get_current), 12000,
-                                         cudaEnableDefault, &q1) != cudaSuccess ||
-        q1 != cudaDriverEntryPointSuccess)
-      get_current = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", reinterpret_cast<void**>(&get_id), 12000, cudaEnableDefault,
-                                         &q2) != cudaSuccess ||
-        q2 != cudaDriverEntryPointSuccess)
-      get_id = nullptr;
-    (void)cudaGetLastError();
-  }
-  if (!get_current || !get_id) return 0;
-  CUcontext c = nullptr;
-  unsigned long long id = 0;
-  if (get_current(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
-  return id;
-}
-
 // Device address of g_noalloc_scratch in the current device's current
 // context. Looked up on the first call on a device (that call should come
 // before any stream capture on the device) and again whenever the current
@@ -95,7 +64,7 @@ int scratch_address(int device, unsigned char** out) {
     s.arch_ok = (major == 10 && minor == 0) ? 1 : 0;
   }
   if (!s.arch_ok) return MVR_E_NO_DEVICE;
-  const unsigned long long id = current_context_id();
+  const unsigned long long id = mvr::current_context_id();
   if (id == 0 || s.addr == nullptr || s.ctx_id != id) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -106,7 +75,7 @@ int scratch_address(int device, unsigned char** out) {
       return MVR_E_CUDA;
     }
     s.addr = p;
-    s.ctx_id = current_context_id();  // the lookup binds the device's context if none was current
+    s.ctx_id = mvr::current_context_id();  // the lookup binds the device's context if none was current
   }
   *out = static_cast<unsigned char*>(s.addr);
   return MVR_OK;

@@ -33,9 +33,11 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "mvr_device.cuh"
@@ -2123,117 +2125,70 @@ pq_seed_update_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, in
   }
 }
 
-// The same update with W warps per subspace (block = 32 x M x W threads, one
-// 1024-row chunk per CTA): warp w of a subspace takes the chunk's rows
-// w x 1024/W .. (w + 1) x 1024/W - 1, lane l of it rows l, l + 32, ..., so
-// each subspace's chunk sums need one warp reduction per warp and, for W > 1,
-// a second one over the W partial sums. W > 1 serves the few-subspace case
-// (a GPU that trains 1 or 2 subspaces of a subspace-sharded training): more
-// warps in flight per chunk for the same 1024-row chunk sums. The partial
-// sums are directed-rounding bounds, valid in any summation order.
+// The same update with one warp per subspace (block = 32 x M threads, one
+// 1024-row chunk per CTA): lane l takes rows l, l + 32, ... of the chunk in
+// batches of 8 (every load of a batch goes out before the first store), so
+// each subspace's chunk sums need one warp reduction instead of one per warp
+// and per subspace. A weight is stored only when it changes: after the first
+// steps few rows move to the new centroid, so most of the pass only reads.
 // A non-finite weight shows up as a non-finite chunk bound (weights are sums
 // of squares, never negative). Odd steps walk the chunks in reverse order, so
 // each pass starts on the rows and weights the previous pass left in L2
 // (every chunk still writes its own sums: the results do not depend on it).
-template <int S, int W>
+// Measured on B200 at 1.52M rows: 6.4 TB/s of row and weight reads for 16
+// subspaces and 2, ahead of splitting a chunk over several warps per
+// subspace (fewer rows in flight per warp, a block reduction, a partial
+// last wave).
+template <int S>
 __global__ void __launch_bounds__(kMaxM * 32)
 pq_seed_update_w_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, int step,
                         const float* __restrict__ cb, float* __restrict__ md, double2* __restrict__ chunk,
                         uint32_t* __restrict__ chunk_cnt, int* __restrict__ nonfinite,
                         const uint8_t* __restrict__ state, const double* __restrict__ thr, int chunk_stride) {
-  static_assert(W == 1 || W == 2 || W == 4 || W == 8, "warps per subspace");
-  constexpr int kRowsPerWarp = kSeedChunk / W;
+  constexpr int kB = 8;
   grid_dependency_wait();  // launched early (programmatic dependent launch): the last step completes first
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int m = warp / W, part = warp % W;
-  const bool live = m < M && state[m] == kRunning;
+  const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+  if (m >= M || state[m] != kRunning) return;
+  float c[S];
+#pragma unroll
+  for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
+  const double T = thr[m];
   const uint32_t ch = (step & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x;
+  const uint64_t r0 = (uint64_t)ch * kSeedChunk;
+  const float* xm = XT + (size_t)m * N * S;
+  float* mm = md + (size_t)m * N;
   double lo = 0.0, hi = 0.0;
   uint32_t cnt = 0;
-  if (live) {
-    float c[S];
+  for (int q0 = 0; q0 < kSeedChunk / 32; q0 += kB) {
+    float x[kB][S], old[kB];
 #pragma unroll
-    for (int k = 0; k < S; ++k) c[k] = cb[((size_t)m * K + step) * S + k];
-    const double T = thr[m];
-    const uint64_t r0 = (uint64_t)ch * kSeedChunk + (uint64_t)part * kRowsPerWarp;
-    const float* xm = XT + (size_t)m * N * S;
-    float* mm = md + (size_t)m * N;
-    // batches of 8 rows per lane: every load of the batch goes out before
-    // the first (conditional) store
-    constexpr int kBmax = S == 4 ? 4 : 8;  // registers: a block of up to 1024 threads
-    constexpr int kB = kRowsPerWarp / 32 < kBmax ? kRowsPerWarp / 32 : kBmax;
-    for (int q0 = 0; q0 < kRowsPerWarp / 32; q0 += kB) {
-      float x[kB][S], old[kB];
-#pragma unroll
-      for (int b = 0; b < kB; ++b) {
-        const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
-        if (r < N) {
-          load_sub<S>(xm + r * S, x[b]);
-          old[b] = step == 0 ? 0.f : mm[r];
-        }
-      }
-#pragma unroll
-      for (int b = 0; b < kB; ++b) {
-        const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
-        if (r < N) {
-          const float d = l2_small<S>(x[b], c);
-          const float w = step == 0 ? d : fminf(d, old[b]);  // the old weight when d is NaN
-          // stored only when it changes: after the first steps few rows
-          // move to the new centroid, so most of the pass only reads
-          if (step == 0 || __float_as_uint(w) != __float_as_uint(old[b])) mm[r] = w;
-          lo = __dadd_rd(lo, (double)w);
-          hi = __dadd_ru(hi, (double)w);
-          cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
-        }
+    for (int b = 0; b < kB; ++b) {
+      const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
+      if (r < N) {
+        load_sub<S>(xm + r * S, x[b]);
+        old[b] = step == 0 ? 0.f : mm[r];
       }
     }
-    lo = warp_sum_rd(lo);
-    hi = warp_sum_ru(hi);
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-  }
-  if constexpr (W > 1) {
-    __shared__ double s_lo[kMaxM * 32 / 32], s_hi[kMaxM * 32 / 32];
-    __shared__ uint32_t s_cnt[kMaxM * 32 / 32];
-    if (lane == 0) {
-      s_lo[warp] = lo;
-      s_hi[warp] = hi;
-      s_cnt[warp] = cnt;
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const uint64_t r = r0 + (uint64_t)((q0 + b) * 32 + lane);
+      if (r < N) {
+        const float d = l2_small<S>(x[b], c);
+        const float w = step == 0 ? d : fminf(d, old[b]);  // the old weight when d is NaN
+        if (step == 0 || __float_as_uint(w) != __float_as_uint(old[b])) mm[r] = w;
+        lo = __dadd_rd(lo, (double)w);
+        hi = __dadd_ru(hi, (double)w);
+        cnt += (w != 0.f && (double)w < T) ? 1u : 0u;
+      }
     }
-    __syncthreads();
-    if (!live || part != 0) return;
-    lo = lane < W ? s_lo[warp + lane] : 0.0;  // adding +0 is exact in either rounding
-    hi = lane < W ? s_hi[warp + lane] : 0.0;
-    cnt = lane < W ? s_cnt[warp + lane] : 0u;
-    lo = warp_sum_rd(lo);
-    hi = warp_sum_ru(hi);
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-  } else {
-    if (!live) return;
   }
+  lo = warp_sum_rd(lo);
+  hi = warp_sum_ru(hi);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
   if (lane == 0) {
     chunk[(size_t)m * chunk_stride + ch] = make_double2(lo, hi);
     chunk_cnt[(size_t)m * chunk_stride + ch] = cnt;
     if (!isfinite(lo) || !isfinite(hi)) nonfinite[m] = 1;
-  }
-}
-
-// Warps per subspace of the weight update: enough warps over the grid to
-// keep about 48 per SM busy when the subspaces alone do not, with the block
-// inside kMaxM x 32 threads.
-static int seed_update_split(uint64_t nchunk, int M, int sms) {
-  const uint64_t want = (uint64_t)std::max(1, sms) * 48;
-  int w = 1;
-  while (w < 8 && nchunk * (uint64_t)M * w < want && M * w * 2 <= kMaxM) w *= 2;
-  return w;
-}
-
-template <int S>
-static decltype(&pq_seed_update_w_kernel<S, 1>) seed_update_kernel(int w) {
-  switch (w) {
-    case 8: return pq_seed_update_w_kernel<S, 8>;
-    case 4: return pq_seed_update_w_kernel<S, 4>;
-    case 2: return pq_seed_update_w_kernel<S, 2>;
-    default: return pq_seed_update_w_kernel<S, 1>;
   }
 }
 
@@ -2721,17 +2676,17 @@ int launch_assign(Ctx* ctx, cudaStream_t st, int mode, const float* R, const flo
   const size_t sm = assign_smem(M, K, S, mode);
   if (mode == kModeLloyd && ubnd) {
     auto kern = pq_assign_kernel<S, kModeLloyd, true>;
-    MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    MVR_CUDA(ctx, raise_smem_limit((const void*)kern, (size_t)(sm)));
     kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
                                         ubnd, lbnd);
   } else if (mode == kModeLloyd) {
     auto kern = pq_assign_kernel<S, kModeLloyd, false>;
-    MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    MVR_CUDA(ctx, raise_smem_limit((const void*)kern, (size_t)(sm)));
     kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
                                         nullptr, nullptr);
   } else {
     auto kern = pq_assign_kernel<S, kModeEncode, false>;
-    MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    MVR_CUDA(ctx, raise_smem_limit((const void*)kern, (size_t)(sm)));
     kern<<<nblk, kAsgThreads, sm, st>>>(R, XT, N, D, M, K, cb, codes, asg, mind, hist, state, 1.0f, rows_per_cta,
                                         nullptr, nullptr);
   }
@@ -2749,7 +2704,7 @@ int launch_tc_assign(Ctx* ctx, cudaStream_t st, int mode, bool use_list, const f
 #define MVR_TC_LAUNCH(MODE_, LIST_)                                                                            \
   {                                                                                                            \
     auto k = pq_tc_assign_kernel<S, MODE_, LIST_>;                                                             \
-    MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes));    \
+    MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(kTcSmemBytes)));    \
     k<<<grid, kTcBlock, kTcSmemBytes, st>>>(R, XT, N, D, M, K, cb, list, lcnt, codes, asg, mind, ubnd, lbnd, state, \
                                             diag);                                                             \
   }
@@ -2775,7 +2730,7 @@ int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int
     const size_t fit = (227 * 1024 / (size_t)per_sm - kChainBulkBarBytes) / stage_bytes;
     const int stages = (int)std::max<size_t>(2, std::min<size_t>(kChainBulkMaxStages, fit));
     const size_t sm = kChainBulkBarBytes + (size_t)stages * stage_bytes;
-    MVR_CUDA(ctx, cudaFuncSetAttribute(pq_chain_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    MVR_CUDA(ctx, raise_smem_limit((const void*)pq_chain_bulk_kernel, (size_t)(sm)));
     pq_chain_bulk_kernel<<<ctas, 64, sm, st>>>(sorted, N, M, K, counts, starts, cb, state, start_sums, raw, stages,
                                                diag);
     MVR_CUDA(ctx, cudaGetLastError());
@@ -2783,7 +2738,7 @@ int launch_chain(Ctx* ctx, cudaStream_t st, const float* sorted, uint64_t N, int
   }
   const size_t sm = (size_t)kChainWarps * kChainStages * CPW * (kChainE * S + S) * sizeof(float);
   auto kern = pq_chain_kernel<S>;
-  MVR_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  MVR_CUDA(ctx, raise_smem_limit((const void*)kern, (size_t)(sm)));
   const int warps = M * ((K + CPW - 1) / CPW);
   const int grid = (warps + kChainWarps - 1) / kChainWarps;
   kern<<<grid, kChainWarps * 32, sm, st>>>(sorted, N, M, K, counts, starts, cb, state, start_sums, raw);
@@ -3199,7 +3154,7 @@ int pq_encode_device(Ctx* ctx, const float* d_cb, int D, int M, const float* d_R
   }
 }
 
-PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
+PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms, bool with_xt) {
   PqLayout L;
   uint64_t rpc = 0;
   grid_for(N, sms, &L.nblk, &rpc);
@@ -3230,7 +3185,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   L.o_diag = carve(4 * sizeof(uint32_t));
   L.o_ldist = carve((size_t)M * 8);
   L.small_bytes = off;
-  L.o_xt = carve((size_t)M * N * S * sizeof(float));
+  L.o_xt = carve(with_xt ? (size_t)M * N * S * sizeof(float) : 0);
   L.o_mind = carve((size_t)M * N * sizeof(float));
   L.o_asg = carve((size_t)M * N);
   L.o_sorted = carve((size_t)M * N * S * sizeof(float));
@@ -3254,18 +3209,37 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms) {
   return L;
 }
 
-int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out, unsigned char* ws,
-                  unsigned char* hsmall, int sms) {
+// Timing events of one engine run, from the context's pool (created on
+// first use, kept for the context's lifetime): v[i] = pool[offset + i].
+static int pool_events(Ctx* ctx, PqTiming* tm, size_t offset, std::vector<cudaEvent_t>& v) {
+  while (tm->pool.size() < offset + v.size()) {
+    cudaEvent_t e = nullptr;
+    MVR_CUDA(ctx, cudaEventCreate(&e));
+    tm->pool.push_back(e);
+  }
+  for (size_t i = 0; i < v.size(); ++i) v[i] = tm->pool[offset + i];
+  return MVR_OK;
+}
+
+// One group of subspaces (all of them when the engine runs one group):
+// seeding + Lloyd on `st`, then the bookkeeping read back and checked.
+// `ev` holds three timing events (created here when null) when the call
+// reports statistics.
+static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out, unsigned char* ws,
+                             unsigned char* hsmall, int sms, PqTiming* tm) {
+  cudaEvent_t* ev = tm ? tm->phase : nullptr;
   const uint64_t N = job.N;
   const int D = job.D, M = job.M, S = job.S, K = job.K;
   MVR_TRY(check_shape(ctx, D, M, S, K));
   if (N == 0) return fail(ctx, MVR_E_EMPTY_VECTOR_SET, "no rows");
   if (N >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows per subspace");
-  const bool timing = out.stats != nullptr && ctx != nullptr;
+  if (job.xt && !job.xt_ready) return fail(ctx, MVR_E_INVALID_ARGUMENT, "external subspace-major rows not filled");
+  const bool timing = out.stats != nullptr && ctx != nullptr && ev != nullptr;
+  const auto host_t0 = std::chrono::steady_clock::now();
   if (timing) {
-    for (int e = 0; e < 4; ++e)
-      if (!ctx->ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ctx->ev[e]));
-    MVR_CUDA(ctx, cudaEventRecord(ctx->ev[0], st));
+    for (int e = 0; e < 3; ++e)
+      if (!ev[e]) MVR_CUDA(ctx, cudaEventCreate(&ev[e]));
+    MVR_CUDA(ctx, cudaEventRecord(ev[0], st));
   }
 
   // ---- degenerate k >= n -------------------------------------------------
@@ -3281,14 +3255,17 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       if (out.h_wcss) out.h_wcss[m] = 0.f;
       if (out.h_iters) out.h_iters[m] = 0;
     }
-    if (out.stats) std::memset(out.stats, 0, sizeof(*out.stats));
+    if (out.stats) {
+      std::memset(out.stats, 0, sizeof(*out.stats));
+      out.stats->groups = 1;
+    }
     return MVR_OK;
   }
 
-  const PqLayout L = pq_layout(N, M, S, K, sms);
+  const PqLayout L = pq_layout(N, M, S, K, sms, job.xt == nullptr);
   const int nblk = L.nblk, nchunk = L.nchunk;
   const uint64_t rpc = L.rows_per_cta;
-  float* XT = (float*)(ws + L.o_xt);
+  float* XT = job.xt ? const_cast<float*>(job.xt) : (float*)(ws + L.o_xt);
   float* mind = (float*)(ws + L.o_mind);
   uint8_t* asg = (uint8_t*)(ws + L.o_asg);
   float* sorted = (float*)(ws + L.o_sorted);
@@ -3352,22 +3329,14 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   std::vector<cudaEvent_t> sev;
   if (timing) {
     sev.resize(2 * (size_t)((K - 2 + 7) / 8), nullptr);
-    for (auto& e : sev) MVR_CUDA(ctx, cudaEventCreate(&e));
+    MVR_TRY(pool_events(ctx, tm, 0, sev));
   }
-  struct SevGuard {
-    std::vector<cudaEvent_t>& v;
-    ~SevGuard() {
-      for (auto e : v)
-        if (e) cudaEventDestroy(e);
-    }
-  } sev_guard{sev};
-  const int split = seed_update_split((uint64_t)nchunk, M, sms);
   for (int step = 0; step + 1 < K; ++step) {
     const bool sample = timing && step >= 1 && (step - 1) % 8 == 0 && (size_t)(2 * ((step - 1) / 8) + 1) < sev.size();
     if (sample) MVR_CUDA(ctx, cudaEventRecord(sev[2 * ((step - 1) / 8)], st));
     {
-      auto upd = S == 1 ? seed_update_kernel<1>(split) : S == 2 ? seed_update_kernel<2>(split) : seed_update_kernel<4>(split);
-      MVR_CUDA(ctx, launch_pdl(upd, dim3(nchunk), dim3(32 * M * split), 0, st, (const float*)XT, N, M, K, step,
+      auto upd = S == 1 ? pq_seed_update_w_kernel<1> : S == 2 ? pq_seed_update_w_kernel<2> : pq_seed_update_w_kernel<4>;
+      MVR_CUDA(ctx, launch_pdl(upd, dim3(nchunk), dim3(32 * M), 0, st, (const float*)XT, N, M, K, step,
                                (const float*)cb, mind, chunk, chunk_cnt, d_nonf, (const uint8_t*)d_state,
                                (const double*)d_thr, nchunk));
     }
@@ -3379,28 +3348,20 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
                              (ulonglong2*)(ws + L.o_xg), (int*)(ws + L.o_xe)));
     launches += 2;
   }
-  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[1], st));
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ev[1], st));
 
   // ---- Lloyd iterations ---------------------------------------------------
   const bool check = !(job.tol == -INFINITY) && !std::isnan(job.tol);
   std::vector<cudaEvent_t> aev;  // assignment-kernel brackets (stats only)
   if (timing) {
     aev.resize(2 * (size_t)job.max_iters, nullptr);
-    for (auto& e : aev) MVR_CUDA(ctx, cudaEventCreate(&e));
+    MVR_TRY(pool_events(ctx, tm, sev.size(), aev));
   }
-  struct EvGuard {
-    std::vector<cudaEvent_t>& v;
-    ~EvGuard() {
-      for (auto e : v)
-        if (e) cudaEventDestroy(e);
-    }
-  } ev_guard{aev};
   std::vector<cudaEvent_t> lev;  // pruned-pass brackets (stats only)
   if (timing) {
     lev.resize(2 * (size_t)job.max_iters, nullptr);
-    for (auto& e : lev) MVR_CUDA(ctx, cudaEventCreate(&e));
+    MVR_TRY(pool_events(ctx, tm, sev.size() + aev.size(), lev));
   }
-  EvGuard lev_guard{lev};
   uint32_t list_passes = 0;
   // Bound pruning (Hamerly) from the second iteration on; exact, see
   // bound_upper / bound_lower.
@@ -3467,9 +3428,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         }
         MVR_CUDA(ctx, cudaGetLastError());
         switch (S) {
-          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
-          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem)); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 1: { auto k = pq_cand_kernel<1>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(csmem))); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          case 2: { auto k = pq_cand_kernel<2>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(csmem))); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
+          default: { auto k = pq_cand_kernel<4>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(csmem))); k<<<cgrid, kCandThreads, csmem, st>>>(XT, N, K, cb, nbr_idx, nbr_last, asg, ubnd, lbnd, drift, maxd, d_state, mind, nm, lcnt, d_ldist); } break;
         }
         MVR_CUDA(ctx, cudaGetLastError());
       } else {
@@ -3487,9 +3448,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
         }
       } else {
         switch (S) {
-          case 1: { auto k = pq_assign_list_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
-          case 2: { auto k = pq_assign_list_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
-          default: { auto k = pq_assign_list_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)list_smem)); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+          case 1: { auto k = pq_assign_list_kernel<1>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(list_smem))); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+          case 2: { auto k = pq_assign_list_kernel<2>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(list_smem))); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
+          default: { auto k = pq_assign_list_kernel<4>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(list_smem))); k<<<nblk, kAsgThreads, list_smem, st>>>(XT, N, M, K, cb, plist, lcnt, asg, mind, ubnd, lbnd, d_state, 1.0f); } break;
         }
       }
       }
@@ -3524,9 +3485,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
       const size_t sm = scatter_tile_smem(S);
       const dim3 sg((unsigned)nblk, (unsigned)M);
       switch (S) {
-        case 1: { auto k = pq_scatter_tile_kernel<1>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
-        case 2: { auto k = pq_scatter_tile_kernel<2>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
-        default: { auto k = pq_scatter_tile_kernel<4>; MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        case 1: { auto k = pq_scatter_tile_kernel<1>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        case 2: { auto k = pq_scatter_tile_kernel<2>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        default: { auto k = pq_scatter_tile_kernel<4>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
       }
     }
     MVR_CUDA(ctx, cudaGetLastError());
@@ -3540,7 +3501,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
                                                   (prune && it > 0) ? lcnt : nullptr, d_exact);
     MVR_CUDA(ctx, cudaGetLastError());
   }
-  if (timing) MVR_CUDA(ctx, cudaEventRecord(ctx->ev[2], st));
+  if (timing) MVR_CUDA(ctx, cudaEventRecord(ev[2], st));
   if (out.d_assign && job.max_iters > 0) {
     // Converged subspaces keep the assignments of their last iteration,
     // which later iterations did not touch.
@@ -3548,13 +3509,17 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     MVR_CUDA(ctx, cudaGetLastError());
     ++launches;
   }
+  // (measured before the read-back: a copy into pageable memory waits for the stream)
+  const double host_enqueue_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - host_t0).count();
   MVR_CUDA(ctx, cudaMemcpyAsync(hsmall, small, small_bytes, cudaMemcpyDeviceToHost, st));
   MVR_CUDA(ctx, cudaStreamSynchronize(st));
 
   const int* hstatus = (const int*)(hsmall + L.o_status);
   for (int m = 0; m < M; ++m)
     if (hstatus[m] != MVR_OK)
-      return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(m) + ": " + mvr_status_name(hstatus[m]));
+      return fail(ctx, hstatus[m], std::string("subspace ") + std::to_string(job.sub0 + m) + ": " +
+                                        mvr_status_name(hstatus[m]));
   if (((const uint32_t*)(hsmall + L.o_diag))[3])
     return fail(ctx, MVR_E_TIMEOUT, "centroid sums: a bulk copy of cluster members did not complete in time");
   const uint32_t* hdiag = (const uint32_t*)(hsmall + L.o_diag);
@@ -3566,7 +3531,7 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     PqJob exact = job;
     exact.tc_filter = false;
     exact.xt_ready = true;
-    MVR_TRY(pq_kmeans_run(ctx, st, exact, out, ws, hsmall, sms));
+    MVR_TRY(pq_kmeans_run_one(ctx, st, exact, out, ws, hsmall, sms, tm));
     if (out.stats) out.stats->filter_violations = viol;
     return MVR_OK;
   }
@@ -3580,9 +3545,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     std::memset(out.stats, 0, sizeof(*out.stats));
     if (timing) {
       float t01 = 0, t12 = 0, t02 = 0;
-      cudaEventElapsedTime(&t01, ctx->ev[0], ctx->ev[1]);
-      cudaEventElapsedTime(&t12, ctx->ev[1], ctx->ev[2]);
-      cudaEventElapsedTime(&t02, ctx->ev[0], ctx->ev[2]);
+      cudaEventElapsedTime(&t01, ev[0], ev[1]);
+      cudaEventElapsedTime(&t12, ev[1], ev[2]);
+      cudaEventElapsedTime(&t02, ev[0], ev[2]);
       out.stats->seed_ms = t01;
       out.stats->lloyd_ms = t12;
       out.stats->total_ms = t02;
@@ -3650,6 +3615,162 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
     out.stats->seed_fallbacks = fb;
     out.stats->reseeds = rs;
     out.stats->launches = launches;
+    out.stats->groups = 1;
+    out.stats->host_enqueue_ms = host_enqueue_ms;
+  }
+  return MVR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Subspace groups side by side: the subspaces split in two contiguous
+// groups, each an independent training (its own bookkeeping, seeds seed + m,
+// draws, bounds) on its own stream and host thread, over one subspace-major
+// copy of the rows. The k-means++ chain of a group is a sequence of short
+// dependent launches (update, draw) and a Lloyd iteration has latency-bound
+// steps (the sequential centroid sums, the scans, the bound bookkeeping):
+// with two groups in flight the GPU fills one group's gaps with the other's
+// work. Results are those of one group over all subspaces (subspaces do not
+// interact).
+// ---------------------------------------------------------------------------
+constexpr int kPqGroups = 2;
+
+int pq_groups(const Ctx* ctx, uint64_t N, int M, int K) {
+  return (ctx != nullptr && ctx->pq_groups >= 2 && M >= 2 && (uint64_t)K < N) ? kPqGroups : 1;
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+static int group_lo(int M, int G, int g) { return (int)((int64_t)M * g / G); }
+
+size_t pq_ws_bytes(uint64_t N, int M, int S, int K, int sms, int groups) {
+  if (groups <= 1) return pq_layout(N, M, S, K, sms).total_bytes;
+  size_t b = align256((size_t)M * N * S * sizeof(float));
+  for (int g = 0; g < groups; ++g) {
+    const int mg = group_lo(M, groups, g + 1) - group_lo(M, groups, g);
+    b += align256(pq_layout(N, mg, S, K, sms, false).total_bytes);
+  }
+  return b;
+}
+
+float* pq_ws_xt(unsigned char* ws, uint64_t N, int M, int S, int K, int sms, int groups) {
+  if (groups <= 1) return (float*)(ws + pq_layout(N, M, S, K, sms).o_xt);
+  return (float*)ws;
+}
+
+int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out, unsigned char* ws,
+                  unsigned char* hsmall, int sms) {
+  const uint64_t N = job.N;
+  const int D = job.D, M = job.M, S = job.S, K = job.K;
+  const int G = pq_groups(ctx, N, M, K);
+  if (G <= 1) return pq_kmeans_run_one(ctx, st, job, out, ws, hsmall, sms, ctx ? &ctx->pq_timing[0] : nullptr);
+  MVR_TRY(check_shape(ctx, D, M, S, K));
+  if (N >= (1ull << 32)) return fail(ctx, MVR_E_INVALID_ARGUMENT, "more than 2^32-1 rows per subspace");
+  if (!job.xt_ready && !job.R) return fail(ctx, MVR_E_INVALID_ARGUMENT, "no rows given");
+  cudaStream_t side = nullptr;
+  MVR_TRY(side_stream(ctx, &side));
+  if (!ctx->fork_ev) MVR_CUDA(ctx, cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming));
+  if (!ctx->join_ev) MVR_CUDA(ctx, cudaEventCreateWithFlags(&ctx->join_ev, cudaEventDisableTiming));
+  const bool timing = out.stats != nullptr;
+  if (timing) {
+    for (auto& e : ctx->pev)
+      if (!e) MVR_CUDA(ctx, cudaEventCreate(&e));
+    MVR_CUDA(ctx, cudaEventRecord(ctx->pev[0], st));
+  }
+  // one subspace-major copy of the rows for both groups
+  float* XT = job.xt ? const_cast<float*>(job.xt) : (float*)ws;
+  uint32_t launches = 0;
+  if (!job.xt_ready) {
+    const int grid = (int)std::min<uint64_t>((N + 255) / 256, (uint64_t)std::max(1, sms) * 8);
+    switch (S) {
+      case 1: pq_transpose_kernel<1><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      case 2: pq_transpose_kernel<2><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+      default: pq_transpose_kernel<4><<<grid, 256, 0, st>>>(job.R, N, D, M, XT); break;
+    }
+    MVR_CUDA(ctx, cudaGetLastError());
+    ++launches;
+  }
+  MVR_CUDA(ctx, cudaEventRecord(ctx->fork_ev, st));
+  MVR_CUDA(ctx, cudaStreamWaitEvent(side, ctx->fork_ev, 0));
+
+  PqJob jg[kPqGroups];
+  PqOut og[kPqGroups];
+  mvr_pq_train_stats sg[kPqGroups] = {};
+  unsigned char* wsg[kPqGroups];
+  std::vector<unsigned char> hs[kPqGroups];
+  size_t off = align256((size_t)M * N * S * sizeof(float));
+  for (int g = 0; g < G; ++g) {
+    const int m0 = group_lo(M, G, g), mg = group_lo(M, G, g + 1) - m0;
+    jg[g] = job;
+    jg[g].M = mg;
+    jg[g].D = mg * S;
+    jg[g].R = nullptr;  // the group reads XT only
+    jg[g].seed = job.seed + (uint64_t)m0;  // subspace m0 + i uses seed +% (m0 + i)
+    jg[g].xt = XT + (size_t)m0 * N * S;
+    jg[g].xt_ready = true;
+    jg[g].sub0 = job.sub0 + m0;
+    og[g].d_codebooks = out.d_codebooks + (size_t)m0 * K * S;
+    og[g].d_assign = out.d_assign ? out.d_assign + (size_t)m0 * N : nullptr;
+    og[g].h_wcss = out.h_wcss ? out.h_wcss + m0 : nullptr;
+    og[g].h_iters = out.h_iters ? out.h_iters + m0 : nullptr;
+    og[g].stats = timing ? &sg[g] : nullptr;
+    const PqLayout Lg = pq_layout(N, mg, S, K, sms, false);
+    wsg[g] = ws + off;
+    off += align256(Lg.total_bytes);
+    hs[g].resize(Lg.small_bytes);
+  }
+  // group 1 on a second host thread and the side stream, group 0 here
+  std::string err1;
+  int rc1 = MVR_OK;
+  std::thread worker([&] {
+    ErrorSink sink(&err1);
+    rc1 = pq_kmeans_run_one(ctx, side, jg[1], og[1], wsg[1], hs[1].data(), sms, &ctx->pq_timing[1]);
+  });
+  std::string err0;
+  int rc0 = MVR_OK;
+  {
+    ErrorSink sink(&err0);
+    rc0 = pq_kmeans_run_one(ctx, st, jg[0], og[0], wsg[0], hs[0].data(), sms, &ctx->pq_timing[0]);
+  }
+  worker.join();
+  // both groups' work is complete (each run synchronises its stream); the
+  // join keeps the caller's stream ordered after the side stream's work
+  const cudaError_t es = cudaStreamSynchronize(side);
+  if (rc0 != MVR_OK) return fail(ctx, rc0, err0);
+  if (rc1 != MVR_OK) return fail(ctx, rc1, err1);
+  MVR_CUDA(ctx, es);
+  MVR_CUDA(ctx, cudaEventRecord(ctx->join_ev, side));
+  MVR_CUDA(ctx, cudaStreamWaitEvent(st, ctx->join_ev, 0));
+  if (timing) {
+    MVR_CUDA(ctx, cudaEventRecord(ctx->pev[1], st));
+    MVR_CUDA(ctx, cudaEventSynchronize(ctx->pev[1]));
+    mvr_pq_train_stats& o = *out.stats;
+    o = sg[0];
+    const mvr_pq_train_stats& b = sg[1];
+    float t = 0.f;
+    MVR_CUDA(ctx, cudaEventElapsedTime(&t, ctx->pev[0], ctx->pev[1]));
+    o.total_ms = t;  // the whole call, both groups
+    o.seed_ms = std::max(o.seed_ms, b.seed_ms);
+    o.lloyd_ms = std::max(o.lloyd_ms, b.lloyd_ms);
+    o.iters_max = std::max(o.iters_max, b.iters_max);
+    o.iters_min = std::min(o.iters_min, b.iters_min);
+    o.seed_fallbacks += b.seed_fallbacks;
+    o.reseeds += b.reseeds;
+    o.assign_ms += b.assign_ms;
+    o.assign_launches += b.assign_launches;
+    o.launches += b.launches + launches;
+    o.assign_first_ms = std::max(o.assign_first_ms, b.assign_first_ms);
+    o.lloyd_rows_total += b.lloyd_rows_total;
+    o.lloyd_rows_exact += b.lloyd_rows_exact;
+    o.filter_rows_rechecked += b.filter_rows_rechecked;
+    o.filter_violations += b.filter_violations;
+    o.seed_update_ms_sampled += b.seed_update_ms_sampled;
+    o.seed_update_samples += b.seed_update_samples;
+    o.list_ms += b.list_ms;
+    o.list_launches += b.list_launches;
+    o.list_distances += b.list_distances;
+    o.groups = (uint32_t)G;
+    o.host_enqueue_ms = std::max(o.host_enqueue_ms, b.host_enqueue_ms);
+  } else {
+    MVR_CUDA(ctx, cudaStreamSynchronize(st));
   }
   return MVR_OK;
 }
@@ -3657,8 +3778,9 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
 int pq_kmeans_device(Ctx* ctx, const PqJob& job, const PqOut& out) {
   MVR_TRY(check_shape(ctx, job.D, job.M, job.S, job.K));
   const PqLayout L = pq_layout(job.N, job.M, job.S, job.K, ctx->sm_count);
+  const int groups = pq_groups(ctx, job.N, job.M, job.K);
   unsigned char* ws = nullptr;
-  MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
+  MVR_TRY(scratch(ctx, kSlotMinDist, pq_ws_bytes(job.N, job.M, job.S, job.K, ctx->sm_count, groups), (void**)&ws));
   std::vector<unsigned char> hsmall(L.small_bytes);
   return pq_kmeans_run(ctx, ctx->stream, job, out, ws, hsmall.data(), ctx->sm_count);
 }
@@ -3901,9 +4023,9 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
       ++launches;
     }
     switch (S) {
-      case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
-      case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
-      default: { auto k = pq_scatter_kernel<4>; const size_t sm = scatter_smem(M, 4); MVR_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      case 1: { auto k = pq_scatter_kernel<1>; const size_t sm = scatter_smem(M, 1); MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      case 2: { auto k = pq_scatter_kernel<2>; const size_t sm = scatter_smem(M, 2); MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
+      default: { auto k = pq_scatter_kernel<4>; const size_t sm = scatter_smem(M, 4); MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<nblk, 32 * M, sm, st>>>(XT, N, M, K, asg, hist, sorted, d_state, rpc); } break;
     }
     MVR_CUDA(ctx, cudaGetLastError());
     // centroid sums continued rank after rank; the last rank scales
@@ -3962,6 +4084,7 @@ int pq_kmeans_run_dist(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t N_tot
     for (int m = 0; m < M; ++m) out.h_wcss[m] = job.max_iters ? hw[m] : 0.f;
   if (out.stats) {
     std::memset(out.stats, 0, sizeof(*out.stats));
+    out.stats->groups = 1;
     float t01 = 0, t12 = 0, t02 = 0;
     cudaEventElapsedTime(&t01, ctx->ev[0], ctx->ev[1]);
     cudaEventElapsedTime(&t12, ctx->ev[1], ctx->ev[2]);
@@ -4057,9 +4180,10 @@ int pq_kmeans_run_subspaces(Ctx* ctx, const PqJob& job, uint64_t row0, uint64_t 
   }
   // ---- engine workspace for the owned subspaces over all rows ----------------
   const PqLayout L = pq_layout(N_total, std::max(Ml, 1), S, K, sms);
+  const int groups = pq_groups(ctx, N_total, std::max(Ml, 1), K);
   unsigned char* ws = nullptr;
-  MVR_TRY(scratch(ctx, kSlotMinDist, L.total_bytes, (void**)&ws));
-  float* XT_own = (float*)(ws + L.o_xt);
+  MVR_TRY(scratch(ctx, kSlotMinDist, pq_ws_bytes(N_total, std::max(Ml, 1), S, K, sms, groups), (void**)&ws));
+  float* XT_own = pq_ws_xt(ws, N_total, std::max(Ml, 1), S, K, sms, groups);
   uint32_t* asg_own = nullptr;
   if (out.d_assign) MVR_TRY(scratch(ctx, kSlotAux0, (size_t)std::max(Ml, 1) * N_total * 4, (void**)&asg_own));
   // exchange: subspace m of rank g's rows goes to the owner of m

@@ -28,6 +28,11 @@ struct PqJob {
   bool xt_ready = false;
   // assignment passes through the tensor-core filter (pq_tc_assign_kernel)
   bool tc_filter = true;
+  // subspace-major rows [M][N][S] held outside the workspace (the workspace
+  // then has no XT region); requires xt_ready
+  const float* xt = nullptr;
+  // index of subspace 0 in failure messages ("subspace <sub0 + m>")
+  int sub0 = 0;
 };
 
 struct PqOut {
@@ -61,17 +66,33 @@ struct PqLayout {
   size_t total_bytes = 0;
 };
 // Workspace layout for N rows, M subspaces of S floats, K centroids on a
-// device with `sms` streaming multiprocessors.
-PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms);
+// device with `sms` streaming multiprocessors (without the XT region when
+// with_xt is false).
+PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms, bool with_xt = true);
+
+// Subspace groups pq_kmeans_run runs side by side on separate streams: 2
+// when a context is given (the second group runs on its side stream), there
+// are two or more subspaces and K < N; 1 otherwise. Each group is an
+// independent training of its own subspaces, so one group's latency-bound
+// steps (the k-means++ draw, the per-iteration bookkeeping kernels) overlap
+// the other group's bandwidth-bound passes.
+int pq_groups(const Ctx* ctx, uint64_t N, int M, int K);
+// Device workspace pq_kmeans_run needs for `groups` groups (256-byte
+// aligned), and where the subspace-major rows XT [M][N][S] sit in it (a
+// caller that sets job.xt_ready fills them there).
+size_t pq_ws_bytes(uint64_t N, int M, int S, int K, int sms, int groups);
+float* pq_ws_xt(unsigned char* ws, uint64_t N, int M, int S, int K, int sms, int groups);
 
 // Multiprocessor count of the current device (148 if it cannot be read).
 int sm_count_current_device();
 
-// Runs seeding + Lloyd for all M subspaces on `stream`, with device
-// workspace `ws` (pq_layout(...).total_bytes, 256-byte aligned) and host
-// buffer `hsmall` (small_bytes). Allocates no device memory. `ctx` may be
-// null (then no timing and no error text). Returns the MVR status of the
-// smallest failing subspace, or MVR_OK; synchronises `stream`.
+// Runs seeding + Lloyd for all M subspaces on `stream` (and, with two
+// groups, the context's side stream), with device workspace `ws`
+// (pq_ws_bytes(..., pq_groups(...)), 256-byte aligned) and host buffer
+// `hsmall` (pq_layout(...).small_bytes; used with one group). Allocates no
+// device memory. `ctx` may be null (then one group, no timing and no error
+// text). Returns the MVR status of the smallest failing subspace, or MVR_OK;
+// synchronises `stream`.
 int pq_kmeans_run(Ctx* ctx, cudaStream_t stream, const PqJob& job, const PqOut& out,
                   unsigned char* ws, unsigned char* hsmall, int sms);
 
