@@ -143,7 +143,8 @@ int mvr_ctx_init_comm(mvr_ctx* h, int nranks, int rank, const void* id, size_t i
   const auto& a = mvr::api();
   if (!a.ok) return mvr::fail(c, MVR_E_NCCL, a.why);
   mvr::destroy_comm(c);
-  if (cudaSetDevice(c->device) != cudaSuccess) return mvr::fail(c, MVR_E_CUDA, "cudaSetDevice");
+  mvr::DeviceScope dev_scope(c);  // NCCL binds the communicator to the current device
+  if (dev_scope.status != MVR_OK) return dev_scope.status;
   auto* cm = new (std::nothrow) mvr::Comm;
   if (!cm) return MVR_E_OUT_OF_MEMORY;
   cm->rank = rank;

@@ -134,6 +134,8 @@ int mvr_write_doc_layouts_device(mvr_ctx* h, const uint64_t* doc_offsets, uint64
                                  uint32_t pq_m, uint8_t* d_out, uint64_t out_len) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   std::vector<uint64_t> pay;
   MVR_TRY(mvr::check_args(c, doc_offsets, n_docs, n_tokens, pq_m, &pay, out_len));
   if (!d_out || (n_tokens && (!d_assignments || !d_codes))) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
@@ -147,6 +149,8 @@ int mvr_write_doc_layouts(mvr_ctx* h, const uint64_t* doc_offsets, uint64_t n_do
                           const uint8_t* codes, uint64_t n_tokens, uint32_t pq_m, uint8_t* out, uint64_t out_len) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   std::vector<uint64_t> pay;
   MVR_TRY(mvr::check_args(c, doc_offsets, n_docs, n_tokens, pq_m, &pay, out_len));
   if (!out || (n_tokens && (!assignments || !codes))) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");

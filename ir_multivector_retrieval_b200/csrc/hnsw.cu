@@ -1101,6 +1101,8 @@ int mvr_hnsw_build_device(mvr_ctx* ctx, const float* d_centroids, uint64_t n_flo
   if (!ctx || !out || (!d_centroids && n_floats)) return MVR_E_INVALID_ARGUMENT;
   *out = nullptr;
   mvr::Ctx* c = &ctx->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   mvr_hnsw* h = new (std::nothrow) mvr_hnsw;
   if (!h) return mvr::fail(c, MVR_E_OUT_OF_MEMORY, "hnsw.build: host allocation");
   const int s = mvr::hnsw_build_device(c, d_centroids, n_floats, dim, seed, ef_construction, m, n_threads, &h->g);
@@ -1117,6 +1119,8 @@ int mvr_hnsw_build(mvr_ctx* ctx, const float* centroids, uint64_t n_floats, uint
   if (!ctx || !out || (!centroids && n_floats)) return MVR_E_INVALID_ARGUMENT;
   *out = nullptr;
   mvr::Ctx* c = &ctx->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   if (dim == 0 || n_floats % dim) return mvr::fail(c, MVR_E_DIM_MISMATCH, "hnsw.build: centroids.len % dim != 0");
   if (n_floats == 0) return mvr::fail(c, MVR_E_EMPTY_CORPUS, "hnsw.build: no centroids");
   float* d = nullptr;  // staged in the context's scratch (the build's workspace uses another slot)
@@ -1155,12 +1159,16 @@ void mvr_hnsw_free(mvr_hnsw* h) { delete h; }
 
 int mvr_normalize_rows_device(mvr_ctx* ctx, float* d_rows, uint64_t n_floats, uint32_t dim) {
   if (!ctx || (!d_rows && n_floats)) return MVR_E_INVALID_ARGUMENT;
+  mvr::DeviceScope dev_scope(&ctx->impl);
+  MVR_TRY(dev_scope.status);
   return mvr::normalize_rows_device(&ctx->impl, d_rows, n_floats, dim);
 }
 
 int mvr_normalize_rows(mvr_ctx* ctx, float* rows, uint64_t n_floats, uint32_t dim) {
   if (!ctx || (!rows && n_floats)) return MVR_E_INVALID_ARGUMENT;
   mvr::Ctx* c = &ctx->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   if (dim == 0) return mvr::fail(c, MVR_E_EMPTY_INPUT, "normalizeRowsInPlace: dim 0");
   if (n_floats % dim) return mvr::fail(c, MVR_E_LENGTH_MISMATCH, "normalizeRowsInPlace: len % dim != 0");
   if (n_floats == 0) return MVR_OK;

@@ -79,6 +79,21 @@ cudaError_t raise_smem_limit(const void* func, size_t bytes) {
 ErrorSink::ErrorSink(std::string* msg) : prev(tl_error_sink) { tl_error_sink = msg; }
 ErrorSink::~ErrorSink() { tl_error_sink = prev; }
 
+DeviceScope::DeviceScope(Ctx* c) : dev(c->device) {
+  if (cudaGetDevice(&prev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    prev = -1;
+  }
+  if (prev != dev) {
+    const cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) status = cuda_fail(c, e, "cudaSetDevice");
+  }
+}
+
+DeviceScope::~DeviceScope() {
+  if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+}
+
 int fail(Ctx* ctx, int status, const std::string& msg) {
   if (tl_error_sink)
     *tl_error_sink = msg;
@@ -149,12 +164,6 @@ int pinned(Ctx* ctx, size_t bytes, void** out) {
 }
 
 namespace {
-
-int set_device(Ctx* c) {
-  cudaError_t e = cudaSetDevice(c->device);
-  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
-  return MVR_OK;
-}
 
 int h2d(Ctx* c, void* d, const void* h, size_t bytes) { return h2d_staged(c, d, h, bytes); }
 
@@ -258,10 +267,13 @@ int mvr_ctx_create(int device_ordinal, mvr_ctx** out) {
   Ctx* c = &h->impl;
   c->device = device_ordinal;
   c->sm_count = prop.multiProcessorCount;
-  if (cudaSetDevice(device_ordinal) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
-    delete h;
-    return MVR_E_CUDA;
+  {
+    mvr::DeviceScope dev_scope(c);  // the stream belongs to the context's device; the caller's stays current
+    if (dev_scope.status != MVR_OK ||
+        cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+      delete h;
+      return MVR_E_CUDA;
+    }
   }
   c->stream = c->own_stream;
   *out = h;
@@ -271,7 +283,7 @@ int mvr_ctx_create(int device_ordinal, mvr_ctx** out) {
 int mvr_ctx_destroy(mvr_ctx* h) {
   if (!h) return MVR_OK;
   Ctx* c = &h->impl;
-  cudaSetDevice(c->device);
+  mvr::DeviceScope dev_scope(c);
   cudaStreamSynchronize(c->stream);
   for (auto& b : c->slots)
     if (b.ptr) cudaFree(b.ptr);
@@ -330,7 +342,8 @@ int mvr_ctx_filter_report(mvr_ctx* h, uint64_t* violations, uint64_t* rows_reche
   Ctx* c = &h->impl;
   uint32_t dg[4] = {0, 0, 0, 0};
   if (c->tc_diag) {
-    MVR_TRY(mvr::set_device(c));
+    mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
     MVR_CUDA(c, cudaMemcpyAsync(dg, c->tc_diag, sizeof(dg), cudaMemcpyDeviceToHost, c->stream));
     MVR_CUDA(c, cudaStreamSynchronize(c->stream));
   }
@@ -374,7 +387,8 @@ int mvr_ctx_set_stream(mvr_ctx* h, void* s) {
 int mvr_ctx_trim(mvr_ctx* h) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_CUDA(c, cudaStreamSynchronize(c->stream));
   for (auto& b : c->slots) {
     if (b.ptr) cudaFree(b.ptr);
@@ -402,7 +416,8 @@ int mvr_pq_train_device(mvr_ctx* h, const float* d_res, uint64_t len, uint32_t d
   Ctx* c = &h->impl;
   MVR_TRY(mvr::pq_validate(c, len, dim, pq_m));
   if (!d_res || !d_cb) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   mvr::PqJob job;
   job.R = d_res;
   job.N = len / dim;
@@ -428,7 +443,8 @@ int mvr_pq_train_sharded_device(mvr_ctx* h, const float* d_rows, uint64_t n_loca
   Ctx* c = &h->impl;
   // pq.train's validation on the global shape (pq.zig:165-168)
   MVR_TRY(mvr::pq_validate(c, n_total * (uint64_t)dim, dim, pq_m));
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   mvr::PqJob job;
   job.R = d_rows;
   job.N = n_local;
@@ -463,7 +479,8 @@ int mvr_pq_train(mvr_ctx* h, const float* res, uint64_t len, uint32_t dim, uint6
   Ctx* c = &h->impl;
   MVR_TRY(mvr::pq_validate(c, len, dim, pq_m));
   if (!res || !cb_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   float* d_res = nullptr;
   float* d_cb = nullptr;
   const size_t cb_floats = (size_t)MVR_PQ_CENTROIDS * dim;  // pq_m * 256 * sub_dim
@@ -486,7 +503,8 @@ int mvr_pq_encode_device(mvr_ctx* h, const float* d_cb, uint32_t dim, uint32_t p
   if (pq_m == 0 || dim % pq_m != 0) return mvr::fail(c, MVR_E_DIM_NOT_DIVISIBLE_BY_M, "dim % pq_m != 0");
   if (n == 0) return MVR_OK;
   if (!d_cb || !d_res || !d_codes) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   return mvr::pq_encode_device(c, d_cb, (int)dim, (int)pq_m, d_res, n, d_codes);
 }
 
@@ -498,7 +516,8 @@ int mvr_pq_encode(mvr_ctx* h, const float* cb, uint32_t dim, uint32_t pq_m, cons
   if (pq_m == 0 || dim % pq_m != 0) return mvr::fail(c, MVR_E_DIM_NOT_DIVISIBLE_BY_M, "dim % pq_m != 0");
   if (n == 0) return MVR_OK;
   if (!cb || !res || !codes_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   float* d_res = nullptr;
   float* d_cb = nullptr;
   uint8_t* d_codes = nullptr;
@@ -589,7 +608,8 @@ int mvr_kmeans_fit(mvr_ctx* h, const float* vectors, uint64_t len, uint32_t dim,
   if (len == 0) return mvr::fail(c, MVR_E_EMPTY_VECTOR_SET, "no vectors");
   if (len % dim != 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "vectors_len % dim != 0");
   if (!vectors || !centroids_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   const uint64_t n = len / dim;
   float* d_v = nullptr;
   float* d_cent = nullptr;
@@ -640,7 +660,8 @@ int mvr_residuals_norms_device(mvr_ctx* h, const float* d_v, const float* d_cent
   if (dim == 0) return mvr::fail(c, MVR_E_DIM_MISMATCH, "dim == 0");
   if (!d_v || !d_cent || !d_asg || !d_res || !d_norms)
     return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   const int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)c->sm_count * 16);
   mvr::residuals_norms_kernel<<<grid, 256, 0, c->stream>>>(d_v, d_cent, d_asg, n, dim, d_res, d_norms);
   MVR_CUDA(c, cudaGetLastError());
@@ -658,7 +679,8 @@ int mvr_residuals_norms(mvr_ctx* h, const float* v, const float* cent, uint32_t 
     return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
   for (uint64_t i = 0; i < n; ++i)
     if (asg[i] >= kappa) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "assignment >= kappa");
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   float *d_v, *d_cent, *d_res, *d_norms;
   uint32_t* d_asg;
   MVR_TRY(mvr::scratch(c, mvr::kSlotResiduals, n * dim * sizeof(float), (void**)&d_v));

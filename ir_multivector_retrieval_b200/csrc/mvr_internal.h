@@ -114,6 +114,19 @@ int side_stream(Ctx* ctx, cudaStream_t* out);
 // Set the context's last error and return `status`.
 int fail(Ctx* ctx, int status, const std::string& msg);
 
+// Makes the context's device current for the lifetime of the scope and then
+// restores the caller's current device, so an entry point never leaves the
+// calling thread on another GPU. `status` is MVR_OK or the failure to switch.
+struct DeviceScope {
+  explicit DeviceScope(Ctx* c);
+  ~DeviceScope();
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+  int status = 0;
+  int prev = -1;
+  int dev = -1;
+};
+
 // Unique id of the calling thread's current CUDA context (cuCtxGetId), 0
 // when there is none or the driver does not provide the calls.
 unsigned long long current_context_id();

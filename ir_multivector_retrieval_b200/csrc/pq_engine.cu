@@ -3722,7 +3722,11 @@ int pq_kmeans_run(Ctx* ctx, cudaStream_t st, const PqJob& job, const PqOut& out,
   int rc1 = MVR_OK;
   std::thread worker([&] {
     ErrorSink sink(&err1);
-    rc1 = pq_kmeans_run_one(ctx, side, jg[1], og[1], wsg[1], hs[1].data(), sms, &ctx->pq_timing[1]);
+    // a new host thread starts on device 0: bind it to the context's device
+    // before it creates events or launches onto the side stream
+    const cudaError_t e = cudaSetDevice(ctx->device);
+    rc1 = e != cudaSuccess ? cuda_fail(ctx, e, "cudaSetDevice(ctx->device)")
+                           : pq_kmeans_run_one(ctx, side, jg[1], og[1], wsg[1], hs[1].data(), sms, &ctx->pq_timing[1]);
   });
   std::string err0;
   int rc0 = MVR_OK;

@@ -38,6 +38,8 @@ __global__ void __launch_bounds__(256) f32x2_rate_kernel(float* __restrict__ out
 extern "C" int mvr_measure_f32x2_rate(mvr_ctx* h, double* lane_ops_per_s) {
   if (!h || !lane_ops_per_s) return MVR_E_INVALID_ARGUMENT;
   mvr::Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_CUDA(c, cudaSetDevice(c->device));
   const int blocks = c->sm_count * 8, threads = 256, iters = 4000;
   float* out = nullptr;

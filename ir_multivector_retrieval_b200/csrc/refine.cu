@@ -239,6 +239,8 @@ int mvr_pq_distance_table_device(mvr_ctx* h, const float* d_codebooks, uint32_t 
                                  uint64_t out_len) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_TRY(mvr::table_checks(c, dim, pq_m, query_len, n_q, out_len));
   if (!d_codebooks || !d_query || !d_out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
   MVR_TRY(mvr::set_dev(c));
@@ -249,6 +251,8 @@ int mvr_pq_distance_table(mvr_ctx* h, const float* codebooks, uint32_t dim, uint
                           uint64_t query_len, uint32_t n_q, float* out, uint64_t out_len) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_TRY(mvr::table_checks(c, dim, pq_m, query_len, n_q, out_len));
   if (!codebooks || !query || !out) return mvr::fail(c, MVR_E_INVALID_ARGUMENT, "null pointer");
   MVR_TRY(mvr::set_dev(c));
@@ -271,6 +275,8 @@ int mvr_refine_batch_device(mvr_ctx* h, const float* d_centroids, uint32_t kappa
                             uint64_t n_cand, float* d_scores, int* d_status) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_TRY(mvr::refine_checks(c, dim, pq_m, query_len, n_q, table_len));
   if (n_cand && (!d_centroids || !d_doc_section || !d_doc_token_offsets || !d_residual_norms || !d_table ||
                  !d_query || !d_doc_ids || !d_scores || !d_status))
@@ -292,6 +298,8 @@ int mvr_refine_batch(mvr_ctx* h, const float* centroids, uint32_t kappa, uint32_
                      const uint32_t* doc_ids, uint64_t n_cand, float* scores_out) {
   if (!h) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_TRY(mvr::refine_checks(c, dim, pq_m, query_len, n_q, table_len));
   if (n_cand == 0) return MVR_OK;
   if (!centroids || !doc_section || !doc_token_offsets || !residual_norms || !table || !query || !doc_ids ||

@@ -232,11 +232,6 @@ __global__ void tac_place_centroids_kernel(const float* __restrict__ CL, const u
     C[(uint64_t)cmap[e / d] * d + e % d] = CL[e];
 }
 
-int set_device(Ctx* c) {
-  cudaError_t e = cudaSetDevice(c->device);
-  if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
-  return MVR_OK;
-}
 
 }  // namespace
 
@@ -309,7 +304,8 @@ int cluster_flat(mvr_ctx* h, const uint32_t* token_ids, uint64_t n_tokens, const
       for (uint32_t q = goff[j]; q < goff[j + 1]; ++q) rowtok[q] = (uint32_t)j;
   };
   host_ms += since(t_start);
-  MVR_TRY(mvr::set_device(c));
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   cudaStream_t st = c->stream;
   cudaEvent_t* tev = nullptr;
   MVR_TRY(mvr::tac_events(c, &tev));

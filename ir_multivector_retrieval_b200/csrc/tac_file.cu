@@ -196,6 +196,8 @@ int mvr_inverted_lists_build(mvr_ctx* h, const uint32_t* assignments, uint64_t n
                              uint64_t payload_cap, uint64_t* payload_len_out) {
   if (!h || !offsets_out || !payload_len_out) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   // inverted_list.zig:70-87, in order
   if (kappa == 0) return mvr::fail(c, MVR_E_KAPPA_ZERO, "kappa == 0");
   if (doc_offsets_len < 1 || !doc_offsets) return mvr::fail(c, MVR_E_DOC_OFFSETS_BAD, "no doc offsets");
@@ -271,6 +273,8 @@ int mvr_tac_file_size(const mvr_tac_parts* p, uint64_t* bytes_out) {
 int mvr_tac_serialise(mvr_ctx* h, const mvr_tac_parts* p, void* out, uint64_t buf_len, uint64_t* written_out) {
   if (!h || !out) return MVR_E_INVALID_ARGUMENT;
   Ctx* c = &h->impl;
+  mvr::DeviceScope dev_scope(c);
+  MVR_TRY(dev_scope.status);
   MVR_TRY(mvr::check_parts(p));
   const uint64_t total = mvr::file_size(p);
   if (buf_len < total) return mvr::fail(c, MVR_E_BUFFER_TOO_SMALL, "serialise: buffer smaller than the image");

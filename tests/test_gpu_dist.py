@@ -96,8 +96,32 @@ def test_sharded_training_on_several_gpus():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr=127.0.0.1", "--master-port=29517", str(ROOT / "tests" / "dist_worker.py")]
-    r = subprocess.run(["timeout", "-k", "30", "600", *cmd], env=env, capture_output=True, text=True)
+    r = subprocess.run(["timeout", "-k", "30", "300", *cmd], env=env, capture_output=True, text=True)
     out = r.stdout + r.stderr
     print(out[-4000:])
     assert r.returncode == 0, out[-4000:]
     assert "[dist] FAIL" not in out
+
+
+def test_second_device_context_with_two_groups(orc):
+    """A context on the second GPU: pq.train's second subspace group runs on
+    its own host thread, which must work on the context's device (a new
+    thread starts on device 0). Same bytes as the oracle, with one group and
+    with two."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two or more GPUs")
+    from ir_multivector_retrieval_b200 import Context, pq
+
+    x = synth.unit_rows(30_000, 32, seed=21)
+    want = orc.pq_train(x, 32, 4, 8, n_threads=THREADS, max_iters=5, tol=-math.inf)
+    before = torch.cuda.current_device()
+    with Context(1) as ctx1:
+        for groups in (2, 1):
+            ctx1.check(ctx1.lib.mvr_ctx_set_pq_groups(ctx1.handle, groups))
+            st = {}
+            got = pq.train(x, 32, 4, pq_m=8, max_iters=5, tol=-math.inf, ctx=ctx1, stats=st)
+            assert st["groups"] == groups
+            assert got.codebooks.tobytes() == want.tobytes()
+            assert torch.cuda.current_device() == before  # entry points restore the caller's device
+    assert torch.cuda.current_device() == before

@@ -370,3 +370,33 @@ def test_host_encode_chunked_matches_device(ctx):
     assert np.array_equal(out_pin.numpy(), want)
     p = pq.PQ(dim=dim, sub_dim=4, codebooks=cb, pq_m=m)
     assert np.array_equal(p.encode_batch(x.reshape(n, dim)).reshape(-1), want)
+
+
+def test_subspace_groups_match_one_group(ctx, orc):
+    """pq.train with its subspaces in two groups on two streams (the default)
+    gives the bytes of one group and of the oracle, assignments included."""
+    import ctypes as C
+
+    from ir_multivector_retrieval_b200._lib import PqTrainStats
+
+    torch = pytest.importorskip("torch")
+    x = synth.unit_rows(50_000, 64, seed=31)
+    want = orc.pq_train(x, 64, 13, 16, n_threads=8, max_iters=6, tol=-math.inf)
+    dx = torch.from_numpy(x).cuda()
+    out = {}
+    for groups in (1, 2):
+        ctx.check(ctx.lib.mvr_ctx_set_pq_groups(ctx.handle, groups))
+        cb = torch.empty(16 * 256 * 4, dtype=torch.float32, device="cuda")
+        asg = torch.empty(16 * 50_000, dtype=torch.int32, device="cuda")
+        st = PqTrainStats()
+        torch.cuda.synchronize()
+        ctx.check(ctx.lib.mvr_pq_train_sharded_device(ctx.handle, C.c_void_p(dx.data_ptr()), 50_000, 0, 50_000, 64,
+                                                      13, 1, 16, 6, C.c_float(-math.inf), C.c_void_p(cb.data_ptr()),
+                                                      C.c_void_p(asg.data_ptr()), C.byref(st)))
+        assert st.groups == groups
+        out[groups] = (cb.cpu().numpy().tobytes(), asg.cpu().numpy().tobytes())
+    ctx.check(ctx.lib.mvr_ctx_set_pq_groups(ctx.handle, 2))
+    assert out[1] == out[2]
+    assert out[2][0] == want.tobytes()
+    with pytest.raises(MvrError):
+        ctx.check(ctx.lib.mvr_ctx_set_pq_groups(ctx.handle, 3))
