@@ -516,6 +516,7 @@ pq_assign_list_kernel(const float* __restrict__ XT, uint64_t N, int M, int K, co
 constexpr int kCandThreads = 256;
 constexpr int kCandWarps = kCandThreads / 32;
 constexpr int kCandL = 32;                       // listed neighbours per centroid
+constexpr int kCandH = 16;                       // neighbours scanned before the second-stage test
 constexpr int kCandQ = 64;                       // warp queue capacity (< 32 left + 32 new)
 constexpr float kCandCut = 2.0f + 0x1p-18f;      // 1 + kPruneMargin
 constexpr float kCandFloor = 0x1p-50f;
@@ -534,8 +535,10 @@ __device__ __forceinline__ uint32_t nbr_key(float v, int j) {
 }
 
 // nbr_idx[m][a][0..kCandL): the min(kCandL, K - 1) nearest centroids other
-// than a, by increasing key; nbr_last[m][a]: the value of the last key when
-// kCandL are listed. One warp per (m, a); each lane holds 8 candidates
+// than a, by increasing key; nbr_last[m][a][0]: the value of the last key
+// when kCandL are listed, nbr_last[m][a][1]: the value of key kCandH (the
+// first of the list's second half; every later entry's bound is at least
+// that). One warp per (m, a); each lane holds 8 candidates
 // sorted in registers, rounds of a warp minimum pop them in order.
 template <int S>
 __global__ void __launch_bounds__(256)
@@ -586,7 +589,10 @@ pq_nbr_kernel(const float* __restrict__ cb, int K, const uint8_t* __restrict__ s
     if (lane == i) mine = mn;
   }
   nbr_idx[((size_t)m * K + a) * kCandL + lane] = (uint8_t)(mine & 0xFFu);
-  if (lane == L - 1) nbr_last[(size_t)m * K + a] = __uint_as_float(mine);
+  if (lane == L - 1) nbr_last[((size_t)m * K + a) * 2] = __uint_as_float(mine);
+  // the bound of the entry that opens the second half of the list (read only
+  // when the list is full)
+  if (lane == kCandH) nbr_last[((size_t)m * K + a) * 2 + 1] = __uint_as_float(mine);
 }
 
 template <int S>
@@ -604,7 +610,7 @@ size_t cand_smem(int K, int S) {
   const size_t cbytes = ((size_t)K * S * 4 + 15) & ~(size_t)15;
   const size_t ibytes = (size_t)K * kCandL;                   // multiple of 16
   const size_t fbytes = ((size_t)K * 4 + 15) & ~(size_t)15;   // per-centroid floats
-  return cbytes + ibytes + 2 * fbytes + (size_t)kCandWarps * kCandQ * 32;
+  return cbytes + ibytes + 3 * fbytes + (size_t)kCandWarps * kCandQ * (32 + 40);
 }
 
 template <int S>
@@ -625,13 +631,24 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
   uint8_t* sI = smem_raw + cbytes;                                                   // [K][kCandL] neighbours
   float* sV = reinterpret_cast<float*>(smem_raw + cbytes + ibytes);                 // [K] v_last
   float* sD = reinterpret_cast<float*>(smem_raw + cbytes + ibytes + fbytes);        // [K] drifts
-  unsigned char* qbase = smem_raw + cbytes + ibytes + 2 * fbytes;
+  float* sH = reinterpret_cast<float*>(smem_raw + cbytes + ibytes + 2 * fbytes);    // [K] mid-list bound
+  unsigned char* qbase = smem_raw + cbytes + ibytes + 3 * fbytes;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float4* qx = reinterpret_cast<float4*>(qbase) + warp * kCandQ;                    // rows
   float* qd = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 16) + warp * kCandQ;  // f_a
   float* qu = reinterpret_cast<float*>(qbase + (size_t)kCandWarps * kCandQ * 20) + warp * kCandQ;  // ut
   uint32_t* qr = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 24) + warp * kCandQ;
   uint32_t* qa = reinterpret_cast<uint32_t*>(qbase + (size_t)kCandWarps * kCandQ * 28) + warp * kCandQ;
+  // second-stage queue: rows that go on to the second half of their list,
+  // with their first-stage minimum, its index and the second smallest
+  unsigned char* q2base = qbase + (size_t)kCandWarps * kCandQ * 32;
+  float4* q2x = reinterpret_cast<float4*>(q2base) + warp * kCandQ;
+  float* q2u = reinterpret_cast<float*>(q2base + (size_t)kCandWarps * kCandQ * 16) + warp * kCandQ;
+  float* q2b = reinterpret_cast<float*>(q2base + (size_t)kCandWarps * kCandQ * 20) + warp * kCandQ;
+  float* q2s = reinterpret_cast<float*>(q2base + (size_t)kCandWarps * kCandQ * 24) + warp * kCandQ;
+  uint32_t* q2i = reinterpret_cast<uint32_t*>(q2base + (size_t)kCandWarps * kCandQ * 28) + warp * kCandQ;
+  uint32_t* q2r = reinterpret_cast<uint32_t*>(q2base + (size_t)kCandWarps * kCandQ * 32) + warp * kCandQ;
+  uint32_t* q2a = reinterpret_cast<uint32_t*>(q2base + (size_t)kCandWarps * kCandQ * 36) + warp * kCandQ;
   if (tid == 0) s_bad = 0;
   __syncthreads();
   {
@@ -644,7 +661,8 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
     const uint4* gi = reinterpret_cast<const uint4*>(nbr_idx + (size_t)m * K * kCandL);
     for (int e = tid; e < K * kCandL / 16; e += kCandThreads) reinterpret_cast<uint4*>(sI)[e] = gi[e];
     for (int c = tid; c < K; c += kCandThreads) {
-      sV[c] = nbr_last[(size_t)m * K + c];
+      sV[c] = nbr_last[((size_t)m * K + c) * 2];
+      sH[c] = nbr_last[((size_t)m * K + c) * 2 + 1];
       sD[c] = drift[(size_t)m * K + c];
     }
     if (bad) atomicOr(&s_bad, 1);
@@ -654,8 +672,32 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
   const int L = min(kCandL, K - 1);  // listed neighbours; L < kCandL: every centroid is listed
   const float md1 = maxd[3 * m], md2 = maxd[3 * m + 2];
   const uint32_t mi1 = (uint32_t)(int)maxd[3 * m + 1];
-  uint32_t qn = 0, listed = 0;
+  uint32_t qn = 0, q2n = 0, listed = 0;
   unsigned long long dists = 0;
+
+  // Exact distances of x to listed neighbours [h * 16, h * 16 + 16) of a
+  // (those below L), folded into the running first minimum (b, bi; smallest
+  // index on equal values) and second smallest sc.
+  auto scan_half = [&](int h, const float (&x)[S], uint32_t a, float& b, int& bi, float& sc) {
+    const uint4 w = reinterpret_cast<const uint4*>(sI + (size_t)a * kCandL)[h];
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      if (h * 16 + q < L) {
+        const int j = (int)((wd[q >> 2] >> (8 * (q & 3))) & 0xFFu);
+        float c[S];
+        load_centroid<S>(sC, j, c);
+        const float f = l2_small<S>(x, c);
+        if (f < b || (f == b && j < bi)) {
+          sc = fminf(sc, b);
+          b = f;
+          bi = j;
+        } else {
+          sc = fminf(sc, f);
+        }
+      }
+    }
+  };
 
   // Scan the last `cnt` (1..32) queued rows, one per lane.
   auto scan_rows = [&](uint32_t cnt) {
@@ -670,34 +712,21 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
     const float ut = qu[e];
     float b = qd[e], sc = __int_as_float(0x7f800000);
     int bi = (int)a;
-    // the listed neighbours, 16 per 128-bit load of indices
-    const uint4* ip = reinterpret_cast<const uint4*>(sI + (size_t)a * kCandL);
-#pragma unroll
-    for (int h = 0; h < kCandL / 16; ++h) {
-      const uint4 w = ip[h];
-      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        if (h * 16 + q < L) {
-          const int j = (int)((wd[q >> 2] >> (8 * (q & 3))) & 0xFFu);
-          float c[S];
-          load_centroid<S>(sC, j, c);
-          const float f = l2_small<S>(x, c);
-          if (f < b || (f == b && j < bi)) {
-            sc = fminf(sc, b);
-            b = f;
-            bi = j;
-          } else {
-            sc = fminf(sc, f);
-          }
-        }
-      }
-    }
+    // first stage: the first half of a full list (all of a shorter one)
+    scan_half(0, x, a, b, bi, sc);
+    if (L < kCandL) scan_half(1, x, a, b, bi, sc);
     const float vlast = sV[a];
     const float T = __fadd_ru(__fmul_ru(ut, kCandCut), kCandFloor);
     const bool full = act && (bad_cb || !(ut <= 3.0e38f) || (L == kCandL && !(vlast > T)));
-    float lb = fminf(bound_lower(sc), L == kCandL ? __fsub_rd(vlast, ut) : __int_as_float(0x7f800000));
-    unsigned long long cnt_d = (unsigned long long)L + 1;
+    // A full list whose second half may hold a centroid inside the cutoff
+    // (its first entry's bound at or below T) goes on to the second stage;
+    // otherwise every unscanned centroid has a bound above T (the second
+    // half's entries and the unlisted ones alike), as the argument above
+    // requires, and the next lower bound uses the second half's first bound.
+    const float vmid = sH[a];
+    const bool cont = act && !full && L == kCandL && !(vmid > T);
+    float lb = fminf(bound_lower(sc), L == kCandL ? __fsub_rd(vmid, ut) : __int_as_float(0x7f800000));
+    unsigned long long cnt_d = (unsigned long long)(L == kCandL ? kCandH : L) + 1;
     // rows whose cutoff reaches past the list: the warp scans all K, one row at a time
     unsigned fm = __ballot_sync(0xffffffffu, full);
     while (fm) {
@@ -756,7 +785,17 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
         cnt_d = (unsigned long long)K;
       }
     }
-    if (act) {
+    const uint32_t cb2 = __ballot_sync(0xffffffffu, cont);
+    if (cont) {
+      const uint32_t q = q2n + __popc(cb2 & lanemask_lt());
+      q2x[q] = v;
+      q2u[q] = ut;
+      q2b[q] = b;
+      q2s[q] = sc;
+      q2i[q] = (uint32_t)bi;
+      q2r[q] = qr[e];
+      q2a[q] = a;
+    } else if (act) {
       const size_t eo = (size_t)m * N + qr[e];
       asg[eo] = (uint8_t)bi;
       mind[eo] = b;
@@ -764,7 +803,36 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
       lbnd[eo] = lb;
       dists += cnt_d;
     }
+    q2n += __popc(cb2);
     qn -= cnt;
+    __syncwarp();
+  };
+
+  // Second stage for the last `cnt` (1..32) rows of the second-stage queue:
+  // the second half of the list, then the bounds as for a full first stage.
+  auto scan2_rows = [&](uint32_t cnt) {
+    const bool act = (uint32_t)lane < cnt;
+    const uint32_t e = q2n - cnt + (act ? (uint32_t)lane : 0u);
+    const float4 v = q2x[e];
+    float x[S];
+    x[0] = v.x;
+    if constexpr (S > 1) x[1] = v.y;
+    if constexpr (S > 2) { x[2] = v.z; x[3] = v.w; }
+    const uint32_t a = q2a[e];
+    const float ut = q2u[e];
+    float b = q2b[e], sc = q2s[e];
+    int bi = (int)q2i[e];
+    scan_half(1, x, a, b, bi, sc);
+    if (act) {
+      const float lb = fminf(bound_lower(sc), __fsub_rd(sV[a], ut));
+      const size_t eo = (size_t)m * N + q2r[e];
+      asg[eo] = (uint8_t)bi;
+      mind[eo] = b;
+      ubnd[eo] = bound_upper(b);
+      lbnd[eo] = lb;
+      dists += (unsigned long long)L + 1;
+    }
+    q2n -= cnt;
     __syncwarp();
   };
 
@@ -822,8 +890,10 @@ pq_cand_kernel(const float* __restrict__ XT, uint64_t N, int K, const float* __r
     listed += __popc(qb);
     __syncwarp();
     if (qn >= 32) scan_rows(32);
+    if (q2n >= 32) scan2_rows(32);
   }
   if (qn > 0) scan_rows(qn);
+  while (q2n > 0) scan2_rows(q2n < 32u ? q2n : 32u);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) dists += __shfl_xor_sync(0xffffffffu, dists, o);
   if (lane == 0) {
@@ -3204,7 +3274,7 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms, bool with_xt) {
   L.o_drift = carve((size_t)M * K * sizeof(float));
   L.o_maxd = carve((size_t)M * 3 * sizeof(float));
   L.o_nbr = carve((size_t)M * K * kCandL);
-  L.o_nbr_last = carve((size_t)M * K * sizeof(float));
+  L.o_nbr_last = carve((size_t)M * K * 2 * sizeof(float));
   L.total_bytes = off;
   return L;
 }
