@@ -172,7 +172,7 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
     const float b = cbi < K ? cb[((size_t)m * K + cbi) * S + k] : f32_nan();
     cbp[e] = make_float2(-a, -b);  // a NaN pad never wins a strict '<'
   }
-  if (MODE == kModeLloyd)
+  if (MODE == kModeLloyd && hist)
     for (int e = threadIdx.x; e < M * K; e += kAsgThreads) h[e] = 0;
   __syncthreads();
 
@@ -243,7 +243,7 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
           if (ok[j]) {
             asg[(size_t)m * N + row[j]] = (uint8_t)bi[j];
             mind[(size_t)m * N + row[j]] = best[j];
-            atomicAdd(&h[m * K + bi[j]], 1u);
+            if (hist) atomicAdd(&h[m * K + bi[j]], 1u);
             if (BOUNDS) {
               ubnd[(size_t)m * N + row[j]] = bound_upper(best[j]);
               lbnd[(size_t)m * N + row[j]] = isnan(d0[j]) ? -__int_as_float(0x7f800000) : bound_lower(sec[j]);
@@ -265,7 +265,7 @@ pq_assign_kernel(const float* __restrict__ R, const float* __restrict__ XT, uint
       }
     }
   }
-  if (MODE == kModeLloyd) {
+  if (MODE == kModeLloyd && hist) {  // per-CTA histograms (the row-sharded path's scatter)
     __syncthreads();
     const int nblk = gridDim.x;
     for (int e = threadIdx.x; e < M * K; e += kAsgThreads) {
@@ -3259,7 +3259,10 @@ PqLayout pq_layout(uint64_t N, int M, int S, int K, int sms, bool with_xt) {
   L.o_mind = carve((size_t)M * N * sizeof(float));
   L.o_asg = carve((size_t)M * N);
   L.o_sorted = carve((size_t)M * N * S * sizeof(float));
-  L.o_hist = carve((size_t)M * L.nblk * K * sizeof(uint32_t));
+  // the histograms, scan and scatter of the Lloyd passes work on CTAs of one
+  // full scatter tile each (the row-sharded path keeps the persistent grid)
+  L.nblk_s = (int)std::max<uint64_t>(1, (N + kScatTile - 1) / kScatTile);
+  L.o_hist = carve((size_t)M * std::max(L.nblk, L.nblk_s) * K * sizeof(uint32_t));
   L.o_chunk = carve((size_t)M * L.nchunk * sizeof(double2));
   L.o_chunk_cnt = carve((size_t)M * L.nchunk * sizeof(uint32_t));
   // exact chained draws (large N): chunk prefix bounds / end sums, G, binade
@@ -3335,6 +3338,8 @@ static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const 
   const PqLayout L = pq_layout(N, M, S, K, sms, job.xt == nullptr);
   const int nblk = L.nblk, nchunk = L.nchunk;
   const uint64_t rpc = L.rows_per_cta;
+  const int sblk = L.nblk_s;  // histogram / scatter CTAs: one kScatTile-row tile each
+  const uint64_t srpc = kScatTile;
   float* XT = job.xt ? const_cast<float*>(job.xt) : (float*)(ws + L.o_xt);
   float* mind = (float*)(ws + L.o_mind);
   uint8_t* asg = (uint8_t*)(ws + L.o_asg);
@@ -3472,17 +3477,20 @@ static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const 
         case 2: MVR_TRY(launch_tc_assign<2>(ctx, st, kModeLloyd, false, job.R, XT, N, D, M, K, cb, nullptr, nullptr, nullptr, asg, mind, ubnd, lbnd, d_state, d_diag, sms)); break;
         default: MVR_TRY(launch_tc_assign<4>(ctx, st, kModeLloyd, false, job.R, XT, N, D, M, K, cb, nullptr, nullptr, nullptr, asg, mind, ubnd, lbnd, d_state, d_diag, sms)); break;
       }
-      pq_hist_kernel<<<nblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, rpc, hist);
+      pq_hist_kernel<<<sblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, srpc, hist);
       MVR_CUDA(ctx, cudaGetLastError());
       ++launches;
     } else if (!prune || it == 0) {
       float* ub_o = prune ? ubnd : nullptr;
       float* lb_o = prune ? lbnd : nullptr;
       switch (S) {
-        case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
-        case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
-        default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, hist, d_state, nblk, rpc, ub_o, lb_o)); break;
+        case 1: MVR_TRY(launch_assign<1>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, nullptr, d_state, nblk, rpc, ub_o, lb_o)); break;
+        case 2: MVR_TRY(launch_assign<2>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, nullptr, d_state, nblk, rpc, ub_o, lb_o)); break;
+        default: MVR_TRY(launch_assign<4>(ctx, st, kModeLloyd, job.R, XT, N, D, M, K, cb, nullptr, asg, mind, nullptr, d_state, nblk, rpc, ub_o, lb_o)); break;
       }
+      pq_hist_kernel<<<sblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, srpc, hist);
+      MVR_CUDA(ctx, cudaGetLastError());
+      ++launches;
     } else {
       pq_drift_kernel<<<M, 256, 0, st>>>(cb_old, cb, M, K, S, d_state, drift, maxd);
       MVR_CUDA(ctx, cudaMemsetAsync(lcnt, 0, (size_t)M * sizeof(uint32_t), st));
@@ -3527,7 +3535,7 @@ static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const 
       MVR_CUDA(ctx, cudaGetLastError());
       if (timing) MVR_CUDA(ctx, cudaEventRecord(lev[2 * list_passes + 1], st));
       ++list_passes;
-      pq_hist_kernel<<<nblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, rpc, hist);
+      pq_hist_kernel<<<sblk, 512, (size_t)M * K * sizeof(uint32_t), st>>>(asg, N, M, K, d_state, srpc, hist);
       MVR_CUDA(ctx, cudaGetLastError());
       launches += 5;
     }
@@ -3538,7 +3546,7 @@ static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const 
       MVR_CUDA(ctx, cudaGetLastError());
       ++launches;
     }
-    pq_scan_kernel<<<M, kScanThreads, 0, st>>>(hist, nblk, K, d_counts, d_starts, d_state);
+    pq_scan_kernel<<<M, kScanThreads, 0, st>>>(hist, sblk, K, d_counts, d_starts, d_state);
     MVR_CUDA(ctx, cudaGetLastError());
     if (prune && it > 0 && !need_mind) {  // kept rows have no fresh distance: refresh where a reseed follows
       const dim3 cg(pgx, (unsigned)M);
@@ -3553,11 +3561,11 @@ static int pq_kmeans_run_one(Ctx* ctx, cudaStream_t st, const PqJob& job, const 
     if (prune) MVR_CUDA(ctx, cudaMemcpyAsync(cb_old, cb, (size_t)M * K * S * sizeof(float), cudaMemcpyDeviceToDevice, st));
     {
       const size_t sm = scatter_tile_smem(S);
-      const dim3 sg((unsigned)nblk, (unsigned)M);
+      const dim3 sg((unsigned)sblk, (unsigned)M);
       switch (S) {
-        case 1: { auto k = pq_scatter_tile_kernel<1>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
-        case 2: { auto k = pq_scatter_tile_kernel<2>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
-        default: { auto k = pq_scatter_tile_kernel<4>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, rpc); } break;
+        case 1: { auto k = pq_scatter_tile_kernel<1>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, srpc); } break;
+        case 2: { auto k = pq_scatter_tile_kernel<2>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, srpc); } break;
+        default: { auto k = pq_scatter_tile_kernel<4>; MVR_CUDA(ctx, raise_smem_limit((const void*)k, (size_t)(sm))); k<<<sg, kScatT, sm, st>>>(XT, N, K, asg, hist, sorted, d_state, srpc); } break;
       }
     }
     MVR_CUDA(ctx, cudaGetLastError());

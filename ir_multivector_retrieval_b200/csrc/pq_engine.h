@@ -47,6 +47,7 @@ struct PqOut {
 // [0, small_bytes) is mirrored on the host (RNG draws in, status out).
 struct PqLayout {
   int nblk = 0, nchunk = 0;
+  int nblk_s = 0;  // Lloyd histogram / scatter CTAs (one kScatTile-row tile each)
   uint64_t rows_per_cta = 0;
   size_t o_draws = 0, o_chosen = 0, o_idx0 = 0, o_thr = 0, o_counts = 0, o_starts = 0, o_wcss = 0,
          o_prev = 0, o_status = 0, o_nonf = 0, o_iters = 0, o_fb = 0, o_rs = 0, o_exact = 0, o_state = 0;
