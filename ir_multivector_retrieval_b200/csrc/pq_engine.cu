@@ -1658,7 +1658,7 @@ size_t scatter_smem(int M, int S) { return (size_t)M * (256 * 8 + (S == 4 ? 256 
 // ---------------------------------------------------------------------------
 constexpr int kScatT = 256;
 constexpr int kScatWarps = kScatT / 32;
-constexpr int kScatTile = 4096;
+constexpr int kScatTile = 2048;
 constexpr int kScatPerWarp = kScatTile / kScatWarps;  // 512 rows: 16 groups of 32
 
 template <int S> struct RowT;
@@ -1671,7 +1671,7 @@ size_t scatter_tile_smem(int S) {
 }
 
 template <int S>
-__global__ void __launch_bounds__(kScatT, 2)
+__global__ void __launch_bounds__(kScatT, 3)
 pq_scatter_tile_kernel(const float* __restrict__ XT, uint64_t N, int K, const uint8_t* __restrict__ asg,
                        const uint32_t* __restrict__ bases, float* __restrict__ sorted,
                        const uint8_t* __restrict__ state, uint64_t rows_per_cta) {
