@@ -535,7 +535,7 @@ def run_b200(args) -> None:
     # those few writes are not counted); launches sampled with CUDA events
     # inside the engine (every 8th step). (2) the pruned Lloyd passes (iterations >= 1): exact
     # (row, centroid) distances actually computed x 12 flops (3 per
-    # coordinate, SURVEY's convention) against the FP32 lanes x sampled clock.
+    # coordinate: subtract, square, add) against the measured f32x2 issue rate.
     # The line's "roofline" is the one with more device time per training.
     # The timed trainings run their subspaces as two groups side by side, so
     # one launch's duration there includes the other group's overlapping
