@@ -1454,7 +1454,7 @@ pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K, uint32_t* __restric
   uint32_t* hm = hist + (size_t)m * nblk * K;
   const int b0 = (int)((int64_t)nblk * warp / kScanWarps), b1 = (int)((int64_t)nblk * (warp + 1) / kScanWarps);
   uint32_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // clusters lane, lane + 32, ...
-#pragma unroll 2
+#pragma unroll 4
   for (int b = b0; b < b1; ++b) {
 #pragma unroll
     for (int q = 0; q < 8; ++q)
@@ -1499,23 +1499,23 @@ pq_scan_kernel(uint32_t* __restrict__ hist, int nblk, int K, uint32_t* __restric
     }
   }
   __syncthreads();
-  uint32_t run[8], v[8];
+  uint32_t run[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) run[q] = cstart[q * 32 + lane] + part[warp][q * 32 + lane];
-  if (b0 < b1) {
+  for (int b = b0; b < b1; b += 4) {  // four rows' loads go out before their stores
+    uint32_t v[4][8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = q * 32 + lane < K ? hm[(size_t)b0 * K + q * 32 + lane] : 0u;
-  }
-  for (int b = b0; b < b1; ++b) {
-    uint32_t nx[8];  // the next row's loads go out before this row's stores
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int q = 0; q < 8; ++q) nx[q] = (b + 1 < b1 && q * 32 + lane < K) ? hm[(size_t)(b + 1) * K + q * 32 + lane] : 0u;
+      for (int q = 0; q < 8; ++q)
+        v[i][q] = (b + i < b1 && q * 32 + lane < K) ? hm[(size_t)(b + i) * K + q * 32 + lane] : 0u;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      if (q * 32 + lane < K) hm[(size_t)b * K + q * 32 + lane] = run[q];
-      run[q] += v[q];
-      v[q] = nx[q];
-    }
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (b + i < b1 && q * 32 + lane < K) hm[(size_t)(b + i) * K + q * 32 + lane] = run[q];
+        run[q] += v[i][q];
+      }
   }
 }
 
